@@ -1,0 +1,185 @@
+/*
+ * llmtoy_cuda.h — C ABI of the B200 (sm_100a) backend for llmtoy-zig's
+ * quantized MoE forward path.
+ *
+ * The reference has no FFI; its operator API is Zig (src/ops, src/quant,
+ * src/model/gemma4/forward.zig) and its device seam is GpuWeights in
+ * src/model/gemma4/gpu_weights.zig, which returns Zig error unions.  Each
+ * entry point below names the reference function it replaces.  Everything is
+ * plain C: fixed-width integers, raw pointers and sizes, no CUDA or torch
+ * types, so a Zig `extern fn`, a C++ host or Python ctypes can bind it.
+ *
+ * Conventions
+ *   - Weights are uploaded once (lt_upload) and owned by the context, like
+ *     GpuWeights.init (gpu_weights.zig:373).  GGUF bytes go up unchanged
+ *     except that each row is padded to a 16-byte pitch on the device so
+ *     every row starts 16-byte aligned; lt_tensor_download undoes it.
+ *   - "dev_" pointers are device memory owned by the caller.  Device ops are
+ *     asynchronous on the context's stream (lt_set_stream); lt_sync joins.
+ *   - Errors are returned as lt_status, never by abort; lt_last_error gives
+ *     the message.  There is no CPU fallback: a missing device is
+ *     LT_ENODEV, an unsupported GGUF type LT_EUNSUPPORTED_TYPE (the
+ *     reference panics there, src/ops/math.zig:206,223).
+ *   - One context per GPU; a context is not re-entrant across host threads.
+ *   - ggml_type uses the GGUF enum (src/gguf/types.zig:23-52):
+ *     F32=0, F16=1, Q8_0=8, Q4_K=12, Q6_K=14.
+ */
+#ifndef LLMTOY_CUDA_H
+#define LLMTOY_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LT_API_VERSION 1
+
+typedef enum lt_status {
+    LT_OK = 0,
+    LT_EINVAL = 1,              /* bad argument, shape or size              */
+    LT_EUNSUPPORTED_TYPE = 2,   /* ggml type other than F32/F16/Q8_0/Q4_K/Q6_K */
+    LT_ENOMEM = 3,              /* device allocation failed                 */
+    LT_ECUDA = 4,               /* a CUDA runtime call failed               */
+    LT_ETIMEOUT = 5,            /* a bounded device-side wait gave up       */
+    LT_ENODEV = 6               /* no usable sm_100 device                  */
+} lt_status;
+
+typedef enum lt_ggml_type {
+    LT_TYPE_F32 = 0,
+    LT_TYPE_F16 = 1,
+    LT_TYPE_Q8_0 = 8,
+    LT_TYPE_Q4_K = 12,
+    LT_TYPE_Q6_K = 14
+} lt_ggml_type;
+
+typedef enum lt_act {
+    LT_ACT_SILU = 0,            /* x / (1 + e^-x), src/ops/math.zig:38-40    */
+    LT_ACT_GELU_TANH = 1        /* tanh GELU, src/ops/math.zig:85-88         */
+} lt_act;
+
+typedef struct lt_ctx lt_ctx;
+typedef struct lt_tensor lt_tensor;
+
+/* Shape of an uploaded tensor. */
+typedef struct lt_tensor_desc {
+    uint32_t ggml_type;
+    uint32_t n_experts;     /* 0 for a plain 2-D matrix                       */
+    uint64_t rows;          /* rows per expert (or total rows when 2-D)       */
+    uint64_t cols;
+    uint64_t row_bytes;     /* rowBytes(type, cols), src/ops/math.zig:194     */
+    uint64_t row_pitch;     /* device row stride: row_bytes rounded up to 16  */
+} lt_tensor_desc;
+
+/* ── context ──────────────────────────────────────────────────────────────
+ * Replaces GpuContext.init/deinit (src/gpu/context.zig:270-960).          */
+int         lt_api_version(void);
+lt_status   lt_init(int device, lt_ctx **out);
+void        lt_free(lt_ctx *ctx);
+/* Use an existing cudaStream_t (passed as void*); NULL selects the
+ * context's own stream. */
+lt_status   lt_set_stream(lt_ctx *ctx, void *cuda_stream);
+lt_status   lt_sync(lt_ctx *ctx);
+const char *lt_last_error(const lt_ctx *ctx);
+const char *lt_status_string(lt_status status);
+/* Pre-size the context's scratch arena for up to max_tokens tokens, so that
+ * later ops allocate nothing (needed before CUDA graph capture). */
+lt_status   lt_reserve(lt_ctx *ctx, uint32_t max_tokens, uint32_t max_k,
+                       uint64_t max_d_model, uint64_t max_d_expert);
+
+/* ── tensors ──────────────────────────────────────────────────────────────
+ * RawMatrix{data,type_,rows,cols} (src/model/model_weights.zig:17-22) with
+ * the 3-D expert flattening of src/model/gemma4/loader.zig:277-292:
+ * n_experts > 0 means `rows` rows per expert, experts back to back.       */
+uint64_t    lt_row_bytes(uint32_t ggml_type, uint64_t cols);   /* == rowBytes */
+lt_status   lt_upload(lt_ctx *ctx, const void *host_bytes, size_t nbytes,
+                      uint32_t ggml_type, uint64_t rows, uint64_t cols,
+                      uint32_t n_experts, lt_tensor **out);
+/* Same as lt_upload with the GGUF bytes already in device memory. */
+lt_status   lt_upload_from_device(lt_ctx *ctx, const void *dev_bytes, size_t nbytes,
+                                  uint32_t ggml_type, uint64_t rows, uint64_t cols,
+                                  uint32_t n_experts, lt_tensor **out);
+lt_status   lt_tensor_download(lt_ctx *ctx, const lt_tensor *t, void *host_bytes,
+                               size_t nbytes);
+lt_status   lt_tensor_describe(const lt_tensor *t, lt_tensor_desc *out);
+lt_status   lt_tensor_free(lt_ctx *ctx, lt_tensor *t);
+
+/* ── device ops (asynchronous on the context stream) ───────────────────── */
+
+/* dequantRow over rows [row0, row0+nrows) (src/ops/math.zig:211-225 and
+ * src/quant/dequant.zig:17-277).  Bit-exact with the reference CPU codecs.
+ * dev_out holds nrows*cols f32.  Expert tensors: row0 counts over all
+ * experts' rows. */
+lt_status lt_dequant(lt_ctx *ctx, const lt_tensor *t, uint64_t row0, uint64_t nrows,
+                     float *dev_out);
+
+/* quantMatvec / quantMatvecPar (src/ops/math.zig:133-171, :277-320) for ntok
+ * input vectors: dev_y[tok][rows] = W[expert] . dev_x[tok][cols].
+ * expert selects one expert of a 3-D tensor (ignored for 2-D). */
+lt_status lt_qmatvec(lt_ctx *ctx, const lt_tensor *w, uint32_t expert,
+                     const float *dev_x, float *dev_y, uint32_t ntok);
+
+/* rmsnorm (src/ops/math.zig:20-26) of ntok rows of length n. */
+lt_status lt_rmsnorm(lt_ctx *ctx, const float *dev_x, const float *dev_w, float eps,
+                     uint32_t n, uint32_t ntok, float *dev_y);
+
+/* In-place softmax (src/ops/math.zig:29-35) of ntok rows of length n. */
+lt_status lt_softmax(lt_ctx *ctx, float *dev_x, uint32_t n, uint32_t ntok);
+
+/* Router: routerTopKSoftmax (src/model/gemma4/forward.zig:648-668).
+ * f32 router logits, top-k with the lowest index winning ties
+ * (forward.zig:598-629), softmax probabilities of the selected experts.
+ * norm_topk != 0 renormalises the k weights to sum 1 (Qwen3-MoE; the
+ * reference has no such mode).  dev_expert_scale (nullable) multiplies in
+ * down_exps_scale[e] (forward.zig:477).  The logits reproduce dotf32's
+ * summation order (src/ops/math.zig:96-116) exactly, so ids match the CPU
+ * path bit for bit.  Outputs: dev_ids[ntok][k], dev_w[ntok][k]. */
+lt_status lt_moe_route(lt_ctx *ctx, const lt_tensor *router, const float *dev_x,
+                       uint32_t ntok, uint32_t k, int norm_topk,
+                       const float *dev_expert_scale, uint32_t *dev_ids, float *dev_w);
+
+/* Dispatch + grouped expert FFN + weighted combine: the expert loop of
+ * src/model/gemma4/forward.zig:463-479 and src/ops/moe.zig:61-76.
+ * gate: [E][F][d] (or the fused gate_up [E][2F][d] when up == NULL),
+ * up: [E][F][d], down: [E][d][F].  dev_out[tok][d] is overwritten with
+ * sum_i w[tok][i] * down_e(act(gate_e.x) * (up_e.x)), summed in slot order. */
+lt_status lt_moe_ffn(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up,
+                     const lt_tensor *down, int act, const float *dev_x, uint32_t ntok,
+                     const uint32_t *dev_ids, const float *dev_w, uint32_t k,
+                     float *dev_out);
+
+/* moeForward (src/ops/moe.zig:18-77) generalised to the routing modes above:
+ * lt_moe_route followed by lt_moe_ffn.  dev_ids / dev_w may be NULL. */
+lt_status lt_moe_forward(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *gate,
+                         const lt_tensor *up, const lt_tensor *down, int act,
+                         int norm_topk, const float *dev_expert_scale,
+                         const float *dev_x, uint32_t ntok, uint32_t k, float *dev_out,
+                         uint32_t *dev_ids, float *dev_w);
+
+/* greedy (src/model/sample.zig:11-17): index of the first maximum of each of
+ * ntok rows of length n (the argmax shader, src/gpu/shaders/argmax.glsl). */
+lt_status lt_argmax(lt_ctx *ctx, const float *dev_x, uint32_t n, uint32_t ntok,
+                    uint32_t *dev_idx);
+
+/* ── host-buffer entry points (synchronous) ─────────────────────────────────
+ * Same semantics with HOST vectors, copies included: the shape of the
+ * reference's own CPU calls, for callers that keep activations on the host. */
+
+/* quantMatvec(out, mat_data, mat_type, vec, rows, cols, row_buf)
+ * (src/ops/math.zig:133): host vec[cols] -> host out[rows]. */
+lt_status lt_quant_matvec_host(lt_ctx *ctx, float *out, const lt_tensor *mat,
+                               uint32_t expert, const float *vec, uint64_t rows,
+                               uint64_t cols);
+
+/* moeForward on host vectors: x[ntok][d] -> out[ntok][d]; ids/w nullable. */
+lt_status lt_moe_forward_host(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *gate,
+                              const lt_tensor *up, const lt_tensor *down, int act,
+                              int norm_topk, const float *expert_scale_host,
+                              const float *x, uint32_t ntok, uint32_t k, float *out,
+                              uint32_t *ids, float *w);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,251 @@
+"""B200 (sm_100a) backend for llmtoy-zig's quantized MoE forward path.
+
+Python binding of the C ABI in include/llmtoy_cuda.h (libllmtoy_cuda.so, built
+in-tree by build.py).  Device buffers are plain integer addresses, so torch
+tensors (``t.data_ptr()``) or any other allocator can feed the ops.  There is
+no CPU fallback: without the built library or an sm_100 GPU every entry point
+raises.
+
+Import with ``importlib.import_module("llmtoy-zig_b200")`` (the directory name
+is not a Python identifier).
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().with_name("libllmtoy_cuda.so")
+
+# GGUF type codes (src/gguf/types.zig:23-52)
+F32, F16, Q8_0, Q4_K, Q6_K = 0, 1, 8, 12, 14
+TYPE_NAMES = {F32: "F32", F16: "F16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K"}
+BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
+ACT_SILU, ACT_GELU_TANH = 0, 1
+
+STATUS = {0: "LT_OK", 1: "LT_EINVAL", 2: "LT_EUNSUPPORTED_TYPE", 3: "LT_ENOMEM",
+          4: "LT_ECUDA", 5: "LT_ETIMEOUT", 6: "LT_ENODEV"}
+
+# Every symbol include/llmtoy_cuda.h declares.
+EXPORTS = [
+    "lt_api_version", "lt_init", "lt_free", "lt_set_stream", "lt_sync", "lt_last_error",
+    "lt_status_string", "lt_reserve", "lt_row_bytes", "lt_upload", "lt_upload_from_device",
+    "lt_tensor_download", "lt_tensor_describe", "lt_tensor_free", "lt_dequant", "lt_qmatvec",
+    "lt_rmsnorm", "lt_softmax", "lt_moe_route", "lt_moe_ffn", "lt_moe_forward", "lt_argmax",
+    "lt_quant_matvec_host", "lt_moe_forward_host",
+]
+
+
+class LtError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS.get(status, status)}: {message}")
+        self.status = status
+
+
+class TensorDesc(ctypes.Structure):
+    _fields_ = [("ggml_type", ctypes.c_uint32), ("n_experts", ctypes.c_uint32),
+                ("rows", ctypes.c_uint64), ("cols", ctypes.c_uint64),
+                ("row_bytes", ctypes.c_uint64), ("row_pitch", ctypes.c_uint64)]
+
+
+_lib = None
+
+
+def load_library() -> ctypes.CDLL:
+    """Load libllmtoy_cuda.so, failing loudly if it was not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `python llmtoy-zig_b200/build.py`")
+    lib = ctypes.CDLL(str(LIB_PATH))
+    P, U32, U64, I, F, SZ = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+    sig = {
+        "lt_api_version": (I, []),
+        "lt_init": (I, [I, ctypes.POINTER(P)]),
+        "lt_free": (None, [P]),
+        "lt_set_stream": (I, [P, P]),
+        "lt_sync": (I, [P]),
+        "lt_last_error": (ctypes.c_char_p, [P]),
+        "lt_status_string": (ctypes.c_char_p, [I]),
+        "lt_reserve": (I, [P, U32, U32, U64, U64]),
+        "lt_row_bytes": (U64, [U32, U64]),
+        "lt_upload": (I, [P, P, SZ, U32, U64, U64, U32, ctypes.POINTER(P)]),
+        "lt_upload_from_device": (I, [P, P, SZ, U32, U64, U64, U32, ctypes.POINTER(P)]),
+        "lt_tensor_download": (I, [P, P, P, SZ]),
+        "lt_tensor_describe": (I, [P, ctypes.POINTER(TensorDesc)]),
+        "lt_tensor_free": (I, [P, P]),
+        "lt_dequant": (I, [P, P, U64, U64, P]),
+        "lt_qmatvec": (I, [P, P, U32, P, P, U32]),
+        "lt_rmsnorm": (I, [P, P, P, F, U32, U32, P]),
+        "lt_softmax": (I, [P, P, U32, U32]),
+        "lt_moe_route": (I, [P, P, P, U32, U32, I, P, P, P]),
+        "lt_moe_ffn": (I, [P, P, P, P, I, P, U32, P, P, U32, P]),
+        "lt_moe_forward": (I, [P, P, P, P, P, I, I, P, P, U32, U32, P, P, P]),
+        "lt_argmax": (I, [P, P, U32, U32, P]),
+        "lt_quant_matvec_host": (I, [P, P, P, U32, P, U64, U64]),
+        "lt_moe_forward_host": (I, [P, P, P, P, P, I, I, P, P, U32, U32, P, P, P]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def row_bytes(ggml_type: int, cols: int) -> int:
+    """rowBytes (src/ops/math.zig:194-208)."""
+    elems, nbytes = BLOCK[ggml_type]
+    return (cols // elems) * nbytes
+
+
+def _ptr(x) -> int | None:
+    """Device address of a torch tensor, or an int address, or None."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    return x.data_ptr()
+
+
+class Tensor:
+    """A GGUF tensor uploaded to the device (RawMatrix, src/model/model_weights.zig:17)."""
+
+    def __init__(self, ctx: "Context", handle: int):
+        self._ctx = ctx
+        self.handle = handle
+        d = TensorDesc()
+        ctx._check(ctx.lib.lt_tensor_describe(handle, ctypes.byref(d)))
+        self.ggml_type, self.n_experts = d.ggml_type, d.n_experts
+        self.rows, self.cols, self.row_bytes, self.row_pitch = d.rows, d.cols, d.row_bytes, d.row_pitch
+
+    @property
+    def total_rows(self) -> int:
+        return self.rows * max(1, self.n_experts)
+
+    def download(self) -> bytes:
+        buf = ctypes.create_string_buffer(self.total_rows * self.row_bytes)
+        self._ctx._check(self._ctx.lib.lt_tensor_download(self._ctx.ptr, self.handle, buf, len(buf)))
+        return buf.raw
+
+    def free(self) -> None:
+        if self.handle:
+            self._ctx.lib.lt_tensor_free(self._ctx.ptr, self.handle)
+            self.handle = None
+
+
+class Context:
+    """One device context (lt_init); ops run on its stream."""
+
+    def __init__(self, device: int = 0):
+        self.lib = load_library()
+        p = ctypes.c_void_p()
+        st = self.lib.lt_init(device, ctypes.byref(p))
+        if st != 0:
+            raise LtError(st, f"lt_init(device={device}) failed")
+        self.ptr = p.value
+        self.device = device
+
+    # -- plumbing ---------------------------------------------------------
+    def _check(self, st: int) -> None:
+        if st != 0:
+            msg = self.lib.lt_last_error(self.ptr) if self.ptr else b""
+            raise LtError(st, (msg or b"").decode())
+
+    def close(self) -> None:
+        if self.ptr:
+            self.lib.lt_free(self.ptr)
+            self.ptr = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def set_stream(self, stream) -> None:
+        """Run ops on a cudaStream_t (int handle or torch.cuda.Stream); None: own stream."""
+        handle = getattr(stream, "cuda_stream", stream)
+        self._check(self.lib.lt_set_stream(self.ptr, handle))
+
+    def sync(self) -> None:
+        self._check(self.lib.lt_sync(self.ptr))
+
+    def reserve(self, max_tokens: int, max_k: int, max_d_model: int, max_d_expert: int) -> None:
+        self._check(self.lib.lt_reserve(self.ptr, max_tokens, max_k, max_d_model, max_d_expert))
+
+    # -- weights ----------------------------------------------------------
+    def upload(self, data, ggml_type: int, rows: int, cols: int, n_experts: int = 0) -> Tensor:
+        """Upload GGUF bytes (bytes / numpy array / host torch tensor)."""
+        import numpy as np
+        arr = np.ascontiguousarray(np.frombuffer(memoryview(data).cast("B"), dtype=np.uint8)
+                                   if not isinstance(data, np.ndarray) else data.view(np.uint8).reshape(-1))
+        h = ctypes.c_void_p()
+        self._check(self.lib.lt_upload(self.ptr, arr.ctypes.data, arr.nbytes, ggml_type, rows, cols,
+                                       n_experts, ctypes.byref(h)))
+        return Tensor(self, h.value)
+
+    def upload_device(self, dev_tensor, ggml_type: int, rows: int, cols: int, n_experts: int = 0) -> Tensor:
+        """Upload GGUF bytes that already sit in device memory (a uint8 CUDA tensor)."""
+        h = ctypes.c_void_p()
+        nbytes = dev_tensor.numel() * dev_tensor.element_size()
+        self._check(self.lib.lt_upload_from_device(self.ptr, dev_tensor.data_ptr(), nbytes, ggml_type, rows,
+                                                   cols, n_experts, ctypes.byref(h)))
+        return Tensor(self, h.value)
+
+    # -- device ops (asynchronous) ----------------------------------------
+    def dequant(self, t: Tensor, row0: int, nrows: int, out) -> None:
+        self._check(self.lib.lt_dequant(self.ptr, t.handle, row0, nrows, _ptr(out)))
+
+    def qmatvec(self, w: Tensor, x, y, ntok: int = 1, expert: int = 0) -> None:
+        self._check(self.lib.lt_qmatvec(self.ptr, w.handle, expert, _ptr(x), _ptr(y), ntok))
+
+    def rmsnorm(self, x, w, eps: float, n: int, ntok: int, y) -> None:
+        self._check(self.lib.lt_rmsnorm(self.ptr, _ptr(x), _ptr(w), eps, n, ntok, _ptr(y)))
+
+    def softmax(self, x, n: int, ntok: int = 1) -> None:
+        self._check(self.lib.lt_softmax(self.ptr, _ptr(x), n, ntok))
+
+    def argmax(self, x, n: int, ntok: int, idx) -> None:
+        self._check(self.lib.lt_argmax(self.ptr, _ptr(x), n, ntok, _ptr(idx)))
+
+    def moe_route(self, router: Tensor, x, ntok: int, k: int, norm_topk: bool, expert_scale, ids, w) -> None:
+        self._check(self.lib.lt_moe_route(self.ptr, router.handle, _ptr(x), ntok, k, int(norm_topk),
+                                          _ptr(expert_scale), _ptr(ids), _ptr(w)))
+
+    def moe_ffn(self, gate: Tensor, up: Tensor | None, down: Tensor, act: int, x, ntok: int, ids, w, k: int,
+                out) -> None:
+        self._check(self.lib.lt_moe_ffn(self.ptr, gate.handle, up.handle if up else None, down.handle, act,
+                                        _ptr(x), ntok, _ptr(ids), _ptr(w), k, _ptr(out)))
+
+    def moe_forward(self, router: Tensor, gate: Tensor, up: Tensor | None, down: Tensor, act: int,
+                    norm_topk: bool, expert_scale, x, ntok: int, k: int, out, ids=None, w=None) -> None:
+        self._check(self.lib.lt_moe_forward(self.ptr, router.handle, gate.handle, up.handle if up else None,
+                                            down.handle, act, int(norm_topk), _ptr(expert_scale), _ptr(x), ntok,
+                                            k, _ptr(out), _ptr(ids), _ptr(w)))
+
+    # -- host-buffer entry points (synchronous) ---------------------------
+    def quant_matvec_host(self, mat: Tensor, vec, expert: int = 0):
+        """quantMatvec on host vectors (src/ops/math.zig:133): numpy f32 in, numpy f32 out."""
+        import numpy as np
+        v = np.ascontiguousarray(vec, dtype=np.float32)
+        out = np.empty(mat.rows, dtype=np.float32)
+        self._check(self.lib.lt_quant_matvec_host(self.ptr, out.ctypes.data, mat.handle, expert, v.ctypes.data,
+                                                  mat.rows, mat.cols))
+        return out
+
+    def moe_forward_host(self, router: Tensor, gate: Tensor, up: Tensor | None, down: Tensor, act: int,
+                         norm_topk: bool, expert_scale, x, k: int, out=None, ids=None, w=None):
+        """moeForward on host arrays: x[ntok][d] -> (out, ids, w)."""
+        import numpy as np
+        xx = np.ascontiguousarray(x, dtype=np.float32)
+        ntok = xx.shape[0]
+        out = np.empty_like(xx) if out is None else out
+        ids = np.empty((ntok, k), dtype=np.uint32) if ids is None else ids
+        w = np.empty((ntok, k), dtype=np.float32) if w is None else w
+        es = None if expert_scale is None else np.ascontiguousarray(expert_scale, dtype=np.float32)
+        self._check(self.lib.lt_moe_forward_host(
+            self.ptr, router.handle, gate.handle, up.handle if up else None, down.handle, act, int(norm_topk),
+            None if es is None else es.ctypes.data, xx.ctypes.data, ntok, k, out.ctypes.data, ids.ctypes.data,
+            w.ctypes.data))
+        return out, ids, w

@@ -1,0 +1,612 @@
+// lt_api.cu — the C ABI declared in include/llmtoy_cuda.h.
+//
+// Host side of the backend: context and stream, weight upload (GGUF rows at a
+// 16-byte device pitch), a scratch arena for intermediate activations, argument
+// checking, and the op entry points that launch the kernels in lt_kernels.cu.
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "llmtoy_cuda.h"
+#include "lt_common.cuh"
+#include "lt_internal.h"
+
+struct lt_tensor {
+    lt::DevMat m;
+    void *dev;
+    size_t dev_bytes;
+    uint64_t total_rows;
+};
+
+struct lt_ctx {
+    int device = 0;
+    cudaStream_t own = nullptr;
+    cudaStream_t stream = nullptr;
+    std::string err;
+    int num_sms = 0;
+    bool pdl = true;
+    int *dev_err = nullptr;          // device error word written by kernels
+    uint8_t *scratch = nullptr;      // activation scratch arena
+    size_t scratch_bytes = 0;
+    uint32_t *counters = nullptr;    // zero-initialised, kernels leave them zero
+    size_t n_counters = 0;
+    uint8_t *pinned = nullptr;       // pinned staging for the host-buffer entry points
+    size_t pinned_bytes = 0;
+};
+
+namespace {
+
+lt_status fail(lt_ctx *ctx, lt_status st, const char *fmt, ...) {
+    if (ctx) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(buf, sizeof buf, fmt, ap);
+        va_end(ap);
+        ctx->err = buf;
+    }
+    return st;
+}
+
+lt_status cuda_fail(lt_ctx *ctx, cudaError_t e, const char *what) {
+    if (e == cudaErrorMemoryAllocation)
+        return fail(ctx, LT_ENOMEM, "%s: %s", what, cudaGetErrorString(e));
+    return fail(ctx, LT_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define LT_CUDA(ctx, call, what)                              \
+    do {                                                      \
+        cudaError_t e_ = (call);                              \
+        if (e_ != cudaSuccess) return cuda_fail(ctx, e_, what); \
+    } while (0)
+
+lt::LaunchCfg cfg_of(lt_ctx *ctx) {
+    lt::LaunchCfg c;
+    c.stream = ctx->stream;
+    c.pdl = ctx->pdl;
+    c.dev_err = ctx->dev_err;
+    c.num_sms = ctx->num_sms;
+    return c;
+}
+
+lt_status enter(lt_ctx *ctx) {
+    if (!ctx) return LT_EINVAL;
+    ctx->err.clear();
+    cudaError_t e = cudaSetDevice(ctx->device);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaSetDevice");
+    return LT_OK;
+}
+
+// Grow the scratch arena; waits for the stream first so nothing in flight
+// still uses the old buffer.
+lt_status ensure_scratch(lt_ctx *ctx, size_t bytes) {
+    if (bytes <= ctx->scratch_bytes) return LT_OK;
+    LT_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    if (ctx->scratch) cudaFree(ctx->scratch);
+    ctx->scratch = nullptr;
+    ctx->scratch_bytes = 0;
+    bytes = (bytes + (1u << 20) - 1) & ~((size_t)(1u << 20) - 1);
+    LT_CUDA(ctx, cudaMalloc(&ctx->scratch, bytes), "cudaMalloc(scratch)");
+    ctx->scratch_bytes = bytes;
+    return LT_OK;
+}
+
+lt_status ensure_counters(lt_ctx *ctx, size_t n) {
+    if (n <= ctx->n_counters) return LT_OK;
+    LT_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    if (ctx->counters) cudaFree(ctx->counters);
+    ctx->counters = nullptr;
+    ctx->n_counters = 0;
+    n = (n + 4095) & ~(size_t)4095;
+    LT_CUDA(ctx, cudaMalloc(&ctx->counters, n * 4), "cudaMalloc(counters)");
+    LT_CUDA(ctx, cudaMemset(ctx->counters, 0, n * 4), "cudaMemset(counters)");
+    ctx->n_counters = n;
+    return LT_OK;
+}
+
+lt_status ensure_pinned(lt_ctx *ctx, size_t bytes) {
+    if (bytes <= ctx->pinned_bytes) return LT_OK;
+    if (ctx->pinned) cudaFreeHost(ctx->pinned);
+    ctx->pinned = nullptr;
+    ctx->pinned_bytes = 0;
+    bytes = (bytes + 65535) & ~(size_t)65535;
+    LT_CUDA(ctx, cudaMallocHost(&ctx->pinned, bytes), "cudaMallocHost");
+    ctx->pinned_bytes = bytes;
+    return LT_OK;
+}
+
+size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+bool quantized(uint32_t t) { return t == lt::T_Q8_0 || t == lt::T_Q4_K || t == lt::T_Q6_K; }
+
+lt_status check_kernel_shape(lt_ctx *ctx, const lt::DevMat &m, const char *what) {
+    if (quantized(m.type)) {
+        if (m.type != lt::T_Q8_0 && m.cols % 256 != 0)
+            return fail(ctx, LT_EINVAL, "%s: K-quant cols %llu not a multiple of 256", what,
+                        (unsigned long long)m.cols);
+        if (m.cols % 32 != 0)
+            return fail(ctx, LT_EINVAL, "%s: cols %llu not a multiple of 32", what, (unsigned long long)m.cols);
+        if (m.cols > 65536) return fail(ctx, LT_EINVAL, "%s: cols %llu too large", what, (unsigned long long)m.cols);
+    }
+    return LT_OK;
+}
+
+// MoE scratch layout for T tokens, k slots, E experts, F expert width.
+struct MoeScratch {
+    uint32_t *ids;
+    float *w;
+    float *h;
+    float *logits;
+    lt::MoePlan plan;
+    size_t bytes;
+};
+
+MoeScratch moe_layout(uint8_t *base, uint32_t T, uint32_t k, uint32_t E, uint64_t F) {
+    MoeScratch s;
+    size_t off = 0;
+    auto take = [&](size_t b) {
+        uint8_t *p = base ? base + off : nullptr;
+        off += al256(b);
+        return p;
+    };
+    const size_t P = (size_t)T * k;
+    s.ids = (uint32_t *)take(P * 4);
+    s.w = (float *)take(P * 4);
+    s.h = (float *)take(P * F * 4);
+    s.logits = (float *)take((size_t)T * E * 4);
+    s.plan.n_active = (uint32_t *)take(4);
+    s.plan.act_e = (uint32_t *)take((size_t)E * 4);
+    s.plan.act_off = (uint32_t *)take((size_t)E * 4);
+    s.plan.act_cnt = (uint32_t *)take((size_t)E * 4);
+    s.plan.pos_pair = (uint32_t *)take(P * 4);
+    s.plan.pair_pos = (uint32_t *)take(P * 4);
+    s.bytes = off;
+    return s;
+}
+
+lt_status launched(lt_ctx *ctx, cudaError_t e, const char *what) {
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+    return LT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int lt_api_version(void) { return LT_API_VERSION; }
+
+const char *lt_status_string(lt_status s) {
+    switch (s) {
+    case LT_OK: return "ok";
+    case LT_EINVAL: return "invalid argument";
+    case LT_EUNSUPPORTED_TYPE: return "unsupported ggml type";
+    case LT_ENOMEM: return "out of device memory";
+    case LT_ECUDA: return "CUDA error";
+    case LT_ETIMEOUT: return "device wait timed out";
+    case LT_ENODEV: return "no sm_100 device";
+    }
+    return "unknown status";
+}
+
+const char *lt_last_error(const lt_ctx *ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+lt_status lt_init(int device, lt_ctx **out) {
+    if (!out) return LT_EINVAL;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return LT_ENODEV;
+    }
+    if (device < 0 || device >= n) return LT_ENODEV;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return LT_ENODEV;
+    if (prop.major != 10) return LT_ENODEV;  // kernels are built for sm_100a only
+    lt_ctx *ctx = new lt_ctx();
+    ctx->device = device;
+    ctx->num_sms = prop.multiProcessorCount;
+    const char *pdl = getenv("LLMTOY_PDL");
+    ctx->pdl = !(pdl && strcmp(pdl, "0") == 0);
+    lt_status st = LT_OK;
+    if (cudaSetDevice(device) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&ctx->own, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&ctx->dev_err, 4) != cudaSuccess || cudaMemset(ctx->dev_err, 0, 4) != cudaSuccess) {
+        st = LT_ECUDA;
+    }
+    ctx->stream = ctx->own;
+    if (st == LT_OK) st = ensure_counters(ctx, 4096);
+    if (st != LT_OK) {
+        lt_free(ctx);
+        return st;
+    }
+    *out = ctx;
+    return LT_OK;
+}
+
+void lt_free(lt_ctx *ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->counters) cudaFree(ctx->counters);
+    if (ctx->dev_err) cudaFree(ctx->dev_err);
+    if (ctx->pinned) cudaFreeHost(ctx->pinned);
+    if (ctx->own) cudaStreamDestroy(ctx->own);
+    delete ctx;
+}
+
+lt_status lt_set_stream(lt_ctx *ctx, void *cuda_stream) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    ctx->stream = cuda_stream ? (cudaStream_t)cuda_stream : ctx->own;
+    return LT_OK;
+}
+
+lt_status lt_sync(lt_ctx *ctx) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    LT_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    int h = 0;
+    LT_CUDA(ctx, cudaMemcpy(&h, ctx->dev_err, 4, cudaMemcpyDeviceToHost), "read device error word");
+    if (h != 0) {
+        cudaMemset(ctx->dev_err, 0, 4);
+        return fail(ctx, LT_ETIMEOUT, "a device-side wait gave up (code %d)", h);
+    }
+    return LT_OK;
+}
+
+lt_status lt_reserve(lt_ctx *ctx, uint32_t max_tokens, uint32_t max_k, uint64_t max_d_model,
+                     uint64_t max_d_expert) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    const size_t moe = moe_layout(nullptr, max_tokens, max_k, lt::kRouterMaxE, max_d_expert).bytes;
+    const size_t io = 2 * al256((size_t)max_tokens * max_d_model * 4) + 2 * al256((size_t)max_tokens * max_k * 4);
+    st = ensure_scratch(ctx, moe + io);
+    if (st != LT_OK) return st;
+    return ensure_counters(ctx, 4096 + lt::router_token_groups(max_tokens) + max_tokens);
+}
+
+uint64_t lt_row_bytes(uint32_t ggml_type, uint64_t cols) {
+    if (!lt::type_supported(ggml_type)) return 0;
+    return lt::row_bytes_of(ggml_type, cols);
+}
+
+static lt_status upload_impl(lt_ctx *ctx, const void *src, bool src_on_device, size_t nbytes, uint32_t type,
+                             uint64_t rows, uint64_t cols, uint32_t n_experts, lt_tensor **out) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!out || !src) return fail(ctx, LT_EINVAL, "lt_upload: null pointer");
+    *out = nullptr;
+    if (!lt::type_supported(type)) return fail(ctx, LT_EUNSUPPORTED_TYPE, "lt_upload: ggml type %u", type);
+    const uint32_t be = lt::block_elems_of(type);
+    if (rows == 0 || cols == 0 || cols % be != 0)
+        return fail(ctx, LT_EINVAL, "lt_upload: cols %llu not a multiple of the %u-element block",
+                    (unsigned long long)cols, be);
+    const uint64_t total_rows = rows * (n_experts ? n_experts : 1);
+    const uint64_t rb = lt::row_bytes_of(type, cols);
+    if ((uint64_t)nbytes != total_rows * rb)
+        return fail(ctx, LT_EINVAL, "lt_upload: %zu bytes given, shape needs %llu", nbytes,
+                    (unsigned long long)(total_rows * rb));
+    const uint64_t pitch = (rb + 15) & ~(uint64_t)15;
+    lt_tensor *t = new lt_tensor();
+    t->total_rows = total_rows;
+    t->dev_bytes = (size_t)(total_rows * pitch) + 256;  // slack: decoders read a little past a row
+    cudaError_t e = cudaMalloc(&t->dev, t->dev_bytes);
+    if (e != cudaSuccess) {
+        delete t;
+        return cuda_fail(ctx, e, "cudaMalloc(tensor)");
+    }
+    e = cudaMemsetAsync(t->dev, 0, t->dev_bytes, ctx->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpy2DAsync(t->dev, pitch, src, rb, rb, total_rows,
+                              src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+        cudaFree(t->dev);
+        delete t;
+        return cuda_fail(ctx, e, "upload copy");
+    }
+    t->m.data = (const uint8_t *)t->dev;
+    t->m.type = type;
+    t->m.rows = rows;
+    t->m.cols = cols;
+    t->m.row_bytes = rb;
+    t->m.pitch = pitch;
+    t->m.n_experts = n_experts;
+    *out = t;
+    return LT_OK;
+}
+
+lt_status lt_upload(lt_ctx *ctx, const void *host_bytes, size_t nbytes, uint32_t ggml_type, uint64_t rows,
+                    uint64_t cols, uint32_t n_experts, lt_tensor **out) {
+    return upload_impl(ctx, host_bytes, false, nbytes, ggml_type, rows, cols, n_experts, out);
+}
+
+lt_status lt_upload_from_device(lt_ctx *ctx, const void *dev_bytes, size_t nbytes, uint32_t ggml_type,
+                                uint64_t rows, uint64_t cols, uint32_t n_experts, lt_tensor **out) {
+    return upload_impl(ctx, dev_bytes, true, nbytes, ggml_type, rows, cols, n_experts, out);
+}
+
+lt_status lt_tensor_download(lt_ctx *ctx, const lt_tensor *t, void *host_bytes, size_t nbytes) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!t || !host_bytes) return fail(ctx, LT_EINVAL, "lt_tensor_download: null pointer");
+    if ((uint64_t)nbytes != t->total_rows * t->m.row_bytes)
+        return fail(ctx, LT_EINVAL, "lt_tensor_download: buffer is %zu bytes, tensor %llu", nbytes,
+                    (unsigned long long)(t->total_rows * t->m.row_bytes));
+    LT_CUDA(ctx,
+            cudaMemcpy2DAsync(host_bytes, t->m.row_bytes, t->dev, t->m.pitch, t->m.row_bytes, t->total_rows,
+                              cudaMemcpyDeviceToHost, ctx->stream),
+            "download copy");
+    LT_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    return LT_OK;
+}
+
+lt_status lt_tensor_describe(const lt_tensor *t, lt_tensor_desc *out) {
+    if (!t || !out) return LT_EINVAL;
+    out->ggml_type = t->m.type;
+    out->n_experts = t->m.n_experts;
+    out->rows = t->m.rows;
+    out->cols = t->m.cols;
+    out->row_bytes = t->m.row_bytes;
+    out->row_pitch = t->m.pitch;
+    return LT_OK;
+}
+
+lt_status lt_tensor_free(lt_ctx *ctx, lt_tensor *t) {
+    if (!t) return LT_OK;
+    if (ctx) {
+        cudaSetDevice(ctx->device);
+        cudaStreamSynchronize(ctx->stream);
+    }
+    cudaFree(t->dev);
+    delete t;
+    return LT_OK;
+}
+
+lt_status lt_dequant(lt_ctx *ctx, const lt_tensor *t, uint64_t row0, uint64_t nrows, float *dev_out) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!t || (!dev_out && nrows)) return fail(ctx, LT_EINVAL, "lt_dequant: null pointer");
+    if (row0 + nrows > t->total_rows || row0 + nrows < row0)
+        return fail(ctx, LT_EINVAL, "lt_dequant: rows [%llu,+%llu) out of %llu", (unsigned long long)row0,
+                    (unsigned long long)nrows, (unsigned long long)t->total_rows);
+    return launched(ctx, lt::launch_dequant(cfg_of(ctx), t->m, row0, nrows, dev_out), "dequant");
+}
+
+lt_status lt_qmatvec(lt_ctx *ctx, const lt_tensor *w, uint32_t expert, const float *dev_x, float *dev_y,
+                     uint32_t ntok) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!w || !dev_x || !dev_y) return fail(ctx, LT_EINVAL, "lt_qmatvec: null pointer");
+    if (ntok == 0) return LT_OK;
+    if (expert >= (w->m.n_experts ? w->m.n_experts : 1u))
+        return fail(ctx, LT_EINVAL, "lt_qmatvec: expert %u out of range", expert);
+    if ((st = check_kernel_shape(ctx, w->m, "lt_qmatvec")) != LT_OK) return st;
+    if (w->m.rows > 0xffffffffull) return fail(ctx, LT_EINVAL, "lt_qmatvec: too many rows");
+    return launched(ctx, lt::launch_qmatvec(cfg_of(ctx), w->m, expert, dev_x, dev_y, ntok), "qmatvec");
+}
+
+lt_status lt_rmsnorm(lt_ctx *ctx, const float *dev_x, const float *dev_w, float eps, uint32_t n, uint32_t ntok,
+                     float *dev_y) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!dev_x || !dev_w || !dev_y || n == 0) return fail(ctx, LT_EINVAL, "lt_rmsnorm: bad argument");
+    if (ntok == 0) return LT_OK;
+    return launched(ctx, lt::launch_rmsnorm(cfg_of(ctx), dev_x, dev_w, eps, n, ntok, dev_y), "rmsnorm");
+}
+
+lt_status lt_softmax(lt_ctx *ctx, float *dev_x, uint32_t n, uint32_t ntok) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!dev_x || n == 0) return fail(ctx, LT_EINVAL, "lt_softmax: bad argument");
+    if (ntok == 0) return LT_OK;
+    return launched(ctx, lt::launch_softmax(cfg_of(ctx), dev_x, n, ntok), "softmax");
+}
+
+lt_status lt_argmax(lt_ctx *ctx, const float *dev_x, uint32_t n, uint32_t ntok, uint32_t *dev_idx) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!dev_x || !dev_idx || n == 0) return fail(ctx, LT_EINVAL, "lt_argmax: bad argument");
+    if (ntok == 0) return LT_OK;
+    const size_t part = (size_t)ntok * 64;
+    if ((st = ensure_scratch(ctx, al256(part * 4) * 2)) != LT_OK) return st;
+    if ((st = ensure_counters(ctx, ntok)) != LT_OK) return st;
+    float *pv = (float *)ctx->scratch;
+    uint32_t *pi = (uint32_t *)(ctx->scratch + al256(part * 4));
+    return launched(ctx, lt::launch_argmax(cfg_of(ctx), dev_x, n, ntok, dev_idx, pv, pi, ctx->counters), "argmax");
+}
+
+static lt_status check_router(lt_ctx *ctx, const lt_tensor *router, uint32_t k) {
+    if (!router) return fail(ctx, LT_EINVAL, "router: null tensor");
+    if (router->m.type != lt::T_F32 || router->m.n_experts != 0)
+        return fail(ctx, LT_EUNSUPPORTED_TYPE, "router: weights must be a 2-D F32 matrix");
+    if (router->m.rows == 0 || router->m.rows > (uint64_t)lt::kRouterMaxE)
+        return fail(ctx, LT_EINVAL, "router: %llu experts (max %d)", (unsigned long long)router->m.rows,
+                    lt::kRouterMaxE);
+    if (k == 0 || k > 16 || k > router->m.rows) return fail(ctx, LT_EINVAL, "router: k=%u", k);
+    return LT_OK;
+}
+
+static lt_status route_impl(lt_ctx *ctx, const lt_tensor *router, const float *x, uint32_t ntok, uint32_t k,
+                            int norm_topk, const float *escale, uint32_t *ids, float *w, float *logits) {
+    const uint32_t groups = lt::router_token_groups(ntok);
+    lt_status st = ensure_counters(ctx, groups);
+    if (st != LT_OK) return st;
+    return launched(ctx,
+                    lt::launch_router(cfg_of(ctx), (const float *)router->m.data, (uint32_t)router->m.rows,
+                                      (uint32_t)router->m.cols, x, ntok, k, norm_topk, escale, ids, w, logits,
+                                      ctx->counters),
+                    "router");
+}
+
+lt_status lt_moe_route(lt_ctx *ctx, const lt_tensor *router, const float *dev_x, uint32_t ntok, uint32_t k,
+                       int norm_topk, const float *dev_expert_scale, uint32_t *dev_ids, float *dev_w) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if ((st = check_router(ctx, router, k)) != LT_OK) return st;
+    if (!dev_x || !dev_ids || !dev_w) return fail(ctx, LT_EINVAL, "lt_moe_route: null pointer");
+    if (ntok == 0) return LT_OK;
+    if ((st = ensure_scratch(ctx, al256((size_t)ntok * router->m.rows * 4))) != LT_OK) return st;
+    return route_impl(ctx, router, dev_x, ntok, k, norm_topk, dev_expert_scale, dev_ids, dev_w,
+                      (float *)ctx->scratch);
+}
+
+static lt_status check_experts(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, const lt_tensor *down,
+                               uint32_t k, uint64_t *F_out) {
+    if (!gate || !down) return fail(ctx, LT_EINVAL, "moe: null expert tensor");
+    const uint32_t E = gate->m.n_experts;
+    if (E == 0 || down->m.n_experts != E || (up && up->m.n_experts != E))
+        return fail(ctx, LT_EINVAL, "moe: gate/up/down must be 3-D expert tensors with the same expert count");
+    if (!quantized(gate->m.type) || !quantized(down->m.type) || (up && up->m.type != gate->m.type))
+        return fail(ctx, LT_EUNSUPPORTED_TYPE, "moe: expert weights must be Q8_0/Q4_K/Q6_K (gate and up alike)");
+    const uint64_t F = up ? gate->m.rows : gate->m.rows / 2;
+    if ((!up && gate->m.rows % 2) || (up && (up->m.rows != F || up->m.cols != gate->m.cols)))
+        return fail(ctx, LT_EINVAL, "moe: gate/up shapes disagree");
+    if (down->m.rows != gate->m.cols || down->m.cols != F)
+        return fail(ctx, LT_EINVAL, "moe: down is %llux%llu, expected %llux%llu", (unsigned long long)down->m.rows,
+                    (unsigned long long)down->m.cols, (unsigned long long)gate->m.cols, (unsigned long long)F);
+    lt_status st;
+    if ((st = check_kernel_shape(ctx, gate->m, "moe gate")) != LT_OK) return st;
+    if ((st = check_kernel_shape(ctx, down->m, "moe down")) != LT_OK) return st;
+    if (k == 0 || k > 16 || k > E) return fail(ctx, LT_EINVAL, "moe: k=%u", k);
+    *F_out = F;
+    return LT_OK;
+}
+
+static lt_status ffn_impl(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, const lt_tensor *down, int act,
+                          const float *x, uint32_t ntok, const uint32_t *ids, const float *w, uint32_t k, float *out,
+                          const MoeScratch &s) {
+    const lt::LaunchCfg c = cfg_of(ctx);
+    const bool direct = ntok == 1;
+    lt::DevMat upm = up ? up->m : lt::DevMat{};
+    if (!up) upm.data = nullptr;
+    lt_status st;
+    if (!direct) {
+        st = launched(ctx, lt::launch_moe_plan(c, ids, ntok, k, gate->m.n_experts, s.plan), "moe plan");
+        if (st != LT_OK) return st;
+    }
+    st = launched(ctx, lt::launch_moe_gate_up(c, gate->m, upm, act, x, ntok, k, ids, direct, s.plan, s.h),
+                  "moe gate_up");
+    if (st != LT_OK) return st;
+    return launched(ctx, lt::launch_moe_down(c, down->m, s.h, ntok, k, ids, w, direct, s.plan, out), "moe down");
+}
+
+lt_status lt_moe_ffn(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, const lt_tensor *down, int act,
+                     const float *dev_x, uint32_t ntok, const uint32_t *dev_ids, const float *dev_w, uint32_t k,
+                     float *dev_out) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    uint64_t F = 0;
+    if ((st = check_experts(ctx, gate, up, down, k, &F)) != LT_OK) return st;
+    if (act != LT_ACT_SILU && act != LT_ACT_GELU_TANH) return fail(ctx, LT_EINVAL, "moe: act %d", act);
+    if (!dev_x || !dev_ids || !dev_w || !dev_out) return fail(ctx, LT_EINVAL, "lt_moe_ffn: null pointer");
+    if (ntok == 0) return LT_OK;
+    const MoeScratch probe = moe_layout(nullptr, ntok, k, gate->m.n_experts, F);
+    if ((st = ensure_scratch(ctx, probe.bytes)) != LT_OK) return st;
+    const MoeScratch s = moe_layout(ctx->scratch, ntok, k, gate->m.n_experts, F);
+    return ffn_impl(ctx, gate, up, down, act, dev_x, ntok, dev_ids, dev_w, k, dev_out, s);
+}
+
+lt_status lt_moe_forward(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *gate, const lt_tensor *up,
+                         const lt_tensor *down, int act, int norm_topk, const float *dev_expert_scale,
+                         const float *dev_x, uint32_t ntok, uint32_t k, float *dev_out, uint32_t *dev_ids,
+                         float *dev_w) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    uint64_t F = 0;
+    if ((st = check_router(ctx, router, k)) != LT_OK) return st;
+    if ((st = check_experts(ctx, gate, up, down, k, &F)) != LT_OK) return st;
+    if (router->m.rows != gate->m.n_experts || router->m.cols != gate->m.cols)
+        return fail(ctx, LT_EINVAL, "lt_moe_forward: router is %llux%llu for %u experts of width %llu",
+                    (unsigned long long)router->m.rows, (unsigned long long)router->m.cols, gate->m.n_experts,
+                    (unsigned long long)gate->m.cols);
+    if (act != LT_ACT_SILU && act != LT_ACT_GELU_TANH) return fail(ctx, LT_EINVAL, "moe: act %d", act);
+    if (!dev_x || !dev_out) return fail(ctx, LT_EINVAL, "lt_moe_forward: null pointer");
+    if (ntok == 0) return LT_OK;
+    const uint32_t E = gate->m.n_experts;
+    const MoeScratch probe = moe_layout(nullptr, ntok, k, E, F);
+    if ((st = ensure_scratch(ctx, probe.bytes)) != LT_OK) return st;
+    const MoeScratch s = moe_layout(ctx->scratch, ntok, k, E, F);
+    uint32_t *ids = dev_ids ? dev_ids : s.ids;
+    float *w = dev_w ? dev_w : s.w;
+    if ((st = route_impl(ctx, router, dev_x, ntok, k, norm_topk, dev_expert_scale, ids, w, s.logits)) != LT_OK)
+        return st;
+    return ffn_impl(ctx, gate, up, down, act, dev_x, ntok, ids, w, k, dev_out, s);
+}
+
+lt_status lt_quant_matvec_host(lt_ctx *ctx, float *out, const lt_tensor *mat, uint32_t expert, const float *vec,
+                               uint64_t rows, uint64_t cols) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!out || !mat || !vec) return fail(ctx, LT_EINVAL, "lt_quant_matvec_host: null pointer");
+    if (rows != mat->m.rows || cols != mat->m.cols)
+        return fail(ctx, LT_EINVAL, "lt_quant_matvec_host: %llux%llu given, tensor is %llux%llu",
+                    (unsigned long long)rows, (unsigned long long)cols, (unsigned long long)mat->m.rows,
+                    (unsigned long long)mat->m.cols);
+    const size_t xb = al256(cols * 4), yb = al256(rows * 4);
+    if ((st = ensure_scratch(ctx, xb + yb)) != LT_OK) return st;
+    if ((st = ensure_pinned(ctx, xb + yb)) != LT_OK) return st;
+    float *dx = (float *)ctx->scratch, *dy = (float *)(ctx->scratch + xb);
+    float *px = (float *)ctx->pinned, *py = (float *)(ctx->pinned + xb);
+    memcpy(px, vec, cols * 4);
+    LT_CUDA(ctx, cudaMemcpyAsync(dx, px, cols * 4, cudaMemcpyHostToDevice, ctx->stream), "H2D");
+    if ((st = lt_qmatvec(ctx, mat, expert, dx, dy, 1)) != LT_OK) return st;
+    LT_CUDA(ctx, cudaMemcpyAsync(py, dy, rows * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H");
+    if ((st = lt_sync(ctx)) != LT_OK) return st;
+    memcpy(out, py, rows * 4);
+    return LT_OK;
+}
+
+lt_status lt_moe_forward_host(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *gate, const lt_tensor *up,
+                              const lt_tensor *down, int act, int norm_topk, const float *expert_scale_host,
+                              const float *x, uint32_t ntok, uint32_t k, float *out, uint32_t *ids, float *w) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!gate || !x || !out) return fail(ctx, LT_EINVAL, "lt_moe_forward_host: null pointer");
+    if (ntok == 0) return LT_OK;
+    const uint64_t d = gate->m.cols;
+    const uint32_t E = gate->m.n_experts;
+    uint64_t F = gate->m.rows;
+    const MoeScratch probe = moe_layout(nullptr, ntok, k, E ? E : 1, F);
+    const size_t xb = al256((size_t)ntok * d * 4), ib = al256((size_t)ntok * k * 4), eb = al256((size_t)E * 4);
+    const size_t io = 2 * xb + 2 * ib + eb;
+    if ((st = ensure_scratch(ctx, probe.bytes + io)) != LT_OK) return st;
+    if ((st = ensure_pinned(ctx, io)) != LT_OK) return st;
+    uint8_t *dbase = ctx->scratch + probe.bytes;
+    float *dx = (float *)dbase, *dout = (float *)(dbase + xb);
+    uint32_t *dids = (uint32_t *)(dbase + 2 * xb);
+    float *dw = (float *)(dbase + 2 * xb + ib);
+    float *dscale = (float *)(dbase + 2 * xb + 2 * ib);
+    uint8_t *hb = ctx->pinned;
+    memcpy(hb, x, (size_t)ntok * d * 4);
+    LT_CUDA(ctx, cudaMemcpyAsync(dx, hb, (size_t)ntok * d * 4, cudaMemcpyHostToDevice, ctx->stream), "H2D x");
+    if (expert_scale_host) {
+        memcpy(hb + 2 * xb + 2 * ib, expert_scale_host, (size_t)E * 4);
+        LT_CUDA(ctx, cudaMemcpyAsync(dscale, hb + 2 * xb + 2 * ib, (size_t)E * 4, cudaMemcpyHostToDevice, ctx->stream),
+                "H2D scale");
+    }
+    // lt_moe_forward places its own scratch at the start of the arena; ours
+    // lives after probe.bytes, so the two do not overlap.
+    st = lt_moe_forward(ctx, router, gate, up, down, act, norm_topk, expert_scale_host ? dscale : nullptr, dx, ntok,
+                        k, dout, dids, dw);
+    if (st != LT_OK) return st;
+    LT_CUDA(ctx, cudaMemcpyAsync(hb + xb, dout, (size_t)ntok * d * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H out");
+    if (ids)
+        LT_CUDA(ctx, cudaMemcpyAsync(hb + 2 * xb, dids, (size_t)ntok * k * 4, cudaMemcpyDeviceToHost, ctx->stream),
+                "D2H ids");
+    if (w)
+        LT_CUDA(ctx, cudaMemcpyAsync(hb + 2 * xb + ib, dw, (size_t)ntok * k * 4, cudaMemcpyDeviceToHost, ctx->stream),
+                "D2H w");
+    if ((st = lt_sync(ctx)) != LT_OK) return st;
+    memcpy(out, hb + xb, (size_t)ntok * d * 4);
+    if (ids) memcpy(ids, hb + 2 * xb, (size_t)ntok * k * 4);
+    if (w) memcpy(w, hb + 2 * xb + ib, (size_t)ntok * k * 4);
+    return LT_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,178 @@
+// lt_common.cuh — device helpers shared by the sm_100a kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define LT_DEVINL __device__ __forceinline__
+
+namespace lt {
+
+// GGUF type codes (src/gguf/types.zig:23-52).
+enum : uint32_t { T_F32 = 0, T_F16 = 1, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14 };
+
+constexpr int kQK = 256;          // K-quant superblock elements
+constexpr int kQ4KBytes = 144;    // src/quant/dequant.zig:155
+constexpr int kQ6KBytes = 210;    // src/quant/dequant.zig:235
+constexpr int kQ8Bytes = 34;      // src/quant/dequant.zig:40
+constexpr int kQ8Elems = 32;
+
+// Elements covered by one "item": the unit of work a lane decodes at once.
+// K-quants: one superblock; Q8_0: eight 34-byte blocks (272 B, 16-B aligned).
+constexpr int kItemElems = 256;
+// x vectors live in shared memory with this per-item stride (floats): the
+// 4-float pad puts consecutive items 4 banks apart, so 8 lanes reading 8
+// different items with 128-bit loads hit 32 distinct banks.
+constexpr int kItemStride = kItemElems + 4;
+
+LT_DEVINL float f16_bits_to_f32(uint32_t h) {
+    return __half2float(__ushort_as_half((unsigned short)(h & 0xffffu)));
+}
+
+// Read-only 128-bit global load (weights are never written while a kernel
+// runs), allocated in L1 only if it streams: weights are touched once.
+LT_DEVINL uint4 ldg_stream(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// Packed fp32x2 arithmetic (sm_100+): two IEEE round-to-nearest results per
+// instruction, identical to the scalar ops lane by lane.
+union f2u {
+    float2 f;
+    unsigned long long u;
+};
+
+LT_DEVINL float2 ffma2(float2 a, float2 b, float2 c) {
+    f2u A, B, C, D;
+    A.f = a; B.f = b; C.f = c;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(D.u) : "l"(A.u), "l"(B.u), "l"(C.u));
+    return D.f;
+}
+
+LT_DEVINL float2 fadd2(float2 a, float2 b) {
+    f2u A, B, D;
+    A.f = a; B.f = b;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(D.u) : "l"(A.u), "l"(B.u));
+    return D.f;
+}
+
+// Exact integer-to-float for a byte in [0,255]: PRMT the byte into the low
+// mantissa of 2^23 (bits 0x4B0000XX == 8388608 + XX); the caller subtracts
+// the bias with one (packed) add.  sel picks byte 0..3 of w.
+LT_DEVINL float byte_biased(uint32_t w, int sel) {
+    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | (uint32_t)sel));
+}
+
+constexpr float kMagic = 8388608.0f;  // 2^23
+
+LT_DEVINL float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Programmatic dependent launch.  Data written by the previous kernel on the
+// stream may only be read after pdl_wait(); kernels that are not launched
+// with the PDL attribute see these as no-ops.
+LT_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+LT_DEVINL void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// ── error reporting ────────────────────────────────────────────────────────
+// Kernels never trap.  A bounded wait that gives up records a code in the
+// context's device error word; the host turns it into LT_ETIMEOUT.
+enum : int { DEV_ERR_NONE = 0, DEV_ERR_TMA_TIMEOUT = 1 };
+
+// ── mbarrier + TMA bulk copy (global -> shared) ────────────────────────────
+LT_DEVINL uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+LT_DEVINL void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+LT_DEVINL void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+LT_DEVINL void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// 1-D bulk copy; dst/src 16-byte aligned, bytes a multiple of 16.
+LT_DEVINL void tma_load_1d(void *dst_smem, const void *src_gmem, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst_smem)),
+        "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+LT_DEVINL bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for `phase` of `bar` with an upper bound of about `limit_ns` of
+// wall time (globaltimer).  Returns false if it gave up.
+LT_DEVINL bool mbar_wait_bounded(uint64_t *bar, uint32_t phase, uint64_t limit_ns) {
+    if (mbar_try_wait(bar, phase)) return true;
+    uint64_t t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (;;) {
+        if (mbar_try_wait(bar, phase)) return true;
+        uint64_t t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (t - t0 > limit_ns) return false;
+    }
+}
+
+LT_DEVINL uint4 lds128(const void *p) {
+    return *reinterpret_cast<const uint4 *>(p);
+}
+LT_DEVINL uint32_t lds32(const void *p) {
+    return *reinterpret_cast<const uint32_t *>(p);
+}
+
+// ── integer dot products ───────────────────────────────────────────────────
+// d = c + a.s16[0]*b.byte[0|2] + a.s16[1]*b.byte[1|3]  (b bytes unsigned)
+LT_DEVINL int dp2a_lo_su(int a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+LT_DEVINL int dp2a_hi_su(int a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// Same with signed bytes (Q8_0 quants).
+LT_DEVINL int dp2a_lo_ss(int a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.lo.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+LT_DEVINL int dp2a_hi_ss(int a, uint32_t b, int c) {
+    int d;
+    asm("dp2a.hi.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Small non-negative integer held in byte `sel` of w, as an exact float.
+LT_DEVINL float byte_to_f32(uint32_t w, int sel) {
+    return byte_biased(w, sel) - kMagic;
+}
+
+}  // namespace lt

@@ -1,0 +1,74 @@
+// lt_internal.h — kernel launchers shared between the kernel files and the
+// C ABI in lt_api.cu.  Not part of the public interface.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lt {
+
+// A weight matrix as the kernels see it: GGUF rows at a 16-byte pitch.
+struct DevMat {
+    const uint8_t *data;
+    uint32_t type;
+    uint64_t rows;       // rows per expert (or all rows for 2-D)
+    uint64_t cols;
+    uint64_t row_bytes;
+    uint64_t pitch;
+    uint32_t n_experts;  // 0 for 2-D
+};
+
+// Routing plan built on the device for the grouped expert kernels.
+struct MoePlan {
+    uint32_t *n_active;   // [1]    experts with at least one token
+    uint32_t *act_e;      // [E]    active expert ids, ascending
+    uint32_t *act_off;    // [E]    first position of each active expert
+    uint32_t *act_cnt;    // [E]    number of (token, slot) pairs routed to it
+    uint32_t *pos_pair;   // [T*k]  position -> pair index (token*k + slot)
+    uint32_t *pair_pos;   // [T*k]  pair index -> position
+};
+
+struct LaunchCfg {
+    cudaStream_t stream;
+    bool pdl;        // launch with programmatic stream serialization
+    int *dev_err;    // device error word (DEV_ERR_*)
+    int num_sms;
+};
+
+constexpr int kRouterMaxE = 256;  // experts per router (top-k runs in one warp)
+
+bool type_supported(uint32_t t);
+uint64_t row_bytes_of(uint32_t t, uint64_t cols);
+uint32_t block_elems_of(uint32_t t);
+
+cudaError_t launch_dequant(const LaunchCfg &c, const DevMat &m, uint64_t row0, uint64_t nrows,
+                           float *out);
+cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert, const float *x,
+                           float *y, uint32_t ntok);
+cudaError_t launch_rmsnorm(const LaunchCfg &c, const float *x, const float *w, float eps, uint32_t n,
+                           uint32_t ntok, float *y);
+cudaError_t launch_softmax(const LaunchCfg &c, float *x, uint32_t n, uint32_t ntok);
+cudaError_t launch_argmax(const LaunchCfg &c, const float *x, uint32_t n, uint32_t ntok,
+                          uint32_t *idx, float *scratch_val, uint32_t *scratch_idx,
+                          uint32_t *counters);
+// Router over f32 weights [E][cols]; logits scratch [ntok][E]; counters
+// zero-initialised, one per token group (reset by the kernel).
+cudaError_t launch_router(const LaunchCfg &c, const float *w, uint32_t E, uint32_t cols,
+                          const float *x, uint32_t ntok, uint32_t k, int norm_topk,
+                          const float *escale, uint32_t *ids, float *wout, float *logits,
+                          uint32_t *counters);
+uint32_t router_token_groups(uint32_t ntok);
+
+cudaError_t launch_moe_plan(const LaunchCfg &c, const uint32_t *ids, uint32_t ntok, uint32_t k,
+                            uint32_t E, const MoePlan &p);
+// h[pos][F] = act(gate_e . x_tok) * (up_e . x_tok).  direct: ntok == 1 and
+// ids are the plan (position = slot).  up.data == nullptr: fused gate_up.
+cudaError_t launch_moe_gate_up(const LaunchCfg &c, const DevMat &gate, const DevMat &up, int act,
+                               const float *x, uint32_t ntok, uint32_t k, const uint32_t *ids,
+                               bool direct, const MoePlan &p, float *h);
+// out[t][d] = sum_s w[t][s] * (down_e(s) . h[pos(t,s)])
+cudaError_t launch_moe_down(const LaunchCfg &c, const DevMat &down, const float *h, uint32_t ntok,
+                            uint32_t k, const uint32_t *ids, const float *w, bool direct,
+                            const MoePlan &p, float *out);
+
+}  // namespace lt

@@ -1,0 +1,112 @@
+"""Seeded synthetic GGUF tensors with the value distributions of the benchmark configs.
+
+Every generator takes a ``numpy.random.Generator`` (PCG64) and returns raw GGUF
+bytes in the reference's block layouts (src/quant/dequant.zig):
+
+* Q4_K (144 B / 256): f16 d ~ U(1e-3, 4e-3), f16 dmin ~ U(0, 2e-3), uniform
+  6-bit scales/mins and uniform nibbles (uniform random bytes give both).
+* Q6_K (210 B / 256): uniform ql/qh bytes, uniform int8 scales, f16 d ~ U(1e-3, 4e-3).
+* Q8_0 (34 B / 32): f16 d = 0.02/127 * U(0.5, 1.5), int8 quants uniform in [-127, 127].
+* router weights f32 N(0, 0.02); hidden states f32 N(0, 1).
+
+``stamp_d`` reproduces the reference's GPU fuzz generator instead: every f16
+scale field set to 0x21CD (~0.012) over random bytes (src/gpu/matvec.zig:4568-4586).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+F32, F16, Q8_0, Q4_K, Q6_K = 0, 1, 8, 12, 14
+BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
+
+CONFIG_SEED_BASE = 0x11A70000
+
+
+def config_seed(index: int) -> int:
+    return CONFIG_SEED_BASE + index
+
+
+def _f16_bytes(vals: np.ndarray) -> np.ndarray:
+    return vals.astype(np.float16).view(np.uint8).reshape(-1, 2)
+
+
+def q4k_blocks(rng: np.random.Generator, n: int, stamp_d: bool = False) -> np.ndarray:
+    b = rng.integers(0, 256, size=(n, 144), dtype=np.uint8)
+    if stamp_d:
+        b[:, 0], b[:, 1], b[:, 2], b[:, 3] = 0xCD, 0x21, 0xCD, 0x21
+    else:
+        b[:, 0:2] = _f16_bytes(rng.uniform(1e-3, 4e-3, n))
+        b[:, 2:4] = _f16_bytes(rng.uniform(0.0, 2e-3, n))
+    return b
+
+
+def q6k_blocks(rng: np.random.Generator, n: int, stamp_d: bool = False) -> np.ndarray:
+    b = rng.integers(0, 256, size=(n, 210), dtype=np.uint8)
+    if stamp_d:
+        b[:, 208], b[:, 209] = 0xCD, 0x21
+    else:
+        b[:, 208:210] = _f16_bytes(rng.uniform(1e-3, 4e-3, n))
+    return b
+
+
+def q8_0_blocks(rng: np.random.Generator, n: int, stamp_d: bool = False) -> np.ndarray:
+    b = np.empty((n, 34), dtype=np.uint8)
+    if stamp_d:
+        b[:, 2:] = rng.integers(0, 256, size=(n, 32), dtype=np.uint8)
+        b[:, 0], b[:, 1] = 0xCD, 0x21
+    else:
+        b[:, 2:] = rng.integers(-127, 128, size=(n, 32), dtype=np.int8).view(np.uint8)
+        b[:, 0:2] = _f16_bytes(0.02 / 127.0 * rng.uniform(0.5, 1.5, n))
+    return b
+
+
+def matrix(rng: np.random.Generator, ggml_type: int, rows: int, cols: int, stamp_d: bool = False) -> np.ndarray:
+    """rows x cols tensor as GGUF bytes, shape [rows, rowBytes]."""
+    elems, nbytes = BLOCK[ggml_type]
+    if cols % elems:
+        raise ValueError(f"cols {cols} not a multiple of {elems}")
+    nb = rows * (cols // elems)
+    if ggml_type == Q4_K:
+        blk = q4k_blocks(rng, nb, stamp_d)
+    elif ggml_type == Q6_K:
+        blk = q6k_blocks(rng, nb, stamp_d)
+    elif ggml_type == Q8_0:
+        blk = q8_0_blocks(rng, nb, stamp_d)
+    elif ggml_type == F32:
+        blk = rng.normal(0.0, 0.02, size=(rows, cols)).astype(np.float32).view(np.uint8)
+    elif ggml_type == F16:
+        blk = rng.normal(0.0, 0.02, size=(rows, cols)).astype(np.float16).view(np.uint8)
+    else:
+        raise ValueError(ggml_type)
+    return np.ascontiguousarray(blk).reshape(rows, (cols // elems) * nbytes)
+
+
+def router_weights(rng: np.random.Generator, n_experts: int, d_model: int) -> np.ndarray:
+    return rng.normal(0.0, 0.02, size=(n_experts, d_model)).astype(np.float32)
+
+
+def hidden(rng: np.random.Generator, n_tok: int, d_model: int) -> np.ndarray:
+    return rng.normal(0.0, 1.0, size=(n_tok, d_model)).astype(np.float32)
+
+
+class MoeLayer:
+    """One MoE FFN layer of the config-1 shape (router + SwiGLU experts)."""
+
+    def __init__(self, rng: np.random.Generator, d_model: int = 2048, n_experts: int = 128, d_expert: int = 768,
+                 gate_type: int = Q4_K, down_type: int = Q4_K, fused: bool = False):
+        self.d_model, self.n_experts, self.d_expert = d_model, n_experts, d_expert
+        self.gate_type, self.down_type, self.fused = gate_type, down_type, fused
+        self.router = router_weights(rng, n_experts, d_model)
+        if fused:
+            self.gate = matrix(rng, gate_type, n_experts * 2 * d_expert, d_model)
+            self.up = None
+        else:
+            self.gate = matrix(rng, gate_type, n_experts * d_expert, d_model)
+            self.up = matrix(rng, gate_type, n_experts * d_expert, d_model)
+        self.down = matrix(rng, down_type, n_experts * d_model, d_expert)
+
+    @property
+    def expert_bytes(self) -> int:
+        """Weight bytes one selected expert streams (gate + up + down)."""
+        e = self.n_experts
+        return (self.gate.nbytes + (self.up.nbytes if self.up is not None else 0) + self.down.nbytes) // e

@@ -1,0 +1,713 @@
+/*
+ * oracle.c — CPU restatement of llmtoy-zig's quantized MoE forward path.
+ *
+ * TEST INFRASTRUCTURE ONLY: the parity checker for the CUDA path and the
+ * timed CPU baseline (bench.py's cpu_baseline leg and --impl reference arm).
+ * The product never links or calls this file.
+ *
+ * Build: oracle/Makefile (-O3 -ffp-contract=off, so a*b+c always rounds
+ * twice, exactly like Zig's strict float mode).  Each function names the
+ * reference function it restates as path:line within llmtoy-zig.
+ */
+#include "oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ── f16 ──────────────────────────────────────────────────────────────────── */
+
+/* src/quant/dequant.zig:302-305 — @floatCast of an f16 is exact. */
+float orc_f16_to_f32(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h >> 15) << 31;
+    const uint32_t exp = (h >> 10) & 0x1fu;
+    const uint32_t mant = h & 0x3ffu;
+    uint32_t bits;
+    if (exp == 0) {
+        /* zero or subnormal: value = mant * 2^-24, exactly representable */
+        float v = ldexpf((float)mant, -24);
+        memcpy(&bits, &v, 4);
+        bits |= sign;
+    } else if (exp == 31) {
+        bits = sign | 0x7f800000u | (mant << 13);
+    } else {
+        bits = sign | ((exp - 15u + 127u) << 23) | (mant << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+uint16_t orc_f32_to_f16(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    const uint16_t sign = (uint16_t)((x >> 16) & 0x8000u);
+    const uint32_t ax = x & 0x7fffffffu;
+    if (ax >= 0x7f800000u) return sign | 0x7c00u | (ax > 0x7f800000u ? 0x200u : 0u);
+    if (ax >= 0x477ff000u) return sign | 0x7c00u; /* rounds to inf */
+    if (ax < 0x38800000u) {                        /* f16 subnormal or zero */
+        float a;
+        memcpy(&a, &ax, 4);
+        /* a * 2^24 rounded to nearest even integer = subnormal mantissa */
+        float m = nearbyintf(ldexpf(a, 24));
+        return sign | (uint16_t)m;
+    }
+    uint32_t mant = ax & 0x7fffffu;
+    uint32_t e = (ax >> 23) - 127u + 15u;
+    uint32_t r = (e << 10) | (mant >> 13);
+    const uint32_t rem = mant & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (r & 1u))) r += 1u;
+    return sign | (uint16_t)r;
+}
+
+static inline float f16_at(const uint8_t *p) {
+    return orc_f16_to_f32((uint16_t)(p[0] | (p[1] << 8)));
+}
+
+/* ── block codecs (src/quant/dequant.zig) ──────────────────────────────────── */
+
+#define Q8_0_BLOCK_ELEMS 32
+#define Q8_0_BLOCK_BYTES 34
+#define QK_K 256
+#define Q4_K_BLOCK_BYTES 144
+#define Q6_K_BLOCK_BYTES 210
+
+/* dequant.zig:17-20 */
+void orc_dequant_f32(const uint8_t *data, float *out, size_t n) { memcpy(out, data, n * 4); }
+
+/* dequant.zig:24-29 */
+void orc_dequant_f16(const uint8_t *data, float *out, size_t n) {
+    for (size_t i = 0; i < n; i++) out[i] = f16_at(data + 2 * i);
+}
+
+/* dequant.zig:42-52: val = d * q */
+void orc_dequant_q8_0(const uint8_t *data, float *out, size_t n) {
+    const size_t nb = n / Q8_0_BLOCK_ELEMS;
+    for (size_t b = 0; b < nb; b++) {
+        const uint8_t *blk = data + b * Q8_0_BLOCK_BYTES;
+        const float d = f16_at(blk);
+        for (size_t i = 0; i < Q8_0_BLOCK_ELEMS; i++)
+            out[b * Q8_0_BLOCK_ELEMS + i] = d * (float)(int8_t)blk[2 + i];
+    }
+}
+
+/* dequant.zig:59-78: per block, 8 lanes x 4 groups (mul then add), ordered
+ * lane reduction, times d, accumulated block by block. */
+float orc_dot_q8_0(const uint8_t *data, const float *vec, size_t n) {
+    const size_t nb = n / Q8_0_BLOCK_ELEMS;
+    float total = 0.0f;
+    for (size_t b = 0; b < nb; b++) {
+        const uint8_t *blk = data + b * Q8_0_BLOCK_BYTES;
+        const float d = f16_at(blk);
+        const int8_t *qs = (const int8_t *)(blk + 2);
+        const float *v = vec + b * Q8_0_BLOCK_ELEMS;
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int j = 0; j < 4; j++)
+            for (int l = 0; l < 8; l++) acc[l] += (float)qs[j * 8 + l] * v[j * 8 + l];
+        float r = -0.0f;
+        for (int l = 0; l < 8; l++) r += acc[l];
+        total += r * d;
+    }
+    return total;
+}
+
+/* dequant.zig:291-300 (get_scale_min_k4) */
+static inline void scale_min(int j, const uint8_t *s, uint8_t *sc, uint8_t *mn) {
+    if (j < 4) {
+        *sc = s[j] & 0x3f;
+        *mn = s[j + 4] & 0x3f;
+    } else {
+        *sc = (uint8_t)((s[j + 4] & 0x0f) | ((s[j - 4] >> 6) << 4));
+        *mn = (uint8_t)((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
+    }
+}
+
+/* dequant.zig:157-187: out = (d*sc)*q - dmin*mn, two roundings */
+void orc_dequant_q4_k(const uint8_t *data, float *out, size_t n) {
+    const size_t nb = n / QK_K;
+    for (size_t b = 0; b < nb; b++) {
+        const uint8_t *blk = data + b * Q4_K_BLOCK_BYTES;
+        const float d = f16_at(blk);
+        const float dmin = f16_at(blk + 2);
+        const uint8_t *scales = blk + 4;
+        const uint8_t *qs = blk + 16;
+        int sub = 0;
+        for (int chunk = 0; chunk < QK_K; chunk += 64) {
+            uint8_t sc1, mn1, sc2, mn2;
+            scale_min(sub, scales, &sc1, &mn1);
+            scale_min(sub + 1, scales, &sc2, &mn2);
+            sub += 2;
+            const float d1 = d * (float)sc1, m1 = dmin * (float)mn1;
+            const float d2 = d * (float)sc2, m2 = dmin * (float)mn2;
+            for (int i = 0; i < 32; i++) {
+                const uint8_t byte = qs[chunk / 2 + i];
+                out[b * QK_K + chunk + i] = d1 * (float)(byte & 0x0f) - m1;
+                out[b * QK_K + chunk + 32 + i] = d2 * (float)(byte >> 4) - m2;
+            }
+        }
+    }
+}
+
+/* dequant.zig:282-287 */
+static inline float q6val(uint8_t ql_byte, uint8_t qh_byte, int qh_shift, int ql_shift) {
+    const uint8_t lo4 = (ql_byte >> ql_shift) & 0x0f;
+    const uint8_t hi2 = (qh_byte >> qh_shift) & 0x03;
+    const uint8_t raw = (uint8_t)(lo4 | (hi2 << 4));
+    return (float)((int)raw - 32);
+}
+
+/* dequant.zig:237-277: out = (d * sc_i8) * (q6 - 32) */
+void orc_dequant_q6_k(const uint8_t *data, float *out, size_t n) {
+    const size_t nb = n / QK_K;
+    for (size_t b = 0; b < nb; b++) {
+        const uint8_t *blk = data + b * Q6_K_BLOCK_BYTES;
+        const uint8_t *ql = blk, *qh = blk + 128;
+        const int8_t *sc = (const int8_t *)(blk + 192);
+        const float d = f16_at(blk + 208);
+        int ql_off = 0, qh_off = 0, sc_off = 0;
+        for (int chunk = 0; chunk < QK_K; chunk += 128, ql_off += 64, qh_off += 32, sc_off += 8) {
+            for (int l = 0; l < 32; l++) {
+                const int is = l / 16;
+                const float q1 = q6val(ql[ql_off + l], qh[qh_off + l], 0, 0);
+                const float q2 = q6val(ql[ql_off + l + 32], qh[qh_off + l], 2, 0);
+                const float q3 = q6val(ql[ql_off + l], qh[qh_off + l], 4, 4);
+                const float q4 = q6val(ql[ql_off + l + 32], qh[qh_off + l], 6, 4);
+                const float s0 = d * (float)sc[sc_off + is + 0];
+                const float s2 = d * (float)sc[sc_off + is + 2];
+                const float s4 = d * (float)sc[sc_off + is + 4];
+                const float s6 = d * (float)sc[sc_off + is + 6];
+                const size_t base = b * QK_K + (size_t)chunk + (size_t)l;
+                out[base + 0] = s0 * q1;
+                out[base + 32] = s2 * q2;
+                out[base + 64] = s4 * q3;
+                out[base + 96] = s6 * q4;
+            }
+        }
+    }
+}
+
+/* math.zig:194-208 */
+size_t orc_row_bytes(uint32_t type, size_t cols) {
+    switch (type) {
+    case ORC_F32: return cols * 4;
+    case ORC_F16: return cols * 2;
+    case ORC_Q8_0: return (cols / Q8_0_BLOCK_ELEMS) * Q8_0_BLOCK_BYTES;
+    case ORC_Q4_K: return (cols / QK_K) * Q4_K_BLOCK_BYTES;
+    case ORC_Q6_K: return (cols / QK_K) * Q6_K_BLOCK_BYTES;
+    default: return 0;
+    }
+}
+
+/* math.zig:211-225 */
+int orc_dequant_row(const uint8_t *data, float *out, size_t n, uint32_t type) {
+    switch (type) {
+    case ORC_F32: orc_dequant_f32(data, out, n); return 0;
+    case ORC_F16: orc_dequant_f16(data, out, n); return 0;
+    case ORC_Q8_0: orc_dequant_q8_0(data, out, n); return 0;
+    case ORC_Q4_K: orc_dequant_q4_k(data, out, n); return 0;
+    case ORC_Q6_K: orc_dequant_q6_k(data, out, n); return 0;
+    default: return -1;
+    }
+}
+
+/* ── src/ops/math.zig ──────────────────────────────────────────────────────── */
+
+/* math.zig:8-17 */
+void orc_matvec(float *out, const float *mat, const float *vec, size_t rows, size_t cols) {
+    for (size_t i = 0; i < rows; i++) {
+        float sum = 0.0f;
+        for (size_t j = 0; j < cols; j++) sum += mat[i * cols + j] * vec[j];
+        out[i] = sum;
+    }
+}
+
+/* math.zig:96-116: 4 accumulators x 8 lanes over 32-element strides,
+ * (a0+a1)+(a2+a3), an 8-wide tail, ordered lane reduction, scalar tail. */
+float orc_dotf32(const float *a, const float *b, size_t n) {
+    float acc0[8] = {0}, acc1[8] = {0}, acc2[8] = {0}, acc3[8] = {0};
+    size_t i = 0;
+    for (; i + 32 <= n; i += 32) {
+        for (int l = 0; l < 8; l++) acc0[l] += a[i + l] * b[i + l];
+        for (int l = 0; l < 8; l++) acc1[l] += a[i + 8 + l] * b[i + 8 + l];
+        for (int l = 0; l < 8; l++) acc2[l] += a[i + 16 + l] * b[i + 16 + l];
+        for (int l = 0; l < 8; l++) acc3[l] += a[i + 24 + l] * b[i + 24 + l];
+    }
+    float acc[8];
+    for (int l = 0; l < 8; l++) acc[l] = (acc0[l] + acc1[l]) + (acc2[l] + acc3[l]);
+    for (; i + 8 <= n; i += 8)
+        for (int l = 0; l < 8; l++) acc[l] += a[i + l] * b[i + l];
+    float sum = -0.0f;
+    for (int l = 0; l < 8; l++) sum += acc[l];
+    for (; i < n; i++) sum += a[i] * b[i];
+    return sum;
+}
+
+/* math.zig:133-171 (plus RowJob.run :243-269, which is the same loop) */
+static int quant_matvec_rows(float *out, const uint8_t *mat, uint32_t type, const float *vec,
+                             size_t row_start, size_t n_rows, size_t cols, float *row_buf) {
+    const size_t rb = orc_row_bytes(type, cols);
+    if (rb == 0) return -1;
+    for (size_t i = 0; i < n_rows; i++) {
+        const uint8_t *row = mat + (row_start + i) * rb;
+        if (type == ORC_Q8_0) {
+            out[i] = orc_dot_q8_0(row, vec, cols);
+            continue;
+        }
+        if (type == ORC_F32 && ((uintptr_t)row % 4) == 0) {
+            out[i] = orc_dotf32((const float *)row, vec, cols);
+            continue;
+        }
+        orc_dequant_row(row, row_buf, cols, type);
+        out[i] = orc_dotf32(row_buf, vec, cols);
+    }
+    return 0;
+}
+
+int orc_quant_matvec(float *out, const uint8_t *mat, uint32_t type, const float *vec,
+                     size_t rows, size_t cols, float *row_buf) {
+    return quant_matvec_rows(out, mat, type, vec, 0, rows, cols, row_buf);
+}
+
+/* math.zig:20-26 */
+void orc_rmsnorm(float *out, const float *x, const float *w, size_t n, float eps) {
+    float ss = 0.0f;
+    for (size_t i = 0; i < n; i++) ss += x[i] * x[i];
+    const float rms_inv = 1.0f / sqrtf(ss / (float)n + eps);
+    for (size_t i = 0; i < n; i++) out[i] = x[i] * rms_inv * w[i];
+}
+
+/* math.zig:43-48 */
+void orc_rmsnorm_raw(float *out, const float *x, size_t n, float eps) {
+    float ss = 0.0f;
+    for (size_t i = 0; i < n; i++) ss += x[i] * x[i];
+    const float rms_inv = 1.0f / sqrtf(ss / (float)n + eps);
+    for (size_t i = 0; i < n; i++) out[i] = x[i] * rms_inv;
+}
+
+/* math.zig:29-35 */
+void orc_softmax(float *x, size_t n) {
+    float max = x[0];
+    for (size_t i = 1; i < n; i++)
+        if (x[i] > max) max = x[i];
+    float sum = 0.0f;
+    for (size_t i = 0; i < n; i++) {
+        x[i] = expf(x[i] - max);
+        sum += x[i];
+    }
+    for (size_t i = 0; i < n; i++) x[i] /= sum;
+}
+
+/* math.zig:38-40 */
+float orc_silu(float x) { return x / (1.0f + expf(-x)); }
+
+/* math.zig:85-88 */
+float orc_gelu(float x) {
+    const float c = 0.7978845608028654f;
+    return 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));
+}
+
+/* ── worker pool (src/ops/thread_pool.zig:15-112) ──────────────────────────── */
+
+typedef void (*orc_func)(void *);
+typedef struct { orc_func func; void *ctx; } orc_entry;
+
+struct orc_pool {
+    pthread_t *threads;
+    int n_threads;
+    orc_entry *queue;
+    size_t cap, head, tail, pending;
+    int shutdown;
+    pthread_mutex_t mutex;
+    pthread_cond_t work_ready, all_done, not_full;
+};
+
+static void *worker_loop(void *arg) {
+    orc_pool *p = (orc_pool *)arg;
+    pthread_mutex_lock(&p->mutex);
+    for (;;) {
+        while (p->head == p->tail && !p->shutdown) pthread_cond_wait(&p->work_ready, &p->mutex);
+        if (p->shutdown && p->head == p->tail) {
+            pthread_mutex_unlock(&p->mutex);
+            return NULL;
+        }
+        orc_entry e = p->queue[p->tail % p->cap];
+        p->tail++;
+        pthread_cond_signal(&p->not_full);
+        pthread_mutex_unlock(&p->mutex);
+        e.func(e.ctx);
+        pthread_mutex_lock(&p->mutex);
+        p->pending--;
+        if (p->pending == 0) pthread_cond_signal(&p->all_done);
+    }
+}
+
+orc_pool *orc_pool_create(int n) {
+    if (n < 1) n = 1;
+    orc_pool *p = (orc_pool *)calloc(1, sizeof(*p));
+    if (!p) return NULL;
+    p->n_threads = n;
+    p->cap = (size_t)(n * 4 > 64 ? n * 4 : 64);
+    p->queue = (orc_entry *)calloc(p->cap, sizeof(orc_entry));
+    p->threads = (pthread_t *)calloc((size_t)n, sizeof(pthread_t));
+    pthread_mutex_init(&p->mutex, NULL);
+    pthread_cond_init(&p->work_ready, NULL);
+    pthread_cond_init(&p->all_done, NULL);
+    pthread_cond_init(&p->not_full, NULL);
+    for (int i = 0; i < n; i++) pthread_create(&p->threads[i], NULL, worker_loop, p);
+    return p;
+}
+
+void orc_pool_destroy(orc_pool *p) {
+    if (!p) return;
+    pthread_mutex_lock(&p->mutex);
+    p->shutdown = 1;
+    pthread_cond_broadcast(&p->work_ready);
+    pthread_mutex_unlock(&p->mutex);
+    for (int i = 0; i < p->n_threads; i++) pthread_join(p->threads[i], NULL);
+    free(p->threads);
+    free(p->queue);
+    free(p);
+}
+
+int orc_pool_threads(const orc_pool *p) { return p ? p->n_threads : 1; }
+
+static void pool_submit(orc_pool *p, orc_func f, void *ctx) {
+    pthread_mutex_lock(&p->mutex);
+    while (p->head - p->tail >= p->cap) pthread_cond_wait(&p->not_full, &p->mutex);
+    p->queue[p->head % p->cap] = (orc_entry){f, ctx};
+    p->head++;
+    p->pending++;
+    pthread_cond_signal(&p->work_ready);
+    pthread_mutex_unlock(&p->mutex);
+}
+
+static void pool_wait(orc_pool *p) {
+    pthread_mutex_lock(&p->mutex);
+    while (p->pending > 0) pthread_cond_wait(&p->all_done, &p->mutex);
+    pthread_mutex_unlock(&p->mutex);
+}
+
+/* ── quantMatvecPar (math.zig:227-320) ─────────────────────────────────────── */
+
+typedef struct {
+    const uint8_t *mat;
+    uint32_t type;
+    const float *vec;
+    float *out;
+    float *row_buf;
+    size_t row_start, n_rows, cols;
+} row_job;
+
+static void row_job_run(void *ctx) {
+    row_job *j = (row_job *)ctx;
+    quant_matvec_rows(j->out, j->mat, j->type, j->vec, j->row_start, j->n_rows, j->cols, j->row_buf);
+}
+
+int orc_quant_matvec_par(float *out, const uint8_t *mat, uint32_t type, const float *vec,
+                         size_t rows, size_t cols, float *scratch, orc_pool *pool) {
+    if (orc_row_bytes(type, cols) == 0) return -1;
+    const size_t min_rows = 64;
+    const size_t n = (size_t)orc_pool_threads(pool);
+    size_t nt = (rows + min_rows - 1) / min_rows;
+    if (n < nt) nt = n;
+    if (nt <= 1 || pool == NULL) return orc_quant_matvec(out, mat, type, vec, rows, cols, scratch);
+    if (nt > 64) nt = 64;
+    row_job jobs[64];
+    const size_t base = rows / nt, extra = rows % nt;
+    size_t row = 0;
+    for (size_t t = 0; t < nt; t++) {
+        const size_t n_rows = base + (t < extra ? 1 : 0);
+        jobs[t] = (row_job){mat, type, vec, out + row, scratch + t * cols, row, n_rows, cols};
+        pool_submit(pool, row_job_run, &jobs[t]);
+        row += n_rows;
+    }
+    pool_wait(pool);
+    return 0;
+}
+
+/* ── router (src/model/gemma4/forward.zig) ─────────────────────────────────── */
+
+/* forward.zig:598-629: one pass, online softmax denominator + insertion top-k
+ * with strict '>' so the lowest index wins ties. */
+orc_softmax_stats orc_topk_with_softmax_stats(const float *scores, size_t n, uint32_t *out, size_t k) {
+    float max = scores[0];
+    float exp_sum = 0.0f;
+    size_t filled = 0;
+    for (size_t j = 0; j < n; j++) {
+        const float s = scores[j];
+        if (s > max) {
+            exp_sum = exp_sum * expf(max - s) + 1.0f;
+            max = s;
+        } else {
+            exp_sum += expf(s - max);
+        }
+        if (filled < k) {
+            size_t pos = filled++;
+            while (pos > 0 && s > scores[out[pos - 1]]) {
+                out[pos] = out[pos - 1];
+                pos--;
+            }
+            out[pos] = (uint32_t)j;
+        } else if (s > scores[out[k - 1]]) {
+            size_t pos = k - 1;
+            while (pos > 0 && s > scores[out[pos - 1]]) {
+                out[pos] = out[pos - 1];
+                pos--;
+            }
+            out[pos] = (uint32_t)j;
+        }
+    }
+    return (orc_softmax_stats){max, exp_sum};
+}
+
+/* forward.zig:637-643 */
+void orc_softmax_topk(float *scores, size_t n, uint32_t *out, size_t k) {
+    const orc_softmax_stats st = orc_topk_with_softmax_stats(scores, n, out, k);
+    for (size_t i = 0; i < k; i++) scores[out[i]] = expf(scores[out[i]] - st.max) / st.exp_sum;
+}
+
+/* forward.zig:748-767 */
+static void insert_topk_index(uint32_t *out, float *sel, size_t k, size_t *filled, uint32_t idx, float score) {
+    if (*filled < k) {
+        size_t pos = (*filled)++;
+        while (pos > 0 && score > sel[pos - 1]) {
+            sel[pos] = sel[pos - 1];
+            out[pos] = out[pos - 1];
+            pos--;
+        }
+        sel[pos] = score;
+        out[pos] = idx;
+    } else if (score > sel[k - 1]) {
+        size_t pos = k - 1;
+        while (pos > 0 && score > sel[pos - 1]) {
+            sel[pos] = sel[pos - 1];
+            out[pos] = out[pos - 1];
+            pos--;
+        }
+        sel[pos] = score;
+        out[pos] = idx;
+    }
+}
+
+/* forward.zig:672-712: streamed router logits (dotf32 per expert row). */
+orc_softmax_stats orc_topk_matvec_f32(const float *w, const float *vec, size_t rows, size_t cols,
+                                      uint32_t *out, float *selected, size_t k) {
+    float max = -INFINITY;
+    float exp_sum = 0.0f;
+    size_t filled = 0;
+    for (size_t j = 0; j < rows; j++) {
+        const float score = orc_dotf32(w + j * cols, vec, cols);
+        if (score > max) {
+            exp_sum = exp_sum * expf(max - score) + 1.0f;
+            max = score;
+        } else {
+            exp_sum += expf(score - max);
+        }
+        insert_topk_index(out, selected, k, &filled, (uint32_t)j, score);
+    }
+    return (orc_softmax_stats){max, exp_sum};
+}
+
+typedef struct {
+    const float *w, *vec;
+    size_t row_start, rows, cols, k;
+    uint32_t top_idx[16];
+    float top_scores[16];
+    orc_softmax_stats stats;
+} router_job;
+
+/* forward.zig:730-745 */
+static void router_job_run(void *ctx) {
+    router_job *j = (router_job *)ctx;
+    uint32_t local_idx[16];
+    float local_scores[16];
+    j->stats = orc_topk_matvec_f32(j->w + j->row_start * j->cols, j->vec, j->rows, j->cols,
+                                   local_idx, local_scores, j->k);
+    for (size_t i = 0; i < j->k; i++) {
+        j->top_idx[i] = (uint32_t)j->row_start + local_idx[i];
+        j->top_scores[i] = local_scores[i];
+    }
+}
+
+/* forward.zig:769-821: row ranges per job, merged in ascending row order. */
+orc_softmax_stats orc_topk_matvec_f32_par(const float *w, const float *vec, size_t rows, size_t cols,
+                                          uint32_t *out, float *selected, size_t k, orc_pool *pool) {
+    const size_t min_rows_per_job = 16;
+    size_t nt = (rows + min_rows_per_job - 1) / min_rows_per_job;
+    const size_t n = (size_t)orc_pool_threads(pool);
+    if (n < nt) nt = n;
+    if (nt <= 1 || pool == NULL) return orc_topk_matvec_f32(w, vec, rows, cols, out, selected, k);
+    if (nt > 64) nt = 64;
+    router_job jobs[64];
+    const size_t base = rows / nt, extra = rows % nt;
+    size_t row = 0;
+    for (size_t t = 0; t < nt; t++) {
+        const size_t n_rows = base + (t < extra ? 1 : 0);
+        memset(&jobs[t], 0, sizeof(jobs[t]));
+        jobs[t].w = w;
+        jobs[t].vec = vec;
+        jobs[t].row_start = row;
+        jobs[t].rows = n_rows;
+        jobs[t].cols = cols;
+        jobs[t].k = k;
+        pool_submit(pool, router_job_run, &jobs[t]);
+        row += n_rows;
+    }
+    pool_wait(pool);
+
+    float max = -INFINITY;
+    float exp_sum = 0.0f;
+    size_t filled = 0;
+    for (size_t t = 0; t < nt; t++) {
+        const router_job *j = &jobs[t];
+        if (j->stats.max > max) {
+            exp_sum = exp_sum * expf(max - j->stats.max) + j->stats.exp_sum;
+            max = j->stats.max;
+        } else {
+            exp_sum += j->stats.exp_sum * expf(j->stats.max - max);
+        }
+        for (size_t i = 0; i < k; i++) insert_topk_index(out, selected, k, &filled, j->top_idx[i], j->top_scores[i]);
+    }
+    return (orc_softmax_stats){max, exp_sum};
+}
+
+/* forward.zig:648-668 (aligned f32 router weights branch) */
+void orc_router_topk_softmax(float *scores, uint32_t *out, size_t k, const float *router_w,
+                             size_t rows, size_t cols, const float *router_in, orc_pool *pool) {
+    float selected[16];
+    const orc_softmax_stats st = orc_topk_matvec_f32_par(router_w, router_in, rows, cols, out, selected, k, pool);
+    for (size_t i = 0; i < k; i++) scores[out[i]] = expf(selected[i] - st.max) / st.exp_sum;
+}
+
+/* src/ops/moe.zig:80-91 */
+void orc_moe_topk(const float *scores, size_t n, uint32_t *out, size_t k) {
+    for (size_t i = 0; i < k; i++) {
+        size_t best = 0;
+        float best_val = -INFINITY;
+        for (size_t j = 0; j < n; j++) {
+            int already = 0;
+            for (size_t p = 0; p < i; p++)
+                if (out[p] == j) { already = 1; break; }
+            if (!already && scores[j] > best_val) {
+                best_val = scores[j];
+                best = j;
+            }
+        }
+        out[i] = (uint32_t)best;
+    }
+}
+
+/* ── MoE FFN ──────────────────────────────────────────────────────────────── */
+
+static size_t max_sz(size_t a, size_t b) { return a > b ? a : b; }
+
+/* src/ops/moe.zig:18-77 */
+int orc_moe_forward(float *out, const float *router_w, size_t n_experts,
+                    const uint8_t *gate_up, uint32_t gate_up_type,
+                    const uint8_t *down, uint32_t down_type,
+                    const float *x, size_t d_model, size_t n_used, size_t d_expert,
+                    orc_pool *pool) {
+    const size_t nthr = (size_t)orc_pool_threads(pool);
+    const size_t max_cols = max_sz(d_model, d_expert);
+    float *gate_buf = (float *)malloc(d_expert * 4), *up_buf = (float *)malloc(d_expert * 4);
+    float *down_buf = (float *)malloc(d_model * 4), *scratch = (float *)malloc(nthr * max_cols * 4);
+    float *scores = (float *)malloc(n_experts * 4);
+    uint32_t top_idx[64];
+    int rc = 0;
+    if (n_used > 64 || !gate_buf || !up_buf || !down_buf || !scratch || !scores) { rc = -1; goto done; }
+
+    orc_quant_matvec(scores, (const uint8_t *)router_w, ORC_F32, x, n_experts, d_model, scratch);
+    orc_softmax(scores, n_experts);
+    orc_moe_topk(scores, n_experts, top_idx, n_used);
+
+    const size_t gu_row_bytes = orc_row_bytes(gate_up_type, d_model);
+    const size_t gu_per_expert = 2 * d_expert * gu_row_bytes;
+    const size_t dn_row_bytes = orc_row_bytes(down_type, d_expert);
+    const size_t dn_per_expert = d_model * dn_row_bytes;
+    if (gu_row_bytes == 0 || dn_row_bytes == 0) { rc = -1; goto done; }
+
+    for (size_t i = 0; i < n_used; i++) {
+        const uint32_t e = top_idx[i];
+        const float w = scores[e];
+        const uint8_t *gate_data = gate_up + e * gu_per_expert;
+        orc_quant_matvec_par(gate_buf, gate_data, gate_up_type, x, d_expert, d_model, scratch, pool);
+        const uint8_t *up_data = gate_data + d_expert * gu_row_bytes;
+        orc_quant_matvec_par(up_buf, up_data, gate_up_type, x, d_expert, d_model, scratch, pool);
+        for (size_t r = 0; r < d_expert; r++) gate_buf[r] = orc_silu(gate_buf[r]) * up_buf[r];
+        orc_quant_matvec_par(down_buf, down + e * dn_per_expert, down_type, gate_buf, d_model, d_expert, scratch, pool);
+        for (size_t r = 0; r < d_model; r++) out[r] += w * down_buf[r];
+    }
+done:
+    free(gate_buf); free(up_buf); free(down_buf); free(scratch); free(scores);
+    return rc;
+}
+
+int orc_moe_layer(float *out, const float *x, size_t n_tok, size_t d_model,
+                  const float *router_w, size_t n_experts, size_t k, int norm_topk,
+                  const float *expert_scale,
+                  const uint8_t *gate, const uint8_t *up, uint32_t gate_type,
+                  const uint8_t *down, uint32_t down_type, size_t d_expert, int act,
+                  orc_pool *pool, uint32_t *ids_out, float *w_out) {
+    if (k == 0 || k > 16 || k > n_experts) return -1;
+    const size_t gu_rb = orc_row_bytes(gate_type, d_model);
+    const size_t dn_rb = orc_row_bytes(down_type, d_expert);
+    if (gu_rb == 0 || dn_rb == 0) return -1;
+    /* fused gate_up: gate rows [0,F), up rows [F,2F) of one expert
+     * (gemma4/forward.zig:464-471); separate: F rows per expert each. */
+    const size_t gate_per_expert = (up ? 1 : 2) * d_expert * gu_rb;
+    const size_t up_per_expert = d_expert * gu_rb;
+    const size_t dn_per_expert = d_model * dn_rb;
+
+    const size_t nthr = (size_t)orc_pool_threads(pool);
+    const size_t max_cols = max_sz(d_model, d_expert);
+    float *eg = (float *)malloc(d_expert * 4), *eu = (float *)malloc(d_expert * 4);
+    float *ed = (float *)malloc(d_model * 4), *scratch = (float *)malloc(nthr * max_cols * 4);
+    float *scores = (float *)malloc(n_experts * 4);
+    int rc = 0;
+    if (!eg || !eu || !ed || !scratch || !scores) { rc = -1; goto done; }
+
+    for (size_t t = 0; t < n_tok; t++) {
+        const float *xt = x + t * d_model;
+        float *ot = out + t * d_model;
+        uint32_t top_idx[16];
+        float w[16];
+        orc_router_topk_softmax(scores, top_idx, k, router_w, n_experts, d_model, xt, pool);
+        for (size_t i = 0; i < k; i++) w[i] = scores[top_idx[i]];
+        if (norm_topk) {
+            float s = 0.0f;
+            for (size_t i = 0; i < k; i++) s += w[i];
+            for (size_t i = 0; i < k; i++) w[i] = w[i] / s;
+        }
+        if (expert_scale)
+            for (size_t i = 0; i < k; i++) w[i] = expert_scale[top_idx[i]] * w[i];
+
+        memset(ot, 0, d_model * 4);
+        for (size_t i = 0; i < k; i++) {
+            const uint32_t e = top_idx[i];
+            const uint8_t *gate_data = gate + e * gate_per_expert;
+            const uint8_t *up_data = up ? up + e * up_per_expert : gate_data + d_expert * gu_rb;
+            orc_quant_matvec_par(eg, gate_data, gate_type, xt, d_expert, d_model, scratch, pool);
+            orc_quant_matvec_par(eu, up_data, gate_type, xt, d_expert, d_model, scratch, pool);
+            if (act == 1)
+                for (size_t r = 0; r < d_expert; r++) eg[r] = orc_gelu(eg[r]) * eu[r];
+            else
+                for (size_t r = 0; r < d_expert; r++) eg[r] = orc_silu(eg[r]) * eu[r];
+            orc_quant_matvec_par(ed, down + e * dn_per_expert, down_type, eg, d_model, d_expert, scratch, pool);
+            for (size_t r = 0; r < d_model; r++) ot[r] += w[i] * ed[r];
+        }
+        if (ids_out) memcpy(ids_out + t * k, top_idx, k * 4);
+        if (w_out) memcpy(w_out + t * k, w, k * 4);
+    }
+done:
+    free(eg); free(eu); free(ed); free(scratch); free(scores);
+    return rc;
+}
+
+/* src/model/sample.zig:11-17 */
+uint32_t orc_greedy(const float *logits, size_t n) {
+    uint32_t best = 0;
+    for (size_t i = 1; i < n; i++)
+        if (logits[i] > logits[best]) best = (uint32_t)i;
+    return best;
+}

@@ -1,0 +1,127 @@
+/*
+ * oracle.h — CPU restatement of llmtoy-zig's quantized MoE forward path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the parity checker for the CUDA
+ * path and the timed CPU baseline in bench.py.  Nothing in the product
+ * (llmtoy-zig_b200/) links, loads or calls it.
+ *
+ * Every function restates one reference function, in the same float
+ * evaluation order, compiled with -ffp-contract=off so that no multiply-add
+ * is fused (Zig's default float mode is strict; the reference never calls
+ * @setFloatMode).  Citations are path:line inside the llmtoy-zig tree.
+ *
+ * Assumptions that cannot be checked here (no Zig toolchain):
+ *   - @reduce(.Add, v) on f32 vectors is the LLVM ordered reduction
+ *     ((((-0 + v0) + v1) + v2) ...), which is what strict float mode lowers to.
+ *   - @exp on f32 resolves to the C library's expf; tanh is std.math.tanh
+ *     (musl-derived), restated here with the C library's tanhf.
+ *   Both only affect last-ulp rounding of activations and softmax weights,
+ *   never the dequantised values or the router's selected ids.
+ */
+#ifndef LLMTOY_ORACLE_H
+#define LLMTOY_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* GgmlType codes, src/gguf/types.zig:23-52 */
+enum {
+    ORC_F32 = 0, ORC_F16 = 1, ORC_Q8_0 = 8, ORC_Q4_K = 12, ORC_Q6_K = 14
+};
+
+/* f16 bits -> f32, exact (src/quant/dequant.zig:302-305) */
+float orc_f16_to_f32(uint16_t h);
+/* round-to-nearest-even f32 -> f16 bits (used only by fixture generators) */
+uint16_t orc_f32_to_f16(float f);
+
+/* rowBytes, src/ops/math.zig:194-208.  Returns 0 for an unsupported type. */
+size_t orc_row_bytes(uint32_t type, size_t cols);
+
+/* Block codecs, src/quant/dequant.zig */
+void orc_dequant_f32(const uint8_t *data, float *out, size_t n);   /* :17  */
+void orc_dequant_f16(const uint8_t *data, float *out, size_t n);   /* :24  */
+void orc_dequant_q8_0(const uint8_t *data, float *out, size_t n);  /* :42  */
+void orc_dequant_q4_k(const uint8_t *data, float *out, size_t n);  /* :157 */
+void orc_dequant_q6_k(const uint8_t *data, float *out, size_t n);  /* :237 */
+float orc_dot_q8_0(const uint8_t *data, const float *vec, size_t n); /* :59 */
+
+/* dequantRow, src/ops/math.zig:211-225.  Returns -1 for an unsupported type. */
+int orc_dequant_row(const uint8_t *data, float *out, size_t n, uint32_t type);
+
+/* src/ops/math.zig */
+void  orc_matvec(float *out, const float *mat, const float *vec, size_t rows, size_t cols); /* :8 */
+float orc_dotf32(const float *a, const float *b, size_t n);                                /* :96 */
+int   orc_quant_matvec(float *out, const uint8_t *mat, uint32_t type, const float *vec,
+                       size_t rows, size_t cols, float *row_buf);                          /* :133 */
+void  orc_rmsnorm(float *out, const float *x, const float *w, size_t n, float eps);        /* :20 */
+void  orc_rmsnorm_raw(float *out, const float *x, size_t n, float eps);                    /* :43 */
+void  orc_softmax(float *x, size_t n);                                                     /* :29 */
+float orc_silu(float x);                                                                   /* :38 */
+float orc_gelu(float x);                                                                   /* :85 */
+
+/* Persistent worker pool, src/ops/thread_pool.zig:15-112 */
+typedef struct orc_pool orc_pool;
+orc_pool *orc_pool_create(int n_threads);
+void      orc_pool_destroy(orc_pool *pool);
+int       orc_pool_threads(const orc_pool *pool);
+
+/* quantMatvecPar, src/ops/math.zig:277-320 (scratch: threads*cols floats) */
+int orc_quant_matvec_par(float *out, const uint8_t *mat, uint32_t type, const float *vec,
+                         size_t rows, size_t cols, float *scratch, orc_pool *pool);
+
+/* Router, src/model/gemma4/forward.zig */
+typedef struct { float max; float exp_sum; } orc_softmax_stats;
+orc_softmax_stats orc_topk_with_softmax_stats(const float *scores, size_t n,
+                                              uint32_t *out, size_t k);            /* :598 */
+void orc_softmax_topk(float *scores, size_t n, uint32_t *out, size_t k);           /* :637 */
+orc_softmax_stats orc_topk_matvec_f32(const float *w, const float *vec, size_t rows, size_t cols,
+                                      uint32_t *out, float *selected, size_t k);   /* :672 */
+orc_softmax_stats orc_topk_matvec_f32_par(const float *w, const float *vec, size_t rows,
+                                          size_t cols, uint32_t *out, float *selected,
+                                          size_t k, orc_pool *pool);               /* :769 */
+/* routerTopKSoftmax (:648): writes softmax probabilities of the k selected
+ * experts into scores[idx] and the ids (descending, lowest index on ties). */
+void orc_router_topk_softmax(float *scores, uint32_t *out, size_t k, const float *router_w,
+                             size_t rows, size_t cols, const float *router_in, orc_pool *pool);
+/* topK of the generic MoE (src/ops/moe.zig:80-91) */
+void orc_moe_topk(const float *scores, size_t n, uint32_t *out, size_t k);
+
+/* Generic moeForward, src/ops/moe.zig:18-77: softmax over all router logits,
+ * topK, fused gate_up tensor (gate rows [0,F), up rows [F,2F)), SiLU, no
+ * renormalisation.  out must be zeroed by the caller. */
+int orc_moe_forward(float *out, const float *router_w, size_t n_experts,
+                    const uint8_t *gate_up, uint32_t gate_up_type,
+                    const uint8_t *down, uint32_t down_type,
+                    const float *x, size_t d_model, size_t n_used, size_t d_expert,
+                    orc_pool *pool);
+
+/*
+ * One MoE FFN layer over T tokens: router + selected experts + weighted
+ * combine.  The router is routerTopKSoftmax (gemma4/forward.zig:648-668);
+ * the expert loop is gemma4/forward.zig:463-479 with a selectable
+ * activation.
+ *   up == NULL      -> `gate` is the fused gate_up tensor (forward.zig:469-471)
+ *   norm_topk != 0  -> weights renormalised over the k selected (Qwen3-MoE;
+ *                      NEW oracle code, the reference has no such mode)
+ *   expert_scale    -> multiplied in as down_exps_scale[e] * w (forward.zig:477)
+ *   act             -> 0 = SiLU (math.zig:38), 1 = GELU tanh (math.zig:85)
+ * ids_out / w_out (T*k) receive the selected ids and final weights.
+ */
+int orc_moe_layer(float *out, const float *x, size_t n_tok, size_t d_model,
+                  const float *router_w, size_t n_experts, size_t k, int norm_topk,
+                  const float *expert_scale,
+                  const uint8_t *gate, const uint8_t *up, uint32_t gate_type,
+                  const uint8_t *down, uint32_t down_type, size_t d_expert, int act,
+                  orc_pool *pool, uint32_t *ids_out, float *w_out);
+
+/* greedy, src/model/sample.zig:11-17 (lowest index among equal maxima) */
+uint32_t orc_greedy(const float *logits, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
