@@ -1,0 +1,426 @@
+"""Benchmark: batch-1 MoE decode through a stack of config-1 MoE layers.
+
+Workload (T=1): one token through L=48 chained MoE
+FFN layers of the Qwen3-30B-A3B shape -- d_model 2048, 128 experts, top-8 with
+renormalised softmax, SwiGLU expert width 768, Q4_K experts, f32 router --
+each layer x <- moe(rmsnorm(x)).  48 distinct weight sets (16.3 GB) make every
+step read ~1.07 GB of weights, far more than the 126 MB L2, so no flush is
+needed.  Weights are seeded synthetic bytes with the config's distributions,
+generated on the device.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One JSON line on rank 0.  `value` is device time of CUDA-graph replays (one
+graph per token, captured through the C ABI); `e2e` adds the per-token
+host->device copy of the input and device->host read of the output through
+the same API.  `--impl reference` times the CPU restatement of the reference
+path (oracle/, C, all host threads) on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+D_MODEL, N_EXPERTS, TOP_K, D_EXPERT = 2048, 128, 8, 768
+Q4K_ROW = lambda cols: (cols // 256) * 144  # noqa: E731
+EXPERT_BYTES = 2 * D_EXPERT * Q4K_ROW(D_MODEL) + D_MODEL * Q4K_ROW(D_EXPERT)  # 2,654,208
+ROUTER_BYTES = N_EXPERTS * D_MODEL * 4
+METRIC = "MoE decode tok/s (config-1 MoE layer, T=1, 48-layer stack)"
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return 6650.0, "fallback"
+
+
+def ncu_traffic() -> dict | None:
+    p = REPO / "profiles" / "ncu_summary.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            return None
+    return None
+
+
+# ── clocks ───────────────────────────────────────────────────────────────────
+
+class ClockSampler:
+    """nvidia-smi every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        try:
+            lines = Path(self.path).read_text().splitlines()
+        except OSError:
+            lines = []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if self.path:
+            try:
+                os.unlink(self.path)
+            except OSError:
+                pass
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ── synthetic weights on the device ──────────────────────────────────────────
+
+def q4k_bytes_device(torch, gen, rows: int, cols: int):
+    nb = rows * (cols // 256)
+    b = torch.randint(0, 256, (nb, 144), dtype=torch.uint8, device="cuda", generator=gen)
+    d = (torch.rand(nb, device="cuda", generator=gen) * 3e-3 + 1e-3).half()
+    dmin = (torch.rand(nb, device="cuda", generator=gen) * 2e-3).half()
+    b[:, 0:2] = d.view(torch.uint8).view(nb, 2)
+    b[:, 2:4] = dmin.view(torch.uint8).view(nb, 2)
+    return b.view(-1)
+
+
+class DeviceLayer:
+    def __init__(self, pkg, ctx, torch, gen):
+        router = torch.randn(N_EXPERTS, D_MODEL, device="cuda", generator=gen) * 0.02
+        self.router = ctx.upload_device(router.view(torch.uint8).view(-1), pkg.F32, N_EXPERTS, D_MODEL)
+        g = q4k_bytes_device(torch, gen, N_EXPERTS * D_EXPERT, D_MODEL)
+        self.gate = ctx.upload_device(g, pkg.Q4_K, D_EXPERT, D_MODEL, N_EXPERTS)
+        del g
+        u = q4k_bytes_device(torch, gen, N_EXPERTS * D_EXPERT, D_MODEL)
+        self.up = ctx.upload_device(u, pkg.Q4_K, D_EXPERT, D_MODEL, N_EXPERTS)
+        del u
+        dn = q4k_bytes_device(torch, gen, N_EXPERTS * D_MODEL, D_EXPERT)
+        self.down = ctx.upload_device(dn, pkg.Q4_K, D_MODEL, D_EXPERT, N_EXPERTS)
+        del dn
+        self.norm = torch.ones(D_MODEL, device="cuda")
+
+
+# ── CPU restatement (oracle) on the same workload ────────────────────────────
+
+class CpuStack:
+    """The reference CPU path (C restatement in oracle/, all host threads)
+    through n_layers MoE layers, cycling `distinct` host weight sets (each
+    340 MB, far beyond the CPU caches)."""
+
+    def __init__(self, n_layers: int, distinct: int = 4, seed: int = 0):
+        sys.path.insert(0, str(REPO / "tests"))
+        self.oracle = importlib.import_module("oracle_lib")
+        synth = importlib.import_module("llmtoy-zig_b200.synth")
+        rng = np.random.Generator(np.random.PCG64(synth.config_seed(1) + seed))
+        self.layers = [synth.MoeLayer(rng, D_MODEL, N_EXPERTS, D_EXPERT) for _ in range(distinct)]
+        self.norm = np.ones(D_MODEL, np.float32)
+        self.n_layers, self.distinct = n_layers, distinct
+        self.threads = os.cpu_count() or 1
+        self.pool = self.oracle.Pool(self.threads)
+        self.x = rng.normal(0, 1, size=(1, D_MODEL)).astype(np.float32)
+
+    def token(self) -> None:
+        L = self.oracle.lib()
+        xx = self.x
+        for li in range(self.n_layers):
+            xn = np.empty_like(xx)
+            L.orc_rmsnorm(xn.ctypes.data, xx.ctypes.data, self.norm.ctypes.data, D_MODEL, 1e-6)
+            xx, _, _ = self.oracle.moe_layer(self.layers[li % self.distinct], xn, TOP_K, True, 0, None, self.pool)
+        self.x = xx
+
+    def rate(self, budget_s: float, min_tokens: int = 1):
+        t0 = time.perf_counter()
+        n = 0
+        while n < min_tokens or time.perf_counter() - t0 < budget_s:
+            self.token()
+            n += 1
+        dt = time.perf_counter() - t0
+        return n / dt, n, dt
+
+    def close(self) -> None:
+        self.pool.close()
+
+
+def cpu_decode_rate(n_layers: int, budget_s: float):
+    s = CpuStack(n_layers)
+    s.token()  # warm
+    rate, n, dt = s.rate(budget_s)
+    s.close()
+    return rate, n, dt, s.threads, s.distinct
+
+
+def run_reference(args) -> None:
+    rank, world, _ = env_rank()
+    if rank != 0:
+        return
+    # per step: one token through the L-layer stack on the CPU restatement
+    s = CpuStack(args.layers)
+    s.rate(0.0, min_tokens=args.warmup)
+    rate, n, dt = s.rate(0.0, min_tokens=args.steps)
+    threads, distinct = s.threads, s.distinct
+    s.close()
+    line = {
+        "metric": METRIC, "value": rate, "unit": "tok/s", "n_gpus": args.gpus, "steps": n, "warmup": args.warmup,
+        "ms_per_step": 1e3 * dt / n, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded, config-1 distributions)", "impl": "reference",
+        "config": config_block(args, world),
+        "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": f"{n} tokens x {args.layers} layers, {distinct} distinct host weight sets "
+                                   f"cycled (C restatement of the Zig CPU path; zig absent)"},
+        "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_block(args, world: int) -> dict:
+    return {"workload": f"config-1 MoE layer (d_model {D_MODEL}, {N_EXPERTS} experts, top-{TOP_K} renormalised, "
+                        f"SwiGLU {D_EXPERT}, Q4_K experts, f32 router), T=1 decode, {args.layers} chained layers "
+                        f"x <- moe(rmsnorm(x))",
+            "model": "qwen3-30b-a3b MoE stack (synthetic)", "global_batch": world, "seq_len": 1,
+            "layers": args.layers, "parallelism": f"replicas x{world}" if world > 1 else "single",
+            "l2": f"inputs larger than L2: {args.layers} distinct layers, "
+                  f"{args.layers * (TOP_K * EXPERT_BYTES + ROUTER_BYTES) / 1e9:.2f} GB read per step"}
+
+
+# ── our path ─────────────────────────────────────────────────────────────────
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline work (rank 0, N=1)")
+    ap.add_argument("--profile-steps", type=int, default=5)
+    ap.add_argument("--no-graph", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    rank, world, local = env_rank()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    pkg = importlib.import_module("llmtoy-zig_b200")
+    ctx = pkg.Context(local)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream)
+    ctx.reserve(1, TOP_K, D_MODEL, D_EXPERT)
+
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0x11A70001 + 1000 * rank)
+    layers = [DeviceLayer(pkg, ctx, torch, gen) for _ in range(args.layers)]
+    torch.cuda.synchronize()
+
+    x0 = torch.randn(1, D_MODEL, device="cuda", generator=gen)
+    xa = torch.empty(1, D_MODEL, device="cuda")
+    xb = torch.empty(1, D_MODEL, device="cuda")
+    xn = torch.empty(1, D_MODEL, device="cuda")
+
+    def step():
+        cur, nxt = xa, xb
+        for L in layers:
+            ctx.rmsnorm(cur, L.norm, 1e-6, D_MODEL, 1, xn)
+            ctx.moe_forward(L.router, L.gate, L.up, L.down, pkg.ACT_SILU, True, None, xn, 1, TOP_K, nxt)
+            cur, nxt = nxt, cur
+        return cur
+
+    with torch.cuda.stream(stream):
+        xa.copy_(x0)
+    out_buf = step()  # eager warm-up (and the buffer that holds each step's result)
+    ctx.sync()
+    graph = None
+    if not args.no_graph:
+        ctx.capture_begin()
+        step()
+        graph = ctx.capture_end()
+
+    def run_step():
+        if graph is not None:
+            graph.launch()
+        else:
+            step()
+
+    def barrier():
+        if dist is not None:
+            t = torch.zeros(1, device="cuda")
+            dist.all_reduce(t)
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-timed throughput (value) ----
+    for _ in range(args.warmup):
+        run_step()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            run_step()
+        ev1.record(stream)
+        stream.synchronize()
+    barrier()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    clocks = clk.summary()
+    ms_step = ms / args.steps
+    value = world * args.steps / (ms / 1e3)
+
+    # ---- end to end: host input -> device -> host result, every step ----
+    x_host = torch.randn(1, D_MODEL, generator=torch.Generator().manual_seed(7)).pin_memory()
+    y_host = torch.empty(1, D_MODEL).pin_memory()
+    for _ in range(args.warmup):
+        with torch.cuda.stream(stream):
+            xa.copy_(x_host, non_blocking=True)
+        run_step()
+        with torch.cuda.stream(stream):
+            y_host.copy_(out_buf, non_blocking=True)
+        stream.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        with torch.cuda.stream(stream):
+            xa.copy_(x_host, non_blocking=True)
+        run_step()
+        with torch.cuda.stream(stream):
+            y_host.copy_(out_buf, non_blocking=True)
+        stream.synchronize()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+    e2e = {"value": world * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": D_MODEL * 4,
+           "d2h_bytes_per_step": D_MODEL * 4, "ms_per_step": 1e3 * e2e_s / args.steps,
+           "path": "C ABI graph replay (lt_graph_launch) with pinned host input/output copies"}
+
+    # ---- per-kernel timing (profiler on, eager launches) ----
+    ctx.profile(True)
+    ctx.profile_reset()
+    for _ in range(args.profile_steps):
+        step()
+    ctx.sync()
+    prof = ctx.profile_read()
+    ctx.profile(False)
+
+    peak, peak_kind = measured_peaks()
+    gu = prof.get("moe_gate_up_q4k")
+    gu_bytes = TOP_K * 2 * D_EXPERT * Q4K_ROW(D_MODEL) + D_MODEL * 4 + TOP_K * D_EXPERT * 4
+    roofline = None
+    if gu and gu["count"]:
+        gu_ms = gu["total_ms"] / gu["count"]
+        achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+        tr = ncu_traffic()
+        traffic = tr.get("moe_gate_up_q4k", {}).get("dram_bytes_per_launch") if tr else None
+        roofline = {"kernel": "moe_gate_up_q4k", "bound": "hbm", "achieved": achieved, "peak": peak,
+                    "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
+                    "algorithmic_bytes_per_launch": gu_bytes, "avg_launch_ms": gu_ms, "traffic": traffic}
+    step_bytes = args.layers * (TOP_K * EXPERT_BYTES + ROUTER_BYTES)
+    kernels = {k: {"count": v["count"], "avg_us": 1e3 * v["total_ms"] / max(1, v["count"])} for k, v in prof.items()}
+    layer_bytes = TOP_K * EXPERT_BYTES + ROUTER_BYTES
+
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_budget > 0:
+        rate, n, dt, threads, distinct = cpu_decode_rate(args.layers, args.cpu_budget)
+        cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": f"{n} tokens x {args.layers} layers in {dt:.1f}s, {distinct} distinct host weight sets "
+                         f"cycled (C restatement of the Zig CPU path; zig absent)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q4_k weights x int16 activations (dp2a), f32 accumulate",
+            "data": "synthetic (seeded, config-1 distributions, generated on device)",
+            "config": config_block(args, world),
+            "expert_hbm_gbs": step_bytes / (ms_step / 1e3) / 1e9,
+            "hbm_frac_of_step": (step_bytes / (ms_step / 1e3) / 1e9) / peak,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": args.steps * 4 * args.layers, "clocks": clocks,
+            "kernels_profiled": kernels, "layer_bytes": layer_bytes,
+            "graph": graph is not None,
+        }
+        print(json.dumps(line), flush=True)
+
+    if graph is not None:
+        graph.free()
+    for L in layers:
+        for t in (L.router, L.gate, L.up, L.down):
+            t.free()
+    ctx.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

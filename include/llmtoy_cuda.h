@@ -162,6 +162,31 @@ lt_status lt_moe_forward(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *
 lt_status lt_argmax(lt_ctx *ctx, const float *dev_x, uint32_t n, uint32_t ntok,
                     uint32_t *dev_idx);
 
+/* ── kernel timing ────────────────────────────────────────────────────────
+ * GpuProfiler (src/gpu/context.zig:34-268, LLMTOY_GPU_PROFILE): when on,
+ * every kernel launch is bracketed by CUDA events on its stream and its
+ * duration is aggregated per kernel label (count/total/min/max in ms).
+ * Timing serialises launches (no programmatic overlap), so take throughput
+ * numbers with it off. */
+lt_status lt_profile_enable(lt_ctx *ctx, int on);
+/* Entry `index` of the aggregate (waits for pending events first);
+ * LT_EINVAL once index is past the last label.  label stays valid for the
+ * life of the library. */
+lt_status lt_profile_read(lt_ctx *ctx, uint32_t index, const char **label, uint64_t *count,
+                          double *total_ms, double *min_ms, double *max_ms);
+lt_status lt_profile_reset(lt_ctx *ctx);
+
+/* ── CUDA graph capture ───────────────────────────────────────────────────
+ * Records the device ops issued between begin and end on the context stream
+ * into a graph that lt_graph_launch replays (one launch per decode token
+ * instead of one per kernel).  The stream must not be the legacy default
+ * stream; call lt_reserve first so no op allocates while capturing. */
+typedef struct lt_graph lt_graph;
+lt_status lt_capture_begin(lt_ctx *ctx);
+lt_status lt_capture_end(lt_ctx *ctx, lt_graph **out);
+lt_status lt_graph_launch(lt_ctx *ctx, const lt_graph *graph);
+lt_status lt_graph_free(lt_ctx *ctx, lt_graph *graph);
+
 /* ── host-buffer entry points (synchronous) ─────────────────────────────────
  * Same semantics with HOST vectors, copies included: the shape of the
  * reference's own CPU calls, for callers that keep activations on the host. */

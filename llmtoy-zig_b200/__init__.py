@@ -31,7 +31,8 @@ EXPORTS = [
     "lt_status_string", "lt_reserve", "lt_row_bytes", "lt_upload", "lt_upload_from_device",
     "lt_tensor_download", "lt_tensor_describe", "lt_tensor_free", "lt_dequant", "lt_qmatvec",
     "lt_rmsnorm", "lt_softmax", "lt_moe_route", "lt_moe_ffn", "lt_moe_forward", "lt_argmax",
-    "lt_quant_matvec_host", "lt_moe_forward_host",
+    "lt_profile_enable", "lt_profile_read", "lt_profile_reset", "lt_capture_begin", "lt_capture_end",
+    "lt_graph_launch", "lt_graph_free", "lt_quant_matvec_host", "lt_moe_forward_host",
 ]
 
 
@@ -82,6 +83,15 @@ def load_library() -> ctypes.CDLL:
         "lt_moe_ffn": (I, [P, P, P, P, I, P, U32, P, P, U32, P]),
         "lt_moe_forward": (I, [P, P, P, P, P, I, I, P, P, U32, U32, P, P, P]),
         "lt_argmax": (I, [P, P, U32, U32, P]),
+        "lt_profile_enable": (I, [P, I]),
+        "lt_profile_read": (I, [P, U32, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(U64),
+                                ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
+                                ctypes.POINTER(ctypes.c_double)]),
+        "lt_profile_reset": (I, [P]),
+        "lt_capture_begin": (I, [P]),
+        "lt_capture_end": (I, [P, ctypes.POINTER(P)]),
+        "lt_graph_launch": (I, [P, P]),
+        "lt_graph_free": (I, [P, P]),
         "lt_quant_matvec_host": (I, [P, P, P, U32, P, U64, U64]),
         "lt_moe_forward_host": (I, [P, P, P, P, P, I, I, P, P, U32, U32, P, P, P]),
     }
@@ -131,6 +141,22 @@ class Tensor:
     def free(self) -> None:
         if self.handle:
             self._ctx.lib.lt_tensor_free(self._ctx.ptr, self.handle)
+            self.handle = None
+
+
+class Graph:
+    """A captured sequence of ops (lt_capture_begin .. lt_capture_end)."""
+
+    def __init__(self, ctx: "Context", handle: int):
+        self._ctx = ctx
+        self.handle = handle
+
+    def launch(self) -> None:
+        self._ctx._check(self._ctx.lib.lt_graph_launch(self._ctx.ptr, self.handle))
+
+    def free(self) -> None:
+        if self.handle:
+            self._ctx.lib.lt_graph_free(self._ctx.ptr, self.handle)
             self.handle = None
 
 
@@ -223,6 +249,37 @@ class Context:
         self._check(self.lib.lt_moe_forward(self.ptr, router.handle, gate.handle, up.handle if up else None,
                                             down.handle, act, int(norm_topk), _ptr(expert_scale), _ptr(x), ntok,
                                             k, _ptr(out), _ptr(ids), _ptr(w)))
+
+    # -- kernel timing / graph capture -------------------------------------
+    def profile(self, on: bool) -> None:
+        self._check(self.lib.lt_profile_enable(self.ptr, int(on)))
+
+    def profile_reset(self) -> None:
+        self._check(self.lib.lt_profile_reset(self.ptr))
+
+    def profile_read(self) -> dict[str, dict]:
+        """{label: {count, total_ms, min_ms, max_ms}} of the timed launches."""
+        out = {}
+        i = 0
+        while True:
+            lab, cnt = ctypes.c_char_p(), ctypes.c_uint64()
+            tot, mn, mx = ctypes.c_double(), ctypes.c_double(), ctypes.c_double()
+            st = self.lib.lt_profile_read(self.ptr, i, ctypes.byref(lab), ctypes.byref(cnt), ctypes.byref(tot),
+                                          ctypes.byref(mn), ctypes.byref(mx))
+            if st != 0:
+                break
+            out[lab.value.decode()] = {"count": cnt.value, "total_ms": tot.value, "min_ms": mn.value,
+                                       "max_ms": mx.value}
+            i += 1
+        return out
+
+    def capture_begin(self) -> None:
+        self._check(self.lib.lt_capture_begin(self.ptr))
+
+    def capture_end(self) -> "Graph":
+        g = ctypes.c_void_p()
+        self._check(self.lib.lt_capture_end(self.ptr, ctypes.byref(g)))
+        return Graph(self, g.value)
 
     # -- host-buffer entry points (synchronous) ---------------------------
     def quant_matvec_host(self, mat: Tensor, vec, expert: int = 0):

@@ -35,6 +35,13 @@ struct lt_ctx {
     size_t n_counters = 0;
     uint8_t *pinned = nullptr;       // pinned staging for the host-buffer entry points
     size_t pinned_bytes = 0;
+    bool capturing = false;          // between lt_capture_begin and lt_capture_end
+    lt::Profiler prof;
+};
+
+struct lt_graph {
+    cudaGraph_t graph;
+    cudaGraphExec_t exec;
 };
 
 namespace {
@@ -69,6 +76,7 @@ lt::LaunchCfg cfg_of(lt_ctx *ctx) {
     c.pdl = ctx->pdl;
     c.dev_err = ctx->dev_err;
     c.num_sms = ctx->num_sms;
+    c.prof = &ctx->prof;
     return c;
 }
 
@@ -80,10 +88,19 @@ lt_status enter(lt_ctx *ctx) {
     return LT_OK;
 }
 
+// Entry points that copy or synchronise cannot be recorded into a graph.
+lt_status enter_uncaptured(lt_ctx *ctx, const char *what) {
+    lt_status st = enter(ctx);
+    if (st == LT_OK && ctx->capturing) return fail(ctx, LT_EINVAL, "%s: not allowed while capturing", what);
+    return st;
+}
+
 // Grow the scratch arena; waits for the stream first so nothing in flight
 // still uses the old buffer.
 lt_status ensure_scratch(lt_ctx *ctx, size_t bytes) {
     if (bytes <= ctx->scratch_bytes) return LT_OK;
+    if (ctx->capturing)
+        return fail(ctx, LT_EINVAL, "op needs %zu scratch bytes while capturing: call lt_reserve first", bytes);
     LT_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
     if (ctx->scratch) cudaFree(ctx->scratch);
     ctx->scratch = nullptr;
@@ -96,6 +113,7 @@ lt_status ensure_scratch(lt_ctx *ctx, size_t bytes) {
 
 lt_status ensure_counters(lt_ctx *ctx, size_t n) {
     if (n <= ctx->n_counters) return LT_OK;
+    if (ctx->capturing) return fail(ctx, LT_EINVAL, "op needs more counters while capturing: call lt_reserve first");
     LT_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
     if (ctx->counters) cudaFree(ctx->counters);
     ctx->counters = nullptr;
@@ -230,7 +248,13 @@ lt_status lt_init(int device, lt_ctx **out) {
 void lt_free(lt_ctx *ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
+    if (ctx->capturing) {
+        cudaGraph_t g = nullptr;
+        cudaStreamEndCapture(ctx->stream, &g);
+        if (g) cudaGraphDestroy(g);
+    }
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    ctx->prof.destroy();
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->counters) cudaFree(ctx->counters);
     if (ctx->dev_err) cudaFree(ctx->dev_err);
@@ -246,9 +270,90 @@ lt_status lt_set_stream(lt_ctx *ctx, void *cuda_stream) {
     return LT_OK;
 }
 
+lt_status lt_profile_enable(lt_ctx *ctx, int on) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (ctx->capturing) return fail(ctx, LT_EINVAL, "lt_profile_enable: not while capturing");
+    ctx->prof.on = on != 0;
+    return LT_OK;
+}
+
+lt_status lt_profile_read(lt_ctx *ctx, uint32_t index, const char **label, uint64_t *count, double *total_ms,
+                          double *min_ms, double *max_ms) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (ctx->capturing) return fail(ctx, LT_EINVAL, "lt_profile_read: not while capturing");
+    LT_CUDA(ctx, ctx->prof.flush(), "profile events");
+    if (index >= (uint32_t)ctx->prof.n_agg) return LT_EINVAL;
+    const lt::Profiler::Agg &a = ctx->prof.agg[index];
+    if (label) *label = a.label;
+    if (count) *count = a.count;
+    if (total_ms) *total_ms = a.total_ms;
+    if (min_ms) *min_ms = a.min_ms;
+    if (max_ms) *max_ms = a.max_ms;
+    return LT_OK;
+}
+
+lt_status lt_profile_reset(lt_ctx *ctx) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    LT_CUDA(ctx, ctx->prof.flush(), "profile events");
+    ctx->prof.reset();
+    return LT_OK;
+}
+
+lt_status lt_capture_begin(lt_ctx *ctx) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (ctx->capturing) return fail(ctx, LT_EINVAL, "lt_capture_begin: already capturing");
+    if (ctx->prof.on) return fail(ctx, LT_EINVAL, "lt_capture_begin: turn profiling off first");
+    LT_CUDA(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+    ctx->capturing = true;
+    return LT_OK;
+}
+
+lt_status lt_capture_end(lt_ctx *ctx, lt_graph **out) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!ctx->capturing) return fail(ctx, LT_EINVAL, "lt_capture_end: not capturing");
+    ctx->capturing = false;
+    cudaGraph_t g = nullptr;
+    LT_CUDA(ctx, cudaStreamEndCapture(ctx->stream, &g), "cudaStreamEndCapture");
+    if (!out) {
+        cudaGraphDestroy(g);
+        return fail(ctx, LT_EINVAL, "lt_capture_end: null output");
+    }
+    cudaGraphExec_t ex = nullptr;
+    cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
+    if (e != cudaSuccess) {
+        cudaGraphDestroy(g);
+        return cuda_fail(ctx, e, "cudaGraphInstantiate");
+    }
+    *out = new lt_graph{g, ex};
+    return LT_OK;
+}
+
+lt_status lt_graph_launch(lt_ctx *ctx, const lt_graph *graph) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!graph) return fail(ctx, LT_EINVAL, "lt_graph_launch: null graph");
+    LT_CUDA(ctx, cudaGraphLaunch(graph->exec, ctx->stream), "cudaGraphLaunch");
+    return LT_OK;
+}
+
+lt_status lt_graph_free(lt_ctx *ctx, lt_graph *graph) {
+    if (!graph) return LT_OK;
+    if (ctx) cudaSetDevice(ctx->device);
+    cudaGraphExecDestroy(graph->exec);
+    cudaGraphDestroy(graph->graph);
+    delete graph;
+    return LT_OK;
+}
+
 lt_status lt_sync(lt_ctx *ctx) {
     lt_status st = enter(ctx);
     if (st != LT_OK) return st;
+    if (ctx->capturing) return fail(ctx, LT_EINVAL, "lt_sync: not while capturing");
     LT_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
     int h = 0;
     LT_CUDA(ctx, cudaMemcpy(&h, ctx->dev_err, 4, cudaMemcpyDeviceToHost), "read device error word");
@@ -261,7 +366,7 @@ lt_status lt_sync(lt_ctx *ctx) {
 
 lt_status lt_reserve(lt_ctx *ctx, uint32_t max_tokens, uint32_t max_k, uint64_t max_d_model,
                      uint64_t max_d_expert) {
-    lt_status st = enter(ctx);
+    lt_status st = enter_uncaptured(ctx, "lt_reserve");
     if (st != LT_OK) return st;
     const size_t moe = moe_layout(nullptr, max_tokens, max_k, lt::kRouterMaxE, max_d_expert).bytes;
     const size_t io = 2 * al256((size_t)max_tokens * max_d_model * 4) + 2 * al256((size_t)max_tokens * max_k * 4);
@@ -277,7 +382,7 @@ uint64_t lt_row_bytes(uint32_t ggml_type, uint64_t cols) {
 
 static lt_status upload_impl(lt_ctx *ctx, const void *src, bool src_on_device, size_t nbytes, uint32_t type,
                              uint64_t rows, uint64_t cols, uint32_t n_experts, lt_tensor **out) {
-    lt_status st = enter(ctx);
+    lt_status st = enter_uncaptured(ctx, "lt_upload");
     if (st != LT_OK) return st;
     if (!out || !src) return fail(ctx, LT_EINVAL, "lt_upload: null pointer");
     *out = nullptr;
@@ -332,7 +437,7 @@ lt_status lt_upload_from_device(lt_ctx *ctx, const void *dev_bytes, size_t nbyte
 }
 
 lt_status lt_tensor_download(lt_ctx *ctx, const lt_tensor *t, void *host_bytes, size_t nbytes) {
-    lt_status st = enter(ctx);
+    lt_status st = enter_uncaptured(ctx, "lt_tensor_download");
     if (st != LT_OK) return st;
     if (!t || !host_bytes) return fail(ctx, LT_EINVAL, "lt_tensor_download: null pointer");
     if ((uint64_t)nbytes != t->total_rows * t->m.row_bytes)
@@ -439,8 +544,8 @@ static lt_status route_impl(lt_ctx *ctx, const lt_tensor *router, const float *x
     if (st != LT_OK) return st;
     return launched(ctx,
                     lt::launch_router(cfg_of(ctx), (const float *)router->m.data, (uint32_t)router->m.rows,
-                                      (uint32_t)router->m.cols, x, ntok, k, norm_topk, escale, ids, w, logits,
-                                      ctx->counters),
+                                      (uint32_t)router->m.cols, (uint32_t)(router->m.pitch / 4), x, ntok, k,
+                                      norm_topk, escale, ids, w, logits, ctx->counters),
                     "router");
 }
 
@@ -541,7 +646,7 @@ lt_status lt_moe_forward(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *
 
 lt_status lt_quant_matvec_host(lt_ctx *ctx, float *out, const lt_tensor *mat, uint32_t expert, const float *vec,
                                uint64_t rows, uint64_t cols) {
-    lt_status st = enter(ctx);
+    lt_status st = enter_uncaptured(ctx, "lt_quant_matvec_host");
     if (st != LT_OK) return st;
     if (!out || !mat || !vec) return fail(ctx, LT_EINVAL, "lt_quant_matvec_host: null pointer");
     if (rows != mat->m.rows || cols != mat->m.cols)
@@ -565,7 +670,7 @@ lt_status lt_quant_matvec_host(lt_ctx *ctx, float *out, const lt_tensor *mat, ui
 lt_status lt_moe_forward_host(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *gate, const lt_tensor *up,
                               const lt_tensor *down, int act, int norm_topk, const float *expert_scale_host,
                               const float *x, uint32_t ntok, uint32_t k, float *out, uint32_t *ids, float *w) {
-    lt_status st = enter(ctx);
+    lt_status st = enter_uncaptured(ctx, "lt_moe_forward_host");
     if (st != LT_OK) return st;
     if (!gate || !x || !out) return fail(ctx, LT_EINVAL, "lt_moe_forward_host: null pointer");
     if (ntok == 0) return LT_OK;

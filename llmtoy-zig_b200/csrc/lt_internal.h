@@ -28,11 +28,40 @@ struct MoePlan {
     uint32_t *pair_pos;   // [T*k]  pair index -> position
 };
 
+// Per-label kernel timing with CUDA events (the reference's GpuProfiler,
+// src/gpu/context.zig:34-268).  Only active when enabled on the context.
+struct Profiler {
+    struct Rec {
+        const char *label;
+        cudaEvent_t a, b;
+    };
+    struct Agg {
+        const char *label;
+        uint64_t count;
+        double total_ms, min_ms, max_ms;
+    };
+    bool on = false;
+    Rec pending[4096];
+    int n_pending = 0;
+    cudaEvent_t pool[8192];
+    int n_pool = 0;
+    Agg agg[64];
+    int n_agg = 0;
+
+    cudaEvent_t get_event();
+    void begin(const char *label, cudaStream_t s, Rec &r);
+    void end(Rec &r, cudaStream_t s);
+    cudaError_t flush();  // waits for pending events and accumulates
+    void reset();
+    void destroy();
+};
+
 struct LaunchCfg {
     cudaStream_t stream;
     bool pdl;        // launch with programmatic stream serialization
     int *dev_err;    // device error word (DEV_ERR_*)
     int num_sms;
+    Profiler *prof;  // nullptr or disabled: no timing
 };
 
 constexpr int kRouterMaxE = 256;  // experts per router (top-k runs in one warp)
@@ -53,7 +82,8 @@ cudaError_t launch_argmax(const LaunchCfg &c, const float *x, uint32_t n, uint32
                           uint32_t *counters);
 // Router over f32 weights [E][cols]; logits scratch [ntok][E]; counters
 // zero-initialised, one per token group (reset by the kernel).
-cudaError_t launch_router(const LaunchCfg &c, const float *w, uint32_t E, uint32_t cols,
+// w_ld: row stride of w in floats (the device row pitch / 4).
+cudaError_t launch_router(const LaunchCfg &c, const float *w, uint32_t E, uint32_t cols, uint32_t w_ld,
                           const float *x, uint32_t ntok, uint32_t k, int norm_topk,
                           const float *escale, uint32_t *ids, float *wout, float *logits,
                           uint32_t *counters);

@@ -44,8 +44,79 @@ uint64_t row_bytes_of(uint32_t t, uint64_t cols) {
 
 // ── launch helper ──────────────────────────────────────────────────────────
 
+cudaEvent_t Profiler::get_event() {
+    if (n_pool > 0) return pool[--n_pool];
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+void Profiler::begin(const char *label, cudaStream_t s, Rec &r) {
+    r.label = label;
+    r.a = get_event();
+    r.b = get_event();
+    cudaEventRecord(r.a, s);
+}
+
+void Profiler::end(Rec &r, cudaStream_t s) {
+    cudaEventRecord(r.b, s);
+    if (n_pending < (int)(sizeof(pending) / sizeof(pending[0]))) {
+        pending[n_pending++] = r;
+    } else {  // table full: drop the sample, recycle its events
+        if (n_pool + 2 <= (int)(sizeof(pool) / sizeof(pool[0]))) {
+            pool[n_pool++] = r.a;
+            pool[n_pool++] = r.b;
+        } else {
+            cudaEventDestroy(r.a);
+            cudaEventDestroy(r.b);
+        }
+    }
+}
+
+cudaError_t Profiler::flush() {
+    cudaError_t err = cudaSuccess;
+    for (int i = 0; i < n_pending; i++) {
+        Rec &r = pending[i];
+        float ms = 0.0f;
+        cudaError_t e = cudaEventSynchronize(r.b);
+        if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, r.a, r.b);
+        if (e != cudaSuccess) {
+            err = e;
+        } else {
+            int j = 0;
+            while (j < n_agg && agg[j].label != r.label) j++;
+            if (j == n_agg && n_agg < (int)(sizeof(agg) / sizeof(agg[0]))) {
+                agg[n_agg++] = Agg{r.label, 0, 0.0, 1e30, 0.0};
+            }
+            if (j < n_agg) {
+                agg[j].count++;
+                agg[j].total_ms += ms;
+                agg[j].min_ms = ms < agg[j].min_ms ? ms : agg[j].min_ms;
+                agg[j].max_ms = ms > agg[j].max_ms ? ms : agg[j].max_ms;
+            }
+        }
+        if (n_pool + 2 <= (int)(sizeof(pool) / sizeof(pool[0]))) {
+            pool[n_pool++] = r.a;
+            pool[n_pool++] = r.b;
+        } else {
+            cudaEventDestroy(r.a);
+            cudaEventDestroy(r.b);
+        }
+    }
+    n_pending = 0;
+    return err;
+}
+
+void Profiler::reset() { n_agg = 0; }
+
+void Profiler::destroy() {
+    flush();
+    for (int i = 0; i < n_pool; i++) cudaEventDestroy(pool[i]);
+    n_pool = 0;
+}
+
 template <typename Kern, typename... Args>
-static cudaError_t launch_k(const LaunchCfg &c, Kern kern, dim3 grid, dim3 block, size_t smem,
+static cudaError_t launch_k(const LaunchCfg &c, const char *label, Kern kern, dim3 grid, dim3 block, size_t smem,
                             Args... args) {
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -58,13 +129,29 @@ static cudaError_t launch_k(const LaunchCfg &c, Kern kern, dim3 grid, dim3 block
     cfg.stream = c.stream;
     cudaLaunchAttribute attr[1];
     cfg.numAttrs = 0;
-    if (c.pdl) {
+    const bool timed = c.prof && c.prof->on;
+    if (c.pdl && !timed) {  // events between kernels would serialise them anyway
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
     }
-    return cudaLaunchKernelEx(&cfg, kern, args...);
+    Profiler::Rec rec;
+    if (timed) c.prof->begin(label, c.stream, rec);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+    if (timed) c.prof->end(rec, c.stream);
+    return e;
+}
+
+// Static per-type profiler labels for "qmv", "moe_gate_up" and "moe_down".
+template <uint32_t TYPE>
+static const char *type_label(const char *kind) {
+    static const char *const names[3][3] = {{"qmv_q4k", "qmv_q6k", "qmv_q8_0"},
+                                            {"moe_gate_up_q4k", "moe_gate_up_q6k", "moe_gate_up_q8_0"},
+                                            {"moe_down_q4k", "moe_down_q6k", "moe_down_q8_0"}};
+    const int t = TYPE == T_Q4_K ? 0 : TYPE == T_Q6_K ? 1 : 2;
+    const int k = kind[0] == 'q' ? 0 : kind[4] == 'g' ? 1 : 2;
+    return names[k][t];
 }
 
 // ── exact element decoders (src/quant/dequant.zig) ─────────────────────────
@@ -135,7 +222,7 @@ cudaError_t launch_dequant(const LaunchCfg &c, const DevMat &m, uint64_t row0, u
     if (n == 0) return cudaSuccess;
     const uint64_t want = (n + 255) / 256;
     const unsigned grid = (unsigned)(want < 65535ull * 8 ? want : 65535ull * 8);
-    return launch_k(c, k_dequant, dim3(grid), dim3(256), 0, m.data, m.type, m.pitch, m.cols, row0, n, out);
+    return launch_k(c, "dequant", k_dequant, dim3(grid), dim3(256), 0, m.data, m.type, m.pitch, m.cols, row0, n, out);
 }
 
 // ── activations quantised in shared memory ─────────────────────────────────
@@ -566,7 +653,7 @@ static cudaError_t launch_qmv_t(const LaunchCfg &c, const DevMat &m, const uint8
     a.dev_err = c.dev_err;
     const size_t smem = tile_smem_bytes((size_t)a.rt * a.pitch, NT, (int)a.nitems, NT * (int)(a.rt * a.nitems));
     const dim3 grid((a.nrows + a.rt - 1) / a.rt);
-    return launch_k(c, k_qmv<TYPE, NT>, grid, dim3(256), smem, a);
+    return launch_k(c, type_label<TYPE>("qmv"), k_qmv<TYPE, NT>, grid, dim3(256), smem, a);
 }
 
 cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert, const float *x, float *y,
@@ -579,7 +666,7 @@ cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert,
     default: {
         const uint64_t want = (m.rows + 7) / 8;
         const uint32_t blocks = (uint32_t)(want < 65535 ? want : 65535);
-        return launch_k(c, k_mv_float, dim3(blocks), dim3(256), 0, rows, m.pitch, m.type, (uint32_t)m.rows,
+        return launch_k(c, "qmv_float", k_mv_float, dim3(blocks), dim3(256), 0, rows, m.pitch, m.type, (uint32_t)m.rows,
                         (uint32_t)m.cols, x, y, ntok);
     }
     }
@@ -625,7 +712,7 @@ __global__ void k_moe_plan(const uint32_t *ids, uint32_t npairs, uint32_t E, Moe
 
 cudaError_t launch_moe_plan(const LaunchCfg &c, const uint32_t *ids, uint32_t ntok, uint32_t k, uint32_t E,
                             const MoePlan &p) {
-    return launch_k(c, k_moe_plan, dim3(1), dim3(1024), (size_t)2 * E * 4, ids, ntok * k, E, p);
+    return launch_k(c, "moe_plan", k_moe_plan, dim3(1), dim3(1024), (size_t)2 * E * 4, ids, ntok * k, E, p);
 }
 
 // ── MoE: grouped gate/up with fused activation ─────────────────────────────
@@ -756,7 +843,7 @@ static cudaError_t launch_gate_up_t(const LaunchCfg &c, const DevMat &gate, cons
     const uint32_t E = gate.n_experts ? gate.n_experts : 1;
     const uint32_t ny = direct ? k : min(E, ntok * k);
     const dim3 grid((a.F + a.rt - 1) / a.rt, ny);
-    return launch_k(c, k_moe_gate_up<TYPE, NT>, grid, dim3(256), smem, a);
+    return launch_k(c, type_label<TYPE>("moe_gate_up"), k_moe_gate_up<TYPE, NT>, grid, dim3(256), smem, a);
 }
 
 cudaError_t launch_moe_gate_up(const LaunchCfg &c, const DevMat &gate, const DevMat &up, int act, const float *x,
@@ -864,7 +951,7 @@ static cudaError_t launch_down_t(const LaunchCfg &c, const DevMat &down, const f
     a.dev_err = c.dev_err;
     const size_t smem = tile_smem_bytes((size_t)k * a.rt * a.pitch, (int)k, (int)a.nitems, (int)(k * a.rt * a.nitems));
     const dim3 grid((a.D + a.rt - 1) / a.rt, ntok);
-    return launch_k(c, k_moe_down<TYPE>, grid, dim3(256), smem, a);
+    return launch_k(c, type_label<TYPE>("moe_down"), k_moe_down<TYPE>, grid, dim3(256), smem, a);
 }
 
 cudaError_t launch_moe_down(const LaunchCfg &c, const DevMat &down, const float *h, uint32_t ntok, uint32_t k,
@@ -920,8 +1007,8 @@ LT_DEVINL float router_logit(const float *wrow, const float *x, uint32_t cols, i
 }
 
 __global__ void __launch_bounds__(kRouterWarps * 32)
-    k_router(const float *W, uint32_t E, uint32_t cols, const float *x, uint32_t ntok, uint32_t k, int norm_topk,
-             const float *escale, uint32_t *ids, float *wout, float *logits, uint32_t *counters) {
+    k_router(const float *W, uint32_t E, uint32_t cols, uint32_t w_ld, const float *x, uint32_t ntok, uint32_t k,
+             int norm_topk, const float *escale, uint32_t *ids, float *wout, float *logits, uint32_t *counters) {
     __shared__ int s_last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t e = blockIdx.x * kRouterWarps + warp;
@@ -930,7 +1017,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32)
     pdl_wait();
     if (e < E) {
         for (uint32_t tt = 0; tt < nt; tt++) {
-            const float v = router_logit(W + (size_t)e * cols, x + (size_t)(t0 + tt) * cols, cols, lane);
+            const float v = router_logit(W + (size_t)e * w_ld, x + (size_t)(t0 + tt) * cols, cols, lane);
             if (lane == 0) logits[(size_t)(t0 + tt) * E + e] = v;
         }
     }
@@ -1004,12 +1091,12 @@ __global__ void __launch_bounds__(kRouterWarps * 32)
     if (threadIdx.x == 0) counters[blockIdx.y] = 0;
 }
 
-cudaError_t launch_router(const LaunchCfg &c, const float *w, uint32_t E, uint32_t cols, const float *x,
-                          uint32_t ntok, uint32_t k, int norm_topk, const float *escale, uint32_t *ids, float *wout,
-                          float *logits, uint32_t *counters) {
+cudaError_t launch_router(const LaunchCfg &c, const float *w, uint32_t E, uint32_t cols, uint32_t w_ld,
+                          const float *x, uint32_t ntok, uint32_t k, int norm_topk, const float *escale, uint32_t *ids,
+                          float *wout, float *logits, uint32_t *counters) {
     const dim3 grid((E + kRouterWarps - 1) / kRouterWarps, router_token_groups(ntok));
-    return launch_k(c, k_router, grid, dim3(kRouterWarps * 32), 0, w, E, cols, x, ntok, k, norm_topk, escale, ids,
-                    wout, logits, counters);
+    return launch_k(c, "router_topk", k_router, grid, dim3(kRouterWarps * 32), 0, w, E, cols, w_ld, x, ntok, k,
+                    norm_topk, escale, ids, wout, logits, counters);
 }
 
 // ── rmsnorm / softmax / argmax ─────────────────────────────────────────────
@@ -1052,7 +1139,7 @@ __global__ void k_rmsnorm(const float *x, const float *w, float eps, uint32_t n,
 
 cudaError_t launch_rmsnorm(const LaunchCfg &c, const float *x, const float *w, float eps, uint32_t n, uint32_t ntok,
                            float *y) {
-    return launch_k(c, k_rmsnorm, dim3(ntok), dim3(256), 0, x, w, eps, n, y);
+    return launch_k(c, "rmsnorm", k_rmsnorm, dim3(ntok), dim3(256), 0, x, w, eps, n, y);
 }
 
 // src/ops/math.zig:29-35
@@ -1074,7 +1161,7 @@ __global__ void k_softmax(float *x, uint32_t n) {
 }
 
 cudaError_t launch_softmax(const LaunchCfg &c, float *x, uint32_t n, uint32_t ntok) {
-    return launch_k(c, k_softmax, dim3(ntok), dim3(256), 0, x, n);
+    return launch_k(c, "softmax", k_softmax, dim3(ntok), dim3(256), 0, x, n);
 }
 
 // greedy (src/model/sample.zig:11-17): first index of the maximum.  NaNs are
@@ -1132,7 +1219,7 @@ __global__ void k_argmax(const float *x, uint32_t n, uint32_t *idx, float *pv, u
 cudaError_t launch_argmax(const LaunchCfg &c, const float *x, uint32_t n, uint32_t ntok, uint32_t *idx, float *pv,
                           uint32_t *pi, uint32_t *counters) {
     const uint32_t nb = max(1u, min(64u, (n + 4095) / 4096));
-    return launch_k(c, k_argmax, dim3(nb, ntok), dim3(256), 0, x, n, idx, pv, pi, counters);
+    return launch_k(c, "argmax", k_argmax, dim3(nb, ntok), dim3(256), 0, x, n, idx, pv, pi, counters);
 }
 
 }  // namespace lt
