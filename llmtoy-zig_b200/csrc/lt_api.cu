@@ -534,6 +534,7 @@ static lt_status check_router(lt_ctx *ctx, const lt_tensor *router, uint32_t k) 
         return fail(ctx, LT_EINVAL, "router: %llu experts (max %d)", (unsigned long long)router->m.rows,
                     lt::kRouterMaxE);
     if (k == 0 || k > 16 || k > router->m.rows) return fail(ctx, LT_EINVAL, "router: k=%u", k);
+    if (router->m.cols > 8192) return fail(ctx, LT_EINVAL, "router: width %llu > 8192", (unsigned long long)router->m.cols);
     return LT_OK;
 }
 

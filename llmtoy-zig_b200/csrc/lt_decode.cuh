@@ -1,0 +1,302 @@
+// lt_decode.cuh — activations quantised in shared memory and the GGUF block
+// decoders that take dot products against them.
+//
+// Activations.  Each 32-element block of an activation row is stored as two
+// int16 terms, x ~= s * (hi + lo / 65534) with s = amax / 32767: hi is
+// round(x / s) and lo rounds the remainder at 1/65534 of a step.  That keeps
+// about 31 bits of the block's dynamic range, so products with the quant
+// values (4-8 bit integers) accumulate exactly in int32 via dp2a and the only
+// rounding left is the f32 block-scale arithmetic.  (One int16 term alone
+// loses too much when expert outputs cancel in the weighted combine.)
+//
+// Layout per token t and item i (256 columns): hi values at xq + t*tok_bytes +
+// i*528, lo values at the same offset from xl; 8 int16 of padding per item put
+// threads that decode different items in different banks.  Per 32-block:
+// scale xs; per 16-group: f32 sum of the original values xsum16 (used for the
+// Q4_K minimum and the Q6_K -32 offset terms, which are applied in f32).
+#pragma once
+
+#include "lt_common.cuh"
+
+namespace lt {
+
+constexpr int kXItemPitch = 528;           // 256 int16 + 16 bytes of padding
+constexpr float kLoScale = 1.0f / 65534.0f;
+
+struct XS {
+    uint8_t *xq;    // hi terms
+    uint8_t *xl;    // lo terms
+    float *xs;      // [t][item*8 + block] scale
+    float *xsum16;  // [t][item*16 + group] sum of x over 16 elements
+    int nitems;
+    int tok_bytes;  // nitems * 528
+    int tok_blk;    // nitems * 8
+};
+
+__host__ __device__ inline size_t xs_bytes(int ntok, int nitems) {
+    return (size_t)ntok * nitems * (2 * kXItemPitch + 8 * 4 + 16 * 4);
+}
+
+LT_DEVINL XS xs_carve(uint8_t *p, int ntok, int nitems) {
+    XS x;
+    x.nitems = nitems;
+    x.tok_bytes = nitems * kXItemPitch;
+    x.tok_blk = nitems * 8;
+    x.xq = p;
+    p += (size_t)ntok * x.tok_bytes;
+    x.xl = p;
+    p += (size_t)ntok * x.tok_bytes;
+    x.xs = reinterpret_cast<float *>(p);
+    p += (size_t)ntok * nitems * 8 * 4;
+    x.xsum16 = reinterpret_cast<float *>(p);
+    return x;
+}
+
+// Quantise nt activation rows (row pointers in shared memory) of `cols`
+// floats.  Warps own 32-blocks; each warp issues up to 16 block loads before
+// it reduces any of them, so the prologue costs one memory latency, not one
+// per block.
+LT_DEVINL void prep_x(const XS &X, const float *const *src, int nt, int cols) {
+    constexpr int kBatch = 16;
+    const int nblk = cols >> 5;
+    const int total = nt * nblk;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int base = warp; base < total; base += nw * kBatch) {
+        float v[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; j++) {
+            const int task = base + j * nw;
+            v[j] = 0.0f;
+            if (task < total) {
+                const int t = task / nblk, b = task - t * nblk;
+                v[j] = src[t][32 * b + lane];
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; j++) {
+            const int task = base + j * nw;
+            if (task >= total) break;
+            const int t = task / nblk, b = task - t * nblk;
+            float amax = fabsf(v[j]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            int qh = 0, ql = 0;
+            float s = 0.0f;
+            if (amax > 0.0f) {
+                const float inv = 32767.0f / amax;
+                s = amax / 32767.0f;
+                qh = max(-32767, min(32767, __float2int_rn(v[j] * inv)));
+                const float r = fmaf(-(float)qh, s, v[j]);  // remainder, |r| <~ s/2
+                ql = max(-32767, min(32767, __float2int_rn(r * inv * 65534.0f)));
+            }
+            const int e = 32 * b + lane;
+            const size_t off = (size_t)t * X.tok_bytes + (e >> 8) * kXItemPitch;
+            reinterpret_cast<int16_t *>(X.xq + off)[e & 255] = (int16_t)qh;
+            reinterpret_cast<int16_t *>(X.xl + off)[e & 255] = (int16_t)ql;
+            float sum = v[j];
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (lane == 0) X.xs[t * X.tok_blk + b] = s;
+            if ((lane & 15) == 0) X.xsum16[t * X.tok_blk * 2 + 2 * b + (lane >> 4)] = sum;
+        }
+    }
+}
+
+// Load 32 consecutive activation values (hi and lo terms) as int16 pairs.
+LT_DEVINL void load_x32(const XS &X, int t, int item, int elem0, uint32_t (&hi)[16], uint32_t (&lo)[16]) {
+    const size_t off = (size_t)t * X.tok_bytes + item * kXItemPitch + 2 * elem0;
+#pragma unroll
+    for (int v = 0; v < 4; v++) {
+        const uint4 h4 = lds128(X.xq + off + 16 * v), l4 = lds128(X.xl + off + 16 * v);
+        hi[4 * v] = h4.x; hi[4 * v + 1] = h4.y; hi[4 * v + 2] = h4.z; hi[4 * v + 3] = h4.w;
+        lo[4 * v] = l4.x; lo[4 * v + 1] = l4.y; lo[4 * v + 2] = l4.z; lo[4 * v + 3] = l4.w;
+    }
+}
+
+// ── Q4_K superblock: [f16 d][f16 dmin][12 B 6-bit scales/mins][128 B nibbles] ──
+template <int NT>
+LT_DEVINL void dot_q4k(const uint8_t *sbp, int item, const XS &X, int t0, int nt, float (&res)[NT]) {
+    const uint4 hdr = lds128(sbp);
+    const float d = f16_bits_to_f32(hdr.x), dmin = f16_bits_to_f32(hdr.x >> 16);
+    // scale_min (src/quant/dequant.zig:291-300) for sub-blocks 0-3 and 4-7, one byte each
+    const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu, mn_lo = hdr.z & 0x3F3F3F3Fu;
+    const uint32_t sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
+    const uint32_t mn_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+        const uint32_t scw = c < 2 ? sc_lo : sc_hi, mnw = c < 2 ? mn_lo : mn_hi;
+        const int j0 = (2 * c) & 3, j1 = (2 * c + 1) & 3;
+        const float dA = d * byte_to_f32(scw, j0), mA = dmin * byte_to_f32(mnw, j0);
+        const float dB = d * byte_to_f32(scw, j1), mB = dmin * byte_to_f32(mnw, j1);
+        const uint4 qa = lds128(sbp + 16 + 32 * c), qb = lds128(sbp + 32 + 32 * c);
+        const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        uint32_t lo[8], hi[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            lo[k] = w[k] & 0x0F0F0F0Fu;          // elements 64c + 4k.. (sub-block 2c)
+            hi[k] = (w[k] >> 4) & 0x0F0F0F0Fu;   // elements 64c + 32 + 4k.. (sub-block 2c+1)
+        }
+#pragma unroll
+        for (int tt = 0; tt < NT; tt++) {
+            if (tt < nt) {
+                const int t = t0 + tt;
+                uint32_t ah[16], al[16], bh[16], bl[16];
+                load_x32(X, t, item, 64 * c, ah, al);
+                load_x32(X, t, item, 64 * c + 32, bh, bl);
+                int aH = 0, aL = 0, bH = 0, bL = 0;
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    aH = dp2a_hi_su((int)ah[2 * k + 1], lo[k], dp2a_lo_su((int)ah[2 * k], lo[k], aH));
+                    aL = dp2a_hi_su((int)al[2 * k + 1], lo[k], dp2a_lo_su((int)al[2 * k], lo[k], aL));
+                    bH = dp2a_hi_su((int)bh[2 * k + 1], hi[k], dp2a_lo_su((int)bh[2 * k], hi[k], bH));
+                    bL = dp2a_hi_su((int)bl[2 * k + 1], hi[k], dp2a_lo_su((int)bl[2 * k], hi[k], bL));
+                }
+                const float *xs = X.xs + t * X.tok_blk + item * 8;
+                const float *x16 = X.xsum16 + t * X.tok_blk * 2 + item * 16;
+                const float qa_ = (float)aH + (float)aL * kLoScale, qb_ = (float)bH + (float)bL * kLoScale;
+                res[tt] += dA * xs[2 * c] * qa_ - mA * (x16[4 * c] + x16[4 * c + 1]);
+                res[tt] += dB * xs[2 * c + 1] * qb_ - mB * (x16[4 * c + 2] + x16[4 * c + 3]);
+            }
+        }
+    }
+}
+
+// 4 bytes starting at static byte offset O of a word array.
+template <int O>
+LT_DEVINL uint32_t word_at(const uint32_t *w) {
+    if constexpr ((O & 3) == 0) {
+        return w[O >> 2];
+    } else {
+        return __byte_perm(w[O >> 2], w[(O >> 2) + 1],
+                           (uint32_t)(((O & 3) + 3) << 12 | ((O & 3) + 2) << 8 | ((O & 3) + 1) << 4 | (O & 3)));
+    }
+}
+
+template <int B, int NT>
+LT_DEVINL void dot_q8_block(const uint32_t *w, int item, const XS &X, int t0, int nt, float (&res)[NT]) {
+    const float d = f16_bits_to_f32(word_at<34 * B>(w) & 0xffffu);
+    uint32_t q[8];
+    q[0] = word_at<34 * B + 2>(w);
+    q[1] = word_at<34 * B + 6>(w);
+    q[2] = word_at<34 * B + 10>(w);
+    q[3] = word_at<34 * B + 14>(w);
+    q[4] = word_at<34 * B + 18>(w);
+    q[5] = word_at<34 * B + 22>(w);
+    q[6] = word_at<34 * B + 26>(w);
+    q[7] = word_at<34 * B + 30>(w);
+#pragma unroll
+    for (int tt = 0; tt < NT; tt++) {
+        if (tt < nt) {
+            const int t = t0 + tt;
+            uint32_t xh[16], xl[16];
+            load_x32(X, t, item, 32 * B, xh, xl);
+            int aH = 0, aL = 0;
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                aH = dp2a_hi_ss((int)xh[2 * k + 1], q[k], dp2a_lo_ss((int)xh[2 * k], q[k], aH));
+                aL = dp2a_hi_ss((int)xl[2 * k + 1], q[k], dp2a_lo_ss((int)xl[2 * k], q[k], aL));
+            }
+            res[tt] += d * X.xs[t * X.tok_blk + item * 8 + B] * ((float)aH + (float)aL * kLoScale);
+        }
+    }
+}
+
+// Q8_0 group of eight 34-byte blocks (272 B, 16-byte aligned); nb < 8 only
+// for the last group of a row whose block count is not a multiple of 8.
+template <int NT>
+LT_DEVINL void dot_q8_0(const uint8_t *gp, int item, int nb, const XS &X, int t0, int nt, float (&res)[NT]) {
+    uint32_t w[68];
+#pragma unroll
+    for (int i = 0; i < 17; i++) {
+        const uint4 v = lds128(gp + 16 * i);
+        w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+    }
+    dot_q8_block<0>(w, item, X, t0, nt, res);
+    if (nb > 1) dot_q8_block<1>(w, item, X, t0, nt, res);
+    if (nb > 2) dot_q8_block<2>(w, item, X, t0, nt, res);
+    if (nb > 3) dot_q8_block<3>(w, item, X, t0, nt, res);
+    if (nb > 4) dot_q8_block<4>(w, item, X, t0, nt, res);
+    if (nb > 5) dot_q8_block<5>(w, item, X, t0, nt, res);
+    if (nb > 6) dot_q8_block<6>(w, item, X, t0, nt, res);
+    if (nb > 7) dot_q8_block<7>(w, item, X, t0, nt, res);
+}
+
+// Q6_K superblock (210 B, only 2-byte aligned): [ql 128][qh 64][i8 sc 16][f16 d].
+// Words are read 4-byte aligned and realigned with one PRMT each.
+template <int NT>
+LT_DEVINL void dot_q6k(const uint8_t *sbp, int item, const XS &X, int t0, int nt, float (&res)[NT]) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(sbp);
+    const uint8_t *pa = reinterpret_cast<const uint8_t *>(a & ~(uintptr_t)3);
+    const uint32_t sel = (a & 2) ? 0x5432u : 0x3210u;
+    uint32_t rs[6];
+#pragma unroll
+    for (int i = 0; i < 6; i++) rs[i] = lds32(pa + 4 * (48 + i));
+    uint32_t scw[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) scw[i] = __byte_perm(rs[i], rs[i + 1], sel);
+    const float d = f16_bits_to_f32(__byte_perm(rs[4], rs[5], sel) & 0xffffu);
+#pragma unroll
+    for (int n = 0; n < 2; n++) {
+        uint32_t rq[17], rh[9];
+#pragma unroll
+        for (int i = 0; i < 17; i++) rq[i] = lds32(pa + 4 * (16 * n + i));
+#pragma unroll
+        for (int i = 0; i < 9; i++) rh[i] = lds32(pa + 4 * (32 + 8 * n + i));
+        uint32_t qv[4][8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            const uint32_t qlA = __byte_perm(rq[k], rq[k + 1], sel);
+            const uint32_t qlB = __byte_perm(rq[8 + k], rq[9 + k], sel);
+            const uint32_t h = __byte_perm(rh[k], rh[k + 1], sel);
+            qv[0][k] = (qlA & 0x0F0F0F0Fu) | ((h << 4) & 0x30303030u);          // 128n + l
+            qv[1][k] = (qlB & 0x0F0F0F0Fu) | ((h << 2) & 0x30303030u);          // 128n + 32 + l
+            qv[2][k] = ((qlA >> 4) & 0x0F0F0F0Fu) | (h & 0x30303030u);          // 128n + 64 + l
+            qv[3][k] = ((qlB >> 4) & 0x0F0F0F0Fu) | ((h >> 2) & 0x30303030u);   // 128n + 96 + l
+        }
+#pragma unroll
+        for (int kind = 0; kind < 4; kind++) {
+            // i8 scales for l in [0,16) and [16,32): sc[8n + is + 2*kind]
+            const int s0 = 8 * n + 2 * kind, s1 = s0 + 1;
+            const float ds0 = d * (float)(int8_t)((scw[s0 >> 2] >> (8 * (s0 & 3))) & 0xffu);
+            const float ds1 = d * (float)(int8_t)((scw[s1 >> 2] >> (8 * (s1 & 3))) & 0xffu);
+#pragma unroll
+            for (int tt = 0; tt < NT; tt++) {
+                if (tt < nt) {
+                    const int t = t0 + tt;
+                    uint32_t xh[16], xl[16];
+                    load_x32(X, t, item, 128 * n + 32 * kind, xh, xl);
+                    int h0 = 0, l0 = 0, h1 = 0, l1 = 0;
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        h0 = dp2a_hi_su((int)xh[2 * k + 1], qv[kind][k], dp2a_lo_su((int)xh[2 * k], qv[kind][k], h0));
+                        l0 = dp2a_hi_su((int)xl[2 * k + 1], qv[kind][k], dp2a_lo_su((int)xl[2 * k], qv[kind][k], l0));
+                        h1 = dp2a_hi_su((int)xh[9 + 2 * k], qv[kind][4 + k], dp2a_lo_su((int)xh[8 + 2 * k], qv[kind][4 + k], h1));
+                        l1 = dp2a_hi_su((int)xl[9 + 2 * k], qv[kind][4 + k], dp2a_lo_su((int)xl[8 + 2 * k], qv[kind][4 + k], l1));
+                    }
+                    const int g = 8 * n + 2 * kind;  // 16-group index inside the item
+                    const float *x16 = X.xsum16 + t * X.tok_blk * 2 + item * 16;
+                    const float xsc = X.xs[t * X.tok_blk + item * 8 + 4 * n + kind];
+                    // sum (q - 32) x = s * sum q*xq - 32 * sum x
+                    res[tt] += ds0 * (xsc * ((float)h0 + (float)l0 * kLoScale) - 32.0f * x16[g]);
+                    res[tt] += ds1 * (xsc * ((float)h1 + (float)l1 * kLoScale) - 32.0f * x16[g + 1]);
+                }
+            }
+        }
+    }
+}
+
+// Dot product of one item of a row held in shared memory.
+template <uint32_t TYPE, int NT>
+LT_DEVINL void dot_item(const uint8_t *rowp, int item, int nblocks_row, const XS &X, int t0, int nt,
+                        float (&res)[NT]) {
+    if constexpr (TYPE == T_Q4_K) {
+        dot_q4k<NT>(rowp + 144 * item, item, X, t0, nt, res);
+    } else if constexpr (TYPE == T_Q6_K) {
+        dot_q6k<NT>(rowp + 210 * item, item, X, t0, nt, res);
+    } else {
+        const int nb = min(8, nblocks_row - 8 * item);
+        dot_q8_0<NT>(rowp + 272 * item, item, nb, X, t0, nt, res);
+    }
+}
+
+}  // namespace lt

@@ -10,6 +10,7 @@
 #include <utility>
 
 #include "lt_common.cuh"
+#include "lt_decode.cuh"
 #include "lt_internal.h"
 
 namespace lt {
@@ -225,273 +226,7 @@ cudaError_t launch_dequant(const LaunchCfg &c, const DevMat &m, uint64_t row0, u
     return launch_k(c, "dequant", k_dequant, dim3(grid), dim3(256), 0, m.data, m.type, m.pitch, m.cols, row0, n, out);
 }
 
-// ── activations quantised in shared memory ─────────────────────────────────
-// Token t, item i (256 columns): int16 values at xq + t*tok_bytes + i*528
-// (8 int16 of padding per item keep lanes on different items in different
-// banks); per 32-block scale xs, f32 block sum xsum; per 16-group int sum xqs.
-
-constexpr int kXItemPitch = 528;  // 256 int16 + 16 bytes of padding
-
-struct XS {
-    uint8_t *xq;
-    float *xs;
-    float *xsum;
-    int *xqs;
-    int nitems;
-    int tok_bytes;  // nitems * 528
-    int tok_blk;    // nitems * 8
-};
-
-__host__ __device__ inline size_t xs_bytes(int ntok, int nitems) {
-    return (size_t)ntok * nitems * (kXItemPitch + 8 * 4 + 8 * 4 + 16 * 4);
-}
-
-LT_DEVINL XS xs_carve(uint8_t *p, int ntok, int nitems) {
-    XS x;
-    x.nitems = nitems;
-    x.tok_bytes = nitems * kXItemPitch;
-    x.tok_blk = nitems * 8;
-    x.xq = p;
-    p += (size_t)ntok * x.tok_bytes;
-    x.xs = reinterpret_cast<float *>(p);
-    p += (size_t)ntok * nitems * 8 * 4;
-    x.xsum = reinterpret_cast<float *>(p);
-    p += (size_t)ntok * nitems * 8 * 4;
-    x.xqs = reinterpret_cast<int *>(p);
-    return x;
-}
-
-// Quantise nt activation rows (pointers in shared memory) of `cols` floats.
-// One warp per 32-block: scale = amax/32767, q = rint(x/scale).
-LT_DEVINL void prep_x(const XS &X, const float *const *src, int nt, int cols) {
-    const int nblk = cols >> 5;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int task = warp; task < nt * nblk; task += nw) {
-        const int t = task / nblk, b = task - t * nblk;
-        const float v = src[t][32 * b + lane];
-        float amax = fabsf(v);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        int q = 0;
-        if (amax > 0.0f) {
-            q = __float2int_rn(v * (32767.0f / amax));
-            q = max(-32767, min(32767, q));
-        }
-        const int e = 32 * b + lane;
-        reinterpret_cast<int16_t *>(X.xq + t * X.tok_bytes + (e >> 8) * kXItemPitch)[e & 255] = (int16_t)q;
-        float s = v;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        int qs = q;
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
-        if (lane == 0) {
-            X.xs[t * X.tok_blk + b] = amax / 32767.0f;
-            X.xsum[t * X.tok_blk + b] = s;
-        }
-        if ((lane & 15) == 0) X.xqs[t * X.tok_blk * 2 + 2 * b + (lane >> 4)] = qs;
-    }
-}
-
-// ── item decoders (weights in shared memory) ───────────────────────────────
-
-// Q4_K superblock: [f16 d][f16 dmin][12 B 6-bit scales/mins][128 B nibbles].
-template <int NT>
-LT_DEVINL void dot_q4k(const uint8_t *sbp, int item, const XS &X, int t0, int nt, float (&res)[NT]) {
-    const uint4 hdr = lds128(sbp);
-    const float d = f16_bits_to_f32(hdr.x), dmin = f16_bits_to_f32(hdr.x >> 16);
-    // scale_min (dequant.zig:291-300) for sub-blocks 0-3 and 4-7, one byte each
-    const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu, mn_lo = hdr.z & 0x3F3F3F3Fu;
-    const uint32_t sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
-    const uint32_t mn_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
-#pragma unroll
-    for (int c = 0; c < 4; c++) {
-        const uint32_t scw = c < 2 ? sc_lo : sc_hi, mnw = c < 2 ? mn_lo : mn_hi;
-        const int j0 = (2 * c) & 3, j1 = (2 * c + 1) & 3;
-        const float dA = d * byte_to_f32(scw, j0), mA = dmin * byte_to_f32(mnw, j0);
-        const float dB = d * byte_to_f32(scw, j1), mB = dmin * byte_to_f32(mnw, j1);
-        const uint4 qa = lds128(sbp + 16 + 32 * c), qb = lds128(sbp + 32 + 32 * c);
-        const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-        uint32_t lo[8], hi[8];
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            lo[k] = w[k] & 0x0F0F0F0Fu;
-            hi[k] = (w[k] >> 4) & 0x0F0F0F0Fu;
-        }
-#pragma unroll
-        for (int tt = 0; tt < NT; tt++) {
-            if (tt < nt) {
-                const int t = t0 + tt;
-                const uint8_t *xq = X.xq + t * X.tok_bytes + item * kXItemPitch + 128 * c;
-                uint32_t xa[16], xb[16];
-#pragma unroll
-                for (int v = 0; v < 4; v++) {
-                    const uint4 a4 = lds128(xq + 16 * v), b4 = lds128(xq + 64 + 16 * v);
-                    xa[4 * v] = a4.x; xa[4 * v + 1] = a4.y; xa[4 * v + 2] = a4.z; xa[4 * v + 3] = a4.w;
-                    xb[4 * v] = b4.x; xb[4 * v + 1] = b4.y; xb[4 * v + 2] = b4.z; xb[4 * v + 3] = b4.w;
-                }
-                int accA = 0, accB = 0;
-#pragma unroll
-                for (int k = 0; k < 8; k++) {
-                    accA = dp2a_lo_su((int)xa[2 * k], lo[k], accA);
-                    accA = dp2a_hi_su((int)xa[2 * k + 1], lo[k], accA);
-                    accB = dp2a_lo_su((int)xb[2 * k], hi[k], accB);
-                    accB = dp2a_hi_su((int)xb[2 * k + 1], hi[k], accB);
-                }
-                const float *xs = X.xs + t * X.tok_blk + item * 8;
-                const float *xsum = X.xsum + t * X.tok_blk + item * 8;
-                res[tt] += dA * xs[2 * c] * (float)accA - mA * xsum[2 * c];
-                res[tt] += dB * xs[2 * c + 1] * (float)accB - mB * xsum[2 * c + 1];
-            }
-        }
-    }
-}
-
-// 4 bytes starting at static byte offset o of a word array.
-template <int O>
-LT_DEVINL uint32_t word_at(const uint32_t *w) {
-    if constexpr ((O & 3) == 0) {
-        return w[O >> 2];
-    } else {
-        return __byte_perm(w[O >> 2], w[(O >> 2) + 1], (uint32_t)(((O & 3) + 3) << 12 | ((O & 3) + 2) << 8 |
-                                                                   ((O & 3) + 1) << 4 | (O & 3)));
-    }
-}
-
-template <int B, int NT>
-LT_DEVINL void dot_q8_block(const uint32_t *w, int item, const XS &X, int t0, int nt, float (&res)[NT]) {
-    const uint32_t dw = word_at<34 * B>(w);
-    const float d = f16_bits_to_f32(dw & 0xffffu);
-    uint32_t q[8];
-    q[0] = word_at<34 * B + 2>(w);
-    q[1] = word_at<34 * B + 6>(w);
-    q[2] = word_at<34 * B + 10>(w);
-    q[3] = word_at<34 * B + 14>(w);
-    q[4] = word_at<34 * B + 18>(w);
-    q[5] = word_at<34 * B + 22>(w);
-    q[6] = word_at<34 * B + 26>(w);
-    q[7] = word_at<34 * B + 30>(w);
-#pragma unroll
-    for (int tt = 0; tt < NT; tt++) {
-        if (tt < nt) {
-            const int t = t0 + tt;
-            const uint8_t *xq = X.xq + t * X.tok_bytes + item * kXItemPitch + 64 * B;
-            int acc = 0;
-#pragma unroll
-            for (int v = 0; v < 4; v++) {
-                const uint4 x4 = lds128(xq + 16 * v);
-                acc = dp2a_lo_ss((int)x4.x, q[2 * v], acc);
-                acc = dp2a_hi_ss((int)x4.y, q[2 * v], acc);
-                acc = dp2a_lo_ss((int)x4.z, q[2 * v + 1], acc);
-                acc = dp2a_hi_ss((int)x4.w, q[2 * v + 1], acc);
-            }
-            res[tt] += d * X.xs[t * X.tok_blk + item * 8 + B] * (float)acc;
-        }
-    }
-}
-
-// Q8_0 group of eight 34-byte blocks (272 B, 16-byte aligned); nb < 8 only
-// for the last group of a row whose block count is not a multiple of 8.
-template <int NT>
-LT_DEVINL void dot_q8_0(const uint8_t *gp, int item, int nb, const XS &X, int t0, int nt, float (&res)[NT]) {
-    uint32_t w[68];
-#pragma unroll
-    for (int i = 0; i < 17; i++) {
-        const uint4 v = lds128(gp + 16 * i);
-        w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
-    }
-    dot_q8_block<0>(w, item, X, t0, nt, res);
-    if (nb > 1) dot_q8_block<1>(w, item, X, t0, nt, res);
-    if (nb > 2) dot_q8_block<2>(w, item, X, t0, nt, res);
-    if (nb > 3) dot_q8_block<3>(w, item, X, t0, nt, res);
-    if (nb > 4) dot_q8_block<4>(w, item, X, t0, nt, res);
-    if (nb > 5) dot_q8_block<5>(w, item, X, t0, nt, res);
-    if (nb > 6) dot_q8_block<6>(w, item, X, t0, nt, res);
-    if (nb > 7) dot_q8_block<7>(w, item, X, t0, nt, res);
-}
-
-// Q6_K superblock (210 B, only 2-byte aligned): [ql 128][qh 64][i8 sc 16][f16 d].
-// Words are read 4-byte aligned and realigned with one PRMT each.
-template <int NT>
-LT_DEVINL void dot_q6k(const uint8_t *sbp, int item, const XS &X, int t0, int nt, float (&res)[NT]) {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(sbp);
-    const uint8_t *pa = reinterpret_cast<const uint8_t *>(a & ~(uintptr_t)3);
-    const uint32_t sel = (a & 2) ? 0x5432u : 0x3210u;
-    uint32_t rs[6];
-#pragma unroll
-    for (int i = 0; i < 6; i++) rs[i] = lds32(pa + 4 * (48 + i));
-    uint32_t scw[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) scw[i] = __byte_perm(rs[i], rs[i + 1], sel);
-    const float d = f16_bits_to_f32(__byte_perm(rs[4], rs[5], sel) & 0xffffu);
-#pragma unroll
-    for (int n = 0; n < 2; n++) {
-        uint32_t rq[17], rh[9];
-#pragma unroll
-        for (int i = 0; i < 17; i++) rq[i] = lds32(pa + 4 * (16 * n + i));
-#pragma unroll
-        for (int i = 0; i < 9; i++) rh[i] = lds32(pa + 4 * (32 + 8 * n + i));
-        uint32_t qv[4][8];
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const uint32_t qlA = __byte_perm(rq[k], rq[k + 1], sel);
-            const uint32_t qlB = __byte_perm(rq[8 + k], rq[9 + k], sel);
-            const uint32_t h = __byte_perm(rh[k], rh[k + 1], sel);
-            qv[0][k] = (qlA & 0x0F0F0F0Fu) | ((h << 4) & 0x30303030u);
-            qv[1][k] = (qlB & 0x0F0F0F0Fu) | ((h << 2) & 0x30303030u);
-            qv[2][k] = ((qlA >> 4) & 0x0F0F0F0Fu) | (h & 0x30303030u);
-            qv[3][k] = ((qlB >> 4) & 0x0F0F0F0Fu) | ((h >> 2) & 0x30303030u);
-        }
-#pragma unroll
-        for (int kind = 0; kind < 4; kind++) {
-            // i8 scales for l in [0,16) and [16,32): sc[8n + is + 2*kind]
-            const int s0 = 8 * n + 2 * kind, s1 = s0 + 1;
-            const float ds0 = d * (float)(int8_t)((scw[s0 >> 2] >> (8 * (s0 & 3))) & 0xffu);
-            const float ds1 = d * (float)(int8_t)((scw[s1 >> 2] >> (8 * (s1 & 3))) & 0xffu);
-#pragma unroll
-            for (int tt = 0; tt < NT; tt++) {
-                if (tt < nt) {
-                    const int t = t0 + tt;
-                    // elements 128n + 32*kind + [0,32)
-                    const uint8_t *xq = X.xq + t * X.tok_bytes + item * kXItemPitch + 2 * (128 * n + 32 * kind);
-                    uint32_t xw[16];
-#pragma unroll
-                    for (int v = 0; v < 4; v++) {
-                        const uint4 x4 = lds128(xq + 16 * v);
-                        xw[4 * v] = x4.x; xw[4 * v + 1] = x4.y; xw[4 * v + 2] = x4.z; xw[4 * v + 3] = x4.w;
-                    }
-                    int acc0 = 0, acc1 = 0;
-#pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        acc0 = dp2a_lo_su((int)xw[2 * k], qv[kind][k], acc0);
-                        acc0 = dp2a_hi_su((int)xw[2 * k + 1], qv[kind][k], acc0);
-                        acc1 = dp2a_lo_su((int)xw[8 + 2 * k], qv[kind][4 + k], acc1);
-                        acc1 = dp2a_hi_su((int)xw[8 + 2 * k + 1], qv[kind][4 + k], acc1);
-                    }
-                    const int g = 8 * n + 2 * kind;  // 16-group index inside the item
-                    const int *xqs = X.xqs + t * X.tok_blk * 2 + item * 16;
-                    const float xsc = X.xs[t * X.tok_blk + item * 8 + 4 * n + kind];
-                    res[tt] += ds0 * xsc * (float)(acc0 - 32 * xqs[g]);
-                    res[tt] += ds1 * xsc * (float)(acc1 - 32 * xqs[g + 1]);
-                }
-            }
-        }
-    }
-}
-
-// Dot product of one item of a row tile held in shared memory.
-template <uint32_t TYPE, int NT>
-LT_DEVINL void dot_item(const uint8_t *rowp, int item, int nblocks_row, const XS &X, int t0, int nt,
-                        float (&res)[NT]) {
-    if constexpr (TYPE == T_Q4_K) {
-        dot_q4k<NT>(rowp + 144 * item, item, X, t0, nt, res);
-    } else if constexpr (TYPE == T_Q6_K) {
-        dot_q6k<NT>(rowp + 210 * item, item, X, t0, nt, res);
-    } else {
-        const int nb = min(8, nblocks_row - 8 * item);
-        dot_q8_0<NT>(rowp + 272 * item, item, nb, X, t0, nt, res);
-    }
-}
+// Activation quantisation and block decoders: lt_decode.cuh.
 
 // ── shared-memory tile bookkeeping ─────────────────────────────────────────
 
@@ -577,6 +312,7 @@ __global__ void __launch_bounds__(256) k_qmv(QmvArgs a) {
         mbar_arrive_expect_tx(S.bar, bytes);
         tma_load_1d(S.tile, a.rows + (uint64_t)r0 * a.pitch, bytes, S.bar);
     }
+    pdl_launch_dependents();
     pdl_wait();
     bool ok = true;
     for (uint32_t c0 = 0; c0 < a.ntok; c0 += NT) {
@@ -677,6 +413,7 @@ cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert,
 __global__ void k_moe_plan(const uint32_t *ids, uint32_t npairs, uint32_t E, MoePlan p) {
     extern __shared__ uint32_t sm_plan[];
     uint32_t *cnt = sm_plan, *cur = sm_plan + E;
+    pdl_launch_dependents();
     pdl_wait();
     for (uint32_t e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
@@ -736,6 +473,9 @@ template <uint32_t TYPE, int NT>
 __global__ void __launch_bounds__(256) k_moe_gate_up(GateUpArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     pdl_wait();
+    // Release the down kernel only now: it reads the router's ids before its
+    // own wait, which is safe once this grid has seen the router complete.
+    pdl_launch_dependents();
     uint32_t e, off, cnt;
     if (a.direct) {
         if (blockIdx.y >= a.k) return;
@@ -877,7 +617,12 @@ struct DownArgs {
 template <uint32_t TYPE>
 __global__ void __launch_bounds__(256) k_moe_down(DownArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    pdl_wait();
+    // Launched early (programmatic dependent launch) while the gate/up kernel
+    // runs.  That kernel only released its dependents after its own wait, so
+    // the router (and the dispatch plan) have completed: the expert ids are
+    // final and this CTA's down-projection weights can stream in now.  The
+    // activations h are read only after pdl_wait().
+    pdl_launch_dependents();
     const uint32_t t = blockIdx.y;
     const uint32_t r0 = blockIdx.x * a.rt;
     const uint32_t nr = min(a.rt, a.D - r0);
@@ -894,16 +639,17 @@ __global__ void __launch_bounds__(256) k_moe_down(DownArgs a) {
         const uint32_t bytes = (uint32_t)(nr * a.pitch);
         mbar_arrive_expect_tx(S.bar, (uint32_t)k * bytes);
         for (int s = 0; s < k; s++) {
-            const uint32_t e = a.ids[t * a.k + s];
+            const uint32_t e = __ldcg(a.ids + t * a.k + s);
             tma_load_1d(S.tile + (size_t)s * nr * a.pitch, a.down + ((uint64_t)e * a.D + r0) * a.pitch, bytes,
                         S.bar);
         }
     }
     if (threadIdx.x < (unsigned)k) {
         const uint32_t pair = t * a.k + threadIdx.x;
-        const uint32_t pos = a.direct ? pair : a.p.pair_pos[pair];
+        const uint32_t pos = a.direct ? pair : __ldcg(a.p.pair_pos + pair);
         S.src[threadIdx.x] = a.h + (size_t)pos * a.F;
     }
+    pdl_wait();
     __syncthreads();
     prep_x(S.X, S.src, k, (int)a.F);
     const bool ok = tile_wait(S.bar, a.dev_err);
@@ -976,48 +722,72 @@ constexpr int kRouterTok = 4;    // tokens per CTA
 
 uint32_t router_token_groups(uint32_t ntok) { return (ntok + kRouterTok - 1) / kRouterTok; }
 
-LT_DEVINL float router_logit(const float *wrow, const float *x, uint32_t cols, int lane) {
+constexpr int kRouterChunk = 64;  // weights per lane kept in registers (2048 columns)
+
+// One expert logit in dotf32 order.  w0 holds this lane's weights for the
+// first 2048 columns (prefetched); xs is the token row in shared memory.
+LT_DEVINL float router_logit(const float *wrow, const float *xs, uint32_t cols, int lane,
+                             const float (&w0)[kRouterChunk]) {
     const uint32_t n32 = cols & ~31u;
     float acc = 0.0f;
-    uint32_t i = 0;
-    for (; i + 256 <= n32; i += 256) {
-        float wv[8], xv[8];
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            wv[j] = __ldg(wrow + i + 32 * j + lane);
-            xv[j] = x[i + 32 * j + lane];
-        }
+    for (int j = 0; j < kRouterChunk; j++)
+        if (32u * j < n32) acc = __fadd_rn(acc, __fmul_rn(w0[j], xs[32 * j + lane]));
+    for (uint32_t base = 32u * kRouterChunk; base < n32; base += 32u * kRouterChunk) {
+        float wv[kRouterChunk];
 #pragma unroll
-        for (int j = 0; j < 8; j++) acc = __fadd_rn(acc, __fmul_rn(wv[j], xv[j]));
+        for (int j = 0; j < kRouterChunk; j++) wv[j] = base + 32u * j < n32 ? __ldg(wrow + base + 32 * j + lane) : 0.f;
+#pragma unroll
+        for (int j = 0; j < kRouterChunk; j++)
+            if (base + 32u * j < n32) acc = __fadd_rn(acc, __fmul_rn(wv[j], xs[base + 32 * j + lane]));
     }
-    for (; i < n32; i += 32) acc = __fadd_rn(acc, __fmul_rn(__ldg(wrow + i + lane), x[i + lane]));
+    uint32_t i = n32;
     // acc = (acc0 + acc1) + (acc2 + acc3), lane l < 8 holds lane l of the 8-vector
     const float a1 = __shfl_sync(0xffffffffu, acc, (lane + 8) & 31);
     const float a2 = __shfl_sync(0xffffffffu, acc, (lane + 16) & 31);
     const float a3 = __shfl_sync(0xffffffffu, acc, (lane + 24) & 31);
     float v = __fadd_rn(__fadd_rn(acc, a1), __fadd_rn(a2, a3));
     for (; i + 8 <= cols; i += 8)
-        if (lane < 8) v = __fadd_rn(v, __fmul_rn(__ldg(wrow + i + lane), x[i + lane]));
+        if (lane < 8) v = __fadd_rn(v, __fmul_rn(__ldg(wrow + i + lane), xs[i + lane]));
     // @reduce(.Add): ((((-0 + v0) + v1) + ...) + v7)
     float sum = -0.0f;
 #pragma unroll
     for (int l = 0; l < 8; l++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, v, l));
-    for (; i < cols; i++) sum = __fadd_rn(sum, __fmul_rn(__ldg(wrow + i), x[i]));
+    for (; i < cols; i++) sum = __fadd_rn(sum, __fmul_rn(__ldg(wrow + i), xs[i]));
     return sum;
 }
 
 __global__ void __launch_bounds__(kRouterWarps * 32)
     k_router(const float *W, uint32_t E, uint32_t cols, uint32_t w_ld, const float *x, uint32_t ntok, uint32_t k,
              int norm_topk, const float *escale, uint32_t *ids, float *wout, float *logits, uint32_t *counters) {
+    extern __shared__ __align__(16) float xsm[];  // [kRouterTok][cols]
     __shared__ int s_last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t e = blockIdx.x * kRouterWarps + warp;
     const uint32_t t0 = blockIdx.y * kRouterTok;
     const uint32_t nt = min((uint32_t)kRouterTok, ntok - t0);
+    const uint32_t n32 = cols & ~31u;
+    // router weights are static: fetch them while the producer of x finishes
+    float w0[kRouterChunk];
+#pragma unroll
+    for (int j = 0; j < kRouterChunk; j++)
+        w0[j] = (e < E && 32u * j < n32) ? __ldg(W + (size_t)e * w_ld + 32 * j + lane) : 0.0f;
+    pdl_launch_dependents();
     pdl_wait();
+    {
+        const float *xt = x + (size_t)t0 * cols;
+        const uint32_t n = nt * cols;
+        if ((cols & 3) == 0 && (reinterpret_cast<uintptr_t>(xt) & 15) == 0) {
+            for (uint32_t i = threadIdx.x; i < n / 4; i += blockDim.x)
+                reinterpret_cast<float4 *>(xsm)[i] = reinterpret_cast<const float4 *>(xt)[i];
+        } else {
+            for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) xsm[i] = xt[i];
+        }
+    }
+    __syncthreads();
     if (e < E) {
         for (uint32_t tt = 0; tt < nt; tt++) {
-            const float v = router_logit(W + (size_t)e * w_ld, x + (size_t)(t0 + tt) * cols, cols, lane);
+            const float v = router_logit(W + (size_t)e * w_ld, xsm + tt * cols, cols, lane, w0);
             if (lane == 0) logits[(size_t)(t0 + tt) * E + e] = v;
         }
     }
@@ -1095,7 +865,8 @@ cudaError_t launch_router(const LaunchCfg &c, const float *w, uint32_t E, uint32
                           const float *x, uint32_t ntok, uint32_t k, int norm_topk, const float *escale, uint32_t *ids,
                           float *wout, float *logits, uint32_t *counters) {
     const dim3 grid((E + kRouterWarps - 1) / kRouterWarps, router_token_groups(ntok));
-    return launch_k(c, "router_topk", k_router, grid, dim3(kRouterWarps * 32), 0, w, E, cols, w_ld, x, ntok, k,
+    const size_t smem = (size_t)kRouterTok * cols * 4;
+    return launch_k(c, "router_topk", k_router, grid, dim3(kRouterWarps * 32), smem, w, E, cols, w_ld, x, ntok, k,
                     norm_topk, escale, ids, wout, logits, counters);
 }
 
@@ -1126,12 +897,23 @@ LT_DEVINL float block_max(float v, float *red) {
 
 // src/ops/math.zig:20-26
 __global__ void k_rmsnorm(const float *x, const float *w, float eps, uint32_t n, float *y) {
+    constexpr int kBatch = 16;
     __shared__ float red[32];
+    pdl_launch_dependents();
     pdl_wait();
     const float *xt = x + (size_t)blockIdx.x * n;
     float *yt = y + (size_t)blockIdx.x * n;
     float ss = 0.0f;
-    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) ss += xt[i] * xt[i];
+    for (uint32_t base = threadIdx.x; base < n; base += kBatch * blockDim.x) {
+        float v[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; j++) {
+            const uint32_t i = base + j * blockDim.x;
+            v[j] = i < n ? xt[i] : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; j++) ss += v[j] * v[j];
+    }
     ss = block_sum(ss, red);
     const float rms_inv = 1.0f / sqrtf(ss / (float)n + eps);
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) yt[i] = xt[i] * rms_inv * w[i];
