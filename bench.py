@@ -3,7 +3,10 @@
 Workload (T=1): one token through L=48 chained MoE
 FFN layers of the Qwen3-30B-A3B shape -- d_model 2048, 128 experts, top-8 with
 renormalised softmax, SwiGLU expert width 768, Q4_K experts, f32 router --
-each layer x <- moe(rmsnorm(x)).  48 distinct weight sets (16.3 GB) make every
+each layer the pre-norm residual MoE block x <- x + moe(rmsnorm(x))
+(src/model/forward.zig:304-309 with the FFN replaced by the MoE; one
+lt_moe_block call: router+norm, gate/up, down+combine+residual kernels).
+48 distinct weight sets (16.3 GB) make every
 step read ~1.07 GB of weights, far more than the 126 MB L2, so no flush is
 needed.  Weights are seeded synthetic bytes with the config's distributions,
 generated on the device.
@@ -184,7 +187,8 @@ class CpuStack:
         for li in range(self.n_layers):
             xn = np.empty_like(xx)
             L.orc_rmsnorm(xn.ctypes.data, xx.ctypes.data, self.norm.ctypes.data, D_MODEL, 1e-6)
-            xx, _, _ = self.oracle.moe_layer(self.layers[li % self.distinct], xn, TOP_K, True, 0, None, self.pool)
+            y, _, _ = self.oracle.moe_layer(self.layers[li % self.distinct], xn, TOP_K, True, 0, None, self.pool)
+            xx = (xx + y).astype(np.float32)
         self.x = xx
 
     def rate(self, budget_s: float, min_tokens: int = 1):
@@ -234,7 +238,7 @@ def run_reference(args) -> None:
 def config_block(args, world: int) -> dict:
     return {"workload": f"config-1 MoE layer (d_model {D_MODEL}, {N_EXPERTS} experts, top-{TOP_K} renormalised, "
                         f"SwiGLU {D_EXPERT}, Q4_K experts, f32 router), T=1 decode, {args.layers} chained layers "
-                        f"x <- moe(rmsnorm(x))",
+                        f"x <- x + moe(rmsnorm(x))",
             "model": "qwen3-30b-a3b MoE stack (synthetic)", "global_batch": world, "seq_len": 1,
             "layers": args.layers, "parallelism": f"replicas x{world}" if world > 1 else "single",
             "l2": f"inputs larger than L2: {args.layers} distinct layers, "
@@ -282,16 +286,11 @@ def main() -> None:
 
     x0 = torch.randn(1, D_MODEL, device="cuda", generator=gen)
     xa = torch.empty(1, D_MODEL, device="cuda")
-    xb = torch.empty(1, D_MODEL, device="cuda")
-    xn = torch.empty(1, D_MODEL, device="cuda")
 
     def step():
-        cur, nxt = xa, xb
-        for L in layers:
-            ctx.rmsnorm(cur, L.norm, 1e-6, D_MODEL, 1, xn)
-            ctx.moe_forward(L.router, L.gate, L.up, L.down, pkg.ACT_SILU, True, None, xn, 1, TOP_K, nxt)
-            cur, nxt = nxt, cur
-        return cur
+        for L in layers:  # in place: xa <- xa + moe(rmsnorm(xa))
+            ctx.moe_block(L.router, L.gate, L.up, L.down, pkg.ACT_SILU, True, None, L.norm, 1e-6, xa, 1, TOP_K, xa)
+        return xa
 
     with torch.cuda.stream(stream):
         xa.copy_(x0)
@@ -406,7 +405,7 @@ def main() -> None:
             "expert_hbm_gbs": step_bytes / (ms_step / 1e3) / 1e9,
             "hbm_frac_of_step": (step_bytes / (ms_step / 1e3) / 1e9) / peak,
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": args.steps * 4 * args.layers, "clocks": clocks,
+            "gpu_launches": args.steps * 3 * args.layers, "clocks": clocks,
             "kernels_profiled": kernels, "layer_bytes": layer_bytes,
             "graph": graph is not None,
         }

@@ -157,6 +157,19 @@ lt_status lt_moe_forward(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *
                          const float *dev_x, uint32_t ntok, uint32_t k, float *dev_out,
                          uint32_t *dev_ids, float *dev_w);
 
+/* The whole MoE FFN block of a decoder layer on device vectors:
+ *   dev_out = dev_x + moe(rmsnorm(dev_x) * dev_norm_w)
+ * i.e. the pre-FFN rmsnorm (src/ops/math.zig:20-26, src/model/forward.zig:304),
+ * the router and experts of lt_moe_forward on the normalised vector, and the
+ * residual add (src/model/forward.zig:309).  The norm and the residual are
+ * fused into the router and down kernels (three launches per layer at one
+ * token).  dev_out may alias dev_x. */
+lt_status lt_moe_block(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *gate,
+                       const lt_tensor *up, const lt_tensor *down, int act, int norm_topk,
+                       const float *dev_expert_scale, const float *dev_norm_w, float eps,
+                       const float *dev_x, uint32_t ntok, uint32_t k, float *dev_out,
+                       uint32_t *dev_ids, float *dev_w);
+
 /* greedy (src/model/sample.zig:11-17): index of the first maximum of each of
  * ntok rows of length n (the argmax shader, src/gpu/shaders/argmax.glsl). */
 lt_status lt_argmax(lt_ctx *ctx, const float *dev_x, uint32_t n, uint32_t ntok,

@@ -30,7 +30,7 @@ EXPORTS = [
     "lt_api_version", "lt_init", "lt_free", "lt_set_stream", "lt_sync", "lt_last_error",
     "lt_status_string", "lt_reserve", "lt_row_bytes", "lt_upload", "lt_upload_from_device",
     "lt_tensor_download", "lt_tensor_describe", "lt_tensor_free", "lt_dequant", "lt_qmatvec",
-    "lt_rmsnorm", "lt_softmax", "lt_moe_route", "lt_moe_ffn", "lt_moe_forward", "lt_argmax",
+    "lt_rmsnorm", "lt_softmax", "lt_moe_route", "lt_moe_ffn", "lt_moe_forward", "lt_moe_block", "lt_argmax",
     "lt_profile_enable", "lt_profile_read", "lt_profile_reset", "lt_capture_begin", "lt_capture_end",
     "lt_graph_launch", "lt_graph_free", "lt_quant_matvec_host", "lt_moe_forward_host",
 ]
@@ -82,6 +82,7 @@ def load_library() -> ctypes.CDLL:
         "lt_moe_route": (I, [P, P, P, U32, U32, I, P, P, P]),
         "lt_moe_ffn": (I, [P, P, P, P, I, P, U32, P, P, U32, P]),
         "lt_moe_forward": (I, [P, P, P, P, P, I, I, P, P, U32, U32, P, P, P]),
+        "lt_moe_block": (I, [P, P, P, P, P, I, I, P, P, F, P, U32, U32, P, P, P]),
         "lt_argmax": (I, [P, P, U32, U32, P]),
         "lt_profile_enable": (I, [P, I]),
         "lt_profile_read": (I, [P, U32, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(U64),
@@ -249,6 +250,13 @@ class Context:
         self._check(self.lib.lt_moe_forward(self.ptr, router.handle, gate.handle, up.handle if up else None,
                                             down.handle, act, int(norm_topk), _ptr(expert_scale), _ptr(x), ntok,
                                             k, _ptr(out), _ptr(ids), _ptr(w)))
+
+    def moe_block(self, router: Tensor, gate: Tensor, up: Tensor | None, down: Tensor, act: int, norm_topk: bool,
+                  expert_scale, norm_w, eps: float, x, ntok: int, k: int, out, ids=None, w=None) -> None:
+        """out = x + moe(rmsnorm(x) * norm_w): the fused MoE FFN block of a layer."""
+        self._check(self.lib.lt_moe_block(self.ptr, router.handle, gate.handle, up.handle if up else None,
+                                          down.handle, act, int(norm_topk), _ptr(expert_scale), _ptr(norm_w), eps,
+                                          _ptr(x), ntok, k, _ptr(out), _ptr(ids), _ptr(w)))
 
     # -- kernel timing / graph capture -------------------------------------
     def profile(self, on: bool) -> None:

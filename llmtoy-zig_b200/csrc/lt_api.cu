@@ -152,17 +152,22 @@ lt_status check_kernel_shape(lt_ctx *ctx, const lt::DevMat &m, const char *what)
     return LT_OK;
 }
 
-// MoE scratch layout for T tokens, k slots, E experts, F expert width.
+// MoE scratch layout for T tokens, k slots, E experts, model width d and
+// expert width F: router outputs, the quantised expert input xq [T] and the
+// quantised expert activations hq [T*k], the dispatch plan.
 struct MoeScratch {
     uint32_t *ids;
     float *w;
-    float *h;
     float *logits;
+    uint8_t *xq;
+    uint64_t xq_pitch;
+    uint8_t *hq;
+    uint64_t hq_pitch;
     lt::MoePlan plan;
     size_t bytes;
 };
 
-MoeScratch moe_layout(uint8_t *base, uint32_t T, uint32_t k, uint32_t E, uint64_t F) {
+MoeScratch moe_layout(uint8_t *base, uint32_t T, uint32_t k, uint32_t E, uint64_t d, uint64_t F) {
     MoeScratch s;
     size_t off = 0;
     auto take = [&](size_t b) {
@@ -171,9 +176,12 @@ MoeScratch moe_layout(uint8_t *base, uint32_t T, uint32_t k, uint32_t E, uint64_
         return p;
     };
     const size_t P = (size_t)T * k;
+    s.xq_pitch = lt::qact_row_pitch(d);
+    s.hq_pitch = lt::qact_row_pitch(F);
     s.ids = (uint32_t *)take(P * 4);
     s.w = (float *)take(P * 4);
-    s.h = (float *)take(P * F * 4);
+    s.xq = take((size_t)T * s.xq_pitch);
+    s.hq = take(P * s.hq_pitch);
     s.logits = (float *)take((size_t)T * E * 4);
     s.plan.n_active = (uint32_t *)take(4);
     s.plan.act_e = (uint32_t *)take((size_t)E * 4);
@@ -368,9 +376,12 @@ lt_status lt_reserve(lt_ctx *ctx, uint32_t max_tokens, uint32_t max_k, uint64_t 
                      uint64_t max_d_expert) {
     lt_status st = enter_uncaptured(ctx, "lt_reserve");
     if (st != LT_OK) return st;
-    const size_t moe = moe_layout(nullptr, max_tokens, max_k, lt::kRouterMaxE, max_d_expert).bytes;
-    const size_t io = 2 * al256((size_t)max_tokens * max_d_model * 4) + 2 * al256((size_t)max_tokens * max_k * 4);
-    st = ensure_scratch(ctx, moe + io);
+    const size_t moe = moe_layout(nullptr, max_tokens, max_k, lt::kRouterMaxE, max_d_model, max_d_expert).bytes;
+    const size_t io = 2 * al256((size_t)max_tokens * max_d_model * 4) + 2 * al256((size_t)max_tokens * max_k * 4) +
+                      al256((size_t)lt::kRouterMaxE * 4);
+    const size_t qmv = al256((size_t)max_tokens * lt::qact_row_pitch(max_d_model > max_d_expert ? max_d_model
+                                                                                                : max_d_expert));
+    st = ensure_scratch(ctx, (moe + io > qmv ? moe + io : qmv));
     if (st != LT_OK) return st;
     return ensure_counters(ctx, 4096 + lt::router_token_groups(max_tokens) + max_tokens);
 }
@@ -493,7 +504,15 @@ lt_status lt_qmatvec(lt_ctx *ctx, const lt_tensor *w, uint32_t expert, const flo
         return fail(ctx, LT_EINVAL, "lt_qmatvec: expert %u out of range", expert);
     if ((st = check_kernel_shape(ctx, w->m, "lt_qmatvec")) != LT_OK) return st;
     if (w->m.rows > 0xffffffffull) return fail(ctx, LT_EINVAL, "lt_qmatvec: too many rows");
-    return launched(ctx, lt::launch_qmatvec(cfg_of(ctx), w->m, expert, dev_x, dev_y, ntok), "qmatvec");
+    const lt::LaunchCfg c = cfg_of(ctx);
+    if (!quantized(w->m.type))
+        return launched(ctx, lt::launch_qmatvec(c, w->m, expert, nullptr, 0, dev_x, dev_y, ntok), "qmatvec");
+    const uint64_t qp = lt::qact_row_pitch(w->m.cols);
+    if ((st = ensure_scratch(ctx, al256((size_t)ntok * qp))) != LT_OK) return st;
+    uint8_t *xq = ctx->scratch;
+    st = launched(ctx, lt::launch_quantize(c, dev_x, (uint32_t)w->m.cols, ntok, xq, qp), "quantize");
+    if (st != LT_OK) return st;
+    return launched(ctx, lt::launch_qmatvec(c, w->m, expert, xq, qp, dev_x, dev_y, ntok), "qmatvec");
 }
 
 lt_status lt_rmsnorm(lt_ctx *ctx, const float *dev_x, const float *dev_w, float eps, uint32_t n, uint32_t ntok,
@@ -538,15 +557,16 @@ static lt_status check_router(lt_ctx *ctx, const lt_tensor *router, uint32_t k) 
     return LT_OK;
 }
 
-static lt_status route_impl(lt_ctx *ctx, const lt_tensor *router, const float *x, uint32_t ntok, uint32_t k,
-                            int norm_topk, const float *escale, uint32_t *ids, float *w, float *logits) {
+static lt_status route_impl(lt_ctx *ctx, const lt_tensor *router, const float *x, const float *norm_w, float eps,
+                            uint32_t ntok, uint32_t k, int norm_topk, const float *escale, uint32_t *ids, float *w,
+                            float *logits, uint8_t *xq, uint64_t xq_pitch) {
     const uint32_t groups = lt::router_token_groups(ntok);
     lt_status st = ensure_counters(ctx, groups);
     if (st != LT_OK) return st;
     return launched(ctx,
                     lt::launch_router(cfg_of(ctx), (const float *)router->m.data, (uint32_t)router->m.rows,
-                                      (uint32_t)router->m.cols, (uint32_t)(router->m.pitch / 4), x, ntok, k,
-                                      norm_topk, escale, ids, w, logits, ctx->counters),
+                                      (uint32_t)router->m.cols, (uint32_t)(router->m.pitch / 4), x, norm_w, eps, ntok,
+                                      k, norm_topk, escale, ids, w, logits, ctx->counters, xq, xq_pitch),
                     "router");
 }
 
@@ -558,8 +578,8 @@ lt_status lt_moe_route(lt_ctx *ctx, const lt_tensor *router, const float *dev_x,
     if (!dev_x || !dev_ids || !dev_w) return fail(ctx, LT_EINVAL, "lt_moe_route: null pointer");
     if (ntok == 0) return LT_OK;
     if ((st = ensure_scratch(ctx, al256((size_t)ntok * router->m.rows * 4))) != LT_OK) return st;
-    return route_impl(ctx, router, dev_x, ntok, k, norm_topk, dev_expert_scale, dev_ids, dev_w,
-                      (float *)ctx->scratch);
+    return route_impl(ctx, router, dev_x, nullptr, 0.0f, ntok, k, norm_topk, dev_expert_scale, dev_ids, dev_w,
+                      (float *)ctx->scratch, nullptr, 0);
 }
 
 static lt_status check_experts(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, const lt_tensor *down,
@@ -579,14 +599,15 @@ static lt_status check_experts(lt_ctx *ctx, const lt_tensor *gate, const lt_tens
     lt_status st;
     if ((st = check_kernel_shape(ctx, gate->m, "moe gate")) != LT_OK) return st;
     if ((st = check_kernel_shape(ctx, down->m, "moe down")) != LT_OK) return st;
+    if (F % 32 != 0) return fail(ctx, LT_EINVAL, "moe: expert width %llu not a multiple of 32", (unsigned long long)F);
     if (k == 0 || k > 16 || k > E) return fail(ctx, LT_EINVAL, "moe: k=%u", k);
     *F_out = F;
     return LT_OK;
 }
 
 static lt_status ffn_impl(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, const lt_tensor *down, int act,
-                          const float *x, uint32_t ntok, const uint32_t *ids, const float *w, uint32_t k, float *out,
-                          const MoeScratch &s) {
+                          uint32_t ntok, const uint32_t *ids, const float *w, uint32_t k, const float *resid,
+                          float *out, const MoeScratch &s) {
     const lt::LaunchCfg c = cfg_of(ctx);
     const bool direct = ntok == 1;
     lt::DevMat upm = up ? up->m : lt::DevMat{};
@@ -596,10 +617,14 @@ static lt_status ffn_impl(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *u
         st = launched(ctx, lt::launch_moe_plan(c, ids, ntok, k, gate->m.n_experts, s.plan), "moe plan");
         if (st != LT_OK) return st;
     }
-    st = launched(ctx, lt::launch_moe_gate_up(c, gate->m, upm, act, x, ntok, k, ids, direct, s.plan, s.h),
+    st = launched(ctx,
+                  lt::launch_moe_gate_up(c, gate->m, upm, act, s.xq, s.xq_pitch, ntok, k, ids, direct, s.plan, s.hq,
+                                         s.hq_pitch),
                   "moe gate_up");
     if (st != LT_OK) return st;
-    return launched(ctx, lt::launch_moe_down(c, down->m, s.h, ntok, k, ids, w, direct, s.plan, out), "moe down");
+    return launched(ctx,
+                    lt::launch_moe_down(c, down->m, s.hq, s.hq_pitch, ntok, k, ids, w, direct, s.plan, resid, out),
+                    "moe down");
 }
 
 lt_status lt_moe_ffn(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, const lt_tensor *down, int act,
@@ -612,10 +637,41 @@ lt_status lt_moe_ffn(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, co
     if (act != LT_ACT_SILU && act != LT_ACT_GELU_TANH) return fail(ctx, LT_EINVAL, "moe: act %d", act);
     if (!dev_x || !dev_ids || !dev_w || !dev_out) return fail(ctx, LT_EINVAL, "lt_moe_ffn: null pointer");
     if (ntok == 0) return LT_OK;
-    const MoeScratch probe = moe_layout(nullptr, ntok, k, gate->m.n_experts, F);
+    const uint64_t d = gate->m.cols;
+    const MoeScratch probe = moe_layout(nullptr, ntok, k, gate->m.n_experts, d, F);
     if ((st = ensure_scratch(ctx, probe.bytes)) != LT_OK) return st;
-    const MoeScratch s = moe_layout(ctx->scratch, ntok, k, gate->m.n_experts, F);
-    return ffn_impl(ctx, gate, up, down, act, dev_x, ntok, dev_ids, dev_w, k, dev_out, s);
+    const MoeScratch s = moe_layout(ctx->scratch, ntok, k, gate->m.n_experts, d, F);
+    st = launched(ctx, lt::launch_quantize(cfg_of(ctx), dev_x, (uint32_t)d, ntok, s.xq, s.xq_pitch), "quantize");
+    if (st != LT_OK) return st;
+    return ffn_impl(ctx, gate, up, down, act, ntok, dev_ids, dev_w, k, nullptr, dev_out, s);
+}
+
+static lt_status forward_impl(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *gate, const lt_tensor *up,
+                              const lt_tensor *down, int act, int norm_topk, const float *dev_expert_scale,
+                              const float *dev_norm_w, float eps, int residual, const float *dev_x, uint32_t ntok,
+                              uint32_t k, float *dev_out, uint32_t *dev_ids, float *dev_w) {
+    lt_status st;
+    uint64_t F = 0;
+    if ((st = check_router(ctx, router, k)) != LT_OK) return st;
+    if ((st = check_experts(ctx, gate, up, down, k, &F)) != LT_OK) return st;
+    if (router->m.rows != gate->m.n_experts || router->m.cols != gate->m.cols)
+        return fail(ctx, LT_EINVAL, "moe: router is %llux%llu for %u experts of width %llu",
+                    (unsigned long long)router->m.rows, (unsigned long long)router->m.cols, gate->m.n_experts,
+                    (unsigned long long)gate->m.cols);
+    if (act != LT_ACT_SILU && act != LT_ACT_GELU_TANH) return fail(ctx, LT_EINVAL, "moe: act %d", act);
+    if (!dev_x || !dev_out) return fail(ctx, LT_EINVAL, "moe: null pointer");
+    if (ntok == 0) return LT_OK;
+    const uint32_t E = gate->m.n_experts;
+    const uint64_t d = gate->m.cols;
+    const MoeScratch probe = moe_layout(nullptr, ntok, k, E, d, F);
+    if ((st = ensure_scratch(ctx, probe.bytes)) != LT_OK) return st;
+    const MoeScratch s = moe_layout(ctx->scratch, ntok, k, E, d, F);
+    uint32_t *ids = dev_ids ? dev_ids : s.ids;
+    float *w = dev_w ? dev_w : s.w;
+    st = route_impl(ctx, router, dev_x, dev_norm_w, eps, ntok, k, norm_topk, dev_expert_scale, ids, w, s.logits, s.xq,
+                    s.xq_pitch);
+    if (st != LT_OK) return st;
+    return ffn_impl(ctx, gate, up, down, act, ntok, ids, w, k, residual ? dev_x : nullptr, dev_out, s);
 }
 
 lt_status lt_moe_forward(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *gate, const lt_tensor *up,
@@ -624,25 +680,19 @@ lt_status lt_moe_forward(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *
                          float *dev_w) {
     lt_status st = enter(ctx);
     if (st != LT_OK) return st;
-    uint64_t F = 0;
-    if ((st = check_router(ctx, router, k)) != LT_OK) return st;
-    if ((st = check_experts(ctx, gate, up, down, k, &F)) != LT_OK) return st;
-    if (router->m.rows != gate->m.n_experts || router->m.cols != gate->m.cols)
-        return fail(ctx, LT_EINVAL, "lt_moe_forward: router is %llux%llu for %u experts of width %llu",
-                    (unsigned long long)router->m.rows, (unsigned long long)router->m.cols, gate->m.n_experts,
-                    (unsigned long long)gate->m.cols);
-    if (act != LT_ACT_SILU && act != LT_ACT_GELU_TANH) return fail(ctx, LT_EINVAL, "moe: act %d", act);
-    if (!dev_x || !dev_out) return fail(ctx, LT_EINVAL, "lt_moe_forward: null pointer");
-    if (ntok == 0) return LT_OK;
-    const uint32_t E = gate->m.n_experts;
-    const MoeScratch probe = moe_layout(nullptr, ntok, k, E, F);
-    if ((st = ensure_scratch(ctx, probe.bytes)) != LT_OK) return st;
-    const MoeScratch s = moe_layout(ctx->scratch, ntok, k, E, F);
-    uint32_t *ids = dev_ids ? dev_ids : s.ids;
-    float *w = dev_w ? dev_w : s.w;
-    if ((st = route_impl(ctx, router, dev_x, ntok, k, norm_topk, dev_expert_scale, ids, w, s.logits)) != LT_OK)
-        return st;
-    return ffn_impl(ctx, gate, up, down, act, dev_x, ntok, ids, w, k, dev_out, s);
+    return forward_impl(ctx, router, gate, up, down, act, norm_topk, dev_expert_scale, nullptr, 0.0f, 0, dev_x, ntok,
+                        k, dev_out, dev_ids, dev_w);
+}
+
+lt_status lt_moe_block(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *gate, const lt_tensor *up,
+                       const lt_tensor *down, int act, int norm_topk, const float *dev_expert_scale,
+                       const float *dev_norm_w, float eps, const float *dev_x, uint32_t ntok, uint32_t k,
+                       float *dev_out, uint32_t *dev_ids, float *dev_w) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!dev_norm_w) return fail(ctx, LT_EINVAL, "lt_moe_block: null norm weights");
+    return forward_impl(ctx, router, gate, up, down, act, norm_topk, dev_expert_scale, dev_norm_w, eps, 1, dev_x,
+                        ntok, k, dev_out, dev_ids, dev_w);
 }
 
 lt_status lt_quant_matvec_host(lt_ctx *ctx, float *out, const lt_tensor *mat, uint32_t expert, const float *vec,
@@ -654,10 +704,11 @@ lt_status lt_quant_matvec_host(lt_ctx *ctx, float *out, const lt_tensor *mat, ui
         return fail(ctx, LT_EINVAL, "lt_quant_matvec_host: %llux%llu given, tensor is %llux%llu",
                     (unsigned long long)rows, (unsigned long long)cols, (unsigned long long)mat->m.rows,
                     (unsigned long long)mat->m.cols);
-    const size_t xb = al256(cols * 4), yb = al256(rows * 4);
-    if ((st = ensure_scratch(ctx, xb + yb)) != LT_OK) return st;
+    // device vectors live past the region lt_qmatvec uses for its quantised input
+    const size_t qb = al256(lt::qact_row_pitch(cols)), xb = al256(cols * 4), yb = al256(rows * 4);
+    if ((st = ensure_scratch(ctx, qb + xb + yb)) != LT_OK) return st;
     if ((st = ensure_pinned(ctx, xb + yb)) != LT_OK) return st;
-    float *dx = (float *)ctx->scratch, *dy = (float *)(ctx->scratch + xb);
+    float *dx = (float *)(ctx->scratch + qb), *dy = (float *)(ctx->scratch + qb + xb);
     float *px = (float *)ctx->pinned, *py = (float *)(ctx->pinned + xb);
     memcpy(px, vec, cols * 4);
     LT_CUDA(ctx, cudaMemcpyAsync(dx, px, cols * 4, cudaMemcpyHostToDevice, ctx->stream), "H2D");
@@ -677,8 +728,7 @@ lt_status lt_moe_forward_host(lt_ctx *ctx, const lt_tensor *router, const lt_ten
     if (ntok == 0) return LT_OK;
     const uint64_t d = gate->m.cols;
     const uint32_t E = gate->m.n_experts;
-    uint64_t F = gate->m.rows;
-    const MoeScratch probe = moe_layout(nullptr, ntok, k, E ? E : 1, F);
+    const MoeScratch probe = moe_layout(nullptr, ntok, k, E ? E : 1, d, gate->m.rows);
     const size_t xb = al256((size_t)ntok * d * 4), ib = al256((size_t)ntok * k * 4), eb = al256((size_t)E * 4);
     const size_t io = 2 * xb + 2 * ib + eb;
     if ((st = ensure_scratch(ctx, probe.bytes + io)) != LT_OK) return st;
@@ -696,8 +746,8 @@ lt_status lt_moe_forward_host(lt_ctx *ctx, const lt_tensor *router, const lt_ten
         LT_CUDA(ctx, cudaMemcpyAsync(dscale, hb + 2 * xb + 2 * ib, (size_t)E * 4, cudaMemcpyHostToDevice, ctx->stream),
                 "H2D scale");
     }
-    // lt_moe_forward places its own scratch at the start of the arena; ours
-    // lives after probe.bytes, so the two do not overlap.
+    // lt_moe_forward places its scratch at the start of the arena (at most
+    // probe.bytes, computed with F <= gate rows); ours lives after it.
     st = lt_moe_forward(ctx, router, gate, up, down, act, norm_topk, expert_scale_host ? dscale : nullptr, dx, ntok,
                         k, dout, dids, dw);
     if (st != LT_OK) return st;

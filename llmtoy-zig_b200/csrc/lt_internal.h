@@ -72,33 +72,45 @@ uint32_t block_elems_of(uint32_t t);
 
 cudaError_t launch_dequant(const LaunchCfg &c, const DevMat &m, uint64_t row0, uint64_t nrows,
                            float *out);
-cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert, const float *x,
-                           float *y, uint32_t ntok);
 cudaError_t launch_rmsnorm(const LaunchCfg &c, const float *x, const float *w, float eps, uint32_t n,
                            uint32_t ntok, float *y);
 cudaError_t launch_softmax(const LaunchCfg &c, float *x, uint32_t n, uint32_t ntok);
 cudaError_t launch_argmax(const LaunchCfg &c, const float *x, uint32_t n, uint32_t ntok,
                           uint32_t *idx, float *scratch_val, uint32_t *scratch_idx,
                           uint32_t *counters);
-// Router over f32 weights [E][cols]; logits scratch [ntok][E]; counters
-// zero-initialised, one per token group (reset by the kernel).
-// w_ld: row stride of w in floats (the device row pitch / 4).
+
+// Bytes of one quantised activation row (lt_qact.cuh) of `cols` values.
+size_t qact_row_pitch(uint64_t cols);
+// nrows f32 rows of `cols` -> quantised activation rows at q (pitch qpitch).
+cudaError_t launch_quantize(const LaunchCfg &c, const float *x, uint32_t cols, uint32_t nrows, uint8_t *q,
+                            uint64_t qpitch);
+
+// y[tok][rows] = W[expert] . x[tok].  Quantised types read the activations
+// from xq (quantised rows); f32/f16 matrices read x directly.
+cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert, const uint8_t *xq,
+                           uint64_t xq_pitch, const float *x, float *y, uint32_t ntok);
+
+// Router over f32 weights [E][cols] (row stride w_ld floats); logits scratch
+// [ntok][E]; counters zero-initialised, one per token group (reset by the
+// kernel).  norm_w != nullptr routes rmsnorm(x) * norm_w.  xq != nullptr also
+// writes the (normalised) input as quantised rows for the expert kernels.
 cudaError_t launch_router(const LaunchCfg &c, const float *w, uint32_t E, uint32_t cols, uint32_t w_ld,
-                          const float *x, uint32_t ntok, uint32_t k, int norm_topk,
-                          const float *escale, uint32_t *ids, float *wout, float *logits,
-                          uint32_t *counters);
+                          const float *x, const float *norm_w, float eps, uint32_t ntok, uint32_t k,
+                          int norm_topk, const float *escale, uint32_t *ids, float *wout, float *logits,
+                          uint32_t *counters, uint8_t *xq, uint64_t xq_pitch);
 uint32_t router_token_groups(uint32_t ntok);
 
 cudaError_t launch_moe_plan(const LaunchCfg &c, const uint32_t *ids, uint32_t ntok, uint32_t k,
                             uint32_t E, const MoePlan &p);
-// h[pos][F] = act(gate_e . x_tok) * (up_e . x_tok).  direct: ntok == 1 and
-// ids are the plan (position = slot).  up.data == nullptr: fused gate_up.
+// hq[pos] = quantised act(gate_e . x_tok) * (up_e . x_tok).  direct: ntok == 1
+// and ids are the plan (position = slot).  up.data == nullptr: fused gate_up.
 cudaError_t launch_moe_gate_up(const LaunchCfg &c, const DevMat &gate, const DevMat &up, int act,
-                               const float *x, uint32_t ntok, uint32_t k, const uint32_t *ids,
-                               bool direct, const MoePlan &p, float *h);
-// out[t][d] = sum_s w[t][s] * (down_e(s) . h[pos(t,s)])
-cudaError_t launch_moe_down(const LaunchCfg &c, const DevMat &down, const float *h, uint32_t ntok,
-                            uint32_t k, const uint32_t *ids, const float *w, bool direct,
-                            const MoePlan &p, float *out);
+                               const uint8_t *xq, uint64_t xq_pitch, uint32_t ntok, uint32_t k,
+                               const uint32_t *ids, bool direct, const MoePlan &p, uint8_t *hq,
+                               uint64_t hq_pitch);
+// out[t][d] = (resid ? resid[t][d] : 0) + sum_s w[t][s] * (down_e(s) . h[pos(t,s)])
+cudaError_t launch_moe_down(const LaunchCfg &c, const DevMat &down, const uint8_t *hq, uint64_t hq_pitch,
+                            uint32_t ntok, uint32_t k, const uint32_t *ids, const float *w, bool direct,
+                            const MoePlan &p, const float *resid, float *out);
 
 }  // namespace lt

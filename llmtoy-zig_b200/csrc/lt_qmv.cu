@@ -1,0 +1,151 @@
+// lt_qmv.cu — dense quantised matvec: quantMatvec / quantMatvecPar
+// (src/ops/math.zig:133-171, :277-320) for ntok activation rows.
+//
+// Each warp owns `rw` consecutive weight rows (rw * items_per_row <= 32, one
+// item per lane) and streams them into its shared-memory slice with one TMA
+// bulk copy issued before the kernel waits on its producer (the weights are
+// static).  Activations come pre-quantised (lt_qact.cuh).
+#include "lt_qact.cuh"
+
+namespace lt {
+
+constexpr int kQmvWarps = 8;
+
+struct QmvArgs {
+    const uint8_t *rows;  // first row of the (expert) matrix
+    uint64_t pitch;
+    uint32_t nrows, cols, nitems, nblocks;
+    const uint8_t *xq;
+    uint64_t xq_pitch;
+    float *y;
+    uint32_t ntok;
+    uint32_t rw;  // rows per warp
+    int *dev_err;
+};
+
+__host__ __device__ inline size_t qmv_smem_bytes(uint64_t pitch, uint32_t rw, int nt, int ipr) {
+    return 64 + 64 + align16((size_t)kQmvWarps * rw * pitch + 256) + align16(xs_bytes(nt, ipr)) +
+           (size_t)kQmvWarps * nt * rw * ipr * 4;
+}
+
+template <uint32_t TYPE, int NT>
+__global__ void __launch_bounds__(kQmvWarps * 32) k_qmv(QmvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ipr = (int)a.nitems;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
+    const uint8_t **src = reinterpret_cast<const uint8_t **>(smem + 64);
+    uint8_t *tile = smem + 128;
+    uint8_t *p = tile + align16((size_t)kQmvWarps * a.rw * a.pitch + 256);
+    const XS X = xs_carve(p, NT, ipr);
+    p += align16(xs_bytes(NT, ipr));
+    float *part = reinterpret_cast<float *>(p);
+
+    const uint32_t wr0 = (blockIdx.x * kQmvWarps + warp) * a.rw;
+    const int nr = wr0 < a.nrows ? (int)min(a.rw, a.nrows - wr0) : 0;
+    uint8_t *wt = tile + (size_t)warp * a.rw * a.pitch;
+    if (lane == 0 && nr > 0) {  // weights are static: fetch before waiting on the producer
+        mbar_init(&bars[warp], 1);
+        fence_barrier_init();
+        const uint32_t bytes = (uint32_t)(nr * a.pitch);
+        mbar_arrive_expect_tx(&bars[warp], bytes);
+        tma_load_1d(wt, a.rows + (uint64_t)wr0 * a.pitch, bytes, &bars[warp]);
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+    bool ok = true;
+    const int nitem = nr * ipr;
+    float *wpart = part + (size_t)warp * NT * a.rw * ipr;
+    for (uint32_t c0 = 0; c0 < a.ntok; c0 += NT) {
+        const int nt = (int)min((uint32_t)NT, a.ntok - c0);
+        if (threadIdx.x < (unsigned)nt) src[threadIdx.x] = a.xq + (size_t)(c0 + threadIdx.x) * a.xq_pitch;
+        __syncthreads();
+        qact_to_smem(X, src, nt, (int)a.cols);
+        __syncthreads();
+        if (c0 == 0 && nr > 0) ok = tile_wait(&bars[warp], a.dev_err);
+        if (ok && nr > 0) {
+            for (int f = lane; f < nitem; f += 32) {
+                const int item = f % ipr, row = f / ipr;
+                float res[NT];
+#pragma unroll
+                for (int t = 0; t < NT; t++) res[t] = 0.0f;
+                dot_item<TYPE, NT>(wt + (size_t)row * a.pitch, item, (int)a.nblocks, X, 0, nt, res);
+#pragma unroll
+                for (int t = 0; t < NT; t++)
+                    if (t < nt) wpart[t * nitem + f] = res[t];
+            }
+            __syncwarp();
+            for (int l = lane; l < nt * nr; l += 32) {
+                const int t = l / nr, r = l - t * nr;
+                const float *pp = wpart + t * nitem + r * ipr;
+                float s = 0.0f;
+                for (int i = 0; i < ipr; i++) s += pp[i];
+                a.y[(size_t)(c0 + t) * a.nrows + wr0 + r] = s;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// f32 / f16 rows: one warp per row, plain loads.
+__global__ void k_mv_float(const uint8_t *rows, uint64_t pitch, uint32_t type, uint32_t nrows, uint32_t cols,
+                           const float *x, float *y, uint32_t ntok) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const uint32_t warps = (blockDim.x >> 5) * gridDim.x;
+    for (uint32_t r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < nrows; r += warps) {
+        const uint8_t *row = rows + (uint64_t)r * pitch;
+        for (uint32_t t = 0; t < ntok; t++) {
+            const float *xt = x + (size_t)t * cols;
+            float s = 0.0f;
+            for (uint32_t i = threadIdx.x & 31; i < cols; i += 32) {
+                const float w = type == T_F32 ? reinterpret_cast<const float *>(row)[i]
+                                              : __half2float(__ushort_as_half(reinterpret_cast<const unsigned short *>(row)[i]));
+                s += w * xt[i];
+            }
+            s = warp_sum(s);
+            if ((threadIdx.x & 31) == 0) y[(size_t)t * nrows + r] = s;
+        }
+    }
+}
+
+template <uint32_t TYPE, int NT>
+static cudaError_t launch_qmv_t(const LaunchCfg &c, const QmvArgs &a) {
+    const size_t smem = qmv_smem_bytes(a.pitch, a.rw, NT, (int)a.nitems);
+    const uint32_t rows_per_cta = kQmvWarps * a.rw;
+    const dim3 grid((a.nrows + rows_per_cta - 1) / rows_per_cta);
+    return launch_k(c, type_label<TYPE>("qmv"), k_qmv<TYPE, NT>, grid, dim3(kQmvWarps * 32), smem, a);
+}
+
+cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert, const uint8_t *xq,
+                           uint64_t xq_pitch, const float *x, float *y, uint32_t ntok) {
+    const uint8_t *rows = m.data + (uint64_t)expert * m.rows * m.pitch;
+    if (m.type == T_F32 || m.type == T_F16) {
+        const uint64_t want = (m.rows + 7) / 8;
+        const uint32_t blocks = (uint32_t)(want < 65535 ? want : 65535);
+        return launch_k(c, "qmv_float", k_mv_float, dim3(blocks), dim3(256), 0, rows, m.pitch, m.type,
+                        (uint32_t)m.rows, (uint32_t)m.cols, x, y, ntok);
+    }
+    QmvArgs a;
+    a.rows = rows;
+    a.pitch = m.pitch;
+    a.nrows = (uint32_t)m.rows;
+    a.cols = (uint32_t)m.cols;
+    a.nitems = items_per_row(m.type, m.cols);
+    a.nblocks = (uint32_t)(m.cols / 32);
+    a.xq = xq;
+    a.xq_pitch = xq_pitch;
+    a.y = y;
+    a.ntok = ntok;
+    a.rw = max(1u, 32u / a.nitems);
+    a.dev_err = c.dev_err;
+    const bool one = ntok == 1;
+    switch (m.type) {
+    case T_Q4_K: return one ? launch_qmv_t<T_Q4_K, 1>(c, a) : launch_qmv_t<T_Q4_K, 4>(c, a);
+    case T_Q6_K: return one ? launch_qmv_t<T_Q6_K, 1>(c, a) : launch_qmv_t<T_Q6_K, 2>(c, a);
+    case T_Q8_0: return one ? launch_qmv_t<T_Q8_0, 1>(c, a) : launch_qmv_t<T_Q8_0, 4>(c, a);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace lt

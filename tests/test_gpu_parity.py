@@ -292,6 +292,29 @@ def test_moe_variants_vs_oracle(ctx, oracle, pool, gate_type, down_type, d, F, E
     _check_moe(ctx, oracle, pool, L, x, k, norm, act, escale)
 
 
+@pytest.mark.parametrize("T", [1, 7])
+def test_moe_block_vs_oracle(ctx, oracle, pool, config1_layer, T):
+    """lt_moe_block: x + moe(rmsnorm(x) * w), norm and residual fused; run in place."""
+    L = config1_layer
+    rng = np.random.Generator(np.random.PCG64(70 + T))
+    x = rng.normal(0, 3, size=(T, 2048)).astype(np.float32)
+    nw = rng.uniform(0.5, 1.5, 2048).astype(np.float32)
+    rt, g, u, dn = _upload_layer(ctx, L)
+    xd = dev(x)
+    ids, ww = empty(T * 8, "int32"), empty(T * 8)
+    ctx.moe_block(rt, g, u, dn, 0, True, None, dev(nw), 1e-6, xd, T, 8, xd, ids, ww)
+    got = host(xd).reshape(T, 2048)
+    xn = np.empty_like(x)
+    for t in range(T):
+        oracle.lib().orc_rmsnorm(xn[t].ctypes.data, x[t].ctypes.data, nw.ctypes.data, 2048, 1e-6)
+    y, rids, rw = oracle.moe_layer(L, xn, 8, True, 0, None, pool)
+    assert np.array_equal(host(ids).view(np.uint32).reshape(T, 8), rids)
+    assert rel_l2(got - x, y) < MOE_L2_TOL
+    np.testing.assert_allclose(got, x + y, rtol=1e-4, atol=1e-3 * float(np.abs(y).max()))
+    for t_ in (rt, g, u, dn):
+        t_.free()
+
+
 def test_moe_ffn_skewed_routing(ctx, oracle, config1_layer):
     """Dispatch with every token on the same few experts (and one expert hit by
     all tokens): the grouped plan must still combine in slot order."""
