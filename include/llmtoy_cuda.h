@@ -200,6 +200,35 @@ lt_status lt_capture_end(lt_ctx *ctx, lt_graph **out);
 lt_status lt_graph_launch(lt_ctx *ctx, const lt_graph *graph);
 lt_status lt_graph_free(lt_ctx *ctx, lt_graph *graph);
 
+/* ── allocation-free MoE FFN ─────────────────────────────────────────────────
+ * No counterpart in the reference (its CPU path allocates per call and its
+ * Vulkan path owns its buffers).  For callers that cannot allocate device
+ * memory themselves -- an embedding runtime or pool hands them every buffer,
+ * or another owner drives the allocator -- this runs the same dispatch +
+ * grouped gate/up + down + weighted combine as lt_moe_ffn without a context
+ * and without allocating: weights, x, ids, w and out are the caller's device
+ * pointers, and the intermediate activations live in a fixed 8 MiB device
+ * array inside the library (held by every GPU that loads it until exit).
+ *   - Weights are GGUF rows used in place: gate [E][F or 2F][d] (fused
+ *     gate_up when up == NULL), up [E][F][d], down [E][d][F]; every row's
+ *     byte size and every weight pointer must be a multiple of 16 (true for
+ *     Q4_K/Q6_K/Q8_0 rows of 2048 or 768 columns).
+ *   - Capacity: 256 + ntok*qact(d) + ntok*k*qact(F) + (3*E + 2*ntok*k + 1)*4
+ *     bytes, each term rounded up to 256, with qact(n) = 4.375*n rounded up
+ *     to 16; larger requests return LT_EINVAL.  (ntok=16, k=8, d=2048, F=768
+ *     uses 0.6 MiB.)
+ *   - Asynchronous on cuda_stream (NULL = legacy default stream).  The first
+ *     call on each device looks up the array's device address; make that
+ *     first call before any stream capture.
+ *   - Calls share the array: calls that overlap on the GPU race.
+ * Returns LT_EINVAL / LT_EUNSUPPORTED_TYPE for bad arguments, LT_ECUDA if a
+ * launch fails. */
+lt_status lt_moe_ffn_noalloc(void *cuda_stream, const void *gate, const void *up,
+                             const void *down, uint32_t gate_type, uint32_t down_type,
+                             uint32_t n_experts, uint64_t d_model, uint64_t d_expert, int act,
+                             const float *dev_x, uint32_t ntok, const uint32_t *dev_ids,
+                             const float *dev_w, uint32_t k, float *dev_out);
+
 /* ── host-buffer entry points (synchronous) ─────────────────────────────────
  * Same semantics with HOST vectors, copies included: the shape of the
  * reference's own CPU calls, for callers that keep activations on the host. */

@@ -32,7 +32,7 @@ EXPORTS = [
     "lt_tensor_download", "lt_tensor_describe", "lt_tensor_free", "lt_dequant", "lt_qmatvec",
     "lt_rmsnorm", "lt_softmax", "lt_moe_route", "lt_moe_ffn", "lt_moe_forward", "lt_moe_block", "lt_argmax",
     "lt_profile_enable", "lt_profile_read", "lt_profile_reset", "lt_capture_begin", "lt_capture_end",
-    "lt_graph_launch", "lt_graph_free", "lt_quant_matvec_host", "lt_moe_forward_host",
+    "lt_graph_launch", "lt_graph_free", "lt_moe_ffn_noalloc", "lt_quant_matvec_host", "lt_moe_forward_host",
 ]
 
 
@@ -93,6 +93,7 @@ def load_library() -> ctypes.CDLL:
         "lt_capture_end": (I, [P, ctypes.POINTER(P)]),
         "lt_graph_launch": (I, [P, P]),
         "lt_graph_free": (I, [P, P]),
+        "lt_moe_ffn_noalloc": (I, [P, P, P, P, U32, U32, U32, U64, U64, I, P, U32, P, P, U32, P]),
         "lt_quant_matvec_host": (I, [P, P, P, U32, P, U64, U64]),
         "lt_moe_forward_host": (I, [P, P, P, P, P, I, I, P, P, U32, U32, P, P, P]),
     }
