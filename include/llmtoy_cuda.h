@@ -213,10 +213,10 @@ lt_status lt_graph_free(lt_ctx *ctx, lt_graph *graph);
  *     gate_up when up == NULL), up [E][F][d], down [E][d][F]; every row's
  *     byte size and every weight pointer must be a multiple of 16 (true for
  *     Q4_K/Q6_K/Q8_0 rows of 2048 or 768 columns).
- *   - Capacity: 256 + ntok*qact(d) + ntok*k*qact(F) + (3*E + 2*ntok*k + 1)*4
- *     bytes, each term rounded up to 256, with qact(n) = 4.375*n rounded up
- *     to 16; larger requests return LT_EINVAL.  (ntok=16, k=8, d=2048, F=768
- *     uses 0.6 MiB.)
+ *   - Capacity: 256 + ntok*qact(d) + ntok*k*(qact(F) + 4*F + F/8)
+ *     + (3*E + 2*ntok*k + 1)*4 bytes, each term rounded up to 256, with
+ *     qact(n) = 3.375*n rounded up to 16; larger requests return LT_EINVAL.
+ *     (ntok=16, k=8, d=2048, F=768 uses 0.9 MiB.)
  *   - Asynchronous on cuda_stream (NULL = legacy default stream).  The first
  *     call on each device looks up the array's device address; make that
  *     first call before any stream capture.

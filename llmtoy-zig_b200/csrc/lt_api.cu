@@ -163,8 +163,10 @@ struct MoeScratch {
     uint64_t xq_pitch;
     uint8_t *hq;
     uint64_t hq_pitch;
+    float *hf;  // f32 h rows, staged before quantisation
     lt::MoePlan plan;
     size_t bytes;
+    size_t counters;  // block counters needed past kMoeCounterBase
 };
 
 MoeScratch moe_layout(uint8_t *base, uint32_t T, uint32_t k, uint32_t E, uint64_t d, uint64_t F) {
@@ -182,6 +184,8 @@ MoeScratch moe_layout(uint8_t *base, uint32_t T, uint32_t k, uint32_t E, uint64_
     s.w = (float *)take(P * 4);
     s.xq = take((size_t)T * s.xq_pitch);
     s.hq = take(P * s.hq_pitch);
+    s.hf = (float *)take(P * F * 4);
+    s.counters = P * (F / 32);
     s.logits = (float *)take((size_t)T * E * 4);
     s.plan.n_active = (uint32_t *)take(4);
     s.plan.act_e = (uint32_t *)take((size_t)E * 4);
@@ -383,7 +387,7 @@ lt_status lt_reserve(lt_ctx *ctx, uint32_t max_tokens, uint32_t max_k, uint64_t 
                                                                                                 : max_d_expert));
     st = ensure_scratch(ctx, (moe + io > qmv ? moe + io : qmv));
     if (st != LT_OK) return st;
-    return ensure_counters(ctx, 4096 + lt::router_token_groups(max_tokens) + max_tokens);
+    return ensure_counters(ctx, lt::kMoeCounterBase + (size_t)max_tokens * max_k * (max_d_expert / 32) + max_tokens);
 }
 
 uint64_t lt_row_bytes(uint32_t ggml_type, uint64_t cols) {
@@ -612,14 +616,15 @@ static lt_status ffn_impl(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *u
     const bool direct = ntok == 1;
     lt::DevMat upm = up ? up->m : lt::DevMat{};
     if (!up) upm.data = nullptr;
-    lt_status st;
+    lt_status st = ensure_counters(ctx, lt::kMoeCounterBase + s.counters);
+    if (st != LT_OK) return st;
     if (!direct) {
         st = launched(ctx, lt::launch_moe_plan(c, ids, ntok, k, gate->m.n_experts, s.plan), "moe plan");
         if (st != LT_OK) return st;
     }
     st = launched(ctx,
-                  lt::launch_moe_gate_up(c, gate->m, upm, act, s.xq, s.xq_pitch, ntok, k, ids, direct, s.plan, s.hq,
-                                         s.hq_pitch),
+                  lt::launch_moe_gate_up(c, gate->m, upm, act, s.xq, s.xq_pitch, ntok, k, ids, direct, s.plan, s.hf,
+                                         ctx->counters + lt::kMoeCounterBase, s.hq, s.hq_pitch),
                   "moe gate_up");
     if (st != LT_OK) return st;
     return launched(ctx,

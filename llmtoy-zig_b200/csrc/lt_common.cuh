@@ -170,6 +170,18 @@ LT_DEVINL int dp2a_hi_ss(int a, uint32_t b, int c) {
     return d;
 }
 
+// d = c + sum_i a.s8[i] * b.byte[i]  (b bytes unsigned / signed)
+LT_DEVINL int dp4a_su(int a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+LT_DEVINL int dp4a_ss(int a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
 // Small non-negative integer held in byte `sel` of w, as an exact float.
 LT_DEVINL float byte_to_f32(uint32_t w, int sel) {
     return byte_biased(w, sel) - kMagic;

@@ -1,27 +1,29 @@
-// lt_decode.cuh — activations quantised in shared memory and the GGUF block
-// decoders that take dot products against them.
+// lt_decode.cuh — GGUF block decoders that take dot products against
+// quantised activations held in shared memory.
 //
-// Activations.  Each 32-element block of an activation row is stored as two
-// int16 terms, x ~= s * (hi + lo / 65534) with s = amax / 32767: hi is
-// round(x / s) and lo rounds the remainder at 1/65534 of a step.  That keeps
-// about 31 bits of the block's dynamic range, so products with the quant
-// values (4-8 bit integers) accumulate exactly in int32 via dp2a and the only
-// rounding left is the f32 block-scale arithmetic.  (One int16 term alone
-// loses too much when expert outputs cancel in the weighted combine.)
+// Activations.  Each 32-element block of an activation row is stored as
+// x ~= s * (hi + lo / 254) with s = amax / 32767: hi = round(x / s) as int16
+// and lo = round of the remainder in 1/254 steps as int8 -- about 2^-24 of the
+// block's range, f32-like.  Products with the quant values (4-8 bit integers)
+// accumulate exactly in int32: hi via dp2a (2 elements per instruction), lo
+// via dp4a (4 per instruction).  The only rounding left is the f32 scale
+// arithmetic.  (A single int16 term loses too much when expert outputs
+// cancel in the weighted combine: measured 3e-4 relative error.)
 //
-// Layout per token t and item i (256 columns): hi values at xq + t*tok_bytes +
-// i*528, lo values at the same offset from xl; 8 int16 of padding per item put
-// threads that decode different items in different banks.  Per 32-block:
-// scale xs; per 16-group: f32 sum of the original values xsum16 (used for the
-// Q4_K minimum and the Q6_K -32 offset terms, which are applied in f32).
+// Shared-memory layout per token t and item i (256 columns): hi at
+// xq + t*tok_hi + i*528, lo at xl + t*tok_lo + i*272; the 16 padding bytes
+// per item put threads that decode different items in different banks.  Per
+// 32-block: scale xs; per 16-group: f32 sum of the original values xsum16
+// (used for the Q4_K minimum and the Q6_K -32 offset terms, applied in f32).
 #pragma once
 
 #include "lt_common.cuh"
 
 namespace lt {
 
-constexpr int kXItemPitch = 528;           // 256 int16 + 16 bytes of padding
-constexpr float kLoScale = 1.0f / 65534.0f;
+constexpr int kXHiPitch = 528;  // 256 int16 + 16 bytes of padding
+constexpr int kXLoPitch = 272;  // 256 int8 + 16 bytes of padding
+constexpr float kLoScale = 1.0f / 254.0f;
 
 struct XS {
     uint8_t *xq;    // hi terms
@@ -29,89 +31,78 @@ struct XS {
     float *xs;      // [t][item*8 + block] scale
     float *xsum16;  // [t][item*16 + group] sum of x over 16 elements
     int nitems;
-    int tok_bytes;  // nitems * 528
-    int tok_blk;    // nitems * 8
+    int tok_hi;   // nitems * 528
+    int tok_lo;   // nitems * 272
+    int tok_blk;  // nitems * 8
 };
 
 __host__ __device__ inline size_t xs_bytes(int ntok, int nitems) {
-    return (size_t)ntok * nitems * (2 * kXItemPitch + 8 * 4 + 16 * 4);
+    return (size_t)ntok * nitems * (kXHiPitch + kXLoPitch + 8 * 4 + 16 * 4);
 }
 
 LT_DEVINL XS xs_carve(uint8_t *p, int ntok, int nitems) {
     XS x;
     x.nitems = nitems;
-    x.tok_bytes = nitems * kXItemPitch;
+    x.tok_hi = nitems * kXHiPitch;
+    x.tok_lo = nitems * kXLoPitch;
     x.tok_blk = nitems * 8;
     x.xq = p;
-    p += (size_t)ntok * x.tok_bytes;
+    p += (size_t)ntok * x.tok_hi;
     x.xl = p;
-    p += (size_t)ntok * x.tok_bytes;
+    p += (size_t)ntok * x.tok_lo;
     x.xs = reinterpret_cast<float *>(p);
     p += (size_t)ntok * nitems * 8 * 4;
     x.xsum16 = reinterpret_cast<float *>(p);
     return x;
 }
 
-// Quantise nt activation rows (row pointers in shared memory) of `cols`
-// floats.  Warps own 32-blocks; each warp issues up to 16 block loads before
-// it reduces any of them, so the prologue costs one memory latency, not one
-// per block.
-LT_DEVINL void prep_x(const XS &X, const float *const *src, int nt, int cols) {
-    constexpr int kBatch = 16;
-    const int nblk = cols >> 5;
-    const int total = nt * nblk;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int base = warp; base < total; base += nw * kBatch) {
-        float v[kBatch];
-#pragma unroll
-        for (int j = 0; j < kBatch; j++) {
-            const int task = base + j * nw;
-            v[j] = 0.0f;
-            if (task < total) {
-                const int t = task / nblk, b = task - t * nblk;
-                v[j] = src[t][32 * b + lane];
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < kBatch; j++) {
-            const int task = base + j * nw;
-            if (task >= total) break;
-            const int t = task / nblk, b = task - t * nblk;
-            float amax = fabsf(v[j]);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            int qh = 0, ql = 0;
-            float s = 0.0f;
-            if (amax > 0.0f) {
-                const float inv = 32767.0f / amax;
-                s = amax / 32767.0f;
-                qh = max(-32767, min(32767, __float2int_rn(v[j] * inv)));
-                const float r = fmaf(-(float)qh, s, v[j]);  // remainder, |r| <~ s/2
-                ql = max(-32767, min(32767, __float2int_rn(r * inv * 65534.0f)));
-            }
-            const int e = 32 * b + lane;
-            const size_t off = (size_t)t * X.tok_bytes + (e >> 8) * kXItemPitch;
-            reinterpret_cast<int16_t *>(X.xq + off)[e & 255] = (int16_t)qh;
-            reinterpret_cast<int16_t *>(X.xl + off)[e & 255] = (int16_t)ql;
-            float sum = v[j];
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            if (lane == 0) X.xs[t * X.tok_blk + b] = s;
-            if ((lane & 15) == 0) X.xsum16[t * X.tok_blk * 2 + 2 * b + (lane >> 4)] = sum;
-        }
-    }
-}
-
-// Load 32 consecutive activation values (hi and lo terms) as int16 pairs.
-LT_DEVINL void load_x32(const XS &X, int t, int item, int elem0, uint32_t (&hi)[16], uint32_t (&lo)[16]) {
-    const size_t off = (size_t)t * X.tok_bytes + item * kXItemPitch + 2 * elem0;
+// 32 consecutive activation values: hi terms as 16 int16 pairs, lo terms as
+// 8 words of 4 int8.
+LT_DEVINL void load_x32(const XS &X, int t, int item, int elem0, uint32_t (&hi)[16], uint32_t (&lo)[8]) {
+    const uint8_t *ph = X.xq + (size_t)t * X.tok_hi + item * kXHiPitch + 2 * elem0;
+    const uint8_t *pl = X.xl + (size_t)t * X.tok_lo + item * kXLoPitch + elem0;
 #pragma unroll
     for (int v = 0; v < 4; v++) {
-        const uint4 h4 = lds128(X.xq + off + 16 * v), l4 = lds128(X.xl + off + 16 * v);
+        const uint4 h4 = lds128(ph + 16 * v);
         hi[4 * v] = h4.x; hi[4 * v + 1] = h4.y; hi[4 * v + 2] = h4.z; hi[4 * v + 3] = h4.w;
+    }
+#pragma unroll
+    for (int v = 0; v < 2; v++) {
+        const uint4 l4 = lds128(pl + 16 * v);
         lo[4 * v] = l4.x; lo[4 * v + 1] = l4.y; lo[4 * v + 2] = l4.z; lo[4 * v + 3] = l4.w;
     }
 }
+
+// sum over 32 elements of q * x_hi and q * x_lo for quant bytes q[8]
+// (4 per word, unsigned), with two accumulators per term for ILP.
+LT_DEVINL void dot32_u(const uint32_t (&q)[8], const uint32_t (&xh)[16], const uint32_t (&xl)[8], int &hi, int &lo) {
+    int h0 = 0, h1 = 0, l0 = 0, l1 = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) {
+        h0 = dp2a_hi_su((int)xh[2 * k + 1], q[k], dp2a_lo_su((int)xh[2 * k], q[k], h0));
+        h1 = dp2a_hi_su((int)xh[2 * k + 3], q[k + 1], dp2a_lo_su((int)xh[2 * k + 2], q[k + 1], h1));
+        l0 = dp4a_su((int)xl[k], q[k], l0);
+        l1 = dp4a_su((int)xl[k + 1], q[k + 1], l1);
+    }
+    hi = h0 + h1;
+    lo = l0 + l1;
+}
+
+// Same with signed quant bytes (Q8_0).
+LT_DEVINL void dot32_s(const uint32_t (&q)[8], const uint32_t (&xh)[16], const uint32_t (&xl)[8], int &hi, int &lo) {
+    int h0 = 0, h1 = 0, l0 = 0, l1 = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) {
+        h0 = dp2a_hi_ss((int)xh[2 * k + 1], q[k], dp2a_lo_ss((int)xh[2 * k], q[k], h0));
+        h1 = dp2a_hi_ss((int)xh[2 * k + 3], q[k + 1], dp2a_lo_ss((int)xh[2 * k + 2], q[k + 1], h1));
+        l0 = dp4a_ss((int)xl[k], q[k], l0);
+        l1 = dp4a_ss((int)xl[k + 1], q[k + 1], l1);
+    }
+    hi = h0 + h1;
+    lo = l0 + l1;
+}
+
+LT_DEVINL float qx(int hi, int lo) { return (float)hi + (float)lo * kLoScale; }
 
 // ── Q4_K superblock: [f16 d][f16 dmin][12 B 6-bit scales/mins][128 B nibbles] ──
 template <int NT>
@@ -140,22 +131,16 @@ LT_DEVINL void dot_q4k(const uint8_t *sbp, int item, const XS &X, int t0, int nt
         for (int tt = 0; tt < NT; tt++) {
             if (tt < nt) {
                 const int t = t0 + tt;
-                uint32_t ah[16], al[16], bh[16], bl[16];
+                uint32_t ah[16], al[8], bh[16], bl[8];
                 load_x32(X, t, item, 64 * c, ah, al);
                 load_x32(X, t, item, 64 * c + 32, bh, bl);
-                int aH = 0, aL = 0, bH = 0, bL = 0;
-#pragma unroll
-                for (int k = 0; k < 8; k++) {
-                    aH = dp2a_hi_su((int)ah[2 * k + 1], lo[k], dp2a_lo_su((int)ah[2 * k], lo[k], aH));
-                    aL = dp2a_hi_su((int)al[2 * k + 1], lo[k], dp2a_lo_su((int)al[2 * k], lo[k], aL));
-                    bH = dp2a_hi_su((int)bh[2 * k + 1], hi[k], dp2a_lo_su((int)bh[2 * k], hi[k], bH));
-                    bL = dp2a_hi_su((int)bl[2 * k + 1], hi[k], dp2a_lo_su((int)bl[2 * k], hi[k], bL));
-                }
+                int aH, aL, bH, bL;
+                dot32_u(lo, ah, al, aH, aL);
+                dot32_u(hi, bh, bl, bH, bL);
                 const float *xs = X.xs + t * X.tok_blk + item * 8;
                 const float *x16 = X.xsum16 + t * X.tok_blk * 2 + item * 16;
-                const float qa_ = (float)aH + (float)aL * kLoScale, qb_ = (float)bH + (float)bL * kLoScale;
-                res[tt] += dA * xs[2 * c] * qa_ - mA * (x16[4 * c] + x16[4 * c + 1]);
-                res[tt] += dB * xs[2 * c + 1] * qb_ - mB * (x16[4 * c + 2] + x16[4 * c + 3]);
+                res[tt] += dA * xs[2 * c] * qx(aH, aL) - mA * (x16[4 * c] + x16[4 * c + 1]);
+                res[tt] += dB * xs[2 * c + 1] * qx(bH, bL) - mB * (x16[4 * c + 2] + x16[4 * c + 3]);
             }
         }
     }
@@ -188,15 +173,11 @@ LT_DEVINL void dot_q8_block(const uint32_t *w, int item, const XS &X, int t0, in
     for (int tt = 0; tt < NT; tt++) {
         if (tt < nt) {
             const int t = t0 + tt;
-            uint32_t xh[16], xl[16];
+            uint32_t xh[16], xl[8];
             load_x32(X, t, item, 32 * B, xh, xl);
-            int aH = 0, aL = 0;
-#pragma unroll
-            for (int k = 0; k < 8; k++) {
-                aH = dp2a_hi_ss((int)xh[2 * k + 1], q[k], dp2a_lo_ss((int)xh[2 * k], q[k], aH));
-                aL = dp2a_hi_ss((int)xl[2 * k + 1], q[k], dp2a_lo_ss((int)xl[2 * k], q[k], aL));
-            }
-            res[tt] += d * X.xs[t * X.tok_blk + item * 8 + B] * ((float)aH + (float)aL * kLoScale);
+            int h, l;
+            dot32_s(q, xh, xl, h, l);
+            res[tt] += d * X.xs[t * X.tok_blk + item * 8 + B] * qx(h, l);
         }
     }
 }
@@ -263,22 +244,24 @@ LT_DEVINL void dot_q6k(const uint8_t *sbp, int item, const XS &X, int t0, int nt
             for (int tt = 0; tt < NT; tt++) {
                 if (tt < nt) {
                     const int t = t0 + tt;
-                    uint32_t xh[16], xl[16];
+                    uint32_t xh[16], xl[8];
                     load_x32(X, t, item, 128 * n + 32 * kind, xh, xl);
+                    // the two 16-element halves carry different scales
                     int h0 = 0, l0 = 0, h1 = 0, l1 = 0;
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
                         h0 = dp2a_hi_su((int)xh[2 * k + 1], qv[kind][k], dp2a_lo_su((int)xh[2 * k], qv[kind][k], h0));
-                        l0 = dp2a_hi_su((int)xl[2 * k + 1], qv[kind][k], dp2a_lo_su((int)xl[2 * k], qv[kind][k], l0));
-                        h1 = dp2a_hi_su((int)xh[9 + 2 * k], qv[kind][4 + k], dp2a_lo_su((int)xh[8 + 2 * k], qv[kind][4 + k], h1));
-                        l1 = dp2a_hi_su((int)xl[9 + 2 * k], qv[kind][4 + k], dp2a_lo_su((int)xl[8 + 2 * k], qv[kind][4 + k], l1));
+                        l0 = dp4a_su((int)xl[k], qv[kind][k], l0);
+                        h1 = dp2a_hi_su((int)xh[9 + 2 * k], qv[kind][4 + k],
+                                        dp2a_lo_su((int)xh[8 + 2 * k], qv[kind][4 + k], h1));
+                        l1 = dp4a_su((int)xl[4 + k], qv[kind][4 + k], l1);
                     }
                     const int g = 8 * n + 2 * kind;  // 16-group index inside the item
                     const float *x16 = X.xsum16 + t * X.tok_blk * 2 + item * 16;
                     const float xsc = X.xs[t * X.tok_blk + item * 8 + 4 * n + kind];
                     // sum (q - 32) x = s * sum q*xq - 32 * sum x
-                    res[tt] += ds0 * (xsc * ((float)h0 + (float)l0 * kLoScale) - 32.0f * x16[g]);
-                    res[tt] += ds1 * (xsc * ((float)h1 + (float)l1 * kLoScale) - 32.0f * x16[g + 1]);
+                    res[tt] += ds0 * (xsc * qx(h0, l0) - 32.0f * x16[g]);
+                    res[tt] += ds1 * (xsc * qx(h1, l1) - 32.0f * x16[g + 1]);
                 }
             }
         }

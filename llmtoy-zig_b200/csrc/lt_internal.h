@@ -104,10 +104,13 @@ cudaError_t launch_moe_plan(const LaunchCfg &c, const uint32_t *ids, uint32_t nt
                             uint32_t E, const MoePlan &p);
 // hq[pos] = quantised act(gate_e . x_tok) * (up_e . x_tok).  direct: ntok == 1
 // and ids are the plan (position = slot).  up.data == nullptr: fused gate_up.
+// hf: f32 h rows [ntok*k][F]; hcnt: [ntok*k][F/32] counters that must be zero
+// on entry (the kernel leaves them zero).
 cudaError_t launch_moe_gate_up(const LaunchCfg &c, const DevMat &gate, const DevMat &up, int act,
                                const uint8_t *xq, uint64_t xq_pitch, uint32_t ntok, uint32_t k,
-                               const uint32_t *ids, bool direct, const MoePlan &p, uint8_t *hq,
-                               uint64_t hq_pitch);
+                               const uint32_t *ids, bool direct, const MoePlan &p, float *hf,
+                               uint32_t *hcnt, uint8_t *hq, uint64_t hq_pitch);
+constexpr size_t kMoeCounterBase = 4096;  // MoE block counters start here in the context's counter array
 // out[t][d] = (resid ? resid[t][d] : 0) + sum_s w[t][s] * (down_e(s) . h[pos(t,s)])
 cudaError_t launch_moe_down(const LaunchCfg &c, const DevMat &down, const uint8_t *hq, uint64_t hq_pitch,
                             uint32_t ntok, uint32_t k, const uint32_t *ids, const float *w, bool direct,

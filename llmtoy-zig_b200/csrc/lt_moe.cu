@@ -77,10 +77,15 @@ cudaError_t launch_moe_plan(const LaunchCfg &c, const uint32_t *ids, uint32_t nt
 }
 
 // ── grouped gate/up with the activation fused ────────────────────────────────
+// A CTA covers 8 rows of one expert (each of its 4 warps: 2 gate rows and the
+// same 2 up rows, one superblock per lane at 2048 columns).  The 8 finished h
+// values go to an f32 buffer; the last of the 4 CTAs that share a 32-element
+// block (device-scope counter, reset by that CTA) quantises the block.
 
-constexpr int kGuWarps = 8;
-constexpr int kGuRowsPerWarp = 4;
-constexpr int kGuRows = kGuWarps * kGuRowsPerWarp;  // 32: one h block per CTA
+constexpr int kGuWarps = 4;
+constexpr int kGuRowsPerWarp = 2;
+constexpr int kGuRows = kGuWarps * kGuRowsPerWarp;  // 8
+constexpr int kGuCtasPerBlock = 32 / kGuRows;       // 4
 
 struct GateUpArgs {
     const uint8_t *gate, *up;  // up == nullptr: fused gate_up tensor
@@ -93,14 +98,16 @@ struct GateUpArgs {
     const uint32_t *ids;
     int direct;
     MoePlan p;
-    uint8_t *hq;  // qact rows of h, one per (token, slot) position
+    float *hf;        // f32 h rows [pos][F]
+    uint32_t *hcnt;   // [pos][F/32] zero-initialised block counters
+    uint8_t *hq;      // qact rows of h, one per (token, slot) position
     uint64_t hq_pitch;
     int *dev_err;
 };
 
 __host__ __device__ inline size_t gu_smem_bytes(uint64_t pitch, int nt, int ipr) {
-    return 64 + 128 + align16((size_t)kGuWarps * 2 * kGuRowsPerWarp * pitch + 256) + align16(xs_bytes(nt, ipr)) +
-           align16((size_t)kGuWarps * nt * 2 * kGuRowsPerWarp * ipr * 4) + (size_t)nt * kGuRows * 4;
+    return 64 + 64 + align16((size_t)kGuWarps * 2 * kGuRowsPerWarp * pitch + 256) + align16(xs_bytes(nt, ipr)) +
+           align16((size_t)kGuWarps * nt * 2 * kGuRowsPerWarp * ipr * 4) + align16((size_t)nt * kGuRows * 4) + 64;
 }
 
 template <uint32_t TYPE, int NT>
@@ -110,7 +117,7 @@ __global__ void __launch_bounds__(kGuWarps * 32) k_moe_gate_up(GateUpArgs a) {
     const int ipr = (int)a.nitems;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
     const uint8_t **src = reinterpret_cast<const uint8_t **>(smem + 64);
-    uint8_t *tile = smem + 64 + 128;
+    uint8_t *tile = smem + 128;
     const size_t wtile = (size_t)2 * kGuRowsPerWarp * a.pitch;
     uint8_t *p = tile + align16((size_t)kGuWarps * wtile + 256);
     const XS X = xs_carve(p, NT, ipr);
@@ -118,6 +125,8 @@ __global__ void __launch_bounds__(kGuWarps * 32) k_moe_gate_up(GateUpArgs a) {
     float *part = reinterpret_cast<float *>(p);
     p += align16((size_t)kGuWarps * NT * 2 * kGuRowsPerWarp * ipr * 4);
     float *hbuf = reinterpret_cast<float *>(p);
+    p += align16((size_t)NT * kGuRows * 4);
+    int *s_fin = reinterpret_cast<int *>(p);
 
     pdl_wait();
     // Release the down kernel only now: it reads the router's ids before its
@@ -158,8 +167,9 @@ __global__ void __launch_bounds__(kGuWarps * 32) k_moe_gate_up(GateUpArgs a) {
         tma_load_1d(wt + bytes, ub + urow * a.pitch, bytes, &bars[warp]);
     }
     bool ok = true;
-    const int nitem = 2 * kGuRowsPerWarp * ipr;  // per warp: 4 gate rows then 4 up rows
+    const int nitem = 2 * kGuRowsPerWarp * ipr;  // per warp: 2 gate rows then 2 up rows
     float *wpart = part + (size_t)warp * NT * nitem;
+    const uint32_t nblkF = a.F / 32, blk = r0 / 32;
     for (uint32_t c0 = 0; c0 < cnt; c0 += NT) {
         const int nt = (int)min((uint32_t)NT, cnt - c0);
         if (threadIdx.x < (unsigned)nt) {
@@ -196,9 +206,24 @@ __global__ void __launch_bounds__(kGuWarps * 32) k_moe_gate_up(GateUpArgs a) {
             }
         }
         __syncthreads();
-        if (warp < nt && ok)
-            qact_store_block(a.hq + (size_t)(off + c0 + warp) * a.hq_pitch, (int)a.F, (int)(r0 / 32),
-                             hbuf[warp * kGuRows + lane], lane);
+        if (threadIdx.x < (unsigned)(nt * kGuRows)) {
+            const int t = threadIdx.x / kGuRows, i = threadIdx.x % kGuRows;
+            a.hf[(size_t)(off + c0 + t) * a.F + r0 + i] = hbuf[t * kGuRows + i];
+            __threadfence();
+        }
+        __syncthreads();
+        if (threadIdx.x < (unsigned)nt) {
+            const uint32_t old = atomicAdd(&a.hcnt[(size_t)(off + c0 + threadIdx.x) * nblkF + blk], 1u);
+            s_fin[threadIdx.x] = old == kGuCtasPerBlock - 1;
+        }
+        __syncthreads();
+        if (warp < nt && s_fin[warp]) {  // last CTA of this 32-element block: quantise it
+            __threadfence();
+            const uint32_t pos = off + c0 + warp;
+            const float v = __ldcg(a.hf + (size_t)pos * a.F + 32 * blk + lane);
+            qact_store_block(a.hq + (size_t)pos * a.hq_pitch, (int)a.F, (int)blk, v, lane);
+            if (lane == 0) a.hcnt[(size_t)pos * nblkF + blk] = 0;
+        }
         __syncthreads();
     }
 }
@@ -212,7 +237,7 @@ static cudaError_t launch_gate_up_t(const LaunchCfg &c, const GateUpArgs &a, uin
 
 cudaError_t launch_moe_gate_up(const LaunchCfg &c, const DevMat &gate, const DevMat &up, int act, const uint8_t *xq,
                                uint64_t xq_pitch, uint32_t ntok, uint32_t k, const uint32_t *ids, bool direct,
-                               const MoePlan &p, uint8_t *hq, uint64_t hq_pitch) {
+                               const MoePlan &p, float *hf, uint32_t *hcnt, uint8_t *hq, uint64_t hq_pitch) {
     GateUpArgs a;
     const bool fused = up.data == nullptr;
     a.gate = gate.data;
@@ -230,6 +255,8 @@ cudaError_t launch_moe_gate_up(const LaunchCfg &c, const DevMat &gate, const Dev
     a.ids = ids;
     a.direct = direct ? 1 : 0;
     a.p = p;
+    a.hf = hf;
+    a.hcnt = hcnt;
     a.hq = hq;
     a.hq_pitch = hq_pitch;
     a.dev_err = c.dev_err;

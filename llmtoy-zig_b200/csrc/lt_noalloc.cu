@@ -11,8 +11,9 @@
 //
 // The array (kNoallocScratchBytes) is part of the module, so every GPU that
 // loads the library holds it until the process exits.  Every call shares it
-// and it keeps the previous call's contents; nothing in it must start at zero
-// (the dispatch plan and activations are fully rewritten each call).  Calls
+// and it keeps the previous call's contents: the dispatch plan and the
+// activations are fully rewritten each call, and the gate/up block counters,
+// which must start at zero, are cleared at the start of every call.  Calls
 // whose work overlaps on the GPU (different streams, or graphs replayed
 // concurrently) race on it; serialise them.
 #include <mutex>
@@ -91,6 +92,7 @@ extern "C" lt_status lt_moe_ffn_noalloc(void *cuda_stream, const void *gate, con
     const size_t o_xq = take((size_t)ntok * xq_pitch), o_hq = take(P * hq_pitch);
     const size_t o_na = take(4), o_ae = take((size_t)n_experts * 4), o_ao = take((size_t)n_experts * 4),
                  o_ac = take((size_t)n_experts * 4), o_pp = take(P * 4), o_ppos = take(P * 4);
+    const size_t o_hf = take(P * d_expert * 4), n_cnt = P * (d_expert / 32), o_cnt = take(n_cnt * 4);
     if (off > kNoallocScratchBytes) return LT_EINVAL;  // beyond the static maximum
 
     int device = 0;
@@ -123,11 +125,14 @@ extern "C" lt_status lt_moe_ffn_noalloc(void *cuda_stream, const void *gate, con
     DevMat dn{static_cast<const uint8_t *>(down), down_type, d_model, F, drb, drb, n_experts};
     const bool direct = ntok == 1;
 
-    cudaError_t e = launch_quantize(c, dev_x, (uint32_t)d_model, ntok, base + o_xq, xq_pitch);
+    // The gate/up block counters must start at zero: clear them (a memset, not an allocation).
+    cudaError_t e = cudaMemsetAsync(base + o_cnt, 0, n_cnt * 4, c.stream);
+    if (e == cudaSuccess) e = launch_quantize(c, dev_x, (uint32_t)d_model, ntok, base + o_xq, xq_pitch);
     if (e == cudaSuccess && !direct) e = launch_moe_plan(c, dev_ids, ntok, k, n_experts, plan);
     if (e == cudaSuccess)
-        e = launch_moe_gate_up(c, g, u, act, base + o_xq, xq_pitch, ntok, k, dev_ids, direct, plan, base + o_hq,
-                               hq_pitch);
+        e = launch_moe_gate_up(c, g, u, act, base + o_xq, xq_pitch, ntok, k, dev_ids, direct, plan,
+                               reinterpret_cast<float *>(base + o_hf), reinterpret_cast<uint32_t *>(base + o_cnt),
+                               base + o_hq, hq_pitch);
     if (e == cudaSuccess)
         e = launch_moe_down(c, dn, base + o_hq, hq_pitch, ntok, k, dev_ids, dev_w, direct, plan, nullptr, dev_out);
     if (e == cudaSuccess) e = cudaGetLastError();

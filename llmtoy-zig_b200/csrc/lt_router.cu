@@ -70,19 +70,29 @@ struct RouterArgs {
 };
 
 __global__ void __launch_bounds__(kRouterWarps * 32) k_router(RouterArgs a) {
-    extern __shared__ __align__(16) float xsm[];  // [kRouterTok][cols]
+    extern __shared__ __align__(16) float xsm[];  // [kRouterTok][cols] x, then [cols] norm weights
     __shared__ int s_last;
+    __shared__ float s_ss[kRouterWarps][kRouterTok];
     __shared__ float s_rms[kRouterTok];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t e = blockIdx.x * kRouterWarps + warp;
     const uint32_t t0 = blockIdx.y * kRouterTok;
     const uint32_t nt = min((uint32_t)kRouterTok, a.ntok - t0);
     const uint32_t cols = a.cols, n32 = cols & ~31u;
-    // router weights are static: fetch them while the producer of x finishes
+    float *nwsm = xsm + kRouterTok * cols;
+    // router and norm weights are static: fetch them while the producer of x finishes
     float w0[kRouterChunk];
 #pragma unroll
     for (int j = 0; j < kRouterChunk; j++)
         w0[j] = (e < a.E && 32u * j < n32) ? __ldg(a.W + (size_t)e * a.w_ld + 32 * j + lane) : 0.0f;
+    if (a.norm_w) {
+        if ((cols & 3) == 0 && (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0) {
+            for (uint32_t i = threadIdx.x; i < cols / 4; i += blockDim.x)
+                reinterpret_cast<float4 *>(nwsm)[i] = __ldg(reinterpret_cast<const float4 *>(a.norm_w) + i);
+        } else {
+            for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) nwsm[i] = __ldg(a.norm_w + i);
+        }
+    }
     pdl_launch_dependents();
     pdl_wait();
     {
@@ -97,16 +107,27 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(RouterArgs a) {
     }
     __syncthreads();
     if (a.norm_w) {  // rmsnorm(out, x, w, eps): x * (1/sqrt(ss/n + eps)) * w
-        if (warp < (int)nt) {
-            float ss = 0.0f;
-            for (uint32_t i = lane; i < cols; i += 32) ss += xsm[warp * cols + i] * xsm[warp * cols + i];
-            ss = warp_sum(ss);
-            if (lane == 0) s_rms[warp] = 1.0f / sqrtf(ss / (float)cols + a.eps);
+        float ss[kRouterTok];
+#pragma unroll
+        for (int tt = 0; tt < kRouterTok; tt++) {
+            ss[tt] = 0.0f;
+            if (tt < (int)nt)
+                for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) ss[tt] += xsm[tt * cols + i] * xsm[tt * cols + i];
+            ss[tt] = warp_sum(ss[tt]);
+        }
+        if (lane == 0)
+#pragma unroll
+            for (int tt = 0; tt < kRouterTok; tt++) s_ss[warp][tt] = ss[tt];
+        __syncthreads();
+        if (threadIdx.x < nt) {
+            float s = 0.0f;
+            for (int w = 0; w < kRouterWarps; w++) s += s_ss[w][threadIdx.x];
+            s_rms[threadIdx.x] = 1.0f / sqrtf(s / (float)cols + a.eps);
         }
         __syncthreads();
         for (uint32_t i = threadIdx.x; i < nt * cols; i += blockDim.x) {
             const uint32_t tt = i / cols, c = i - tt * cols;
-            xsm[i] = xsm[i] * s_rms[tt] * a.norm_w[c];
+            xsm[i] = xsm[i] * s_rms[tt] * nwsm[c];
         }
         __syncthreads();
     }
@@ -200,7 +221,7 @@ cudaError_t launch_router(const LaunchCfg &c, const float *w, uint32_t E, uint32
                           uint8_t *xq, uint64_t xq_pitch) {
     RouterArgs a{w, E, cols, w_ld, x, norm_w, eps, ntok, k, norm_topk, escale, ids, wout, logits, counters, xq, xq_pitch};
     const dim3 grid((E + kRouterWarps - 1) / kRouterWarps, router_token_groups(ntok));
-    const size_t smem = (size_t)kRouterTok * cols * 4;
+    const size_t smem = (size_t)(kRouterTok + (norm_w ? 1 : 0)) * cols * 4;
     return launch_k(c, "router_topk", k_router, grid, dim3(kRouterWarps * 32), smem, a);
 }
 
