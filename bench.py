@@ -5,7 +5,8 @@ FFN layers of the Qwen3-30B-A3B shape -- d_model 2048, 128 experts, top-8 with
 renormalised softmax, SwiGLU expert width 768, Q4_K experts, f32 router --
 each layer the pre-norm residual MoE block x <- x + moe(rmsnorm(x))
 (src/model/forward.zig:304-309 with the FFN replaced by the MoE; one
-lt_moe_block call: router+norm, gate/up, down+combine+residual kernels).
+lt_moe_block call per layer, which at one token is a single persistent kernel:
+norm, router, top-k, gate/up, down, combine and residual).
 48 distinct weight sets (16.3 GB) make every
 step read ~1.07 GB of weights, far more than the 126 MB L2, so no flush is
 needed.  Weights are seeded synthetic bytes with the config's distributions,
@@ -373,17 +374,25 @@ def main() -> None:
     ctx.profile(False)
 
     peak, peak_kind = measured_peaks()
-    gu = prof.get("moe_gate_up_q4k")
-    gu_bytes = TOP_K * 2 * D_EXPERT * Q4K_ROW(D_MODEL) + D_MODEL * 4 + TOP_K * D_EXPERT * 4
     roofline = None
-    if gu and gu["count"]:
-        gu_ms = gu["total_ms"] / gu["count"]
-        achieved = gu_bytes / (gu_ms / 1e3) / 1e9
-        tr = ncu_traffic()
-        traffic = tr.get("moe_gate_up_q4k", {}).get("dram_bytes_per_launch") if tr else None
-        roofline = {"kernel": "moe_gate_up_q4k", "bound": "hbm", "achieved": achieved, "peak": peak,
+    tr = ncu_traffic()
+    if prof.get("moe_decode", {}).get("count"):
+        # one launch = the whole block: router rows, 8 experts' gate/up/down
+        # rows, norm weights, x in and out
+        kname = "moe_decode"
+        kbytes = TOP_K * EXPERT_BYTES + ROUTER_BYTES + 3 * D_MODEL * 4
+    else:
+        kname = "moe_gate_up_q4k"
+        kbytes = TOP_K * 2 * D_EXPERT * Q4K_ROW(D_MODEL) + D_MODEL * 4 + TOP_K * D_EXPERT * 4
+    kp = prof.get(kname)
+    if kp and kp["count"]:
+        k_ms = kp["total_ms"] / kp["count"]
+        achieved = kbytes / (k_ms / 1e3) / 1e9
+        traffic = tr.get(kname, {}).get("dram_bytes_per_launch") if tr else None
+        roofline = {"kernel": kname, "bound": "hbm", "achieved": achieved, "peak": peak,
                     "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
-                    "algorithmic_bytes_per_launch": gu_bytes, "avg_launch_ms": gu_ms, "traffic": traffic}
+                    "algorithmic_bytes_per_launch": kbytes, "avg_launch_ms": k_ms, "traffic": traffic}
+    launches_per_step = sum(v["count"] for v in prof.values()) / max(1, args.profile_steps)
     step_bytes = args.layers * (TOP_K * EXPERT_BYTES + ROUTER_BYTES)
     kernels = {k: {"count": v["count"], "avg_us": 1e3 * v["total_ms"] / max(1, v["count"])} for k, v in prof.items()}
     layer_bytes = TOP_K * EXPERT_BYTES + ROUTER_BYTES
@@ -405,7 +414,7 @@ def main() -> None:
             "expert_hbm_gbs": step_bytes / (ms_step / 1e3) / 1e9,
             "hbm_frac_of_step": (step_bytes / (ms_step / 1e3) / 1e9) / peak,
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": args.steps * 3 * args.layers, "clocks": clocks,
+            "gpu_launches": int(round(args.steps * launches_per_step)), "clocks": clocks,
             "kernels_profiled": kernels, "layer_bytes": layer_bytes,
             "graph": graph is not None,
         }

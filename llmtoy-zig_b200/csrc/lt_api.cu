@@ -28,7 +28,9 @@ struct lt_ctx {
     std::string err;
     int num_sms = 0;
     bool pdl = true;
+    bool decode_kernel = true;       // single-token MoE blocks run as one persistent kernel
     int *dev_err = nullptr;          // device error word written by kernels
+    uint8_t *dec_sync = nullptr;     // counters and tagged logits of the persistent decode kernel
     uint8_t *scratch = nullptr;      // activation scratch arena
     size_t scratch_bytes = 0;
     uint32_t *counters = nullptr;    // zero-initialised, kernels leave them zero
@@ -164,6 +166,7 @@ struct MoeScratch {
     uint8_t *hq;
     uint64_t hq_pitch;
     float *hf;  // f32 h rows, staged before quantisation
+    uint8_t *himg;  // single-token decode kernel: quantised h slot images
     lt::MoePlan plan;
     size_t bytes;
     size_t counters;  // block counters needed past kMoeCounterBase
@@ -185,6 +188,7 @@ MoeScratch moe_layout(uint8_t *base, uint32_t T, uint32_t k, uint32_t E, uint64_
     s.xq = take((size_t)T * s.xq_pitch);
     s.hq = take(P * s.hq_pitch);
     s.hf = (float *)take(P * F * 4);
+    s.himg = take(P * lt::moe_decode_img_bytes(F));
     s.counters = P * (F / 32);
     s.logits = (float *)take((size_t)T * E * 4);
     s.plan.n_active = (uint32_t *)take(4);
@@ -241,10 +245,14 @@ lt_status lt_init(int device, lt_ctx **out) {
     ctx->num_sms = prop.multiProcessorCount;
     const char *pdl = getenv("LLMTOY_PDL");
     ctx->pdl = !(pdl && strcmp(pdl, "0") == 0);
+    const char *dk = getenv("LLMTOY_DECODE_KERNEL");
+    ctx->decode_kernel = !(dk && strcmp(dk, "0") == 0);
     lt_status st = LT_OK;
     if (cudaSetDevice(device) != cudaSuccess ||
         cudaStreamCreateWithFlags(&ctx->own, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaMalloc(&ctx->dev_err, 4) != cudaSuccess || cudaMemset(ctx->dev_err, 0, 4) != cudaSuccess) {
+        cudaMalloc(&ctx->dev_err, 4) != cudaSuccess || cudaMemset(ctx->dev_err, 0, 4) != cudaSuccess ||
+        cudaMalloc(&ctx->dec_sync, lt::kDecodeSyncBytes) != cudaSuccess ||
+        cudaMemset(ctx->dec_sync, 0, lt::kDecodeSyncBytes) != cudaSuccess) {
         st = LT_ECUDA;
     }
     ctx->stream = ctx->own;
@@ -270,6 +278,7 @@ void lt_free(lt_ctx *ctx) {
     if (ctx->scratch) cudaFree(ctx->scratch);
     if (ctx->counters) cudaFree(ctx->counters);
     if (ctx->dev_err) cudaFree(ctx->dev_err);
+    if (ctx->dec_sync) cudaFree(ctx->dec_sync);
     if (ctx->pinned) cudaFreeHost(ctx->pinned);
     if (ctx->own) cudaStreamDestroy(ctx->own);
     delete ctx;
@@ -673,6 +682,31 @@ static lt_status forward_impl(lt_ctx *ctx, const lt_tensor *router, const lt_ten
     const MoeScratch s = moe_layout(ctx->scratch, ntok, k, E, d, F);
     uint32_t *ids = dev_ids ? dev_ids : s.ids;
     float *w = dev_w ? dev_w : s.w;
+    if (ntok == 1 && ctx->decode_kernel) {
+        lt::DecodeParams p;
+        p.router = (const float *)router->m.data;
+        p.E = E;
+        p.d = (uint32_t)d;
+        p.router_ld = (uint32_t)(router->m.pitch / 4);
+        p.x = dev_x;
+        p.norm_w = dev_norm_w;
+        p.eps = eps;
+        p.k = k;
+        p.norm_topk = norm_topk;
+        p.escale = dev_expert_scale;
+        p.ids = ids;
+        p.w = w;
+        p.gate = gate->m;
+        p.up_data = up ? up->m.data : nullptr;
+        p.down = down->m;
+        p.F = (uint32_t)F;
+        p.act = act;
+        p.himg = s.himg;
+        p.residual = residual;
+        p.out = dev_out;
+        p.sync = ctx->dec_sync;
+        if (lt::moe_decode_fits(p, ctx->num_sms)) return launched(ctx, lt::launch_moe_decode(cfg_of(ctx), p), "moe decode");
+    }
     st = route_impl(ctx, router, dev_x, dev_norm_w, eps, ntok, k, norm_topk, dev_expert_scale, ids, w, s.logits, s.xq,
                     s.xq_pitch);
     if (st != LT_OK) return st;

@@ -85,7 +85,7 @@ LT_DEVINL void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dep
 // ── error reporting ────────────────────────────────────────────────────────
 // Kernels never trap.  A bounded wait that gives up records a code in the
 // context's device error word; the host turns it into LT_ETIMEOUT.
-enum : int { DEV_ERR_NONE = 0, DEV_ERR_TMA_TIMEOUT = 1 };
+enum : int { DEV_ERR_NONE = 0, DEV_ERR_TMA_TIMEOUT = 1, DEV_ERR_GRID_TIMEOUT = 2 };
 
 // ── mbarrier + TMA bulk copy (global -> shared) ────────────────────────────
 LT_DEVINL uint32_t smem_u32(const void *p) {
@@ -137,6 +137,72 @@ LT_DEVINL bool mbar_wait_bounded(uint64_t *bar, uint32_t phase, uint64_t limit_n
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
         if (t - t0 > limit_ns) return false;
     }
+}
+
+LT_DEVINL uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ── grid-wide synchronisation for kernels whose CTAs are all resident ────────
+// Counters that only grow.  Each CTA adds exactly 1 per launch to each, so
+// with G CTAs a counter is a multiple of G between launches (the next launch
+// starts after the previous one completed), and launch n's arrivals complete
+// it at (n + 1) * G: the "epoch" of the launch, the same number in every CTA.
+// Arrival is unconditional (also after a timed-out wait), which keeps that
+// invariant.
+LT_DEVINL uint64_t ld_acquire_u64(const unsigned long long *p) {
+    uint64_t v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+LT_DEVINL uint64_t ld_relaxed_u64(const unsigned long long *p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+LT_DEVINL void st_relaxed_u64(unsigned long long *p, uint64_t v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+LT_DEVINL void red_release_add_u64(unsigned long long *p, uint64_t v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Orders this thread's generic-proxy global accesses with its later (or, on
+// the producer side, other threads' later) TMA accesses of global memory.
+LT_DEVINL void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Thread 0: arrive on the epoch counter and return this launch's epoch.
+LT_DEVINL uint64_t grid_epoch(unsigned long long *ctr, uint32_t G) {
+    const uint64_t old = atomicAdd(ctr, 1ull);
+    return old - old % G + G;
+}
+
+// Whole block: publish this CTA's global writes and arrive (no return value).
+LT_DEVINL void grid_arrive(unsigned long long *ctr) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        red_release_add_u64(ctr, 1ull);
+    }
+}
+
+// Whole block: bounded wait (limit_ns of wall time) until the counter
+// reaches target; on timeout records DEV_ERR_GRID_TIMEOUT and continues.
+LT_DEVINL void grid_wait(const unsigned long long *ctr, uint64_t target, int *dev_err, uint64_t limit_ns) {
+    if (threadIdx.x == 0) {
+        if (ld_acquire_u64(ctr) < target) {
+            const uint64_t t0 = globaltimer_ns();
+            while (ld_acquire_u64(ctr) < target) {
+                if (globaltimer_ns() - t0 > limit_ns) {
+                    if (dev_err) atomicExch(dev_err, DEV_ERR_GRID_TIMEOUT);
+                    break;
+                }
+            }
+        }
+        __threadfence();
+    }
+    __syncthreads();
 }
 
 LT_DEVINL uint4 lds128(const void *p) {

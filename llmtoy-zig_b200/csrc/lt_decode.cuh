@@ -1,7 +1,7 @@
 // lt_decode.cuh — GGUF block decoders that take dot products against
 // quantised activations held in shared memory.
 //
-// Activations.  Each 32-element block of an activation row is stored as
+// Activations.  Each 16-element group of an activation row is stored as
 // x ~= s * (hi + lo / 254) with s = amax / 32767: hi = round(x / s) as int16
 // and lo = round of the remainder in 1/254 steps as int8 -- about 2^-24 of the
 // block's range, f32-like.  Products with the quant values (4-8 bit integers)
@@ -13,8 +13,8 @@
 // Shared-memory layout per token t and item i (256 columns): hi at
 // xq + t*tok_hi + i*528, lo at xl + t*tok_lo + i*272; the 16 padding bytes
 // per item put threads that decode different items in different banks.  Per
-// 32-block: scale xs; per 16-group: f32 sum of the original values xsum16
-// (used for the Q4_K minimum and the Q6_K -32 offset terms, applied in f32).
+// 16-group: scale xs and the f32 sum of the original values xsum16 (used for
+// the Q4_K minimum and the Q6_K -32 offset terms, applied in f32).
 #pragma once
 
 #include "lt_common.cuh"
@@ -28,16 +28,16 @@ constexpr float kLoScale = 1.0f / 254.0f;
 struct XS {
     uint8_t *xq;    // hi terms
     uint8_t *xl;    // lo terms
-    float *xs;      // [t][item*8 + block] scale
+    float *xs;      // [t][item*16 + group] scale
     float *xsum16;  // [t][item*16 + group] sum of x over 16 elements
     int nitems;
-    int tok_hi;   // nitems * 528
-    int tok_lo;   // nitems * 272
-    int tok_blk;  // nitems * 8
+    int tok_hi;  // nitems * 528
+    int tok_lo;  // nitems * 272
+    int tok_g;   // nitems * 16
 };
 
 __host__ __device__ inline size_t xs_bytes(int ntok, int nitems) {
-    return (size_t)ntok * nitems * (kXHiPitch + kXLoPitch + 8 * 4 + 16 * 4);
+    return (size_t)ntok * nitems * (kXHiPitch + kXLoPitch + 16 * 4 + 16 * 4);
 }
 
 LT_DEVINL XS xs_carve(uint8_t *p, int ntok, int nitems) {
@@ -45,13 +45,13 @@ LT_DEVINL XS xs_carve(uint8_t *p, int ntok, int nitems) {
     x.nitems = nitems;
     x.tok_hi = nitems * kXHiPitch;
     x.tok_lo = nitems * kXLoPitch;
-    x.tok_blk = nitems * 8;
+    x.tok_g = nitems * 16;
     x.xq = p;
     p += (size_t)ntok * x.tok_hi;
     x.xl = p;
     p += (size_t)ntok * x.tok_lo;
     x.xs = reinterpret_cast<float *>(p);
-    p += (size_t)ntok * nitems * 8 * 4;
+    p += (size_t)ntok * nitems * 16 * 4;
     x.xsum16 = reinterpret_cast<float *>(p);
     return x;
 }
@@ -73,33 +73,35 @@ LT_DEVINL void load_x32(const XS &X, int t, int item, int elem0, uint32_t (&hi)[
     }
 }
 
-// sum over 32 elements of q * x_hi and q * x_lo for quant bytes q[8]
-// (4 per word, unsigned), with two accumulators per term for ILP.
-LT_DEVINL void dot32_u(const uint32_t (&q)[8], const uint32_t (&xh)[16], const uint32_t (&xl)[8], int &hi, int &lo) {
+// sums over 32 elements of q * x_hi and q * x_lo for quant bytes q[8] (4 per
+// word, unsigned), kept per 16-element half (each half has its own scale).
+LT_DEVINL void dot32_u(const uint32_t (&q)[8], const uint32_t (&xh)[16], const uint32_t (&xl)[8], int (&hi)[2],
+                       int (&lo)[2]) {
     int h0 = 0, h1 = 0, l0 = 0, l1 = 0;
 #pragma unroll
-    for (int k = 0; k < 8; k += 2) {
+    for (int k = 0; k < 4; k++) {
         h0 = dp2a_hi_su((int)xh[2 * k + 1], q[k], dp2a_lo_su((int)xh[2 * k], q[k], h0));
-        h1 = dp2a_hi_su((int)xh[2 * k + 3], q[k + 1], dp2a_lo_su((int)xh[2 * k + 2], q[k + 1], h1));
+        h1 = dp2a_hi_su((int)xh[2 * k + 9], q[k + 4], dp2a_lo_su((int)xh[2 * k + 8], q[k + 4], h1));
         l0 = dp4a_su((int)xl[k], q[k], l0);
-        l1 = dp4a_su((int)xl[k + 1], q[k + 1], l1);
+        l1 = dp4a_su((int)xl[k + 4], q[k + 4], l1);
     }
-    hi = h0 + h1;
-    lo = l0 + l1;
+    hi[0] = h0; hi[1] = h1;
+    lo[0] = l0; lo[1] = l1;
 }
 
 // Same with signed quant bytes (Q8_0).
-LT_DEVINL void dot32_s(const uint32_t (&q)[8], const uint32_t (&xh)[16], const uint32_t (&xl)[8], int &hi, int &lo) {
+LT_DEVINL void dot32_s(const uint32_t (&q)[8], const uint32_t (&xh)[16], const uint32_t (&xl)[8], int (&hi)[2],
+                       int (&lo)[2]) {
     int h0 = 0, h1 = 0, l0 = 0, l1 = 0;
 #pragma unroll
-    for (int k = 0; k < 8; k += 2) {
+    for (int k = 0; k < 4; k++) {
         h0 = dp2a_hi_ss((int)xh[2 * k + 1], q[k], dp2a_lo_ss((int)xh[2 * k], q[k], h0));
-        h1 = dp2a_hi_ss((int)xh[2 * k + 3], q[k + 1], dp2a_lo_ss((int)xh[2 * k + 2], q[k + 1], h1));
+        h1 = dp2a_hi_ss((int)xh[2 * k + 9], q[k + 4], dp2a_lo_ss((int)xh[2 * k + 8], q[k + 4], h1));
         l0 = dp4a_ss((int)xl[k], q[k], l0);
-        l1 = dp4a_ss((int)xl[k + 1], q[k + 1], l1);
+        l1 = dp4a_ss((int)xl[k + 4], q[k + 4], l1);
     }
-    hi = h0 + h1;
-    lo = l0 + l1;
+    hi[0] = h0; hi[1] = h1;
+    lo[0] = l0; lo[1] = l1;
 }
 
 LT_DEVINL float qx(int hi, int lo) { return (float)hi + (float)lo * kLoScale; }
@@ -134,13 +136,13 @@ LT_DEVINL void dot_q4k(const uint8_t *sbp, int item, const XS &X, int t0, int nt
                 uint32_t ah[16], al[8], bh[16], bl[8];
                 load_x32(X, t, item, 64 * c, ah, al);
                 load_x32(X, t, item, 64 * c + 32, bh, bl);
-                int aH, aL, bH, bL;
+                int aH[2], aL[2], bH[2], bL[2];
                 dot32_u(lo, ah, al, aH, aL);
                 dot32_u(hi, bh, bl, bH, bL);
-                const float *xs = X.xs + t * X.tok_blk + item * 8;
-                const float *x16 = X.xsum16 + t * X.tok_blk * 2 + item * 16;
-                res[tt] += dA * xs[2 * c] * qx(aH, aL) - mA * (x16[4 * c] + x16[4 * c + 1]);
-                res[tt] += dB * xs[2 * c + 1] * qx(bH, bL) - mB * (x16[4 * c + 2] + x16[4 * c + 3]);
+                const float *xs = X.xs + t * X.tok_g + item * 16 + 4 * c;
+                const float *x16 = X.xsum16 + t * X.tok_g + item * 16 + 4 * c;
+                res[tt] += dA * (xs[0] * qx(aH[0], aL[0]) + xs[1] * qx(aH[1], aL[1])) - mA * (x16[0] + x16[1]);
+                res[tt] += dB * (xs[2] * qx(bH[0], bL[0]) + xs[3] * qx(bH[1], bL[1])) - mB * (x16[2] + x16[3]);
             }
         }
     }
@@ -175,9 +177,10 @@ LT_DEVINL void dot_q8_block(const uint32_t *w, int item, const XS &X, int t0, in
             const int t = t0 + tt;
             uint32_t xh[16], xl[8];
             load_x32(X, t, item, 32 * B, xh, xl);
-            int h, l;
+            int h[2], l[2];
             dot32_s(q, xh, xl, h, l);
-            res[tt] += d * X.xs[t * X.tok_blk + item * 8 + B] * qx(h, l);
+            const float *xs = X.xs + t * X.tok_g + item * 16 + 2 * B;
+            res[tt] += d * (xs[0] * qx(h[0], l[0]) + xs[1] * qx(h[1], l[1]));
         }
     }
 }
@@ -257,11 +260,11 @@ LT_DEVINL void dot_q6k(const uint8_t *sbp, int item, const XS &X, int t0, int nt
                         l1 = dp4a_su((int)xl[4 + k], qv[kind][4 + k], l1);
                     }
                     const int g = 8 * n + 2 * kind;  // 16-group index inside the item
-                    const float *x16 = X.xsum16 + t * X.tok_blk * 2 + item * 16;
-                    const float xsc = X.xs[t * X.tok_blk + item * 8 + 4 * n + kind];
+                    const float *x16 = X.xsum16 + t * X.tok_g + item * 16;
+                    const float *xs = X.xs + t * X.tok_g + item * 16;
                     // sum (q - 32) x = s * sum q*xq - 32 * sum x
-                    res[tt] += ds0 * (xsc * qx(h0, l0) - 32.0f * x16[g]);
-                    res[tt] += ds1 * (xsc * qx(h1, l1) - 32.0f * x16[g + 1]);
+                    res[tt] += ds0 * (xs[g] * qx(h0, l0) - 32.0f * x16[g]);
+                    res[tt] += ds1 * (xs[g + 1] * qx(h1, l1) - 32.0f * x16[g + 1]);
                 }
             }
         }

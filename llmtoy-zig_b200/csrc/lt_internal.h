@@ -116,4 +116,37 @@ cudaError_t launch_moe_down(const LaunchCfg &c, const DevMat &down, const uint8_
                             uint32_t ntok, uint32_t k, const uint32_t *ids, const float *w, bool direct,
                             const MoePlan &p, const float *resid, float *out);
 
+
+// One token through a whole MoE block in one persistent kernel (one CTA per
+// SM, grid barriers): RMSNorm (norm_w != nullptr), router, top-k, gate/up,
+// down, combine, residual (residual != 0: out = x + moe).  out may alias x.
+struct DecodeParams {
+    const float *router;  // F32 [E][router_ld]
+    uint32_t E, d, router_ld;
+    const float *x, *norm_w;
+    float eps;
+    uint32_t k;
+    int norm_topk;
+    const float *escale;
+    uint32_t *ids;
+    float *w;
+    DevMat gate;
+    const uint8_t *up_data;  // nullptr: fused gate_up
+    DevMat down;
+    uint32_t F;
+    int act;
+    uint8_t *himg;  // [k][moe_decode_img_bytes(F)] scratch
+    int residual;
+    float *out;
+    // kDecodeSyncBytes, zero-initialised, used by no other kernel and only
+    // with grid = num_sms: epoch and barrier counters, tagged logits
+    uint8_t *sync;
+};
+constexpr size_t kDecodeSyncBytes = 4096;
+size_t moe_decode_img_bytes(uint64_t F);
+constexpr size_t kDecodeSmemLimit = 227 * 1024;
+// Whether the persistent kernel's per-CTA share fits in shared memory.
+bool moe_decode_fits(const DecodeParams &p, int num_sms);
+cudaError_t launch_moe_decode(const LaunchCfg &c, const DecodeParams &p);
+
 }  // namespace lt

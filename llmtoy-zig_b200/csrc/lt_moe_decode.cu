@@ -1,0 +1,454 @@
+// lt_moe_decode.cu — one token through a whole MoE block in one persistent
+// kernel: pre-FFN RMSNorm, router logits, top-k + softmax weights, grouped
+// gate/up with the activation, down projection, weighted combine and the
+// residual add (src/model/gemma4/forward.zig:463-479 and 648-668,
+// src/ops/moe.zig:61-76).
+//
+// At batch 1 the block is a chain of small dependent steps (x -> logits ->
+// ids -> expert rows -> h -> out) whose weights are read once, and every
+// global round trip on the chain costs about a microsecond.  One CTA per SM
+// runs the chain with two grid-wide hand-offs:
+//
+//   phase R  every CTA stages x and normalises it (the router kernel's
+//            reduction order); CTA e % G computes the logit of expert e with
+//            its router row prefetched into registers before the wait for the
+//            previous kernel, and publishes it as one 64-bit word tagged with
+//            the launch's epoch.  Every CTA polls the E words directly (no
+//            separate barrier) and ranks them itself: identical inputs and
+//            code, so identical ids everywhere.
+//   phase G  each CTA issues one TMA bulk copy per 8 gate/up pairs of its
+//            share (whole 16-pair units of the k*F (slot, row) pairs) and one
+//            per slot for its share of the down rows, all at once, computes
+//            its h values as the copies land, quantises them (16-groups) and
+//            writes them into the shared-memory image of their slot in global
+//            memory.                                      -> grid barrier
+//   phase D  each CTA copies the k slot images with one TMA copy each and
+//            finishes its down rows for every slot, combines them in slot
+//            order and adds the residual kept from phase R.
+//
+// Per-item decoding, partial-sum orders and the combine are those of the
+// router / gate_up / down kernels, so both paths give the same bits.
+#include "lt_qact.cuh"
+#include "lt_router.cuh"
+
+namespace lt {
+
+constexpr int kDecWarps = 16;
+constexpr int kDecThreads = kDecWarps * 32;
+constexpr int kDecChunk = 8;          // gate/up pairs per TMA chunk
+constexpr int kDecUnit = 16;          // pairs per work unit (one quantisation group)
+constexpr int kDecMaxChunks = 48;     // chunk mbarriers; then k down-slot barriers, then the h barrier
+constexpr int kDecNormThreads = 128;  // RMSNorm reduction width of the router kernel
+
+// Layout of the context's sync block (DecodeParams::sync).
+constexpr size_t kSyncEpoch = 0;   // u64 counter: epoch arrivals
+constexpr size_t kSyncB = 8;       // u64 counter: barrier after h
+constexpr size_t kSyncLogits = 256;  // u64 [kRouterMaxE]: tagged logits
+
+struct DecodeArgs {
+    // router
+    const float *rw;  // [E][rw_ld]
+    uint32_t E, d, rw_ld;
+    const float *x;       // [d]
+    const float *norm_w;  // nullable
+    float eps;
+    uint32_t k;
+    int norm_topk;
+    const float *escale;  // nullable
+    uint32_t *ids;
+    float *wout;
+    // experts
+    const uint8_t *gate, *up;  // up == nullptr: fused gate_up tensor
+    uint64_t gpitch;
+    uint32_t F, gi, gnb;  // items and 32-blocks per gate row
+    int act;
+    const uint8_t *down;
+    uint64_t dpitch;
+    uint32_t di, dnb;
+    uint8_t *himg;  // [k][img] quantised h in the shared-memory layout (xs_bytes(1, di) per slot)
+    uint32_t img;
+    int residual;
+    float *out;  // [d], may alias x
+    uint8_t *sync;
+    int *dev_err;
+    uint32_t maxpairs, maxrows;  // per-CTA maxima the layout is sized for
+};
+
+struct DecodeLayout {
+    size_t bars, misc, lg, keys, cnt, part, ys, hs, xres, xsx, rr, gt, dt, total;
+};
+
+__host__ __device__ inline DecodeLayout decode_layout(uint32_t E, uint32_t d, uint32_t k, uint64_t gpitch,
+                                                      uint32_t gi, uint64_t dpitch, uint32_t di, uint32_t img,
+                                                      uint32_t maxpairs, uint32_t maxrows) {
+    DecodeLayout L;
+    size_t off = 0;
+    auto take = [&](size_t b) {
+        const size_t o = off;
+        off += (b + 127) & ~(size_t)127;
+        return o;
+    };
+    L.bars = take((size_t)(kDecMaxChunks + 17) * 8);
+    L.misc = take(256);
+    L.lg = take((size_t)E * 4);
+    L.keys = take((size_t)(E + 2) * 8);
+    L.cnt = take((size_t)4 * E * 4);
+    const size_t pg = (size_t)maxpairs * 2 * gi, pd = (size_t)k * maxrows * di;
+    L.part = take((pg > pd ? pg : pd) * 4);
+    L.ys = take((size_t)k * maxrows * 4);
+    L.hs = take((size_t)maxpairs * 4);
+    L.xres = take((size_t)maxrows * 4);
+    L.xsx = take(xs_bytes(1, gi));
+    const size_t rr0 = (size_t)2 * d * 4, rr1 = (size_t)k * img;
+    L.rr = take(rr0 > rr1 ? rr0 : rr1);
+    L.gt = take((size_t)maxpairs * 2 * gpitch);
+    L.dt = take((size_t)k * maxrows * dpitch);
+    L.total = off;
+    return L;
+}
+
+template <uint32_t GT, uint32_t DT>
+__global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t G = gridDim.x, c = blockIdx.x;
+    const DecodeLayout L =
+        decode_layout(a.E, a.d, a.k, a.gpitch, a.gi, a.dpitch, a.di, a.img, a.maxpairs, a.maxrows);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
+    uint64_t *hbar = bars + kDecMaxChunks + 16;
+    uint32_t *s_sel = reinterpret_cast<uint32_t *>(smem + L.misc);    // [16]
+    float *s_w = reinterpret_cast<float *>(smem + L.misc + 64);       // [16]
+    float *s_ss = reinterpret_cast<float *>(smem + L.misc + 128);     // [4]
+    float *s_stat = reinterpret_cast<float *>(smem + L.misc + 160);   // rms, max, expsum
+    uint64_t *s_epoch = reinterpret_cast<uint64_t *>(smem + L.misc + 192);
+    float *s_lg = reinterpret_cast<float *>(smem + L.lg);
+    uint64_t *s_key = reinterpret_cast<uint64_t *>(smem + L.keys);
+    uint32_t *s_cnt = reinterpret_cast<uint32_t *>(smem + L.cnt);
+    float *part = reinterpret_cast<float *>(smem + L.part);
+    float *s_y = reinterpret_cast<float *>(smem + L.ys);
+    float *s_h = reinterpret_cast<float *>(smem + L.hs);
+    float *s_xres = reinterpret_cast<float *>(smem + L.xres);
+    const XS Xx = xs_carve(smem + L.xsx, 1, (int)a.gi);
+    float *xsm = reinterpret_cast<float *>(smem + L.rr);  // [d] x, normalised in place
+    float *nwsm = xsm + a.d;                              // [d] norm weights
+    uint8_t *gt = smem + L.gt, *dt = smem + L.dt;
+    unsigned long long *ctr_epoch = reinterpret_cast<unsigned long long *>(a.sync + kSyncEpoch);
+    unsigned long long *ctr_b = reinterpret_cast<unsigned long long *>(a.sync + kSyncB);
+    unsigned long long *lslots = reinterpret_cast<unsigned long long *>(a.sync + kSyncLogits);
+
+    // this CTA's shares: gate/up pairs [p0, p1) of the k*F (slot, row) pairs
+    // in whole 16-pair units, down rows [r0, r1) of d (for every slot)
+    const uint32_t nunits = a.k * a.F / kDecUnit;
+    const uint32_t p0 = kDecUnit * (uint32_t)((uint64_t)c * nunits / G);
+    const uint32_t p1 = kDecUnit * (uint32_t)((uint64_t)(c + 1) * nunits / G);
+    const uint32_t r0 = (uint32_t)((uint64_t)c * a.d / G), r1 = (uint32_t)((uint64_t)(c + 1) * a.d / G);
+    const uint32_t np = p1 - p0, nr = r1 - r0;
+    const uint32_t ch0 = p0 / kDecChunk;
+    const uint32_t nchunks = np / kDecChunk;  // p0, p1 are multiples of 16
+
+    if (tid < 16) s_sel[tid] = 0;  // ranks form a permutation; this only keeps ids in range regardless
+    if (tid == 0) {
+        for (uint32_t i = 0; i < nchunks; i++) mbar_init(&bars[i], 1);
+        for (uint32_t i = 0; i < a.k; i++) mbar_init(&bars[kDecMaxChunks + i], 1);
+        mbar_init(hbar, 1);
+        fence_barrier_init();
+    }
+    // static inputs first: this CTA's router rows and the norm weights
+    float w0[kRouterChunk];
+    const uint32_t e_mine = c + (uint32_t)warp * G;
+    const bool has_e = e_mine < a.E;
+    router_prefetch(a.rw + (size_t)(has_e ? e_mine : 0) * a.rw_ld, a.d, lane, has_e, w0);
+    if (a.norm_w)
+        for (uint32_t i = tid; i < a.d; i += kDecThreads) nwsm[i] = __ldg(a.norm_w + i);
+    pdl_launch_dependents();
+    pdl_wait();
+
+    // ── phase R ──────────────────────────────────────────────────────────────
+    uint64_t epoch = 0;
+    if (tid == 0) epoch = grid_epoch(ctr_epoch, G);  // returns while x streams in
+    if ((a.d & 3) == 0) {
+#pragma unroll 4
+        for (uint32_t i = tid; i < a.d / 4; i += kDecThreads)
+            reinterpret_cast<float4 *>(xsm)[i] = __ldcg(reinterpret_cast<const float4 *>(a.x) + i);
+    } else {
+#pragma unroll 4
+        for (uint32_t i = tid; i < a.d; i += kDecThreads) xsm[i] = __ldcg(a.x + i);
+    }
+    __syncthreads();
+    for (uint32_t r = tid; r < nr; r += kDecThreads) s_xres[r] = xsm[r0 + r];
+    if (a.norm_w) {  // rmsnorm(out, x, w, eps) with the router kernel's reduction order
+        float ss = 0.0f;
+        if (tid < kDecNormThreads)
+            for (uint32_t i = tid; i < a.d; i += kDecNormThreads) ss += xsm[i] * xsm[i];
+        ss = warp_sum(ss);
+        if (lane == 0 && warp < kDecNormThreads / 32) s_ss[warp] = ss;
+        __syncthreads();
+        if (tid == 0) {
+            float s = 0.0f;
+            for (int w = 0; w < kDecNormThreads / 32; w++) s += s_ss[w];
+            s_stat[0] = 1.0f / sqrtf(s / (float)a.d + a.eps);
+        }
+        __syncthreads();
+        const float rms = s_stat[0];
+        for (uint32_t i = tid; i < a.d; i += kDecThreads) xsm[i] = xsm[i] * rms * nwsm[i];
+    }
+    if (tid == 0) *s_epoch = epoch;  // the atomic has long returned by now
+    __syncthreads();
+    epoch = *s_epoch;
+    const uint32_t tag = (uint32_t)epoch;
+    // warps [0, nlw) compute this CTA's logits; the others quantise the
+    // normalised x for this CTA's gate/up meanwhile
+    const uint32_t nlw = a.E > c ? (a.E - c + G - 1) / G : 0;
+    if (has_e) {
+        const float v = router_logit(a.rw + (size_t)e_mine * a.rw_ld, xsm, a.d, lane, w0);
+        if (lane == 0) st_relaxed_u64(lslots + e_mine, ((uint64_t)tag << 32) | __float_as_uint(v));
+    } else {
+        for (uint32_t b = warp - nlw; b < a.d / 32; b += kDecWarps - nlw)
+            qact_block_to_xs(Xx, 0, (int)b, xsm[32 * b + lane], lane);
+    }
+    if (tid < a.E) {  // poll this expert's logit until it carries this launch's tag
+        uint64_t v = ld_relaxed_u64(lslots + tid);
+        if ((uint32_t)(v >> 32) != tag) {
+            const uint64_t t0 = globaltimer_ns();
+            for (;;) {
+                v = ld_relaxed_u64(lslots + tid);
+                if ((uint32_t)(v >> 32) == tag) break;
+                if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                    if (a.dev_err) atomicExch(a.dev_err, DEV_ERR_GRID_TIMEOUT);
+                    break;
+                }
+            }
+        }
+        const float lv = __uint_as_float((uint32_t)v);
+        s_lg[tid] = lv;
+        s_key[tid] = router_key(lv, tid);
+    }
+    if (tid == 0) s_key[a.E] = 0;
+    __syncthreads();
+    if (warp == kDecWarps - 1) {  // softmax statistics while the other warps rank
+        float mx, es;
+        router_softmax_stats(s_lg, a.E, lane, mx, es);
+        if (lane == 0) {
+            s_stat[1] = mx;
+            s_stat[2] = es;
+        }
+    }
+    router_rank_keys_split(s_key, a.E, a.k, s_sel, min(4u, (uint32_t)(kDecThreads - 32) / a.E), s_cnt, tid);
+    __syncthreads();
+
+    // ── phase G ──────────────────────────────────────────────────────────────
+    if (warp == 0) {  // one TMA chunk per lane: [n gate rows][n up rows]
+        for (uint32_t j = lane; j < nchunks; j += 32) {
+            const uint32_t q0 = p0 + j * kDecChunk;
+            const uint32_t s = q0 / a.F, f0 = q0 - s * a.F;
+            const uint32_t e = min(s_sel[s], a.E - 1);
+            const uint32_t bytes = (uint32_t)(kDecChunk * a.gpitch);
+            uint64_t grow, urow;
+            const uint8_t *ub;
+            if (a.up) {
+                grow = (uint64_t)e * a.F + f0;
+                urow = grow;
+                ub = a.up;
+            } else {  // fused: gate rows [0,F), up rows [F,2F) (gemma4/forward.zig:469-471)
+                grow = (uint64_t)e * 2 * a.F + f0;
+                urow = grow + a.F;
+                ub = a.gate;
+            }
+            uint8_t *dst = gt + (size_t)2 * j * kDecChunk * a.gpitch;
+            mbar_arrive_expect_tx(&bars[j], 2 * bytes);
+            tma_load_1d(dst, a.gate + grow * a.gpitch, bytes, &bars[j]);
+            tma_load_1d(dst + bytes, ub + urow * a.gpitch, bytes, &bars[j]);
+        }
+    } else if (warp == 1) {  // down rows [r0, r1) of each slot's expert
+        if ((uint32_t)lane < a.k && nr) {
+            const uint32_t e = min(s_sel[lane], a.E - 1);
+            const uint32_t bytes = (uint32_t)(nr * a.dpitch);
+            mbar_arrive_expect_tx(&bars[kDecMaxChunks + lane], bytes);
+            tma_load_1d(dt + (size_t)lane * a.maxrows * a.dpitch, a.down + ((uint64_t)e * a.d + r0) * a.dpitch, bytes,
+                        &bars[kDecMaxChunks + lane]);
+        }
+    } else if (warp == 2 && lane == 0) {
+        router_weights(s_lg, s_sel, a.k, s_stat[1], s_stat[2], a.norm_topk, a.escale, s_w);
+        if (c == 0)
+            for (uint32_t i = 0; i < a.k; i++) {
+                a.ids[i] = s_sel[i];
+                a.wout[i] = s_w[i];
+            }
+    }
+    // gate/up items in pair order: item w -> local pair w / (2 gi), gate or up, item
+    {
+        const uint32_t per_pair = 2 * a.gi, nwork = np * per_pair;
+        int waited = -1;
+        bool ok = true;
+        for (uint32_t w = tid; w < nwork; w += kDecThreads) {
+            const uint32_t lp = w / per_pair, rem = w - lp * per_pair;
+            const uint32_t gu = rem / a.gi, item = rem - gu * a.gi;
+            const uint32_t ch = lp / kDecChunk;
+            if ((int)ch != waited) {
+                ok = tile_wait(&bars[ch], a.dev_err);
+                waited = (int)ch;
+            }
+            const uint32_t row = 2 * ch * kDecChunk + gu * kDecChunk + (lp - ch * kDecChunk);
+            float res[1] = {0.0f};
+            if (ok) dot_item<GT, 1>(gt + (size_t)row * a.gpitch, (int)item, (int)a.gnb, Xx, 0, 1, res);
+            part[w] = res[0];
+        }
+    }
+    __syncthreads();
+    for (uint32_t lp = tid; lp < np; lp += kDecThreads) {
+        const float *pg = part + (size_t)lp * 2 * a.gi, *pu = pg + a.gi;
+        float g = 0.0f, u = 0.0f;
+        for (uint32_t i = 0; i < a.gi; i++) {
+            g += pg[i];
+            u += pu[i];
+        }
+        s_h[lp] = act_apply(a.act, g) * u;
+    }
+    __syncthreads();
+    // quantise this CTA's h values into their slots' images (32-blocks; a
+    // block may be half this CTA's)
+    for (uint32_t b = p0 / 32 + warp; b * 32 < p1; b += kDecWarps) {
+        const uint32_t q = 32 * b + lane;
+        const bool own = q >= p0 && q < p1;
+        const uint32_t s = (32 * b) / a.F, bs = (32 * b - s * a.F) / 32;  // F % 32 == 0: blocks stay in a slot
+        const XS Xs = xs_carve(a.himg + (size_t)s * a.img, 1, (int)a.di);
+        qact_block_to_xs(Xs, 0, (int)bs, own ? s_h[q - p0] : 0.0f, lane, own);
+    }
+    fence_proxy_async_global();  // the images are read by TMA after the barrier
+    // the slot images land (by TMA) where x and the norm weights were
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    grid_arrive(ctr_b);
+    grid_wait(ctr_b, epoch, a.dev_err, kWaitLimitNs);
+
+    // ── phase D ──────────────────────────────────────────────────────────────
+    uint8_t *himg_s = smem + L.rr;  // k slot images, a.img bytes each
+    if (tid == 0) {
+        fence_proxy_async_global();
+        mbar_arrive_expect_tx(hbar, a.k * a.img);
+        for (uint32_t s = 0; s < a.k; s++)
+            tma_load_1d(himg_s + (size_t)s * a.img, a.himg + (size_t)s * a.img, a.img, hbar);
+    }
+    const bool hok = tile_wait(hbar, a.dev_err);
+    {
+        const uint32_t per_slot = nr * a.di, nwork = a.k * per_slot;
+        int waited = -1;
+        bool ok = true;
+        for (uint32_t w = tid; w < nwork; w += kDecThreads) {
+            const uint32_t s = w / per_slot, rem = w - s * per_slot;
+            const uint32_t row = rem / a.di, item = rem - row * a.di;
+            if ((int)s != waited) {
+                ok = tile_wait(&bars[kDecMaxChunks + s], a.dev_err) && hok;
+                waited = (int)s;
+            }
+            float res[1] = {0.0f};
+            if (ok) {
+                const XS Xh = xs_carve(himg_s + (size_t)s * a.img, 1, (int)a.di);
+                dot_item<DT, 1>(dt + ((size_t)s * a.maxrows + row) * a.dpitch, (int)item, (int)a.dnb, Xh, 0, 1, res);
+            }
+            part[(s * a.maxrows + row) * a.di + item] = res[0];
+        }
+    }
+    __syncthreads();
+    for (uint32_t w = tid; w < a.k * nr; w += kDecThreads) {  // y[s][r], items in order
+        const uint32_t s = w / nr, r = w - s * nr;
+        const float *pp = part + (s * a.maxrows + r) * a.di;
+        float y = 0.0f;
+        for (uint32_t i = 0; i < a.di; i++) y += pp[i];
+        s_y[s * a.maxrows + r] = y;
+    }
+    __syncthreads();
+    for (uint32_t r = tid; r < nr; r += kDecThreads) {
+        float o = 0.0f;  // moe_buf is zeroed, then += scale * down, slot by slot
+        for (uint32_t s = 0; s < a.k; s++) o += s_w[s] * s_y[s * a.maxrows + r];
+        a.out[r0 + r] = a.residual ? s_xres[r] + o : o;
+    }
+}
+
+namespace {
+
+struct DecodePlan {
+    DecodeArgs a;
+    size_t smem;
+};
+
+bool decode_plan(const DecodeParams &p, int num_sms, DecodePlan &out) {
+    if (num_sms <= 0 || p.k == 0 || p.k > 16 || p.E == 0 || p.E > (uint32_t)kRouterMaxE) return false;
+    const uint32_t G = (uint32_t)num_sms;
+    DecodeArgs &a = out.a;
+    a.rw = p.router;
+    a.E = p.E;
+    a.d = p.d;
+    a.rw_ld = p.router_ld;
+    a.x = p.x;
+    a.norm_w = p.norm_w;
+    a.eps = p.eps;
+    a.k = p.k;
+    a.norm_topk = p.norm_topk;
+    a.escale = p.escale;
+    a.ids = p.ids;
+    a.wout = p.w;
+    a.gate = p.gate.data;
+    a.up = p.up_data;
+    a.gpitch = p.gate.pitch;
+    a.F = p.F;
+    a.gi = items_per_row(p.gate.type, p.gate.cols);
+    a.gnb = (uint32_t)(p.gate.cols / 32);
+    a.act = p.act;
+    a.down = p.down.data;
+    a.dpitch = p.down.pitch;
+    a.di = items_per_row(p.down.type, p.down.cols);
+    a.dnb = (uint32_t)(p.down.cols / 32);
+    a.himg = p.himg;
+    a.img = (uint32_t)moe_decode_img_bytes(p.F);
+    a.residual = p.residual;
+    a.out = p.out;
+    a.sync = p.sync;
+    a.dev_err = nullptr;
+    if (p.d % 32 != 0 || p.F % 32 != 0) return false;
+    const uint64_t nunits = (uint64_t)p.k * p.F / kDecUnit;
+    a.maxpairs = (uint32_t)(kDecUnit * ((nunits + G - 1) / G));
+    a.maxrows = (p.d + G - 1) / G;
+    if (a.maxpairs / kDecChunk > (uint32_t)kDecMaxChunks) return false;
+    const DecodeLayout L =
+        decode_layout(a.E, a.d, a.k, a.gpitch, a.gi, a.dpitch, a.di, a.img, a.maxpairs, a.maxrows);
+    out.smem = L.total;
+    return L.total <= kDecodeSmemLimit;
+}
+
+template <uint32_t GT, uint32_t DT>
+cudaError_t launch_decode_t(const LaunchCfg &c, const DecodePlan &pl) {
+    return launch_k(c, "moe_decode", k_moe_decode<GT, DT>, dim3((unsigned)c.num_sms), dim3(kDecThreads), pl.smem, pl.a);
+}
+
+template <uint32_t GT>
+cudaError_t launch_decode_g(const LaunchCfg &c, const DecodePlan &pl, uint32_t dtype) {
+    switch (dtype) {
+    case T_Q4_K: return launch_decode_t<GT, T_Q4_K>(c, pl);
+    case T_Q6_K: return launch_decode_t<GT, T_Q6_K>(c, pl);
+    case T_Q8_0: return launch_decode_t<GT, T_Q8_0>(c, pl);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
+size_t moe_decode_img_bytes(uint64_t F) { return xs_bytes(1, (int)((F + 255) / 256)); }
+
+bool moe_decode_fits(const DecodeParams &p, int num_sms) {
+    DecodePlan pl;
+    return decode_plan(p, num_sms, pl);
+}
+
+cudaError_t launch_moe_decode(const LaunchCfg &c, const DecodeParams &p) {
+    DecodePlan pl;
+    if (!decode_plan(p, c.num_sms, pl)) return cudaErrorInvalidValue;
+    pl.a.dev_err = c.dev_err;
+    switch (p.gate.type) {
+    case T_Q4_K: return launch_decode_g<T_Q4_K>(c, pl, p.down.type);
+    case T_Q6_K: return launch_decode_g<T_Q6_K>(c, pl, p.down.type);
+    case T_Q8_0: return launch_decode_g<T_Q8_0>(c, pl, p.down.type);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace lt

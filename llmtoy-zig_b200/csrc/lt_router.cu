@@ -2,55 +2,18 @@
 // 648-668) with the pre-FFN RMSNorm (src/ops/math.zig:20-26) and the
 // activation quantisation for the expert kernels fused in.
 //
-// Each warp computes one expert's logit with dotf32's exact evaluation order
-// (src/ops/math.zig:96-116): lane l owns the chain over elements l, l+32, ...
-// (acc_{l/8}[l%8] in the reference), then (a0+a1)+(a2+a3), the 8-wide tail,
-// the ordered 8-lane reduction and the scalar tail.  Given the same input
-// vector the logits, and so the selected ids, equal the CPU path bit for bit.
-// The last CTA of each token group selects the top-k (strict '>', lowest
-// index on ties, forward.zig:598-629) and the softmax weights.
+// Each warp computes one expert's logit (router_logit, lt_router.cuh: dotf32's
+// exact order).  The last CTA of each token group selects the top-k and the
+// softmax weights (lt_router.cuh).
 #include "lt_qact.cuh"
+#include "lt_router.cuh"
 
 namespace lt {
 
 constexpr int kRouterWarps = 4;  // experts per CTA
 constexpr int kRouterTok = 4;    // tokens per CTA (one warp each for norm and top-k)
-constexpr int kRouterChunk = 64;  // weights per lane kept in registers (2048 columns)
 
 uint32_t router_token_groups(uint32_t ntok) { return (ntok + kRouterTok - 1) / kRouterTok; }
-
-// One expert logit in dotf32 order.  w0 holds this lane's weights for the
-// first 2048 columns (prefetched); xs is the token row in shared memory.
-LT_DEVINL float router_logit(const float *wrow, const float *xs, uint32_t cols, int lane,
-                             const float (&w0)[kRouterChunk]) {
-    const uint32_t n32 = cols & ~31u;
-    float acc = 0.0f;
-#pragma unroll
-    for (int j = 0; j < kRouterChunk; j++)
-        if (32u * j < n32) acc = __fadd_rn(acc, __fmul_rn(w0[j], xs[32 * j + lane]));
-    for (uint32_t base = 32u * kRouterChunk; base < n32; base += 32u * kRouterChunk) {
-        float wv[kRouterChunk];
-#pragma unroll
-        for (int j = 0; j < kRouterChunk; j++) wv[j] = base + 32u * j < n32 ? __ldg(wrow + base + 32 * j + lane) : 0.f;
-#pragma unroll
-        for (int j = 0; j < kRouterChunk; j++)
-            if (base + 32u * j < n32) acc = __fadd_rn(acc, __fmul_rn(wv[j], xs[base + 32 * j + lane]));
-    }
-    uint32_t i = n32;
-    // acc = (acc0 + acc1) + (acc2 + acc3), lane l < 8 holds lane l of the 8-vector
-    const float a1 = __shfl_sync(0xffffffffu, acc, (lane + 8) & 31);
-    const float a2 = __shfl_sync(0xffffffffu, acc, (lane + 16) & 31);
-    const float a3 = __shfl_sync(0xffffffffu, acc, (lane + 24) & 31);
-    float v = __fadd_rn(__fadd_rn(acc, a1), __fadd_rn(a2, a3));
-    for (; i + 8 <= cols; i += 8)
-        if (lane < 8) v = __fadd_rn(v, __fmul_rn(__ldg(wrow + i + lane), xs[i + lane]));
-    // @reduce(.Add): ((((-0 + v0) + v1) + ...) + v7)
-    float sum = -0.0f;
-#pragma unroll
-    for (int l = 0; l < 8; l++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, v, l));
-    for (; i < cols; i++) sum = __fadd_rn(sum, __fmul_rn(__ldg(wrow + i), xs[i]));
-    return sum;
-}
 
 struct RouterArgs {
     const float *W;  // [E][w_ld]
@@ -74,6 +37,8 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(RouterArgs a) {
     __shared__ int s_last;
     __shared__ float s_ss[kRouterWarps][kRouterTok];
     __shared__ float s_rms[kRouterTok];
+    __shared__ uint32_t s_sel[kRouterTok][16];
+    __shared__ float s_mx[kRouterTok], s_es[kRouterTok];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t e = blockIdx.x * kRouterWarps + warp;
     const uint32_t t0 = blockIdx.y * kRouterTok;
@@ -154,62 +119,36 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(RouterArgs a) {
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // top-k + softmax statistics, one warp per token
-    for (uint32_t tt = warp; tt < nt; tt += kRouterWarps) {
-        const float *lg = a.logits + (size_t)(t0 + tt) * a.E;
-        float v[kRouterMaxE / 32];
-        float mx = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < kRouterMaxE / 32; j++) {
-            const uint32_t ee = lane + 32 * j;
-            v[j] = ee < a.E ? __ldcg(lg + ee) : -INFINITY;
-            mx = fmaxf(mx, v[j]);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float es = 0.0f;
-#pragma unroll
-        for (int j = 0; j < kRouterMaxE / 32; j++)
-            if (lane + 32 * j < a.E) es += expf(v[j] - mx);
-        es = warp_sum(es);
-        uint32_t taken = 0;  // bit j: element lane+32j selected
-        float psel[16];
-        uint32_t isel[16];
-        for (uint32_t i = 0; i < a.k; i++) {
-            // best untaken: larger value, ties -> lower index
-            float bv = -INFINITY;
-            uint32_t bi = 0xffffffffu;
-#pragma unroll
-            for (int j = 0; j < kRouterMaxE / 32; j++) {
-                const uint32_t ee = lane + 32 * j;
-                if (ee < a.E && !((taken >> j) & 1u) && (v[j] > bv || bi == 0xffffffffu)) {
-                    bv = v[j];
-                    bi = ee;
-                }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (oi != 0xffffffffu && (bi == 0xffffffffu || ov > bv || (ov == bv && oi < bi))) {
-                    bv = ov;
-                    bi = oi;
-                }
-            }
-            if (bi != 0xffffffffu && (bi & 31u) == (uint32_t)lane) taken |= 1u << (bi >> 5);
-            isel[i] = bi;
-            psel[i] = expf(bv - mx) / es;
-        }
+    // top-k + softmax weights per token (lt_router.cuh); x is no longer needed,
+    // its shared memory holds the logits and sort keys
+    float(*s_lg)[kRouterMaxE] = reinterpret_cast<float(*)[kRouterMaxE]>(xsm);
+    uint64_t(*s_key)[kRouterMaxE + 2] =
+        reinterpret_cast<uint64_t(*)[kRouterMaxE + 2]>(xsm + kRouterTok * kRouterMaxE);
+    for (uint32_t i = threadIdx.x; i < nt * a.E; i += blockDim.x) {
+        const uint32_t tt = i / a.E, ee = i - tt * a.E;
+        const float v = __ldcg(a.logits + (size_t)(t0 + tt) * a.E + ee);
+        s_lg[tt][ee] = v;
+        s_key[tt][ee] = router_key(v, ee);
+    }
+    if (threadIdx.x < nt) s_key[threadIdx.x][a.E] = 0;
+    __syncthreads();
+    for (uint32_t tt = 0; tt < nt; tt++) router_rank_keys(s_key[tt], a.E, a.k, s_sel[tt], threadIdx.x, blockDim.x);
+    if (warp < (int)nt) {
+        float mx, es;
+        router_softmax_stats(s_lg[warp], a.E, lane, mx, es);
         if (lane == 0) {
-            float sum = 0.0f;
-            if (a.norm_topk)
-                for (uint32_t i = 0; i < a.k; i++) sum += psel[i];
-            for (uint32_t i = 0; i < a.k; i++) {
-                float w = a.norm_topk ? psel[i] / sum : psel[i];
-                if (a.escale) w = a.escale[isel[i]] * w;
-                a.ids[(size_t)(t0 + tt) * a.k + i] = isel[i];
-                a.wout[(size_t)(t0 + tt) * a.k + i] = w;
-            }
+            s_mx[warp] = mx;
+            s_es[warp] = es;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < nt) {
+        const uint32_t tt = threadIdx.x;
+        float w[16];
+        router_weights(s_lg[tt], s_sel[tt], a.k, s_mx[tt], s_es[tt], a.norm_topk, a.escale, w);
+        for (uint32_t i = 0; i < a.k; i++) {
+            a.ids[(size_t)(t0 + tt) * a.k + i] = s_sel[tt][i];
+            a.wout[(size_t)(t0 + tt) * a.k + i] = w[i];
         }
     }
     if (threadIdx.x == 0) a.counters[blockIdx.y] = 0;
@@ -221,7 +160,9 @@ cudaError_t launch_router(const LaunchCfg &c, const float *w, uint32_t E, uint32
                           uint8_t *xq, uint64_t xq_pitch) {
     RouterArgs a{w, E, cols, w_ld, x, norm_w, eps, ntok, k, norm_topk, escale, ids, wout, logits, counters, xq, xq_pitch};
     const dim3 grid((E + kRouterWarps - 1) / kRouterWarps, router_token_groups(ntok));
-    const size_t smem = (size_t)(kRouterTok + (norm_w ? 1 : 0)) * cols * 4;
+    const size_t smem_x = (size_t)(kRouterTok + (norm_w ? 1 : 0)) * cols * 4;
+    const size_t smem_topk = (size_t)kRouterTok * (kRouterMaxE * 4 + (kRouterMaxE + 2) * 8);
+    const size_t smem = smem_x > smem_topk ? smem_x : smem_topk;
     return launch_k(c, "router_topk", k_router, grid, dim3(kRouterWarps * 32), smem, a);
 }
 
