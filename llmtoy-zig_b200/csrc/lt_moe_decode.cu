@@ -30,6 +30,7 @@
 // router / gate_up / down kernels, so both paths give the same bits.
 #include "lt_qact.cuh"
 #include "lt_router.cuh"
+#include "lt_rowdot.cuh"
 
 namespace lt {
 
@@ -78,7 +79,9 @@ struct DecodeLayout {
     size_t bars, misc, lg, keys, cnt, part, ys, hs, xres, xsx, rr, gt, dt, total;
 };
 
-__host__ __device__ inline DecodeLayout decode_layout(uint32_t E, uint32_t d, uint32_t k, uint64_t gpitch,
+__host__ __device__ inline uint32_t chunks64(uint32_t cols) { return (cols + 63) / 64; }
+
+__host__ __device__ inline DecodeLayout decode_layout(uint32_t E, uint32_t d, uint32_t F, uint32_t k, uint64_t gpitch,
                                                       uint32_t gi, uint64_t dpitch, uint32_t di, uint32_t img,
                                                       uint32_t maxpairs, uint32_t maxrows) {
     DecodeLayout L;
@@ -93,7 +96,7 @@ __host__ __device__ inline DecodeLayout decode_layout(uint32_t E, uint32_t d, ui
     L.lg = take((size_t)E * 4);
     L.keys = take((size_t)(E + 2) * 8);
     L.cnt = take((size_t)4 * E * 4);
-    const size_t pg = (size_t)maxpairs * 2 * gi, pd = (size_t)k * maxrows * di;
+    const size_t pg = (size_t)(2 * maxpairs + 1) * chunks64(d), pd = (size_t)(k * maxrows + 1) * chunks64(F);
     L.part = take((pg > pd ? pg : pd) * 4);
     L.ys = take((size_t)k * maxrows * 4);
     L.hs = take((size_t)maxpairs * 4);
@@ -103,6 +106,7 @@ __host__ __device__ inline DecodeLayout decode_layout(uint32_t E, uint32_t d, ui
     L.rr = take(rr0 > rr1 ? rr0 : rr1);
     L.gt = take((size_t)maxpairs * 2 * gpitch);
     L.dt = take((size_t)k * maxrows * dpitch);
+    take(128);  // the last Q8_0 chunk of a row reads up to 34 bytes past it
     L.total = off;
     return L;
 }
@@ -113,7 +117,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t G = gridDim.x, c = blockIdx.x;
     const DecodeLayout L =
-        decode_layout(a.E, a.d, a.k, a.gpitch, a.gi, a.dpitch, a.di, a.img, a.maxpairs, a.maxrows);
+        decode_layout(a.E, a.d, a.F, a.k, a.gpitch, a.gi, a.dpitch, a.di, a.img, a.maxpairs, a.maxrows);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
     uint64_t *hbar = bars + kDecMaxChunks + 16;
     uint32_t *s_sel = reinterpret_cast<uint32_t *>(smem + L.misc);    // [16]
@@ -275,32 +279,43 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
                 a.wout[i] = s_w[i];
             }
     }
-    // gate/up items in pair order: item w -> local pair w / (2 gi), gate or up, item
+    // gate/up: warp w takes tile rows w*rps.., one TMA chunk (16 tile rows)
+    // after another; a lane owns one 64-column chunk of x in registers
+    const uint32_t cpr_g = chunks64(a.d);
+    const uint32_t gstride = 2 * a.maxpairs + 1;  // partials [chunk][tile row], odd stride: no bank conflicts
     {
-        const uint32_t per_pair = 2 * a.gi, nwork = np * per_pair;
-        int waited = -1;
-        bool ok = true;
-        for (uint32_t w = tid; w < nwork; w += kDecThreads) {
-            const uint32_t lp = w / per_pair, rem = w - lp * per_pair;
-            const uint32_t gu = rem / a.gi, item = rem - gu * a.gi;
-            const uint32_t ch = lp / kDecChunk;
-            if ((int)ch != waited) {
-                ok = tile_wait(&bars[ch], a.dev_err);
-                waited = (int)ch;
+        const uint32_t lpr = min(cpr_g, 32u), rps = 32 / lpr;  // lanes per row, rows per step
+        const uint32_t sub = lane / lpr, cb0 = lane % lpr, nrows = 2 * np;
+        if (sub < rps) {
+            for (uint32_t cb = cb0; cb < cpr_g; cb += lpr) {
+                XChunk xc;
+                xchunk_load(Xx, 0, (int)cb, xc);
+                // two rows per iteration (independent chains for the scheduler);
+                // an odd last row is computed twice and stored once
+                const uint32_t step = kDecWarps * rps;
+                for (uint32_t r = warp * rps + sub; r < nrows; r += 2 * step) {
+                    const uint32_t rb = r + step < nrows ? r + step : r;
+                    const bool ok = tile_wait(&bars[r / (2 * kDecChunk)], a.dev_err) &
+                                    tile_wait(&bars[rb / (2 * kDecChunk)], a.dev_err);
+                    float ya = 0.0f, yb = 0.0f;
+                    if (ok) {
+                        ya = dot64<GT>(gt + (size_t)r * a.gpitch, (int)cb, (int)a.gnb, xc);
+                        yb = dot64<GT>(gt + (size_t)rb * a.gpitch, (int)cb, (int)a.gnb, xc);
+                    }
+                    part[cb * gstride + r] = ya;
+                    part[cb * gstride + rb] = yb;
+                }
             }
-            const uint32_t row = 2 * ch * kDecChunk + gu * kDecChunk + (lp - ch * kDecChunk);
-            float res[1] = {0.0f};
-            if (ok) dot_item<GT, 1>(gt + (size_t)row * a.gpitch, (int)item, (int)a.gnb, Xx, 0, 1, res);
-            part[w] = res[0];
         }
     }
     __syncthreads();
-    for (uint32_t lp = tid; lp < np; lp += kDecThreads) {
-        const float *pg = part + (size_t)lp * 2 * a.gi, *pu = pg + a.gi;
+    for (uint32_t lp = tid; lp < np; lp += kDecThreads) {  // chunk partials summed in column order
+        const uint32_t rg = 2 * kDecChunk * (lp / kDecChunk) + lp % kDecChunk;
+        const float *pg = part + rg, *pu = pg + kDecChunk;
         float g = 0.0f, u = 0.0f;
-        for (uint32_t i = 0; i < a.gi; i++) {
-            g += pg[i];
-            u += pu[i];
+        for (uint32_t i = 0; i < cpr_g; i++) {
+            g += pg[i * gstride];
+            u += pu[i * gstride];
         }
         s_h[lp] = act_apply(a.act, g) * u;
     }
@@ -329,31 +344,42 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
             tma_load_1d(himg_s + (size_t)s * a.img, a.himg + (size_t)s * a.img, a.img, hbar);
     }
     const bool hok = tile_wait(hbar, a.dev_err);
+    // down: warps [s*wps, (s+1)*wps) take slot s; a lane owns one 64-column
+    // chunk of that slot's h in registers
+    const uint32_t cpr_d = chunks64(a.F);
+    const uint32_t dstride = a.k * a.maxrows + 1;  // partials [chunk][slot row]
     {
-        const uint32_t per_slot = nr * a.di, nwork = a.k * per_slot;
-        int waited = -1;
-        bool ok = true;
-        for (uint32_t w = tid; w < nwork; w += kDecThreads) {
-            const uint32_t s = w / per_slot, rem = w - s * per_slot;
-            const uint32_t row = rem / a.di, item = rem - row * a.di;
-            if ((int)s != waited) {
-                ok = tile_wait(&bars[kDecMaxChunks + s], a.dev_err) && hok;
-                waited = (int)s;
+        const uint32_t lpr = min(cpr_d, 32u), rps = 32 / lpr;
+        const uint32_t sub = lane / lpr, cb0 = lane % lpr;
+        const uint32_t wps = max(1u, (uint32_t)kDecWarps / a.k);
+        const uint32_t s = warp / wps, ws = warp % wps;
+        if (s < a.k && sub < rps && nr) {
+            const bool ok = tile_wait(&bars[kDecMaxChunks + s], a.dev_err) && hok;
+            const XS Xh = xs_carve(himg_s + (size_t)s * a.img, 1, (int)a.di);
+            for (uint32_t cb = cb0; cb < cpr_d; cb += lpr) {
+                XChunk xc;
+                xchunk_load(Xh, 0, (int)cb, xc);
+                const uint32_t step = wps * rps;
+                for (uint32_t r = ws * rps + sub; r < nr; r += 2 * step) {
+                    const uint32_t rb = r + step < nr ? r + step : r;
+                    const uint32_t ta = s * a.maxrows + r, tb = s * a.maxrows + rb;
+                    float ya = 0.0f, yb = 0.0f;
+                    if (ok) {
+                        ya = dot64<DT>(dt + (size_t)ta * a.dpitch, (int)cb, (int)a.dnb, xc);
+                        yb = dot64<DT>(dt + (size_t)tb * a.dpitch, (int)cb, (int)a.dnb, xc);
+                    }
+                    part[cb * dstride + ta] = ya;
+                    part[cb * dstride + tb] = yb;
+                }
             }
-            float res[1] = {0.0f};
-            if (ok) {
-                const XS Xh = xs_carve(himg_s + (size_t)s * a.img, 1, (int)a.di);
-                dot_item<DT, 1>(dt + ((size_t)s * a.maxrows + row) * a.dpitch, (int)item, (int)a.dnb, Xh, 0, 1, res);
-            }
-            part[(s * a.maxrows + row) * a.di + item] = res[0];
         }
     }
     __syncthreads();
-    for (uint32_t w = tid; w < a.k * nr; w += kDecThreads) {  // y[s][r], items in order
+    for (uint32_t w = tid; w < a.k * nr; w += kDecThreads) {  // y[s][r]: chunk partials in column order
         const uint32_t s = w / nr, r = w - s * nr;
-        const float *pp = part + (s * a.maxrows + r) * a.di;
+        const float *pp = part + s * a.maxrows + r;
         float y = 0.0f;
-        for (uint32_t i = 0; i < a.di; i++) y += pp[i];
+        for (uint32_t i = 0; i < cpr_d; i++) y += pp[i * dstride];
         s_y[s * a.maxrows + r] = y;
     }
     __syncthreads();
@@ -410,7 +436,7 @@ bool decode_plan(const DecodeParams &p, int num_sms, DecodePlan &out) {
     a.maxrows = (p.d + G - 1) / G;
     if (a.maxpairs / kDecChunk > (uint32_t)kDecMaxChunks) return false;
     const DecodeLayout L =
-        decode_layout(a.E, a.d, a.k, a.gpitch, a.gi, a.dpitch, a.di, a.img, a.maxpairs, a.maxrows);
+        decode_layout(a.E, a.d, a.F, a.k, a.gpitch, a.gi, a.dpitch, a.di, a.img, a.maxpairs, a.maxrows);
     out.smem = L.total;
     return L.total <= kDecodeSmemLimit;
 }

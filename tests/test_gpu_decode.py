@@ -2,10 +2,12 @@
 multi-kernel path (router -> gate/up -> down) and against the CPU oracle.
 
 A one-token lt_moe_forward / lt_moe_block runs as one persistent kernel when
-its per-CTA share fits in shared memory.  It uses the same router arithmetic,
-block decoders and summation orders as the multi-kernel path, so the two must
-agree bit for bit (outputs, ids and weights); the oracle checks them both.
-A context created with LLMTOY_DECODE_KERNEL=0 runs the multi-kernel path.
+its per-CTA share fits in shared memory.  Its router arithmetic is the router
+kernel's, so expert ids and weights agree with the multi-kernel path bit for
+bit; the expert dot products are summed in a different order (64-column
+chunks instead of superblocks), so outputs agree to DECODE_VS_MULTI_L2.  The
+oracle checks both.  A context created with LLMTOY_DECODE_KERNEL=0 runs the
+multi-kernel path.
 """
 from __future__ import annotations
 
@@ -18,6 +20,8 @@ import pytest
 from test_gpu_parity import MOE_L2_TOL, _upload_layer, bits, dev, empty, host, rel_l2
 
 pytestmark = pytest.mark.gpu
+
+DECODE_VS_MULTI_L2 = 2e-5  # two quantised-activation evaluations of the same layer
 
 
 @pytest.fixture(scope="module")
@@ -82,7 +86,7 @@ def _run(ctx, L, case, x, nw, escale, block):
     else:
         out = empty(d)
         ctx.moe_forward(rt, g, u, dn, act, norm, es, xd, 1, k, out, ids, ww)
-    res = host(out), host(ids).view(np.uint32), host(ww)
+    res = host(out) - (x if block else 0), host(ids).view(np.uint32), host(ww)
     for t_ in (rt, g, u, dn):
         if t_ is not None:
             t_.free()
@@ -97,7 +101,7 @@ def test_decode_kernel_matches_multi_kernel_path(ctx, multi_ctx, case, block):
     o2, i2, w2 = _run(multi_ctx, L, case, x, nw, escale, block)
     assert np.array_equal(i1, i2)
     assert np.array_equal(bits(w1), bits(w2))
-    assert np.array_equal(bits(o1), bits(o2))
+    assert rel_l2(o1, o2) < DECODE_VS_MULTI_L2
 
 
 @pytest.mark.parametrize("case", CASES[:3] + CASES[7:], ids=_case_id)
@@ -138,8 +142,8 @@ def config1_layer_decode():
 
 def test_decode_stack_graph_replay(ctx, multi_ctx, config1_layer_decode):
     """Six chained blocks applied in place (x <- x + moe(rmsnorm(x))), eagerly
-    and as a captured graph replayed twice: all runs agree bit for bit with
-    each other and with the multi-kernel path."""
+    and as a captured graph replayed twice: the runs agree bit for bit with
+    each other and closely with the multi-kernel path."""
     import torch
     L = config1_layer_decode
     rng = np.random.Generator(np.random.PCG64(66))
@@ -180,5 +184,8 @@ def test_decode_stack_graph_replay(ctx, multi_ctx, config1_layer_decode):
             if t_ is not None:
                 t_.free()
     assert len(results) == 4
-    assert all(np.array_equal(results[0], r) for r in results[1:])
+    # [0] eager, [1] [2] graph replays (decode kernel); [3] multi-kernel path
+    assert np.array_equal(results[0], results[1]) and np.array_equal(results[0], results[2])
+    f = [r.view(np.float32) - x0 for r in results]
+    assert rel_l2(f[0], f[3]) < 1e-4
     ctx.sync()  # raises if a device-side wait gave up
