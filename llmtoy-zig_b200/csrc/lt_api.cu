@@ -29,6 +29,7 @@ struct lt_ctx {
     int num_sms = 0;
     bool pdl = true;
     bool decode_kernel = true;       // single-token MoE blocks run as one persistent kernel
+    uint32_t tc_min_tokens = 64;     // batches of at least this many tokens use the tensor-core expert GEMM
     int *dev_err = nullptr;          // device error word written by kernels
     uint8_t *dec_sync = nullptr;     // counters and tagged logits of the persistent decode kernel
     uint8_t *scratch = nullptr;      // activation scratch arena
@@ -167,12 +168,15 @@ struct MoeScratch {
     uint64_t hq_pitch;
     float *hf;  // f32 h rows, staged before quantisation
     uint8_t *himg;  // single-token decode kernel: quantised h slot images
+    float *xn;      // f32 normalised expert input rows (tensor-core path)
+    uint8_t *gemm;  // tensor-core path scratch (lt_moe_gemm.cu)
     lt::MoePlan plan;
     size_t bytes;
     size_t counters;  // block counters needed past kMoeCounterBase
 };
 
-MoeScratch moe_layout(uint8_t *base, uint32_t T, uint32_t k, uint32_t E, uint64_t d, uint64_t F) {
+MoeScratch moe_layout(uint8_t *base, uint32_t T, uint32_t k, uint32_t E, uint64_t d, uint64_t F,
+                      size_t gemm_bytes = 0) {
     MoeScratch s;
     size_t off = 0;
     auto take = [&](size_t b) {
@@ -189,6 +193,8 @@ MoeScratch moe_layout(uint8_t *base, uint32_t T, uint32_t k, uint32_t E, uint64_
     s.hq = take(P * s.hq_pitch);
     s.hf = (float *)take(P * F * 4);
     s.himg = take(P * lt::moe_decode_img_bytes(F));
+    s.xn = gemm_bytes ? (float *)take((size_t)T * d * 4) : nullptr;
+    s.gemm = gemm_bytes ? take(gemm_bytes) : nullptr;
     s.counters = P * (F / 32);
     s.logits = (float *)take((size_t)T * E * 4);
     s.plan.n_active = (uint32_t *)take(4);
@@ -247,6 +253,8 @@ lt_status lt_init(int device, lt_ctx **out) {
     ctx->pdl = !(pdl && strcmp(pdl, "0") == 0);
     const char *dk = getenv("LLMTOY_DECODE_KERNEL");
     ctx->decode_kernel = !(dk && strcmp(dk, "0") == 0);
+    const char *tc = getenv("LLMTOY_TC_MIN_TOKENS");  // 0 turns the tensor-core expert GEMM off
+    if (tc) ctx->tc_min_tokens = (uint32_t)strtoul(tc, nullptr, 10);
     lt_status st = LT_OK;
     if (cudaSetDevice(device) != cudaSuccess ||
         cudaStreamCreateWithFlags(&ctx->own, cudaStreamNonBlocking) != cudaSuccess ||
@@ -389,7 +397,11 @@ lt_status lt_reserve(lt_ctx *ctx, uint32_t max_tokens, uint32_t max_k, uint64_t 
                      uint64_t max_d_expert) {
     lt_status st = enter_uncaptured(ctx, "lt_reserve");
     if (st != LT_OK) return st;
-    const size_t moe = moe_layout(nullptr, max_tokens, max_k, lt::kRouterMaxE, max_d_model, max_d_expert).bytes;
+    const size_t gemm = max_tokens > 1 ? lt::moe_gemm_scratch(max_tokens, max_k, lt::kRouterMaxE, max_d_model,
+                                                               max_d_expert)
+                                       : 0;
+    const size_t moe =
+        moe_layout(nullptr, max_tokens, max_k, lt::kRouterMaxE, max_d_model, max_d_expert, gemm).bytes;
     const size_t io = 2 * al256((size_t)max_tokens * max_d_model * 4) + 2 * al256((size_t)max_tokens * max_k * 4) +
                       al256((size_t)lt::kRouterMaxE * 4);
     const size_t qmv = al256((size_t)max_tokens * lt::qact_row_pitch(max_d_model > max_d_expert ? max_d_model
@@ -572,14 +584,14 @@ static lt_status check_router(lt_ctx *ctx, const lt_tensor *router, uint32_t k) 
 
 static lt_status route_impl(lt_ctx *ctx, const lt_tensor *router, const float *x, const float *norm_w, float eps,
                             uint32_t ntok, uint32_t k, int norm_topk, const float *escale, uint32_t *ids, float *w,
-                            float *logits, uint8_t *xq, uint64_t xq_pitch) {
+                            float *logits, uint8_t *xq, uint64_t xq_pitch, float *xn = nullptr) {
     const uint32_t groups = lt::router_token_groups(ntok);
     lt_status st = ensure_counters(ctx, groups);
     if (st != LT_OK) return st;
     return launched(ctx,
                     lt::launch_router(cfg_of(ctx), (const float *)router->m.data, (uint32_t)router->m.rows,
                                       (uint32_t)router->m.cols, (uint32_t)(router->m.pitch / 4), x, norm_w, eps, ntok,
-                                      k, norm_topk, escale, ids, w, logits, ctx->counters, xq, xq_pitch),
+                                      k, norm_topk, escale, ids, w, logits, ctx->counters, xq, xq_pitch, xn),
                     "router");
 }
 
@@ -618,14 +630,34 @@ static lt_status check_experts(lt_ctx *ctx, const lt_tensor *gate, const lt_tens
     return LT_OK;
 }
 
+// Scratch bytes of the tensor-core expert GEMM when a batch of ntok tokens
+// takes that path, else 0.
+static size_t gemm_bytes_of(const lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *down, uint32_t ntok, uint32_t k) {
+    const uint64_t F = down->m.cols;
+    if (ntok < 2 || ctx->tc_min_tokens == 0 || ntok < ctx->tc_min_tokens) return 0;
+    if (!lt::moe_gemm_supported(gate->m, down->m, F)) return 0;
+    return lt::moe_gemm_scratch(ntok, k, gate->m.n_experts, gate->m.cols, F);
+}
+
+// xf: f32 expert input rows (used by the tensor-core path; the CUDA-core
+// path reads the quantised rows s.xq).
 static lt_status ffn_impl(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, const lt_tensor *down, int act,
                           uint32_t ntok, const uint32_t *ids, const float *w, uint32_t k, const float *resid,
-                          float *out, const MoeScratch &s) {
+                          float *out, const float *xf, const MoeScratch &s) {
     const lt::LaunchCfg c = cfg_of(ctx);
     const bool direct = ntok == 1;
     lt::DevMat upm = up ? up->m : lt::DevMat{};
     if (!up) upm.data = nullptr;
-    lt_status st = ensure_counters(ctx, lt::kMoeCounterBase + s.counters);
+    lt_status st;
+    if (!direct && s.gemm) {
+        st = launched(ctx, lt::launch_moe_plan(c, ids, ntok, k, gate->m.n_experts, s.plan), "moe plan");
+        if (st != LT_OK) return st;
+        return launched(ctx,
+                        lt::launch_moe_gemm_ffn(c, gate->m, upm.data, down->m, act, xf, ntok, k, w, s.plan, resid,
+                                                out, s.gemm),
+                        "moe gemm");
+    }
+    st = ensure_counters(ctx, lt::kMoeCounterBase + s.counters);
     if (st != LT_OK) return st;
     if (!direct) {
         st = launched(ctx, lt::launch_moe_plan(c, ids, ntok, k, gate->m.n_experts, s.plan), "moe plan");
@@ -652,12 +684,15 @@ lt_status lt_moe_ffn(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, co
     if (!dev_x || !dev_ids || !dev_w || !dev_out) return fail(ctx, LT_EINVAL, "lt_moe_ffn: null pointer");
     if (ntok == 0) return LT_OK;
     const uint64_t d = gate->m.cols;
-    const MoeScratch probe = moe_layout(nullptr, ntok, k, gate->m.n_experts, d, F);
+    const size_t gb = gemm_bytes_of(ctx, gate, down, ntok, k);
+    const MoeScratch probe = moe_layout(nullptr, ntok, k, gate->m.n_experts, d, F, gb);
     if ((st = ensure_scratch(ctx, probe.bytes)) != LT_OK) return st;
-    const MoeScratch s = moe_layout(ctx->scratch, ntok, k, gate->m.n_experts, d, F);
-    st = launched(ctx, lt::launch_quantize(cfg_of(ctx), dev_x, (uint32_t)d, ntok, s.xq, s.xq_pitch), "quantize");
-    if (st != LT_OK) return st;
-    return ffn_impl(ctx, gate, up, down, act, ntok, dev_ids, dev_w, k, nullptr, dev_out, s);
+    const MoeScratch s = moe_layout(ctx->scratch, ntok, k, gate->m.n_experts, d, F, gb);
+    if (!s.gemm) {
+        st = launched(ctx, lt::launch_quantize(cfg_of(ctx), dev_x, (uint32_t)d, ntok, s.xq, s.xq_pitch), "quantize");
+        if (st != LT_OK) return st;
+    }
+    return ffn_impl(ctx, gate, up, down, act, ntok, dev_ids, dev_w, k, nullptr, dev_out, dev_x, s);
 }
 
 static lt_status forward_impl(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *gate, const lt_tensor *up,
@@ -677,9 +712,10 @@ static lt_status forward_impl(lt_ctx *ctx, const lt_tensor *router, const lt_ten
     if (ntok == 0) return LT_OK;
     const uint32_t E = gate->m.n_experts;
     const uint64_t d = gate->m.cols;
-    const MoeScratch probe = moe_layout(nullptr, ntok, k, E, d, F);
+    const size_t gb = gemm_bytes_of(ctx, gate, down, ntok, k);
+    const MoeScratch probe = moe_layout(nullptr, ntok, k, E, d, F, gb);
     if ((st = ensure_scratch(ctx, probe.bytes)) != LT_OK) return st;
-    const MoeScratch s = moe_layout(ctx->scratch, ntok, k, E, d, F);
+    const MoeScratch s = moe_layout(ctx->scratch, ntok, k, E, d, F, gb);
     uint32_t *ids = dev_ids ? dev_ids : s.ids;
     float *w = dev_w ? dev_w : s.w;
     if (ntok == 1 && ctx->decode_kernel) {
@@ -707,10 +743,12 @@ static lt_status forward_impl(lt_ctx *ctx, const lt_tensor *router, const lt_ten
         p.sync = ctx->dec_sync;
         if (lt::moe_decode_fits(p, ctx->num_sms)) return launched(ctx, lt::launch_moe_decode(cfg_of(ctx), p), "moe decode");
     }
-    st = route_impl(ctx, router, dev_x, dev_norm_w, eps, ntok, k, norm_topk, dev_expert_scale, ids, w, s.logits, s.xq,
-                    s.xq_pitch);
+    float *xn = s.gemm && dev_norm_w ? s.xn : nullptr;  // the tensor-core path reads f32 rows
+    st = route_impl(ctx, router, dev_x, dev_norm_w, eps, ntok, k, norm_topk, dev_expert_scale, ids, w, s.logits,
+                    s.gemm ? nullptr : s.xq, s.xq_pitch, xn);
     if (st != LT_OK) return st;
-    return ffn_impl(ctx, gate, up, down, act, ntok, ids, w, k, residual ? dev_x : nullptr, dev_out, s);
+    return ffn_impl(ctx, gate, up, down, act, ntok, ids, w, k, residual ? dev_x : nullptr, dev_out, xn ? xn : dev_x,
+                    s);
 }
 
 lt_status lt_moe_forward(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *gate, const lt_tensor *up,
@@ -767,7 +805,8 @@ lt_status lt_moe_forward_host(lt_ctx *ctx, const lt_tensor *router, const lt_ten
     if (ntok == 0) return LT_OK;
     const uint64_t d = gate->m.cols;
     const uint32_t E = gate->m.n_experts;
-    const MoeScratch probe = moe_layout(nullptr, ntok, k, E ? E : 1, d, gate->m.rows);
+    const MoeScratch probe = moe_layout(nullptr, ntok, k, E ? E : 1, d, gate->m.rows,
+                                        down ? gemm_bytes_of(ctx, gate, down, ntok, k) : 0);
     const size_t xb = al256((size_t)ntok * d * 4), ib = al256((size_t)ntok * k * 4), eb = al256((size_t)E * 4);
     const size_t io = 2 * xb + 2 * ib + eb;
     if ((st = ensure_scratch(ctx, probe.bytes + io)) != LT_OK) return st;

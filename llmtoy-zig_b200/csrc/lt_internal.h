@@ -97,7 +97,7 @@ cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert,
 cudaError_t launch_router(const LaunchCfg &c, const float *w, uint32_t E, uint32_t cols, uint32_t w_ld,
                           const float *x, const float *norm_w, float eps, uint32_t ntok, uint32_t k,
                           int norm_topk, const float *escale, uint32_t *ids, float *wout, float *logits,
-                          uint32_t *counters, uint8_t *xq, uint64_t xq_pitch);
+                          uint32_t *counters, uint8_t *xq, uint64_t xq_pitch, float *xn = nullptr);
 uint32_t router_token_groups(uint32_t ntok);
 
 cudaError_t launch_moe_plan(const LaunchCfg &c, const uint32_t *ids, uint32_t ntok, uint32_t k,
@@ -143,6 +143,16 @@ struct DecodeParams {
     uint8_t *sync;
 };
 constexpr size_t kDecodeSyncBytes = 4096;
+
+// Grouped expert GEMM on the tensor cores (lt_moe_gemm.cu) for multi-token
+// batches with Q4_K gate/up/down (K <= 2048).  x: [T][d] expert input (already
+// normalised), w: [T][k] slot weights, p: dispatch plan of the T*k pairs;
+// out = (resid ? resid : 0) + sum_s w_s * down(act(gate x) * up x).
+bool moe_gemm_supported(const DevMat &gate, const DevMat &down, uint64_t F);
+size_t moe_gemm_scratch(uint32_t T, uint32_t k, uint32_t E, uint64_t d, uint64_t F);
+cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const uint8_t *up, const DevMat &down, int act,
+                                const float *x, uint32_t T, uint32_t k, const float *w, const MoePlan &p,
+                                const float *resid, float *out, uint8_t *scratch);
 size_t moe_decode_img_bytes(uint64_t F);
 constexpr size_t kDecodeSmemLimit = 227 * 1024;
 // Whether the persistent kernel's per-CTA share fits in shared memory.

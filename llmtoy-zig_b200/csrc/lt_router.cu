@@ -30,6 +30,7 @@ struct RouterArgs {
     uint32_t *counters;
     uint8_t *xq;  // nullable: qact rows of the (normalised) input for the experts
     uint64_t xq_pitch;
+    float *xn;  // nullable: f32 rows of the (normalised) input, written by the CTAs of blockIdx.x == 0
 };
 
 __global__ void __launch_bounds__(kRouterWarps * 32) k_router(RouterArgs a) {
@@ -96,6 +97,8 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(RouterArgs a) {
         }
         __syncthreads();
     }
+    if (a.xn && blockIdx.x == 0)
+        for (uint32_t i = threadIdx.x; i < nt * cols; i += blockDim.x) a.xn[(size_t)t0 * cols + i] = xsm[i];
     if (a.xq) {  // quantise this CTA's share of the 32-blocks for the expert kernels
         const uint32_t nblk = cols / 32;
         for (uint32_t task = blockIdx.x * kRouterWarps + warp; task < nt * nblk; task += gridDim.x * kRouterWarps) {
@@ -157,8 +160,9 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(RouterArgs a) {
 cudaError_t launch_router(const LaunchCfg &c, const float *w, uint32_t E, uint32_t cols, uint32_t w_ld,
                           const float *x, const float *norm_w, float eps, uint32_t ntok, uint32_t k, int norm_topk,
                           const float *escale, uint32_t *ids, float *wout, float *logits, uint32_t *counters,
-                          uint8_t *xq, uint64_t xq_pitch) {
-    RouterArgs a{w, E, cols, w_ld, x, norm_w, eps, ntok, k, norm_topk, escale, ids, wout, logits, counters, xq, xq_pitch};
+                          uint8_t *xq, uint64_t xq_pitch, float *xn) {
+    RouterArgs a{w,      E,   cols,      w_ld,   x,    norm_w, eps,      ntok, k,
+                 norm_topk, escale, ids, wout, logits, counters, xq, xq_pitch, xn};
     const dim3 grid((E + kRouterWarps - 1) / kRouterWarps, router_token_groups(ntok));
     const size_t smem_x = (size_t)(kRouterTok + (norm_w ? 1 : 0)) * cols * 4;
     const size_t smem_topk = (size_t)kRouterTok * (kRouterMaxE * 4 + (kRouterMaxE + 2) * 8);
