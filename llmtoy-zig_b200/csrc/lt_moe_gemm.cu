@@ -19,43 +19,71 @@
 //     j) is one more MMA: dmin*m is exact in f32 and split into two f16
 //     planes, the sub-block sums likewise (hi*hi + hi*lo + lo*hi).
 //
-// CTA tile: 128 weight rows x 32 positions.  For gate/up the rows are 64
+// Work item: 128 weight rows x 32 positions.  For gate/up the rows are 64
 // gate rows and the same 64 up rows, so the epilogue forms h = act(g)*u.
-// Per stage (half a superblock, K = 128) the CTA's 128 threads dequantise
-// one weight row each (raw Q4_K rows arrive by TMA bulk copies, a superblock
-// ahead) and cp.async gathers the activation rows of the tile's positions,
-// two stages ahead; one thread issues the MMAs, which run while the next
-// stage is prepared.
+// Per stage (half a superblock, K = 128) four warps dequantise one weight row
+// per thread from raw Q4_K rows that a producer warp streams in by TMA bulk
+// copies; another warp gathers the activation rows of the item's positions
+// with cp.async; one lane issues the MMAs.  Each superblock accumulates in
+// one of two TMEM buffers, which the dequantising warps fold into registers
+// (y += d * acc) while the next superblock runs.
+#include <cuda.h>  // CUtensorMap (encoded through the runtime's driver entry point)
 #include <cuda_fp16.h>
+
+#include <mutex>
 
 #include "lt_launch.cuh"
 #include "lt_umma.cuh"
 
 namespace lt {
 
-constexpr int kGThreads = 128;
 constexpr int kGN = 32;     // positions per tile (MMA N)
 constexpr int kGM = 128;    // weight rows per tile (MMA M)
 constexpr int kGMaxSb = 8;  // superblocks per row (K <= 2048)
 
+// Roles (warps): 0-7 dequantise weight rows into the A stages and run the
+// epilogue (two threads per tile row: one per 64-column pair of the stage;
+// row = TMEM lane); 8 streams raw Q4_K superblocks (tiled TMA); 9 gathers
+// the activation stages (cp.async, one position per lane) and the min-term
+// operand; 10 issues the MMAs (one lane).  The CTA is persistent: it walks the
+// (tile, 128-row block) work items of the launch with stride gridDim.x, and
+// every ring keeps running across items.
+//
+// The activation operand stacks the two planes: rows 0-31 of B are the hi
+// plane of the 32 positions, rows 32-63 the lo plane, so one N = 64 MMA per
+// K step covers both and the accumulator's column halves are added.
+constexpr int kGMath = 256;
+constexpr int kGWarpRaw = 8, kGWarpB = 9, kGWarpMma = 10;
+constexpr int kGThreadsV2 = 11 * 32;
+constexpr int kGNN = 2 * kGN;  // MMA N: hi and lo planes
+constexpr int kGRawSlots = 3;  // raw superblocks in flight
+constexpr int kGAStages = 2;   // dequantised A stages (K = 128 each)
+constexpr int kGBStages = 3;   // activation stages
+constexpr uint32_t kGTmemCols = 256;  // 2 x 64 superblock accumulators + 64 min-term columns
+
 // Dynamic shared memory, offsets from a 1024-byte aligned base.
-constexpr uint32_t kOffA = 0;                          // 2 stages x 2 atoms x 16 KB
-constexpr uint32_t kOffB = 64 * 1024;                  // 4 stages x 2 planes x 2 atoms x 4 KB
-constexpr uint32_t kOffAm = kOffB + 64 * 1024;         // min-term A: 2 planes x 16 KB
-constexpr uint32_t kOffBm = kOffAm + 32 * 1024;        // min-term B: 2 planes x 4 KB
-constexpr uint32_t kRawStage = kGM * 144;              // one superblock of 128 rows
-constexpr uint32_t kOffRaw = kOffBm + 8 * 1024;        // 2 x raw superblock
-constexpr uint32_t kOffHdr = kOffRaw + 2 * kRawStage;  // d per superblock and row, f32 [8][128]
-constexpr uint32_t kOffMisc = kOffHdr + kGMaxSb * kGM * 4;
-constexpr uint32_t kGSmem = kOffMisc + 512 + 1024;     // + misc + alignment slack
+constexpr uint32_t kRawStage = kGM * 144;                          // one superblock of 128 rows
+constexpr uint32_t kOffA = 0;                                       // kGAStages x 2 atoms x 16 KB
+constexpr uint32_t kOffB = kOffA + kGAStages * 32768;               // kGBStages x 2 atoms x 8 KB (64 rows)
+constexpr uint32_t kOffAm = kOffB + kGBStages * 16384;              // min-term A: 2 planes x 16 KB
+constexpr uint32_t kOffBm = kOffAm + 32768;                         // min-term B: one 64-row atom
+constexpr uint32_t kOffRaw = kOffBm + 8192;                         // kGRawSlots x raw superblock
+constexpr uint32_t kOffHdr = kOffRaw + kGRawSlots * kRawStage;      // d [8][128] f32
+constexpr uint32_t kOffMisc = kOffHdr + kGMaxSb * kGM * 4;          // barriers, TMEM address, scales
+constexpr uint32_t kGSmem = kOffMisc + 512 + 1024;                  // + alignment slack
 
 struct GemmArgs {
+    // 2-D byte views [rows][pitch] of the weights for tiled TMA: one load
+    // moves a 64-row x 144-byte box (one Q4_K superblock column)
+    alignas(64) CUtensorMap map_w;
+    alignas(64) CUtensorMap map_up;
     const uint8_t *w;     // gate (mode 0) or down (mode 1) weights
     const uint8_t *w_up;  // mode 0: up weights; nullptr when w holds [gate; up] per expert
     uint64_t pitch;
     uint32_t K;       // columns (multiple of 256, <= 2048)
     uint32_t rows_e;  // rows per expert in w
     uint32_t F;       // mode 0: expert width
+    uint32_t mt;      // 128-row blocks per tile
     int act;
     MoePlan p;
     const uint2 *tiles;  // (active expert slot, first position within it)
@@ -74,11 +102,34 @@ LT_DEVINL void cp_async16(void *dst_smem, const void *src, uint32_t src_bytes) {
                  "r"(src_bytes)
                  : "memory");
 }
-LT_DEVINL void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-LT_DEVINL void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+// Arrive on an mbarrier once this thread's earlier cp.async copies land
+// (the arrival counts against the barrier's expected count).
+LT_DEVINL void cp_async_arrive(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+LT_DEVINL void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// 2-D tiled TMA load of box (x, y) of a tensor map held in kernel parameters.
+LT_DEVINL void tma_load_2d(void *dst_smem, const CUtensorMap *map, uint32_t x, uint32_t y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst_smem)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 16 consecutive 32-bit TMEM columns of this thread's lane.
+LT_DEVINL void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
+
+// Barrier among the eight dequantising warps only.
+LT_DEVINL void math_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 LT_DEVINL uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
     __half2 r = __hfma2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b),
@@ -96,244 +147,313 @@ LT_DEVINL void split_f16(float v, __half &h, __half &l) {
     l = __float2half_rn(v - __half2float(h));
 }
 
-LT_DEVINL void gemm_wait(uint64_t *bar, uint32_t parity, int *dev_err) {
-    if (!mbar_wait_bounded(bar, parity, kWaitLimitNs) && dev_err) atomicExch(dev_err, DEV_ERR_TMA_TIMEOUT);
+// Wait for completion number n (0, 1, ...) of a barrier.
+LT_DEVINL void gemm_wait(uint64_t *bar, uint32_t n, int *dev_err) {
+    if (!mbar_wait_bounded(bar, n & 1, kWaitLimitNs) && dev_err) atomicExch(dev_err, DEV_ERR_TMA_TIMEOUT);
+}
+
+struct GemmItem {
+    uint32_t e, pos0, nvalid, m0;
+};
+
+LT_DEVINL GemmItem gemm_item(const GemmArgs &a, uint32_t w) {
+    const uint2 tile = a.tiles[w / a.mt];
+    GemmItem it;
+    it.m0 = w % a.mt;
+    it.e = a.p.act_e[tile.x];
+    it.pos0 = a.p.act_off[tile.x] + tile.y;
+    it.nvalid = min((uint32_t)kGN, a.p.act_cnt[tile.x] - tile.y);
+    return it;
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kGThreads, 1) k_moe_gemm(GemmArgs a) {
+__global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_constant__ GemmArgs a) {
     extern __shared__ uint8_t g_smem_raw[];
     uint8_t *sm = g_smem_raw + ((1024u - (smem_u32(g_smem_raw) & 1023u)) & 1023u);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    pdl_wait();
-    if (blockIdx.y >= *a.n_tiles) return;
-    const uint2 tile = a.tiles[blockIdx.y];
-    const uint32_t slot = tile.x, n0 = tile.y;
-    const uint32_t e = a.p.act_e[slot];
-    const uint32_t pos0 = a.p.act_off[slot] + n0;
-    const uint32_t nvalid = min((uint32_t)kGN, a.p.act_cnt[slot] - n0);
-    const uint32_t m0 = blockIdx.x;
-    const uint32_t nsb = a.K / 256, nks = 2 * nsb;
-    const uint32_t ncols = nsb + 1 <= 4 ? 128u : nsb + 1 <= 8 ? 256u : 512u;
-
-    uint64_t *bar_raw = reinterpret_cast<uint64_t *>(sm + kOffMisc);  // [2]
-    uint64_t *bar_mma = bar_raw + 2;                                    // [2]
-    uint64_t *bar_fin = bar_raw + 4;
-    uint32_t *s_taddr = reinterpret_cast<uint32_t *>(bar_raw + 5);
-    uint32_t *s_row = s_taddr + 1;  // [32] activation row of each tile position
-    float *s_inv = reinterpret_cast<float *>(s_row + kGN);  // [32]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kOffMisc);
+    uint64_t *raw_full = bars, *raw_empty = bars + 3;        // [3]
+    uint64_t *a_full = bars + 6, *a_empty = bars + 8;        // [2]
+    uint64_t *b_full = bars + 10, *b_empty = bars + 13;      // [3]
+    uint64_t *acc_full = bars + 16, *acc_empty = bars + 18;  // [2]
+    uint64_t *min_full = bars + 20, *min_empty = bars + 21, *bm_full = bars + 22;
+    uint32_t *s_taddr = reinterpret_cast<uint32_t *>(bars + 23);
+    float *s_inv = reinterpret_cast<float *>(s_taddr + 4);  // [2][32] by item parity
     float *hdr_d = reinterpret_cast<float *>(sm + kOffHdr);
 
-    // the weight row this thread dequantises (tile row = tid)
-    auto wrow_of = [&](uint32_t r) -> const uint8_t * {
-        if (MODE == 0) {
-            const uint32_t f = 64 * m0 + (r & 63);
-            if (r < 64) return a.w + ((uint64_t)e * a.rows_e + f) * a.pitch;
-            return a.w_up ? a.w_up + ((uint64_t)e * a.F + f) * a.pitch
-                          : a.w + ((uint64_t)e * a.rows_e + a.F + f) * a.pitch;  // fused: up rows [F, 2F)
-        }
-        return a.w + ((uint64_t)e * a.rows_e + kGM * m0 + r) * a.pitch;
-    };
-
-    if (tid < kGN) {
-        uint32_t row = 0xffffffffu;
-        float inv = 0.0f;
-        if ((uint32_t)tid < nvalid) {
-            const uint32_t pos = pos0 + tid;
-            row = MODE == 0 ? a.p.pos_pair[pos] / a.k : pos;
-            inv = a.xinv[row];
-        }
-        s_row[tid] = row;
-        s_inv[tid] = inv;
-    }
+    const uint32_t nsb = a.K / 256;
     if (tid == 0) {
-        for (int i = 0; i < 5; i++) mbar_init(&bar_raw[i], 1);
+        for (int i = 0; i < 3; i++) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], kGMath);
+            mbar_init(&b_full[i], 32);
+            mbar_init(&b_empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&a_full[i], kGMath);
+            mbar_init(&a_empty[i], 1);
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], kGMath);
+        }
+        mbar_init(min_full, 1);
+        mbar_init(min_empty, kGMath);
+        mbar_init(bm_full, 32);
         fence_barrier_init();
     }
     if (warp == 0) {
-        tmem_alloc(s_taddr, ncols);
+        tmem_alloc(s_taddr, kGTmemCols);
         tmem_relinquish();
     }
-    // min-term operands: zero (K beyond 8*nsb stays zero), then B from the sums
-    for (uint32_t i = tid; i < (40u * 1024) / 16; i += kGThreads)
+    // min-term operands stay zero beyond K = 8*nsb
+    for (uint32_t i = tid; i < (40u * 1024) / 16; i += blockDim.x)
         reinterpret_cast<uint4 *>(sm + kOffAm)[i] = make_uint4(0, 0, 0, 0);
+    pdl_wait();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t taddr = *s_taddr;
+    const uint32_t n_work = *a.n_tiles * a.mt;
 
-    // raw Q4_K superblocks 0 and 1 (one 144-byte bulk copy per row)
-    auto issue_raw = [&](uint32_t sb) {
-        if (warp != 0) return;
-        uint64_t *bar = &bar_raw[sb & 1];
-        if (lane == 0) mbar_arrive_expect_tx(bar, kRawStage);
-        __syncwarp();
-        uint8_t *dst = sm + kOffRaw + (sb & 1) * kRawStage;
-        for (uint32_t r = lane; r < (uint32_t)kGM; r += 32) tma_load_1d(dst + r * 144, wrow_of(r) + 144 * sb, 144, bar);
-    };
-    issue_raw(0);
-    if (nsb > 1) issue_raw(1);
-
-    // activation stage ks: 32 positions x 128 columns x 2 planes, gathered by cp.async
-    auto fill_b = [&](uint32_t ks) {
-        uint8_t *bs = sm + kOffB + (ks & 3) * 16384;
-        const uint32_t k0 = ks * 128;
-        for (uint32_t i = tid; i < 2u * kGN * 16; i += kGThreads) {
-            const uint32_t plane = i >> 9, rem = i & 511, n = rem >> 4, cc = rem & 15;
-            const uint32_t row = s_row[n];
-            const __half *src = (plane ? a.xl : a.xh) + (size_t)(row == 0xffffffffu ? 0 : row) * a.K + k0 + cc * 8;
-            uint8_t *dst = bs + plane * 8192 + (cc >> 3) * 4096 + n * 128 + (((cc & 7) ^ (n & 7)) << 4);
-            cp_async16(dst, src, row == 0xffffffffu ? 0u : 16u);
-        }
-        cp_async_commit();
-    };
-    fill_b(0);
-    if (nks > 1) fill_b(1); else cp_async_commit();
-
-    // min-term B: sub-block sums of each position, two planes
-    for (uint32_t i = tid; i < kGN * 8 * nsb; i += kGThreads) {
-        const uint32_t n = i / (8 * nsb), j = i - n * (8 * nsb);
-        const uint32_t row = s_row[n];
-        const float v = row == 0xffffffffu ? 0.0f : a.xsum[(size_t)row * (a.K / 32) + j];
-        __half h, l;
-        split_f16(v, h, l);
-        *reinterpret_cast<__half *>(sm + kOffBm + sw128_offset(n, j)) = h;
-        *reinterpret_cast<__half *>(sm + kOffBm + 4096 + sw128_offset(n, j)) = l;
-    }
-
-    const uint32_t idesc = umma_idesc_f16_f32(kGM, kGN);
-    for (uint32_t ks = 0; ks < nks; ks++) {
-        const uint32_t sb = ks >> 1, hf = ks & 1;
-        if (ks >= 2) gemm_wait(&bar_mma[ks & 1], ((ks >> 1) - 1) & 1, a.dev_err);  // MMAs of stage ks-2 done
-        if (ks + 2 < nks) fill_b(ks + 2); else cp_async_commit();
-        if (hf == 0) gemm_wait(&bar_raw[sb & 1], (sb >> 1) & 1, a.dev_err);
-
-        // dequantise this thread's row: pairs c = 2hf, 2hf+1 -> atoms 0, 1
-        {
-            const uint8_t *raw = sm + kOffRaw + (sb & 1) * kRawStage + tid * 144;
-            const uint4 hdr = lds128(raw);
-            // scale_min (dequant.zig:291-300) of sub-blocks 4hf .. 4hf+3
-            const uint32_t scw = hf == 0 ? (hdr.y & 0x3F3F3F3Fu)
-                                         : ((hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u));
-            const uint32_t mnw = hf == 0 ? (hdr.z & 0x3F3F3F3Fu)
-                                         : (((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u));
-            if (hf == 0) hdr_d[sb * kGM + tid] = f16_bits_to_f32(hdr.x);
-            const float dmin = f16_bits_to_f32(hdr.x >> 16);
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const float v = dmin * (float)((mnw >> (8 * j)) & 0xffu);  // exact in f32
-                __half h, l;
-                split_f16(v, h, l);
-                const uint32_t kk = 8 * sb + 4 * hf + j;
-                *reinterpret_cast<__half *>(sm + kOffAm + sw128_offset(tid, kk)) = h;
-                *reinterpret_cast<__half *>(sm + kOffAm + 16384 + sw128_offset(tid, kk)) = l;
-            }
-            uint8_t *as = sm + kOffA + (ks & 1) * 32768 + tid * 128;
-#pragma unroll
-            for (int cl = 0; cl < 2; cl++) {
-                const float sc0 = (float)((scw >> (16 * cl)) & 0xffu), sc1 = (float)((scw >> (16 * cl + 8)) & 0xffu);
-                const uint32_t s0 = half2_splat(sc0), b0 = half2_splat(-1024.0f * sc0);
-                const uint32_t s1 = half2_splat(sc1), b1 = half2_splat(-1024.0f * sc1);
-                const uint4 qa = lds128(raw + 16 + 32 * (2 * hf + cl)), qb = lds128(raw + 32 + 32 * (2 * hf + cl));
-                const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-                uint8_t *arow = as + cl * 16384;
-                const uint32_t sw = tid & 7;
-#pragma unroll
-                for (int m = 0; m < 4; m++) {
-                    // positions 8m..8m+7 hold elements 8m + (0,2,1,3,4,6,5,7) of sub-block 2c
-                    uint4 lo, hi;
-                    lo.x = hfma2_u32((w[2 * m] & 0x000F000Fu) | 0x64006400u, s0, b0);
-                    lo.y = hfma2_u32(((w[2 * m] >> 8) & 0x000F000Fu) | 0x64006400u, s0, b0);
-                    lo.z = hfma2_u32((w[2 * m + 1] & 0x000F000Fu) | 0x64006400u, s0, b0);
-                    lo.w = hfma2_u32(((w[2 * m + 1] >> 8) & 0x000F000Fu) | 0x64006400u, s0, b0);
-                    hi.x = hfma2_u32(((w[2 * m] >> 4) & 0x000F000Fu) | 0x64006400u, s1, b1);
-                    hi.y = hfma2_u32(((w[2 * m] >> 12) & 0x000F000Fu) | 0x64006400u, s1, b1);
-                    hi.z = hfma2_u32(((w[2 * m + 1] >> 4) & 0x000F000Fu) | 0x64006400u, s1, b1);
-                    hi.w = hfma2_u32(((w[2 * m + 1] >> 12) & 0x000F000Fu) | 0x64006400u, s1, b1);
-                    *reinterpret_cast<uint4 *>(arow + ((m ^ sw) << 4)) = lo;
-                    *reinterpret_cast<uint4 *>(arow + (((4 + m) ^ sw) << 4)) = hi;
+    if (warp == kGWarpRaw) {
+        // ── raw Q4_K superblocks: two 64-row x 144-byte tiled loads ──
+        if (lane == 0) {
+            uint32_t gsb = 0;
+            for (uint32_t w = blockIdx.x; w < n_work; w += gridDim.x) {
+                const GemmItem it = gemm_item(a, w);
+                uint32_t y0, y1;  // first weight row of tile rows 0-63 and 64-127
+                const CUtensorMap *m1 = &a.map_w;
+                if (MODE == 0) {
+                    y0 = it.e * a.rows_e + 64 * it.m0;
+                    if (a.w_up) {
+                        y1 = it.e * a.F + 64 * it.m0;
+                        m1 = &a.map_up;
+                    } else {
+                        y1 = y0 + a.F;  // fused: up rows [F, 2F)
+                    }
+                } else {
+                    y0 = it.e * a.rows_e + kGM * it.m0;
+                    y1 = y0 + 64;
+                }
+                for (uint32_t sb = 0; sb < nsb; sb++, gsb++) {
+                    const uint32_t slot = gsb % kGRawSlots;
+                    if (gsb >= (uint32_t)kGRawSlots) gemm_wait(&raw_empty[slot], gsb / kGRawSlots - 1, a.dev_err);
+                    uint8_t *dst = sm + kOffRaw + slot * kRawStage;
+                    mbar_arrive_expect_tx(&raw_full[slot], kRawStage);
+                    tma_load_2d(dst, &a.map_w, 144 * sb, y0, &raw_full[slot]);
+                    tma_load_2d(dst + 64 * 144, m1, 144 * sb, y1, &raw_full[slot]);
                 }
             }
         }
-        if (hf == 1 && sb + 2 < nsb) {  // raw slot sb&1 is consumed: fetch superblock sb+2 into it
-            __syncthreads();
-            issue_raw(sb + 2);
-        }
-        cp_async_wait<2>();  // this thread's copies of stage ks have landed
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t abase = smem_u32(sm + kOffA + (ks & 1) * 32768);
-            const uint32_t bbase = smem_u32(sm + kOffB + (ks & 3) * 16384);
-            const uint32_t d_tmem = taddr + sb * kGN;
+    } else if (warp == kGWarpB) {
+        // ── activation stages (lane n gathers position n, zero past the item)
+        //    and, once per item, the min-term B rows and 2^e of the positions ──
+        uint32_t gs = 0, gi = 0;
+        for (uint32_t w = blockIdx.x; w < n_work; w += gridDim.x, gi++) {
+            const GemmItem it = gemm_item(a, w);
+            uint32_t row = 0;
+            const bool valid = (uint32_t)lane < it.nvalid;
+            if (valid) row = MODE == 0 ? a.p.pos_pair[it.pos0 + lane] / a.k : it.pos0 + lane;
+            const __half *srch = a.xh + (size_t)row * a.K, *srcl = a.xl + (size_t)row * a.K;
+            const uint32_t nks = 2 * nsb, ks_bm = nks > 2 ? 2 : nks - 1;
+            for (uint32_t ks = 0; ks < nks; ks++, gs++) {
+                const uint32_t s = gs % kGBStages;
+                if (gs >= (uint32_t)kGBStages) gemm_wait(&b_empty[s], gs / kGBStages - 1, a.dev_err);
+                uint8_t *bs = sm + kOffB + s * 16384 + lane * 128;
 #pragma unroll
-            for (uint32_t s = 0; s < 8; s++) {
-                const uint32_t ao = abase + (s >> 2) * 16384 + (s & 3) * 32;
-                const uint32_t bo = bbase + (s >> 2) * 4096 + (s & 3) * 32;
-                umma_f16(d_tmem, umma_desc_sw128(ao), umma_desc_sw128(bo), idesc, (hf | s) != 0);
-                umma_f16(d_tmem, umma_desc_sw128(ao), umma_desc_sw128(bo + 8192), idesc, 1);
+                for (uint32_t cc = 0; cc < 16; cc++) {
+                    const uint32_t o = (cc >> 3) * 8192 + (((cc & 7) ^ (lane & 7)) << 4);
+                    cp_async16(bs + o, srch + ks * 128 + cc * 8, valid ? 16u : 0u);
+                    cp_async16(bs + 4096 + o, srcl + ks * 128 + cc * 8, valid ? 16u : 0u);
+                }
+                cp_async_arrive(&b_full[s]);
+                if (ks == ks_bm) {
+                    // the previous item's min term has consumed the old B rows
+                    if (gi >= 1) gemm_wait(min_full, gi - 1, a.dev_err);
+                    const float inv = valid ? a.xinv[row] : 0.0f;
+                    const float *xs = a.xsum + (size_t)row * (a.K / 32);
+                    for (uint32_t j = 0; j < 8 * nsb; j += 4) {
+                        float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (valid) v4 = *reinterpret_cast<const float4 *>(xs + j);
+                        const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+                        for (int q = 0; q < 4; q++) {
+                            __half h, l;
+                            split_f16(v[q], h, l);
+                            *reinterpret_cast<__half *>(sm + kOffBm + sw128_offset(lane, j + q)) = h;
+                            *reinterpret_cast<__half *>(sm + kOffBm + sw128_offset(32 + lane, j + q)) = l;
+                        }
+                    }
+                    s_inv[(gi & 1) * kGN + lane] = inv;
+                    fence_async_smem();
+                    mbar_arrive(bm_full);
+                }
             }
-            umma_commit(&bar_mma[ks & 1]);
         }
-    }
-    // min term into the last accumulator: hi*hi + hi*lo + lo*hi over K = 8*nsb
-    if (tid == 0) {
-        const uint32_t am = smem_u32(sm + kOffAm), bm = smem_u32(sm + kOffBm);
-        const uint32_t d_tmem = taddr + nsb * kGN;
-        const uint32_t nkm = (8 * nsb + 15) / 16;
-        for (uint32_t s = 0; s < nkm; s++) {
-            umma_f16(d_tmem, umma_desc_sw128(am + s * 32), umma_desc_sw128(bm + s * 32), idesc, s != 0);
-            umma_f16(d_tmem, umma_desc_sw128(am + s * 32), umma_desc_sw128(bm + 4096 + s * 32), idesc, 1);
-            umma_f16(d_tmem, umma_desc_sw128(am + 16384 + s * 32), umma_desc_sw128(bm + s * 32), idesc, 1);
+    } else if (warp == kGWarpMma) {
+        // ── MMA issue ──
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_f16_f32(kGM, kGNN);
+            uint32_t gs = 0, gsb = 0, gi = 0;
+            for (uint32_t w = blockIdx.x; w < n_work; w += gridDim.x, gi++) {
+                for (uint32_t sb = 0; sb < nsb; sb++, gsb++) {
+                    const uint32_t ab = gsb & 1;
+                    if (gsb >= 2) gemm_wait(&acc_empty[ab], gsb / 2 - 1, a.dev_err);
+                    const uint32_t d_tmem = taddr + ab * kGNN;
+                    for (uint32_t hf = 0; hf < 2; hf++, gs++) {
+                        const uint32_t sa = gs % kGAStages, s3 = gs % kGBStages;
+                        gemm_wait(&a_full[sa], gs / kGAStages, a.dev_err);
+                        gemm_wait(&b_full[s3], gs / kGBStages, a.dev_err);
+                        tc_fence_after();
+                        const uint32_t abase = smem_u32(sm + kOffA + sa * 32768);
+                        const uint32_t bbase = smem_u32(sm + kOffB + s3 * 16384);
+#pragma unroll
+                        for (uint32_t st = 0; st < 8; st++) {
+                            const uint32_t ao = abase + (st >> 2) * 16384 + (st & 3) * 32;
+                            const uint32_t bo = bbase + (st >> 2) * 8192 + (st & 3) * 32;
+                            umma_f16(d_tmem, umma_desc_sw128(ao), umma_desc_sw128(bo), idesc, (hf | st) != 0);
+                        }
+                        umma_commit(&a_empty[sa]);
+                        umma_commit(&b_empty[s3]);
+                    }
+                    umma_commit(&acc_full[ab]);
+                }
+                // min term: A planes (hi, lo) x B rows (hi plane | lo plane) over K = 8*nsb
+                gemm_wait(bm_full, gi, a.dev_err);
+                if (gi >= 1) gemm_wait(min_empty, gi - 1, a.dev_err);
+                tc_fence_after();
+                const uint32_t am = smem_u32(sm + kOffAm), bm = smem_u32(sm + kOffBm);
+                const uint32_t d_tmem = taddr + 2 * kGNN;
+                const uint32_t nkm = (8 * nsb + 15) / 16;
+                for (uint32_t st = 0; st < nkm; st++) {
+                    umma_f16(d_tmem, umma_desc_sw128(am + st * 32), umma_desc_sw128(bm + st * 32), idesc, st != 0);
+                    umma_f16(d_tmem, umma_desc_sw128(am + 16384 + st * 32), umma_desc_sw128(bm + st * 32), idesc, 1);
+                }
+                umma_commit(min_full);
+            }
         }
-        umma_commit(bar_fin);
-    }
-    gemm_wait(bar_fin, 0, a.dev_err);
-    tc_fence_after();
-
-    // epilogue: thread tid owns tile row tid (TMEM lane), all 32 positions
-    const uint32_t lane_addr = taddr + ((uint32_t)(32 * warp) << 16);
-    float y[kGN];
+    } else {
+        // ── dequantise (thread = tile row x column pair) and epilogue ──
+        const uint32_t r = tid & 127, hh = tid >> 7;  // row, pair within the stage / position half
+        const uint32_t lane_addr = taddr + ((uint32_t)(32 * (warp & 3)) << 16);
+        uint32_t gs = 0, gsb = 0, gi = 0;
+        float y[kGN / 2];
+        auto fold = [&](uint32_t n, uint32_t sb) {  // superblock accumulator n (global count) of superblock sb
+            gemm_wait(&acc_full[n & 1], n / 2, a.dev_err);
+            tc_fence_after();
+            uint32_t vh[16], vl[16];
+            tmem_ld16(lane_addr + (n & 1) * kGNN + 16 * hh, vh);
+            tmem_ld16(lane_addr + (n & 1) * kGNN + kGN + 16 * hh, vl);
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(&acc_empty[n & 1]);
+            const float dsb = hdr_d[sb * kGM + r];
 #pragma unroll
-    for (int n = 0; n < kGN; n++) y[n] = 0.0f;
-    for (uint32_t sb = 0; sb < nsb; sb++) {
-        uint32_t v[32];
-        tmem_ld32(lane_addr + sb * kGN, v);
-        tmem_wait_ld();
-        const float dsb = hdr_d[sb * kGM + tid];
+            for (int q = 0; q < kGN / 2; q++)
+                y[q] = fmaf(dsb, __uint_as_float(vh[q]) + __uint_as_float(vl[q]), y[q]);
+        };
+        for (uint32_t w = blockIdx.x; w < n_work; w += gridDim.x, gi++) {
+            const GemmItem it = gemm_item(a, w);
 #pragma unroll
-        for (int n = 0; n < kGN; n++) y[n] = fmaf(dsb, __uint_as_float(v[n]), y[n]);
-    }
-    {
-        uint32_t v[32];
-        tmem_ld32(lane_addr + nsb * kGN, v);
-        tmem_wait_ld();
+            for (int q = 0; q < kGN / 2; q++) y[q] = 0.0f;
+            for (uint32_t sb = 0; sb < nsb; sb++, gsb++) {
+                const uint32_t slot = gsb % kGRawSlots;
+                gemm_wait(&raw_full[slot], gsb / kGRawSlots, a.dev_err);
+                const uint8_t *raw = sm + kOffRaw + slot * kRawStage + r * 144;
+                const uint4 hdr = lds128(raw);
+                if (hh == 0) hdr_d[sb * kGM + r] = f16_bits_to_f32(hdr.x);
+                const float dmin = f16_bits_to_f32(hdr.x >> 16);
+                for (uint32_t hf = 0; hf < 2; hf++, gs++) {
+                    const uint32_t sa = gs % kGAStages;
+                    if (gs >= (uint32_t)kGAStages) gemm_wait(&a_empty[sa], gs / kGAStages - 1, a.dev_err);
+                    // scale_min (dequant.zig:291-300) of sub-blocks 4hf .. 4hf+3
+                    const uint32_t scw = hf == 0 ? (hdr.y & 0x3F3F3F3Fu)
+                                                 : ((hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u));
+                    const uint32_t mnw = hf == 0 ? (hdr.z & 0x3F3F3F3Fu)
+                                                 : (((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u));
+                    // this thread: pair c = 2hf + hh (sub-blocks 2c, 2c+1) -> atom hh
 #pragma unroll
-        for (int n = 0; n < kGN; n++) y[n] = (y[n] - __uint_as_float(v[n])) * s_inv[n];
+                    for (int j = 0; j < 2; j++) {
+                        const float v = dmin * (float)((mnw >> (16 * hh + 8 * j)) & 0xffu);  // exact in f32
+                        __half h, l;
+                        split_f16(v, h, l);
+                        const uint32_t kk = 8 * sb + 4 * hf + 2 * hh + j;
+                        *reinterpret_cast<__half *>(sm + kOffAm + sw128_offset(r, kk)) = h;
+                        *reinterpret_cast<__half *>(sm + kOffAm + 16384 + sw128_offset(r, kk)) = l;
+                    }
+                    {
+                        const float sc0 = (float)((scw >> (16 * hh)) & 0xffu);
+                        const float sc1 = (float)((scw >> (16 * hh + 8)) & 0xffu);
+                        const uint32_t s0 = half2_splat(sc0), b0 = half2_splat(-1024.0f * sc0);
+                        const uint32_t s1 = half2_splat(sc1), b1 = half2_splat(-1024.0f * sc1);
+                        const uint4 qa = lds128(raw + 16 + 32 * (2 * hf + hh));
+                        const uint4 qb = lds128(raw + 32 + 32 * (2 * hf + hh));
+                        const uint32_t wq[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                        uint8_t *arow = sm + kOffA + sa * 32768 + hh * 16384 + r * 128;
+                        const uint32_t swz = r & 7;
+#pragma unroll
+                        for (int m = 0; m < 4; m++) {
+                            // positions 8m..8m+7 hold elements 8m + (0,2,1,3,4,6,5,7) of sub-block 2c
+                            uint4 lo, hi;
+                            lo.x = hfma2_u32((wq[2 * m] & 0x000F000Fu) | 0x64006400u, s0, b0);
+                            lo.y = hfma2_u32(((wq[2 * m] >> 8) & 0x000F000Fu) | 0x64006400u, s0, b0);
+                            lo.z = hfma2_u32((wq[2 * m + 1] & 0x000F000Fu) | 0x64006400u, s0, b0);
+                            lo.w = hfma2_u32(((wq[2 * m + 1] >> 8) & 0x000F000Fu) | 0x64006400u, s0, b0);
+                            hi.x = hfma2_u32(((wq[2 * m] >> 4) & 0x000F000Fu) | 0x64006400u, s1, b1);
+                            hi.y = hfma2_u32(((wq[2 * m] >> 12) & 0x000F000Fu) | 0x64006400u, s1, b1);
+                            hi.z = hfma2_u32(((wq[2 * m + 1] >> 4) & 0x000F000Fu) | 0x64006400u, s1, b1);
+                            hi.w = hfma2_u32(((wq[2 * m + 1] >> 12) & 0x000F000Fu) | 0x64006400u, s1, b1);
+                            *reinterpret_cast<uint4 *>(arow + ((m ^ swz) << 4)) = lo;
+                            *reinterpret_cast<uint4 *>(arow + (((4 + m) ^ swz) << 4)) = hi;
+                        }
+                    }
+                    fence_async_smem();
+                    mbar_arrive(&a_full[sa]);
+                }
+                mbar_arrive(&raw_empty[slot]);
+                if (sb >= 1) fold(gsb - 1, sb - 1);
+            }
+            fold(gsb - 1, nsb - 1);
+            gemm_wait(min_full, gi, a.dev_err);
+            tc_fence_after();
+            {
+                uint32_t vh[16], vl[16];
+                tmem_ld16(lane_addr + 2 * kGNN + 16 * hh, vh);
+                tmem_ld16(lane_addr + 2 * kGNN + kGN + 16 * hh, vl);
+                tmem_wait_ld();
+                tc_fence_before();
+                mbar_arrive(min_empty);
+                const float *inv = s_inv + (gi & 1) * kGN + 16 * hh;  // written before bm_full, which min_full follows
+#pragma unroll
+                for (int q = 0; q < kGN / 2; q++)
+                    y[q] = (y[q] - (__uint_as_float(vh[q]) + __uint_as_float(vl[q]))) * inv[q];
+            }
+            const uint32_t q0 = 16 * hh;
+            if (MODE == 1) {
+                const uint32_t orow = kGM * it.m0 + r;
+#pragma unroll
+                for (uint32_t q = 0; q < (uint32_t)kGN / 2; q++)
+                    if (q0 + q < it.nvalid) a.out[(size_t)(it.pos0 + q0 + q) * a.out_ld + orow] = y[q];
+            } else {
+                // the A stages are idle here: every MMA of this item has completed
+                float *uex = reinterpret_cast<float *>(sm + kOffA);  // [64][33]
+                if (r >= 64)
+#pragma unroll
+                    for (int q = 0; q < kGN / 2; q++) uex[(r - 64) * 33 + q0 + q] = y[q];
+                math_sync();
+                if (r < 64) {
+                    const uint32_t f = 64 * it.m0 + r;
+#pragma unroll
+                    for (uint32_t q = 0; q < (uint32_t)kGN / 2; q++)
+                        if (q0 + q < it.nvalid)
+                            a.out[(size_t)(it.pos0 + q0 + q) * a.F + f] = act_apply(a.act, y[q]) * uex[r * 33 + q0 + q];
+                }
+            }
+            math_sync();  // uex read before the next item's A writes
+        }
     }
     tc_fence_before();
-    if (MODE == 1) {
-        const uint32_t r = kGM * m0 + tid;
-#pragma unroll
-        for (uint32_t n = 0; n < (uint32_t)kGN; n++)
-            if (n < nvalid) a.out[(size_t)(pos0 + n) * a.out_ld + r] = y[n];
-    } else {
-        float *uex = reinterpret_cast<float *>(sm + kOffA);  // [64][33]; the A stages are free now
-        if (tid >= 64)
-#pragma unroll
-            for (int n = 0; n < kGN; n++) uex[(tid - 64) * 33 + n] = y[n];
-        __syncthreads();
-        if (tid < 64) {
-            const uint32_t f = 64 * m0 + tid;
-#pragma unroll
-            for (uint32_t n = 0; n < (uint32_t)kGN; n++)
-                if (n < nvalid) a.out[(size_t)(pos0 + n) * a.F + f] = act_apply(a.act, y[n]) * uex[tid * 33 + n];
-        }
-    }
     __syncthreads();
-    if (warp == 0) tmem_dealloc(taddr, ncols);
+    if (warp == 0) tmem_dealloc(taddr, kGTmemCols);
 }
 
 // ── activation prep: f32 rows -> f16 hi/lo planes (K permuted in groups of 4
@@ -401,6 +521,42 @@ __global__ void k_gemm_combine(const float *y, uint32_t D, const uint32_t *pair_
     out[oi] = resid ? resid[oi] + o : o;
 }
 
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+    static std::once_flag once;
+    static EncodeTiledFn fn = nullptr;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+
+// [total rows][pitch] byte view of a weight tensor, box = 144 bytes x 64 rows.
+bool encode_rows(CUtensorMap *map, const void *base, uint64_t pitch, uint64_t total_rows) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {pitch, total_rows};
+    const cuuint64_t strides[1] = {pitch};
+    const cuuint32_t box[2] = {144, 64};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
 bool moe_gemm_supported(const DevMat &gate, const DevMat &down, uint64_t F) {
     return gate.type == T_Q4_K && down.type == T_Q4_K && gate.cols % 256 == 0 && F % 256 == 0 &&
            gate.cols <= 256u * kGMaxSb && F <= 256u * kGMaxSb && down.rows % kGM == 0;
@@ -444,12 +600,18 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
     if (e == cudaSuccess)
         e = launch_k(c, "moe_gemm_prep", k_gemm_prep, dim3(T), dim3(256), 0, x, (uint32_t)d, xh, xl, xsum, xinv);
     GemmArgs g;
+    const uint32_t E1 = E ? E : 1;
+    if (!encode_rows(&g.map_w, gate.data, gate.pitch, (uint64_t)gate.rows * E1) ||
+        (up && !encode_rows(&g.map_up, up, gate.pitch, (uint64_t)F * E1)))
+        return cudaErrorInvalidValue;
+    if (!up) g.map_up = g.map_w;
     g.w = gate.data;
     g.w_up = up;
     g.pitch = gate.pitch;
     g.K = (uint32_t)d;
     g.rows_e = (uint32_t)gate.rows;
     g.F = (uint32_t)F;
+    g.mt = (uint32_t)(F / 64);
     g.act = act;
     g.p = p;
     g.tiles = tiles;
@@ -463,17 +625,20 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
     g.out_ld = (uint32_t)F;
     g.dev_err = c.dev_err;
     if (e == cudaSuccess)
-        e = launch_k(c, "moe_gemm_gate_up", k_moe_gemm<0>, dim3((uint32_t)(F / 64), (uint32_t)max_tiles),
-                     dim3(kGThreads), (size_t)kGSmem, g);
+        e = launch_k(c, "moe_gemm_gate_up", k_moe_gemm<0>, dim3((uint32_t)c.num_sms), dim3(kGThreadsV2),
+                     (size_t)kGSmem, g);
     if (e == cudaSuccess)
         e = launch_k(c, "moe_gemm_prep", k_gemm_prep, dim3((uint32_t)P), dim3(256), 0, (const float *)hbuf,
                      (uint32_t)F, hh, hl, hsum, hinv);
     GemmArgs gd = g;
+    if (!encode_rows(&gd.map_w, down.data, down.pitch, (uint64_t)down.rows * E1)) return cudaErrorInvalidValue;
+    gd.map_up = gd.map_w;
     gd.w = down.data;
     gd.w_up = nullptr;
     gd.pitch = down.pitch;
     gd.K = (uint32_t)F;
     gd.rows_e = (uint32_t)down.rows;
+    gd.mt = (uint32_t)(d / kGM);
     gd.xh = hh;
     gd.xl = hl;
     gd.xsum = hsum;
@@ -481,8 +646,8 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
     gd.out = ybuf;
     gd.out_ld = (uint32_t)d;
     if (e == cudaSuccess)
-        e = launch_k(c, "moe_gemm_down", k_moe_gemm<1>, dim3((uint32_t)(d / kGM), (uint32_t)max_tiles),
-                     dim3(kGThreads), (size_t)kGSmem, gd);
+        e = launch_k(c, "moe_gemm_down", k_moe_gemm<1>, dim3((uint32_t)c.num_sms), dim3(kGThreadsV2),
+                     (size_t)kGSmem, gd);
     if (e == cudaSuccess)
         e = launch_k(c, "moe_gemm_combine", k_gemm_combine, dim3((uint32_t)((d + 255) / 256), T), dim3(256), 0,
                      (const float *)ybuf, (uint32_t)d, (const uint32_t *)p.pair_pos, w, k, resid, out);
