@@ -465,6 +465,7 @@ __global__ void __launch_bounds__(256) k_gemm_prep(const float *src, uint32_t K,
     const uint32_t row = blockIdx.x;
     const float *s = src + (size_t)row * K;
     float amax = 0.0f;
+#pragma unroll 8
     for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) amax = fmaxf(amax, fabsf(s[i]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -491,22 +492,40 @@ __global__ void __launch_bounds__(256) k_gemm_prep(const float *src, uint32_t K,
         *reinterpret_cast<uint4 *>(xl + (size_t)row * K + 8 * m) = *reinterpret_cast<uint4 *>(l);
     }
     for (uint32_t j = threadIdx.x; j < K / 32; j += blockDim.x) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) v[i] = s[32 * j + i];
         float t = 0.0f;
-        for (int i = 0; i < 32; i++) t += s[32 * j + i] * scale;
+#pragma unroll
+        for (int i = 0; i < 32; i++) t += v[i] * scale;
         xsum[(size_t)row * (K / 32) + j] = t;
     }
     if (threadIdx.x == 0) xinv[row] = ldexpf(1.0f, ex);
 }
 
 // ── tile list: (active expert slot, first position) per 32 positions ───────
-__global__ void k_gemm_tiles(MoePlan p, uint2 *tiles, uint32_t *n_tiles) {
+// One block of kRouterMaxE threads: thread s counts the tiles of active slot
+// s, a block-wide exclusive scan places them.
+__global__ void __launch_bounds__(kRouterMaxE) k_gemm_tiles(MoePlan p, uint2 *tiles, uint32_t *n_tiles) {
+    __shared__ uint32_t s_warp[kRouterMaxE / 32];
     pdl_wait();
-    if (threadIdx.x != 0) return;
-    uint32_t n = 0;
+    const uint32_t s = threadIdx.x, lane = s & 31, warp = s >> 5;
     const uint32_t na = *p.n_active;
-    for (uint32_t s = 0; s < na; s++)
-        for (uint32_t n0 = 0; n0 < p.act_cnt[s]; n0 += kGN) tiles[n++] = make_uint2(s, n0);
-    *n_tiles = n;
+    const uint32_t cnt = s < na ? p.act_cnt[s] : 0;
+    const uint32_t nt = (cnt + kGN - 1) / kGN;
+    uint32_t incl = nt;  // inclusive scan within the warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= (uint32_t)o) incl += v;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    uint32_t base = 0;
+    for (uint32_t w = 0; w < warp; w++) base += s_warp[w];
+    const uint32_t first = base + incl - nt;
+    for (uint32_t i = 0; i < nt; i++) tiles[first + i] = make_uint2(s, i * kGN);
+    if (s == blockDim.x - 1) *n_tiles = base + incl;
 }
 
 // ── weighted combine in slot order (+ residual) ─────────────────────────────
@@ -558,7 +577,8 @@ bool encode_rows(CUtensorMap *map, const void *base, uint64_t pitch, uint64_t to
 }  // namespace
 
 bool moe_gemm_supported(const DevMat &gate, const DevMat &down, uint64_t F) {
-    return gate.type == T_Q4_K && down.type == T_Q4_K && gate.cols % 256 == 0 && F % 256 == 0 &&
+    return gate.type == T_Q4_K && down.type == T_Q4_K && gate.n_experts <= (uint32_t)kRouterMaxE &&
+           gate.cols % 256 == 0 && F % 256 == 0 &&
            gate.cols <= 256u * kGMaxSb && F <= 256u * kGMaxSb && down.rows % kGM == 0;
 }
 
@@ -596,7 +616,7 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
     float *hinv = reinterpret_cast<float *>(take(P * 4));
     float *ybuf = reinterpret_cast<float *>(take(P * d * 4));
 
-    cudaError_t e = launch_k(c, "moe_gemm_tiles", k_gemm_tiles, dim3(1), dim3(32), 0, p, tiles, n_tiles);
+    cudaError_t e = launch_k(c, "moe_gemm_tiles", k_gemm_tiles, dim3(1), dim3(kRouterMaxE), 0, p, tiles, n_tiles);
     if (e == cudaSuccess)
         e = launch_k(c, "moe_gemm_prep", k_gemm_prep, dim3(T), dim3(256), 0, x, (uint32_t)d, xh, xl, xsum, xinv);
     GemmArgs g;

@@ -10,8 +10,9 @@
 
 namespace lt {
 
-constexpr int kRouterWarps = 4;  // experts per CTA
-constexpr int kRouterTok = 4;    // tokens per CTA (one warp each for norm and top-k)
+constexpr int kRouterWarps = 8;  // experts per CTA
+constexpr int kRouterTok = 4;    // tokens per CTA (one warp each for the top-k)
+constexpr int kRouterNormThreads = 128;  // RMSNorm reduction width (the decode kernel uses the same)
 
 uint32_t router_token_groups(uint32_t ntok) { return (ntok + kRouterTok - 1) / kRouterTok; }
 
@@ -53,9 +54,11 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(RouterArgs a) {
         w0[j] = (e < a.E && 32u * j < n32) ? __ldg(a.W + (size_t)e * a.w_ld + 32 * j + lane) : 0.0f;
     if (a.norm_w) {
         if ((cols & 3) == 0 && (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0) {
+#pragma unroll 8
             for (uint32_t i = threadIdx.x; i < cols / 4; i += blockDim.x)
                 reinterpret_cast<float4 *>(nwsm)[i] = __ldg(reinterpret_cast<const float4 *>(a.norm_w) + i);
         } else {
+#pragma unroll 8
             for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) nwsm[i] = __ldg(a.norm_w + i);
         }
     }
@@ -65,9 +68,11 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(RouterArgs a) {
         const float *xt = a.x + (size_t)t0 * cols;
         const uint32_t n = nt * cols;
         if ((cols & 3) == 0 && (reinterpret_cast<uintptr_t>(xt) & 15) == 0) {
+#pragma unroll 8
             for (uint32_t i = threadIdx.x; i < n / 4; i += blockDim.x)
                 reinterpret_cast<float4 *>(xsm)[i] = reinterpret_cast<const float4 *>(xt)[i];
         } else {
+#pragma unroll 8
             for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) xsm[i] = xt[i];
         }
     }
@@ -77,17 +82,18 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(RouterArgs a) {
 #pragma unroll
         for (int tt = 0; tt < kRouterTok; tt++) {
             ss[tt] = 0.0f;
-            if (tt < (int)nt)
-                for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) ss[tt] += xsm[tt * cols + i] * xsm[tt * cols + i];
+            if (tt < (int)nt && threadIdx.x < kRouterNormThreads)
+                for (uint32_t i = threadIdx.x; i < cols; i += kRouterNormThreads)
+                    ss[tt] += xsm[tt * cols + i] * xsm[tt * cols + i];
             ss[tt] = warp_sum(ss[tt]);
         }
-        if (lane == 0)
+        if (lane == 0 && warp < kRouterNormThreads / 32)
 #pragma unroll
             for (int tt = 0; tt < kRouterTok; tt++) s_ss[warp][tt] = ss[tt];
         __syncthreads();
         if (threadIdx.x < nt) {
             float s = 0.0f;
-            for (int w = 0; w < kRouterWarps; w++) s += s_ss[w][threadIdx.x];
+            for (int w = 0; w < kRouterNormThreads / 32; w++) s += s_ss[w][threadIdx.x];
             s_rms[threadIdx.x] = 1.0f / sqrtf(s / (float)cols + a.eps);
         }
         __syncthreads();
