@@ -61,6 +61,16 @@ def measured_peaks() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
+def measured_tflops() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return 1590.0, "fallback"
+
+
 def ncu_traffic() -> dict | None:
     p = REPO / "profiles" / "ncu_summary.json"
     if p.exists():
@@ -258,6 +268,8 @@ def main() -> None:
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline work (rank 0, N=1)")
     ap.add_argument("--profile-steps", type=int, default=5)
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--prefill-tokens", type=int, default=512, help="T of the prefill measurement (0: skip)")
+    ap.add_argument("--prefill-layers", type=int, default=8)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -404,6 +416,15 @@ def main() -> None:
                "sample": f"{n} tokens x {args.layers} layers in {dt:.1f}s, {distinct} distinct host weight sets "
                          f"cycled (C restatement of the Zig CPU path; zig absent)"}
 
+    if graph is not None:
+        graph.free()
+        graph = None
+
+    # ---- prefill: T tokens through the MoE blocks (tensor-core expert GEMM) ----
+    prefill = None
+    if args.prefill_tokens > 0:
+        prefill = measure_prefill(args, pkg, ctx, torch, stream, gen, layers, rank, world, dist)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -416,18 +437,102 @@ def main() -> None:
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": int(round(args.steps * launches_per_step)), "clocks": clocks,
             "kernels_profiled": kernels, "layer_bytes": layer_bytes,
-            "graph": graph is not None,
+            "graph": not args.no_graph, "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
 
-    if graph is not None:
-        graph.free()
     for L in layers:
         for t in (L.router, L.gate, L.up, L.down):
             t.free()
     ctx.close()
     if dist is not None:
         dist.destroy_process_group()
+
+
+def measure_prefill(args, pkg, ctx, torch, stream, gen, layers, rank, world, dist) -> dict:
+    """T prompt tokens through `prefill_layers` MoE blocks in place (router,
+    dispatch, tensor-core gate/up and down GEMMs, combine, residual); value =
+    tokens per second through one MoE layer, all ranks (replicas)."""
+    T = args.prefill_tokens
+    nl = min(args.prefill_layers, len(layers))
+    xp = torch.randn(T, D_MODEL, device="cuda", generator=gen)
+    xp0 = xp.clone()
+
+    def pstep():
+        for L in layers[:nl]:
+            ctx.moe_block(L.router, L.gate, L.up, L.down, pkg.ACT_SILU, True, None, L.norm, 1e-6, xp, T, TOP_K, xp)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            xp.copy_(xp0)
+            pstep()
+    ctx.sync()
+    reps = max(1, args.steps // 10)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(reps):
+        pstep()
+    ev1.record(stream)
+    stream.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_layer = ms / (reps * nl)
+    ctx.sync()
+    ctx.profile(True)
+    ctx.profile_reset()
+    pstep()
+    ctx.sync()
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    ctx.profile_reset()
+    k_us = {k: 1e3 * v["total_ms"] / v["count"] for k, v in prof.items()}
+    gemm_us = k_us.get("moe_gemm_gate_up", 0.0) + k_us.get("moe_gemm_down", 0.0)
+    flops = 2.0 * T * TOP_K * 3 * D_EXPERT * D_MODEL  # gate + up + down, algorithmic
+    peak, kind = measured_tflops()
+    out = {
+        "metric": f"MoE layer prefill tok/s (config 1, T={T})", "value": world * T / (ms_layer / 1e3),
+        "unit": "tok/s", "ms_per_layer": ms_layer, "layers_timed": nl, "reps": reps,
+        "stack_equivalent_tok_s": world * T / (ms_layer / 1e3) / args.layers,
+        "kernels_us": {k: round(v, 1) for k, v in k_us.items()},
+        "roofline": {"kernel": "moe_gemm_gate_up + moe_gemm_down", "bound": "tensor",
+                     "achieved": flops / (gemm_us * 1e-6) / 1e12 if gemm_us else None, "peak": peak,
+                     "unit": "TFLOP/s", "peak_kind": kind,
+                     "frac": (flops / (gemm_us * 1e-6) / 1e12) / peak if gemm_us else None,
+                     "algorithmic_flops": flops, "traffic": None,
+                     "note": "f16 tcgen05 MMAs; the activation's lo plane doubles the issued MMA work"},
+    }
+    if rank == 0 and world == 1 and args.cpu_budget > 0:
+        out["cpu_baseline"] = cpu_prefill_rate(min(args.cpu_budget, 10.0))
+    return out
+
+
+def cpu_prefill_rate(budget_s: float) -> dict:
+    """The CPU restatement on a bounded sample of the same prefill: batches of
+    16 tokens through one MoE layer (router + experts), all host threads."""
+    sys.path.insert(0, str(REPO / "tests"))
+    oracle = importlib.import_module("oracle_lib")
+    synth = importlib.import_module("llmtoy-zig_b200.synth")
+    rng = np.random.Generator(np.random.PCG64(synth.config_seed(1) + 77))
+    L = synth.MoeLayer(rng, D_MODEL, N_EXPERTS, D_EXPERT)
+    threads = os.cpu_count() or 1
+    pool = oracle.Pool(threads)
+    x = rng.normal(0, 1, size=(16, D_MODEL)).astype(np.float32)
+    oracle.moe_layer(L, x, TOP_K, True, 0, None, pool)
+    t0 = time.perf_counter()
+    n = 0
+    while n == 0 or time.perf_counter() - t0 < budget_s:
+        oracle.moe_layer(L, x, TOP_K, True, 0, None, pool)
+        n += 1
+    dt = time.perf_counter() - t0
+    pool.close()
+    return {"value": 16 * n / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{n} batches of 16 tokens through one config-1 MoE layer in {dt:.1f}s"}
 
 
 if __name__ == "__main__":
