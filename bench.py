@@ -270,6 +270,9 @@ def main() -> None:
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--prefill-tokens", type=int, default=512, help="T of the prefill measurement (0: skip)")
     ap.add_argument("--prefill-layers", type=int, default=8)
+    ap.add_argument("--ep-tokens", type=int, default=8 * 2048,
+                    help="config 4: prompt tokens over all ranks, experts sharded 128/N (0: skip)")
+    ap.add_argument("--ep-layers", type=int, default=2)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -425,6 +428,10 @@ def main() -> None:
     if args.prefill_tokens > 0:
         prefill = measure_prefill(args, pkg, ctx, torch, stream, gen, layers, rank, world, dist)
 
+    ep_prefill = None
+    if args.ep_tokens > 0:
+        ep_prefill = measure_ep_prefill(args, pkg, torch, stream, rank, world, local, dist)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -437,7 +444,7 @@ def main() -> None:
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": int(round(args.steps * launches_per_step)), "clocks": clocks,
             "kernels_profiled": kernels, "layer_bytes": layer_bytes,
-            "graph": not args.no_graph, "prefill": prefill,
+            "graph": not args.no_graph, "prefill": prefill, "ep_prefill": ep_prefill,
         }
         print(json.dumps(line), flush=True)
 
@@ -509,6 +516,164 @@ def measure_prefill(args, pkg, ctx, torch, stream, gen, layers, rank, world, dis
     }
     if rank == 0 and world == 1 and args.cpu_budget > 0:
         out["cpu_baseline"] = cpu_prefill_rate(min(args.cpu_budget, 10.0))
+    return out
+
+
+def zipf_router(torch, n_experts: int, d: int, s: float, mu: float, seed: int):
+    """Router weights (replicated: the same seed on every rank) whose logits
+    carry a bias b_e = 0.9 * log(1 / rank_e^s) along a fixed unit direction u,
+    with expert ranks a seeded permutation; hidden states get mu * u added, so
+    after the RMSNorm each token's logit of expert e shifts by about b_e and
+    expert popularity falls off like Zipf(s).  0.9 is the spread of the
+    unbiased logits (N(0, 0.02^2) weights over 2048 unit-variance inputs)."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    base = torch.randn(n_experts, d, device="cuda", generator=g) * 0.02
+    u = torch.randn(d, device="cuda", generator=g)
+    u = u / u.norm()
+    order = torch.randperm(n_experts, device="cuda", generator=g)
+    ranks = torch.empty(n_experts, device="cuda")
+    ranks[order] = torch.arange(1, n_experts + 1, device="cuda", dtype=torch.float32)
+    b = -0.9 * s * torch.log(ranks)
+    b = b - b.mean()
+    rms = (1.0 + mu * mu / d) ** 0.5
+    return (base + (b * rms / mu)[:, None] * u[None, :]).contiguous(), u
+
+
+def measure_ep_prefill(args, pkg, torch, stream, rank, world, local, dist) -> dict:
+    """Config 4: args.ep_tokens prompt tokens (8 sequences x 2048) through
+    args.ep_layers MoE blocks of the config-2 shape, tokens split evenly over
+    the ranks, experts sharded 128/N, Zipf(1.1)-biased routing.  N = 1 runs
+    the single-device path (no exchange); N > 1 the expert-parallel layer
+    (llmtoy-zig_b200/ep.py: dispatch, NCCL all-to-all-v of rows, local
+    grouped GEMM, all-to-all-v back, combine).  Each layer reads the same
+    input (out = x + moe(rmsnorm(x))), so every step routes alike.  value =
+    total tokens through one layer per second (strong scaling: the total is
+    fixed)."""
+    ep = importlib.import_module("llmtoy-zig_b200.ep")
+    G = args.ep_tokens
+    if G % world:
+        return {"skipped": f"{G} tokens do not split over {world} ranks"}
+    T = G // world
+    lo, hi = ep.expert_range(N_EXPERTS, rank, world)
+    ne = hi - lo
+    mu = 4.0
+    ctx = pkg.Context(local)
+    out: dict = {}
+    with torch.cuda.stream(stream):
+        ops = ep.DeviceOps(ctx, f"cuda:{local}")
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(0x11A70004 + 1000 * rank)
+        layers = []
+        for li in range(args.ep_layers):
+            rw, u = zipf_router(torch, N_EXPERTS, D_MODEL, 1.1, mu, 0x11A74000 + li)
+            router = ctx.upload_device(rw.view(torch.uint8).view(-1), pkg.F32, N_EXPERTS, D_MODEL)
+            del rw
+            g = q4k_bytes_device(torch, gen, ne * D_EXPERT, D_MODEL)
+            gate = ctx.upload_device(g, pkg.Q4_K, D_EXPERT, D_MODEL, ne)
+            g = q4k_bytes_device(torch, gen, ne * D_EXPERT, D_MODEL)
+            up = ctx.upload_device(g, pkg.Q4_K, D_EXPERT, D_MODEL, ne)
+            g = q4k_bytes_device(torch, gen, ne * D_MODEL, D_EXPERT)
+            down = ctx.upload_device(g, pkg.Q4_K, D_MODEL, D_EXPERT, ne)
+            del g
+            layers.append((ep.EPLayer(router=router, gate=gate, up=up, down=down, n_experts=N_EXPERTS,
+                                      d_model=D_MODEL, norm_w=torch.ones(D_MODEL, device="cuda")), u))
+        x = torch.randn(T, D_MODEL, device="cuda", generator=gen) + mu * layers[0][1][None, :]
+        moe = ep.ExpertParallelMoE(ops, TOP_K)
+
+        a2a_ms = []
+
+        def timed_a2a(o, i, os_=None, is_=None):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            dist.all_to_all_single(o, i, os_, is_)
+            e1.record()
+            a2a_ms.append((e0, e1, (o.numel() + i.numel()) * o.element_size()))
+
+        def pstep():
+            for L, _ in layers:
+                moe.forward(L, x)
+
+        for _ in range(args.warmup):
+            pstep()
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        reps = max(1, args.steps // 10)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for _ in range(reps):
+            pstep()
+        ev1.record()
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1)
+        if dist is not None:
+            t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        ms_layer = ms / (reps * args.ep_layers)
+
+        # one more pass with the kernel profiler and the exchanges timed alone
+        ctx.profile(True)
+        ctx.profile_reset()
+        if world > 1:
+            moe._a2a = timed_a2a
+        for L, _ in layers:
+            moe.forward(L, x)
+        torch.cuda.synchronize()
+        prof = ctx.profile_read()
+        ctx.profile(False)
+        k_us = {k: 1e3 * v["total_ms"] / v["count"] for k, v in prof.items()}
+        k_layer_us = sum(v["total_ms"] for v in prof.values()) * 1e3 / args.ep_layers
+        recv = torch.tensor([float(moe.last_stats.get("received_pairs", T * TOP_K))], device="cuda")
+        if world > 1:
+            a2a_us = sum(e0.elapsed_time(e1) for e0, e1, _ in a2a_ms) * 1e3 / args.ep_layers
+            a2a_bytes = sum(b for _, _, b in a2a_ms) / args.ep_layers
+            allr = [torch.zeros_like(recv) for _ in range(world)]
+            dist.all_gather(allr, recv)
+            loads = [float(t.item()) for t in allr]
+        else:
+            a2a_us, a2a_bytes, loads = 0.0, 0, [float(recv.item())]
+        # expert popularity of the biased router over this rank's tokens
+        xn = torch.empty_like(x)
+        ctx.rmsnorm(x, layers[0][0].norm_w, 1e-6, D_MODEL, T, xn)
+        ids = torch.empty(T, TOP_K, dtype=torch.int32, device="cuda")
+        wts = torch.empty(T, TOP_K, device="cuda")
+        ctx.moe_route(layers[0][0].router, xn, T, TOP_K, True, None, ids, wts)
+        cnt = torch.bincount(ids.view(-1).long(), minlength=N_EXPERTS).float()
+        if dist is not None:
+            dist.all_reduce(cnt)
+        torch.cuda.synchronize()
+    gemm_us = k_us.get("moe_gemm_gate_up", 0.0) + k_us.get("moe_gemm_down", 0.0)
+    flops_rank = 2.0 * max(loads) * 3 * D_EXPERT * D_MODEL
+    peak, kind = measured_tflops()
+    mean_load = sum(loads) / len(loads)
+    out = {
+        "metric": f"expert-parallel prefill tok/s (config 4: {G} tokens, 128 experts / {world} GPUs, Zipf 1.1)",
+        "value": G / (ms_layer / 1e3), "unit": "tok/s", "n_gpus": world, "scaling": "strong",
+        "ms_per_layer": ms_layer, "layers_timed": args.ep_layers, "reps": reps,
+        "tokens_per_rank": T, "experts_per_rank": ne,
+        "path": "single-device lt_moe_block" if world == 1 else "ExpertParallelMoE over NCCL all_to_all_single",
+        "kernels_us": {k: round(v, 1) for k, v in k_us.items()}, "kernel_us_per_layer": k_layer_us,
+        "load_pairs_per_rank": loads, "load_imbalance_max_over_mean": max(loads) / mean_load,
+        "expert_popularity_max_over_mean": float(cnt.max() / cnt.mean()),
+        "expert_popularity_top8_share": float(cnt.sort(descending=True).values[:8].sum() / cnt.sum()),
+        "roofline": {"kernel": "moe_gemm_gate_up + moe_gemm_down (busiest rank)", "bound": "tensor",
+                     "achieved": flops_rank / (gemm_us * 1e-6) / 1e12 if gemm_us else None, "peak": peak,
+                     "unit": "TFLOP/s", "peak_kind": kind,
+                     "frac": flops_rank / (gemm_us * 1e-6) / 1e12 / peak if gemm_us else None},
+    }
+    if world > 1:
+        out["all_to_all"] = {"us_per_layer": a2a_us, "bytes_per_layer_per_rank": a2a_bytes,
+                             "gbs": a2a_bytes / (a2a_us * 1e-6) / 1e9 if a2a_us else None,
+                             "nvlink_ref_gbs": 770.0,
+                             "note": "rank-0 view: bytes sent + received per rank over the time of its four "
+                                     "all_to_all_single calls (counts, rows, ids, results)"}
+    for L, _ in layers:
+        for t_ in (L.router, L.gate, L.up, L.down):
+            t_.free()
+    ctx.close()
     return out
 
 

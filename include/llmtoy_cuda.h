@@ -229,6 +229,35 @@ lt_status lt_moe_ffn_noalloc(void *cuda_stream, const void *gate, const void *up
                              const float *dev_x, uint32_t ntok, const uint32_t *dev_ids,
                              const float *dev_w, uint32_t k, float *dev_out);
 
+/* ── expert parallelism building blocks ──────────────────────────────────────
+ * No counterpart in the reference, whose MoE runs on one device: these let a
+ * host shard the experts across ranks (experts [r*E/n, (r+1)*E/n) on rank r)
+ * and exchange tokens with an all-to-all of its own (NCCL, or any transport).
+ * Per layer: lt_moe_route -> lt_ep_dispatch -> lt_gather_rows (send buffer)
+ * -> all-to-all (rows and local ids) -> lt_moe_ffn on the received rows with
+ * k = 1 and weight 1 -> all-to-all back -> lt_moe_combine. */
+
+/* Stable sort of the ntok*k (token, slot) pairs of ids [ntok][k] by
+ * destination rank.  Outputs (device): send_counts[nranks] pairs per rank,
+ * and per send position send_token (the pair's token) and send_local (its
+ * expert index on the destination rank); pair_pos[ntok*k] is the send
+ * position of each pair.  n_experts % nranks == 0, nranks <= 8. */
+lt_status lt_ep_dispatch(lt_ctx *ctx, const uint32_t *dev_ids, uint32_t ntok, uint32_t k,
+                         uint32_t n_experts, uint32_t nranks, uint32_t *dev_send_counts,
+                         uint32_t *dev_send_token, uint32_t *dev_send_local,
+                         uint32_t *dev_pair_pos);
+
+/* dev_dst[i][:] = dev_src[dev_idx[i]][:] for i < n rows of cols floats
+ * (cols % 4 == 0). */
+lt_status lt_gather_rows(lt_ctx *ctx, const float *dev_src, uint64_t cols, const uint32_t *dev_idx,
+                         uint32_t n, float *dev_dst);
+
+/* Weighted combine in slot order (forward.zig:463-479):
+ * out[t][:] = (resid ? resid[t][:] : 0) + sum_s w[t][s] * y[pair_pos[t*k + s]][:]. */
+lt_status lt_moe_combine(lt_ctx *ctx, const float *dev_y, uint64_t cols, const uint32_t *dev_pair_pos,
+                         const float *dev_w, uint32_t ntok, uint32_t k, const float *dev_resid,
+                         float *dev_out);
+
 /* ── host-buffer entry points (synchronous) ─────────────────────────────────
  * Same semantics with HOST vectors, copies included: the shape of the
  * reference's own CPU calls, for callers that keep activations on the host. */

@@ -33,6 +33,7 @@ EXPORTS = [
     "lt_rmsnorm", "lt_softmax", "lt_moe_route", "lt_moe_ffn", "lt_moe_forward", "lt_moe_block", "lt_argmax",
     "lt_profile_enable", "lt_profile_read", "lt_profile_reset", "lt_capture_begin", "lt_capture_end",
     "lt_graph_launch", "lt_graph_free", "lt_moe_ffn_noalloc", "lt_quant_matvec_host", "lt_moe_forward_host",
+    "lt_ep_dispatch", "lt_gather_rows", "lt_moe_combine",
 ]
 
 
@@ -94,6 +95,9 @@ def load_library() -> ctypes.CDLL:
         "lt_graph_launch": (I, [P, P]),
         "lt_graph_free": (I, [P, P]),
         "lt_moe_ffn_noalloc": (I, [P, P, P, P, U32, U32, U32, U64, U64, I, P, U32, P, P, U32, P]),
+        "lt_ep_dispatch": (I, [P, P, U32, U32, U32, U32, P, P, P, P]),
+        "lt_gather_rows": (I, [P, P, U64, P, U32, P]),
+        "lt_moe_combine": (I, [P, P, U64, P, P, U32, U32, P, P]),
         "lt_quant_matvec_host": (I, [P, P, P, U32, P, U64, U64]),
         "lt_moe_forward_host": (I, [P, P, P, P, P, I, I, P, P, U32, U32, P, P, P]),
     }
@@ -258,6 +262,19 @@ class Context:
         self._check(self.lib.lt_moe_block(self.ptr, router.handle, gate.handle, up.handle if up else None,
                                           down.handle, act, int(norm_topk), _ptr(expert_scale), _ptr(norm_w), eps,
                                           _ptr(x), ntok, k, _ptr(out), _ptr(ids), _ptr(w)))
+
+    # -- expert parallelism building blocks (see ep.py) --------------------
+    def ep_dispatch(self, ids, ntok: int, k: int, n_experts: int, nranks: int, send_counts, send_token, send_local,
+                    pair_pos) -> None:
+        self._check(self.lib.lt_ep_dispatch(self.ptr, _ptr(ids), ntok, k, n_experts, nranks, _ptr(send_counts),
+                                            _ptr(send_token), _ptr(send_local), _ptr(pair_pos)))
+
+    def gather_rows(self, src, cols: int, idx, n: int, dst) -> None:
+        self._check(self.lib.lt_gather_rows(self.ptr, _ptr(src), cols, _ptr(idx), n, _ptr(dst)))
+
+    def moe_combine(self, y, cols: int, pair_pos, w, ntok: int, k: int, resid, out) -> None:
+        self._check(self.lib.lt_moe_combine(self.ptr, _ptr(y), cols, _ptr(pair_pos), _ptr(w), ntok, k, _ptr(resid),
+                                            _ptr(out)))
 
     # -- kernel timing / graph capture -------------------------------------
     def profile(self, on: bool) -> None:

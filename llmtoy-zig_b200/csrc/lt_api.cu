@@ -657,6 +657,8 @@ static lt_status ffn_impl(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *u
                                                 out, s.gemm),
                         "moe gemm");
     }
+    if (ntok > 65535u)  // the CUDA-core down kernel puts tokens in grid.y
+        return fail(ctx, LT_EINVAL, "moe: %u tokens exceed 65535 outside the tensor-core path", ntok);
     st = ensure_counters(ctx, lt::kMoeCounterBase + s.counters);
     if (st != LT_OK) return st;
     if (!direct) {
@@ -770,6 +772,45 @@ lt_status lt_moe_block(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *ga
     if (!dev_norm_w) return fail(ctx, LT_EINVAL, "lt_moe_block: null norm weights");
     return forward_impl(ctx, router, gate, up, down, act, norm_topk, dev_expert_scale, dev_norm_w, eps, 1, dev_x,
                         ntok, k, dev_out, dev_ids, dev_w);
+}
+
+lt_status lt_ep_dispatch(lt_ctx *ctx, const uint32_t *dev_ids, uint32_t ntok, uint32_t k, uint32_t n_experts,
+                         uint32_t nranks, uint32_t *dev_send_counts, uint32_t *dev_send_token,
+                         uint32_t *dev_send_local, uint32_t *dev_pair_pos) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!dev_ids || !dev_send_counts || !dev_send_token || !dev_send_local || !dev_pair_pos)
+        return fail(ctx, LT_EINVAL, "lt_ep_dispatch: null pointer");
+    if (nranks == 0 || nranks > 8 || n_experts == 0 || n_experts % nranks != 0 || k == 0)
+        return fail(ctx, LT_EINVAL, "lt_ep_dispatch: %u experts over %u ranks", n_experts, nranks);
+    if (ntok == 0)  // nothing to send: every count is zero
+        return launched(ctx, cudaMemsetAsync(dev_send_counts, 0, nranks * sizeof(uint32_t), ctx->stream),
+                        "ep dispatch counts");
+    return launched(ctx,
+                    lt::launch_ep_dispatch(cfg_of(ctx), dev_ids, ntok, k, n_experts, nranks, dev_send_counts,
+                                           dev_send_token, dev_send_local, dev_pair_pos),
+                    "ep dispatch");
+}
+
+lt_status lt_gather_rows(lt_ctx *ctx, const float *dev_src, uint64_t cols, const uint32_t *dev_idx, uint32_t n,
+                         float *dev_dst) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!dev_src || !dev_idx || !dev_dst) return fail(ctx, LT_EINVAL, "lt_gather_rows: null pointer");
+    if (cols == 0 || cols % 4 != 0) return fail(ctx, LT_EINVAL, "lt_gather_rows: cols %llu", (unsigned long long)cols);
+    if (n == 0) return LT_OK;
+    return launched(ctx, lt::launch_gather_rows(cfg_of(ctx), dev_src, cols, dev_idx, n, dev_dst), "gather rows");
+}
+
+lt_status lt_moe_combine(lt_ctx *ctx, const float *dev_y, uint64_t cols, const uint32_t *dev_pair_pos,
+                         const float *dev_w, uint32_t ntok, uint32_t k, const float *dev_resid, float *dev_out) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!dev_y || !dev_pair_pos || !dev_w || !dev_out) return fail(ctx, LT_EINVAL, "lt_moe_combine: null pointer");
+    if (cols == 0 || k == 0) return fail(ctx, LT_EINVAL, "lt_moe_combine: cols %llu, k %u", (unsigned long long)cols, k);
+    if (ntok == 0) return LT_OK;
+    return launched(ctx, lt::launch_combine(cfg_of(ctx), dev_y, cols, dev_pair_pos, dev_w, ntok, k, dev_resid, dev_out),
+                    "combine");
 }
 
 lt_status lt_quant_matvec_host(lt_ctx *ctx, float *out, const lt_tensor *mat, uint32_t expert, const float *vec,

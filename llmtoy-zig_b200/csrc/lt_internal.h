@@ -159,4 +159,15 @@ constexpr size_t kDecodeSmemLimit = 227 * 1024;
 bool moe_decode_fits(const DecodeParams &p, int num_sms);
 cudaError_t launch_moe_decode(const LaunchCfg &c, const DecodeParams &p);
 
+// out[t] = (resid ? resid[t] : 0) + sum_s w[t][s] * y[pair_pos[t*k + s]]  (slot order), D columns.
+cudaError_t launch_combine(const LaunchCfg &c, const float *y, uint64_t D, const uint32_t *pair_pos, const float *w,
+                           uint32_t ntok, uint32_t k, const float *resid, float *out);
+
+// Expert parallelism (lt_ep.cu): experts [r*E/nranks, (r+1)*E/nranks) live on rank r.
+cudaError_t launch_ep_dispatch(const LaunchCfg &c, const uint32_t *ids, uint32_t ntok, uint32_t k, uint32_t E,
+                               uint32_t nranks, uint32_t *send_counts, uint32_t *send_token, uint32_t *send_local,
+                               uint32_t *pair_pos);
+cudaError_t launch_gather_rows(const LaunchCfg &c, const float *src, uint64_t cols, const uint32_t *idx, uint32_t n,
+                               float *dst);
+
 }  // namespace lt

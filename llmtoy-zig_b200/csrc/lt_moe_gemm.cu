@@ -532,10 +532,11 @@ __global__ void __launch_bounds__(kRouterMaxE) k_gemm_tiles(MoePlan p, uint2 *ti
 __global__ void k_gemm_combine(const float *y, uint32_t D, const uint32_t *pair_pos, const float *w, uint32_t k,
                                const float *resid, float *out) {
     pdl_wait();
-    const uint32_t t = blockIdx.y, c = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t t = blockIdx.x, c = blockIdx.y * blockDim.x + threadIdx.x;  // token rows in x: no 65535 cap
     if (c >= D) return;
-    float o = 0.0f;  // moe_buf is zeroed, then += scale * down, slot by slot
-    for (uint32_t s = 0; s < k; s++) o += w[(size_t)t * k + s] * y[(size_t)pair_pos[(size_t)t * k + s] * D + c];
+    float o = 0.0f;  // moe_buf is zeroed, then += scale * down, slot by slot (no fused multiply-add)
+    for (uint32_t s = 0; s < k; s++)
+        o = __fadd_rn(o, __fmul_rn(w[(size_t)t * k + s], y[(size_t)pair_pos[(size_t)t * k + s] * D + c]));
     const size_t oi = (size_t)t * D + c;
     out[oi] = resid ? resid[oi] + o : o;
 }
@@ -575,6 +576,12 @@ bool encode_rows(CUtensorMap *map, const void *base, uint64_t pitch, uint64_t to
 }
 
 }  // namespace
+
+cudaError_t launch_combine(const LaunchCfg &c, const float *y, uint64_t D, const uint32_t *pair_pos, const float *w,
+                           uint32_t ntok, uint32_t k, const float *resid, float *out) {
+    return launch_k(c, "moe_combine", k_gemm_combine, dim3(ntok, (uint32_t)((D + 255) / 256)), dim3(256), 0, y,
+                    (uint32_t)D, pair_pos, w, k, resid, out);
+}
 
 bool moe_gemm_supported(const DevMat &gate, const DevMat &down, uint64_t F) {
     return gate.type == T_Q4_K && down.type == T_Q4_K && gate.n_experts <= (uint32_t)kRouterMaxE &&
@@ -669,7 +676,7 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
         e = launch_k(c, "moe_gemm_down", k_moe_gemm<1>, dim3((uint32_t)c.num_sms), dim3(kGThreadsV2),
                      (size_t)kGSmem, gd);
     if (e == cudaSuccess)
-        e = launch_k(c, "moe_gemm_combine", k_gemm_combine, dim3((uint32_t)((d + 255) / 256), T), dim3(256), 0,
+        e = launch_k(c, "moe_gemm_combine", k_gemm_combine, dim3(T, (uint32_t)((d + 255) / 256)), dim3(256), 0,
                      (const float *)ybuf, (uint32_t)d, (const uint32_t *)p.pair_pos, w, k, resid, out);
     return e;
 }
