@@ -78,7 +78,10 @@ int         lt_api_version(void);
 lt_status   lt_init(int device, lt_ctx **out);
 void        lt_free(lt_ctx *ctx);
 /* Use an existing cudaStream_t (passed as void*); NULL selects the
- * context's own stream. */
+ * context's own stream (non-blocking).  The legacy default stream is
+ * cudaStreamLegacy ((void *)1), the per-thread one cudaStreamPerThread
+ * ((void *)2); on those two the kernels launch without programmatic
+ * dependent launch. */
 lt_status   lt_set_stream(lt_ctx *ctx, void *cuda_stream);
 lt_status   lt_sync(lt_ctx *ctx);
 const char *lt_last_error(const lt_ctx *ctx);
@@ -257,6 +260,74 @@ lt_status lt_gather_rows(lt_ctx *ctx, const float *dev_src, uint64_t cols, const
 lt_status lt_moe_combine(lt_ctx *ctx, const float *dev_y, uint64_t cols, const uint32_t *dev_pair_pos,
                          const float *dev_w, uint32_t ntok, uint32_t k, const float *dev_resid,
                          float *dev_out);
+
+/* ── device buffers ──────────────────────────────────────────────────────────
+ * For hosts without a CUDA runtime of their own (the Zig forward loop, the
+ * C++ host in this package): activation buffers, KV caches and token streams.
+ * Copies are asynchronous on the context stream; lt_sync joins. */
+lt_status lt_device_alloc(lt_ctx *ctx, size_t bytes, void **dev_out);  /* zero-filled */
+lt_status lt_device_free(lt_ctx *ctx, void *dev);
+lt_status lt_copy_to_device(lt_ctx *ctx, void *dev_dst, const void *host_src, size_t bytes);
+lt_status lt_copy_to_host(lt_ctx *ctx, void *host_dst, const void *dev_src, size_t bytes);
+
+/* ── decode-step ops ─────────────────────────────────────────────────────────
+ * The pieces of one token of forwardOneModel (src/model/forward.zig:229-316)
+ * beyond the matvecs and the MoE block.  Each reads the token position from
+ * a device word (dev_pos), so one captured graph (lt_capture_begin) serves
+ * every step of a generation: the host writes the prompt into a device token
+ * stream once and replays the graph. */
+
+/* Geometry of one attention layer. */
+typedef struct lt_attn_cfg {
+    uint32_t n_heads, n_kv_heads, head_dim;   /* head_dim 64, 128 or 256 */
+    uint32_t rope_neox;  /* 0: consecutive pairs (rope.zig:14), 1: NeoX halves (rope.zig:56) */
+    float rope_theta;
+    float eps;           /* per-head Q/K RMSNorm epsilon */
+    float scale;         /* score scale: 1/sqrt(head_dim) (forward.zig:300), 1 for Gemma 4 */
+    uint32_t kv_cap;     /* positions per layer cache; slot = pos % kv_cap */
+    uint32_t window;     /* 0: attend to every position; else the last `window` (sliding) */
+} lt_attn_cfg;
+
+/* embedLookup (src/model/forward.zig:319-341): dev_out[cols] = dequantised
+ * row dev_tokens[*dev_pos] of emb.  An id beyond the table is reported by
+ * lt_sync as LT_EINVAL (the row read is row 0). */
+lt_status lt_embed(lt_ctx *ctx, const lt_tensor *emb, const uint32_t *dev_tokens,
+                   const uint32_t *dev_pos, float *dev_out);
+
+/* quantMatvec plus an addend of y's shape: y = W . x + add -- the residual
+ * `x += wo . attn` (forward.zig:304-305) or the Q/K/V biases (:285-287).
+ * dev_add may alias dev_y. */
+lt_status lt_qmatvec_add(lt_ctx *ctx, const lt_tensor *w, uint32_t expert, const float *dev_x,
+                         const float *dev_add, float *dev_y, uint32_t ntok);
+
+/* dev_qkv = [q (n_heads*hd) | k (n_kv*hd) | v (n_kv*hd)] of this position:
+ * per-head RMSNorm of q and k when their weights (head_dim floats) are
+ * given (gemma4/forward.zig:267-268), RoPE on q and k (rope.zig), q updated in
+ * place; k and v written to the caches at slot *dev_pos % kv_cap.  Caches are
+ * [kv_cap][n_kv*hd] f32. */
+lt_status lt_attn_prep(lt_ctx *ctx, const lt_attn_cfg *cfg, float *dev_qkv, const float *dev_q_norm,
+                       const float *dev_k_norm, const uint32_t *dev_pos, float *dev_k_cache,
+                       float *dev_v_cache);
+
+/* sdpAttn (src/ops/attn.zig:13-42) of every query head over the cached
+ * positions max(0, pos+1-window) .. pos (query head h reads KV head
+ * h / (n_heads / n_kv_heads)); dev_out[n_heads*hd]. */
+lt_status lt_attn_decode(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_q,
+                         const float *dev_k_cache, const float *dev_v_cache,
+                         const uint32_t *dev_pos, float *dev_out);
+
+/* The dense FFN block of a decoder layer (forward.zig:307-312):
+ * out = x + down . (act(gate . xn) * (up . xn)), xn = rmsnorm(x) * norm_w,
+ * for 2-D gate/up [F][d] and down [d][F].  dev_out may alias dev_x. */
+lt_status lt_ffn_block(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, const lt_tensor *down,
+                       int act, const float *dev_norm_w, float eps, const float *dev_x, uint32_t ntok,
+                       float *dev_out);
+
+/* greedy (sample.zig:11-17) as the last op of a decode step: with
+ * p = *dev_pos, dev_tokens[p + 1] = argmax(logits) unless p + 1 is still a
+ * prompt position (< *dev_n_prompt); then *dev_pos = p + 1. */
+lt_status lt_greedy_step(lt_ctx *ctx, const float *dev_logits, uint32_t n, uint32_t *dev_tokens,
+                         uint32_t *dev_pos, const uint32_t *dev_n_prompt);
 
 /* ── host-buffer entry points (synchronous) ─────────────────────────────────
  * Same semantics with HOST vectors, copies included: the shape of the

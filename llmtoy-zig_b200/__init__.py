@@ -34,6 +34,8 @@ EXPORTS = [
     "lt_profile_enable", "lt_profile_read", "lt_profile_reset", "lt_capture_begin", "lt_capture_end",
     "lt_graph_launch", "lt_graph_free", "lt_moe_ffn_noalloc", "lt_quant_matvec_host", "lt_moe_forward_host",
     "lt_ep_dispatch", "lt_gather_rows", "lt_moe_combine",
+    "lt_device_alloc", "lt_device_free", "lt_copy_to_device", "lt_copy_to_host",
+    "lt_embed", "lt_qmatvec_add", "lt_attn_prep", "lt_attn_decode", "lt_ffn_block", "lt_greedy_step",
 ]
 
 
@@ -47,6 +49,13 @@ class TensorDesc(ctypes.Structure):
     _fields_ = [("ggml_type", ctypes.c_uint32), ("n_experts", ctypes.c_uint32),
                 ("rows", ctypes.c_uint64), ("cols", ctypes.c_uint64),
                 ("row_bytes", ctypes.c_uint64), ("row_pitch", ctypes.c_uint64)]
+
+
+class AttnCfg(ctypes.Structure):
+    """lt_attn_cfg: geometry of one attention layer."""
+    _fields_ = [("n_heads", ctypes.c_uint32), ("n_kv_heads", ctypes.c_uint32), ("head_dim", ctypes.c_uint32),
+                ("rope_neox", ctypes.c_uint32), ("rope_theta", ctypes.c_float), ("eps", ctypes.c_float),
+                ("scale", ctypes.c_float), ("kv_cap", ctypes.c_uint32), ("window", ctypes.c_uint32)]
 
 
 _lib = None
@@ -98,6 +107,16 @@ def load_library() -> ctypes.CDLL:
         "lt_ep_dispatch": (I, [P, P, U32, U32, U32, U32, P, P, P, P]),
         "lt_gather_rows": (I, [P, P, U64, P, U32, P]),
         "lt_moe_combine": (I, [P, P, U64, P, P, U32, U32, P, P]),
+        "lt_device_alloc": (I, [P, SZ, ctypes.POINTER(P)]),
+        "lt_device_free": (I, [P, P]),
+        "lt_copy_to_device": (I, [P, P, P, SZ]),
+        "lt_copy_to_host": (I, [P, P, P, SZ]),
+        "lt_embed": (I, [P, P, P, P, P]),
+        "lt_qmatvec_add": (I, [P, P, U32, P, P, P, U32]),
+        "lt_attn_prep": (I, [P, ctypes.POINTER(AttnCfg), P, P, P, P, P, P]),
+        "lt_attn_decode": (I, [P, ctypes.POINTER(AttnCfg), P, P, P, P, P]),
+        "lt_greedy_step": (I, [P, P, U32, P, P, P]),
+        "lt_ffn_block": (I, [P, P, P, P, I, P, F, P, U32, P]),
         "lt_quant_matvec_host": (I, [P, P, P, U32, P, U64, U64]),
         "lt_moe_forward_host": (I, [P, P, P, P, P, I, I, P, P, U32, U32, P, P, P]),
     }
@@ -196,8 +215,14 @@ class Context:
         self.close()
 
     def set_stream(self, stream) -> None:
-        """Run ops on a cudaStream_t (int handle or torch.cuda.Stream); None: own stream."""
-        handle = getattr(stream, "cuda_stream", stream)
+        """Run ops on a cudaStream_t (int handle or torch.cuda.Stream); None: the context's own
+        stream.  Handle 0, torch's default stream, means the legacy default stream
+        (cudaStreamLegacy), so work torch queues there orders with these ops."""
+        if stream is None:
+            handle = None
+        else:
+            handle = getattr(stream, "cuda_stream", stream)
+            handle = handle or 1  # cudaStreamLegacy
         self._check(self.lib.lt_set_stream(self.ptr, handle))
 
     def sync(self) -> None:
@@ -275,6 +300,55 @@ class Context:
     def moe_combine(self, y, cols: int, pair_pos, w, ntok: int, k: int, resid, out) -> None:
         self._check(self.lib.lt_moe_combine(self.ptr, _ptr(y), cols, _ptr(pair_pos), _ptr(w), ntok, k, _ptr(resid),
                                             _ptr(out)))
+
+    # -- device buffers ----------------------------------------------------
+    def device_alloc(self, nbytes: int) -> int:
+        """A zero-filled device buffer (free with device_free)."""
+        p = ctypes.c_void_p()
+        self._check(self.lib.lt_device_alloc(self.ptr, nbytes, ctypes.byref(p)))
+        return p.value
+
+    def device_free(self, dev: int) -> None:
+        self._check(self.lib.lt_device_free(self.ptr, dev))
+
+    def copy_to_device(self, dev, host_array) -> None:
+        import numpy as np
+        a = np.ascontiguousarray(host_array)
+        self._check(self.lib.lt_copy_to_device(self.ptr, _ptr(dev), a.ctypes.data, a.nbytes))
+        self.sync()
+
+    def copy_to_host(self, dev, nbytes: int, dtype="float32"):
+        """nbytes at a device address -> numpy array of dtype (synchronises)."""
+        import numpy as np
+        out = np.empty(nbytes // np.dtype(dtype).itemsize, dtype=dtype)
+        self._check(self.lib.lt_copy_to_host(self.ptr, out.ctypes.data, _ptr(dev), out.nbytes))
+        self.sync()
+        return out
+
+    # -- decode-step ops ---------------------------------------------------
+    def embed(self, emb: Tensor, tokens, pos, out) -> None:
+        self._check(self.lib.lt_embed(self.ptr, emb.handle, _ptr(tokens), _ptr(pos), _ptr(out)))
+
+    def qmatvec_add(self, w: Tensor, x, add, y, ntok: int = 1, expert: int = 0) -> None:
+        self._check(self.lib.lt_qmatvec_add(self.ptr, w.handle, expert, _ptr(x), _ptr(add), _ptr(y), ntok))
+
+    def attn_prep(self, cfg: AttnCfg, qkv, q_norm, k_norm, pos, k_cache, v_cache) -> None:
+        self._check(self.lib.lt_attn_prep(self.ptr, ctypes.byref(cfg), _ptr(qkv), _ptr(q_norm), _ptr(k_norm),
+                                          _ptr(pos), _ptr(k_cache), _ptr(v_cache)))
+
+    def attn_decode(self, cfg: AttnCfg, q, k_cache, v_cache, pos, out) -> None:
+        self._check(self.lib.lt_attn_decode(self.ptr, ctypes.byref(cfg), _ptr(q), _ptr(k_cache), _ptr(v_cache),
+                                            _ptr(pos), _ptr(out)))
+
+    def ffn_block(self, gate: Tensor, up: Tensor, down: Tensor, act: int, norm_w, eps: float, x, ntok: int,
+                  out) -> None:
+        """out = x + down . (act(gate . xn) * (up . xn)), xn = rmsnorm(x) * norm_w (dense FFN block)."""
+        self._check(self.lib.lt_ffn_block(self.ptr, gate.handle, up.handle, down.handle, act, _ptr(norm_w), eps,
+                                          _ptr(x), ntok, _ptr(out)))
+
+    def greedy_step(self, logits, n: int, tokens, pos, n_prompt) -> None:
+        """n_prompt: a device word (the prompt length of the token stream)."""
+        self._check(self.lib.lt_greedy_step(self.ptr, _ptr(logits), n, _ptr(tokens), _ptr(pos), _ptr(n_prompt)))
 
     # -- kernel timing / graph capture -------------------------------------
     def profile(self, on: bool) -> None:

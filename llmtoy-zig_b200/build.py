@@ -75,6 +75,24 @@ def build_cuda(force: bool = False, verbose: bool = False) -> Path:
     return LIB
 
 
+HOST_LIB = PKG / "libllmtoy_host.so"
+
+
+def build_host(force: bool = False) -> Path:
+    """The C++ host decode loop (host/decoder.cpp), linked against the C ABI."""
+    srcs = sorted((PKG / "host").glob("*.cpp"))
+    deps = srcs + sorted((PKG / "host").glob("*.h")) + sorted(INCLUDE.glob("*.h")) + [LIB]
+    if force or _stale(HOST_LIB, deps):
+        cxx = os.environ.get("CXX", "g++")
+        cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-Wall", "-Wextra", f"-I{INCLUDE}",
+               *map(str, srcs), "-o", str(HOST_LIB), f"-L{PKG}", "-lllmtoy_cuda", "-Wl,-rpath,$ORIGIN"]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            sys.stderr.write(res.stdout + res.stderr)
+            raise RuntimeError("host library build failed")
+    return HOST_LIB
+
+
 def build_oracle() -> Path:
     res = subprocess.run(["make", "-s", "-C", str(REPO / "oracle")], capture_output=True, text=True)
     if res.returncode != 0:
@@ -89,6 +107,7 @@ def main() -> None:
     ap.add_argument("--verbose", action="store_true")
     a = ap.parse_args()
     print(build_cuda(a.force, a.verbose))
+    print(build_host(a.force))
     print(build_oracle())
 
 

@@ -32,6 +32,9 @@ struct lt_ctx {
     uint32_t tc_min_tokens = 64;     // batches of at least this many tokens use the tensor-core expert GEMM
     int *dev_err = nullptr;          // device error word written by kernels
     uint8_t *dec_sync = nullptr;     // counters and tagged logits of the persistent decode kernel
+    float *ones = nullptr;           // n_const slot weights of 1 (dense FFN blocks)
+    uint32_t *zeros = nullptr;       // n_const expert ids of 0
+    size_t n_const = 0;
     uint8_t *scratch = nullptr;      // activation scratch arena
     size_t scratch_bytes = 0;
     uint32_t *counters = nullptr;    // zero-initialised, kernels leave them zero
@@ -76,7 +79,10 @@ lt_status cuda_fail(lt_ctx *ctx, cudaError_t e, const char *what) {
 lt::LaunchCfg cfg_of(lt_ctx *ctx) {
     lt::LaunchCfg c;
     c.stream = ctx->stream;
-    c.pdl = ctx->pdl;
+    // No programmatic dependent launch on the default streams (legacy or
+    // per-thread): only on explicit streams.
+    c.pdl = ctx->pdl && ctx->stream != cudaStreamLegacy && ctx->stream != cudaStreamPerThread &&
+            ctx->stream != nullptr;
     c.dev_err = ctx->dev_err;
     c.num_sms = ctx->num_sms;
     c.prof = &ctx->prof;
@@ -125,6 +131,25 @@ lt_status ensure_counters(lt_ctx *ctx, size_t n) {
     LT_CUDA(ctx, cudaMalloc(&ctx->counters, n * 4), "cudaMalloc(counters)");
     LT_CUDA(ctx, cudaMemset(ctx->counters, 0, n * 4), "cudaMemset(counters)");
     ctx->n_counters = n;
+    return LT_OK;
+}
+
+// Constant slot weights (1) and expert ids (0) for n tokens.
+lt_status ensure_consts(lt_ctx *ctx, size_t n) {
+    if (n <= ctx->n_const) return LT_OK;
+    if (ctx->capturing) return fail(ctx, LT_EINVAL, "dense FFN for %zu tokens while capturing: run it once first", n);
+    LT_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    if (ctx->ones) cudaFree(ctx->ones);
+    if (ctx->zeros) cudaFree(ctx->zeros);
+    ctx->ones = nullptr;
+    ctx->zeros = nullptr;
+    ctx->n_const = 0;
+    n = (n + 1023) & ~(size_t)1023;
+    LT_CUDA(ctx, cudaMalloc(&ctx->ones, n * 4), "cudaMalloc(ones)");
+    LT_CUDA(ctx, cudaMalloc(&ctx->zeros, n * 4), "cudaMalloc(zeros)");
+    LT_CUDA(ctx, cudaMemsetAsync(ctx->zeros, 0, n * 4, ctx->stream), "cudaMemsetAsync");
+    LT_CUDA(ctx, lt::launch_fill_f32(ctx->stream, ctx->ones, n, 1.0f), "fill");
+    ctx->n_const = n;
     return LT_OK;
 }
 
@@ -287,6 +312,8 @@ void lt_free(lt_ctx *ctx) {
     if (ctx->counters) cudaFree(ctx->counters);
     if (ctx->dev_err) cudaFree(ctx->dev_err);
     if (ctx->dec_sync) cudaFree(ctx->dec_sync);
+    if (ctx->ones) cudaFree(ctx->ones);
+    if (ctx->zeros) cudaFree(ctx->zeros);
     if (ctx->pinned) cudaFreeHost(ctx->pinned);
     if (ctx->own) cudaStreamDestroy(ctx->own);
     delete ctx;
@@ -388,6 +415,7 @@ lt_status lt_sync(lt_ctx *ctx) {
     LT_CUDA(ctx, cudaMemcpy(&h, ctx->dev_err, 4, cudaMemcpyDeviceToHost), "read device error word");
     if (h != 0) {
         cudaMemset(ctx->dev_err, 0, 4);
+        if (h == lt::DEV_ERR_BAD_INDEX) return fail(ctx, LT_EINVAL, "a device-side index was out of range");
         return fail(ctx, LT_ETIMEOUT, "a device-side wait gave up (code %d)", h);
     }
     return LT_OK;
@@ -519,8 +547,8 @@ lt_status lt_dequant(lt_ctx *ctx, const lt_tensor *t, uint64_t row0, uint64_t nr
     return launched(ctx, lt::launch_dequant(cfg_of(ctx), t->m, row0, nrows, dev_out), "dequant");
 }
 
-lt_status lt_qmatvec(lt_ctx *ctx, const lt_tensor *w, uint32_t expert, const float *dev_x, float *dev_y,
-                     uint32_t ntok) {
+static lt_status qmatvec_impl(lt_ctx *ctx, const lt_tensor *w, uint32_t expert, const float *dev_x, float *dev_y,
+                              uint32_t ntok, const float *dev_add) {
     lt_status st = enter(ctx);
     if (st != LT_OK) return st;
     if (!w || !dev_x || !dev_y) return fail(ctx, LT_EINVAL, "lt_qmatvec: null pointer");
@@ -531,13 +559,18 @@ lt_status lt_qmatvec(lt_ctx *ctx, const lt_tensor *w, uint32_t expert, const flo
     if (w->m.rows > 0xffffffffull) return fail(ctx, LT_EINVAL, "lt_qmatvec: too many rows");
     const lt::LaunchCfg c = cfg_of(ctx);
     if (!quantized(w->m.type))
-        return launched(ctx, lt::launch_qmatvec(c, w->m, expert, nullptr, 0, dev_x, dev_y, ntok), "qmatvec");
+        return launched(ctx, lt::launch_qmatvec(c, w->m, expert, nullptr, 0, dev_x, dev_y, ntok, dev_add), "qmatvec");
     const uint64_t qp = lt::qact_row_pitch(w->m.cols);
     if ((st = ensure_scratch(ctx, al256((size_t)ntok * qp))) != LT_OK) return st;
     uint8_t *xq = ctx->scratch;
     st = launched(ctx, lt::launch_quantize(c, dev_x, (uint32_t)w->m.cols, ntok, xq, qp), "quantize");
     if (st != LT_OK) return st;
-    return launched(ctx, lt::launch_qmatvec(c, w->m, expert, xq, qp, dev_x, dev_y, ntok), "qmatvec");
+    return launched(ctx, lt::launch_qmatvec(c, w->m, expert, xq, qp, dev_x, dev_y, ntok, dev_add), "qmatvec");
+}
+
+lt_status lt_qmatvec(lt_ctx *ctx, const lt_tensor *w, uint32_t expert, const float *dev_x, float *dev_y,
+                     uint32_t ntok) {
+    return qmatvec_impl(ctx, w, expert, dev_x, dev_y, ntok, nullptr);
 }
 
 lt_status lt_rmsnorm(lt_ctx *ctx, const float *dev_x, const float *dev_w, float eps, uint32_t n, uint32_t ntok,
@@ -568,6 +601,135 @@ lt_status lt_argmax(lt_ctx *ctx, const float *dev_x, uint32_t n, uint32_t ntok, 
     float *pv = (float *)ctx->scratch;
     uint32_t *pi = (uint32_t *)(ctx->scratch + al256(part * 4));
     return launched(ctx, lt::launch_argmax(cfg_of(ctx), dev_x, n, ntok, dev_idx, pv, pi, ctx->counters), "argmax");
+}
+
+// ── device buffers ─────────────────────────────────────────────────────────
+
+lt_status lt_device_alloc(lt_ctx *ctx, size_t bytes, void **dev_out) {
+    lt_status st = enter_uncaptured(ctx, "lt_device_alloc");
+    if (st != LT_OK) return st;
+    if (!dev_out) return fail(ctx, LT_EINVAL, "lt_device_alloc: null output");
+    *dev_out = nullptr;
+    if (bytes == 0) return fail(ctx, LT_EINVAL, "lt_device_alloc: zero bytes");
+    void *p = nullptr;
+    LT_CUDA(ctx, cudaMalloc(&p, bytes), "cudaMalloc");
+    cudaError_t e = cudaMemsetAsync(p, 0, bytes, ctx->stream);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail(ctx, e, "cudaMemsetAsync");
+    }
+    *dev_out = p;
+    return LT_OK;
+}
+
+lt_status lt_device_free(lt_ctx *ctx, void *dev) {
+    lt_status st = enter_uncaptured(ctx, "lt_device_free");
+    if (st != LT_OK) return st;
+    if (!dev) return LT_OK;
+    LT_CUDA(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    LT_CUDA(ctx, cudaFree(dev), "cudaFree");
+    return LT_OK;
+}
+
+lt_status lt_copy_to_device(lt_ctx *ctx, void *dev_dst, const void *host_src, size_t bytes) {
+    lt_status st = enter_uncaptured(ctx, "lt_copy_to_device");
+    if (st != LT_OK) return st;
+    if (bytes == 0) return LT_OK;
+    if (!dev_dst || !host_src) return fail(ctx, LT_EINVAL, "lt_copy_to_device: null pointer");
+    LT_CUDA(ctx, cudaMemcpyAsync(dev_dst, host_src, bytes, cudaMemcpyHostToDevice, ctx->stream), "cudaMemcpyAsync");
+    return LT_OK;
+}
+
+lt_status lt_copy_to_host(lt_ctx *ctx, void *host_dst, const void *dev_src, size_t bytes) {
+    lt_status st = enter_uncaptured(ctx, "lt_copy_to_host");
+    if (st != LT_OK) return st;
+    if (bytes == 0) return LT_OK;
+    if (!host_dst || !dev_src) return fail(ctx, LT_EINVAL, "lt_copy_to_host: null pointer");
+    LT_CUDA(ctx, cudaMemcpyAsync(host_dst, dev_src, bytes, cudaMemcpyDeviceToHost, ctx->stream), "cudaMemcpyAsync");
+    return LT_OK;
+}
+
+// ── decode-step ops ────────────────────────────────────────────────────────
+
+lt_status lt_embed(lt_ctx *ctx, const lt_tensor *emb, const uint32_t *dev_tokens, const uint32_t *dev_pos,
+                   float *dev_out) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!emb || !dev_tokens || !dev_pos || !dev_out) return fail(ctx, LT_EINVAL, "lt_embed: null pointer");
+    if (emb->m.n_experts != 0) return fail(ctx, LT_EINVAL, "lt_embed: 3-D tensor");
+    return launched(ctx, lt::launch_embed(cfg_of(ctx), emb->m, dev_tokens, dev_pos, dev_out), "embed");
+}
+
+lt_status lt_qmatvec_add(lt_ctx *ctx, const lt_tensor *w, uint32_t expert, const float *dev_x, const float *dev_add,
+                         float *dev_y, uint32_t ntok) {
+    if (!dev_add) {
+        lt_status st = enter(ctx);
+        return st != LT_OK ? st : fail(ctx, LT_EINVAL, "lt_qmatvec_add: null addend");
+    }
+    return qmatvec_impl(ctx, w, expert, dev_x, dev_y, ntok, dev_add);
+}
+
+static lt_status attn_geom(lt_ctx *ctx, const lt_attn_cfg *cfg, lt::AttnGeom &g, const char *what) {
+    if (!cfg) return fail(ctx, LT_EINVAL, "%s: null cfg", what);
+    if (cfg->head_dim != 64 && cfg->head_dim != 128 && cfg->head_dim != 256)
+        return fail(ctx, LT_EINVAL, "%s: head_dim %u (64, 128 or 256)", what, cfg->head_dim);
+    if (cfg->n_heads == 0 || cfg->n_kv_heads == 0 || cfg->n_heads % cfg->n_kv_heads != 0 || cfg->n_heads > 1024)
+        return fail(ctx, LT_EINVAL, "%s: %u query heads over %u KV heads", what, cfg->n_heads, cfg->n_kv_heads);
+    if (cfg->kv_cap == 0) return fail(ctx, LT_EINVAL, "%s: kv_cap 0", what);
+    if (cfg->window > cfg->kv_cap) return fail(ctx, LT_EINVAL, "%s: window %u > kv_cap %u", what, cfg->window, cfg->kv_cap);
+    g.n_heads = cfg->n_heads;
+    g.n_kv = cfg->n_kv_heads;
+    g.hd = cfg->head_dim;
+    g.rope_neox = cfg->rope_neox ? 1u : 0u;
+    g.theta = cfg->rope_theta;
+    g.eps = cfg->eps;
+    g.scale = cfg->scale;
+    g.cap = cfg->kv_cap;
+    g.window = cfg->window;
+    return LT_OK;
+}
+
+lt_status lt_attn_prep(lt_ctx *ctx, const lt_attn_cfg *cfg, float *dev_qkv, const float *dev_q_norm,
+                       const float *dev_k_norm, const uint32_t *dev_pos, float *dev_k_cache, float *dev_v_cache) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    lt::AttnGeom g;
+    if ((st = attn_geom(ctx, cfg, g, "lt_attn_prep")) != LT_OK) return st;
+    if (!dev_qkv || !dev_pos || !dev_k_cache || !dev_v_cache) return fail(ctx, LT_EINVAL, "lt_attn_prep: null pointer");
+    return launched(ctx, lt::launch_attn_prep(cfg_of(ctx), g, dev_qkv, dev_q_norm, dev_k_norm, dev_pos, dev_k_cache,
+                                              dev_v_cache),
+                    "attn prep");
+}
+
+lt_status lt_attn_decode(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_q, const float *dev_k_cache,
+                         const float *dev_v_cache, const uint32_t *dev_pos, float *dev_out) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    lt::AttnGeom g;
+    if ((st = attn_geom(ctx, cfg, g, "lt_attn_decode")) != LT_OK) return st;
+    if (!dev_q || !dev_k_cache || !dev_v_cache || !dev_pos || !dev_out)
+        return fail(ctx, LT_EINVAL, "lt_attn_decode: null pointer");
+    if ((st = ensure_scratch(ctx, lt::attn_scratch_floats(g, ctx->num_sms) * 4)) != LT_OK) return st;
+    if ((st = ensure_counters(ctx, g.n_heads)) != LT_OK) return st;
+    return launched(ctx, lt::launch_attn_decode(cfg_of(ctx), g, dev_q, dev_k_cache, dev_v_cache, dev_pos, dev_out,
+                                                (float *)ctx->scratch, ctx->counters),
+                    "attn decode");
+}
+
+lt_status lt_greedy_step(lt_ctx *ctx, const float *dev_logits, uint32_t n, uint32_t *dev_tokens, uint32_t *dev_pos,
+                         const uint32_t *dev_n_prompt) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!dev_logits || !dev_tokens || !dev_pos || !dev_n_prompt || n == 0)
+        return fail(ctx, LT_EINVAL, "lt_greedy_step: bad argument");
+    if ((st = ensure_scratch(ctx, al256(64 * 4) * 2)) != LT_OK) return st;
+    if ((st = ensure_counters(ctx, 1)) != LT_OK) return st;
+    float *pv = (float *)ctx->scratch;
+    uint32_t *pi = (uint32_t *)(ctx->scratch + al256(64 * 4));
+    return launched(ctx,
+                    lt::launch_argmax(cfg_of(ctx), dev_logits, n, 1, nullptr, pv, pi, ctx->counters, dev_tokens,
+                                      dev_pos, dev_n_prompt),
+                    "greedy step");
 }
 
 static lt_status check_router(lt_ctx *ctx, const lt_tensor *router, uint32_t k) {
@@ -772,6 +934,38 @@ lt_status lt_moe_block(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *ga
     if (!dev_norm_w) return fail(ctx, LT_EINVAL, "lt_moe_block: null norm weights");
     return forward_impl(ctx, router, gate, up, down, act, norm_topk, dev_expert_scale, dev_norm_w, eps, 1, dev_x,
                         ntok, k, dev_out, dev_ids, dev_w);
+}
+
+lt_status lt_ffn_block(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, const lt_tensor *down, int act,
+                       const float *dev_norm_w, float eps, const float *dev_x, uint32_t ntok, float *dev_out) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!gate || !up || !down || !dev_norm_w || !dev_x || !dev_out) return fail(ctx, LT_EINVAL, "lt_ffn_block: null argument");
+    if (gate->m.n_experts || up->m.n_experts || down->m.n_experts)
+        return fail(ctx, LT_EINVAL, "lt_ffn_block: dense (2-D) tensors expected");
+    if (!quantized(gate->m.type) || !quantized(down->m.type) || up->m.type != gate->m.type)
+        return fail(ctx, LT_EUNSUPPORTED_TYPE, "lt_ffn_block: weights must be Q8_0/Q4_K/Q6_K (gate and up alike)");
+    const uint64_t d = gate->m.cols, F = gate->m.rows;
+    if (up->m.rows != F || up->m.cols != d || down->m.rows != d || down->m.cols != F)
+        return fail(ctx, LT_EINVAL, "lt_ffn_block: gate/up/down shapes disagree");
+    if ((st = check_kernel_shape(ctx, gate->m, "lt_ffn_block gate")) != LT_OK) return st;
+    if ((st = check_kernel_shape(ctx, down->m, "lt_ffn_block down")) != LT_OK) return st;
+    if (F % 32 != 0) return fail(ctx, LT_EINVAL, "lt_ffn_block: width %llu not a multiple of 32", (unsigned long long)F);
+    if (act != LT_ACT_SILU && act != LT_ACT_GELU_TANH) return fail(ctx, LT_EINVAL, "lt_ffn_block: act %d", act);
+    if (ntok == 0) return LT_OK;
+    if ((st = ensure_consts(ctx, ntok)) != LT_OK) return st;
+    // the expert kernels with one expert (id 0) of weight 1 per token
+    const MoeScratch probe = moe_layout(nullptr, ntok, 1, 1, d, F, 0);
+    const size_t xn_bytes = al256((size_t)ntok * d * 4);
+    if ((st = ensure_scratch(ctx, probe.bytes + xn_bytes)) != LT_OK) return st;
+    const MoeScratch s = moe_layout(ctx->scratch, ntok, 1, 1, d, F, 0);
+    float *xn = (float *)(ctx->scratch + probe.bytes);
+    const lt::LaunchCfg c = cfg_of(ctx);
+    st = launched(ctx, lt::launch_rmsnorm(c, dev_x, dev_norm_w, eps, (uint32_t)d, ntok, xn), "rmsnorm");
+    if (st != LT_OK) return st;
+    st = launched(ctx, lt::launch_quantize(c, xn, (uint32_t)d, ntok, s.xq, s.xq_pitch), "quantize");
+    if (st != LT_OK) return st;
+    return ffn_impl(ctx, gate, up, down, act, ntok, ctx->zeros, ctx->ones, 1, dev_x, dev_out, xn, s);
 }
 
 lt_status lt_ep_dispatch(lt_ctx *ctx, const uint32_t *dev_ids, uint32_t ntok, uint32_t k, uint32_t n_experts,

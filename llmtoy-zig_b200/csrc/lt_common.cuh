@@ -85,7 +85,7 @@ LT_DEVINL void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dep
 // ── error reporting ────────────────────────────────────────────────────────
 // Kernels never trap.  A bounded wait that gives up records a code in the
 // context's device error word; the host turns it into LT_ETIMEOUT.
-enum : int { DEV_ERR_NONE = 0, DEV_ERR_TMA_TIMEOUT = 1, DEV_ERR_GRID_TIMEOUT = 2 };
+enum : int { DEV_ERR_NONE = 0, DEV_ERR_TMA_TIMEOUT = 1, DEV_ERR_GRID_TIMEOUT = 2, DEV_ERR_BAD_INDEX = 3 };
 
 // ── mbarrier + TMA bulk copy (global -> shared) ────────────────────────────
 LT_DEVINL uint32_t smem_u32(const void *p) {

@@ -75,9 +75,33 @@ cudaError_t launch_dequant(const LaunchCfg &c, const DevMat &m, uint64_t row0, u
 cudaError_t launch_rmsnorm(const LaunchCfg &c, const float *x, const float *w, float eps, uint32_t n,
                            uint32_t ntok, float *y);
 cudaError_t launch_softmax(const LaunchCfg &c, float *x, uint32_t n, uint32_t ntok);
+// tokens != nullptr (ntok == 1): greedy step of a decode graph -- with
+// p = *pos, tokens[p + 1] = argmax when p + 1 >= *n_prompt, then *pos = p + 1.
 cudaError_t launch_argmax(const LaunchCfg &c, const float *x, uint32_t n, uint32_t ntok,
                           uint32_t *idx, float *scratch_val, uint32_t *scratch_idx,
-                          uint32_t *counters);
+                          uint32_t *counters, uint32_t *tokens = nullptr, uint32_t *pos = nullptr,
+                          const uint32_t *n_prompt = nullptr);
+cudaError_t launch_fill_f32(cudaStream_t s, float *p, size_t n, float v);
+// out = dequantised row tokens[*pos] of m (embedLookup); rows >= m.rows set
+// DEV_ERR_BAD_INDEX and read row 0.
+cudaError_t launch_embed(const LaunchCfg &c, const DevMat &m, const uint32_t *tokens, const uint32_t *pos,
+                         float *out);
+
+// Decode attention (lt_attn.cu).  KV cache per layer: [cap][n_kv * hd] f32
+// for K and for V; position slot = pos % cap.
+struct AttnGeom {
+    uint32_t n_heads, n_kv, hd;
+    uint32_t rope_neox;  // 0: consecutive pairs (rope.zig:14), 1: halves (rope.zig:56)
+    float theta, eps, scale;
+    uint32_t cap;
+    uint32_t window;  // 0: every cached position; else the last `window`
+};
+uint32_t attn_splits(const AttnGeom &g, int num_sms);
+size_t attn_scratch_floats(const AttnGeom &g, int num_sms);
+cudaError_t launch_attn_prep(const LaunchCfg &c, const AttnGeom &g, float *qkv, const float *q_norm,
+                             const float *k_norm, const uint32_t *pos, float *kc, float *vc);
+cudaError_t launch_attn_decode(const LaunchCfg &c, const AttnGeom &g, const float *q, const float *kc,
+                               const float *vc, const uint32_t *pos, float *out, float *part, uint32_t *counters);
 
 // Bytes of one quantised activation row (lt_qact.cuh) of `cols` values.
 size_t qact_row_pitch(uint64_t cols);
@@ -87,8 +111,10 @@ cudaError_t launch_quantize(const LaunchCfg &c, const float *x, uint32_t cols, u
 
 // y[tok][rows] = W[expert] . x[tok].  Quantised types read the activations
 // from xq (quantised rows); f32/f16 matrices read x directly.
+// add != nullptr: y = W . x + add (same shape as y; may alias y).
 cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert, const uint8_t *xq,
-                           uint64_t xq_pitch, const float *x, float *y, uint32_t ntok);
+                           uint64_t xq_pitch, const float *x, float *y, uint32_t ntok,
+                           const float *add = nullptr);
 
 // Router over f32 weights [E][cols] (row stride w_ld floats); logits scratch
 // [ntok][E]; counters zero-initialised, one per token group (reset by the

@@ -173,6 +173,39 @@ __global__ void k_dequant(const uint8_t *base, uint32_t type, uint64_t pitch, ui
     }
 }
 
+__global__ void k_fill_f32(float *p, size_t n, float v) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        p[i] = v;
+}
+
+cudaError_t launch_fill_f32(cudaStream_t s, float *p, size_t n, float v) {
+    const size_t want = (n + 255) / 256;
+    k_fill_f32<<<(unsigned)(want < 4096 ? (want ? want : 1) : 4096), 256, 0, s>>>(p, n, v);
+    return cudaGetLastError();
+}
+
+// embedLookup (src/model/forward.zig:319-341) of the token at the current
+// position of a decode graph's token stream.
+__global__ void k_embed(const uint8_t *base, uint32_t type, uint64_t pitch, uint32_t cols, uint64_t rows,
+                        const uint32_t *tokens, const uint32_t *pos, float *out, int *dev_err) {
+    pdl_wait();
+    uint32_t row = tokens[*pos];
+    if (row >= rows) {
+        if (threadIdx.x == 0 && blockIdx.x == 0 && dev_err) atomicExch(dev_err, DEV_ERR_BAD_INDEX);
+        row = 0;
+    }
+    const uint8_t *r = base + (uint64_t)row * pitch;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < cols; i += gridDim.x * blockDim.x)
+        out[i] = dq_elem(r, type, i);
+}
+
+cudaError_t launch_embed(const LaunchCfg &c, const DevMat &m, const uint32_t *tokens, const uint32_t *pos,
+                         float *out) {
+    const uint32_t cols = (uint32_t)m.cols;
+    return launch_k(c, "embed", k_embed, dim3((cols + 255) / 256), dim3(256), 0, m.data, m.type, m.pitch, cols,
+                    m.rows, tokens, pos, out, c.dev_err);
+}
+
 cudaError_t launch_dequant(const LaunchCfg &c, const DevMat &m, uint64_t row0, uint64_t nrows, float *out) {
     const uint64_t n = nrows * m.cols;
     if (n == 0) return cudaSuccess;
@@ -269,7 +302,8 @@ LT_DEVINL void argmax_combine(float &bv, uint32_t &bi, float ov, uint32_t oi) {
     }
 }
 
-__global__ void k_argmax(const float *x, uint32_t n, uint32_t *idx, float *pv, uint32_t *pi, uint32_t *counters) {
+__global__ void k_argmax(const float *x, uint32_t n, uint32_t *idx, float *pv, uint32_t *pi, uint32_t *counters,
+                         uint32_t *tokens, uint32_t *pos, const uint32_t *n_prompt) {
     __shared__ float sv[32];
     __shared__ uint32_t si[32];
     __shared__ int s_last;
@@ -307,14 +341,21 @@ __global__ void k_argmax(const float *x, uint32_t n, uint32_t *idx, float *pv, u
         argmax_combine(fv, fi, __ldcg(pv + (size_t)t * gridDim.x + b), __ldcg(pi + (size_t)t * gridDim.x + b));
     const float x0 = xt[0];
     if (x0 != x0 || fi == 0xffffffffu) fi = 0;
-    idx[t] = fi;
+    if (idx) idx[t] = fi;
+    if (tokens) {  // the step's sampled token goes after the prompt; advance the position
+        const uint32_t p = *pos;
+        if (p + 1 >= *n_prompt) tokens[p + 1] = fi;
+        *pos = p + 1;
+    }
     counters[t] = 0;
 }
 
 cudaError_t launch_argmax(const LaunchCfg &c, const float *x, uint32_t n, uint32_t ntok, uint32_t *idx, float *pv,
-                          uint32_t *pi, uint32_t *counters) {
+                          uint32_t *pi, uint32_t *counters, uint32_t *tokens, uint32_t *pos,
+                          const uint32_t *n_prompt) {
     const uint32_t nb = max(1u, min(64u, (n + 4095) / 4096));
-    return launch_k(c, "argmax", k_argmax, dim3(nb, ntok), dim3(256), 0, x, n, idx, pv, pi, counters);
+    return launch_k(c, "argmax", k_argmax, dim3(nb, ntok), dim3(256), 0, x, n, idx, pv, pi, counters, tokens, pos,
+                    n_prompt);
 }
 
 }  // namespace lt

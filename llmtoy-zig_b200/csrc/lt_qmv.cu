@@ -18,6 +18,7 @@ struct QmvArgs {
     const uint8_t *xq;
     uint64_t xq_pitch;
     float *y;
+    const float *add;  // nullptr or y's shape: y = W . x + add
     uint32_t ntok;
     uint32_t rw;  // rows per warp
     int *dev_err;
@@ -80,7 +81,8 @@ __global__ void __launch_bounds__(kQmvWarps * 32) k_qmv(QmvArgs a) {
                 const float *pp = wpart + t * nitem + r * ipr;
                 float s = 0.0f;
                 for (int i = 0; i < ipr; i++) s += pp[i];
-                a.y[(size_t)(c0 + t) * a.nrows + wr0 + r] = s;
+                const size_t yi = (size_t)(c0 + t) * a.nrows + wr0 + r;
+                a.y[yi] = a.add ? __fadd_rn(a.add[yi], s) : s;
             }
         }
         __syncthreads();
@@ -89,7 +91,7 @@ __global__ void __launch_bounds__(kQmvWarps * 32) k_qmv(QmvArgs a) {
 
 // f32 / f16 rows: one warp per row, plain loads.
 __global__ void k_mv_float(const uint8_t *rows, uint64_t pitch, uint32_t type, uint32_t nrows, uint32_t cols,
-                           const float *x, float *y, uint32_t ntok) {
+                           const float *x, float *y, uint32_t ntok, const float *add) {
     pdl_launch_dependents();
     pdl_wait();
     const uint32_t warps = (blockDim.x >> 5) * gridDim.x;
@@ -104,7 +106,8 @@ __global__ void k_mv_float(const uint8_t *rows, uint64_t pitch, uint32_t type, u
                 s += w * xt[i];
             }
             s = warp_sum(s);
-            if ((threadIdx.x & 31) == 0) y[(size_t)t * nrows + r] = s;
+            const size_t yi = (size_t)t * nrows + r;
+            if ((threadIdx.x & 31) == 0) y[yi] = add ? __fadd_rn(add[yi], s) : s;
         }
     }
 }
@@ -118,13 +121,13 @@ static cudaError_t launch_qmv_t(const LaunchCfg &c, const QmvArgs &a) {
 }
 
 cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert, const uint8_t *xq,
-                           uint64_t xq_pitch, const float *x, float *y, uint32_t ntok) {
+                           uint64_t xq_pitch, const float *x, float *y, uint32_t ntok, const float *add) {
     const uint8_t *rows = m.data + (uint64_t)expert * m.rows * m.pitch;
     if (m.type == T_F32 || m.type == T_F16) {
         const uint64_t want = (m.rows + 7) / 8;
         const uint32_t blocks = (uint32_t)(want < 65535 ? want : 65535);
         return launch_k(c, "qmv_float", k_mv_float, dim3(blocks), dim3(256), 0, rows, m.pitch, m.type,
-                        (uint32_t)m.rows, (uint32_t)m.cols, x, y, ntok);
+                        (uint32_t)m.rows, (uint32_t)m.cols, x, y, ntok, add);
     }
     QmvArgs a;
     a.rows = rows;
@@ -136,6 +139,7 @@ cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert,
     a.xq = xq;
     a.xq_pitch = xq_pitch;
     a.y = y;
+    a.add = add;
     a.ntok = ntok;
     a.rw = max(1u, 32u / a.nitems);
     a.dev_err = c.dev_err;

@@ -1,0 +1,218 @@
+"""Python binding of the C++ host decode loop (host/decoder.h,
+libllmtoy_host.so): forwardOneModel (src/model/forward.zig:229-316) per token
+over the C ABI, one captured CUDA graph per step, greedy sampling on the
+device.
+
+    ctx = Context(0)
+    dec = Decoder(ctx, ModelSpec(...), layers=[LayerSpec(...), ...], ...)
+    tokens = dec.generate(prompt, n_gen)
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+from . import Context, LtError, Tensor, _ptr, load_library, LIB_PATH
+
+HOST_LIB_PATH = LIB_PATH.with_name("libllmtoy_host.so")
+
+P = ctypes.c_void_p
+U32 = ctypes.c_uint32
+
+
+class _Layer(ctypes.Structure):
+    _fields_ = [("attn_norm", P), ("ffn_norm", P), ("wqkv", P), ("wq", P), ("wk", P), ("wv", P), ("wo", P),
+                ("qkv_bias", P), ("q_norm", P), ("k_norm", P), ("ffn_gate", P), ("ffn_up", P), ("ffn_down", P),
+                ("router", P), ("exp_gate", P), ("exp_up", P), ("exp_down", P)]
+
+
+class _Model(ctypes.Structure):
+    _fields_ = [("n_layers", U32), ("d_model", U32), ("n_heads", U32), ("n_kv_heads", U32), ("head_dim", U32),
+                ("vocab", U32), ("n_used", U32), ("norm_topk", U32), ("rope_neox", U32), ("act", U32),
+                ("eps", ctypes.c_float), ("rope_theta", ctypes.c_float), ("kv_cap", U32),
+                ("token_emb", P), ("lm_head", P), ("out_norm", P), ("layers", ctypes.POINTER(_Layer))]
+
+
+_host = None
+
+
+def load_host_library() -> ctypes.CDLL:
+    global _host
+    if _host is not None:
+        return _host
+    load_library()  # the C ABI first (the host library links against it)
+    if not HOST_LIB_PATH.exists():
+        raise RuntimeError(f"{HOST_LIB_PATH} is missing: build it with `python llmtoy-zig_b200/build.py`")
+    L = ctypes.CDLL(str(HOST_LIB_PATH))
+    I = ctypes.c_int
+    sig = {
+        "lth_decoder_create": (I, [P, ctypes.POINTER(_Model), ctypes.POINTER(P)]),
+        "lth_decoder_free": (None, [P]),
+        "lth_decoder_start": (I, [P, P, U32]),
+        "lth_decoder_step": (I, [P]),
+        "lth_decoder_capture": (I, [P]),
+        "lth_decoder_replay": (I, [P, U32]),
+        "lth_decoder_logits": (P, [P]),
+        "lth_decoder_tokens": (I, [P, P, U32]),
+        "lth_generate": (I, [P, P, U32, U32, P]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _host = L
+    return L
+
+
+def _h(t: Tensor | None):
+    return None if t is None else t.handle
+
+
+@dataclass
+class LayerSpec:
+    """One decoder layer: Tensors from Context.upload, norms/biases as device
+    tensors (torch CUDA float32)."""
+    attn_norm: object
+    ffn_norm: object
+    wo: Tensor
+    wqkv: Tensor | None = None
+    wq: Tensor | None = None
+    wk: Tensor | None = None
+    wv: Tensor | None = None
+    qkv_bias: object = None
+    q_norm: object = None
+    k_norm: object = None
+    ffn_gate: Tensor | None = None
+    ffn_up: Tensor | None = None
+    ffn_down: Tensor | None = None
+    router: Tensor | None = None
+    exp_gate: Tensor | None = None
+    exp_up: Tensor | None = None
+    exp_down: Tensor | None = None
+
+
+@dataclass
+class ModelSpec:
+    d_model: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    vocab: int
+    token_emb: Tensor
+    lm_head: Tensor
+    out_norm: object
+    layers: list = field(default_factory=list)
+    n_used: int = 0
+    norm_topk: bool = False
+    rope_neox: bool = False
+    act: int = 0
+    eps: float = 1e-6
+    rope_theta: float = 1e6
+    kv_cap: int = 4096
+
+
+class Decoder:
+    """A greedy decoder over a device model (lth_decoder)."""
+
+    def __init__(self, ctx: Context, spec: ModelSpec):
+        self.lib = load_host_library()
+        self.ctx, self.spec = ctx, spec
+        self._layers = (_Layer * len(spec.layers))()
+        for i, L in enumerate(spec.layers):
+            self._layers[i] = _Layer(
+                _ptr(L.attn_norm), _ptr(L.ffn_norm), _h(L.wqkv), _h(L.wq), _h(L.wk), _h(L.wv), _h(L.wo),
+                _ptr(L.qkv_bias), _ptr(L.q_norm), _ptr(L.k_norm), _h(L.ffn_gate), _h(L.ffn_up), _h(L.ffn_down),
+                _h(L.router), _h(L.exp_gate), _h(L.exp_up), _h(L.exp_down))
+        s = spec
+        self._model = _Model(len(s.layers), s.d_model, s.n_heads, s.n_kv_heads, s.head_dim, s.vocab, s.n_used,
+                             int(s.norm_topk), int(s.rope_neox), s.act, s.eps, s.rope_theta, s.kv_cap,
+                             _h(s.token_emb), _h(s.lm_head), _ptr(s.out_norm), self._layers)
+        h = P()
+        self._check(self.lib.lth_decoder_create(ctx.ptr, ctypes.byref(self._model), ctypes.byref(h)))
+        self.ptr = h.value
+
+    def _check(self, st: int) -> None:
+        if st != 0:
+            msg = self.ctx.lib.lt_last_error(self.ctx.ptr) or b""
+            raise LtError(st, msg.decode())
+
+    def close(self) -> None:
+        if getattr(self, "ptr", None):
+            self.lib.lth_decoder_free(self.ptr)
+            self.ptr = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    # -- step-level control (parity tests, timing) ----------------------------
+    def start(self, prompt) -> None:
+        arr = (ctypes.c_uint32 * len(prompt))(*[int(t) for t in prompt])
+        self._check(self.lib.lth_decoder_start(self.ptr, arr, len(prompt)))
+
+    def step(self) -> None:
+        self._check(self.lib.lth_decoder_step(self.ptr))
+
+    def capture(self) -> None:
+        self._check(self.lib.lth_decoder_capture(self.ptr))
+
+    def replay(self, n_steps: int) -> None:
+        self._check(self.lib.lth_decoder_replay(self.ptr, n_steps))
+
+    def logits_ptr(self) -> int:
+        return self.lib.lth_decoder_logits(self.ptr)
+
+    def tokens(self, n: int) -> list[int]:
+        arr = (ctypes.c_uint32 * n)()
+        self._check(self.lib.lth_decoder_tokens(self.ptr, arr, n))
+        return list(arr)
+
+    def generate(self, prompt, n_gen: int) -> list[int]:
+        """Greedy generation: prompt ids -> n_gen new ids."""
+        arr = (ctypes.c_uint32 * len(prompt))(*[int(t) for t in prompt])
+        out = (ctypes.c_uint32 * n_gen)()
+        self._check(self.lib.lth_generate(self.ptr, arr, len(prompt), n_gen, out))
+        return list(out)
+
+
+def upload_decoder(ctx: Context, m, kv_cap: int = 4096, stacked_qkv: bool = True) -> ModelSpec:
+    """Upload a synth.DecoderModel (host GGUF bytes) and return its ModelSpec.
+    Norm weights and biases go to torch CUDA tensors, which the spec keeps
+    alive; stacked_qkv uploads Q, K and V rows as one tensor (one matvec)."""
+    import numpy as np
+    import torch
+
+    def dev(a):
+        return None if a is None else torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda()
+
+    d = m.d_model
+    layers = []
+    for L in m.layers:
+        nq, nkv = m.n_heads * m.head_dim, m.n_kv_heads * m.head_dim
+        ls = LayerSpec(attn_norm=dev(L.attn_norm), ffn_norm=dev(L.ffn_norm),
+                       wo=ctx.upload(L.wo, L.attn_type, d, nq), qkv_bias=dev(L.qkv_bias),
+                       q_norm=dev(L.q_norm), k_norm=dev(L.k_norm))
+        if stacked_qkv:
+            ls.wqkv = ctx.upload(L.wqkv, L.attn_type, nq + 2 * nkv, d)
+        else:
+            ls.wq = ctx.upload(L.wq, L.attn_type, nq, d)
+            ls.wk = ctx.upload(L.wk, L.attn_type, nkv, d)
+            ls.wv = ctx.upload(L.wv, L.attn_type, nkv, d)
+        if L.moe is None:
+            ls.ffn_gate = ctx.upload(L.ffn_gate, L.ffn_type, m.d_ffn, d)
+            ls.ffn_up = ctx.upload(L.ffn_up, L.ffn_type, m.d_ffn, d)
+            ls.ffn_down = ctx.upload(L.ffn_down, L.ffn_type, d, m.d_ffn)
+        else:
+            E, F = m.n_experts, m.d_expert
+            ls.router = ctx.upload(L.moe.router, 0, E, d)
+            ls.exp_gate = ctx.upload(L.moe.gate, L.moe.gate_type, F, d, n_experts=E)
+            ls.exp_up = ctx.upload(L.moe.up, L.moe.gate_type, F, d, n_experts=E)
+            ls.exp_down = ctx.upload(L.moe.down, L.moe.down_type, d, F, n_experts=E)
+        layers.append(ls)
+    return ModelSpec(d_model=d, n_heads=m.n_heads, n_kv_heads=m.n_kv_heads, head_dim=m.head_dim, vocab=m.vocab,
+                     token_emb=ctx.upload(m.token_emb, m.emb_type, m.vocab, d),
+                     lm_head=ctx.upload(m.lm_head, m.lm_type, m.vocab, d), out_norm=dev(m.out_norm),
+                     layers=layers, n_used=m.k, norm_topk=m.norm_topk, rope_neox=m.rope_neox, eps=m.eps,
+                     rope_theta=m.rope_theta, kv_cap=kv_cap)

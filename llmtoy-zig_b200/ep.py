@@ -78,8 +78,10 @@ class DeviceOps:
     def empty(self, shape, dtype):
         return self.torch.empty(shape, dtype=dtype, device=self.device)
 
+    # A rank with no tokens still takes part in every exchange; its tensors are
+    # empty (null data pointers, which the C ABI rejects), so no kernel runs.
     def normed(self, layer: EPLayer, x, T: int):
-        if layer.norm_w is None:
+        if layer.norm_w is None or T == 0:
             return x
         y = self.empty(x.shape, self.torch.float32)
         self.ctx.rmsnorm(x, layer.norm_w, layer.eps, layer.d_model, T, y)
@@ -88,6 +90,8 @@ class DeviceOps:
     def route(self, layer: EPLayer, x, T: int, k: int):
         ids = self.empty((T, k), self.torch.int32)
         w = self.empty((T, k), self.torch.float32)
+        if T == 0:
+            return ids, w
         self.ctx.moe_route(layer.router, x, T, k, layer.norm_topk, layer.expert_scale, ids, w)
         return ids, w
 
@@ -97,6 +101,9 @@ class DeviceOps:
         send_token = self.empty((T * k,), t.int32)
         send_local = self.empty((T * k,), t.int32)
         pair_pos = self.empty((T * k,), t.int32)
+        if T == 0:
+            counts.zero_()
+            return counts, send_token, send_local, pair_pos
         self.ctx.ep_dispatch(ids, T, k, n_experts, world, counts, send_token, send_local, pair_pos)
         return counts, send_token, send_local, pair_pos
 
@@ -115,12 +122,16 @@ class DeviceOps:
 
     def combine(self, y, pair_pos, w, T: int, k: int, resid):
         out = self.empty((T, y.shape[1]), self.torch.float32)
+        if T == 0:
+            return out
         self.ctx.moe_combine(y, y.shape[1], pair_pos, w, T, k, resid, out)
         return out
 
     def local_forward(self, layer: EPLayer, x, T: int, k: int):
         """The whole layer on this device (one rank)."""
         out = self.empty((T, layer.d_model), self.torch.float32)
+        if T == 0:
+            return out
         if layer.norm_w is None:
             self.ctx.moe_forward(layer.router, layer.gate, layer.up, layer.down, layer.act, layer.norm_topk,
                                  layer.expert_scale, x, T, k, out)

@@ -1,0 +1,206 @@
+// decoder.cpp — host decode loop over the C ABI (see decoder.h).
+//
+// One step is forwardOneModel (src/model/forward.zig:229-316) with the
+// device position word standing in for its `pos` argument:
+//   x = embedLookup(tokens[pos])                               (:319-341)
+//   per layer: xb = rmsnorm(x); qkv = W_qkv xb (+ bias)        (:272-287)
+//              per-head Q/K norm, RoPE, K/V into the cache     (:289-292)
+//              att = sdpAttn per head                          (:294-302)
+//              x = x + wo att                                  (:304-305)
+//              x = x + ffn(rmsnorm(x))  dense or MoE block     (:307-312)
+//   logits = lm_head rmsnorm(x); tokens[pos+1] = greedy; pos++ (:314-316)
+#include "decoder.h"
+
+#include <cstring>
+#include <new>
+#include <vector>
+
+struct lth_decoder {
+    lt_ctx *ctx = nullptr;
+    lth_model m{};
+    std::vector<lth_layer> layers;
+    lt_attn_cfg attn{};
+    uint32_t nq = 0, nkv = 0;
+    float *x = nullptr, *xb = nullptr, *qkv = nullptr, *att = nullptr, *logits = nullptr;
+    float *kcache = nullptr, *vcache = nullptr;
+    uint32_t *tokens = nullptr;  // [kv_cap + 1]
+    uint32_t *state = nullptr;   // {pos, n_prompt}
+    lt_graph *graph = nullptr;
+    bool warmed = false;
+};
+
+namespace {
+
+template <class T>
+lt_status alloc(lth_decoder *d, T **p, size_t count) {
+    void *v = nullptr;
+    lt_status st = lt_device_alloc(d->ctx, count * sizeof(T), &v);
+    *p = static_cast<T *>(v);
+    return st;
+}
+
+#define LTH_TRY(expr)                        \
+    do {                                     \
+        lt_status st_ = (expr);              \
+        if (st_ != LT_OK) return st_;        \
+    } while (0)
+
+lt_status layer_step(lth_decoder *d, uint32_t l) {
+    const lth_model &m = d->m;
+    const lth_layer &L = d->layers[l];
+    lt_ctx *c = d->ctx;
+    const uint32_t *pos = d->state;
+    LTH_TRY(lt_rmsnorm(c, d->x, L.attn_norm, m.eps, m.d_model, 1, d->xb));
+    if (L.wqkv) {
+        if (L.qkv_bias)
+            LTH_TRY(lt_qmatvec_add(c, L.wqkv, 0, d->xb, L.qkv_bias, d->qkv, 1));
+        else
+            LTH_TRY(lt_qmatvec(c, L.wqkv, 0, d->xb, d->qkv, 1));
+    } else {
+        const lt_tensor *w[3] = {L.wq, L.wk, L.wv};
+        const uint32_t off[3] = {0, d->nq, d->nq + d->nkv};
+        for (int i = 0; i < 3; i++) {
+            if (L.qkv_bias)
+                LTH_TRY(lt_qmatvec_add(c, w[i], 0, d->xb, L.qkv_bias + off[i], d->qkv + off[i], 1));
+            else
+                LTH_TRY(lt_qmatvec(c, w[i], 0, d->xb, d->qkv + off[i], 1));
+        }
+    }
+    const size_t cache = (size_t)m.kv_cap * d->nkv;
+    float *kc = d->kcache + (size_t)l * cache, *vc = d->vcache + (size_t)l * cache;
+    LTH_TRY(lt_attn_prep(c, &d->attn, d->qkv, L.q_norm, L.k_norm, pos, kc, vc));
+    LTH_TRY(lt_attn_decode(c, &d->attn, d->qkv, kc, vc, pos, d->att));
+    LTH_TRY(lt_qmatvec_add(c, L.wo, 0, d->att, d->x, d->x, 1));
+    if (L.router)
+        return lt_moe_block(c, L.router, L.exp_gate, L.exp_up, L.exp_down, (int)m.act, (int)m.norm_topk, nullptr,
+                            L.ffn_norm, m.eps, d->x, 1, m.n_used, d->x, nullptr, nullptr);
+    return lt_ffn_block(c, L.ffn_gate, L.ffn_up, L.ffn_down, (int)m.act, L.ffn_norm, m.eps, d->x, 1, d->x);
+}
+
+lt_status step(lth_decoder *d) {
+    const lth_model &m = d->m;
+    LTH_TRY(lt_embed(d->ctx, m.token_emb, d->tokens, d->state, d->x));
+    for (uint32_t l = 0; l < m.n_layers; l++) LTH_TRY(layer_step(d, l));
+    LTH_TRY(lt_rmsnorm(d->ctx, d->x, m.out_norm, m.eps, m.d_model, 1, d->xb));
+    LTH_TRY(lt_qmatvec(d->ctx, m.lm_head, 0, d->xb, d->logits, 1));
+    return lt_greedy_step(d->ctx, d->logits, m.vocab, d->tokens, d->state, d->state + 1);
+}
+
+void release(lth_decoder *d) {
+    if (d->graph) lt_graph_free(d->ctx, d->graph);
+    void *bufs[] = {d->x, d->xb, d->qkv, d->att, d->logits, d->kcache, d->vcache, d->tokens, d->state};
+    for (void *b : bufs)
+        if (b) lt_device_free(d->ctx, b);
+}
+
+}  // namespace
+
+extern "C" {
+
+lt_status lth_decoder_create(lt_ctx *ctx, const lth_model *m, lth_decoder **out) {
+    if (!ctx || !m || !out || !m->layers || !m->token_emb || !m->lm_head || !m->out_norm) return LT_EINVAL;
+    *out = nullptr;
+    if (m->n_layers == 0 || m->n_heads == 0 || m->n_kv_heads == 0 || m->kv_cap == 0 || m->vocab == 0) return LT_EINVAL;
+    lth_decoder *d = new (std::nothrow) lth_decoder;
+    if (!d) return LT_ENOMEM;
+    d->ctx = ctx;
+    d->m = *m;
+    d->layers.assign(m->layers, m->layers + m->n_layers);
+    d->m.layers = nullptr;
+    d->nq = m->n_heads * m->head_dim;
+    d->nkv = m->n_kv_heads * m->head_dim;
+    d->attn.n_heads = m->n_heads;
+    d->attn.n_kv_heads = m->n_kv_heads;
+    d->attn.head_dim = m->head_dim;
+    d->attn.rope_neox = m->rope_neox;
+    d->attn.rope_theta = m->rope_theta;
+    d->attn.eps = m->eps;
+    d->attn.scale = 1.0f / __builtin_sqrtf((float)m->head_dim);  // forward.zig:300
+    d->attn.kv_cap = m->kv_cap;
+    d->attn.window = 0;
+    const size_t cache = (size_t)m->n_layers * m->kv_cap * d->nkv;
+    lt_status st;
+    if ((st = alloc(d, &d->x, m->d_model)) != LT_OK || (st = alloc(d, &d->xb, m->d_model)) != LT_OK ||
+        (st = alloc(d, &d->qkv, d->nq + 2 * d->nkv)) != LT_OK || (st = alloc(d, &d->att, d->nq)) != LT_OK ||
+        (st = alloc(d, &d->logits, m->vocab)) != LT_OK || (st = alloc(d, &d->kcache, cache)) != LT_OK ||
+        (st = alloc(d, &d->vcache, cache)) != LT_OK || (st = alloc(d, &d->tokens, (size_t)m->kv_cap + 1)) != LT_OK ||
+        (st = alloc(d, &d->state, 2)) != LT_OK) {
+        release(d);
+        delete d;
+        return st;
+    }
+    *out = d;
+    return LT_OK;
+}
+
+void lth_decoder_free(lth_decoder *d) {
+    if (!d) return;
+    release(d);
+    delete d;
+}
+
+lt_status lth_decoder_start(lth_decoder *d, const uint32_t *prompt, uint32_t n_prompt) {
+    if (!d || !prompt || n_prompt == 0 || n_prompt > d->m.kv_cap) return LT_EINVAL;
+    const uint32_t state[2] = {0, n_prompt};
+    LTH_TRY(lt_copy_to_device(d->ctx, d->tokens, prompt, (size_t)n_prompt * 4));
+    LTH_TRY(lt_copy_to_device(d->ctx, d->state, state, sizeof state));
+    return lt_sync(d->ctx);  // the host arrays may go away after this call
+}
+
+lt_status lth_decoder_step(lth_decoder *d) {
+    if (!d) return LT_EINVAL;
+    LTH_TRY(step(d));
+    d->warmed = true;
+    return LT_OK;
+}
+
+lt_status lth_decoder_capture(lth_decoder *d) {
+    if (!d) return LT_EINVAL;
+    if (d->graph) return LT_OK;
+    if (!d->warmed) return LT_EINVAL;  // an eager step first sizes the scratch buffers
+    LTH_TRY(lt_capture_begin(d->ctx));
+    lt_status st = step(d);
+    lt_graph *g = nullptr;
+    lt_status st2 = lt_capture_end(d->ctx, &g);
+    if (st != LT_OK) {
+        if (g) lt_graph_free(d->ctx, g);
+        return st;
+    }
+    if (st2 != LT_OK) return st2;
+    d->graph = g;
+    return LT_OK;
+}
+
+lt_status lth_decoder_replay(lth_decoder *d, uint32_t n_steps) {
+    if (!d) return LT_EINVAL;
+    if (!d->graph) return LT_EINVAL;
+    for (uint32_t i = 0; i < n_steps; i++) LTH_TRY(lt_graph_launch(d->ctx, d->graph));
+    return LT_OK;
+}
+
+const float *lth_decoder_logits(const lth_decoder *d) { return d ? d->logits : nullptr; }
+
+lt_status lth_decoder_tokens(lth_decoder *d, uint32_t *host_out, uint32_t n) {
+    if (!d || !host_out || n > d->m.kv_cap + 1) return LT_EINVAL;
+    LTH_TRY(lt_copy_to_host(d->ctx, host_out, d->tokens, (size_t)n * 4));
+    return lt_sync(d->ctx);
+}
+
+lt_status lth_generate(lth_decoder *d, const uint32_t *prompt, uint32_t n_prompt, uint32_t n_gen, uint32_t *out) {
+    if (!d || !out || n_gen == 0 || (size_t)n_prompt + n_gen > d->m.kv_cap) return LT_EINVAL;
+    LTH_TRY(lth_decoder_start(d, prompt, n_prompt));
+    const uint32_t steps = n_prompt + n_gen - 1;
+    uint32_t done = 0;
+    if (!d->graph) {  // first use: one eager step sizes the scratch, then capture
+        LTH_TRY(lth_decoder_step(d));
+        done = 1;
+        LTH_TRY(lth_decoder_capture(d));
+    }
+    LTH_TRY(lth_decoder_replay(d, steps - done));
+    std::vector<uint32_t> all((size_t)n_prompt + n_gen);
+    LTH_TRY(lth_decoder_tokens(d, all.data(), n_prompt + n_gen));
+    std::memcpy(out, all.data() + n_prompt, (size_t)n_gen * 4);
+    return LT_OK;
+}
+
+}  // extern "C"

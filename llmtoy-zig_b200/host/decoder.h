@@ -1,0 +1,77 @@
+/*
+ * decoder.h — C API of the host decode loop (libllmtoy_host.so).
+ *
+ * The reference's forward loop is host code (src/model/forward.zig:229-316,
+ * forwardOneModel; the generate loop of src/main.zig) that calls its ops per
+ * token.  This is that loop restated in C++ on top of the C ABI alone
+ * (include/llmtoy_cuda.h), as a Zig host would bind it: weights are lt_tensor
+ * handles, norms and caches device buffers from lt_device_alloc.  One decode
+ * step is captured once as a CUDA graph and replayed per token; the position
+ * and the token stream live on the device, so a whole generation runs without
+ * a host round trip.
+ *
+ * Model shapes covered (per layer): RMSNorm -> Q/K/V (stacked or separate,
+ * optional biases) -> optional per-head Q/K RMSNorm -> RoPE -> KV cache ->
+ * attention -> wo + residual -> FFN block (dense SwiGLU, or the MoE block with
+ * router/top-k/experts) + residual; then the final norm, lm_head, greedy.
+ */
+#ifndef LLMTOY_HOST_DECODER_H
+#define LLMTOY_HOST_DECODER_H
+
+#include "llmtoy_cuda.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct lth_layer {
+    const float *attn_norm, *ffn_norm;   /* device [d_model]                           */
+    const lt_tensor *wqkv;               /* [nq + 2 nkv][d] stacked rows, or NULL:      */
+    const lt_tensor *wq, *wk, *wv;       /*   separate [nq][d], [nkv][d], [nkv][d]      */
+    const lt_tensor *wo;                 /* [d][nq]                                     */
+    const float *qkv_bias;               /* device [nq + 2 nkv] or NULL (forward.zig:285) */
+    const float *q_norm, *k_norm;        /* device [head_dim] or NULL (per-head RMSNorm) */
+    const lt_tensor *ffn_gate, *ffn_up, *ffn_down;         /* dense FFN (router NULL)   */
+    const lt_tensor *router, *exp_gate, *exp_up, *exp_down; /* MoE FFN                 */
+} lth_layer;
+
+typedef struct lth_model {
+    uint32_t n_layers, d_model, n_heads, n_kv_heads, head_dim, vocab;
+    uint32_t n_used;       /* experts per token (MoE layers) */
+    uint32_t norm_topk;    /* renormalise the selected weights */
+    uint32_t rope_neox;    /* 0: rope.zig:14 pairs, 1: rope.zig:56 halves */
+    uint32_t act;          /* lt_act of the FFN */
+    float eps, rope_theta;
+    uint32_t kv_cap;       /* positions per sequence */
+    const lt_tensor *token_emb, *lm_head;
+    const float *out_norm; /* device [d_model] */
+    const lth_layer *layers;
+} lth_model;
+
+typedef struct lth_decoder lth_decoder;
+
+/* The model description is copied; tensors and device buffers it points to
+ * must outlive the decoder. */
+lt_status lth_decoder_create(lt_ctx *ctx, const lth_model *m, lth_decoder **out);
+void lth_decoder_free(lth_decoder *d);
+/* Start a sequence: prompt into the device token stream, position 0. */
+lt_status lth_decoder_start(lth_decoder *d, const uint32_t *prompt, uint32_t n_prompt);
+/* Enqueue one step with eager launches (the first call also sizes every
+ * scratch buffer, so a capture afterwards allocates nothing). */
+lt_status lth_decoder_step(lth_decoder *d);
+/* Capture one step as a graph (done on first use by lth_decoder_replay). */
+lt_status lth_decoder_capture(lth_decoder *d);
+/* Replay the captured step n_steps times (asynchronous). */
+lt_status lth_decoder_replay(lth_decoder *d, uint32_t n_steps);
+/* Device address of the last step's logits [vocab]. */
+const float *lth_decoder_logits(const lth_decoder *d);
+/* Copy tokens[0, n) of the device token stream to the host (synchronises). */
+lt_status lth_decoder_tokens(lth_decoder *d, uint32_t *host_out, uint32_t n);
+/* Prompt -> n_gen greedy tokens into out (n_prompt + n_gen - 1 steps). */
+lt_status lth_generate(lth_decoder *d, const uint32_t *prompt, uint32_t n_prompt, uint32_t n_gen,
+                       uint32_t *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

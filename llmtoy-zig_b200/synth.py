@@ -110,3 +110,71 @@ class MoeLayer:
         """Weight bytes one selected expert streams (gate + up + down)."""
         e = self.n_experts
         return (self.gate.nbytes + (self.up.nbytes if self.up is not None else 0) + self.down.nbytes) // e
+
+
+class DecoderLayer:
+    """Attention + FFN weights of one decoder layer (GGUF bytes, f32 norms)."""
+
+    def __init__(self, rng, d: int, n_heads: int, n_kv: int, hd: int, attn_type: int, qk_norm: bool,
+                 qkv_bias: bool, norms_random: bool, d_ffn: int, ffn_type: int, moe: "MoeLayer | None"):
+        nq, nkv = n_heads * hd, n_kv * hd
+        norm = (lambda n: rng.uniform(0.5, 1.5, n).astype(np.float32)) if norms_random else \
+            (lambda n: np.ones(n, np.float32))
+        self.attn_norm, self.ffn_norm = norm(d), norm(d)
+        self.wq = matrix(rng, attn_type, nq, d)
+        self.wk = matrix(rng, attn_type, nkv, d)
+        self.wv = matrix(rng, attn_type, nkv, d)
+        self.wo = matrix(rng, attn_type, d, nq)
+        self.attn_type = attn_type
+        self.q_norm = norm(hd) if qk_norm else None
+        self.k_norm = norm(hd) if qk_norm else None
+        self.qkv_bias = rng.normal(0.0, 0.02, nq + 2 * nkv).astype(np.float32) if qkv_bias else None
+        self.moe = moe
+        if moe is None:
+            self.ffn_type = ffn_type
+            self.ffn_gate = matrix(rng, ffn_type, d_ffn, d)
+            self.ffn_up = matrix(rng, ffn_type, d_ffn, d)
+            self.ffn_down = matrix(rng, ffn_type, d, d_ffn)
+
+    @property
+    def wqkv(self) -> np.ndarray:
+        """Q, K and V rows stacked (one matvec on the device)."""
+        return np.concatenate([self.wq, self.wk, self.wv], axis=0)
+
+
+class DecoderModel:
+    """Seeded synthetic decoder: config 0 (dense Qwen2-0.5B shape: Q8_0
+    everywhere, consecutive-pair RoPE) or config 2 (Qwen3-30B-A3B shape:
+    Q8_0 attention with per-head Q/K RMSNorm and NeoX RoPE, Q4_K MoE FFN with
+    renormalised top-k, Q6_K lm_head), at any size."""
+
+    def __init__(self, rng, n_layers: int, d_model: int, n_heads: int, n_kv_heads: int, head_dim: int, vocab: int,
+                 d_ffn: int = 0, n_experts: int = 0, k: int = 0, d_expert: int = 0, attn_type: int = Q8_0,
+                 emb_type: int = Q8_0, lm_type: int = Q8_0, ffn_type: int = Q8_0, expert_type: int = Q4_K,
+                 qk_norm: bool = False, qkv_bias: bool = False, rope_neox: bool = False, norm_topk: bool = False,
+                 norms_random: bool = False, eps: float = 1e-6, rope_theta: float = 1e6):
+        self.n_layers, self.d_model, self.n_heads, self.n_kv_heads = n_layers, d_model, n_heads, n_kv_heads
+        self.head_dim, self.vocab, self.d_ffn = head_dim, vocab, d_ffn
+        self.n_experts, self.k, self.d_expert = n_experts, k, d_expert
+        self.emb_type, self.lm_type, self.attn_type = emb_type, lm_type, attn_type
+        self.ffn_type, self.expert_type = ffn_type, expert_type
+        self.rope_neox, self.norm_topk, self.eps, self.rope_theta = rope_neox, norm_topk, eps, rope_theta
+        self.token_emb = matrix(rng, emb_type, vocab, d_model)
+        self.layers = []
+        for _ in range(n_layers):
+            moe = MoeLayer(rng, d_model, n_experts, d_expert, expert_type, expert_type) if n_experts else None
+            self.layers.append(DecoderLayer(rng, d_model, n_heads, n_kv_heads, head_dim, attn_type, qk_norm,
+                                            qkv_bias, norms_random, d_ffn, ffn_type, moe))
+        self.out_norm = (rng.uniform(0.5, 1.5, d_model) if norms_random else np.ones(d_model)).astype(np.float32)
+        self.lm_head = matrix(rng, lm_type, vocab, d_model)
+
+
+def config0_model(rng, n_layers: int = 24, vocab: int = 151936, **kw) -> DecoderModel:
+    """Config 0: dense Qwen2-0.5B shape, all Q8_0."""
+    return DecoderModel(rng, n_layers, 896, 14, 2, 64, vocab, d_ffn=4864, **kw)
+
+
+def config2_model(rng, n_layers: int = 48, vocab: int = 151936, **kw) -> DecoderModel:
+    """Config 2: Qwen3-30B-A3B shape, Q8_0 attention, Q4_K experts, Q6_K lm_head."""
+    return DecoderModel(rng, n_layers, 2048, 32, 4, 128, vocab, n_experts=128, k=8, d_expert=768,
+                        lm_type=Q6_K, qk_norm=True, rope_neox=True, norm_topk=True, **kw)

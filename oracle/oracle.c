@@ -711,3 +711,97 @@ uint32_t orc_greedy(const float *logits, size_t n) {
         if (logits[i] > logits[best]) best = (uint32_t)i;
     return best;
 }
+
+/* rope.zig:14-31 and :56-75 */
+void orc_rope(float *vec, size_t len, size_t pos, float theta, int neox) {
+    const size_t half = len / 2;
+    for (size_t i = 0; i < half; i++) {
+        const float freq = 1.0f / powf(theta, (float)(2 * i) / (float)len);
+        const float angle = (float)pos * freq;
+        const float c = cosf(angle), s = sinf(angle);
+        const size_t i0 = neox ? i : 2 * i, i1 = neox ? i + half : 2 * i + 1;
+        const float x0 = vec[i0], x1 = vec[i1];
+        vec[i0] = x0 * c - x1 * s;
+        vec[i1] = x0 * s + x1 * c;
+    }
+}
+
+/* attn.zig:13-42 */
+void orc_sdp_attn(float *out, const float *q, const float *ks, const float *vs, size_t seq_len,
+                  size_t head_dim, float scale) {
+    float *scores = (float *)malloc(seq_len * 4);
+    for (size_t i = 0; i < seq_len; i++) {
+        float dot = 0.0f;
+        for (size_t j = 0; j < head_dim; j++) dot += q[j] * ks[i * head_dim + j];
+        scores[i] = dot * scale;
+    }
+    orc_softmax(scores, seq_len);
+    memset(out, 0, head_dim * 4);
+    for (size_t i = 0; i < seq_len; i++)
+        for (size_t j = 0; j < head_dim; j++) out[j] += scores[i] * vs[i * head_dim + j];
+    free(scores);
+}
+
+/* forward.zig:229-316 (see oracle.h) */
+int orc_model_step(const orc_model *m, float *k_cache, float *v_cache, size_t kv_cap, uint32_t token,
+                   size_t pos, float *logits, orc_pool *pool) {
+    const size_t d = m->d_model, hd = m->head_dim, nq = m->n_heads * hd, nkv = m->n_kv_heads * hd;
+    const size_t ff = m->d_ffn, seq = pos + 1;
+    if (pos >= kv_cap || token >= m->vocab) return -1;
+    size_t max_cols = d > nq ? d : nq;
+    if (ff > max_cols) max_cols = ff;
+    const size_t nthr = (size_t)orc_pool_threads(pool);
+    float *scratch = (float *)malloc((nthr ? nthr : 1) * max_cols * 4);
+    float *x = (float *)malloc(d * 4), *xb = (float *)malloc(d * 4), *q = (float *)malloc(nq * 4);
+    float *kn = (float *)malloc(nkv * 4), *vn = (float *)malloc(nkv * 4), *att = (float *)malloc(nq * 4);
+    float *ks = (float *)malloc(seq * hd * 4), *vs = (float *)malloc(seq * hd * 4);
+    float *proj = (float *)malloc(d * 4), *g = (float *)malloc((ff ? ff : 1) * 4);
+    float *u = (float *)malloc((ff ? ff : 1) * 4), *fo = (float *)malloc(d * 4);
+    const float scale = 1.0f / sqrtf((float)hd);
+    int rc = orc_dequant_row(m->token_emb + (size_t)token * orc_row_bytes(m->emb_type, d), x, d, m->emb_type);
+    for (size_t l = 0; l < m->n_layers && rc == 0; l++) {
+        const orc_layer *L = &m->layers[l];
+        float *kc = k_cache + l * kv_cap * nkv, *vc = v_cache + l * kv_cap * nkv;
+        orc_rmsnorm(xb, x, L->attn_norm, d, m->eps);
+        rc |= orc_quant_matvec_par(q, L->wq, L->wq_type, xb, nq, d, scratch, pool);
+        rc |= orc_quant_matvec_par(kn, L->wk, L->wk_type, xb, nkv, d, scratch, pool);
+        rc |= orc_quant_matvec_par(vn, L->wv, L->wv_type, xb, nkv, d, scratch, pool);
+        if (L->q_bias) for (size_t i = 0; i < nq; i++) q[i] += L->q_bias[i];
+        if (L->k_bias) for (size_t i = 0; i < nkv; i++) kn[i] += L->k_bias[i];
+        if (L->v_bias) for (size_t i = 0; i < nkv; i++) vn[i] += L->v_bias[i];
+        if (L->q_norm) for (size_t h = 0; h < m->n_heads; h++) orc_rmsnorm(q + h * hd, q + h * hd, L->q_norm, hd, m->eps);
+        if (L->k_norm) for (size_t h = 0; h < m->n_kv_heads; h++) orc_rmsnorm(kn + h * hd, kn + h * hd, L->k_norm, hd, m->eps);
+        for (size_t h = 0; h < m->n_heads; h++) orc_rope(q + h * hd, hd, pos, m->rope_theta, m->rope_neox);
+        for (size_t h = 0; h < m->n_kv_heads; h++) orc_rope(kn + h * hd, hd, pos, m->rope_theta, m->rope_neox);
+        memcpy(kc + pos * nkv, kn, nkv * 4);
+        memcpy(vc + pos * nkv, vn, nkv * 4);
+        for (size_t h = 0; h < m->n_heads; h++) {
+            const size_t kvh = h / (m->n_heads / m->n_kv_heads);
+            for (size_t s = 0; s < seq; s++) {
+                memcpy(ks + s * hd, kc + s * nkv + kvh * hd, hd * 4);
+                memcpy(vs + s * hd, vc + s * nkv + kvh * hd, hd * 4);
+            }
+            orc_sdp_attn(att + h * hd, q + h * hd, ks, vs, seq, hd, scale);
+        }
+        rc |= orc_quant_matvec_par(proj, L->wo, L->wo_type, att, d, nq, scratch, pool);
+        for (size_t i = 0; i < d; i++) x[i] += proj[i];
+        orc_rmsnorm(xb, x, L->ffn_norm, d, m->eps);
+        if (L->router) {
+            rc |= orc_moe_layer(fo, xb, 1, d, L->router, m->n_experts, m->k, m->norm_topk, NULL, L->e_gate, L->e_up,
+                                L->e_gate_type, L->e_down, L->e_down_type, m->d_expert, 0, pool, NULL, NULL);
+        } else {
+            rc |= orc_quant_matvec_par(g, L->w_gate, L->ffn_gate_type, xb, ff, d, scratch, pool);
+            rc |= orc_quant_matvec_par(u, L->w_up, L->ffn_gate_type, xb, ff, d, scratch, pool);
+            for (size_t i = 0; i < ff; i++) g[i] = orc_silu(g[i]) * u[i];
+            rc |= orc_quant_matvec_par(fo, L->w_down, L->ffn_down_type, g, d, ff, scratch, pool);
+        }
+        for (size_t i = 0; i < d; i++) x[i] += fo[i];
+    }
+    if (rc == 0) {
+        orc_rmsnorm(xb, x, m->out_norm, d, m->eps);
+        rc |= orc_quant_matvec_par(logits, m->lm_head, m->lm_type, xb, m->vocab, d, scratch, pool);
+    }
+    free(scratch); free(x); free(xb); free(q); free(kn); free(vn); free(att); free(ks); free(vs);
+    free(proj); free(g); free(u); free(fo);
+    return rc ? -1 : 0;
+}

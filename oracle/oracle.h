@@ -121,6 +121,55 @@ int orc_moe_layer(float *out, const float *x, size_t n_tok, size_t d_model,
 /* greedy, src/model/sample.zig:11-17 (lowest index among equal maxima) */
 uint32_t orc_greedy(const float *logits, size_t n);
 
+/* RoPE on one head vector, src/ops/rope.zig:14-31 (consecutive pairs) and
+ * :56-75 (NeoX halves, neox != 0). */
+void orc_rope(float *vec, size_t len, size_t pos, float theta, int neox);
+
+/* sdpAttn, src/ops/attn.zig:13-42: one query over seq_len cached rows. */
+void orc_sdp_attn(float *out, const float *q, const float *ks, const float *vs, size_t seq_len,
+                  size_t head_dim, float scale);
+
+/*
+ * One token of a decoder: forwardOneModel (src/model/forward.zig:229-316).
+ * Per layer: rmsnorm -> Q/K/V matvecs (+ optional biases, :285-287) ->
+ * optional per-head Q/K RMSNorm (the style of gemma4/forward.zig:267-268) ->
+ * RoPE (rope_neox selects rope.zig:56 over :14) -> KV store at pos ->
+ * sdpAttn per head with scale 1/sqrt(hd) -> wo + residual -> FFN block:
+ * dense SwiGLU (router == NULL, forward.zig:307-312) or the MoE layer of
+ * orc_moe_layer (norm_topk renormalisation, SiLU) -> residual.  Then the final
+ * rmsnorm, lm_head and logits.  The Qwen3-MoE assembly (QK norm + NeoX RoPE +
+ * MoE block) is NEW oracle code: the reference has no such model.
+ * KV caches: [n_layers][kv_cap][n_kv*hd] f32, slot = pos (pos < kv_cap).
+ */
+typedef struct orc_layer {
+    const float *attn_norm, *ffn_norm;          /* [d] */
+    const uint8_t *wq, *wk, *wv, *wo;
+    uint32_t wq_type, wk_type, wv_type, wo_type;
+    const float *q_bias, *k_bias, *v_bias;      /* nullable */
+    const float *q_norm, *k_norm;               /* [hd], nullable */
+    /* dense FFN: gate/up [d_ffn][d], down [d][d_ffn] */
+    const uint8_t *w_gate, *w_up, *w_down;
+    uint32_t ffn_gate_type, ffn_down_type;
+    /* MoE FFN when router != NULL */
+    const float *router;                        /* [n_experts][d] */
+    const uint8_t *e_gate, *e_up, *e_down;
+    uint32_t e_gate_type, e_down_type;
+} orc_layer;
+
+typedef struct orc_model {
+    size_t n_layers, d_model, n_heads, n_kv_heads, head_dim, d_ffn, vocab;
+    size_t n_experts, k, d_expert;
+    int norm_topk, rope_neox;
+    float eps, rope_theta;
+    const uint8_t *token_emb; uint32_t emb_type;
+    const float *out_norm;
+    const uint8_t *lm_head; uint32_t lm_type;
+    const orc_layer *layers;
+} orc_model;
+
+int orc_model_step(const orc_model *m, float *k_cache, float *v_cache, size_t kv_cap, uint32_t token,
+                   size_t pos, float *logits, orc_pool *pool);
+
 #ifdef __cplusplus
 }
 #endif

@@ -57,6 +57,6 @@ def ctx(pkg):
     assert torch.cuda.is_available(), "gpu test needs a CUDA device"
     torch.cuda.init()
     c = pkg.Context(0)
-    c.set_stream(torch.cuda.current_stream())
+    c.set_stream(None)  # own stream: inputs are copied synchronously, results read after a device sync
     yield c
     c.close()

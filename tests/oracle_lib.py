@@ -58,6 +58,9 @@ def lib() -> ctypes.CDLL:
         "orc_moe_forward": (I, [P, P, SZ, P, U32, P, U32, P, SZ, SZ, SZ, P]),
         "orc_moe_layer": (I, [P, P, SZ, SZ, P, SZ, SZ, I, P, P, P, U32, P, U32, SZ, I, P, P, P]),
         "orc_greedy": (U32, [P, SZ]),
+        "orc_rope": (None, [P, SZ, SZ, F, I]),
+        "orc_sdp_attn": (None, [P, P, P, P, SZ, SZ, F]),
+        "orc_model_step": (I, [P, P, P, SZ, U32, SZ, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -163,3 +166,83 @@ def moe_layer(layer, x: np.ndarray, k: int, norm_topk: bool, act: int = 0, exper
 def greedy(logits) -> int:
     a = f32(logits)
     return int(lib().orc_greedy(_p(a), a.size))
+
+
+# ── decoder model (orc_model_step) ───────────────────────────────────────────
+
+class OrcLayer(ctypes.Structure):
+    P = ctypes.c_void_p
+    _fields_ = [("attn_norm", P), ("ffn_norm", P), ("wq", P), ("wk", P), ("wv", P), ("wo", P),
+                ("wq_type", ctypes.c_uint32), ("wk_type", ctypes.c_uint32), ("wv_type", ctypes.c_uint32),
+                ("wo_type", ctypes.c_uint32), ("q_bias", P), ("k_bias", P), ("v_bias", P), ("q_norm", P),
+                ("k_norm", P), ("w_gate", P), ("w_up", P), ("w_down", P), ("ffn_gate_type", ctypes.c_uint32),
+                ("ffn_down_type", ctypes.c_uint32), ("router", P), ("e_gate", P), ("e_up", P), ("e_down", P),
+                ("e_gate_type", ctypes.c_uint32), ("e_down_type", ctypes.c_uint32)]
+
+
+class OrcModel(ctypes.Structure):
+    SZ = ctypes.c_size_t
+    _fields_ = [("n_layers", SZ), ("d_model", SZ), ("n_heads", SZ), ("n_kv_heads", SZ), ("head_dim", SZ),
+                ("d_ffn", SZ), ("vocab", SZ), ("n_experts", SZ), ("k", SZ), ("d_expert", SZ),
+                ("norm_topk", ctypes.c_int), ("rope_neox", ctypes.c_int), ("eps", ctypes.c_float),
+                ("rope_theta", ctypes.c_float), ("token_emb", ctypes.c_void_p), ("emb_type", ctypes.c_uint32),
+                ("out_norm", ctypes.c_void_p), ("lm_head", ctypes.c_void_p), ("lm_type", ctypes.c_uint32),
+                ("layers", ctypes.POINTER(OrcLayer))]
+
+
+class OracleDecoder:
+    """orc_model_step over a synth.DecoderModel, with its own f32 KV cache."""
+
+    def __init__(self, m, kv_cap: int, pool: Pool | None = None):
+        self.m, self.cap, self.pool = m, kv_cap, pool
+        self._keep = []
+
+        def p(a):
+            if a is None:
+                return None
+            a = np.ascontiguousarray(a)
+            self._keep.append(a)
+            return a.ctypes.data
+
+        nq, nkv = m.n_heads * m.head_dim, m.n_kv_heads * m.head_dim
+        self._layers = (OrcLayer * m.n_layers)()
+        for i, L in enumerate(m.layers):
+            b = L.qkv_bias
+            o = OrcLayer()
+            o.attn_norm, o.ffn_norm = p(L.attn_norm), p(L.ffn_norm)
+            o.wq, o.wk, o.wv, o.wo = p(L.wq), p(L.wk), p(L.wv), p(L.wo)
+            o.wq_type = o.wk_type = o.wv_type = o.wo_type = L.attn_type
+            if b is not None:
+                o.q_bias, o.k_bias, o.v_bias = p(b[:nq]), p(b[nq:nq + nkv]), p(b[nq + nkv:])
+            o.q_norm, o.k_norm = p(L.q_norm), p(L.k_norm)
+            if L.moe is None:
+                o.w_gate, o.w_up, o.w_down = p(L.ffn_gate), p(L.ffn_up), p(L.ffn_down)
+                o.ffn_gate_type = o.ffn_down_type = L.ffn_type
+            else:
+                o.router = p(f32(L.moe.router))
+                o.e_gate, o.e_up, o.e_down = p(L.moe.gate), p(L.moe.up), p(L.moe.down)
+                o.e_gate_type, o.e_down_type = L.moe.gate_type, L.moe.down_type
+            self._layers[i] = o
+        self.model = OrcModel(m.n_layers, m.d_model, m.n_heads, m.n_kv_heads, m.head_dim, m.d_ffn, m.vocab,
+                              m.n_experts, m.k, m.d_expert, int(m.norm_topk), int(m.rope_neox), m.eps, m.rope_theta,
+                              p(m.token_emb), m.emb_type, p(m.out_norm), p(m.lm_head), m.lm_type, self._layers)
+        self.kc = np.zeros(m.n_layers * kv_cap * nkv, np.float32)
+        self.vc = np.zeros_like(self.kc)
+
+    def step(self, token: int, pos: int) -> np.ndarray:
+        logits = np.empty(self.m.vocab, np.float32)
+        rc = lib().orc_model_step(ctypes.byref(self.model), _p(self.kc), _p(self.vc), self.cap, token, pos,
+                                  _p(logits), self.pool.ptr if self.pool else None)
+        assert rc == 0
+        return logits
+
+    def generate(self, prompt, n_gen: int):
+        """(generated ids, logits of every step) -- the reference generate loop."""
+        toks = list(prompt)
+        all_logits = []
+        for pos in range(len(prompt) + n_gen - 1):
+            lg = self.step(toks[pos], pos)
+            all_logits.append(lg)
+            if pos + 1 >= len(prompt):
+                toks.append(greedy(lg))
+        return toks[len(prompt):], all_logits

@@ -33,7 +33,7 @@ def tc(pkg):
             del os.environ["LLMTOY_TC_MIN_TOKENS"]
         else:
             os.environ["LLMTOY_TC_MIN_TOKENS"] = old
-    c.set_stream(torch.cuda.current_stream())
+    c.set_stream(None)  # own stream: inputs are copied synchronously, results read after a device sync
     yield c
     c.close()
 
