@@ -157,6 +157,25 @@ def q4k_bytes_device(torch, gen, rows: int, cols: int):
     return b.view(-1)
 
 
+def q8_0_bytes_device(torch, gen, rows: int, cols: int):
+    """Q8_0 blocks: f16 d = 0.02/127 * U(0.5, 1.5), int8 quants uniform in [-127, 127]."""
+    nb = rows * (cols // 32)
+    b = torch.empty((nb, 34), dtype=torch.uint8, device="cuda")
+    b[:, 2:] = torch.randint(-127, 128, (nb, 32), dtype=torch.int8, device="cuda", generator=gen).view(torch.uint8)
+    d = ((torch.rand(nb, device="cuda", generator=gen) + 0.5) * (0.02 / 127)).half()
+    b[:, 0:2] = d.view(torch.uint8).view(nb, 2)
+    return b.view(-1)
+
+
+def q6k_bytes_device(torch, gen, rows: int, cols: int):
+    """Q6_K superblocks: uniform ql/qh/scale bytes, f16 d ~ U(1e-3, 4e-3) at the end."""
+    nb = rows * (cols // 256)
+    b = torch.randint(0, 256, (nb, 210), dtype=torch.uint8, device="cuda", generator=gen)
+    d = (torch.rand(nb, device="cuda", generator=gen) * 3e-3 + 1e-3).half()
+    b[:, 208:210] = d.view(torch.uint8).view(nb, 2)
+    return b.view(-1)
+
+
 class DeviceLayer:
     def __init__(self, pkg, ctx, torch, gen):
         router = torch.randn(N_EXPERTS, D_MODEL, device="cuda", generator=gen) * 0.02
@@ -273,6 +292,8 @@ def main() -> None:
     ap.add_argument("--ep-tokens", type=int, default=8 * 2048,
                     help="config 4: prompt tokens over all ranks, experts sharded 128/N (0: skip)")
     ap.add_argument("--ep-layers", type=int, default=2)
+    ap.add_argument("--model-tokens", type=int, default=128,
+                    help="configs 2 and 0: greedy tokens after a 32-token prompt (0: skip)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -428,6 +449,13 @@ def main() -> None:
     if args.prefill_tokens > 0:
         prefill = measure_prefill(args, pkg, ctx, torch, stream, gen, layers, rank, world, dist)
 
+    model_decode = None
+    if args.model_tokens > 0:
+        model_decode = {"config2": measure_model_decode(args, pkg, ctx, torch, stream, layers, rank, world, dist,
+                                                        "config2"),
+                        "config0": measure_model_decode(args, pkg, ctx, torch, stream, layers, rank, world, dist,
+                                                        "config0")}
+
     ep_prefill = None
     if args.ep_tokens > 0:
         ep_prefill = measure_ep_prefill(args, pkg, torch, stream, rank, world, local, dist)
@@ -444,7 +472,8 @@ def main() -> None:
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": int(round(args.steps * launches_per_step)), "clocks": clocks,
             "kernels_profiled": kernels, "layer_bytes": layer_bytes,
-            "graph": not args.no_graph, "prefill": prefill, "ep_prefill": ep_prefill,
+            "graph": not args.no_graph, "prefill": prefill, "model_decode": model_decode,
+            "ep_prefill": ep_prefill,
         }
         print(json.dumps(line), flush=True)
 
@@ -519,13 +548,173 @@ def measure_prefill(args, pkg, ctx, torch, stream, gen, layers, rank, world, dis
     return out
 
 
+MODEL_CFG = {
+    # name: (layers, d, heads, kv heads, head dim, vocab, d_ffn, lm type, qk norm, neox, MoE)
+    "config2": (48, 2048, 32, 4, 128, 151936, 0, "q6_k", True, True, True),
+    "config0": (24, 896, 14, 2, 64, 151936, 4864, "q8_0", False, False, False),
+}
+
+
+def model_bytes_per_token(name: str, ctx_len: float) -> float:
+    """Algorithmic HBM bytes of one decode step: every weight the token reads
+    (attention projections, router + 8 experts or the dense FFN, norms, the
+    embedding row, lm_head) plus the KV cache read at the mean context."""
+    L, d, nh, nkv, hd, V, F, lm, _, _, moe = MODEL_CFG[name]
+    q8 = lambda r, c: r * (c // 32) * 34  # noqa: E731
+    attn = q8(nh * hd + 2 * nkv * hd, d) + q8(d, nh * hd)
+    ffn = TOP_K * EXPERT_BYTES + ROUTER_BYTES if moe else 3 * q8(F, d)
+    lm_bytes = V * (d // 256) * 210 if lm == "q6_k" else q8(V, d)
+    kv = 2 * ctx_len * nkv * hd * 4
+    return L * (attn + ffn + kv + 2 * d * 4) + lm_bytes + q8(1, d)
+
+
+def measure_model_decode(args, pkg, ctx, torch, stream, moe_layers, rank, world, dist, name: str) -> dict:
+    """Greedy decode of a whole model through the C++ host loop
+    (llmtoy-zig_b200/host/decoder.cpp): a 32-token prompt, then
+    args.model_tokens tokens, one captured graph per token.  config2 reuses
+    the stack's 48 MoE layers (router + experts) and adds Q8_0 attention with
+    QK norm, NeoX RoPE, a Q8_0 embedding and the Q6_K lm_head; config0 is the
+    dense Q8_0 Qwen2-0.5B shape.  Device time of all steps (prompt and
+    generated tokens are the same one-token step), replicas on N > 1."""
+    decoder = importlib.import_module("llmtoy-zig_b200.decoder")
+    L, d, nh, nkv, hd, V, F, lm, qk, neox, moe = MODEL_CFG[name]
+    n_prompt, n_gen = 32, args.model_tokens
+    cap = 4096
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0x11A70002 + 1000 * rank if moe else 0x11A70000 + 1000 * rank)
+    keep, tensors = [], []
+
+    def up(b, t, r, c, e=0):
+        tt = ctx.upload_device(b, t, r, c, e)
+        tensors.append(tt)
+        return tt
+
+    ones = lambda n: keep.append(torch.ones(n, device="cuda")) or keep[-1]  # noqa: E731
+    specs = []
+    for li in range(L):
+        ls = decoder.LayerSpec(attn_norm=ones(d), ffn_norm=ones(d),
+                               wo=up(q8_0_bytes_device(torch, gen, d, nh * hd), pkg.Q8_0, d, nh * hd),
+                               wqkv=up(q8_0_bytes_device(torch, gen, nh * hd + 2 * nkv * hd, d), pkg.Q8_0,
+                                       nh * hd + 2 * nkv * hd, d),
+                               q_norm=ones(hd) if qk else None, k_norm=ones(hd) if qk else None)
+        if moe:
+            ML = moe_layers[li % len(moe_layers)]
+            ls.router, ls.exp_gate, ls.exp_up, ls.exp_down = ML.router, ML.gate, ML.up, ML.down
+        else:
+            ls.ffn_gate = up(q8_0_bytes_device(torch, gen, F, d), pkg.Q8_0, F, d)
+            ls.ffn_up = up(q8_0_bytes_device(torch, gen, F, d), pkg.Q8_0, F, d)
+            ls.ffn_down = up(q8_0_bytes_device(torch, gen, d, F), pkg.Q8_0, d, F)
+        specs.append(ls)
+    emb = up(q8_0_bytes_device(torch, gen, V, d), pkg.Q8_0, V, d)
+    lmh = up(q6k_bytes_device(torch, gen, V, d), pkg.Q6_K, V, d) if lm == "q6_k" else \
+        up(q8_0_bytes_device(torch, gen, V, d), pkg.Q8_0, V, d)
+    spec = decoder.ModelSpec(d_model=d, n_heads=nh, n_kv_heads=nkv, head_dim=hd, vocab=V, token_emb=emb,
+                             lm_head=lmh, out_norm=ones(d), layers=specs, n_used=TOP_K if moe else 0,
+                             norm_topk=moe, rope_neox=neox, eps=1e-6, rope_theta=1e6, kv_cap=cap)
+    torch.cuda.synchronize()
+    prompt = np.random.Generator(np.random.PCG64(0x11A70000 + (2 if moe else 0))).integers(0, V, n_prompt).tolist()
+    steps = n_prompt + n_gen - 1
+    dec = decoder.Decoder(ctx, spec)
+    first = dec.generate(prompt, n_gen)  # warm-up: eager step, capture, replays
+    for _ in range(max(0, args.warmup - 1)):
+        dec.generate(prompt, n_gen)
+    # device time of the whole generation (graph replays on the context stream)
+    dec.start(prompt)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ev0.record(stream)
+        dec.replay(steps)
+        ev1.record(stream)
+        stream.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    toks = dec.tokens(n_prompt + n_gen)[n_prompt:]
+    deterministic = toks == first
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / steps
+    # end to end through the public entry point: host prompt in, host tokens out
+    t0 = time.perf_counter()
+    dec.generate(prompt, n_gen)
+    e2e_s = time.perf_counter() - t0
+    if dist is not None:
+        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    # per-kernel times of one eager step
+    dec.start(prompt)
+    ctx.profile(True)
+    ctx.profile_reset()
+    dec.step()
+    ctx.sync()
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    ctx.profile_reset()
+    dec.close()
+    for tt in tensors:
+        tt.free()
+    peak, kind = measured_peaks()
+    mean_ctx = n_prompt + (n_gen - 1) / 2.0
+    bpt = model_bytes_per_token(name, mean_ctx)
+    achieved = bpt / (ms_step / 1e3) / 1e9
+    out = {
+        "metric": f"greedy decode tok/s ({name}: {'Qwen3-30B-A3B' if moe else 'Qwen2-0.5B'} shape, {L} layers)",
+        "value": world / (ms_step / 1e3), "unit": "tok/s", "ms_per_token": ms_step, "steps": steps,
+        "prompt_tokens": n_prompt, "generated_tokens": n_gen, "scaling": "weak",
+        "deterministic_stream": deterministic,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": kind, "algorithmic_bytes_per_token": bpt,
+                     "note": "whole decode step (all kernels of one token); weights + KV at the mean context"},
+        "e2e": {"value": world * n_gen / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * n_prompt / n_gen,
+                "d2h_bytes_per_step": 4.0 * (n_prompt + n_gen) / n_gen,
+                "path": "lth_generate: host prompt ids in, host token ids out (prompt steps included)"},
+        "kernels_per_token": {k: {"count": v["count"], "us": round(1e3 * v["total_ms"], 1)} for k, v in prof.items()},
+        "gpu_launches_per_token": int(sum(v["count"] for v in prof.values())),
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and args.cpu_budget > 0:
+        out["cpu_baseline"] = cpu_model_rate(name, min(args.cpu_budget, 10.0))
+    return out
+
+
+def cpu_model_rate(name: str, budget_s: float) -> dict:
+    """The CPU restatement (orc_model_step, all host threads) on the same
+    model shape: 4 distinct host layer sets cycled through all layers (each
+    ~360 MB for config2, far beyond the CPU caches), full vocabulary."""
+    sys.path.insert(0, str(REPO / "tests"))
+    oracle = importlib.import_module("oracle_lib")
+    synth = importlib.import_module("llmtoy-zig_b200.synth")
+    rng = np.random.Generator(np.random.PCG64(synth.config_seed(2 if name == "config2" else 0)))
+    L = MODEL_CFG[name][0]
+    m = synth.config2_model(rng, n_layers=4) if name == "config2" else synth.config0_model(rng, n_layers=4)
+    m.layers = [m.layers[i % 4] for i in range(L)]
+    m.n_layers = L
+    threads = os.cpu_count() or 1
+    pool = oracle.Pool(threads)
+    dec = oracle.OracleDecoder(m, 64, pool)
+    dec.step(1, 0)
+    t0 = time.perf_counter()
+    n = 0
+    while n < 2 or time.perf_counter() - t0 < budget_s:
+        dec.step(1 + n, (n + 1) % 64)
+        n += 1
+    dt = time.perf_counter() - t0
+    pool.close()
+    return {"value": n / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{n} decode steps of the {L}-layer model in {dt:.1f}s (4 distinct layer weight sets "
+                      f"cycled; C restatement of forwardOneModel, zig absent)"}
+
+
 def zipf_router(torch, n_experts: int, d: int, s: float, mu: float, seed: int):
     """Router weights (replicated: the same seed on every rank) whose logits
-    carry a bias b_e = 0.9 * log(1 / rank_e^s) along a fixed unit direction u,
-    with expert ranks a seeded permutation; hidden states get mu * u added, so
-    after the RMSNorm each token's logit of expert e shifts by about b_e and
-    expert popularity falls off like Zipf(s).  0.9 is the spread of the
-    unbiased logits (N(0, 0.02^2) weights over 2048 unit-variance inputs)."""
+    carry a bias b_e = ln p_e, p_e proportional to rank_e^-s (Zipf), along a
+    fixed unit direction u, with expert ranks a seeded permutation; hidden
+    states get mu * u added, so after the RMSNorm each token's logit of
+    expert e shifts by about b_e."""
     g = torch.Generator(device="cuda")
     g.manual_seed(seed)
     base = torch.randn(n_experts, d, device="cuda", generator=g) * 0.02
@@ -534,7 +723,7 @@ def zipf_router(torch, n_experts: int, d: int, s: float, mu: float, seed: int):
     order = torch.randperm(n_experts, device="cuda", generator=g)
     ranks = torch.empty(n_experts, device="cuda")
     ranks[order] = torch.arange(1, n_experts + 1, device="cuda", dtype=torch.float32)
-    b = -0.9 * s * torch.log(ranks)
+    b = -s * torch.log(ranks)  # ln p_e up to a constant
     b = b - b.mean()
     rms = (1.0 + mu * mu / d) ** 0.5
     return (base + (b * rms / mu)[:, None] * u[None, :]).contiguous(), u
