@@ -316,6 +316,26 @@ lt_status lt_attn_decode(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_q
                          const float *dev_k_cache, const float *dev_v_cache,
                          const uint32_t *dev_pos, float *dev_out);
 
+/* The attention half of a decoder layer for one token (forward.zig:272-305
+ * with the per-head Q/K norms of gemma4/forward.zig:267-268):
+ *   xn = rmsnorm(x) * norm_w;  qkv = wqkv . xn (+ bias);  per-head Q/K norm,
+ *   RoPE, K/V into the caches at *dev_pos;  att = attention per head;
+ *   out = x + wo . att.
+ * wqkv holds the Q, K and V rows stacked ([nq + 2 nkv][d]).  On one GPU this
+ * runs as a single persistent kernel (one CTA per SM, grid-wide hand-offs,
+ * weight tiles loaded before the previous kernel ends); shapes it does not
+ * cover run as the separate ops.  dev_out may alias dev_x. */
+lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x, const float *dev_norm_w,
+                        float eps, const lt_tensor *wqkv, const float *dev_qkv_bias,
+                        const float *dev_q_norm, const float *dev_k_norm, const uint32_t *dev_pos,
+                        float *dev_k_cache, float *dev_v_cache, const lt_tensor *wo, float *dev_out);
+
+/* L2 prefetch hint: the next lt_attn_block, or single-token lt_moe_block /
+ * lt_moe_forward, launched on this context starts by prefetching these
+ * tensors into L2 (a later op's weights, fetched while this one waits on its
+ * own dependency chain).  Either may be NULL; the hint is used once. */
+lt_status lt_prefetch_next(lt_ctx *ctx, const lt_tensor *a, const lt_tensor *b);
+
 /* The dense FFN block of a decoder layer (forward.zig:307-312):
  * out = x + down . (act(gate . xn) * (up . xn)), xn = rmsnorm(x) * norm_w,
  * for 2-D gate/up [F][d] and down [d][F].  dev_out may alias dev_x. */

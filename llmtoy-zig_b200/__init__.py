@@ -35,7 +35,8 @@ EXPORTS = [
     "lt_graph_launch", "lt_graph_free", "lt_moe_ffn_noalloc", "lt_quant_matvec_host", "lt_moe_forward_host",
     "lt_ep_dispatch", "lt_gather_rows", "lt_moe_combine",
     "lt_device_alloc", "lt_device_free", "lt_copy_to_device", "lt_copy_to_host",
-    "lt_embed", "lt_qmatvec_add", "lt_attn_prep", "lt_attn_decode", "lt_ffn_block", "lt_greedy_step",
+    "lt_embed", "lt_qmatvec_add", "lt_attn_prep", "lt_attn_decode", "lt_attn_block", "lt_prefetch_next",
+    "lt_ffn_block", "lt_greedy_step",
 ]
 
 
@@ -117,6 +118,8 @@ def load_library() -> ctypes.CDLL:
         "lt_attn_decode": (I, [P, ctypes.POINTER(AttnCfg), P, P, P, P, P]),
         "lt_greedy_step": (I, [P, P, U32, P, P, P]),
         "lt_ffn_block": (I, [P, P, P, P, I, P, F, P, U32, P]),
+        "lt_attn_block": (I, [P, ctypes.POINTER(AttnCfg), P, P, F, P, P, P, P, P, P, P, P, P]),
+        "lt_prefetch_next": (I, [P, P, P]),
         "lt_quant_matvec_host": (I, [P, P, P, U32, P, U64, U64]),
         "lt_moe_forward_host": (I, [P, P, P, P, P, I, I, P, P, U32, U32, P, P, P]),
     }
@@ -339,6 +342,16 @@ class Context:
     def attn_decode(self, cfg: AttnCfg, q, k_cache, v_cache, pos, out) -> None:
         self._check(self.lib.lt_attn_decode(self.ptr, ctypes.byref(cfg), _ptr(q), _ptr(k_cache), _ptr(v_cache),
                                             _ptr(pos), _ptr(out)))
+
+    def attn_block(self, cfg: AttnCfg, x, norm_w, eps: float, wqkv: Tensor, qkv_bias, q_norm, k_norm, pos,
+                   k_cache, v_cache, wo: Tensor, out) -> None:
+        """out = x + wo . attention(...) for one token: the attention half of a decoder layer."""
+        self._check(self.lib.lt_attn_block(self.ptr, ctypes.byref(cfg), _ptr(x), _ptr(norm_w), eps, wqkv.handle,
+                                           _ptr(qkv_bias), _ptr(q_norm), _ptr(k_norm), _ptr(pos), _ptr(k_cache),
+                                           _ptr(v_cache), wo.handle, _ptr(out)))
+
+    def prefetch_next(self, a: Tensor | None, b: Tensor | None = None) -> None:
+        self._check(self.lib.lt_prefetch_next(self.ptr, a.handle if a else None, b.handle if b else None))
 
     def ffn_block(self, gate: Tensor, up: Tensor, down: Tensor, act: int, norm_w, eps: float, x, ntok: int,
                   out) -> None:

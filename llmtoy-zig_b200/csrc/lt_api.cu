@@ -32,6 +32,10 @@ struct lt_ctx {
     uint32_t tc_min_tokens = 64;     // batches of at least this many tokens use the tensor-core expert GEMM
     int *dev_err = nullptr;          // device error word written by kernels
     uint8_t *dec_sync = nullptr;     // counters and tagged logits of the persistent decode kernel
+    uint8_t *attn_sync = nullptr;    // epoch and barrier counters of the attention-block kernel
+    bool attn_block = true;          // single-token attention halves run as one persistent kernel
+    const uint8_t *pf[2] = {nullptr, nullptr};  // L2 prefetch hint for the next block kernel
+    uint64_t pf_bytes[2] = {0, 0};
     float *ones = nullptr;           // n_const slot weights of 1 (dense FFN blocks)
     uint32_t *zeros = nullptr;       // n_const expert ids of 0
     size_t n_const = 0;
@@ -132,6 +136,11 @@ lt_status ensure_counters(lt_ctx *ctx, size_t n) {
     LT_CUDA(ctx, cudaMemset(ctx->counters, 0, n * 4), "cudaMemset(counters)");
     ctx->n_counters = n;
     return LT_OK;
+}
+
+void clear_prefetch(lt_ctx *ctx) {
+    ctx->pf[0] = ctx->pf[1] = nullptr;
+    ctx->pf_bytes[0] = ctx->pf_bytes[1] = 0;
 }
 
 // Constant slot weights (1) and expert ids (0) for n tokens.
@@ -278,6 +287,8 @@ lt_status lt_init(int device, lt_ctx **out) {
     ctx->pdl = !(pdl && strcmp(pdl, "0") == 0);
     const char *dk = getenv("LLMTOY_DECODE_KERNEL");
     ctx->decode_kernel = !(dk && strcmp(dk, "0") == 0);
+    const char *ab = getenv("LLMTOY_ATTN_BLOCK");  // 0: attention halves as separate kernels
+    ctx->attn_block = !(ab && strcmp(ab, "0") == 0);
     const char *tc = getenv("LLMTOY_TC_MIN_TOKENS");  // 0 turns the tensor-core expert GEMM off
     if (tc) ctx->tc_min_tokens = (uint32_t)strtoul(tc, nullptr, 10);
     lt_status st = LT_OK;
@@ -285,7 +296,9 @@ lt_status lt_init(int device, lt_ctx **out) {
         cudaStreamCreateWithFlags(&ctx->own, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(&ctx->dev_err, 4) != cudaSuccess || cudaMemset(ctx->dev_err, 0, 4) != cudaSuccess ||
         cudaMalloc(&ctx->dec_sync, lt::kDecodeSyncBytes) != cudaSuccess ||
-        cudaMemset(ctx->dec_sync, 0, lt::kDecodeSyncBytes) != cudaSuccess) {
+        cudaMemset(ctx->dec_sync, 0, lt::kDecodeSyncBytes) != cudaSuccess ||
+        cudaMalloc(&ctx->attn_sync, lt::kAttnSyncBytes) != cudaSuccess ||
+        cudaMemset(ctx->attn_sync, 0, lt::kAttnSyncBytes) != cudaSuccess) {
         st = LT_ECUDA;
     }
     ctx->stream = ctx->own;
@@ -312,6 +325,7 @@ void lt_free(lt_ctx *ctx) {
     if (ctx->counters) cudaFree(ctx->counters);
     if (ctx->dev_err) cudaFree(ctx->dev_err);
     if (ctx->dec_sync) cudaFree(ctx->dec_sync);
+    if (ctx->attn_sync) cudaFree(ctx->attn_sync);
     if (ctx->ones) cudaFree(ctx->ones);
     if (ctx->zeros) cudaFree(ctx->zeros);
     if (ctx->pinned) cudaFreeHost(ctx->pinned);
@@ -716,6 +730,99 @@ lt_status lt_attn_decode(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_q
                     "attn decode");
 }
 
+lt_status lt_prefetch_next(lt_ctx *ctx, const lt_tensor *a, const lt_tensor *b) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    const lt_tensor *t[2] = {a, b};
+    for (int i = 0; i < 2; i++) {
+        ctx->pf[i] = t[i] ? t[i]->m.data : nullptr;
+        ctx->pf_bytes[i] = t[i] ? (t[i]->dev_bytes & ~(size_t)15) : 0;
+    }
+    return LT_OK;
+}
+
+lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x, const float *dev_norm_w, float eps,
+                        const lt_tensor *wqkv, const float *dev_qkv_bias, const float *dev_q_norm,
+                        const float *dev_k_norm, const uint32_t *dev_pos, float *dev_k_cache, float *dev_v_cache,
+                        const lt_tensor *wo, float *dev_out) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    struct Clear {
+        lt_ctx *c;
+        ~Clear() { clear_prefetch(c); }
+    } clear{ctx};
+    lt::AttnGeom g;
+    if ((st = attn_geom(ctx, cfg, g, "lt_attn_block")) != LT_OK) return st;
+    if (!dev_x || !dev_norm_w || !wqkv || !wo || !dev_pos || !dev_k_cache || !dev_v_cache || !dev_out)
+        return fail(ctx, LT_EINVAL, "lt_attn_block: null argument");
+    const uint32_t nq = g.n_heads * g.hd, nkv = g.n_kv * g.hd;
+    const uint64_t d = wo->m.rows;
+    if (wqkv->m.n_experts || wo->m.n_experts || wqkv->m.rows != (uint64_t)nq + 2 * nkv || wqkv->m.cols != d ||
+        wo->m.cols != nq)
+        return fail(ctx, LT_EINVAL, "lt_attn_block: wqkv %llux%llu / wo %llux%llu do not fit the heads",
+                    (unsigned long long)wqkv->m.rows, (unsigned long long)wqkv->m.cols,
+                    (unsigned long long)wo->m.rows, (unsigned long long)wo->m.cols);
+    if ((st = check_kernel_shape(ctx, wqkv->m, "lt_attn_block wqkv")) != LT_OK) return st;
+    if ((st = check_kernel_shape(ctx, wo->m, "lt_attn_block wo")) != LT_OK) return st;
+    const bool fused = ctx->attn_block && lt::attn_block_supported(g, wqkv->m, wo->m, (uint32_t)d) &&
+                       lt::attn_block_smem(g, ctx->num_sms, (uint32_t)d, wqkv->m, wo->m) <= lt::kDecodeSmemLimit;
+    if (fused) {
+        const size_t sf = lt::attn_block_scratch_floats(g, ctx->num_sms, (uint32_t)d, wqkv->m, wo->m);
+        if ((st = ensure_scratch(ctx, sf * 4 + 1024)) != LT_OK) return st;
+        if ((st = ensure_counters(ctx, g.n_heads)) != LT_OK) return st;
+        lt::AttnBlockParams p;
+        p.g = g;
+        p.d = (uint32_t)d;
+        p.x = dev_x;
+        p.norm_w = dev_norm_w;
+        p.eps = eps;
+        p.wqkv = wqkv->m;
+        p.wo = wo->m;
+        p.bias = dev_qkv_bias;
+        p.q_norm = dev_q_norm;
+        p.k_norm = dev_k_norm;
+        p.pos = dev_pos;
+        p.kc = dev_k_cache;
+        p.vc = dev_v_cache;
+        p.out = dev_out;
+        p.scratch = (float *)ctx->scratch;
+        p.head_ctr = ctx->counters;
+        p.sync = ctx->attn_sync;
+        for (int i = 0; i < 2; i++) {
+            p.pf[i] = ctx->pf[i];
+            p.pf_bytes[i] = ctx->pf_bytes[i];
+        }
+        return launched(ctx, lt::launch_attn_block(cfg_of(ctx), p), "attn block");
+    }
+    // the same computation as separate kernels: norm, Q/K/V, prep, attention, wo + residual
+    const size_t xb_b = al256((size_t)d * 4), qkv_b = al256(((size_t)nq + 2 * nkv) * 4), att_b = al256((size_t)nq * 4);
+    // [0, base): the quantised activation row of each matvec, then the attention partials
+    const size_t attn_sc = lt::attn_scratch_floats(g, ctx->num_sms) * 4;
+    const size_t qrow = lt::qact_row_pitch(d > nq ? d : nq);
+    const size_t base = al256(attn_sc > qrow ? attn_sc : qrow);
+    if ((st = ensure_scratch(ctx, base + xb_b + qkv_b + att_b)) != LT_OK) return st;
+    float *xb = (float *)(ctx->scratch + base), *qkv = (float *)(ctx->scratch + base + xb_b);
+    float *att = (float *)(ctx->scratch + base + xb_b + qkv_b);
+    const lt::LaunchCfg c = cfg_of(ctx);
+    if ((st = launched(ctx, lt::launch_rmsnorm(c, dev_x, dev_norm_w, eps, (uint32_t)d, 1, xb), "rmsnorm")) != LT_OK)
+        return st;
+    const uint64_t qp = lt::qact_row_pitch(d);
+    if ((st = launched(ctx, lt::launch_quantize(c, xb, (uint32_t)d, 1, ctx->scratch, qp), "quantize")) != LT_OK) return st;
+    if ((st = launched(ctx, lt::launch_qmatvec(c, wqkv->m, 0, ctx->scratch, qp, xb, qkv, 1, dev_qkv_bias), "qmatvec")) != LT_OK)
+        return st;
+    if ((st = ensure_counters(ctx, g.n_heads)) != LT_OK) return st;
+    if ((st = launched(ctx, lt::launch_attn_prep(c, g, qkv, dev_q_norm, dev_k_norm, dev_pos, dev_k_cache, dev_v_cache),
+                       "attn prep")) != LT_OK)
+        return st;
+    if ((st = launched(ctx, lt::launch_attn_decode(c, g, qkv, dev_k_cache, dev_v_cache, dev_pos, att,
+                                                   (float *)ctx->scratch, ctx->counters),
+                       "attn decode")) != LT_OK)
+        return st;
+    const uint64_t qo = lt::qact_row_pitch(nq);
+    if ((st = launched(ctx, lt::launch_quantize(c, att, nq, 1, ctx->scratch, qo), "quantize")) != LT_OK) return st;
+    return launched(ctx, lt::launch_qmatvec(c, wo->m, 0, ctx->scratch, qo, att, dev_out, 1, dev_x), "qmatvec");
+}
+
 lt_status lt_greedy_step(lt_ctx *ctx, const float *dev_logits, uint32_t n, uint32_t *dev_tokens, uint32_t *dev_pos,
                          const uint32_t *dev_n_prompt) {
     lt_status st = enter(ctx);
@@ -863,6 +970,10 @@ static lt_status forward_impl(lt_ctx *ctx, const lt_tensor *router, const lt_ten
                               const lt_tensor *down, int act, int norm_topk, const float *dev_expert_scale,
                               const float *dev_norm_w, float eps, int residual, const float *dev_x, uint32_t ntok,
                               uint32_t k, float *dev_out, uint32_t *dev_ids, float *dev_w) {
+    struct Clear {
+        lt_ctx *c;
+        ~Clear() { clear_prefetch(c); }
+    } clear{ctx};  // the hint applies to this call only
     lt_status st;
     uint64_t F = 0;
     if ((st = check_router(ctx, router, k)) != LT_OK) return st;
@@ -905,6 +1016,10 @@ static lt_status forward_impl(lt_ctx *ctx, const lt_tensor *router, const lt_ten
         p.residual = residual;
         p.out = dev_out;
         p.sync = ctx->dec_sync;
+        for (int i = 0; i < 2; i++) {
+            p.pf[i] = ctx->pf[i];
+            p.pf_bytes[i] = ctx->pf_bytes[i];
+        }
         if (lt::moe_decode_fits(p, ctx->num_sms)) return launched(ctx, lt::launch_moe_decode(cfg_of(ctx), p), "moe decode");
     }
     float *xn = s.gemm && dev_norm_w ? s.xn : nullptr;  // the tensor-core path reads f32 rows

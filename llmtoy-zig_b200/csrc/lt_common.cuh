@@ -205,6 +205,18 @@ LT_DEVINL void grid_wait(const unsigned long long *ctr, uint64_t target, int *de
     __syncthreads();
 }
 
+// Fire-and-forget prefetch of [p, p + bytes) into L2 (16-byte aligned, bytes a multiple of 16).
+LT_DEVINL void prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// CTA c of G prefetches its 16-byte aligned share of [p, p + bytes) into L2.
+LT_DEVINL void prefetch_l2_share(const uint8_t *p, uint64_t bytes, uint32_t c, uint32_t G) {
+    const uint64_t n = bytes / 16;
+    const uint64_t b0 = 16 * (c * n / G), b1 = 16 * ((c + 1) * n / G);
+    for (uint64_t b = b0; b < b1; b += 65536) prefetch_l2(p + b, (uint32_t)(b1 - b < 65536 ? b1 - b : 65536));
+}
+
 LT_DEVINL uint4 lds128(const void *p) {
     return *reinterpret_cast<const uint4 *>(p);
 }

@@ -103,6 +103,31 @@ cudaError_t launch_attn_prep(const LaunchCfg &c, const AttnGeom &g, float *qkv, 
 cudaError_t launch_attn_decode(const LaunchCfg &c, const AttnGeom &g, const float *q, const float *kc,
                                const float *vc, const uint32_t *pos, float *out, float *part, uint32_t *counters);
 
+// The attention half of a decoder layer for one token in one persistent
+// kernel (lt_attn_block.cu): out = x + wo . attention(rope(norm(W_qkv .
+// rmsnorm(x) + bias))), KV append included.  Grid = num_sms, all resident.
+struct AttnBlockParams {
+    AttnGeom g;
+    uint32_t d;
+    const float *x, *norm_w;
+    float eps;
+    DevMat wqkv, wo;
+    const float *bias, *q_norm, *k_norm;
+    const uint32_t *pos;
+    float *kc, *vc;
+    float *out;            // may alias x
+    float *scratch;        // attn_block_scratch_floats floats
+    uint32_t *head_ctr;    // [n_heads] zero-initialised counters (left zero)
+    uint8_t *sync;         // kAttnSyncBytes zero-initialised, this kernel only
+    const uint8_t *pf[2];  // optional L2 prefetch ranges (the next kernel's weights)
+    uint64_t pf_bytes[2];
+};
+constexpr size_t kAttnSyncBytes = 256;
+bool attn_block_supported(const AttnGeom &g, const DevMat &wqkv, const DevMat &wo, uint32_t d);
+size_t attn_block_smem(const AttnGeom &g, int num_sms, uint32_t d, const DevMat &wqkv, const DevMat &wo);
+size_t attn_block_scratch_floats(const AttnGeom &g, int num_sms, uint32_t d, const DevMat &wqkv, const DevMat &wo);
+cudaError_t launch_attn_block(const LaunchCfg &c, const AttnBlockParams &p);
+
 // Bytes of one quantised activation row (lt_qact.cuh) of `cols` values.
 size_t qact_row_pitch(uint64_t cols);
 // nrows f32 rows of `cols` -> quantised activation rows at q (pitch qpitch).
@@ -167,6 +192,9 @@ struct DecodeParams {
     // kDecodeSyncBytes, zero-initialised, used by no other kernel and only
     // with grid = num_sms: epoch and barrier counters, tagged logits
     uint8_t *sync;
+    // optional L2 prefetch ranges issued at kernel start (the next kernel's weights)
+    const uint8_t *pf[2] = {nullptr, nullptr};
+    uint64_t pf_bytes[2] = {0, 0};
 };
 constexpr size_t kDecodeSyncBytes = 4096;
 

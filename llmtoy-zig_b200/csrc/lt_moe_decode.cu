@@ -73,6 +73,8 @@ struct DecodeArgs {
     uint8_t *sync;
     int *dev_err;
     uint32_t maxpairs, maxrows;  // per-CTA maxima the layout is sized for
+    const uint8_t *pf[2];        // optional L2 prefetch ranges (the next kernel's weights)
+    uint64_t pf_bytes[2];
 };
 
 struct DecodeLayout {
@@ -164,6 +166,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     router_prefetch(a.rw + (size_t)(has_e ? e_mine : 0) * a.rw_ld, a.d, lane, has_e, w0);
     if (a.norm_w)
         for (uint32_t i = tid; i < a.d; i += kDecThreads) nwsm[i] = __ldg(a.norm_w + i);
+    if (tid < 2 && a.pf[tid]) prefetch_l2_share(a.pf[tid], a.pf_bytes[tid], c, G);
     pdl_launch_dependents();
     pdl_wait();
 
@@ -430,6 +433,10 @@ bool decode_plan(const DecodeParams &p, int num_sms, DecodePlan &out) {
     a.out = p.out;
     a.sync = p.sync;
     a.dev_err = nullptr;
+    for (int i = 0; i < 2; i++) {
+        a.pf[i] = p.pf[i];
+        a.pf_bytes[i] = p.pf_bytes[i];
+    }
     if (p.d % 32 != 0 || p.F % 32 != 0) return false;
     const uint64_t nunits = (uint64_t)p.k * p.F / kDecUnit;
     a.maxpairs = (uint32_t)(kDecUnit * ((nunits + G - 1) / G));

@@ -45,9 +45,34 @@ lt_status alloc(lth_decoder *d, T **p, size_t count) {
         if (st_ != LT_OK) return st_;        \
     } while (0)
 
+lt_status attn_ops(lth_decoder *d, const lth_layer &L, float *kc, float *vc);
+
 lt_status layer_step(lth_decoder *d, uint32_t l) {
     const lth_model &m = d->m;
     const lth_layer &L = d->layers[l];
+    lt_ctx *c = d->ctx;
+    const uint32_t *pos = d->state;
+    const size_t cache = (size_t)m.kv_cap * d->nkv;
+    float *kc = d->kcache + (size_t)l * cache, *vc = d->vcache + (size_t)l * cache;
+    const lth_layer *next = l + 1 < m.n_layers ? &d->layers[l + 1] : nullptr;
+    if (L.wqkv) {  // the whole attention half in one launch; warm this layer's router in L2 meanwhile
+        LTH_TRY(lt_prefetch_next(c, L.router, nullptr));
+        LTH_TRY(lt_attn_block(c, &d->attn, d->x, L.attn_norm, m.eps, L.wqkv, L.qkv_bias, L.q_norm, L.k_norm, pos,
+                              kc, vc, L.wo, d->x));
+    } else {
+        LTH_TRY(attn_ops(d, L, kc, vc));
+    }
+    if (L.router) {  // the MoE block warms the next layer's attention weights in L2
+        if (next && next->wqkv) LTH_TRY(lt_prefetch_next(c, next->wqkv, next->wo));
+        return lt_moe_block(c, L.router, L.exp_gate, L.exp_up, L.exp_down, (int)m.act, (int)m.norm_topk, nullptr,
+                            L.ffn_norm, m.eps, d->x, 1, m.n_used, d->x, nullptr, nullptr);
+    }
+    return lt_ffn_block(c, L.ffn_gate, L.ffn_up, L.ffn_down, (int)m.act, L.ffn_norm, m.eps, d->x, 1, d->x);
+}
+
+// The attention half as separate ops (separate Q/K/V tensors).
+lt_status attn_ops(lth_decoder *d, const lth_layer &L, float *kc, float *vc) {
+    const lth_model &m = d->m;
     lt_ctx *c = d->ctx;
     const uint32_t *pos = d->state;
     LTH_TRY(lt_rmsnorm(c, d->x, L.attn_norm, m.eps, m.d_model, 1, d->xb));
@@ -66,15 +91,9 @@ lt_status layer_step(lth_decoder *d, uint32_t l) {
                 LTH_TRY(lt_qmatvec(c, w[i], 0, d->xb, d->qkv + off[i], 1));
         }
     }
-    const size_t cache = (size_t)m.kv_cap * d->nkv;
-    float *kc = d->kcache + (size_t)l * cache, *vc = d->vcache + (size_t)l * cache;
     LTH_TRY(lt_attn_prep(c, &d->attn, d->qkv, L.q_norm, L.k_norm, pos, kc, vc));
     LTH_TRY(lt_attn_decode(c, &d->attn, d->qkv, kc, vc, pos, d->att));
-    LTH_TRY(lt_qmatvec_add(c, L.wo, 0, d->att, d->x, d->x, 1));
-    if (L.router)
-        return lt_moe_block(c, L.router, L.exp_gate, L.exp_up, L.exp_down, (int)m.act, (int)m.norm_topk, nullptr,
-                            L.ffn_norm, m.eps, d->x, 1, m.n_used, d->x, nullptr, nullptr);
-    return lt_ffn_block(c, L.ffn_gate, L.ffn_up, L.ffn_down, (int)m.act, L.ffn_norm, m.eps, d->x, 1, d->x);
+    return lt_qmatvec_add(c, L.wo, 0, d->att, d->x, d->x, 1);
 }
 
 lt_status step(lth_decoder *d) {

@@ -197,3 +197,57 @@ def test_decoder_config2_shape_vs_oracle(ctx, oracle, pool):
     synth, _ = _mods()
     m = synth.config2_model(np.random.default_rng(24), n_layers=2)
     _compare_generation(ctx, oracle, pool, m, [100, 2000, 30000, 151935], 6, graph_check=False)
+
+
+@pytest.mark.parametrize("name,d,nh,nkv,hd,wt,neox,qk,bias,window", [
+    ("config2", 2048, 32, 4, 128, 8, True, True, False, 0),
+    ("config0", 896, 14, 2, 64, 8, False, False, True, 0),
+    ("gemma-swa", 1024, 8, 4, 256, 12, True, True, False, 16),
+    ("q6k", 512, 4, 4, 128, 14, False, True, True, 0),
+])
+def test_attn_block_matches_separate_ops(pkg, oracle, name, d, nh, nkv, hd, wt, neox, qk, bias, window):
+    """The persistent attention-block kernel against the same computation as
+    separate ops (rmsnorm, Q/K/V matvec, prep, attention, wo + residual),
+    step by step over 24 positions with shared caches."""
+    import os
+    import torch
+    synth, _ = _mods()
+    rng = np.random.default_rng(d + nh)
+    nq, nk = nh * hd, nkv * hd
+    wqkv = np.concatenate([synth.matrix(rng, wt, nq, d), synth.matrix(rng, wt, 2 * nk, d)])
+    wo = synth.matrix(rng, wt, d, nq)
+    nw = rng.uniform(0.5, 1.5, d).astype(np.float32)
+    qn = rng.uniform(0.5, 1.5, hd).astype(np.float32) if qk else None
+    kn = rng.uniform(0.5, 1.5, hd).astype(np.float32) if qk else None
+    bs = rng.normal(0, 0.1, nq + 2 * nk).astype(np.float32) if bias else None
+    cap = window if window else 64
+    cfg = pkg.AttnCfg(nh, nkv, hd, int(neox), 1e6, 1e-6, 1.0 / np.sqrt(hd), cap, window)
+    ctxs = []
+    old = os.environ.get("LLMTOY_ATTN_BLOCK")
+    for flag in ("1", "0"):
+        os.environ["LLMTOY_ATTN_BLOCK"] = flag
+        c = pkg.Context(0)
+        c.set_stream(None)
+        ctxs.append(c)
+    if old is None:
+        del os.environ["LLMTOY_ATTN_BLOCK"]
+    else:
+        os.environ["LLMTOY_ATTN_BLOCK"] = old
+    res = []
+    for c in ctxs:
+        tq, to = c.upload(wqkv, wt, nq + 2 * nk, d), c.upload(wo, wt, d, nq)
+        kc, vc = empty(cap * nk), empty(cap * nk)
+        xs = []
+        rng2 = np.random.default_rng(77)
+        for pos in range(24):
+            x = dev(rng2.normal(0, 1, d).astype(np.float32))
+            out = empty(d)
+            c.attn_block(cfg, x, dev(nw), 1e-6, tq, None if bs is None else dev(bs), None if qn is None else dev(qn),
+                         None if kn is None else dev(kn), dev(np.array([pos], np.int32)), kc, vc, to, out)
+            c.sync()
+            xs.append(host(out) - host(x))
+        res.append(np.stack(xs))
+        tq.free()
+        to.free()
+        c.close()
+    assert rel_l2(res[0], res[1]) < 2e-5, rel_l2(res[0], res[1])
