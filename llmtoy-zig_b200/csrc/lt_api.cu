@@ -769,7 +769,6 @@ lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x,
     if (fused) {
         const size_t sf = lt::attn_block_scratch_floats(g, ctx->num_sms, (uint32_t)d, wqkv->m, wo->m);
         if ((st = ensure_scratch(ctx, sf * 4 + 1024)) != LT_OK) return st;
-        if ((st = ensure_counters(ctx, g.n_heads)) != LT_OK) return st;
         lt::AttnBlockParams p;
         p.g = g;
         p.d = (uint32_t)d;
@@ -786,7 +785,6 @@ lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x,
         p.vc = dev_v_cache;
         p.out = dev_out;
         p.scratch = (float *)ctx->scratch;
-        p.head_ctr = ctx->counters;
         p.sync = ctx->attn_sync;
         for (int i = 0; i < 2; i++) {
             p.pf[i] = ctx->pf[i];

@@ -11,9 +11,10 @@
 //            this position (by split 0 of the group's first head), and
 //            online-softmax attention over the split's positions; the
 //            current position's K/V come from registers, older ones from the
-//            cache.  The last split of a head to finish merges the head.
+//            cache; each split publishes (max, sum, weighted values).
 //                                                      -> grid barrier
-//   phase O  every CTA quantises the attention vector and computes its wo
+//   phase O  every CTA merges the splits of every head itself (no third
+//            hand-off), quantises the attention vector and computes its wo
 //            rows plus the residual: out = x + wo . att (forward.zig:304-305).
 //
 // The weights are static, so both tiles (this CTA's Q/K/V rows and wo rows)
@@ -29,6 +30,7 @@ constexpr int kAbThreads = kAbWarps * 32;
 
 // Layout of the context's attention sync block.
 constexpr size_t kAbEpoch = 0, kAbB1 = 8, kAbB2 = 16;
+constexpr uint32_t kAbMaxSplits = 8;  // splits of a head's positions (one CTA each)
 
 struct AttnBlockArgs {
     AttnGeom g;
@@ -47,7 +49,6 @@ struct AttnBlockArgs {
     uint32_t onb;  // 32-blocks per wo row (nq / 32)
     float *out;
     float *qkv, *part, *att;  // global scratch
-    uint32_t *head_ctr;       // [n_heads], zero between launches
     uint8_t *sync;
     const uint8_t *pf[2];
     uint64_t pf_bytes[2];
@@ -103,54 +104,100 @@ LT_DEVINL void ab_quantise(const XS &X, const float *xf, uint32_t n, int warp, i
     }
 }
 
-// rows [0, nrows) of a shared tile (pitch) against X: y[r] per row, lanes own
-// 64-column chunks (cb = lane, lane + 32, ...), warp w takes rows w, w+16, ...
+// n f32 values from global (written by other CTAs of this launch) into
+// shared memory, float4 at a time with every load issued before any store.
+LT_DEVINL void ab_load(float *dst, const float *src, uint32_t n) {
+    const uint32_t n4 = n / 4;
+    for (uint32_t i0 = threadIdx.x; i0 < n4; i0 += 4 * kAbThreads) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const uint32_t i = i0 + u * kAbThreads;
+            if (i < n4) v[u] = __ldcg(reinterpret_cast<const float4 *>(src) + i);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const uint32_t i = i0 + u * kAbThreads;
+            if (i < n4) reinterpret_cast<float4 *>(dst)[i] = v[u];
+        }
+    }
+    for (uint32_t i = 4 * n4 + threadIdx.x; i < n; i += kAbThreads) dst[i] = __ldcg(src + i);
+}
+
+// rows [0, nrows) of a shared tile (pitch) against X: y[r] per row.  Lanes
+// own 64-column chunks (cb = lane, lane + 32, ...), loaded once per chunk;
+// warp w takes rows w, w+16, ... (up to 4 at a time).
 template <uint32_t T>
 LT_DEVINL void ab_rows(const uint8_t *tile, uint64_t pitch, uint32_t nrows, uint32_t cols, uint32_t nb, const XS &X,
                        int warp, int lane, float *y) {
+    constexpr int R = 4;
     const uint32_t nch = (cols + 63) / 64;
-    for (uint32_t r = warp; r < nrows; r += kAbWarps) {
-        float acc = 0.0f;
+    for (uint32_t r0 = warp; r0 < nrows; r0 += kAbWarps * R) {
+        float acc[R];
+#pragma unroll
+        for (int i = 0; i < R; i++) acc[i] = 0.0f;
         for (uint32_t cb = lane; cb < nch; cb += 32) {
             XChunk xc;
             xchunk_load(X, 0, (int)cb, xc);
-            acc += dot64<T>(tile + (size_t)r * pitch, (int)cb, (int)nb, xc);
+#pragma unroll
+            for (int i = 0; i < R; i++) {
+                const uint32_t r = r0 + i * kAbWarps;
+                if (r < nrows) acc[i] += dot64<T>(tile + (size_t)r * pitch, (int)cb, (int)nb, xc);
+            }
         }
-        acc = warp_sum(acc);
-        if (lane == 0) y[r] = acc;
+#pragma unroll
+        for (int i = 0; i < R; i++) {
+            const uint32_t r = r0 + i * kAbWarps;
+            const float v = warp_sum(acc[i]);
+            if (lane == 0 && r < nrows) y[r] = v;
+        }
     }
 }
 
-// Per-head RMSNorm (optional weights) and RoPE of hd values in shared memory.
-LT_DEVINL void ab_norm_rope(float *v, const float *nw, const AttnGeom &g, uint32_t pos, float *red) {
-    const uint32_t hd = g.hd, half = hd / 2;
-    if (nw) {
-        float ss = 0.0f;
-        for (uint32_t i = threadIdx.x; i < hd; i += kAbThreads) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
-        ss = ab_block_sum(ss, red);
-        const float rms_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), g.eps)));
-        __syncthreads();
-        for (uint32_t i = threadIdx.x; i < hd; i += kAbThreads) v[i] = __fmul_rn(__fmul_rn(v[i], rms_inv), nw[i]);
+// Per-head RMSNorm (optional weights) and RoPE of the query head hq and the
+// key head hk (hd values each, shared memory), both at once: threads
+// [0, hd) work on q, [hd, 2 hd) on k.
+LT_DEVINL void ab_norm_rope2(float *hq, const float *qn, float *hk, const float *kn, const AttnGeom &g, uint32_t pos,
+                             float *red) {
+    const uint32_t hd = g.hd, half = hd / 2, tid = threadIdx.x;
+    const int warp = (int)(tid >> 5), lane = (int)(tid & 31);
+    const bool isq = tid < hd, isk = tid >= hd && tid < 2 * hd;
+    float *v = isq ? hq : hk;
+    const float *nw = isq ? qn : kn;
+    const uint32_t e = isq ? tid : tid - hd;
+    float ss = 0.0f;
+    if ((isq || isk) && nw) ss = __fmul_rn(v[e], v[e]);
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if ((isq || isk) && nw) {
+        const uint32_t w0 = isq ? 0 : hd / 32;
+        float t = 0.0f;
+        for (uint32_t w = 0; w < hd / 32; w++) t = __fadd_rn(t, red[w0 + w]);
+        const float rms_inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)hd), g.eps)));
+        v[e] = __fmul_rn(__fmul_rn(v[e], rms_inv), nw[e]);
     }
     __syncthreads();
+    // rope: threads [0, half) rotate q's pairs, [half, hd) k's
     float r0 = 0.0f, r1 = 0.0f;
     uint32_t i0 = 0, i1 = 0;
-    const bool act = threadIdx.x < half;
+    float *rv = tid < half ? hq : hk;
+    const bool act = tid < hd;
     if (act) {
-        const uint32_t i = threadIdx.x;
+        const uint32_t i = tid < half ? tid : tid - half;
         const float ang = __fmul_rn((float)pos, __fdiv_rn(1.0f, powf(g.theta, __fdiv_rn((float)(2 * i), (float)hd))));
-        float s, c;
-        sincosf(ang, &s, &c);
+        float sn, cs;
+        sincosf(ang, &sn, &cs);
         i0 = g.rope_neox ? i : 2 * i;
         i1 = g.rope_neox ? i + half : 2 * i + 1;
-        const float x0 = v[i0], x1 = v[i1];
-        r0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-        r1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+        const float x0 = rv[i0], x1 = rv[i1];
+        r0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+        r1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
     }
     __syncthreads();
     if (act) {
-        v[i0] = r0;
-        v[i1] = r1;
+        rv[i0] = r0;
+        rv[i1] = r1;
     }
     __syncthreads();
 }
@@ -159,13 +206,13 @@ template <uint32_t QT, uint32_t OT, int HD>
 __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int PER = HD / 32;
+    constexpr int NB = HD <= 128 ? 4 : 2;  // positions a warp loads before using them
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t G = gridDim.x, c = blockIdx.x;
     const AbLayout L = ab_layout(a);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
     float *red = reinterpret_cast<float *>(smem + L.misc);            // [16]
     uint64_t *s_epoch = reinterpret_cast<uint64_t *>(smem + L.misc + 64);
-    int *s_flag = reinterpret_cast<int *>(smem + L.misc + 72);
     uint8_t *wq = smem + L.wq, *wo = smem + L.wo;
     const XS Xx = xs_carve(smem + L.xs, 1, (int)((a.d + 255) / 256));
     const uint32_t nq = a.g.n_heads * HD, nkv = a.g.n_kv * HD;
@@ -205,7 +252,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     // ── phase Q ──────────────────────────────────────────────────────────────
     if (tid == 0) *s_epoch = grid_epoch(ctr_epoch, G);
     const uint32_t pos = *a.pos;
-    for (uint32_t i = tid; i < a.d; i += kAbThreads) xf[i] = __ldcg(a.x + i);
+    ab_load(xf, a.x, a.d);
     __syncthreads();
     for (uint32_t r = tid; r < nor; r += kAbThreads) xres[r] = xf[o0 + r];
     {
@@ -232,14 +279,13 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     const uint32_t seq = pos + 1, win = a.g.window ? min(seq, a.g.window) : seq, first = seq - win;
     for (uint32_t item = c; item < a.g.n_heads * S; item += G) {
         const uint32_t h = item / S, s = item - h * S, kh = h / group;
-        for (uint32_t i = tid; i < HD; i += kAbThreads) {
-            hq[i] = __ldcg(a.qkv + h * HD + i);
-            hk[i] = __ldcg(a.qkv + nq + kh * HD + i);
-            hv[i] = __ldcg(a.qkv + nq + nkv + kh * HD + i);
+        if (tid < 3 * HD / 4) {  // q, k, v heads: one float4 each
+            const uint32_t part = tid / (HD / 4), i = tid % (HD / 4);
+            const size_t off = part == 0 ? (size_t)h * HD : part == 1 ? nq + (size_t)kh * HD : nq + nkv + (size_t)kh * HD;
+            reinterpret_cast<float4 *>(hq + part * HD)[i] = __ldcg(reinterpret_cast<const float4 *>(a.qkv + off) + i);
         }
         __syncthreads();
-        ab_norm_rope(hq, a.q_norm, a.g, pos, red);
-        ab_norm_rope(hk, a.k_norm, a.g, pos, red);
+        ab_norm_rope2(hq, a.q_norm, hk, a.k_norm, a.g, pos, red);
         if (s == 0 && h % group == 0) {  // this position's K/V into the cache
             const size_t slot = (size_t)(pos % a.g.cap) * nkv + (size_t)kh * HD;
             for (uint32_t i = tid; i < HD; i += kAbThreads) {
@@ -254,33 +300,50 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
             o[i] = 0.0f;
         }
         float m = -INFINITY, l = 0.0f;
-        for (uint32_t j = s * kAbWarps + warp; j < win; j += S * kAbWarps) {
-            float kv[PER], vv[PER];
-            if (j == win - 1) {  // the current position
+        const uint32_t stride = S * kAbWarps;
+        for (uint32_t j0 = s * kAbWarps + warp; j0 < win; j0 += NB * stride) {
+            float kv[NB][PER], vv[NB][PER];
 #pragma unroll
-                for (int i = 0; i < PER; i++) {
-                    kv[i] = hk[lane + 32 * i];
-                    vv[i] = hv[lane + 32 * i];
-                }
-            } else {
-                const size_t slot = (size_t)((first + j) % a.g.cap) * nkv + (size_t)kh * HD;
+            for (int b = 0; b < NB; b++) {
+                const uint32_t j = j0 + b * stride;
+                if (j + 1 < win) {
+                    const size_t slot = (size_t)((first + j) % a.g.cap) * nkv + (size_t)kh * HD;
 #pragma unroll
-                for (int i = 0; i < PER; i++) {
-                    kv[i] = a.kc[slot + lane + 32 * i];
-                    vv[i] = a.vc[slot + lane + 32 * i];
+                    for (int i = 0; i < PER; i++) {
+                        kv[b][i] = a.kc[slot + lane + 32 * i];
+                        vv[b][i] = a.vc[slot + lane + 32 * i];
+                    }
+                } else {  // the current position (or past the window: unused)
+#pragma unroll
+                    for (int i = 0; i < PER; i++) {
+                        kv[b][i] = hk[lane + 32 * i];
+                        vv[b][i] = hv[lane + 32 * i];
+                    }
                 }
             }
-            float dot = 0.0f;
+            float dot[NB];
 #pragma unroll
-            for (int i = 0; i < PER; i++) dot = fmaf(qv[i], kv[i], dot);
-            dot = warp_sum(dot);
-            const float sc = dot * a.g.scale;
-            const float mn = fmaxf(m, sc);
-            const float al = expf(m - mn), p = expf(sc - mn);
-            l = l * al + p;
+            for (int b = 0; b < NB; b++) {
+                dot[b] = 0.0f;
 #pragma unroll
-            for (int i = 0; i < PER; i++) o[i] = fmaf(p, vv[i], o[i] * al);
-            m = mn;
+                for (int i = 0; i < PER; i++) dot[b] = fmaf(qv[i], kv[b][i], dot[b]);
+            }
+#pragma unroll
+            for (int o2 = 16; o2 > 0; o2 >>= 1)
+#pragma unroll
+                for (int b = 0; b < NB; b++) dot[b] += __shfl_xor_sync(0xffffffffu, dot[b], o2);
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                if (j0 + b * stride < win) {
+                    const float sc = dot[b] * a.g.scale;
+                    const float mn = fmaxf(m, sc);
+                    const float al = expf(m - mn), p = expf(sc - mn);
+                    l = l * al + p;
+#pragma unroll
+                    for (int i = 0; i < PER; i++) o[i] = fmaf(p, vv[b][i], o[i] * al);
+                    m = mn;
+                }
+            }
         }
         float *wp = wpart + warp * (HD + 2);
         if (lane == 0) {
@@ -293,7 +356,9 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
         float M = -INFINITY;
 #pragma unroll
         for (int w = 0; w < kAbWarps; w++) M = fmaxf(M, wpart[w * (HD + 2)]);
-        float *pp = a.part + ((size_t)h * S + s) * (HD + 2);
+        // split partials: o [h][s][HD] (16-byte aligned rows), (max, sum) [h][s]
+        float *po = a.part + ((size_t)h * S + s) * HD;
+        float *pml = a.part + (size_t)a.g.n_heads * S * HD + 2 * ((size_t)h * S + s);
         for (uint32_t t = tid; t < HD; t += kAbThreads) {
             float acc = 0.0f;
 #pragma unroll
@@ -301,7 +366,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
                 const float mw = wpart[w * (HD + 2)];
                 if (mw != -INFINITY) acc += wpart[w * (HD + 2) + 2 + t] * expf(mw - M);
             }
-            pp[2 + t] = acc;
+            po[t] = acc;
         }
         if (tid == 0) {
             float Lsum = 0.0f;
@@ -309,32 +374,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
                 const float mw = wpart[w * (HD + 2)];
                 if (mw != -INFINITY) Lsum += wpart[w * (HD + 2) + 1] * expf(mw - M);
             }
-            pp[0] = M;
-            pp[1] = Lsum;
-        }
-        __threadfence();
-        __syncthreads();
-        if (tid == 0) *s_flag = atomicAdd(&a.head_ctr[h], 1u) == S - 1;
-        __syncthreads();
-        if (*s_flag) {  // the last split of head h merges it
-            __threadfence();
-            const float *hp = a.part + (size_t)h * S * (HD + 2);
-            float GM = -INFINITY;
-            for (uint32_t k = 0; k < S; k++) GM = fmaxf(GM, __ldcg(hp + k * (HD + 2)));
-            float GL = 0.0f;
-            for (uint32_t k = 0; k < S; k++) {
-                const float mk = __ldcg(hp + k * (HD + 2));
-                if (mk != -INFINITY) GL += __ldcg(hp + k * (HD + 2) + 1) * expf(mk - GM);
-            }
-            for (uint32_t t = tid; t < HD; t += kAbThreads) {
-                float acc = 0.0f;
-                for (uint32_t k = 0; k < S; k++) {
-                    const float mk = __ldcg(hp + k * (HD + 2));
-                    if (mk != -INFINITY) acc += __ldcg(hp + k * (HD + 2) + 2 + t) * expf(mk - GM);
-                }
-                a.att[h * HD + t] = acc / GL;
-            }
-            if (tid == 0) a.head_ctr[h] = 0;
+            *reinterpret_cast<float2 *>(pml) = make_float2(M, Lsum);
         }
         __syncthreads();
     }
@@ -342,7 +382,44 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     grid_wait(ctr2, epoch, a.dev_err, kWaitLimitNs);
 
     // ── phase O ──────────────────────────────────────────────────────────────
-    for (uint32_t i = tid; i < nq; i += kAbThreads) xf[i] = __ldcg(a.att + i);
+    // every CTA merges the heads' splits itself: 4 output values per thread
+    for (uint32_t g4 = tid; g4 < nq / 4; g4 += kAbThreads) {
+        const uint32_t h = 4 * g4 / HD, t = 4 * g4 - h * HD;
+        const float *ho = a.part + (size_t)h * S * HD + t;
+        const float *hml = a.part + (size_t)a.g.n_heads * S * HD + 2 * (size_t)h * S;
+        float ms[kAbMaxSplits], ls[kAbMaxSplits];
+        float4 os[kAbMaxSplits];
+#pragma unroll
+        for (int k = 0; k < (int)kAbMaxSplits; k++) {
+            if ((uint32_t)k < S) {
+                const float2 ml = __ldcg(reinterpret_cast<const float2 *>(hml) + k);
+                ms[k] = ml.x;
+                ls[k] = ml.y;
+                os[k] = __ldcg(reinterpret_cast<const float4 *>(ho + (size_t)k * HD));
+            }
+        }
+        float GM = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < (int)kAbMaxSplits; k++)
+            if ((uint32_t)k < S) GM = fmaxf(GM, ms[k]);
+        float GL = 0.0f;
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int k = 0; k < (int)kAbMaxSplits; k++) {
+            if ((uint32_t)k < S && ms[k] != -INFINITY) {
+                const float f = expf(ms[k] - GM);
+                GL += ls[k] * f;
+                acc.x += os[k].x * f;
+                acc.y += os[k].y * f;
+                acc.z += os[k].z * f;
+                acc.w += os[k].w * f;
+            }
+        }
+        xf[4 * g4] = acc.x / GL;
+        xf[4 * g4 + 1] = acc.y / GL;
+        xf[4 * g4 + 2] = acc.z / GL;
+        xf[4 * g4 + 3] = acc.w / GL;
+    }
     __syncthreads();
     ab_quantise(Xa, xf, nq, warp, lane);
     __syncthreads();
@@ -371,7 +448,7 @@ static AttnBlockArgs ab_args(const AttnGeom &g, int num_sms, uint32_t d, const D
     a.opitch = wo.pitch;
     a.onb = (uint32_t)(wo.cols / 32);
     const uint32_t G = (uint32_t)num_sms;
-    a.splits = max(1u, G / g.n_heads);
+    a.splits = max(1u, min(kAbMaxSplits, G / g.n_heads));
     a.maxq = (a.qrows + G - 1) / G;
     a.maxo = (d + G - 1) / G;
     return a;
@@ -423,8 +500,7 @@ cudaError_t launch_attn_block(const LaunchCfg &c, const AttnBlockParams &p) {
     float *sc = p.scratch;
     a.qkv = sc;
     a.part = sc + ((a.qrows + 31) & ~31u);
-    a.att = a.part + (((size_t)p.g.n_heads * a.splits * (p.g.hd + 2) + 31) & ~(size_t)31);
-    a.head_ctr = p.head_ctr;
+    a.att = a.part + (((size_t)p.g.n_heads * a.splits * (p.g.hd + 2) + 31) & ~(size_t)31);  // o then (max, sum)
     a.sync = p.sync;
     for (int i = 0; i < 2; i++) {
         a.pf[i] = p.pf[i];

@@ -117,7 +117,6 @@ struct AttnBlockParams {
     float *kc, *vc;
     float *out;            // may alias x
     float *scratch;        // attn_block_scratch_floats floats
-    uint32_t *head_ctr;    // [n_heads] zero-initialised counters (left zero)
     uint8_t *sync;         // kAttnSyncBytes zero-initialised, this kernel only
     const uint8_t *pf[2];  // optional L2 prefetch ranges (the next kernel's weights)
     uint64_t pf_bytes[2];
