@@ -55,6 +55,16 @@ def load_host_library() -> ctypes.CDLL:
         "lth_decoder_logits": (P, [P]),
         "lth_decoder_tokens": (I, [P, P, U32]),
         "lth_generate": (I, [P, P, U32, U32, P]),
+        "lth_gguf_open": (I, [ctypes.c_char_p, ctypes.POINTER(P)]),
+        "lth_gguf_close": (None, [P]),
+        "lth_gguf_info": (ctypes.c_size_t, [P, P, ctypes.c_size_t]),
+        "lth_gguf_tensor_count": (ctypes.c_uint64, [P]),
+        "lth_gguf_tensor": (I, [P, ctypes.c_uint64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(U32),
+                                ctypes.POINTER(ctypes.c_uint64)]),
+        "lth_model_load": (I, [P, P, U32, ctypes.POINTER(P)]),
+        "lth_loaded_decoder": (P, [P]),
+        "lth_loaded_shape": (None, [P, ctypes.POINTER(U32)]),
+        "lth_loaded_free": (None, [P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -114,9 +124,13 @@ class ModelSpec:
 class Decoder:
     """A greedy decoder over a device model (lth_decoder)."""
 
-    def __init__(self, ctx: Context, spec: ModelSpec):
+    def __init__(self, ctx: Context, spec: ModelSpec | None, _handle: int | None = None):
         self.lib = load_host_library()
         self.ctx, self.spec = ctx, spec
+        if _handle is not None:  # owned by a LoadedModel
+            self.ptr, self._owned = _handle, False
+            return
+        self._owned = True
         self._layers = (_Layer * len(spec.layers))()
         for i, L in enumerate(spec.layers):
             self._layers[i] = _Layer(
@@ -138,7 +152,8 @@ class Decoder:
 
     def close(self) -> None:
         if getattr(self, "ptr", None):
-            self.lib.lth_decoder_free(self.ptr)
+            if self._owned:
+                self.lib.lth_decoder_free(self.ptr)
             self.ptr = None
 
     def __enter__(self):
@@ -216,3 +231,74 @@ def upload_decoder(ctx: Context, m, kv_cap: int = 4096, stacked_qkv: bool = True
                      lm_head=ctx.upload(m.lm_head, m.lm_type, m.vocab, d), out_norm=dev(m.out_norm),
                      layers=layers, n_used=m.k, norm_topk=m.norm_topk, rope_neox=m.rope_neox, eps=m.eps,
                      rope_theta=m.rope_theta, kv_cap=kv_cap)
+
+
+class GgufFile:
+    """A memory-mapped GGUF file (lth_gguf_open): metadata, tensors, info report."""
+
+    def __init__(self, path):
+        self.lib = load_host_library()
+        h = P()
+        st = self.lib.lth_gguf_open(str(path).encode(), ctypes.byref(h))
+        if st != 0:
+            raise LtError(st, f"cannot parse GGUF file {path}")
+        self.ptr = h.value
+
+    def info(self) -> str:
+        n = self.lib.lth_gguf_info(self.ptr, None, 0)
+        buf = ctypes.create_string_buffer(n + 1)
+        self.lib.lth_gguf_info(self.ptr, buf, n + 1)
+        return buf.value.decode()
+
+    def tensors(self) -> list[tuple[str, int, int]]:
+        out = []
+        for i in range(self.lib.lth_gguf_tensor_count(self.ptr)):
+            nm, t, nb = ctypes.c_char_p(), U32(), ctypes.c_uint64()
+            self.lib.lth_gguf_tensor(self.ptr, i, ctypes.byref(nm), ctypes.byref(t), ctypes.byref(nb))
+            out.append((nm.value.decode(), t.value, nb.value))
+        return out
+
+    def close(self) -> None:
+        if self.ptr:
+            self.lib.lth_gguf_close(self.ptr)
+            self.ptr = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+
+class LoadedModel:
+    """A decoder uploaded from a GGUF file (lth_model_load)."""
+
+    def __init__(self, ctx: Context, gguf: GgufFile, kv_cap: int = 4096):
+        self.lib = load_host_library()
+        self.ctx = ctx
+        h = P()
+        st = self.lib.lth_model_load(ctx.ptr, gguf.ptr, kv_cap, ctypes.byref(h))
+        if st != 0:
+            msg = ctx.lib.lt_last_error(ctx.ptr) or b""
+            raise LtError(st, f"model load failed: {msg.decode()}")
+        self.ptr = h.value
+        sh = (U32 * 8)()
+        self.lib.lth_loaded_shape(self.ptr, sh)
+        (self.n_layers, self.d_model, self.n_heads, self.n_kv_heads, self.head_dim, self.vocab, self.n_experts,
+         self.n_used) = list(sh)
+        self.decoder = Decoder(ctx, None, _handle=self.lib.lth_loaded_decoder(self.ptr))
+
+    def generate(self, prompt, n_gen: int) -> list[int]:
+        return self.decoder.generate(prompt, n_gen)
+
+    def close(self) -> None:
+        if self.ptr:
+            self.decoder.close()
+            self.lib.lth_loaded_free(self.ptr)
+            self.ptr = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()

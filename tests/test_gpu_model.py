@@ -251,3 +251,25 @@ def test_attn_block_matches_separate_ops(pkg, oracle, name, d, nh, nkv, hd, wt, 
         to.free()
         c.close()
     assert rel_l2(res[0], res[1]) < 2e-5, rel_l2(res[0], res[1])
+
+
+@pytest.mark.parametrize("moe", [True, False])
+def test_gguf_loaded_model_matches_oracle(ctx, oracle, pool, tmp_path, moe):
+    """A synthetic model written as a GGUF file, loaded by the C++ loader
+    (host/gguf.cpp: mmap, parse, upload, Q/K/V stacked) and decoded greedily:
+    the same tokens as the CPU oracle on the in-memory model."""
+    synth, decoder = _mods()
+    gguf = importlib.import_module("llmtoy-zig_b200.gguf")
+    if moe:
+        m = synth.DecoderModel(np.random.default_rng(31), 2, 256, 4, 2, 64, 3000, n_experts=8, k=2, d_expert=256,
+                               lm_type=14, qk_norm=True, rope_neox=True, norm_topk=True, norms_random=True)
+    else:
+        m = synth.DecoderModel(np.random.default_rng(32), 2, 256, 4, 2, 64, 3000, d_ffn=512, qkv_bias=True,
+                               norms_random=True)
+    path = gguf.write_model(tmp_path / "m.gguf", m)
+    prompt, n_gen = [11, 22, 2999, 7], 10
+    ref_toks, _ = oracle.OracleDecoder(m, 64, pool).generate(prompt, n_gen)
+    with decoder.GgufFile(path) as g, decoder.LoadedModel(ctx, g, kv_cap=64) as lm:
+        assert (lm.n_layers, lm.d_model, lm.vocab, lm.n_experts) == (2, 256, 3000, 8 if moe else 0)
+        assert lm.generate(prompt, n_gen) == ref_toks
+        assert lm.generate(prompt, n_gen) == ref_toks  # graph replay
