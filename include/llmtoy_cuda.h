@@ -286,6 +286,7 @@ typedef struct lt_attn_cfg {
     float scale;         /* score scale: 1/sqrt(head_dim) (forward.zig:300), 1 for Gemma 4 */
     uint32_t kv_cap;     /* positions per layer cache; slot = pos % kv_cap */
     uint32_t window;     /* 0: attend to every position; else the last `window` (sliding) */
+    uint32_t v_norm;     /* 1: RMSNorm without weights on each V head (gemma4/forward.zig:269) */
 } lt_attn_cfg;
 
 /* embedLookup (src/model/forward.zig:319-341): dev_out[cols] = dequantised
@@ -337,11 +338,27 @@ lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x,
 lt_status lt_prefetch_next(lt_ctx *ctx, const lt_tensor *a, const lt_tensor *b);
 
 /* The dense FFN block of a decoder layer (forward.zig:307-312):
- * out = x + down . (act(gate . xn) * (up . xn)), xn = rmsnorm(x) * norm_w,
- * for 2-D gate/up [F][d] and down [d][F].  dev_out may alias dev_x. */
+ * out = (residual ? x : 0) + down . (act(gate . xn) * (up . xn)),
+ * xn = rmsnorm(x) * norm_w, for 2-D gate/up [F][d] and down [d][F].
+ * dev_out may alias dev_x. */
 lt_status lt_ffn_block(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, const lt_tensor *down,
                        int act, const float *dev_norm_w, float eps, const float *dev_x, uint32_t ntok,
-                       float *dev_out);
+                       int residual, float *dev_out);
+
+/* Gemma 4 layer glue on ntok rows of n values (src/model/gemma4/forward.zig):
+ *   lt_scale        x *= s                                   (:117-120 embedding, :531 layer_output_scale)
+ *   lt_add_rmsnorm  x += rmsnorm(y) * w                      (:329-333 post_attention_norm)
+ *   lt_norm_pair    a = rmsnorm(x) * w, b = x * rms_inv * gs * g   (:401-410, math.zig:51-82)
+ *   lt_ffn_tail     m = rmsnorm(m) * w2; x = (x + rmsnorm(f + m) * w) * los   (:520-532)
+ *   lt_softcap      x = tanh(x / cap) * cap over n values   (:560-564) */
+lt_status lt_scale(lt_ctx *ctx, float *dev_x, uint32_t n, uint32_t ntok, float s);
+lt_status lt_add_rmsnorm(lt_ctx *ctx, const float *dev_y, const float *dev_w, float eps, uint32_t n,
+                         uint32_t ntok, float *dev_x);
+lt_status lt_norm_pair(lt_ctx *ctx, const float *dev_x, const float *dev_w, const float *dev_g, float gs,
+                       float eps, uint32_t n, uint32_t ntok, float *dev_a, float *dev_b);
+lt_status lt_ffn_tail(lt_ctx *ctx, const float *dev_f, float *dev_m, const float *dev_w2, const float *dev_w,
+                      float los, float eps, uint32_t n, uint32_t ntok, float *dev_x);
+lt_status lt_softcap(lt_ctx *ctx, float *dev_x, uint64_t n, float cap);
 
 /* greedy (sample.zig:11-17) as the last op of a decode step: with
  * p = *dev_pos, dev_tokens[p + 1] = argmax(logits) unless p + 1 is still a

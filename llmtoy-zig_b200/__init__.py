@@ -36,7 +36,7 @@ EXPORTS = [
     "lt_ep_dispatch", "lt_gather_rows", "lt_moe_combine",
     "lt_device_alloc", "lt_device_free", "lt_copy_to_device", "lt_copy_to_host",
     "lt_embed", "lt_qmatvec_add", "lt_attn_prep", "lt_attn_decode", "lt_attn_block", "lt_prefetch_next",
-    "lt_ffn_block", "lt_greedy_step",
+    "lt_ffn_block", "lt_greedy_step", "lt_scale", "lt_add_rmsnorm", "lt_norm_pair", "lt_ffn_tail", "lt_softcap",
 ]
 
 
@@ -56,7 +56,8 @@ class AttnCfg(ctypes.Structure):
     """lt_attn_cfg: geometry of one attention layer."""
     _fields_ = [("n_heads", ctypes.c_uint32), ("n_kv_heads", ctypes.c_uint32), ("head_dim", ctypes.c_uint32),
                 ("rope_neox", ctypes.c_uint32), ("rope_theta", ctypes.c_float), ("eps", ctypes.c_float),
-                ("scale", ctypes.c_float), ("kv_cap", ctypes.c_uint32), ("window", ctypes.c_uint32)]
+                ("scale", ctypes.c_float), ("kv_cap", ctypes.c_uint32), ("window", ctypes.c_uint32),
+                ("v_norm", ctypes.c_uint32)]
 
 
 _lib = None
@@ -117,7 +118,12 @@ def load_library() -> ctypes.CDLL:
         "lt_attn_prep": (I, [P, ctypes.POINTER(AttnCfg), P, P, P, P, P, P]),
         "lt_attn_decode": (I, [P, ctypes.POINTER(AttnCfg), P, P, P, P, P]),
         "lt_greedy_step": (I, [P, P, U32, P, P, P]),
-        "lt_ffn_block": (I, [P, P, P, P, I, P, F, P, U32, P]),
+        "lt_ffn_block": (I, [P, P, P, P, I, P, F, P, U32, I, P]),
+        "lt_scale": (I, [P, P, U32, U32, F]),
+        "lt_add_rmsnorm": (I, [P, P, P, F, U32, U32, P]),
+        "lt_norm_pair": (I, [P, P, P, P, F, F, U32, U32, P, P]),
+        "lt_ffn_tail": (I, [P, P, P, P, P, F, F, U32, U32, P]),
+        "lt_softcap": (I, [P, P, U64, F]),
         "lt_attn_block": (I, [P, ctypes.POINTER(AttnCfg), P, P, F, P, P, P, P, P, P, P, P, P]),
         "lt_prefetch_next": (I, [P, P, P]),
         "lt_quant_matvec_host": (I, [P, P, P, U32, P, U64, U64]),
@@ -354,10 +360,26 @@ class Context:
         self._check(self.lib.lt_prefetch_next(self.ptr, a.handle if a else None, b.handle if b else None))
 
     def ffn_block(self, gate: Tensor, up: Tensor, down: Tensor, act: int, norm_w, eps: float, x, ntok: int,
-                  out) -> None:
-        """out = x + down . (act(gate . xn) * (up . xn)), xn = rmsnorm(x) * norm_w (dense FFN block)."""
+                  out, residual: bool = True) -> None:
+        """out = (x if residual) + down . (act(gate . xn) * (up . xn)), xn = rmsnorm(x) * norm_w."""
         self._check(self.lib.lt_ffn_block(self.ptr, gate.handle, up.handle, down.handle, act, _ptr(norm_w), eps,
-                                          _ptr(x), ntok, _ptr(out)))
+                                          _ptr(x), ntok, int(residual), _ptr(out)))
+
+    # -- Gemma 4 layer glue -------------------------------------------------
+    def scale(self, x, n: int, ntok: int, s: float) -> None:
+        self._check(self.lib.lt_scale(self.ptr, _ptr(x), n, ntok, s))
+
+    def add_rmsnorm(self, y, w, eps: float, n: int, ntok: int, x) -> None:
+        self._check(self.lib.lt_add_rmsnorm(self.ptr, _ptr(y), _ptr(w), eps, n, ntok, _ptr(x)))
+
+    def norm_pair(self, x, w, g, gs: float, eps: float, n: int, ntok: int, a, b) -> None:
+        self._check(self.lib.lt_norm_pair(self.ptr, _ptr(x), _ptr(w), _ptr(g), gs, eps, n, ntok, _ptr(a), _ptr(b)))
+
+    def ffn_tail(self, f, m, w2, w, los: float, eps: float, n: int, ntok: int, x) -> None:
+        self._check(self.lib.lt_ffn_tail(self.ptr, _ptr(f), _ptr(m), _ptr(w2), _ptr(w), los, eps, n, ntok, _ptr(x)))
+
+    def softcap(self, x, n: int, cap: float) -> None:
+        self._check(self.lib.lt_softcap(self.ptr, _ptr(x), n, cap))
 
     def greedy_step(self, logits, n: int, tokens, pos, n_prompt) -> None:
         """n_prompt: a device word (the prompt length of the token stream)."""

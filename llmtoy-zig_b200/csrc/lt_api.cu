@@ -700,6 +700,7 @@ static lt_status attn_geom(lt_ctx *ctx, const lt_attn_cfg *cfg, lt::AttnGeom &g,
     g.scale = cfg->scale;
     g.cap = cfg->kv_cap;
     g.window = cfg->window;
+    g.v_norm = cfg->v_norm ? 1u : 0u;
     return LT_OK;
 }
 
@@ -1049,8 +1050,54 @@ lt_status lt_moe_block(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *ga
                         ntok, k, dev_out, dev_ids, dev_w);
 }
 
+lt_status lt_scale(lt_ctx *ctx, float *dev_x, uint32_t n, uint32_t ntok, float s) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!dev_x || n == 0) return fail(ctx, LT_EINVAL, "lt_scale: bad argument");
+    if (ntok == 0) return LT_OK;
+    return launched(ctx, lt::launch_scale(cfg_of(ctx), dev_x, n, ntok, s), "scale");
+}
+
+lt_status lt_add_rmsnorm(lt_ctx *ctx, const float *dev_y, const float *dev_w, float eps, uint32_t n, uint32_t ntok,
+                         float *dev_x) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!dev_y || !dev_w || !dev_x || n == 0) return fail(ctx, LT_EINVAL, "lt_add_rmsnorm: bad argument");
+    if (ntok == 0) return LT_OK;
+    return launched(ctx, lt::launch_add_rmsnorm(cfg_of(ctx), dev_y, dev_w, eps, n, ntok, dev_x), "add_rmsnorm");
+}
+
+lt_status lt_norm_pair(lt_ctx *ctx, const float *dev_x, const float *dev_w, const float *dev_g, float gs, float eps,
+                       uint32_t n, uint32_t ntok, float *dev_a, float *dev_b) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!dev_x || !dev_w || !dev_g || !dev_a || !dev_b || n == 0) return fail(ctx, LT_EINVAL, "lt_norm_pair: bad argument");
+    if (ntok == 0) return LT_OK;
+    return launched(ctx, lt::launch_norm_pair(cfg_of(ctx), dev_x, dev_w, dev_g, gs, eps, n, ntok, dev_a, dev_b),
+                    "norm_pair");
+}
+
+lt_status lt_ffn_tail(lt_ctx *ctx, const float *dev_f, float *dev_m, const float *dev_w2, const float *dev_w, float los,
+                      float eps, uint32_t n, uint32_t ntok, float *dev_x) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!dev_f || !dev_m || !dev_w2 || !dev_w || !dev_x || n == 0) return fail(ctx, LT_EINVAL, "lt_ffn_tail: bad argument");
+    if (ntok == 0) return LT_OK;
+    return launched(ctx, lt::launch_ffn_tail(cfg_of(ctx), dev_f, dev_m, dev_w2, dev_w, los, eps, n, ntok, dev_x),
+                    "ffn_tail");
+}
+
+lt_status lt_softcap(lt_ctx *ctx, float *dev_x, uint64_t n, float cap) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!dev_x || cap == 0.0f) return fail(ctx, LT_EINVAL, "lt_softcap: bad argument");
+    if (n == 0) return LT_OK;
+    return launched(ctx, lt::launch_softcap(cfg_of(ctx), dev_x, n, cap), "softcap");
+}
+
 lt_status lt_ffn_block(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, const lt_tensor *down, int act,
-                       const float *dev_norm_w, float eps, const float *dev_x, uint32_t ntok, float *dev_out) {
+                       const float *dev_norm_w, float eps, const float *dev_x, uint32_t ntok, int residual,
+                       float *dev_out) {
     lt_status st = enter(ctx);
     if (st != LT_OK) return st;
     if (!gate || !up || !down || !dev_norm_w || !dev_x || !dev_out) return fail(ctx, LT_EINVAL, "lt_ffn_block: null argument");
@@ -1078,7 +1125,8 @@ lt_status lt_ffn_block(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, 
     if (st != LT_OK) return st;
     st = launched(ctx, lt::launch_quantize(c, xn, (uint32_t)d, ntok, s.xq, s.xq_pitch), "quantize");
     if (st != LT_OK) return st;
-    return ffn_impl(ctx, gate, up, down, act, ntok, ctx->zeros, ctx->ones, 1, dev_x, dev_out, xn, s);
+    return ffn_impl(ctx, gate, up, down, act, ntok, ctx->zeros, ctx->ones, 1, residual ? dev_x : nullptr, dev_out, xn,
+                    s);
 }
 
 lt_status lt_ep_dispatch(lt_ctx *ctx, const uint32_t *dev_ids, uint32_t ntok, uint32_t k, uint32_t n_experts,

@@ -79,7 +79,16 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_prep(AttnGeom g, float *q
     if (!is_q) {
         const float *vs = qkv + nq + nkv + (size_t)kh * hd;
         float *vd = vc + (size_t)(pos % g.cap) * nkv + (size_t)kh * hd;
-        for (uint32_t i = threadIdx.x; i < hd; i += kAttnThreads) vd[i] = vs[i];
+        if (g.v_norm) {  // rmsnormRaw (math.zig:43-48) of the V head
+            __syncthreads();
+            float ss = 0.0f;
+            for (uint32_t i = threadIdx.x; i < hd; i += kAttnThreads) ss = __fadd_rn(ss, __fmul_rn(vs[i], vs[i]));
+            ss = block_sum128(ss, red);
+            const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), g.eps)));
+            for (uint32_t i = threadIdx.x; i < hd; i += kAttnThreads) vd[i] = __fmul_rn(vs[i], r);
+        } else {
+            for (uint32_t i = threadIdx.x; i < hd; i += kAttnThreads) vd[i] = vs[i];
+        }
     }
 }
 

@@ -285,6 +285,14 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
             reinterpret_cast<float4 *>(hq + part * HD)[i] = __ldcg(reinterpret_cast<const float4 *>(a.qkv + off) + i);
         }
         __syncthreads();
+        if (a.g.v_norm) {  // rmsnormRaw (math.zig:43-48) of the V head
+            const float vv = tid < HD ? hv[tid] : 0.0f;
+            const float ss = ab_block_sum(tid < HD ? __fmul_rn(vv, vv) : 0.0f, red);
+            const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)HD), a.g.eps)));
+            __syncthreads();
+            if (tid < HD) hv[tid] = __fmul_rn(vv, r);
+            __syncthreads();
+        }
         ab_norm_rope2(hq, a.q_norm, hk, a.k_norm, a.g, pos, red);
         if (s == 0 && h % group == 0) {  // this position's K/V into the cache
             const size_t slot = (size_t)(pos % a.g.cap) * nkv + (size_t)kh * HD;

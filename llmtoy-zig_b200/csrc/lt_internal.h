@@ -82,6 +82,15 @@ cudaError_t launch_argmax(const LaunchCfg &c, const float *x, uint32_t n, uint32
                           uint32_t *counters, uint32_t *tokens = nullptr, uint32_t *pos = nullptr,
                           const uint32_t *n_prompt = nullptr);
 cudaError_t launch_fill_f32(cudaStream_t s, float *p, size_t n, float v);
+// Gemma 4 layer glue (lt_glue.cu), ntok rows of n values.
+cudaError_t launch_scale(const LaunchCfg &c, float *x, uint32_t n, uint32_t ntok, float s);
+cudaError_t launch_add_rmsnorm(const LaunchCfg &c, const float *y, const float *w, float eps, uint32_t n,
+                               uint32_t ntok, float *x);
+cudaError_t launch_norm_pair(const LaunchCfg &c, const float *x, const float *w, const float *g, float gs, float eps,
+                             uint32_t n, uint32_t ntok, float *a, float *b);
+cudaError_t launch_ffn_tail(const LaunchCfg &c, const float *f, float *m, const float *w2, const float *w, float los,
+                            float eps, uint32_t n, uint32_t ntok, float *x);
+cudaError_t launch_softcap(const LaunchCfg &c, float *x, size_t n, float cap);
 // out = dequantised row tokens[*pos] of m (embedLookup); rows >= m.rows set
 // DEV_ERR_BAD_INDEX and read row 0.
 cudaError_t launch_embed(const LaunchCfg &c, const DevMat &m, const uint32_t *tokens, const uint32_t *pos,
@@ -95,6 +104,7 @@ struct AttnGeom {
     float theta, eps, scale;
     uint32_t cap;
     uint32_t window;  // 0: every cached position; else the last `window`
+    uint32_t v_norm;  // 1: RMSNorm without weights on each V head before caching (gemma4/forward.zig:269)
 };
 uint32_t attn_splits(const AttnGeom &g, int num_sms);
 size_t attn_scratch_floats(const AttnGeom &g, int num_sms);

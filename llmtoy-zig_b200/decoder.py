@@ -23,14 +23,21 @@ U32 = ctypes.c_uint32
 class _Layer(ctypes.Structure):
     _fields_ = [("attn_norm", P), ("ffn_norm", P), ("wqkv", P), ("wq", P), ("wk", P), ("wv", P), ("wo", P),
                 ("qkv_bias", P), ("q_norm", P), ("k_norm", P), ("ffn_gate", P), ("ffn_up", P), ("ffn_down", P),
-                ("router", P), ("exp_gate", P), ("exp_up", P), ("exp_down", P)]
+                ("router", P), ("exp_gate", P), ("exp_up", P), ("exp_down", P),
+                ("post_attention_norm", P), ("pre_ffw_norm_2", P), ("post_ffw_norm_1", P), ("post_ffw_norm_2", P),
+                ("post_ffw_norm", P), ("router_scale", P), ("down_exps_scale", P),
+                ("layer_output_scale", ctypes.c_float), ("is_swa", U32), ("n_kv_heads", U32), ("head_dim", U32)]
 
 
 class _Model(ctypes.Structure):
     _fields_ = [("n_layers", U32), ("d_model", U32), ("n_heads", U32), ("n_kv_heads", U32), ("head_dim", U32),
                 ("vocab", U32), ("n_used", U32), ("norm_topk", U32), ("rope_neox", U32), ("act", U32),
                 ("eps", ctypes.c_float), ("rope_theta", ctypes.c_float), ("kv_cap", U32),
-                ("token_emb", P), ("lm_head", P), ("out_norm", P), ("layers", ctypes.POINTER(_Layer))]
+                ("token_emb", P), ("lm_head", P), ("out_norm", P), ("layers", ctypes.POINTER(_Layer)),
+                ("family", U32), ("rope_theta_swa", ctypes.c_float), ("logit_softcap", ctypes.c_float),
+                ("sliding_window", U32)]
+
+LLAMA, GEMMA4 = 0, 1
 
 
 _host = None
@@ -99,6 +106,18 @@ class LayerSpec:
     exp_gate: Tensor | None = None
     exp_up: Tensor | None = None
     exp_down: Tensor | None = None
+    # Gemma 4 only
+    post_attention_norm: object = None
+    pre_ffw_norm_2: object = None
+    post_ffw_norm_1: object = None
+    post_ffw_norm_2: object = None
+    post_ffw_norm: object = None
+    router_scale: object = None
+    down_exps_scale: object = None
+    layer_output_scale: float = 1.0
+    is_swa: bool = False
+    n_kv_heads: int = 0
+    head_dim: int = 0
 
 
 @dataclass
@@ -119,6 +138,10 @@ class ModelSpec:
     eps: float = 1e-6
     rope_theta: float = 1e6
     kv_cap: int = 4096
+    family: int = 0
+    rope_theta_swa: float = 1e4
+    logit_softcap: float = 0.0
+    sliding_window: int = 0
 
 
 class Decoder:
@@ -136,11 +159,15 @@ class Decoder:
             self._layers[i] = _Layer(
                 _ptr(L.attn_norm), _ptr(L.ffn_norm), _h(L.wqkv), _h(L.wq), _h(L.wk), _h(L.wv), _h(L.wo),
                 _ptr(L.qkv_bias), _ptr(L.q_norm), _ptr(L.k_norm), _h(L.ffn_gate), _h(L.ffn_up), _h(L.ffn_down),
-                _h(L.router), _h(L.exp_gate), _h(L.exp_up), _h(L.exp_down))
+                _h(L.router), _h(L.exp_gate), _h(L.exp_up), _h(L.exp_down), _ptr(L.post_attention_norm),
+                _ptr(L.pre_ffw_norm_2), _ptr(L.post_ffw_norm_1), _ptr(L.post_ffw_norm_2), _ptr(L.post_ffw_norm),
+                _ptr(L.router_scale), _ptr(L.down_exps_scale), L.layer_output_scale, int(L.is_swa), L.n_kv_heads,
+                L.head_dim)
         s = spec
         self._model = _Model(len(s.layers), s.d_model, s.n_heads, s.n_kv_heads, s.head_dim, s.vocab, s.n_used,
                              int(s.norm_topk), int(s.rope_neox), s.act, s.eps, s.rope_theta, s.kv_cap,
-                             _h(s.token_emb), _h(s.lm_head), _ptr(s.out_norm), self._layers)
+                             _h(s.token_emb), _h(s.lm_head), _ptr(s.out_norm), self._layers, s.family,
+                             s.rope_theta_swa, s.logit_softcap, s.sliding_window)
         h = P()
         self._check(self.lib.lth_decoder_create(ctx.ptr, ctypes.byref(self._model), ctypes.byref(h)))
         self.ptr = h.value
@@ -302,3 +329,40 @@ class LoadedModel:
 
     def __exit__(self, *a):
         self.close()
+
+
+def upload_gemma(ctx: Context, m, kv_cap: int = 4096) -> ModelSpec:
+    """Upload a synth.GemmaModel (host GGUF bytes) and return its ModelSpec."""
+    import numpy as np
+    import torch
+
+    def dev(a):
+        return None if a is None else torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda()
+
+    d, E, F = m.d_model, m.n_experts, m.d_expert
+    layers = []
+    for L in m.layers:
+        nq, nkv = m.n_heads * L.head_dim, L.n_kv_heads * L.head_dim
+        t = L.types
+        ls = LayerSpec(attn_norm=dev(L.attn_norm), ffn_norm=dev(L.ffn_norm), wo=ctx.upload(L.wo, t["wo"], d, nq),
+                       wq=ctx.upload(L.wq, t["wq"], nq, d), wk=ctx.upload(L.wk, t["wk"], nkv, d),
+                       wv=None if L.wv is None else ctx.upload(L.wv, t["wv"], nkv, d),
+                       q_norm=dev(L.q_norm), k_norm=dev(L.k_norm),
+                       ffn_gate=ctx.upload(L.w_gate, t["gate"], m.d_ffn, d),
+                       ffn_up=ctx.upload(L.w_up, t["up"], m.d_ffn, d),
+                       ffn_down=ctx.upload(L.w_down, t["down"], d, m.d_ffn),
+                       router=ctx.upload(L.router_w, 0, E, d),
+                       exp_gate=ctx.upload(L.gate_up_exps, t["gate_up_exps"], 2 * F, d, n_experts=E),
+                       exp_down=ctx.upload(L.down_exps, t["down_exps"], d, F, n_experts=E),
+                       post_attention_norm=dev(L.post_attention_norm), pre_ffw_norm_2=dev(L.pre_ffw_norm_2),
+                       post_ffw_norm_1=dev(L.post_ffw_norm_1), post_ffw_norm_2=dev(L.post_ffw_norm_2),
+                       post_ffw_norm=dev(L.post_ffw_norm), router_scale=dev(L.router_scale),
+                       down_exps_scale=dev(L.down_exps_scale), layer_output_scale=float(L.layer_output_scale),
+                       is_swa=L.is_swa, n_kv_heads=L.n_kv_heads, head_dim=L.head_dim)
+        layers.append(ls)
+    return ModelSpec(d_model=d, n_heads=m.n_heads, n_kv_heads=m.layers[0].n_kv_heads, head_dim=m.layers[0].head_dim,
+                     vocab=m.vocab, token_emb=ctx.upload(m.token_emb, m.emb_type, m.vocab, d),
+                     lm_head=ctx.upload(m.lm_head, m.lm_type, m.vocab, d), out_norm=dev(m.out_norm), layers=layers,
+                     n_used=m.k, norm_topk=False, rope_neox=True, act=1, eps=m.eps, rope_theta=m.rope_theta_global,
+                     kv_cap=kv_cap, family=GEMMA4, rope_theta_swa=m.rope_theta_swa, logit_softcap=m.logit_softcap,
+                     sliding_window=m.sliding_window)

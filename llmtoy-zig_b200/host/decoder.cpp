@@ -23,6 +23,12 @@ struct lth_decoder {
     uint32_t nq = 0, nkv = 0;
     float *x = nullptr, *xb = nullptr, *qkv = nullptr, *att = nullptr, *logits = nullptr;
     float *kcache = nullptr, *vcache = nullptr;
+    std::vector<size_t> kv_off;  // per layer: offset of its cache (floats)
+    // Gemma 4: attention output, dense FFN, MoE accumulator, expert and router inputs, routing
+    float *ybuf = nullptr, *fbuf = nullptr, *mbuf = nullptr, *moe_in = nullptr, *router_in = nullptr;
+    uint32_t *ids = nullptr;
+    float *wts = nullptr;
+    uint32_t *ids_zero = nullptr;  // {0}: row index of a one-row gather
     uint32_t *tokens = nullptr;  // [kv_cap + 1]
     uint32_t *state = nullptr;   // {pos, n_prompt}
     lt_graph *graph = nullptr;
@@ -52,8 +58,7 @@ lt_status layer_step(lth_decoder *d, uint32_t l) {
     const lth_layer &L = d->layers[l];
     lt_ctx *c = d->ctx;
     const uint32_t *pos = d->state;
-    const size_t cache = (size_t)m.kv_cap * d->nkv;
-    float *kc = d->kcache + (size_t)l * cache, *vc = d->vcache + (size_t)l * cache;
+    float *kc = d->kcache + d->kv_off[l], *vc = d->vcache + d->kv_off[l];
     const lth_layer *next = l + 1 < m.n_layers ? &d->layers[l + 1] : nullptr;
     if (L.wqkv) {  // the whole attention half in one launch; warm this layer's router in L2 meanwhile
         LTH_TRY(lt_prefetch_next(c, L.router, nullptr));
@@ -67,7 +72,7 @@ lt_status layer_step(lth_decoder *d, uint32_t l) {
         return lt_moe_block(c, L.router, L.exp_gate, L.exp_up, L.exp_down, (int)m.act, (int)m.norm_topk, nullptr,
                             L.ffn_norm, m.eps, d->x, 1, m.n_used, d->x, nullptr, nullptr);
     }
-    return lt_ffn_block(c, L.ffn_gate, L.ffn_up, L.ffn_down, (int)m.act, L.ffn_norm, m.eps, d->x, 1, d->x);
+    return lt_ffn_block(c, L.ffn_gate, L.ffn_up, L.ffn_down, (int)m.act, L.ffn_norm, m.eps, d->x, 1, 1, d->x);
 }
 
 // The attention half as separate ops (separate Q/K/V tensors).
@@ -96,18 +101,73 @@ lt_status attn_ops(lth_decoder *d, const lth_layer &L, float *kc, float *vc) {
     return lt_qmatvec_add(c, L.wo, 0, d->att, d->x, d->x, 1);
 }
 
+// One Gemma 4 layer (gemma4/forward.zig:195-533, the CPU branches).
+lt_status gemma_layer(lth_decoder *d, uint32_t l) {
+    const lth_model &m = d->m;
+    const lth_layer &L = d->layers[l];
+    lt_ctx *c = d->ctx;
+    const uint32_t *pos = d->state;
+    const uint32_t hd = L.head_dim ? L.head_dim : m.head_dim, nkvh = L.n_kv_heads ? L.n_kv_heads : m.n_kv_heads;
+    const uint32_t nq = m.n_heads * hd, nkv = nkvh * hd;
+    lt_attn_cfg a{};
+    a.n_heads = m.n_heads;
+    a.n_kv_heads = nkvh;
+    a.head_dim = hd;
+    a.rope_neox = 1;  // applyRopeNeox / applyRopeFreqsNeox
+    a.rope_theta = L.is_swa ? m.rope_theta_swa : m.rope_theta;
+    a.eps = m.eps;
+    a.scale = 1.0f;  // per-head Q/K norms control the magnitude (forward.zig:324)
+    a.kv_cap = L.is_swa ? m.sliding_window : m.kv_cap;
+    a.window = L.is_swa ? m.sliding_window : 0;
+    a.v_norm = 1;
+    float *kc = d->kcache + d->kv_off[l], *vc = d->vcache + d->kv_off[l];
+    LTH_TRY(lt_rmsnorm(c, d->x, L.attn_norm, m.eps, m.d_model, 1, d->xb));
+    LTH_TRY(lt_qmatvec(c, L.wq, 0, d->xb, d->qkv, 1));
+    LTH_TRY(lt_qmatvec(c, L.wk, 0, d->xb, d->qkv + nq, 1));
+    if (L.wv) {
+        LTH_TRY(lt_qmatvec(c, L.wv, 0, d->xb, d->qkv + nq + nkv, 1));
+    } else {  // V = K before the norms (forward.zig:250)
+        LTH_TRY(lt_gather_rows(c, d->qkv + nq, nkv, d->ids_zero, 1, d->qkv + nq + nkv));
+    }
+    LTH_TRY(lt_attn_prep(c, &a, d->qkv, L.q_norm, L.k_norm, pos, kc, vc));
+    LTH_TRY(lt_attn_decode(c, &a, d->qkv, kc, vc, pos, d->att));
+    LTH_TRY(lt_qmatvec(c, L.wo, 0, d->att, d->ybuf, 1));
+    LTH_TRY(lt_add_rmsnorm(c, d->ybuf, L.post_attention_norm, m.eps, m.d_model, 1, d->x));
+    // dense GeGLU FFN, post_ffw_norm_1 (:390-396)
+    LTH_TRY(lt_ffn_block(c, L.ffn_gate, L.ffn_up, L.ffn_down, LT_ACT_GELU_TANH, L.ffn_norm, m.eps, d->x, 1, 0,
+                         d->fbuf));
+    LTH_TRY(lt_rmsnorm(c, d->fbuf, L.post_ffw_norm_1, m.eps, m.d_model, 1, d->fbuf));
+    // MoE: weighted and raw-scaled norms of x, router, experts (:401-494)
+    LTH_TRY(lt_norm_pair(c, d->x, L.pre_ffw_norm_2, L.router_scale, 1.0f / __builtin_sqrtf((float)m.d_model), m.eps,
+                         m.d_model, 1, d->moe_in, d->router_in));
+    LTH_TRY(lt_moe_route(c, L.router, d->router_in, 1, m.n_used, 0, L.down_exps_scale, d->ids, d->wts));
+    LTH_TRY(lt_moe_ffn(c, L.exp_gate, L.exp_up, L.exp_down, LT_ACT_GELU_TANH, d->moe_in, 1, d->ids, d->wts, m.n_used,
+                       d->mbuf));
+    return lt_ffn_tail(c, d->fbuf, d->mbuf, L.post_ffw_norm_2, L.post_ffw_norm, L.layer_output_scale, m.eps,
+                       m.d_model, 1, d->x);
+}
+
 lt_status step(lth_decoder *d) {
     const lth_model &m = d->m;
     LTH_TRY(lt_embed(d->ctx, m.token_emb, d->tokens, d->state, d->x));
-    for (uint32_t l = 0; l < m.n_layers; l++) LTH_TRY(layer_step(d, l));
+    if (m.family == LTH_GEMMA4) {
+        LTH_TRY(lt_scale(d->ctx, d->x, m.d_model, 1, __builtin_sqrtf((float)m.d_model)));  // forward.zig:117-120
+        for (uint32_t l = 0; l < m.n_layers; l++) LTH_TRY(gemma_layer(d, l));
+    } else {
+        for (uint32_t l = 0; l < m.n_layers; l++) LTH_TRY(layer_step(d, l));
+    }
     LTH_TRY(lt_rmsnorm(d->ctx, d->x, m.out_norm, m.eps, m.d_model, 1, d->xb));
     LTH_TRY(lt_qmatvec(d->ctx, m.lm_head, 0, d->xb, d->logits, 1));
+    if (m.family == LTH_GEMMA4 && m.logit_softcap != 0.0f)
+        LTH_TRY(lt_softcap(d->ctx, d->logits, m.vocab, m.logit_softcap));
     return lt_greedy_step(d->ctx, d->logits, m.vocab, d->tokens, d->state, d->state + 1);
 }
 
 void release(lth_decoder *d) {
     if (d->graph) lt_graph_free(d->ctx, d->graph);
-    void *bufs[] = {d->x, d->xb, d->qkv, d->att, d->logits, d->kcache, d->vcache, d->tokens, d->state};
+    void *bufs[] = {d->x,    d->xb,     d->qkv,       d->att,       d->logits,    d->kcache, d->vcache,
+                    d->ybuf, d->fbuf,   d->mbuf,      d->moe_in,    d->router_in, d->ids,    d->wts,
+                    d->ids_zero, d->tokens, d->state};
     for (void *b : bufs)
         if (b) lt_device_free(d->ctx, b);
 }
@@ -137,13 +197,36 @@ lt_status lth_decoder_create(lt_ctx *ctx, const lth_model *m, lth_decoder **out)
     d->attn.scale = 1.0f / __builtin_sqrtf((float)m->head_dim);  // forward.zig:300
     d->attn.kv_cap = m->kv_cap;
     d->attn.window = 0;
-    const size_t cache = (size_t)m->n_layers * m->kv_cap * d->nkv;
+    // per-layer caches: the model's heads and kv_cap positions, or (Gemma 4)
+    // this layer's heads and, for sliding-window layers, a ring of the window
+    size_t cache = 0, max_q = d->nq, max_kv = d->nkv;
+    for (uint32_t l = 0; l < m->n_layers; l++) {
+        const lth_layer &L = m->layers[l];
+        const bool g4 = m->family == LTH_GEMMA4;
+        const size_t hd = g4 && L.head_dim ? L.head_dim : m->head_dim;
+        const size_t nkv = (g4 && L.n_kv_heads ? L.n_kv_heads : m->n_kv_heads) * hd;
+        const size_t cap = g4 && L.is_swa ? m->sliding_window : m->kv_cap;
+        if (g4 && L.is_swa && (m->sliding_window == 0 || m->sliding_window > m->kv_cap)) {
+            delete d;
+            return LT_EINVAL;
+        }
+        d->kv_off.push_back(cache);
+        cache += cap * nkv;
+        if (m->n_heads * hd > max_q) max_q = m->n_heads * hd;
+        if (nkv > max_kv) max_kv = nkv;
+    }
+    const size_t dm = m->d_model;
     lt_status st;
-    if ((st = alloc(d, &d->x, m->d_model)) != LT_OK || (st = alloc(d, &d->xb, m->d_model)) != LT_OK ||
-        (st = alloc(d, &d->qkv, d->nq + 2 * d->nkv)) != LT_OK || (st = alloc(d, &d->att, d->nq)) != LT_OK ||
+    if ((st = alloc(d, &d->x, dm)) != LT_OK || (st = alloc(d, &d->xb, dm)) != LT_OK ||
+        (st = alloc(d, &d->qkv, max_q + 2 * max_kv)) != LT_OK || (st = alloc(d, &d->att, max_q)) != LT_OK ||
         (st = alloc(d, &d->logits, m->vocab)) != LT_OK || (st = alloc(d, &d->kcache, cache)) != LT_OK ||
         (st = alloc(d, &d->vcache, cache)) != LT_OK || (st = alloc(d, &d->tokens, (size_t)m->kv_cap + 1)) != LT_OK ||
-        (st = alloc(d, &d->state, 2)) != LT_OK) {
+        (st = alloc(d, &d->state, 2)) != LT_OK || (st = alloc(d, &d->ids_zero, 4)) != LT_OK ||
+        (m->family == LTH_GEMMA4 &&
+         ((st = alloc(d, &d->ybuf, dm)) != LT_OK || (st = alloc(d, &d->fbuf, dm)) != LT_OK ||
+          (st = alloc(d, &d->mbuf, dm)) != LT_OK || (st = alloc(d, &d->moe_in, dm)) != LT_OK ||
+          (st = alloc(d, &d->router_in, dm)) != LT_OK || (st = alloc(d, &d->ids, 16)) != LT_OK ||
+          (st = alloc(d, &d->wts, 16)) != LT_OK))) {
         release(d);
         delete d;
         return st;

@@ -33,7 +33,17 @@ typedef struct lth_layer {
     const float *q_norm, *k_norm;        /* device [head_dim] or NULL (per-head RMSNorm) */
     const lt_tensor *ffn_gate, *ffn_up, *ffn_down;         /* dense FFN (router NULL)   */
     const lt_tensor *router, *exp_gate, *exp_up, *exp_down; /* MoE FFN                 */
+    /* family LTH_GEMMA4 only (src/model/gemma4/weights.zig): exp_up NULL, exp_gate
+     * is the fused gate_up tensor; wv NULL means V = K */
+    const float *post_attention_norm, *pre_ffw_norm_2, *post_ffw_norm_1, *post_ffw_norm_2, *post_ffw_norm;
+    const float *router_scale;           /* device [d_model] */
+    const float *down_exps_scale;        /* device [n_experts] */
+    float layer_output_scale;
+    uint32_t is_swa;                     /* sliding-window layer */
+    uint32_t n_kv_heads, head_dim;       /* this layer's (0: the model's) */
 } lth_layer;
+
+enum { LTH_LLAMA = 0, LTH_GEMMA4 = 1 };
 
 typedef struct lth_model {
     uint32_t n_layers, d_model, n_heads, n_kv_heads, head_dim, vocab;
@@ -46,6 +56,12 @@ typedef struct lth_model {
     const lt_tensor *token_emb, *lm_head;
     const float *out_norm; /* device [d_model] */
     const lth_layer *layers;
+    /* LTH_LLAMA: forwardOneModel (src/model/forward.zig:229-316) with the MoE
+     * block option; LTH_GEMMA4: gemma4/forward.zig:37-567 (embedding scale,
+     * SWA ring caches, post norms, dense + MoE GeGLU FFNs, logit soft-cap) */
+    uint32_t family;
+    float rope_theta_swa, logit_softcap;
+    uint32_t sliding_window;
 } lth_model;
 
 typedef struct lth_decoder lth_decoder;

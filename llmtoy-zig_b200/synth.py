@@ -178,3 +178,71 @@ def config2_model(rng, n_layers: int = 48, vocab: int = 151936, **kw) -> Decoder
     """Config 2: Qwen3-30B-A3B shape, Q8_0 attention, Q4_K experts, Q6_K lm_head."""
     return DecoderModel(rng, n_layers, 2048, 32, 4, 128, vocab, n_experts=128, k=8, d_expert=768,
                         lm_type=Q6_K, qk_norm=True, rope_neox=True, norm_topk=True, **kw)
+
+
+class GemmaLayer:
+    """One Gemma 4 decoder layer (src/model/gemma4/weights.zig) with a seeded
+    per-tensor quantisation mix; tensors whose columns are not a multiple of
+    256 are Q8_0 (the K-quants need whole superblocks)."""
+
+    def __init__(self, rng, d, n_heads, n_kv, hd, d_ffn, n_experts, d_expert, is_swa, pick, norms_random, wv=True):
+        self.is_swa, self.n_kv_heads, self.head_dim = is_swa, n_kv, hd
+        nq, nkv = n_heads * hd, n_kv * hd
+        norm = (lambda n: rng.uniform(0.5, 1.5, n).astype(np.float32)) if norms_random else \
+            (lambda n: np.ones(n, np.float32))
+        self.attn_norm, self.post_attention_norm, self.ffn_norm = norm(d), norm(d), norm(d)
+        self.pre_ffw_norm_2, self.post_ffw_norm_1, self.post_ffw_norm_2 = norm(d), norm(d), norm(d)
+        self.post_ffw_norm = norm(d)
+        self.q_norm, self.k_norm = norm(hd), norm(hd)
+        self.layer_output_scale = np.float32(rng.uniform(0.5, 1.0) if norms_random else 1.0)
+        self.types = {}
+
+        def mat(name, rows, cols, n=1):
+            t = pick(cols)
+            self.types[name] = t
+            return matrix(rng, t, n * rows, cols)
+
+        self.wq = mat("wq", nq, d)
+        self.wk = mat("wk", nkv, d)
+        self.wv = mat("wv", nkv, d) if wv else None
+        self.wo = mat("wo", d, nq)
+        self.w_gate = mat("gate", d_ffn, d)
+        t = self.types["gate"]  # gate and up share a type (one dense GeGLU pair)
+        self.types["up"] = t
+        self.w_up = matrix(rng, t, d_ffn, d)
+        self.w_down = mat("down", d, d_ffn)
+        self.router_w = router_weights(rng, n_experts, d)
+        self.router_scale = norm(d)
+        self.gate_up_exps = mat("gate_up_exps", 2 * d_expert, d, n_experts)
+        self.down_exps = mat("down_exps", d, d_expert, n_experts)
+        self.down_exps_scale = rng.uniform(0.5, 1.5, n_experts).astype(np.float32)
+
+
+class GemmaModel:
+    """Config 3: a Gemma-4-26B-A4B-like decoder (sliding-window : global = 5 : 1,
+    128 GeGLU experts top-8 + a dense GeGLU FFN, soft-capped logits) with a
+    seeded per-tensor mix of 60% Q4_K, 25% Q6_K, 15% Q8_0, Q8_0 where the
+    columns are not a multiple of 256."""
+
+    def __init__(self, rng, n_layers=30, d_model=2816, n_heads=16, n_kv_heads=8, head_dim=256, d_ffn=2112,
+                 n_experts=128, k=8, d_expert=704, vocab=262144, sliding_window=1024, swa_period=6,
+                 norms_random=False, eps=1e-6, rope_theta_swa=1e4, rope_theta_global=1e6, logit_softcap=30.0,
+                 lm_type=Q6_K):
+        self.n_layers, self.d_model, self.n_heads, self.d_ffn = n_layers, d_model, n_heads, d_ffn
+        self.n_experts, self.k, self.d_expert, self.vocab = n_experts, k, d_expert, vocab
+        self.sliding_window, self.eps = sliding_window, eps
+        self.rope_theta_swa, self.rope_theta_global, self.logit_softcap = rope_theta_swa, rope_theta_global, logit_softcap
+
+        def pick(cols):
+            if cols % 256:
+                return Q8_0
+            u = rng.uniform()
+            return Q4_K if u < 0.60 else Q6_K if u < 0.85 else Q8_0
+
+        self.emb_type = pick(d_model)
+        self.token_emb = matrix(rng, self.emb_type, vocab, d_model)
+        self.layers = [GemmaLayer(rng, d_model, n_heads, n_kv_heads, head_dim, d_ffn, n_experts, d_expert,
+                                  (i + 1) % swa_period != 0, pick, norms_random) for i in range(n_layers)]
+        self.out_norm = (rng.uniform(0.5, 1.5, d_model) if norms_random else np.ones(d_model)).astype(np.float32)
+        self.lm_type = lm_type
+        self.lm_head = matrix(rng, lm_type, vocab, d_model)

@@ -805,3 +805,139 @@ int orc_model_step(const orc_model *m, float *k_cache, float *v_cache, size_t kv
     free(proj); free(g); free(u); free(fo);
     return rc ? -1 : 0;
 }
+
+/* gemma4/forward.zig:37-567, CPU branches (see oracle.h) */
+int orc_gemma_step(const orc_gemma *m, float *k_cache, float *v_cache, size_t global_cap, uint32_t token,
+                   size_t pos, float *logits, orc_pool *pool) {
+    const size_t d = m->d_model, seq = pos + 1, hdg = m->head_dim_global;
+    if (token >= m->vocab) return -1;
+    size_t max_hd = m->head_dim_swa > hdg ? m->head_dim_swa : hdg, max_nkv = 0;
+    for (size_t l = 0; l < m->n_layers; l++) {
+        const size_t hd = m->layers[l].is_swa ? m->head_dim_swa : hdg;
+        if (m->layers[l].n_kv_heads * hd > max_nkv) max_nkv = m->layers[l].n_kv_heads * hd;
+    }
+    const size_t max_nq = m->n_heads * max_hd;
+    size_t max_cols = d > max_nq ? d : max_nq;
+    if (m->d_ffn > max_cols) max_cols = m->d_ffn;
+    const size_t nthr = (size_t)orc_pool_threads(pool);
+    float *scratch = (float *)malloc((nthr ? nthr : 1) * max_cols * 4);
+    float *x = (float *)malloc(d * 4), *xb = (float *)malloc(d * 4), *attn_buf = (float *)malloc(d * 4);
+    float *ffn = (float *)malloc(d * 4), *moe = (float *)malloc(d * 4), *moe_in = (float *)malloc(d * 4);
+    float *router_in = (float *)malloc(d * 4), *scores = (float *)malloc(m->n_experts * 4);
+    float *q = (float *)malloc(max_nq * 4), *kk = (float *)malloc(max_nkv * 4), *vv = (float *)malloc(max_nkv * 4);
+    float *att = (float *)malloc(max_nq * 4);
+    const size_t max_win = seq > m->sliding_window ? seq : m->sliding_window;
+    float *ks = (float *)malloc(max_win * max_hd * 4), *vs = (float *)malloc(max_win * max_hd * 4);
+    float *g = (float *)malloc(m->d_ffn * 4), *u = (float *)malloc(m->d_ffn * 4);
+    float *eg = (float *)malloc(m->d_expert * 4), *eu = (float *)malloc(m->d_expert * 4), *ed = (float *)malloc(d * 4);
+    float *freqs = (float *)malloc((hdg / 2) * 4);
+    uint32_t top_idx[16];
+    int rc = 0;
+    if (m->k > 16) rc = -1;
+    for (size_t i = 0; i < hdg / 2; i++)  /* loader.zig:225-233 fallback */
+        freqs[i] = m->rope_freqs ? m->rope_freqs[i] : 1.0f / powf(1000000.0f, (float)(2 * i) / (float)hdg);
+    if (rc == 0) rc = orc_dequant_row(m->token_emb + (size_t)token * orc_row_bytes(m->emb_type, d), x, d, m->emb_type);
+    const float emb_scale = sqrtf((float)d);  /* forward.zig:117-120 */
+    for (size_t i = 0; i < d; i++) x[i] *= emb_scale;
+    size_t kv_off = 0;
+    for (size_t l = 0; l < m->n_layers && rc == 0; l++) {
+        const orc_gemma_layer *L = &m->layers[l];
+        const size_t hd = L->is_swa ? m->head_dim_swa : hdg, nq = m->n_heads * hd, nkv = L->n_kv_heads * hd;
+        const size_t cap = L->is_swa ? m->sliding_window : global_cap;
+        float *kc = k_cache + kv_off, *vc = v_cache + kv_off;
+        kv_off += cap * nkv;
+        const size_t slot = pos % cap;
+        const size_t win = L->is_swa ? (seq < m->sliding_window ? seq : m->sliding_window) : seq;
+        orc_rmsnorm(xb, x, L->attn_norm, d, m->eps);
+        rc |= orc_quant_matvec_par(q, L->wq, L->wq_type, xb, nq, d, scratch, pool);
+        rc |= orc_quant_matvec_par(kk, L->wk, L->wk_type, xb, nkv, d, scratch, pool);
+        if (L->wv)
+            rc |= orc_quant_matvec_par(vv, L->wv, L->wv_type, xb, nkv, d, scratch, pool);
+        else
+            memcpy(vv, kk, nkv * 4);
+        for (size_t h = 0; h < m->n_heads; h++) orc_rmsnorm(q + h * hd, q + h * hd, L->q_norm, hd, m->eps);
+        for (size_t h = 0; h < L->n_kv_heads; h++) orc_rmsnorm(kk + h * hd, kk + h * hd, L->k_norm, hd, m->eps);
+        for (size_t h = 0; h < L->n_kv_heads; h++) orc_rmsnorm_raw(vv + h * hd, vv + h * hd, hd, m->eps);
+        if (L->is_swa) {
+            for (size_t h = 0; h < m->n_heads; h++) orc_rope(q + h * hd, hd, pos, m->rope_theta_swa, 1);
+            for (size_t h = 0; h < L->n_kv_heads; h++) orc_rope(kk + h * hd, hd, pos, m->rope_theta_swa, 1);
+        } else {  /* rope.zig:78-94, applyRopeFreqsNeox */
+            float *vecs[2] = {q, kk};
+            const size_t nh[2] = {m->n_heads, L->n_kv_heads};
+            for (int w = 0; w < 2; w++)
+                for (size_t h = 0; h < nh[w]; h++) {
+                    float *v = vecs[w] + h * hd;
+                    const size_t half = hd / 2;
+                    for (size_t i = 0; i < half; i++) {
+                        const float angle = (float)pos * freqs[i];
+                        const float c = cosf(angle), sn = sinf(angle);
+                        const float x0 = v[i], x1 = v[i + half];
+                        v[i] = x0 * c - x1 * sn;
+                        v[i + half] = x0 * sn + x1 * c;
+                    }
+                }
+        }
+        memcpy(kc + slot * nkv, kk, nkv * 4);
+        memcpy(vc + slot * nkv, vv, nkv * 4);
+        for (size_t h = 0; h < m->n_heads; h++) {  /* forward.zig:306-327 */
+            const size_t kvh = h / (m->n_heads / L->n_kv_heads);
+            for (size_t wi = 0; wi < win; wi++) {
+                const size_t s2 = ((seq - win) + wi) % cap;
+                memcpy(ks + wi * hd, kc + s2 * nkv + kvh * hd, hd * 4);
+                memcpy(vs + wi * hd, vc + s2 * nkv + kvh * hd, hd * 4);
+            }
+            orc_sdp_attn(att + h * hd, q + h * hd, ks, vs, win, hd, 1.0f);
+        }
+        rc |= orc_quant_matvec_par(attn_buf, L->wo, L->wo_type, att, d, nq, scratch, pool);
+        orc_rmsnorm(attn_buf, attn_buf, L->post_attention_norm, d, m->eps);
+        for (size_t i = 0; i < d; i++) x[i] += attn_buf[i];
+        /* dense GeGLU FFN (:390-396) */
+        orc_rmsnorm(xb, x, L->ffn_norm, d, m->eps);
+        rc |= orc_quant_matvec_par(g, L->w_gate, L->gate_type, xb, m->d_ffn, d, scratch, pool);
+        rc |= orc_quant_matvec_par(u, L->w_up, L->up_type, xb, m->d_ffn, d, scratch, pool);
+        for (size_t i = 0; i < m->d_ffn; i++) g[i] = orc_gelu(g[i]) * u[i];
+        rc |= orc_quant_matvec_par(ffn, L->w_down, L->down_type, g, d, m->d_ffn, scratch, pool);
+        orc_rmsnorm(ffn, ffn, L->post_ffw_norm_1, d, m->eps);
+        /* MoE (:401-494): math.zig:51-82 then routerTopKSoftmax and the expert loop */
+        {
+            float ss = 0.0f;
+            for (size_t i = 0; i < d; i++) ss += x[i] * x[i];
+            const float rms_inv = 1.0f / sqrtf(ss / (float)d + m->eps);
+            const float raw_base = rms_inv * (1.0f / sqrtf((float)d));
+            for (size_t i = 0; i < d; i++) {
+                moe_in[i] = x[i] * rms_inv * L->pre_ffw_norm_2[i];
+                router_in[i] = x[i] * raw_base * L->router_scale[i];
+            }
+        }
+        orc_router_topk_softmax(scores, top_idx, m->k, L->router_w, m->n_experts, d, router_in, pool);
+        memset(moe, 0, d * 4);
+        const size_t gu_rb = orc_row_bytes(L->gu_type, d), dn_rb = orc_row_bytes(L->dn_type, m->d_expert);
+        for (size_t i = 0; i < m->k; i++) {
+            const uint32_t e = top_idx[i];
+            const uint8_t *gd = L->gate_up_exps + (size_t)e * 2 * m->d_expert * gu_rb;
+            rc |= orc_quant_matvec_par(eg, gd, L->gu_type, moe_in, m->d_expert, d, scratch, pool);
+            rc |= orc_quant_matvec_par(eu, gd + m->d_expert * gu_rb, L->gu_type, moe_in, m->d_expert, d, scratch, pool);
+            for (size_t r = 0; r < m->d_expert; r++) eg[r] = orc_gelu(eg[r]) * eu[r];
+            rc |= orc_quant_matvec_par(ed, L->down_exps + (size_t)e * d * dn_rb, L->dn_type, eg, d, m->d_expert,
+                                       scratch, pool);
+            const float es = L->down_exps_scale[e] * scores[e];
+            for (size_t r = 0; r < d; r++) moe[r] += es * ed[r];
+        }
+        orc_rmsnorm(moe, moe, L->post_ffw_norm_2, d, m->eps);
+        for (size_t i = 0; i < d; i++) ffn[i] += moe[i];
+        orc_rmsnorm(ffn, ffn, L->post_ffw_norm, d, m->eps);
+        for (size_t i = 0; i < d; i++) x[i] += ffn[i];
+        if (L->layer_output_scale != 1.0f)
+            for (size_t i = 0; i < d; i++) x[i] *= L->layer_output_scale;
+    }
+    if (rc == 0) {
+        orc_rmsnorm(xb, x, m->out_norm, d, m->eps);
+        rc |= orc_quant_matvec_par(logits, m->lm_head, m->lm_type, xb, m->vocab, d, scratch, pool);
+        if (m->logit_softcap != 0.0f)
+            for (size_t i = 0; i < m->vocab; i++) logits[i] = tanhf(logits[i] / m->logit_softcap) * m->logit_softcap;
+    }
+    free(scratch); free(x); free(xb); free(attn_buf); free(ffn); free(moe); free(moe_in); free(router_in);
+    free(scores); free(q); free(kk); free(vv); free(att); free(ks); free(vs); free(g); free(u); free(eg); free(eu);
+    free(ed); free(freqs);
+    return rc ? -1 : 0;
+}

@@ -170,6 +170,48 @@ typedef struct orc_model {
 int orc_model_step(const orc_model *m, float *k_cache, float *v_cache, size_t kv_cap, uint32_t token,
                    size_t pos, float *logits, orc_pool *pool);
 
+/*
+ * One token of the Gemma 4 decoder: forwardOne's CPU path
+ * (src/model/gemma4/forward.zig:37-567).  Per layer: attention with per-head
+ * Q/K norms, raw V norm and NeoX RoPE (sliding-window layers: theta_swa and
+ * a ring of `sliding_window` positions; global layers: the rope_freqs table,
+ * or 1/1e6^(2i/hd) when absent, loader.zig:225-233), scale 1; post-attention
+ * norm + residual; dense GeGLU FFN + post_ffw_norm_1; MoE (fused gate_up,
+ * GELU, router on the raw-scaled norm, weights down_exps_scale[e] * p_e) +
+ * post_ffw_norm_2; post_ffw_norm of their sum + residual; layer_output_scale.
+ * Then the final norm, lm_head and the tanh soft-cap.
+ * KV caches: layer l at offset sum_{j<l} cap_j * nkv_j floats, cap_l =
+ * sliding_window for SWA layers, global_cap otherwise.
+ */
+typedef struct orc_gemma_layer {
+    int is_swa;
+    size_t n_kv_heads;
+    const float *attn_norm, *post_attention_norm, *q_norm, *k_norm, *ffn_norm;
+    const float *pre_ffw_norm_2, *post_ffw_norm_1, *post_ffw_norm_2, *post_ffw_norm;
+    float layer_output_scale;
+    const uint8_t *wq, *wk, *wv, *wo;   /* wv NULL: V = K (forward.zig:250) */
+    uint32_t wq_type, wk_type, wv_type, wo_type;
+    const uint8_t *w_gate, *w_up, *w_down;
+    uint32_t gate_type, up_type, down_type;
+    const float *router_w, *router_scale, *down_exps_scale;
+    const uint8_t *gate_up_exps, *down_exps;
+    uint32_t gu_type, dn_type;
+} orc_gemma_layer;
+
+typedef struct orc_gemma {
+    size_t n_layers, d_model, n_heads, head_dim_swa, head_dim_global, d_ffn, d_expert, n_experts, k;
+    size_t vocab, sliding_window;
+    float eps, rope_theta_swa, logit_softcap;
+    const float *rope_freqs;            /* [head_dim_global / 2] or NULL */
+    const uint8_t *token_emb; uint32_t emb_type;
+    const float *out_norm;
+    const uint8_t *lm_head; uint32_t lm_type;
+    const orc_gemma_layer *layers;
+} orc_gemma;
+
+int orc_gemma_step(const orc_gemma *m, float *k_cache, float *v_cache, size_t global_cap, uint32_t token,
+                   size_t pos, float *logits, orc_pool *pool);
+
 #ifdef __cplusplus
 }
 #endif

@@ -61,6 +61,7 @@ def lib() -> ctypes.CDLL:
         "orc_rope": (None, [P, SZ, SZ, F, I]),
         "orc_sdp_attn": (None, [P, P, P, P, SZ, SZ, F]),
         "orc_model_step": (I, [P, P, P, SZ, U32, SZ, P, P]),
+        "orc_gemma_step": (I, [P, P, P, SZ, U32, SZ, P, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -238,6 +239,89 @@ class OracleDecoder:
 
     def generate(self, prompt, n_gen: int):
         """(generated ids, logits of every step) -- the reference generate loop."""
+        toks = list(prompt)
+        all_logits = []
+        for pos in range(len(prompt) + n_gen - 1):
+            lg = self.step(toks[pos], pos)
+            all_logits.append(lg)
+            if pos + 1 >= len(prompt):
+                toks.append(greedy(lg))
+        return toks[len(prompt):], all_logits
+
+
+# ── Gemma 4 decoder (orc_gemma_step) ─────────────────────────────────────────
+
+class OrcGemmaLayer(ctypes.Structure):
+    P, U = ctypes.c_void_p, ctypes.c_uint32
+    _fields_ = [("is_swa", ctypes.c_int), ("n_kv_heads", ctypes.c_size_t),
+                ("attn_norm", P), ("post_attention_norm", P), ("q_norm", P), ("k_norm", P), ("ffn_norm", P),
+                ("pre_ffw_norm_2", P), ("post_ffw_norm_1", P), ("post_ffw_norm_2", P), ("post_ffw_norm", P),
+                ("layer_output_scale", ctypes.c_float),
+                ("wq", P), ("wk", P), ("wv", P), ("wo", P), ("wq_type", U), ("wk_type", U), ("wv_type", U),
+                ("wo_type", U), ("w_gate", P), ("w_up", P), ("w_down", P), ("gate_type", U), ("up_type", U),
+                ("down_type", U), ("router_w", P), ("router_scale", P), ("down_exps_scale", P),
+                ("gate_up_exps", P), ("down_exps", P), ("gu_type", U), ("dn_type", U)]
+
+
+class OrcGemma(ctypes.Structure):
+    SZ = ctypes.c_size_t
+    _fields_ = [("n_layers", SZ), ("d_model", SZ), ("n_heads", SZ), ("head_dim_swa", SZ), ("head_dim_global", SZ),
+                ("d_ffn", SZ), ("d_expert", SZ), ("n_experts", SZ), ("k", SZ), ("vocab", SZ),
+                ("sliding_window", SZ), ("eps", ctypes.c_float), ("rope_theta_swa", ctypes.c_float),
+                ("logit_softcap", ctypes.c_float), ("rope_freqs", ctypes.c_void_p), ("token_emb", ctypes.c_void_p),
+                ("emb_type", ctypes.c_uint32), ("out_norm", ctypes.c_void_p), ("lm_head", ctypes.c_void_p),
+                ("lm_type", ctypes.c_uint32), ("layers", ctypes.POINTER(OrcGemmaLayer))]
+
+
+class OracleGemma:
+    """orc_gemma_step over a synth.GemmaModel with its own f32 KV caches."""
+
+    def __init__(self, m, global_cap: int, pool: Pool | None = None):
+        self.m, self.cap, self.pool = m, global_cap, pool
+        self._keep = []
+
+        def p(a):
+            if a is None:
+                return None
+            a = np.ascontiguousarray(a)
+            self._keep.append(a)
+            return a.ctypes.data
+
+        self._layers = (OrcGemmaLayer * m.n_layers)()
+        total = 0
+        for i, L in enumerate(m.layers):
+            o = OrcGemmaLayer()
+            o.is_swa, o.n_kv_heads = int(L.is_swa), L.n_kv_heads
+            for f in ("attn_norm", "post_attention_norm", "q_norm", "k_norm", "ffn_norm", "pre_ffw_norm_2",
+                      "post_ffw_norm_1", "post_ffw_norm_2", "post_ffw_norm", "router_scale", "down_exps_scale"):
+                setattr(o, f, p(getattr(L, f)))
+            o.layer_output_scale = float(L.layer_output_scale)
+            o.wq, o.wk, o.wv, o.wo = p(L.wq), p(L.wk), p(L.wv), p(L.wo)
+            t = L.types
+            o.wq_type, o.wk_type, o.wv_type, o.wo_type = t["wq"], t["wk"], t.get("wv", 0), t["wo"]
+            o.w_gate, o.w_up, o.w_down = p(L.w_gate), p(L.w_up), p(L.w_down)
+            o.gate_type, o.up_type, o.down_type = t["gate"], t["up"], t["down"]
+            o.router_w = p(f32(L.router_w))
+            o.gate_up_exps, o.down_exps = p(L.gate_up_exps), p(L.down_exps)
+            o.gu_type, o.dn_type = t["gate_up_exps"], t["down_exps"]
+            self._layers[i] = o
+            cap = m.sliding_window if L.is_swa else global_cap
+            total += cap * L.n_kv_heads * L.head_dim
+        hd = m.layers[0].head_dim
+        self.model = OrcGemma(m.n_layers, m.d_model, m.n_heads, hd, hd, m.d_ffn, m.d_expert, m.n_experts, m.k,
+                              m.vocab, m.sliding_window, m.eps, m.rope_theta_swa, m.logit_softcap, None,
+                              p(m.token_emb), m.emb_type, p(m.out_norm), p(m.lm_head), m.lm_type, self._layers)
+        self.kc = np.zeros(total, np.float32)
+        self.vc = np.zeros(total, np.float32)
+
+    def step(self, token: int, pos: int) -> np.ndarray:
+        logits = np.empty(self.m.vocab, np.float32)
+        rc = lib().orc_gemma_step(ctypes.byref(self.model), _p(self.kc), _p(self.vc), self.cap, token, pos,
+                                  _p(logits), self.pool.ptr if self.pool else None)
+        assert rc == 0
+        return logits
+
+    def generate(self, prompt, n_gen: int):
         toks = list(prompt)
         all_logits = []
         for pos in range(len(prompt) + n_gen - 1):

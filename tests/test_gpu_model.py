@@ -273,3 +273,43 @@ def test_gguf_loaded_model_matches_oracle(ctx, oracle, pool, tmp_path, moe):
         assert (lm.n_layers, lm.d_model, lm.vocab, lm.n_experts) == (2, 256, 3000, 8 if moe else 0)
         assert lm.generate(prompt, n_gen) == ref_toks
         assert lm.generate(prompt, n_gen) == ref_toks  # graph replay
+
+
+def _compare_gemma(ctx, oracle, pool, m, prompt, n_gen, tol=LOGIT_TOL):
+    _, decoder = _mods()
+    spec = decoder.upload_gemma(ctx, m, kv_cap=64)
+    dec = decoder.Decoder(ctx, spec)
+    ref_toks, ref_logits = oracle.OracleGemma(m, 64, pool).generate(prompt, n_gen)
+    dec.start(prompt)
+    for i, rl in enumerate(ref_logits):
+        dec.step()
+        got = ctx.copy_to_host(dec.logits_ptr(), m.vocab * 4)
+        err = rel_l2(got, rl)
+        assert err < tol, (i, err)
+        if i + 1 >= len(prompt):
+            top = np.sort(rl)[-2:]
+            assert top[1] - top[0] > 10 * err * np.linalg.norm(rl) / np.sqrt(rl.size), (i, top)
+    assert dec.tokens(len(prompt) + n_gen)[len(prompt):] == ref_toks
+    assert dec.generate(prompt, n_gen) == ref_toks  # graph replay
+    dec.close()
+
+
+def test_gemma_small_vs_oracle(ctx, oracle, pool):
+    """A 6-layer Gemma-4-like decoder (5 sliding-window layers with a 4-position
+    ring, 1 global layer, dense + MoE GeGLU FFNs, mixed Q4_K/Q6_K/Q8_0,
+    per-layer output scales, soft-capped logits) over 15 positions."""
+    synth, _ = _mods()
+    m = synth.GemmaModel(np.random.default_rng(41), n_layers=6, d_model=256, n_heads=4, n_kv_heads=2, head_dim=64,
+                         d_ffn=512, n_experts=8, k=2, d_expert=256, vocab=2000, sliding_window=4, norms_random=True,
+                         lm_type=8)
+    _compare_gemma(ctx, oracle, pool, m, [3, 1, 4, 1, 5, 9, 2], 8)
+
+
+def test_gemma_config3_shape_vs_oracle(ctx, oracle, pool):
+    """Config 3's layer shape (d 2816, 16/8 heads of 256, GeGLU experts of 704
+    with Q8_0 down, dense GeGLU 2112) with 6 layers (5 SWA of window 8, 1
+    global) and a 4096-token vocabulary."""
+    synth, _ = _mods()
+    m = synth.GemmaModel(np.random.default_rng(42), n_layers=6, vocab=4096, sliding_window=8, norms_random=True,
+                         lm_type=8)
+    _compare_gemma(ctx, oracle, pool, m, [7, 70, 700, 4000, 1, 2, 3, 4, 5, 6], 6)
