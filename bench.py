@@ -454,7 +454,8 @@ def main() -> None:
         model_decode = {"config2": measure_model_decode(args, pkg, ctx, torch, stream, layers, rank, world, dist,
                                                         "config2"),
                         "config0": measure_model_decode(args, pkg, ctx, torch, stream, layers, rank, world, dist,
-                                                        "config0")}
+                                                        "config0"),
+                        "config3": measure_gemma_decode(args, pkg, ctx, torch, stream, rank, world, dist)}
 
     ep_prefill = None
     if args.ep_tokens > 0:
@@ -679,6 +680,189 @@ def measure_model_decode(args, pkg, ctx, torch, stream, moe_layers, rank, world,
     if rank == 0 and world == 1 and args.cpu_budget > 0:
         out["cpu_baseline"] = cpu_model_rate(name, min(args.cpu_budget, 10.0))
     return out
+
+
+GEMMA = dict(n_layers=30, d=2816, n_heads=16, n_kv=8, hd=256, d_ffn=2112, E=128, k=8, F=704, vocab=262144,
+             window=1024, period=6)
+
+
+def gemma_types(seed: int) -> list[dict]:
+    """The seeded per-tensor type mix of config 3 (60% Q4_K, 25% Q6_K, 15%
+    Q8_0; Q8_0 where the columns are not a multiple of 256), per layer."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    g = GEMMA
+
+    def pick(cols):
+        if cols % 256:
+            return 8
+        u = rng.uniform()
+        return 12 if u < 0.60 else 14 if u < 0.85 else 8
+
+    out = []
+    for _ in range(g["n_layers"]):
+        t = {"wq": pick(g["d"]), "wk": pick(g["d"]), "wv": pick(g["d"]), "wo": pick(g["n_heads"] * g["hd"]),
+             "gate": pick(g["d"]), "down": pick(g["d_ffn"]), "gate_up_exps": pick(g["d"]), "down_exps": pick(g["F"])}
+        t["up"] = t["gate"]
+        out.append(t)
+    return out
+
+
+def gemma_bytes_per_token(types: list[dict], ctx_len: float) -> float:
+    """Algorithmic bytes of one config-3 step: every weight read (attention,
+    dense FFN, router, the 8 selected experts, norms), the lm_head, the
+    embedding row and the KV read (SWA layers see at most the window)."""
+    g = GEMMA
+    d, nq, nkv = g["d"], g["n_heads"] * g["hd"], g["n_kv"] * g["hd"]
+    rb = lambda t, c: (c // 32) * 34 if t == 8 else (c // 256) * (144 if t == 12 else 210)  # noqa: E731
+    total = 0.0
+    for i, t in enumerate(types):
+        swa = (i + 1) % g["period"] != 0
+        total += nq * rb(t["wq"], d) + nkv * rb(t["wk"], d) + nkv * rb(t["wv"], d) + d * rb(t["wo"], nq)
+        total += 2 * g["d_ffn"] * rb(t["gate"], d) + d * rb(t["down"], g["d_ffn"])
+        total += g["E"] * d * 4 + g["k"] * (2 * g["F"] * rb(t["gate_up_exps"], d) + d * rb(t["down_exps"], g["F"]))
+        win = min(ctx_len, g["window"]) if swa else ctx_len
+        total += 2 * win * nkv * 4 + 10 * d * 4
+    return total + g["vocab"] * (d // 256) * 210 + rb(12, d)
+
+
+def measure_gemma_decode(args, pkg, ctx, torch, stream, rank, world, dist) -> dict:
+    """Config 3: greedy decode of the Gemma-4-26B-A4B-like model through the
+    C++ host loop (Gemma 4 family): a 64-token prompt, then 80 tokens (the
+    config's workload; args.model_tokens caps it), weights generated on the
+    device with the seeded per-tensor type mix, Q6_K lm_head."""
+    decoder = importlib.import_module("llmtoy-zig_b200.decoder")
+    g = GEMMA
+    d, nq, nkv, E, F = g["d"], g["n_heads"] * g["hd"], g["n_kv"] * g["hd"], g["E"], g["F"]
+    n_prompt, n_gen = 64, min(80, args.model_tokens)
+    types = gemma_types(0x11A70003)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0x11A70003 + 1000 * rank)
+    keep, tensors = [], []
+    dev_gen = {8: q8_0_bytes_device, 12: q4k_bytes_device, 14: q6k_bytes_device}
+
+    def up(t, r, c, e=0):
+        tt = ctx.upload_device(dev_gen[t](torch, gen, r * max(1, e), c), t, r, c, e)
+        tensors.append(tt)
+        return tt
+
+    def vec(n, v=1.0):
+        keep.append(torch.full((n,), v, device="cuda"))
+        return keep[-1]
+
+    specs = []
+    for i, t in enumerate(types):
+        rw = torch.randn(E, d, device="cuda", generator=gen) * 0.02
+        router = ctx.upload_device(rw.view(torch.uint8).view(-1), pkg.F32, E, d)
+        tensors.append(router)
+        del rw
+        specs.append(decoder.LayerSpec(
+            attn_norm=vec(d), ffn_norm=vec(d), wo=up(t["wo"], d, nq), wq=up(t["wq"], nq, d), wk=up(t["wk"], nkv, d),
+            wv=up(t["wv"], nkv, d), q_norm=vec(g["hd"]), k_norm=vec(g["hd"]), ffn_gate=up(t["gate"], g["d_ffn"], d),
+            ffn_up=up(t["up"], g["d_ffn"], d), ffn_down=up(t["down"], d, g["d_ffn"]), router=router,
+            exp_gate=up(t["gate_up_exps"], 2 * F, d, E), exp_down=up(t["down_exps"], d, F, E),
+            post_attention_norm=vec(d), pre_ffw_norm_2=vec(d), post_ffw_norm_1=vec(d), post_ffw_norm_2=vec(d),
+            post_ffw_norm=vec(d), router_scale=vec(d), down_exps_scale=vec(E), layer_output_scale=1.0,
+            is_swa=(i + 1) % g["period"] != 0, n_kv_heads=g["n_kv"], head_dim=g["hd"]))
+    emb = up(12, g["vocab"], d)
+    lmh = up(14, g["vocab"], d)
+    spec = decoder.ModelSpec(d_model=d, n_heads=g["n_heads"], n_kv_heads=g["n_kv"], head_dim=g["hd"],
+                             vocab=g["vocab"], token_emb=emb, lm_head=lmh, out_norm=vec(d), layers=specs, n_used=g["k"],
+                             rope_neox=True, act=1, eps=1e-6, rope_theta=1e6, kv_cap=4096, family=decoder.GEMMA4,
+                             rope_theta_swa=1e4, logit_softcap=30.0, sliding_window=g["window"])
+    torch.cuda.synchronize()
+    prompt = np.random.Generator(np.random.PCG64(0x11A70003)).integers(0, g["vocab"], n_prompt).tolist()
+    steps = n_prompt + n_gen - 1
+    dec = decoder.Decoder(ctx, spec)
+    first = dec.generate(prompt, n_gen)
+    dec.start(prompt)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ev0.record(stream)
+        dec.replay(steps)
+        ev1.record(stream)
+        stream.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    deterministic = dec.tokens(n_prompt + n_gen)[n_prompt:] == first
+    if dist is not None:
+        tt = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    ms_step = ms / steps
+    t0 = time.perf_counter()
+    dec.generate(prompt, n_gen)
+    e2e_s = time.perf_counter() - t0
+    dec.start(prompt)
+    ctx.profile(True)
+    ctx.profile_reset()
+    dec.step()
+    ctx.sync()
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    ctx.profile_reset()
+    dec.close()
+    for tt in tensors:
+        tt.free()
+    peak, kind = measured_peaks()
+    bpt = gemma_bytes_per_token(types, n_prompt + (n_gen - 1) / 2.0)
+    achieved = bpt / (ms_step / 1e3) / 1e9
+    mix = {}
+    for t in types:
+        for v in t.values():
+            mix[{8: "q8_0", 12: "q4_k", 14: "q6_k"}[v]] = mix.get({8: "q8_0", 12: "q4_k", 14: "q6_k"}[v], 0) + 1
+    out = {
+        "metric": "greedy decode tok/s (config3: Gemma-4-26B-A4B-like, 30 layers, 5 SWA : 1 global)",
+        "value": world / (ms_step / 1e3), "unit": "tok/s", "ms_per_token": ms_step, "steps": steps,
+        "prompt_tokens": n_prompt, "generated_tokens": n_gen, "scaling": "weak", "deterministic_stream": deterministic,
+        "tensor_type_mix": mix,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": kind, "algorithmic_bytes_per_token": bpt},
+        "e2e": {"value": world * n_gen / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * n_prompt / n_gen,
+                "d2h_bytes_per_step": 4.0 * (n_prompt + n_gen) / n_gen,
+                "path": "lth_generate: host prompt ids in, host token ids out (prompt steps included)"},
+        "kernels_per_token": {k: {"count": v["count"], "us": round(1e3 * v["total_ms"], 1)} for k, v in prof.items()},
+        "gpu_launches_per_token": int(sum(v["count"] for v in prof.values())),
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and args.cpu_budget > 0:
+        out["cpu_baseline"] = cpu_gemma_rate(min(args.cpu_budget, 10.0))
+    return out
+
+
+def cpu_gemma_rate(budget_s: float) -> dict:
+    """orc_gemma_step (all host threads) on the config-3 shape: 3 distinct host
+    layer weight sets cycled through the 30 layers, full vocabulary."""
+    sys.path.insert(0, str(REPO / "tests"))
+    oracle = importlib.import_module("oracle_lib")
+    synth = importlib.import_module("llmtoy-zig_b200.synth")
+    rng = np.random.Generator(np.random.PCG64(synth.config_seed(3)))
+    m = synth.GemmaModel(rng, n_layers=3)
+    L = GEMMA["n_layers"]
+    base = m.layers
+    m.layers = []
+    for i in range(L):  # per-index sliding-window pattern over the cycled weights
+        src = base[i % 3]
+        lay = object.__new__(type(src))
+        lay.__dict__.update(src.__dict__)
+        lay.is_swa = (i + 1) % GEMMA["period"] != 0
+        m.layers.append(lay)
+    m.n_layers = L
+    threads = os.cpu_count() or 1
+    pool = oracle.Pool(threads)
+    dec = oracle.OracleGemma(m, 64, pool)
+    dec.step(1, 0)
+    t0 = time.perf_counter()
+    n = 0
+    while n < 2 or time.perf_counter() - t0 < budget_s:
+        dec.step(1 + n, (n + 1) % 64)
+        n += 1
+    dt = time.perf_counter() - t0
+    pool.close()
+    return {"value": n / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{n} decode steps of the 30-layer model in {dt:.1f}s (3 distinct layer weight sets cycled; "
+                      f"C restatement of gemma4 forwardOne, zig absent)"}
 
 
 def cpu_model_rate(name: str, budget_s: float) -> dict:
