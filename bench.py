@@ -294,6 +294,7 @@ def main() -> None:
     ap.add_argument("--ep-layers", type=int, default=2)
     ap.add_argument("--model-tokens", type=int, default=128,
                     help="configs 2 and 0: greedy tokens after a 32-token prompt (0: skip)")
+    ap.add_argument("--models", default="config2,config0,config3", help="whole-model decode lines to run")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -451,11 +452,13 @@ def main() -> None:
 
     model_decode = None
     if args.model_tokens > 0:
-        model_decode = {"config2": measure_model_decode(args, pkg, ctx, torch, stream, layers, rank, world, dist,
-                                                        "config2"),
-                        "config0": measure_model_decode(args, pkg, ctx, torch, stream, layers, rank, world, dist,
-                                                        "config0"),
-                        "config3": measure_gemma_decode(args, pkg, ctx, torch, stream, rank, world, dist)}
+        model_decode = {}
+        for name in [m for m in args.models.split(",") if m]:
+            if name == "config3":
+                model_decode[name] = measure_gemma_decode(args, pkg, ctx, torch, stream, rank, world, dist)
+            else:
+                model_decode[name] = measure_model_decode(args, pkg, ctx, torch, stream, layers, rank, world, dist,
+                                                          name)
 
     ep_prefill = None
     if args.ep_tokens > 0:
