@@ -163,12 +163,160 @@ __global__ void __launch_bounds__(kRouterWarps * 32) k_router(RouterArgs a) {
     if (threadIdx.x == 0) a.counters[blockIdx.y] = 0;
 }
 
+// Token-major router for large batches: a CTA owns kRtTok tokens and computes
+// all E logits for them, 8 experts at a time with each warp's router row in
+// registers reused across the tokens, then ranks them itself.  Per token the
+// arithmetic is the expert-major kernel's (the same norm reduction order, the
+// same router_logit, ranking and weights), so the ids and weights are
+// identical; the router weights are read once per kRtTok tokens instead of
+// once per 4, and no logits go through global memory.
+constexpr int kRtWarps = 8;
+constexpr int kRtTok = 8;
+constexpr uint32_t kRtMinTokens = 32;  // smaller batches: the expert-major kernel (more CTAs)
+constexpr uint32_t kRtMaxCols = 4096;
+
+// Shared-memory layout (byte offsets, 16-byte aligned): x rows, norm
+// weights, logits, sort keys with an even row stride of at least E + 2 so
+// that every row starts 16-byte aligned (router_rank_keys loads key pairs).
+struct RtLayout {
+    size_t nw, lg, keys, total;
+    uint32_t kstride;
+};
+__host__ __device__ inline RtLayout rt_layout(uint32_t cols, uint32_t E) {
+    auto al = [](size_t v) { return (v + 15) & ~(size_t)15; };
+    RtLayout L;
+    L.kstride = (E + 3) & ~1u;
+    L.nw = al((size_t)kRtTok * cols * 4);
+    L.lg = al(L.nw + (size_t)cols * 4);
+    L.keys = al(L.lg + (size_t)kRtTok * E * 4);
+    L.total = L.keys + (size_t)kRtTok * L.kstride * 8;
+    return L;
+}
+
+__global__ void __launch_bounds__(kRtWarps * 32, 2) k_router_tok(RouterArgs a) {
+    extern __shared__ __align__(16) float rsm[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t cols = a.cols, E = a.E;
+    const uint32_t t0 = blockIdx.x * kRtTok;
+    const uint32_t nt = min((uint32_t)kRtTok, a.ntok - t0);
+    const RtLayout Lr = rt_layout(cols, E);
+    uint8_t *base = reinterpret_cast<uint8_t *>(rsm);
+    float *xs = rsm;                                           // [kRtTok][cols]
+    float *nwsm = reinterpret_cast<float *>(base + Lr.nw);     // [cols]
+    float *lg = reinterpret_cast<float *>(base + Lr.lg);       // [kRtTok][E]
+    uint64_t *keys = reinterpret_cast<uint64_t *>(base + Lr.keys);  // [kRtTok][Lr.kstride], 16-byte aligned rows
+    __shared__ float s_ss[kRtWarps];
+    __shared__ float s_rms[kRtTok];
+    __shared__ uint32_t s_sel[kRtTok][16];
+    __shared__ float s_mx[kRtTok], s_es[kRtTok];
+    if (a.norm_w)
+        for (uint32_t i = tid; i < cols; i += kRtWarps * 32) nwsm[i] = __ldg(a.norm_w + i);
+    pdl_launch_dependents();
+    pdl_wait();
+    {
+        const float *xt = a.x + (size_t)t0 * cols;
+        const uint32_t n = nt * cols;
+        if ((cols & 3) == 0 && (reinterpret_cast<uintptr_t>(xt) & 15) == 0) {
+#pragma unroll 8
+            for (uint32_t i = tid; i < n / 4; i += kRtWarps * 32)
+                reinterpret_cast<float4 *>(xs)[i] = reinterpret_cast<const float4 *>(xt)[i];
+        } else {
+            for (uint32_t i = tid; i < n; i += kRtWarps * 32) xs[i] = xt[i];
+        }
+    }
+    __syncthreads();
+    if (a.norm_w) {
+        // the expert-major kernel's order: per token, 128 threads stride the
+        // columns, then their 4 warp sums in order; two tokens at a time here
+        constexpr int G = kRtWarps * 32 / kRouterNormThreads;
+        for (uint32_t base = 0; base < nt; base += G) {
+            const uint32_t g = tid / kRouterNormThreads, tt = base + g, ti = tid % kRouterNormThreads;
+            float ss = 0.0f;
+            if (tt < nt)
+                for (uint32_t i = ti; i < cols; i += kRouterNormThreads) ss += xs[tt * cols + i] * xs[tt * cols + i];
+            ss = warp_sum(ss);
+            if (lane == 0) s_ss[warp] = ss;
+            __syncthreads();
+            if (ti == 0 && tt < nt) {
+                float sum = 0.0f;
+                for (int w = 0; w < kRouterNormThreads / 32; w++) sum += s_ss[g * (kRouterNormThreads / 32) + w];
+                s_rms[tt] = 1.0f / sqrtf(sum / (float)cols + a.eps);
+            }
+            __syncthreads();
+        }
+        for (uint32_t i = tid; i < nt * cols; i += kRtWarps * 32) {
+            const uint32_t tt = i / cols, cc = i - tt * cols;
+            xs[i] = xs[i] * s_rms[tt] * nwsm[cc];
+        }
+        __syncthreads();
+    }
+    if (a.xn)
+        for (uint32_t i = tid; i < nt * cols; i += kRtWarps * 32) a.xn[(size_t)t0 * cols + i] = xs[i];
+    if (a.xq) {
+        const uint32_t nblk = cols / 32;
+        for (uint32_t task = warp; task < nt * nblk; task += kRtWarps) {
+            const uint32_t tt = task / nblk, b = task - tt * nblk;
+            qact_store_block(a.xq + (size_t)(t0 + tt) * a.xq_pitch, (int)cols, (int)b, xs[tt * cols + 32 * b + lane],
+                             lane);
+        }
+    }
+    for (uint32_t e0 = 0; e0 < E; e0 += kRtWarps) {
+        const uint32_t e = e0 + warp;
+        if (e < E) {
+            float w0[kRouterChunk];
+            router_prefetch(a.W + (size_t)e * a.w_ld, cols, lane, true, w0);
+            for (uint32_t tt = 0; tt < nt; tt++) {
+                const float v = router_logit(a.W + (size_t)e * a.w_ld, xs + tt * cols, cols, lane, w0);
+                if (lane == 0) lg[tt * E + e] = v;
+            }
+        }
+    }
+    __syncthreads();
+    const uint32_t E2 = Lr.kstride;
+    for (uint32_t i = tid; i < nt * E; i += kRtWarps * 32) {
+        const uint32_t tt = i / E, ee = i - tt * E;
+        keys[tt * E2 + ee] = router_key(lg[i], ee);
+    }
+    if ((uint32_t)tid < nt) keys[tid * E2 + E] = 0;
+    __syncthreads();
+    {  // rank: one group of kRouterNormThreads threads per token at a time
+        constexpr int G = kRtWarps * 32 / kRouterNormThreads;
+        const uint32_t g = tid / kRouterNormThreads, ti = tid % kRouterNormThreads;
+        for (uint32_t base = 0; base < nt; base += G)
+            if (base + g < nt)
+                router_rank_keys(keys + (base + g) * E2, E, a.k, s_sel[base + g], (int)ti, kRouterNormThreads);
+    }
+    for (uint32_t tt = warp; tt < nt; tt += kRtWarps) {
+        float mx, es;
+        router_softmax_stats(lg + tt * E, E, lane, mx, es);
+        if (lane == 0) {
+            s_mx[tt] = mx;
+            s_es[tt] = es;
+        }
+    }
+    __syncthreads();
+    if ((uint32_t)tid < nt) {
+        const uint32_t tt = tid;
+        float w[16];
+        router_weights(lg + tt * E, s_sel[tt], a.k, s_mx[tt], s_es[tt], a.norm_topk, a.escale, w);
+        for (uint32_t i = 0; i < a.k; i++) {
+            a.ids[(size_t)(t0 + tt) * a.k + i] = s_sel[tt][i];
+            a.wout[(size_t)(t0 + tt) * a.k + i] = w[i];
+        }
+    }
+}
+
 cudaError_t launch_router(const LaunchCfg &c, const float *w, uint32_t E, uint32_t cols, uint32_t w_ld,
                           const float *x, const float *norm_w, float eps, uint32_t ntok, uint32_t k, int norm_topk,
                           const float *escale, uint32_t *ids, float *wout, float *logits, uint32_t *counters,
                           uint8_t *xq, uint64_t xq_pitch, float *xn) {
     RouterArgs a{w,      E,   cols,      w_ld,   x,    norm_w, eps,      ntok, k,
                  norm_topk, escale, ids, wout, logits, counters, xq, xq_pitch, xn};
+    if (ntok >= kRtMinTokens && cols <= kRtMaxCols) {
+        const size_t smem = rt_layout(cols, E).total;
+        return launch_k(c, "router_topk", k_router_tok, dim3((ntok + kRtTok - 1) / kRtTok), dim3(kRtWarps * 32), smem,
+                        a);
+    }
     const dim3 grid((E + kRouterWarps - 1) / kRouterWarps, router_token_groups(ntok));
     const size_t smem_x = (size_t)(kRouterTok + (norm_w ? 1 : 0)) * cols * 4;
     const size_t smem_topk = (size_t)kRouterTok * (kRouterMaxE * 4 + (kRouterMaxE + 2) * 8);

@@ -454,3 +454,40 @@ def test_error_paths(ctx, pkg):
     t.free()
     r.free()
     ctx.sync()
+
+
+@pytest.mark.parametrize("norm", [False, True])
+def test_router_token_major_matches_expert_major(ctx, oracle, norm):
+    """Batches of 32+ tokens take the token-major router kernel; its ids,
+    weights and normalised/quantised rows equal the expert-major kernel's
+    (31 tokens) bit for bit, and the ids equal the oracle's."""
+    import importlib
+    synth = importlib.import_module("llmtoy-zig_b200.synth")
+    rng = np.random.Generator(np.random.PCG64(2024))
+    E, d, k = 128, 2048, 8
+    w = synth.router_weights(rng, E, d)
+    x = synth.hidden(rng, 40, d)
+    nw = rng.uniform(0.5, 1.5, d).astype(np.float32)
+    rt = ctx.upload(w, 0, E, d)
+    outs = []
+    for T in (31, 40):
+        ids, ww = empty(T * k, "int32"), empty(T * k)
+        if norm:
+            L = synth.MoeLayer(np.random.default_rng(5), d, E, 256, 12, 12)
+            g = ctx.upload(L.gate, 12, 256, d, n_experts=E)
+            u = ctx.upload(L.up, 12, 256, d, n_experts=E)
+            dn = ctx.upload(L.down, 12, d, 256, n_experts=E)
+            out = empty(T * d)
+            ctx.moe_block(rt, g, u, dn, 0, True, None, dev(nw), 1e-6, dev(x[:T]), T, k, out, ids, ww)
+            for t_ in (g, u, dn):
+                t_.free()
+        else:
+            ctx.moe_route(rt, dev(x[:T]), T, k, True, None, ids, ww)
+        outs.append((host(ids).reshape(T, k)[:31], host(ww).reshape(T, k)[:31]))
+    np.testing.assert_array_equal(outs[0][0], outs[1][0])
+    np.testing.assert_array_equal(bits(outs[0][1]), bits(outs[1][1]))
+    if not norm:
+        for t in range(31):
+            rid, _ = oracle.router_topk_softmax(w, x[t], k)
+            assert np.array_equal(outs[1][0][t].astype(np.uint32), rid)
+    rt.free()
