@@ -37,7 +37,7 @@
 
 namespace lt {
 
-constexpr int kGN = 32;     // positions per tile (MMA N)
+constexpr int kGN = 32;     // positions per tile of the small-batch shape (MMA N = 64)
 constexpr int kGM = 128;    // weight rows per tile (MMA M)
 constexpr int kGMaxSb = 8;  // superblocks per row (K <= 2048)
 
@@ -49,28 +49,40 @@ constexpr int kGMaxSb = 8;  // superblocks per row (K <= 2048)
 // (tile, 128-row block) work items of the launch with stride gridDim.x, and
 // every ring keeps running across items.
 //
-// The activation operand stacks the two planes: rows 0-31 of B are the hi
-// plane of the 32 positions, rows 32-63 the lo plane, so one N = 64 MMA per
-// K step covers both and the accumulator's column halves are added.
+// The activation operand stacks the two planes: rows 0-(NP-1) of B are the hi
+// plane of the NP positions, rows NP-(2NP-1) the lo plane, so one N = 2 NP MMA
+// per K step covers both and the accumulator's column halves are added.  NP
+// is 32 for small per-expert batches and 64 for large ones: one
+// tcgen05.mma takes about as long at N = 128 as at N = 64, so the wider tile
+// halves the MMA issue and the dequantisation per FLOP.
 constexpr int kGMath = 256;
 constexpr int kGWarpRaw = 8, kGWarpB = 9, kGWarpMma = 10;
 constexpr int kGThreadsV2 = 11 * 32;
-constexpr int kGNN = 2 * kGN;  // MMA N: hi and lo planes
-constexpr int kGRawSlots = 3;  // raw superblocks in flight
 constexpr int kGAStages = 2;   // dequantised A stages (K = 128 each)
-constexpr int kGBStages = 3;   // activation stages
-constexpr uint32_t kGTmemCols = 256;  // 2 x 64 superblock accumulators + 64 min-term columns
+constexpr uint32_t kRawStage = kGM * 144;  // one superblock of 128 rows
 
-// Dynamic shared memory, offsets from a 1024-byte aligned base.
-constexpr uint32_t kRawStage = kGM * 144;                          // one superblock of 128 rows
-constexpr uint32_t kOffA = 0;                                       // kGAStages x 2 atoms x 16 KB
-constexpr uint32_t kOffB = kOffA + kGAStages * 32768;               // kGBStages x 2 atoms x 8 KB (64 rows)
-constexpr uint32_t kOffAm = kOffB + kGBStages * 16384;              // min-term A: 2 planes x 16 KB
-constexpr uint32_t kOffBm = kOffAm + 32768;                         // min-term B: one 64-row atom
-constexpr uint32_t kOffRaw = kOffBm + 8192;                         // kGRawSlots x raw superblock
-constexpr uint32_t kOffHdr = kOffRaw + kGRawSlots * kRawStage;      // d [8][128] f32
-constexpr uint32_t kOffMisc = kOffHdr + kGMaxSb * kGM * 4;          // barriers, TMEM address, scales
-constexpr uint32_t kGSmem = kOffMisc + 512 + 1024;                  // + alignment slack
+// Per tile width NP: MMA N, rings, TMEM columns (2 x 2NP superblock
+// accumulators + 2NP min-term columns) and the shared-memory map (offsets
+// from a 1024-byte aligned base).
+template <int NP>
+struct GemmGeo {
+    static constexpr int NNP = 2 * NP;                      // MMA N: hi and lo planes
+    static constexpr int kBStages = NP == 32 ? 3 : 2;       // activation stages
+    static constexpr int kRawSlots = NP == 32 ? 3 : 2;      // raw superblocks in flight
+    static constexpr uint32_t kBAtom = NNP * 128;           // NNP rows x 64 K (f16)
+    static constexpr uint32_t kBStage = 2 * kBAtom;         // K = 128
+    static constexpr uint32_t kTmemCols = NP == 32 ? 256 : 512;
+    static constexpr uint32_t kOffA = 0;                                  // kGAStages x 2 atoms x 16 KB
+    static constexpr uint32_t kOffB = kOffA + kGAStages * 32768;
+    static constexpr uint32_t kOffAm = kOffB + kBStages * kBStage;        // min-term A: 2 planes x 16 KB
+    static constexpr uint32_t kOffBm = kOffAm + 32768;                    // min-term B: one NNP-row atom
+    static constexpr uint32_t kOffRaw = kOffBm + kBAtom;
+    static constexpr uint32_t kOffHdr = kOffRaw + kRawSlots * kRawStage;  // d [8][128] f32
+    static constexpr uint32_t kOffMisc = kOffHdr + kGMaxSb * kGM * 4;     // barriers, TMEM address, scales
+    static constexpr uint32_t kSmem = kOffMisc + 1024 + 1024;             // + alignment slack
+};
+static_assert(GemmGeo<64>::kSmem <= 227 * 1024, "NP = 64 shared memory");
+static_assert(GemmGeo<32>::kSmem <= 227 * 1024, "NP = 32 shared memory");
 
 struct GemmArgs {
     // 2-D byte views [rows][pitch] of the weights for tiled TMA: one load
@@ -156,18 +168,24 @@ struct GemmItem {
     uint32_t e, pos0, nvalid, m0;
 };
 
+template <int NP>
 LT_DEVINL GemmItem gemm_item(const GemmArgs &a, uint32_t w) {
     const uint2 tile = a.tiles[w / a.mt];
     GemmItem it;
     it.m0 = w % a.mt;
     it.e = a.p.act_e[tile.x];
     it.pos0 = a.p.act_off[tile.x] + tile.y;
-    it.nvalid = min((uint32_t)kGN, a.p.act_cnt[tile.x] - tile.y);
+    it.nvalid = min((uint32_t)NP, a.p.act_cnt[tile.x] - tile.y);
     return it;
 }
 
-template <int MODE>
+template <int MODE, int NP>
 __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_constant__ GemmArgs a) {
+    using Geo = GemmGeo<NP>;
+    constexpr int NNP = Geo::NNP, kGBStages = Geo::kBStages, kGRawSlots = Geo::kRawSlots;
+    constexpr uint32_t kOffA = Geo::kOffA, kOffB = Geo::kOffB, kOffAm = Geo::kOffAm, kOffBm = Geo::kOffBm;
+    constexpr uint32_t kOffRaw = Geo::kOffRaw, kOffHdr = Geo::kOffHdr, kOffMisc = Geo::kOffMisc;
+    constexpr int PH = NP / 2;  // positions per epilogue thread
     extern __shared__ uint8_t g_smem_raw[];
     uint8_t *sm = g_smem_raw + ((1024u - (smem_u32(g_smem_raw) & 1023u)) & 1023u);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -178,7 +196,7 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
     uint64_t *acc_full = bars + 16, *acc_empty = bars + 18;  // [2]
     uint64_t *min_full = bars + 20, *min_empty = bars + 21, *bm_full = bars + 22;
     uint32_t *s_taddr = reinterpret_cast<uint32_t *>(bars + 23);
-    float *s_inv = reinterpret_cast<float *>(s_taddr + 4);  // [2][32] by item parity
+    float *s_inv = reinterpret_cast<float *>(s_taddr + 4);  // [2][NP] by item parity
     float *hdr_d = reinterpret_cast<float *>(sm + kOffHdr);
 
     const uint32_t nsb = a.K / 256;
@@ -201,11 +219,11 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
         fence_barrier_init();
     }
     if (warp == 0) {
-        tmem_alloc(s_taddr, kGTmemCols);
+        tmem_alloc(s_taddr, Geo::kTmemCols);
         tmem_relinquish();
     }
     // min-term operands stay zero beyond K = 8*nsb
-    for (uint32_t i = tid; i < (40u * 1024) / 16; i += blockDim.x)
+    for (uint32_t i = tid; i < (32768u + Geo::kBAtom) / 16; i += blockDim.x)
         reinterpret_cast<uint4 *>(sm + kOffAm)[i] = make_uint4(0, 0, 0, 0);
     pdl_wait();
     tc_fence_before();
@@ -219,7 +237,7 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
         if (lane == 0) {
             uint32_t gsb = 0;
             for (uint32_t w = blockIdx.x; w < n_work; w += gridDim.x) {
-                const GemmItem it = gemm_item(a, w);
+                const GemmItem it = gemm_item<NP>(a, w);
                 uint32_t y0, y1;  // first weight row of tile rows 0-63 and 64-127
                 const CUtensorMap *m1 = &a.map_w;
                 if (MODE == 0) {
@@ -245,45 +263,59 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
             }
         }
     } else if (warp == kGWarpB) {
-        // ── activation stages (lane n gathers position n, zero past the item)
-        //    and, once per item, the min-term B rows and 2^e of the positions ──
+        // ── activation stages (lane n gathers positions n, n + 32, ...; zero
+        //    past the item) and, once per item, the min-term B rows and 2^e ──
+        constexpr int PPL = NP / 32;  // positions per lane
         uint32_t gs = 0, gi = 0;
         for (uint32_t w = blockIdx.x; w < n_work; w += gridDim.x, gi++) {
-            const GemmItem it = gemm_item(a, w);
-            uint32_t row = 0;
-            const bool valid = (uint32_t)lane < it.nvalid;
-            if (valid) row = MODE == 0 ? a.p.pos_pair[it.pos0 + lane] / a.k : it.pos0 + lane;
-            const __half *srch = a.xh + (size_t)row * a.K, *srcl = a.xl + (size_t)row * a.K;
+            const GemmItem it = gemm_item<NP>(a, w);
+            uint32_t row[PPL];
+            bool valid[PPL];
+#pragma unroll
+            for (int pp = 0; pp < PPL; pp++) {
+                const uint32_t n = lane + 32 * pp;
+                valid[pp] = n < it.nvalid;
+                row[pp] = !valid[pp] ? 0 : MODE == 0 ? a.p.pos_pair[it.pos0 + n] / a.k : it.pos0 + n;
+            }
             const uint32_t nks = 2 * nsb, ks_bm = nks > 2 ? 2 : nks - 1;
             for (uint32_t ks = 0; ks < nks; ks++, gs++) {
                 const uint32_t s = gs % kGBStages;
                 if (gs >= (uint32_t)kGBStages) gemm_wait(&b_empty[s], gs / kGBStages - 1, a.dev_err);
-                uint8_t *bs = sm + kOffB + s * 16384 + lane * 128;
 #pragma unroll
-                for (uint32_t cc = 0; cc < 16; cc++) {
-                    const uint32_t o = (cc >> 3) * 8192 + (((cc & 7) ^ (lane & 7)) << 4);
-                    cp_async16(bs + o, srch + ks * 128 + cc * 8, valid ? 16u : 0u);
-                    cp_async16(bs + 4096 + o, srcl + ks * 128 + cc * 8, valid ? 16u : 0u);
+                for (int pp = 0; pp < PPL; pp++) {
+                    const uint32_t n = lane + 32 * pp;
+                    const __half *srch = a.xh + (size_t)row[pp] * a.K, *srcl = a.xl + (size_t)row[pp] * a.K;
+                    uint8_t *bs = sm + kOffB + s * Geo::kBStage + n * 128;
+#pragma unroll
+                    for (uint32_t cc = 0; cc < 16; cc++) {
+                        const uint32_t o = (cc >> 3) * Geo::kBAtom + (((cc & 7) ^ (n & 7)) << 4);
+                        cp_async16(bs + o, srch + ks * 128 + cc * 8, valid[pp] ? 16u : 0u);
+                        cp_async16(bs + NP * 128 + o, srcl + ks * 128 + cc * 8, valid[pp] ? 16u : 0u);
+                    }
                 }
                 cp_async_arrive(&b_full[s]);
                 if (ks == ks_bm) {
                     // the previous item's min term has consumed the old B rows
                     if (gi >= 1) gemm_wait(min_full, gi - 1, a.dev_err);
-                    const float inv = valid ? a.xinv[row] : 0.0f;
-                    const float *xs = a.xsum + (size_t)row * (a.K / 32);
-                    for (uint32_t j = 0; j < 8 * nsb; j += 4) {
-                        float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                        if (valid) v4 = *reinterpret_cast<const float4 *>(xs + j);
-                        const float v[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
-                        for (int q = 0; q < 4; q++) {
-                            __half h, l;
-                            split_f16(v[q], h, l);
-                            *reinterpret_cast<__half *>(sm + kOffBm + sw128_offset(lane, j + q)) = h;
-                            *reinterpret_cast<__half *>(sm + kOffBm + sw128_offset(32 + lane, j + q)) = l;
+                    for (int pp = 0; pp < PPL; pp++) {
+                        const uint32_t n = lane + 32 * pp;
+                        const float inv = valid[pp] ? a.xinv[row[pp]] : 0.0f;
+                        const float *xs = a.xsum + (size_t)row[pp] * (a.K / 32);
+                        for (uint32_t j = 0; j < 8 * nsb; j += 4) {
+                            float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                            if (valid[pp]) v4 = *reinterpret_cast<const float4 *>(xs + j);
+                            const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+                            for (int q = 0; q < 4; q++) {
+                                __half h, l;
+                                split_f16(v[q], h, l);
+                                *reinterpret_cast<__half *>(sm + kOffBm + sw128_offset(n, j + q)) = h;
+                                *reinterpret_cast<__half *>(sm + kOffBm + sw128_offset(NP + n, j + q)) = l;
+                            }
                         }
+                        s_inv[(gi & 1) * NP + n] = inv;
                     }
-                    s_inv[(gi & 1) * kGN + lane] = inv;
                     fence_async_smem();
                     mbar_arrive(bm_full);
                 }
@@ -292,24 +324,24 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
     } else if (warp == kGWarpMma) {
         // ── MMA issue ──
         if (lane == 0) {
-            const uint32_t idesc = umma_idesc_f16_f32(kGM, kGNN);
+            const uint32_t idesc = umma_idesc_f16_f32(kGM, NNP);
             uint32_t gs = 0, gsb = 0, gi = 0;
             for (uint32_t w = blockIdx.x; w < n_work; w += gridDim.x, gi++) {
                 for (uint32_t sb = 0; sb < nsb; sb++, gsb++) {
                     const uint32_t ab = gsb & 1;
                     if (gsb >= 2) gemm_wait(&acc_empty[ab], gsb / 2 - 1, a.dev_err);
-                    const uint32_t d_tmem = taddr + ab * kGNN;
+                    const uint32_t d_tmem = taddr + ab * NNP;
                     for (uint32_t hf = 0; hf < 2; hf++, gs++) {
                         const uint32_t sa = gs % kGAStages, s3 = gs % kGBStages;
                         gemm_wait(&a_full[sa], gs / kGAStages, a.dev_err);
                         gemm_wait(&b_full[s3], gs / kGBStages, a.dev_err);
                         tc_fence_after();
                         const uint32_t abase = smem_u32(sm + kOffA + sa * 32768);
-                        const uint32_t bbase = smem_u32(sm + kOffB + s3 * 16384);
+                        const uint32_t bbase = smem_u32(sm + kOffB + s3 * Geo::kBStage);
 #pragma unroll
                         for (uint32_t st = 0; st < 8; st++) {
                             const uint32_t ao = abase + (st >> 2) * 16384 + (st & 3) * 32;
-                            const uint32_t bo = bbase + (st >> 2) * 8192 + (st & 3) * 32;
+                            const uint32_t bo = bbase + (st >> 2) * Geo::kBAtom + (st & 3) * 32;
                             umma_f16(d_tmem, umma_desc_sw128(ao), umma_desc_sw128(bo), idesc, (hf | st) != 0);
                         }
                         umma_commit(&a_empty[sa]);
@@ -322,7 +354,7 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
                 if (gi >= 1) gemm_wait(min_empty, gi - 1, a.dev_err);
                 tc_fence_after();
                 const uint32_t am = smem_u32(sm + kOffAm), bm = smem_u32(sm + kOffBm);
-                const uint32_t d_tmem = taddr + 2 * kGNN;
+                const uint32_t d_tmem = taddr + 2 * NNP;
                 const uint32_t nkm = (8 * nsb + 15) / 16;
                 for (uint32_t st = 0; st < nkm; st++) {
                     umma_f16(d_tmem, umma_desc_sw128(am + st * 32), umma_desc_sw128(bm + st * 32), idesc, st != 0);
@@ -336,25 +368,35 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
         const uint32_t r = tid & 127, hh = tid >> 7;  // row, pair within the stage / position half
         const uint32_t lane_addr = taddr + ((uint32_t)(32 * (warp & 3)) << 16);
         uint32_t gs = 0, gsb = 0, gi = 0;
-        float y[kGN / 2];
+        float y[PH];  // positions [PH hh, PH hh + PH) of tile row r
+        // PH consecutive accumulator columns of this thread's lane (hi plane at
+        // column c0, lo plane at c0 + NP)
+        auto tload = [&](uint32_t c0, uint32_t (&vh)[PH], uint32_t (&vl)[PH]) {
+            if constexpr (PH == 16) {
+                tmem_ld16(lane_addr + c0, vh);
+                tmem_ld16(lane_addr + c0 + NP, vl);
+            } else {
+                tmem_ld32(lane_addr + c0, vh);
+                tmem_ld32(lane_addr + c0 + NP, vl);
+            }
+            tmem_wait_ld();
+        };
         auto fold = [&](uint32_t n, uint32_t sb) {  // superblock accumulator n (global count) of superblock sb
             gemm_wait(&acc_full[n & 1], n / 2, a.dev_err);
             tc_fence_after();
-            uint32_t vh[16], vl[16];
-            tmem_ld16(lane_addr + (n & 1) * kGNN + 16 * hh, vh);
-            tmem_ld16(lane_addr + (n & 1) * kGNN + kGN + 16 * hh, vl);
-            tmem_wait_ld();
+            uint32_t vh[PH], vl[PH];
+            tload((n & 1) * NNP + PH * hh, vh, vl);
             tc_fence_before();
             mbar_arrive(&acc_empty[n & 1]);
             const float dsb = hdr_d[sb * kGM + r];
 #pragma unroll
-            for (int q = 0; q < kGN / 2; q++)
+            for (int q = 0; q < PH; q++)
                 y[q] = fmaf(dsb, __uint_as_float(vh[q]) + __uint_as_float(vl[q]), y[q]);
         };
         for (uint32_t w = blockIdx.x; w < n_work; w += gridDim.x, gi++) {
-            const GemmItem it = gemm_item(a, w);
+            const GemmItem it = gemm_item<NP>(a, w);
 #pragma unroll
-            for (int q = 0; q < kGN / 2; q++) y[q] = 0.0f;
+            for (int q = 0; q < PH; q++) y[q] = 0.0f;
             for (uint32_t sb = 0; sb < nsb; sb++, gsb++) {
                 const uint32_t slot = gsb % kGRawSlots;
                 gemm_wait(&raw_full[slot], gsb / kGRawSlots, a.dev_err);
@@ -416,36 +458,35 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
             gemm_wait(min_full, gi, a.dev_err);
             tc_fence_after();
             {
-                uint32_t vh[16], vl[16];
-                tmem_ld16(lane_addr + 2 * kGNN + 16 * hh, vh);
-                tmem_ld16(lane_addr + 2 * kGNN + kGN + 16 * hh, vl);
-                tmem_wait_ld();
+                uint32_t vh[PH], vl[PH];
+                tload(2 * NNP + PH * hh, vh, vl);
                 tc_fence_before();
                 mbar_arrive(min_empty);
-                const float *inv = s_inv + (gi & 1) * kGN + 16 * hh;  // written before bm_full, which min_full follows
+                const float *inv = s_inv + (gi & 1) * NP + PH * hh;  // written before bm_full, which min_full follows
 #pragma unroll
-                for (int q = 0; q < kGN / 2; q++)
+                for (int q = 0; q < PH; q++)
                     y[q] = (y[q] - (__uint_as_float(vh[q]) + __uint_as_float(vl[q]))) * inv[q];
             }
-            const uint32_t q0 = 16 * hh;
+            const uint32_t q0 = PH * hh;
             if (MODE == 1) {
                 const uint32_t orow = kGM * it.m0 + r;
 #pragma unroll
-                for (uint32_t q = 0; q < (uint32_t)kGN / 2; q++)
+                for (uint32_t q = 0; q < (uint32_t)PH; q++)
                     if (q0 + q < it.nvalid) a.out[(size_t)(it.pos0 + q0 + q) * a.out_ld + orow] = y[q];
             } else {
                 // the A stages are idle here: every MMA of this item has completed
-                float *uex = reinterpret_cast<float *>(sm + kOffA);  // [64][33]
+                constexpr int UX = NP + 1;  // odd stride: no bank conflicts
+                float *uex = reinterpret_cast<float *>(sm + kOffA);  // [64][UX]
                 if (r >= 64)
 #pragma unroll
-                    for (int q = 0; q < kGN / 2; q++) uex[(r - 64) * 33 + q0 + q] = y[q];
+                    for (int q = 0; q < PH; q++) uex[(r - 64) * UX + q0 + q] = y[q];
                 math_sync();
                 if (r < 64) {
                     const uint32_t f = 64 * it.m0 + r;
 #pragma unroll
-                    for (uint32_t q = 0; q < (uint32_t)kGN / 2; q++)
+                    for (uint32_t q = 0; q < (uint32_t)PH; q++)
                         if (q0 + q < it.nvalid)
-                            a.out[(size_t)(it.pos0 + q0 + q) * a.F + f] = act_apply(a.act, y[q]) * uex[r * 33 + q0 + q];
+                            a.out[(size_t)(it.pos0 + q0 + q) * a.F + f] = act_apply(a.act, y[q]) * uex[r * UX + q0 + q];
                 }
             }
             math_sync();  // uex read before the next item's A writes
@@ -453,7 +494,7 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(taddr, kGTmemCols);
+    if (warp == 0) tmem_dealloc(taddr, Geo::kTmemCols);
 }
 
 // ── activation prep: f32 rows -> f16 hi/lo planes (K permuted in groups of 4
@@ -503,16 +544,17 @@ __global__ void __launch_bounds__(256) k_gemm_prep(const float *src, uint32_t K,
     if (threadIdx.x == 0) xinv[row] = ldexpf(1.0f, ex);
 }
 
-// ── tile list: (active expert slot, first position) per 32 positions ───────
+// ── tile list: (active expert slot, first position) per NP positions ───────
 // One block of kRouterMaxE threads: thread s counts the tiles of active slot
 // s, a block-wide exclusive scan places them.
+template <int NP>
 __global__ void __launch_bounds__(kRouterMaxE) k_gemm_tiles(MoePlan p, uint2 *tiles, uint32_t *n_tiles) {
     __shared__ uint32_t s_warp[kRouterMaxE / 32];
     pdl_wait();
     const uint32_t s = threadIdx.x, lane = s & 31, warp = s >> 5;
     const uint32_t na = *p.n_active;
     const uint32_t cnt = s < na ? p.act_cnt[s] : 0;
-    const uint32_t nt = (cnt + kGN - 1) / kGN;
+    const uint32_t nt = (cnt + NP - 1) / NP;
     uint32_t incl = nt;  // inclusive scan within the warp
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -524,7 +566,7 @@ __global__ void __launch_bounds__(kRouterMaxE) k_gemm_tiles(MoePlan p, uint2 *ti
     uint32_t base = 0;
     for (uint32_t w = 0; w < warp; w++) base += s_warp[w];
     const uint32_t first = base + incl - nt;
-    for (uint32_t i = 0; i < nt; i++) tiles[first + i] = make_uint2(s, i * kGN);
+    for (uint32_t i = 0; i < nt; i++) tiles[first + i] = make_uint2(s, i * NP);
     if (s == blockDim.x - 1) *n_tiles = base + incl;
 }
 
@@ -623,7 +665,12 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
     float *hinv = reinterpret_cast<float *>(take(P * 4));
     float *ybuf = reinterpret_cast<float *>(take(P * d * 4));
 
-    cudaError_t e = launch_k(c, "moe_gemm_tiles", k_gemm_tiles, dim3(1), dim3(kRouterMaxE), 0, p, tiles, n_tiles);
+    // wide tiles when the experts average at least 48 positions
+    const bool wide = P >= (size_t)48 * (E ? E : 1);
+    cudaError_t e = wide ? launch_k(c, "moe_gemm_tiles", k_gemm_tiles<64>, dim3(1), dim3(kRouterMaxE), 0, p, tiles,
+                                    n_tiles)
+                         : launch_k(c, "moe_gemm_tiles", k_gemm_tiles<32>, dim3(1), dim3(kRouterMaxE), 0, p, tiles,
+                                    n_tiles);
     if (e == cudaSuccess)
         e = launch_k(c, "moe_gemm_prep", k_gemm_prep, dim3(T), dim3(256), 0, x, (uint32_t)d, xh, xl, xsum, xinv);
     GemmArgs g;
@@ -652,8 +699,10 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
     g.out_ld = (uint32_t)F;
     g.dev_err = c.dev_err;
     if (e == cudaSuccess)
-        e = launch_k(c, "moe_gemm_gate_up", k_moe_gemm<0>, dim3((uint32_t)c.num_sms), dim3(kGThreadsV2),
-                     (size_t)kGSmem, g);
+        e = wide ? launch_k(c, "moe_gemm_gate_up", k_moe_gemm<0, 64>, dim3((uint32_t)c.num_sms), dim3(kGThreadsV2),
+                            (size_t)GemmGeo<64>::kSmem, g)
+                 : launch_k(c, "moe_gemm_gate_up", k_moe_gemm<0, 32>, dim3((uint32_t)c.num_sms), dim3(kGThreadsV2),
+                            (size_t)GemmGeo<32>::kSmem, g);
     if (e == cudaSuccess)
         e = launch_k(c, "moe_gemm_prep", k_gemm_prep, dim3((uint32_t)P), dim3(256), 0, (const float *)hbuf,
                      (uint32_t)F, hh, hl, hsum, hinv);
@@ -673,8 +722,10 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
     gd.out = ybuf;
     gd.out_ld = (uint32_t)d;
     if (e == cudaSuccess)
-        e = launch_k(c, "moe_gemm_down", k_moe_gemm<1>, dim3((uint32_t)c.num_sms), dim3(kGThreadsV2),
-                     (size_t)kGSmem, gd);
+        e = wide ? launch_k(c, "moe_gemm_down", k_moe_gemm<1, 64>, dim3((uint32_t)c.num_sms), dim3(kGThreadsV2),
+                            (size_t)GemmGeo<64>::kSmem, gd)
+                 : launch_k(c, "moe_gemm_down", k_moe_gemm<1, 32>, dim3((uint32_t)c.num_sms), dim3(kGThreadsV2),
+                            (size_t)GemmGeo<32>::kSmem, gd);
     if (e == cudaSuccess)
         e = launch_k(c, "moe_gemm_combine", k_gemm_combine, dim3(T, (uint32_t)((d + 255) / 256)), dim3(256), 0,
                      (const float *)ybuf, (uint32_t)d, (const uint32_t *)p.pair_pos, w, k, resid, out);

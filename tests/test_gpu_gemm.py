@@ -59,6 +59,9 @@ CASES = [
     (1024, 512, 8, 2, False, 0, True, False, 200),      # ~50 tokens per expert: several 32-position tiles
     (1024, 512, 16, 8, True, 1, False, True, 33),       # fused gate_up, GELU, expert scale
     (2048, 256, 32, 4, False, 0, True, False, 40),      # one superblock of down columns
+    # 48+ positions per expert on average: 64-position tiles (N = 128 MMAs)
+    (2048, 768, 16, 8, False, 0, True, False, 300),
+    (1024, 512, 4, 2, True, 1, False, True, 130),       # fused gate_up, GELU, expert scale
 ]
 
 
@@ -117,13 +120,15 @@ def test_gemm_moe_block_and_determinism(tc, oracle, pool):
         t_.free()
 
 
-def test_gemm_skewed_routing(tc, oracle):
+@pytest.mark.parametrize("T", [70, 300])
+def test_gemm_skewed_routing(tc, oracle, T):
     """Every token on the same few experts: one expert gets all T positions
-    (several tiles), the combine still runs in slot order."""
+    (several tiles; 64-position tiles at T = 300), the combine still runs in
+    slot order."""
     synth = _synth()
     rng = np.random.Generator(np.random.PCG64(31))
     L = synth.MoeLayer(rng, 1024, 16, 512)
-    T, k = 70, 4
+    k = 4
     x = rng.normal(0, 1, size=(T, 1024)).astype(np.float32)
     ids = np.stack([np.r_[[3], rng.choice(np.arange(4, 9), size=k - 1, replace=False)] for _ in range(T)])
     ids = ids.astype(np.uint32)
