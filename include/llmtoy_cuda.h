@@ -366,6 +366,24 @@ lt_status lt_softcap(lt_ctx *ctx, float *dev_x, uint64_t n, float cap);
 lt_status lt_greedy_step(lt_ctx *ctx, const float *dev_logits, uint32_t n, uint32_t *dev_tokens,
                          uint32_t *dev_pos, const uint32_t *dev_n_prompt);
 
+/* sample (src/model/sample.zig:27-183) as the last op of a decode step, like
+ * lt_greedy_step: temperature 0 is greedy; top_k in 1..256 takes the
+ * reference's fast path (sampleTopK) with optional top_p; otherwise softmax,
+ * top-k threshold, top-p cut, renormalisation and a multinomial draw.  The
+ * generator is std.Random.DefaultPrng (xoshiro256++, four 64-bit words in
+ * dev_rng_state, seeded by lt_rng_seed) with Random.float(f32); it advances
+ * only on sampled positions.  Scratch: n floats of the context arena. */
+typedef struct lt_sample_params {
+    float temperature;   /* 0: greedy */
+    uint32_t top_k;      /* 0: off */
+    float top_p;         /* 1: off */
+} lt_sample_params;
+lt_status lt_sample_step(lt_ctx *ctx, const float *dev_logits, uint32_t n, const lt_sample_params *params,
+                         uint64_t *dev_rng_state, uint32_t *dev_tokens, uint32_t *dev_pos,
+                         const uint32_t *dev_n_prompt);
+/* DefaultPrng.init(seed): the four xoshiro256++ words from SplitMix64 (host). */
+void lt_rng_seed(uint64_t seed, uint64_t state_out[4]);
+
 /* ── host-buffer entry points (synchronous) ─────────────────────────────────
  * Same semantics with HOST vectors, copies included: the shape of the
  * reference's own CPU calls, for callers that keep activations on the host. */

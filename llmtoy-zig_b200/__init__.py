@@ -37,6 +37,7 @@ EXPORTS = [
     "lt_device_alloc", "lt_device_free", "lt_copy_to_device", "lt_copy_to_host",
     "lt_embed", "lt_qmatvec_add", "lt_attn_prep", "lt_attn_decode", "lt_attn_block", "lt_prefetch_next",
     "lt_ffn_block", "lt_greedy_step", "lt_scale", "lt_add_rmsnorm", "lt_norm_pair", "lt_ffn_tail", "lt_softcap",
+    "lt_sample_step", "lt_rng_seed",
 ]
 
 
@@ -58,6 +59,18 @@ class AttnCfg(ctypes.Structure):
                 ("rope_neox", ctypes.c_uint32), ("rope_theta", ctypes.c_float), ("eps", ctypes.c_float),
                 ("scale", ctypes.c_float), ("kv_cap", ctypes.c_uint32), ("window", ctypes.c_uint32),
                 ("v_norm", ctypes.c_uint32)]
+
+
+class SampleParams(ctypes.Structure):
+    """lt_sample_params (src/model/sample.zig:4-8)."""
+    _fields_ = [("temperature", ctypes.c_float), ("top_k", ctypes.c_uint32), ("top_p", ctypes.c_float)]
+
+
+def rng_seed(seed: int) -> list[int]:
+    """DefaultPrng.init(seed): the four xoshiro256++ state words."""
+    out = (ctypes.c_uint64 * 4)()
+    load_library().lt_rng_seed(seed, out)
+    return list(out)
 
 
 _lib = None
@@ -124,6 +137,8 @@ def load_library() -> ctypes.CDLL:
         "lt_norm_pair": (I, [P, P, P, P, F, F, U32, U32, P, P]),
         "lt_ffn_tail": (I, [P, P, P, P, P, F, F, U32, U32, P]),
         "lt_softcap": (I, [P, P, U64, F]),
+        "lt_sample_step": (I, [P, P, U32, ctypes.POINTER(SampleParams), P, P, P, P]),
+        "lt_rng_seed": (None, [U64, ctypes.POINTER(U64)]),
         "lt_attn_block": (I, [P, ctypes.POINTER(AttnCfg), P, P, F, P, P, P, P, P, P, P, P, P]),
         "lt_prefetch_next": (I, [P, P, P]),
         "lt_quant_matvec_host": (I, [P, P, P, U32, P, U64, U64]),
@@ -380,6 +395,10 @@ class Context:
 
     def softcap(self, x, n: int, cap: float) -> None:
         self._check(self.lib.lt_softcap(self.ptr, _ptr(x), n, cap))
+
+    def sample_step(self, logits, n: int, params: SampleParams, rng_state, tokens, pos, n_prompt) -> None:
+        self._check(self.lib.lt_sample_step(self.ptr, _ptr(logits), n, ctypes.byref(params), _ptr(rng_state),
+                                            _ptr(tokens), _ptr(pos), _ptr(n_prompt)))
 
     def greedy_step(self, logits, n: int, tokens, pos, n_prompt) -> None:
         """n_prompt: a device word (the prompt length of the token stream)."""

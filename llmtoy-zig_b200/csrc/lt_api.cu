@@ -822,6 +822,34 @@ lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x,
     return launched(ctx, lt::launch_qmatvec(c, wo->m, 0, ctx->scratch, qo, att, dev_out, 1, dev_x), "qmatvec");
 }
 
+void lt_rng_seed(uint64_t seed, uint64_t state_out[4]) {
+    uint64_t st = seed;  // SplitMix64
+    for (int i = 0; i < 4; i++) {
+        st += 0x9e3779b97f4a7c15ull;
+        uint64_t z = st;
+        z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+        z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+        state_out[i] = z ^ (z >> 31);
+    }
+}
+
+lt_status lt_sample_step(lt_ctx *ctx, const float *dev_logits, uint32_t n, const lt_sample_params *params,
+                         uint64_t *dev_rng_state, uint32_t *dev_tokens, uint32_t *dev_pos,
+                         const uint32_t *dev_n_prompt) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!dev_logits || !params || !dev_rng_state || !dev_tokens || !dev_pos || !dev_n_prompt || n == 0)
+        return fail(ctx, LT_EINVAL, "lt_sample_step: bad argument");
+    if (!(params->temperature >= 0.0f) || !(params->top_p >= 0.0f))
+        return fail(ctx, LT_EINVAL, "lt_sample_step: temperature %g, top_p %g", params->temperature, params->top_p);
+    if ((st = ensure_scratch(ctx, (size_t)n * 4)) != LT_OK) return st;
+    return launched(ctx,
+                    lt::launch_sample(cfg_of(ctx), dev_logits, n, params->temperature, params->top_k, params->top_p,
+                                      reinterpret_cast<unsigned long long *>(dev_rng_state), dev_tokens, dev_pos,
+                                      dev_n_prompt, (float *)ctx->scratch),
+                    "sample");
+}
+
 lt_status lt_greedy_step(lt_ctx *ctx, const float *dev_logits, uint32_t n, uint32_t *dev_tokens, uint32_t *dev_pos,
                          const uint32_t *dev_n_prompt) {
     lt_status st = enter(ctx);

@@ -82,6 +82,10 @@ cudaError_t launch_argmax(const LaunchCfg &c, const float *x, uint32_t n, uint32
                           uint32_t *counters, uint32_t *tokens = nullptr, uint32_t *pos = nullptr,
                           const uint32_t *n_prompt = nullptr);
 cudaError_t launch_fill_f32(cudaStream_t s, float *p, size_t n, float v);
+// sample.zig:27-183 as a decode-step op (lt_sample.cu); probs: n floats of scratch.
+cudaError_t launch_sample(const LaunchCfg &c, const float *logits, uint32_t n, float temperature, uint32_t top_k,
+                          float top_p, unsigned long long *rng, uint32_t *tokens, uint32_t *pos,
+                          const uint32_t *n_prompt, float *probs);
 // Gemma 4 layer glue (lt_glue.cu), ntok rows of n values.
 cudaError_t launch_scale(const LaunchCfg &c, float *x, uint32_t n, uint32_t ntok, float s);
 cudaError_t launch_add_rmsnorm(const LaunchCfg &c, const float *y, const float *w, float eps, uint32_t n,

@@ -62,6 +62,7 @@ def load_host_library() -> ctypes.CDLL:
         "lth_decoder_logits": (P, [P]),
         "lth_decoder_tokens": (I, [P, P, U32]),
         "lth_generate": (I, [P, P, U32, U32, P]),
+        "lth_decoder_set_sampling": (I, [P, ctypes.c_float, U32, ctypes.c_float, ctypes.c_uint64]),
         "lth_gguf_open": (I, [ctypes.c_char_p, ctypes.POINTER(P)]),
         "lth_gguf_close": (None, [P]),
         "lth_gguf_info": (ctypes.c_size_t, [P, P, ctypes.c_size_t]),
@@ -211,8 +212,12 @@ class Decoder:
         self._check(self.lib.lth_decoder_tokens(self.ptr, arr, n))
         return list(arr)
 
+    def set_sampling(self, temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0, seed: int = 42) -> None:
+        """sample.zig parameters for the following steps (temperature 0: greedy)."""
+        self._check(self.lib.lth_decoder_set_sampling(self.ptr, temperature, top_k, top_p, seed))
+
     def generate(self, prompt, n_gen: int) -> list[int]:
-        """Greedy generation: prompt ids -> n_gen new ids."""
+        """Generation (greedy unless set_sampling chose otherwise): prompt ids -> n_gen new ids."""
         arr = (ctypes.c_uint32 * len(prompt))(*[int(t) for t in prompt])
         out = (ctypes.c_uint32 * n_gen)()
         self._check(self.lib.lth_generate(self.ptr, arr, len(prompt), n_gen, out))

@@ -33,6 +33,8 @@ struct lth_decoder {
     uint32_t *state = nullptr;   // {pos, n_prompt}
     lt_graph *graph = nullptr;
     bool warmed = false;
+    lt_sample_params sampling{0.0f, 0, 1.0f};  // temperature 0: greedy
+    uint64_t *rng = nullptr;                   // xoshiro256++ state (device)
 };
 
 namespace {
@@ -160,6 +162,8 @@ lt_status step(lth_decoder *d) {
     LTH_TRY(lt_qmatvec(d->ctx, m.lm_head, 0, d->xb, d->logits, 1));
     if (m.family == LTH_GEMMA4 && m.logit_softcap != 0.0f)
         LTH_TRY(lt_softcap(d->ctx, d->logits, m.vocab, m.logit_softcap));
+    if (d->sampling.temperature != 0.0f)
+        return lt_sample_step(d->ctx, d->logits, m.vocab, &d->sampling, d->rng, d->tokens, d->state, d->state + 1);
     return lt_greedy_step(d->ctx, d->logits, m.vocab, d->tokens, d->state, d->state + 1);
 }
 
@@ -167,7 +171,7 @@ void release(lth_decoder *d) {
     if (d->graph) lt_graph_free(d->ctx, d->graph);
     void *bufs[] = {d->x,    d->xb,     d->qkv,       d->att,       d->logits,    d->kcache, d->vcache,
                     d->ybuf, d->fbuf,   d->mbuf,      d->moe_in,    d->router_in, d->ids,    d->wts,
-                    d->ids_zero, d->tokens, d->state};
+                    d->ids_zero, d->tokens, d->state, d->rng};
     for (void *b : bufs)
         if (b) lt_device_free(d->ctx, b);
 }
@@ -222,6 +226,7 @@ lt_status lth_decoder_create(lt_ctx *ctx, const lth_model *m, lth_decoder **out)
         (st = alloc(d, &d->logits, m->vocab)) != LT_OK || (st = alloc(d, &d->kcache, cache)) != LT_OK ||
         (st = alloc(d, &d->vcache, cache)) != LT_OK || (st = alloc(d, &d->tokens, (size_t)m->kv_cap + 1)) != LT_OK ||
         (st = alloc(d, &d->state, 2)) != LT_OK || (st = alloc(d, &d->ids_zero, 4)) != LT_OK ||
+        (st = alloc(d, &d->rng, 4)) != LT_OK ||
         (m->family == LTH_GEMMA4 &&
          ((st = alloc(d, &d->ybuf, dm)) != LT_OK || (st = alloc(d, &d->fbuf, dm)) != LT_OK ||
           (st = alloc(d, &d->mbuf, dm)) != LT_OK || (st = alloc(d, &d->moe_in, dm)) != LT_OK ||
@@ -281,6 +286,22 @@ lt_status lth_decoder_replay(lth_decoder *d, uint32_t n_steps) {
 }
 
 const float *lth_decoder_logits(const lth_decoder *d) { return d ? d->logits : nullptr; }
+
+lt_status lth_decoder_set_sampling(lth_decoder *d, float temperature, uint32_t top_k, float top_p, uint64_t seed) {
+    if (!d || !(temperature >= 0.0f) || !(top_p >= 0.0f)) return LT_EINVAL;
+    d->sampling.temperature = temperature;
+    d->sampling.top_k = top_k;
+    d->sampling.top_p = top_p;
+    uint64_t st[4];
+    lt_rng_seed(seed, st);
+    LTH_TRY(lt_copy_to_device(d->ctx, d->rng, st, sizeof st));
+    LTH_TRY(lt_sync(d->ctx));
+    if (d->graph) {  // the step's last op changed
+        lt_graph_free(d->ctx, d->graph);
+        d->graph = nullptr;
+    }
+    return LT_OK;
+}
 
 lt_status lth_decoder_tokens(lth_decoder *d, uint32_t *host_out, uint32_t n) {
     if (!d || !host_out || n > d->m.kv_cap + 1) return LT_EINVAL;

@@ -83,7 +83,11 @@ lt_status lth_decoder_replay(lth_decoder *d, uint32_t n_steps);
 const float *lth_decoder_logits(const lth_decoder *d);
 /* Copy tokens[0, n) of the device token stream to the host (synchronises). */
 lt_status lth_decoder_tokens(lth_decoder *d, uint32_t *host_out, uint32_t n);
-/* Prompt -> n_gen greedy tokens into out (n_prompt + n_gen - 1 steps). */
+/* Sampling for the following steps (src/model/sample.zig; temperature 0:
+ * greedy), the generator seeded as DefaultPrng.init(seed).  Re-captures the
+ * step graph on its next use. */
+lt_status lth_decoder_set_sampling(lth_decoder *d, float temperature, uint32_t top_k, float top_p, uint64_t seed);
+/* Prompt -> n_gen tokens into out (n_prompt + n_gen - 1 steps). */
 lt_status lth_generate(lth_decoder *d, const uint32_t *prompt, uint32_t n_prompt, uint32_t n_gen,
                        uint32_t *out);
 

@@ -941,3 +941,159 @@ int orc_gemma_step(const orc_gemma *m, float *k_cache, float *v_cache, size_t gl
     free(ed); free(freqs);
     return rc ? -1 : 0;
 }
+
+/* ── sampling (sample.zig:27-183) ─────────────────────────────────────────── */
+
+static uint64_t rotl64(uint64_t x, int k) { return (x << k) | (x >> (64 - k)); }
+
+/* SplitMix64 (Vigna), the seeding of std.Random.Xoshiro256 */
+void orc_rng_seed(orc_rng *r, uint64_t seed) {
+    uint64_t st = seed;
+    for (int i = 0; i < 4; i++) {
+        st += 0x9e3779b97f4a7c15ull;
+        uint64_t z = st;
+        z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+        z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+        r->s[i] = z ^ (z >> 31);
+    }
+}
+
+/* xoshiro256++ (Blackman & Vigna) */
+static uint64_t rng_next(orc_rng *r) {
+    uint64_t *s = r->s;
+    const uint64_t res = rotl64(s[0] + s[3], 23) + s[0];
+    const uint64_t t = s[1] << 17;
+    s[2] ^= s[0];
+    s[3] ^= s[1];
+    s[1] ^= s[2];
+    s[0] ^= s[3];
+    s[2] ^= t;
+    s[3] = rotl64(s[3], 45);
+    return res;
+}
+
+static int clz64(uint64_t v) { return v ? __builtin_clzll(v) : 64; }
+
+/* Random.float(f32): 23 random mantissa bits, an exponentially distributed
+ * exponent from the leading zeros of the rest */
+float orc_rng_float(orc_rng *r) {
+    const uint64_t rnd = rng_next(r);
+    int lz = clz64(rnd);
+    if (lz >= 41) {
+        lz = 41 + clz64(rng_next(r));
+        if (lz == 41 + 64) lz += __builtin_clz((uint32_t)rng_next(r) | 0x7FFu);
+    }
+    const uint32_t bits = ((uint32_t)(126 - lz) << 23) | ((uint32_t)rnd & 0x7FFFFFu);
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+typedef struct { uint32_t idx; float val; } orc_cand;
+
+static int cmp_desc_f32(const void *a, const void *b) {
+    const float x = *(const float *)a, y = *(const float *)b;
+    return x > y ? -1 : x < y ? 1 : 0;
+}
+
+static const float *g_sort_probs;
+static int cmp_idx_desc(const void *a, const void *b) {
+    const size_t i = *(const size_t *)a, j = *(const size_t *)b;
+    const float x = g_sort_probs[i], y = g_sort_probs[j];
+    if (x > y) return -1;
+    if (x < y) return 1;
+    return i < j ? -1 : i > j ? 1 : 0;
+}
+
+uint32_t orc_sample(float *logits, size_t n, float temperature, uint32_t top_k, float top_p, orc_rng *rng) {
+    if (temperature == 0.0f) return orc_greedy(logits, n);
+    if (temperature != 1.0f) {
+        const float inv_t = 1.0f / temperature;
+        for (size_t i = 0; i < n; i++) logits[i] *= inv_t;
+    }
+    if (top_k > 0 && top_k < n && top_k <= 256) {  /* sampleTopK, sample.zig:82-145 */
+        orc_cand c[256];
+        size_t filled = 0;
+        const size_t k = top_k;
+        float max_logit = logits[0], exp_sum = 0.0f;
+        for (size_t i = 0; i < n; i++) {
+            const float logit = logits[i];
+            if (logit > max_logit) {
+                exp_sum = exp_sum * expf(max_logit - logit) + 1.0f;
+                max_logit = logit;
+            } else {
+                exp_sum += expf(logit - max_logit);
+            }
+            if (filled < k) {
+                size_t pos = filled++;
+                while (pos > 0 && logit > logits[c[pos - 1].idx]) { c[pos] = c[pos - 1]; pos--; }
+                c[pos].idx = (uint32_t)i;
+                c[pos].val = logit;
+            } else if (logit > logits[c[k - 1].idx]) {
+                size_t pos = k - 1;
+                while (pos > 0 && logit > logits[c[pos - 1].idx]) { c[pos] = c[pos - 1]; pos--; }
+                c[pos].idx = (uint32_t)i;
+                c[pos].val = logit;
+            }
+        }
+        for (size_t i = 0; i < k; i++) c[i].val = expf(c[i].val - max_logit) / exp_sum;
+        size_t kept = k;
+        if (top_p < 1.0f) {
+            float cum = 0.0f;
+            for (size_t i = 0; i < k; i++) {
+                cum += c[i].val;
+                if (cum >= top_p) { kept = i + 1; break; }
+            }
+        }
+        float kept_sum = 0.0f;
+        for (size_t i = 0; i < kept; i++) kept_sum += c[i].val;
+        if (kept_sum <= 0.0f) return c[0].idx;
+        const float r = orc_rng_float(rng) * kept_sum;
+        float cum = 0.0f;
+        for (size_t i = 0; i < kept; i++) {
+            cum += c[i].val;
+            if (r <= cum) return c[i].idx;
+        }
+        return c[kept - 1].idx;
+    }
+    orc_softmax(logits, n);
+    if (top_k > 0 && top_k < n) {  /* applyTopK, sample.zig:147-155 */
+        float *tmp = (float *)malloc(n * 4);
+        memcpy(tmp, logits, n * 4);
+        qsort(tmp, n, 4, cmp_desc_f32);
+        const float thr = tmp[(top_k < n ? top_k : n) - 1];
+        for (size_t i = 0; i < n; i++)
+            if (logits[i] < thr) logits[i] = 0.0f;
+        free(tmp);
+    }
+    if (top_p < 1.0f) {  /* applyTopP, sample.zig:157-178 */
+        size_t *idx = (size_t *)malloc(n * sizeof(size_t));
+        for (size_t i = 0; i < n; i++) idx[i] = i;
+        g_sort_probs = logits;
+        qsort(idx, n, sizeof(size_t), cmp_idx_desc);
+        float cum = 0.0f;
+        int cutoff = 0;
+        for (size_t j = 0; j < n; j++) {
+            if (cutoff) {
+                logits[idx[j]] = 0.0f;
+            } else {
+                cum += logits[idx[j]];
+                if (cum >= top_p) cutoff = 1;
+            }
+        }
+        free(idx);
+    }
+    float sum = 0.0f;  /* renormalize, sample.zig:180-187 */
+    for (size_t i = 0; i < n; i++) sum += logits[i];
+    if (sum > 0.0f) {
+        const float inv = 1.0f / sum;
+        for (size_t i = 0; i < n; i++) logits[i] *= inv;
+    }
+    const float r = orc_rng_float(rng);
+    float cum = 0.0f;
+    for (size_t i = 0; i < n; i++) {
+        cum += logits[i];
+        if (r <= cum) return (uint32_t)i;
+    }
+    return (uint32_t)(n - 1);
+}

@@ -209,6 +209,18 @@ typedef struct orc_gemma {
     const orc_gemma_layer *layers;
 } orc_gemma;
 
+/*
+ * Sampling, src/model/sample.zig:27-183, with std.Random.DefaultPrng
+ * (xoshiro256++ seeded through SplitMix64) and Random.float(f32) restated
+ * from the published algorithms (no Zig compiler here to confirm the stream).
+ * The full path's top-p sort is unstable in the reference (ties in an
+ * unspecified order); here ties keep index order.
+ */
+typedef struct orc_rng { uint64_t s[4]; } orc_rng;
+void orc_rng_seed(orc_rng *r, uint64_t seed);
+float orc_rng_float(orc_rng *r);
+uint32_t orc_sample(float *logits, size_t n, float temperature, uint32_t top_k, float top_p, orc_rng *rng);
+
 int orc_gemma_step(const orc_gemma *m, float *k_cache, float *v_cache, size_t global_cap, uint32_t token,
                    size_t pos, float *logits, orc_pool *pool);
 

@@ -62,6 +62,9 @@ def lib() -> ctypes.CDLL:
         "orc_sdp_attn": (None, [P, P, P, P, SZ, SZ, F]),
         "orc_model_step": (I, [P, P, P, SZ, U32, SZ, P, P]),
         "orc_gemma_step": (I, [P, P, P, SZ, U32, SZ, P, P]),
+        "orc_rng_seed": (None, [P, ctypes.c_uint64]),
+        "orc_rng_float": (F, [P]),
+        "orc_sample": (U32, [P, SZ, F, U32, F, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -330,3 +333,27 @@ class OracleGemma:
             if pos + 1 >= len(prompt):
                 toks.append(greedy(lg))
         return toks[len(prompt):], all_logits
+
+
+class Rng:
+    """orc_rng: DefaultPrng (xoshiro256++ seeded by SplitMix64)."""
+
+    def __init__(self, seed: int):
+        self.state = (ctypes.c_uint64 * 4)()
+        lib().orc_rng_seed(self.state, seed)
+
+    def float(self) -> float:
+        return lib().orc_rng_float(self.state)
+
+    def words(self) -> list[int]:
+        return list(self.state)
+
+    def copy(self) -> "Rng":
+        r = Rng(0)
+        r.state[:] = self.state[:]
+        return r
+
+
+def sample(logits, temperature: float, top_k: int, top_p: float, rng: Rng) -> int:
+    a = f32(logits).copy()
+    return int(lib().orc_sample(_p(a), a.size, temperature, top_k, top_p, rng.state))
