@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(kSmpThreads) k_sample(SampleArgs a) {
                         float cum = above;
                         uint32_t d = 255;
                         for (;; d--) {
-                            if (cum + hsum[d] >= a.top_p || d == 0) break;
+                            if ((hsum[d] > 0.0f && cum + hsum[d] >= a.top_p) || d == 0) break;
                             cum += hsum[d];
                         }
                         s_sel[0] = d;
