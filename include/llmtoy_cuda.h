@@ -21,8 +21,12 @@
  *     LT_ENODEV, an unsupported GGUF type LT_EUNSUPPORTED_TYPE (the
  *     reference panics there, src/ops/math.zig:206,223).
  *   - One context per GPU; a context is not re-entrant across host threads.
- *   - ggml_type uses the GGUF enum (src/gguf/types.zig:23-52):
- *     F32=0, F16=1, Q8_0=8, Q4_K=12, Q6_K=14.
+ *   - ggml_type uses the GGUF enum (src/gguf/types.zig:23-52): F32=0,
+ *     F16=1, Q5_0=6, Q5_1=7, Q8_0=8, Q3_K=11, Q4_K=12, Q5_K=13, Q6_K=14,
+ *     IQ4_NL=20 -- the types src/ops/math.zig:194-225 (rowBytes, dequantRow)
+ *     handle.  K-quants (Q3_K..Q6_K) need cols % 256 == 0, the rest cols % 32.
+ *     The fused single-token kernels (lt_attn_block, the T = 1 MoE block) take
+ *     Q8_0/Q4_K/Q6_K weights; the other types run through the separate ops.
  */
 #ifndef LLMTOY_CUDA_H
 #define LLMTOY_CUDA_H
@@ -39,7 +43,7 @@ extern "C" {
 typedef enum lt_status {
     LT_OK = 0,
     LT_EINVAL = 1,              /* bad argument, shape or size              */
-    LT_EUNSUPPORTED_TYPE = 2,   /* ggml type other than F32/F16/Q8_0/Q4_K/Q6_K */
+    LT_EUNSUPPORTED_TYPE = 2,   /* a ggml type outside the list above      */
     LT_ENOMEM = 3,              /* device allocation failed                 */
     LT_ECUDA = 4,               /* a CUDA runtime call failed               */
     LT_ETIMEOUT = 5,            /* a bounded device-side wait gave up       */
@@ -49,9 +53,14 @@ typedef enum lt_status {
 typedef enum lt_ggml_type {
     LT_TYPE_F32 = 0,
     LT_TYPE_F16 = 1,
+    LT_TYPE_Q5_0 = 6,
+    LT_TYPE_Q5_1 = 7,
     LT_TYPE_Q8_0 = 8,
+    LT_TYPE_Q3_K = 11,
     LT_TYPE_Q4_K = 12,
-    LT_TYPE_Q6_K = 14
+    LT_TYPE_Q5_K = 13,
+    LT_TYPE_Q6_K = 14,
+    LT_TYPE_IQ4_NL = 20
 } lt_ggml_type;
 
 typedef enum lt_act {
@@ -116,6 +125,17 @@ lt_status   lt_tensor_free(lt_ctx *ctx, lt_tensor *t);
  * experts' rows. */
 lt_status lt_dequant(lt_ctx *ctx, const lt_tensor *t, uint64_t row0, uint64_t nrows,
                      float *dev_out);
+
+/* quantizeQ8_1 (src/quant/dequant.zig:517-547): n f32 values (n % 32 == 0)
+ * into n/32 Q8_1 blocks of 36 bytes (f16 d = amax/127, f16 s = d*sum(q),
+ * 32 int8 q rounded half away from zero), bit-exact with the reference; with
+ * x4 != 0 in the block_q8_1_x4 layout instead (packQ8_1_x4, :569-586: 144
+ * bytes per 4 blocks, a partial last group zero-padded, so dev_out holds
+ * ceil(n/128)*144 bytes).  The reference's GPU activation format; the
+ * matvecs here quantise activations their own way (qact, exact products). */
+lt_status lt_quantize_q8_1(lt_ctx *ctx, const float *dev_x, uint64_t n, int x4, uint8_t *dev_out);
+/* dequantQ8_1 (src/quant/dequant.zig:549-558) of n values, either layout. */
+lt_status lt_dequant_q8_1(lt_ctx *ctx, const uint8_t *dev_q, uint64_t n, int x4, float *dev_out);
 
 /* quantMatvec / quantMatvecPar (src/ops/math.zig:133-171, :277-320) for ntok
  * input vectors: dev_y[tok][rows] = W[expert] . dev_x[tok][cols].

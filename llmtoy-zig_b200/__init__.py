@@ -18,8 +18,11 @@ LIB_PATH = Path(__file__).resolve().with_name("libllmtoy_cuda.so")
 
 # GGUF type codes (src/gguf/types.zig:23-52)
 F32, F16, Q8_0, Q4_K, Q6_K = 0, 1, 8, 12, 14
-TYPE_NAMES = {F32: "F32", F16: "F16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K"}
-BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
+Q5_0, Q5_1, Q3_K, Q5_K, IQ4_NL = 6, 7, 11, 13, 20
+TYPE_NAMES = {F32: "F32", F16: "F16", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K", Q5_0: "Q5_0", Q5_1: "Q5_1",
+              Q3_K: "Q3_K", Q5_K: "Q5_K", IQ4_NL: "IQ4_NL"}
+BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), Q5_0: (32, 22),
+         Q5_1: (32, 24), Q3_K: (256, 110), Q5_K: (256, 176), IQ4_NL: (32, 18)}
 ACT_SILU, ACT_GELU_TANH = 0, 1
 
 STATUS = {0: "LT_OK", 1: "LT_EINVAL", 2: "LT_EUNSUPPORTED_TYPE", 3: "LT_ENOMEM",
@@ -37,7 +40,7 @@ EXPORTS = [
     "lt_device_alloc", "lt_device_free", "lt_copy_to_device", "lt_copy_to_host",
     "lt_embed", "lt_qmatvec_add", "lt_attn_prep", "lt_attn_decode", "lt_attn_block", "lt_prefetch_next",
     "lt_ffn_block", "lt_greedy_step", "lt_scale", "lt_add_rmsnorm", "lt_norm_pair", "lt_ffn_tail", "lt_softcap",
-    "lt_sample_step", "lt_rng_seed",
+    "lt_sample_step", "lt_rng_seed", "lt_quantize_q8_1", "lt_dequant_q8_1",
 ]
 
 
@@ -101,6 +104,8 @@ def load_library() -> ctypes.CDLL:
         "lt_tensor_describe": (I, [P, ctypes.POINTER(TensorDesc)]),
         "lt_tensor_free": (I, [P, P]),
         "lt_dequant": (I, [P, P, U64, U64, P]),
+        "lt_quantize_q8_1": (I, [P, P, U64, I, P]),
+        "lt_dequant_q8_1": (I, [P, P, U64, I, P]),
         "lt_qmatvec": (I, [P, P, U32, P, P, U32]),
         "lt_rmsnorm": (I, [P, P, P, F, U32, U32, P]),
         "lt_softmax": (I, [P, P, U32, U32]),
@@ -277,6 +282,12 @@ class Context:
     # -- device ops (asynchronous) ----------------------------------------
     def dequant(self, t: Tensor, row0: int, nrows: int, out) -> None:
         self._check(self.lib.lt_dequant(self.ptr, t.handle, row0, nrows, _ptr(out)))
+
+    def quantize_q8_1(self, x, n: int, out, x4: bool = False) -> None:
+        self._check(self.lib.lt_quantize_q8_1(self.ptr, _ptr(x), n, int(x4), _ptr(out)))
+
+    def dequant_q8_1(self, q, n: int, out, x4: bool = False) -> None:
+        self._check(self.lib.lt_dequant_q8_1(self.ptr, _ptr(q), n, int(x4), _ptr(out)))
 
     def qmatvec(self, w: Tensor, x, y, ntok: int = 1, expert: int = 0) -> None:
         self._check(self.lib.lt_qmatvec(self.ptr, w.handle, expert, _ptr(x), _ptr(y), ntok))

@@ -175,11 +175,11 @@ lt_status ensure_pinned(lt_ctx *ctx, size_t bytes) {
 
 size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
 
-bool quantized(uint32_t t) { return t == lt::T_Q8_0 || t == lt::T_Q4_K || t == lt::T_Q6_K; }
+bool quantized(uint32_t t) { return lt::is_quant_type(t); }
 
 lt_status check_kernel_shape(lt_ctx *ctx, const lt::DevMat &m, const char *what) {
     if (quantized(m.type)) {
-        if (m.type != lt::T_Q8_0 && m.cols % 256 != 0)
+        if (lt::is_k_type(m.type) && m.cols % 256 != 0)
             return fail(ctx, LT_EINVAL, "%s: K-quant cols %llu not a multiple of 256", what,
                         (unsigned long long)m.cols);
         if (m.cols % 32 != 0)
@@ -561,6 +561,22 @@ lt_status lt_dequant(lt_ctx *ctx, const lt_tensor *t, uint64_t row0, uint64_t nr
     return launched(ctx, lt::launch_dequant(cfg_of(ctx), t->m, row0, nrows, dev_out), "dequant");
 }
 
+lt_status lt_quantize_q8_1(lt_ctx *ctx, const float *dev_x, uint64_t n, int x4, uint8_t *dev_out) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (n % 32 != 0) return fail(ctx, LT_EINVAL, "lt_quantize_q8_1: n=%llu not a multiple of 32", (unsigned long long)n);
+    if (n && (!dev_x || !dev_out)) return fail(ctx, LT_EINVAL, "lt_quantize_q8_1: null pointer");
+    return launched(ctx, lt::launch_quantize_q8_1(cfg_of(ctx), dev_x, n, x4 != 0, dev_out), "quantize_q8_1");
+}
+
+lt_status lt_dequant_q8_1(lt_ctx *ctx, const uint8_t *dev_q, uint64_t n, int x4, float *dev_out) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (n % 32 != 0) return fail(ctx, LT_EINVAL, "lt_dequant_q8_1: n=%llu not a multiple of 32", (unsigned long long)n);
+    if (n && (!dev_q || !dev_out)) return fail(ctx, LT_EINVAL, "lt_dequant_q8_1: null pointer");
+    return launched(ctx, lt::launch_dequant_q8_1(cfg_of(ctx), dev_q, n, x4 != 0, dev_out), "dequant_q8_1");
+}
+
 static lt_status qmatvec_impl(lt_ctx *ctx, const lt_tensor *w, uint32_t expert, const float *dev_x, float *dev_y,
                               uint32_t ntok, const float *dev_add) {
     lt_status st = enter(ctx);
@@ -910,7 +926,7 @@ static lt_status check_experts(lt_ctx *ctx, const lt_tensor *gate, const lt_tens
     if (E == 0 || down->m.n_experts != E || (up && up->m.n_experts != E))
         return fail(ctx, LT_EINVAL, "moe: gate/up/down must be 3-D expert tensors with the same expert count");
     if (!quantized(gate->m.type) || !quantized(down->m.type) || (up && up->m.type != gate->m.type))
-        return fail(ctx, LT_EUNSUPPORTED_TYPE, "moe: expert weights must be Q8_0/Q4_K/Q6_K (gate and up alike)");
+        return fail(ctx, LT_EUNSUPPORTED_TYPE, "moe: expert weights must be block-quantised (gate and up alike)");
     const uint64_t F = up ? gate->m.rows : gate->m.rows / 2;
     if ((!up && gate->m.rows % 2) || (up && (up->m.rows != F || up->m.cols != gate->m.cols)))
         return fail(ctx, LT_EINVAL, "moe: gate/up shapes disagree");
@@ -1132,7 +1148,7 @@ lt_status lt_ffn_block(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, 
     if (gate->m.n_experts || up->m.n_experts || down->m.n_experts)
         return fail(ctx, LT_EINVAL, "lt_ffn_block: dense (2-D) tensors expected");
     if (!quantized(gate->m.type) || !quantized(down->m.type) || up->m.type != gate->m.type)
-        return fail(ctx, LT_EUNSUPPORTED_TYPE, "lt_ffn_block: weights must be Q8_0/Q4_K/Q6_K (gate and up alike)");
+        return fail(ctx, LT_EUNSUPPORTED_TYPE, "lt_ffn_block: weights must be block-quantised (gate and up alike)");
     const uint64_t d = gate->m.cols, F = gate->m.rows;
     if (up->m.rows != F || up->m.cols != d || down->m.rows != d || down->m.cols != F)
         return fail(ctx, LT_EINVAL, "lt_ffn_block: gate/up/down shapes disagree");

@@ -10,9 +10,40 @@
 namespace lt {
 
 // GGUF type codes (src/gguf/types.zig:23-52).
-enum : uint32_t { T_F32 = 0, T_F16 = 1, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14 };
+enum : uint32_t {
+    T_F32 = 0, T_F16 = 1, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_Q3_K = 11, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14,
+    T_IQ4_NL = 20
+};
+
+// Block-quantised weight types the matvec kernels decode.
+__host__ __device__ constexpr bool is_quant_type(uint32_t t) {
+    return t == T_Q5_0 || t == T_Q5_1 || t == T_Q8_0 || t == T_Q3_K || t == T_Q4_K || t == T_Q5_K || t == T_Q6_K ||
+           t == T_IQ4_NL;
+}
+// 256-element superblock types (the rest use 32-element blocks).
+__host__ __device__ constexpr bool is_k_type(uint32_t t) {
+    return t == T_Q3_K || t == T_Q4_K || t == T_Q5_K || t == T_Q6_K;
+}
 
 constexpr int kQK = 256;          // K-quant superblock elements
+// IQ4_NL's non-linear table (src/quant/dequant.zig:618-621) as int8 bytes,
+// entries 0-3, 4-7, 8-11, 12-15 little-endian: byte-permute lookups.
+constexpr uint32_t kIq4T0 = 0xBFAD9881u, kIq4T1 = 0xF6EADDCFu, kIq4T2 = 0x26190D01u, kIq4T3 = 0x71594535u;
+
+LT_DEVINL int iq4nl_value(uint32_t nib) {
+    const uint32_t v = nib < 8 ? __byte_perm(kIq4T0, kIq4T1, nib) : __byte_perm(kIq4T2, kIq4T3, nib & 7u);
+    return (int)(int8_t)(v & 0xffu);
+}
+
+// Four nibbles (one per byte of n, values 0..15) to their four int8 table values.
+LT_DEVINL uint32_t iq4nl_lookup4(uint32_t n) {
+    const uint32_t x = n & 0x07070707u, y = x | (x >> 4);
+    const uint32_t sel = (y & 0xffu) | ((y >> 8) & 0xff00u);
+    const uint32_t lo = __byte_perm(kIq4T0, kIq4T1, sel), hi = __byte_perm(kIq4T2, kIq4T3, sel);
+    const uint32_t m = ((n >> 3) & 0x01010101u) * 0xffu;
+    return (hi & m) | (lo & ~m);
+}
+
 constexpr int kQ4KBytes = 144;    // src/quant/dequant.zig:155
 constexpr int kQ6KBytes = 210;    // src/quant/dequant.zig:235
 constexpr int kQ8Bytes = 34;      // src/quant/dequant.zig:40

@@ -72,6 +72,8 @@ uint32_t block_elems_of(uint32_t t);
 
 cudaError_t launch_dequant(const LaunchCfg &c, const DevMat &m, uint64_t row0, uint64_t nrows,
                            float *out);
+cudaError_t launch_quantize_q8_1(const LaunchCfg &c, const float *x, uint64_t n, int x4, uint8_t *out);
+cudaError_t launch_dequant_q8_1(const LaunchCfg &c, const uint8_t *q, uint64_t n, int x4, float *out);
 cudaError_t launch_rmsnorm(const LaunchCfg &c, const float *x, const float *w, float eps, uint32_t n,
                            uint32_t ntok, float *y);
 cudaError_t launch_softmax(const LaunchCfg &c, float *x, uint32_t n, uint32_t ntok);

@@ -11,27 +11,25 @@ namespace lt {
 
 // ── GGUF type table (src/gguf/types.zig:138-173, src/ops/math.zig:194) ─────
 
-bool type_supported(uint32_t t) {
-    return t == T_F32 || t == T_F16 || t == T_Q8_0 || t == T_Q4_K || t == T_Q6_K;
-}
+bool type_supported(uint32_t t) { return t == T_F32 || t == T_F16 || is_quant_type(t); }
 
 uint32_t block_elems_of(uint32_t t) {
-    switch (t) {
-    case T_F32:
-    case T_F16: return 1;
-    case T_Q8_0: return 32;
-    case T_Q4_K:
-    case T_Q6_K: return 256;
-    default: return 0;
-    }
+    if (t == T_F32 || t == T_F16) return 1;
+    if (is_k_type(t)) return 256;
+    return is_quant_type(t) ? 32 : 0;
 }
 
 uint64_t row_bytes_of(uint32_t t, uint64_t cols) {
     switch (t) {
     case T_F32: return cols * 4;
     case T_F16: return cols * 2;
+    case T_Q5_0: return (cols / 32) * 22;
+    case T_Q5_1: return (cols / 32) * 24;
     case T_Q8_0: return (cols / 32) * 34;
+    case T_IQ4_NL: return (cols / 32) * 18;
+    case T_Q3_K: return (cols / 256) * 110;
     case T_Q4_K: return (cols / 256) * 144;
+    case T_Q5_K: return (cols / 256) * 176;
     case T_Q6_K: return (cols / 256) * 210;
     default: return 0;
     }
@@ -127,6 +125,15 @@ LT_DEVINL void scale_min_k4(int j, const uint8_t *s, uint32_t &sc, uint32_t &mn)
     }
 }
 
+// The 6-bit Q3_K scale k (0..15) from its 12 packed bytes (dequant.zig:398-411):
+// low nibble from byte (k % 8) (high nibble for k >= 8), two high bits from
+// byte 8 + k % 4 at bit 2 * (k / 4).
+LT_DEVINL uint32_t q3k_scale(const uint8_t *s, uint32_t k) {
+    const uint32_t b = k & 3, w = k >> 2;
+    const uint32_t lo = (w & 2) ? (uint32_t)(s[4 * (w & 1) + b] >> 4) : (s[4 * (w & 1) + b] & 15u);
+    return lo | (((uint32_t)s[8 + b] >> (2 * w)) & 3u) << 4;
+}
+
 LT_DEVINL float dq_elem(const uint8_t *row, uint32_t type, uint32_t i) {
     switch (type) {
     case T_F32: return reinterpret_cast<const float *>(row)[i];
@@ -158,6 +165,46 @@ LT_DEVINL float dq_elem(const uint8_t *row, uint32_t type, uint32_t i) {
         const int8_t sc = (int8_t)sb[192 + 8 * n + (l >> 4) + 2 * kind];
         const float s = __fmul_rn(f16_at(sb + 208), (float)sc);
         return __fmul_rn(s, (float)q);
+    }
+    case T_Q5_0: {  // dequant.zig:201-217: d * (nibble | bit e of qh << 4) - 16
+        const uint8_t *b = row + (i / 32) * 22;
+        const uint32_t e = i & 31, qh = (uint32_t)b[2] | (uint32_t)b[3] << 8 | (uint32_t)b[4] << 16 | (uint32_t)b[5] << 24;
+        const uint32_t nib = e < 16 ? (b[6 + e] & 15u) : (uint32_t)(b[6 + e - 16] >> 4);
+        return __fmul_rn(f16_at(b), (float)((int)(nib | ((qh >> e) & 1u) << 4) - 16));
+    }
+    case T_Q5_1: {  // dequant.zig:469-487: d * q + m
+        const uint8_t *b = row + (i / 32) * 24;
+        const uint32_t e = i & 31;
+        const uint32_t nib = e < 16 ? (b[8 + e] & 15u) : (uint32_t)(b[8 + e - 16] >> 4);
+        const uint32_t q = nib | (((uint32_t)b[4 + e / 8] >> (e % 8)) & 1u) << 4;
+        return __fadd_rn(__fmul_rn(f16_at(b), (float)q), f16_at(b + 2));
+    }
+    case T_IQ4_NL: {  // dequant.zig:618-640: d * table[nibble]
+        const uint8_t *b = row + (i / 32) * 18;
+        const uint32_t e = i & 31;
+        const uint32_t nib = e < 16 ? (b[2 + e] & 15u) : (uint32_t)(b[2 + e - 16] >> 4);
+        return __fmul_rn(f16_at(b), (float)iq4nl_value(nib));
+    }
+    case T_Q5_K: {  // dequant.zig:324-367: Q4_K with a fifth bit from qh
+        const uint8_t *sb = row + (i / 256) * 176;
+        const uint32_t e = i & 255, c = e >> 6, p = e & 63, up = p >= 32 ? 1u : 0u;
+        const uint8_t byte = sb[48 + 32 * c + (p & 31)];
+        const uint32_t lo = up ? (uint32_t)(byte >> 4) : (byte & 15u);
+        const uint32_t q = lo + (((uint32_t)sb[16 + (p & 31)] >> (2 * c + up)) & 1u) * 16u;
+        uint32_t sc, mn;
+        scale_min_k4((int)(2 * c + up), sb + 4, sc, mn);
+        const float d1 = __fmul_rn(f16_at(sb), (float)sc);
+        const float m1 = __fmul_rn(f16_at(sb + 2), (float)mn);
+        return __fsub_rn(__fmul_rn(d1, (float)q), m1);
+    }
+    case T_Q3_K: {  // dequant.zig:388-464
+        const uint8_t *sb = row + (i / 256) * 110;
+        const uint32_t e = i & 255, h = e >> 7, j = (e >> 5) & 3, g = (e >> 4) & 1, l = e & 15;
+        const uint32_t lo2 = ((uint32_t)sb[32 + 32 * h + 16 * g + l] >> (2 * j)) & 3u;
+        const bool hb = (sb[16 * g + l] >> (4 * h + j)) & 1u;
+        const int v = (int)lo2 - (hb ? 0 : 4);
+        const float dl = __fmul_rn(f16_at(sb + 108), (float)q3k_scale(sb + 96, 8 * h + 2 * j + g) - 32.0f);
+        return __fmul_rn(dl, (float)v);
     }
     default: return 0.0f;
     }
@@ -212,6 +259,73 @@ cudaError_t launch_dequant(const LaunchCfg &c, const DevMat &m, uint64_t row0, u
     const uint64_t want = (n + 255) / 256;
     const unsigned grid = (unsigned)(want < 65535ull * 8 ? want : 65535ull * 8);
     return launch_k(c, "dequant", k_dequant, dim3(grid), dim3(256), 0, m.data, m.type, m.pitch, m.cols, row0, n, out);
+}
+
+// ── Q8_1 activation blocks (src/quant/dequant.zig:508-613) ─────────────────
+// Block b of 36 bytes: f16 d = amax / 127, f16 s = d * sum(q), 32 int8 q =
+// clamp(round(x / d)) with halves away from zero (Zig's @round, CUDA's
+// roundf).  The x4 layout groups four blocks as {ds[4], qs[4][32]} (144 B).
+
+LT_DEVINL size_t q81_ds_off(uint64_t b, int x4) { return x4 ? (b >> 2) * 144 + (b & 3) * 4 : b * 36; }
+LT_DEVINL size_t q81_qs_off(uint64_t b, int x4) { return x4 ? (b >> 2) * 144 + 16 + (b & 3) * 32 : b * 36 + 4; }
+
+// One warp per block; blocks past nb (the x4 padding of a partial last group) are zeroed.
+__global__ void k_quantize_q8_1(const float *x, uint64_t nb, uint64_t nb_pad, int x4, uint8_t *out) {
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const uint64_t nw = (uint64_t)gridDim.x * (blockDim.x >> 5);
+    for (uint64_t b = blockIdx.x * (uint64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); b < nb_pad; b += nw) {
+        uint8_t *ds = out + q81_ds_off(b, x4), *qs = out + q81_qs_off(b, x4);
+        if (b >= nb) {
+            qs[lane] = 0;
+            if (lane < 4) ds[lane] = 0;
+            continue;
+        }
+        const float v = x[32 * b + lane];
+        float amax = fabsf(v);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float inv = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        const float q = fminf(fmaxf(roundf(__fmul_rn(v, inv)), -127.0f), 127.0f);
+        const int qi = (int)q;
+        int sum = qi;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        qs[lane] = (uint8_t)(int8_t)qi;
+        if (lane == 0) {
+            const unsigned short dh = __half_as_ushort(__float2half_rn(d));
+            const unsigned short sh = __half_as_ushort(__float2half_rn(__fmul_rn(d, (float)sum)));
+            ds[0] = (uint8_t)(dh & 0xff);
+            ds[1] = (uint8_t)(dh >> 8);
+            ds[2] = (uint8_t)(sh & 0xff);
+            ds[3] = (uint8_t)(sh >> 8);
+        }
+    }
+}
+
+__global__ void k_dequant_q8_1(const uint8_t *q, uint64_t n, int x4, float *out) {
+    pdl_wait();
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t b = i >> 5;
+        const float d = f16_at(q + q81_ds_off(b, x4));
+        out[i] = __fmul_rn(d, (float)(int8_t)q[q81_qs_off(b, x4) + (i & 31)]);
+    }
+}
+
+cudaError_t launch_quantize_q8_1(const LaunchCfg &c, const float *x, uint64_t n, int x4, uint8_t *out) {
+    const uint64_t nb = n / 32, nb_pad = x4 ? (nb + 3) / 4 * 4 : nb;
+    if (nb_pad == 0) return cudaSuccess;
+    const uint64_t want = (nb_pad + 7) / 8;
+    const unsigned grid = (unsigned)(want < 65535ull * 8 ? want : 65535ull * 8);
+    return launch_k(c, "quantize_q8_1", k_quantize_q8_1, dim3(grid), dim3(256), 0, x, nb, nb_pad, x4, out);
+}
+
+cudaError_t launch_dequant_q8_1(const LaunchCfg &c, const uint8_t *q, uint64_t n, int x4, float *out) {
+    if (n == 0) return cudaSuccess;
+    const uint64_t want = (n + 255) / 256;
+    const unsigned grid = (unsigned)(want < 65535ull * 8 ? want : 65535ull * 8);
+    return launch_k(c, "dequant_q8_1", k_dequant_q8_1, dim3(grid), dim3(256), 0, q, n, x4, out);
 }
 
 // Activation quantisation and block decoders: lt_decode.cuh.

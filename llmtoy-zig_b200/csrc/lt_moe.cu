@@ -267,6 +267,11 @@ cudaError_t launch_moe_gate_up(const LaunchCfg &c, const DevMat &gate, const Dev
         case T_Q4_K: return launch_gate_up_t<T_Q4_K, 1>(c, a, ny);
         case T_Q6_K: return launch_gate_up_t<T_Q6_K, 1>(c, a, ny);
         case T_Q8_0: return launch_gate_up_t<T_Q8_0, 1>(c, a, ny);
+        case T_Q5_0: return launch_gate_up_t<T_Q5_0, 1>(c, a, ny);
+        case T_Q5_1: return launch_gate_up_t<T_Q5_1, 1>(c, a, ny);
+        case T_IQ4_NL: return launch_gate_up_t<T_IQ4_NL, 1>(c, a, ny);
+        case T_Q5_K: return launch_gate_up_t<T_Q5_K, 1>(c, a, ny);
+        case T_Q3_K: return launch_gate_up_t<T_Q3_K, 1>(c, a, ny);
         default: return cudaErrorInvalidValue;
         }
     }
@@ -274,6 +279,11 @@ cudaError_t launch_moe_gate_up(const LaunchCfg &c, const DevMat &gate, const Dev
     case T_Q4_K: return launch_gate_up_t<T_Q4_K, 4>(c, a, ny);
     case T_Q6_K: return launch_gate_up_t<T_Q6_K, 2>(c, a, ny);
     case T_Q8_0: return launch_gate_up_t<T_Q8_0, 4>(c, a, ny);
+    case T_Q5_0: return launch_gate_up_t<T_Q5_0, 4>(c, a, ny);
+    case T_Q5_1: return launch_gate_up_t<T_Q5_1, 4>(c, a, ny);
+    case T_IQ4_NL: return launch_gate_up_t<T_IQ4_NL, 4>(c, a, ny);
+    case T_Q5_K: return launch_gate_up_t<T_Q5_K, 4>(c, a, ny);
+    case T_Q3_K: return launch_gate_up_t<T_Q3_K, 2>(c, a, ny);
     default: return cudaErrorInvalidValue;
     }
 }
@@ -395,12 +405,20 @@ cudaError_t launch_moe_down(const LaunchCfg &c, const DevMat &down, const uint8_
     a.dev_err = c.dev_err;
     const size_t smem = dn_smem_bytes(a.pitch, a.rt, (int)k, (int)a.nitems);
     const dim3 grid((a.D + a.rt - 1) / a.rt, ntok);
+#define LT_DOWN_CASE(T) \
+    case T: return launch_k(c, type_label<T>("moe_down"), k_moe_down<T>, grid, dim3(kDnWarps * 32), smem, a);
     switch (down.type) {
-    case T_Q4_K: return launch_k(c, type_label<T_Q4_K>("moe_down"), k_moe_down<T_Q4_K>, grid, dim3(kDnWarps * 32), smem, a);
-    case T_Q6_K: return launch_k(c, type_label<T_Q6_K>("moe_down"), k_moe_down<T_Q6_K>, grid, dim3(kDnWarps * 32), smem, a);
-    case T_Q8_0: return launch_k(c, type_label<T_Q8_0>("moe_down"), k_moe_down<T_Q8_0>, grid, dim3(kDnWarps * 32), smem, a);
+        LT_DOWN_CASE(T_Q4_K)
+        LT_DOWN_CASE(T_Q6_K)
+        LT_DOWN_CASE(T_Q8_0)
+        LT_DOWN_CASE(T_Q5_0)
+        LT_DOWN_CASE(T_Q5_1)
+        LT_DOWN_CASE(T_IQ4_NL)
+        LT_DOWN_CASE(T_Q5_K)
+        LT_DOWN_CASE(T_Q3_K)
     default: return cudaErrorInvalidValue;
     }
+#undef LT_DOWN_CASE
 }
 
 }  // namespace lt

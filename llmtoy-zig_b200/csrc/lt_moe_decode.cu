@@ -402,6 +402,8 @@ struct DecodePlan {
 
 bool decode_plan(const DecodeParams &p, int num_sms, DecodePlan &out) {
     if (num_sms <= 0 || p.k == 0 || p.k > 16 || p.E == 0 || p.E > (uint32_t)kRouterMaxE) return false;
+    auto ok_type = [](uint32_t t) { return t == T_Q8_0 || t == T_Q4_K || t == T_Q6_K; };
+    if (!ok_type(p.gate.type) || !ok_type(p.down.type)) return false;  // the grouped kernels take the rest
     const uint32_t G = (uint32_t)num_sms;
     DecodeArgs &a = out.a;
     a.rw = p.router;

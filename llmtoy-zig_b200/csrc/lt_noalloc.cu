@@ -53,7 +53,7 @@ lt_status scratch_address(int device, uint8_t **out) {
 
 size_t al256(size_t v) { return (v + 255) & ~(size_t)255; }
 
-bool quantized_type(uint32_t t) { return t == T_Q8_0 || t == T_Q4_K || t == T_Q6_K; }
+bool quantized_type(uint32_t t) { return is_quant_type(t); }
 
 }  // namespace
 }  // namespace lt
@@ -69,7 +69,7 @@ extern "C" lt_status lt_moe_ffn_noalloc(void *cuda_stream, const void *gate, con
     if (n_experts == 0 || n_experts > 1024 || k == 0 || k > 16 || k > n_experts) return LT_EINVAL;
     if (act != LT_ACT_SILU && act != LT_ACT_GELU_TANH) return LT_EINVAL;
     if (d_expert % 32 != 0 || d_model % 32 != 0 || d_model > 65536 || d_expert > 65536) return LT_EINVAL;
-    if ((gate_type != T_Q8_0 && d_model % 256 != 0) || (down_type != T_Q8_0 && d_expert % 256 != 0))
+    if ((is_k_type(gate_type) && d_model % 256 != 0) || (is_k_type(down_type) && d_expert % 256 != 0))
         return LT_EINVAL;
     // The caller's weights are used in place, so each GGUF row must already
     // sit at a 16-byte multiple (TMA bulk copies need 16-byte aligned rows).

@@ -148,6 +148,11 @@ cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert,
     case T_Q4_K: return one ? launch_qmv_t<T_Q4_K, 1>(c, a) : launch_qmv_t<T_Q4_K, 4>(c, a);
     case T_Q6_K: return one ? launch_qmv_t<T_Q6_K, 1>(c, a) : launch_qmv_t<T_Q6_K, 2>(c, a);
     case T_Q8_0: return one ? launch_qmv_t<T_Q8_0, 1>(c, a) : launch_qmv_t<T_Q8_0, 4>(c, a);
+    case T_Q5_0: return one ? launch_qmv_t<T_Q5_0, 1>(c, a) : launch_qmv_t<T_Q5_0, 4>(c, a);
+    case T_Q5_1: return one ? launch_qmv_t<T_Q5_1, 1>(c, a) : launch_qmv_t<T_Q5_1, 4>(c, a);
+    case T_IQ4_NL: return one ? launch_qmv_t<T_IQ4_NL, 1>(c, a) : launch_qmv_t<T_IQ4_NL, 4>(c, a);
+    case T_Q5_K: return one ? launch_qmv_t<T_Q5_K, 1>(c, a) : launch_qmv_t<T_Q5_K, 4>(c, a);
+    case T_Q3_K: return one ? launch_qmv_t<T_Q3_K, 1>(c, a) : launch_qmv_t<T_Q3_K, 2>(c, a);
     default: return cudaErrorInvalidValue;
     }
 }

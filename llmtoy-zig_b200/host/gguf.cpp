@@ -77,7 +77,9 @@ const char *type_label(uint32_t t) {
 }
 
 // The types this backend decodes on the device (lt_upload accepts).
-bool device_type(uint32_t t) { return t == 0 || t == 1 || t == 8 || t == 12 || t == 14; }
+bool device_type(uint32_t t) {
+    return t == 0 || t == 1 || t == 6 || t == 7 || t == 8 || t == 11 || t == 12 || t == 13 || t == 14 || t == 20;
+}
 
 struct Cursor {
     const uint8_t *p;
@@ -312,7 +314,8 @@ size_t lth_gguf_info(const lth_gguf *g, char *buf, size_t size) {
     for (const TensorInfo &t : g->tensors) counts[t.type]++;
     for (auto &kv : counts) put("  %s: %u\n", type_label(kv.first), kv.second);
     // the reference lists the tensors its GPU backend cannot decode; here:
-    // the types this backend's device kernels decode (F32, F16, Q8_0, Q4_K, Q6_K)
+    // the types this backend's device kernels decode (F32, F16, Q5_0, Q5_1, Q8_0, Q3_K, Q4_K, Q5_K,
+    // Q6_K, IQ4_NL)
     o += "\nunsupported GPU quant tensors:\n";
     size_t bad = 0;
     for (const TensorInfo &t : g->tensors) {

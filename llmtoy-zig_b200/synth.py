@@ -7,6 +7,9 @@ bytes in the reference's block layouts (src/quant/dequant.zig):
   6-bit scales/mins and uniform nibbles (uniform random bytes give both).
 * Q6_K (210 B / 256): uniform ql/qh bytes, uniform int8 scales, f16 d ~ U(1e-3, 4e-3).
 * Q8_0 (34 B / 32): f16 d = 0.02/127 * U(0.5, 1.5), int8 quants uniform in [-127, 127].
+* Q5_0 (22 B / 32), Q5_1 (24 B / 32), IQ4_NL (18 B / 32), Q5_K (176 B / 256),
+  Q3_K (110 B / 256): uniform random bytes with finite f16 scales of the same
+  weight magnitude (~0.02); these formats appear in no benchmark config.
 * router weights f32 N(0, 0.02); hidden states f32 N(0, 1).
 
 ``stamp_d`` reproduces the reference's GPU fuzz generator instead: every f16
@@ -17,7 +20,9 @@ from __future__ import annotations
 import numpy as np
 
 F32, F16, Q8_0, Q4_K, Q6_K = 0, 1, 8, 12, 14
-BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210)}
+Q5_0, Q5_1, Q3_K, Q5_K, IQ4_NL = 6, 7, 11, 13, 20
+BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), Q5_0: (32, 22),
+         Q5_1: (32, 24), IQ4_NL: (32, 18), Q5_K: (256, 176), Q3_K: (256, 110)}
 
 CONFIG_SEED_BASE = 0x11A70000
 
@@ -49,6 +54,24 @@ def q6k_blocks(rng: np.random.Generator, n: int, stamp_d: bool = False) -> np.nd
     return b
 
 
+def other_blocks(rng: np.random.Generator, t: int, n: int) -> np.ndarray:
+    """Random blocks of the further formats with their f16 scale fields set."""
+    b = rng.integers(0, 256, size=(n, BLOCK[t][1]), dtype=np.uint8)
+    if t == Q5_0:
+        b[:, 0:2] = _f16_bytes(0.02 / 16.0 * rng.uniform(0.5, 1.5, n))
+    elif t == Q5_1:
+        b[:, 0:2] = _f16_bytes(0.04 / 31.0 * rng.uniform(0.5, 1.5, n))
+        b[:, 2:4] = _f16_bytes(-0.02 * rng.uniform(0.5, 1.5, n))
+    elif t == IQ4_NL:
+        b[:, 0:2] = _f16_bytes(0.02 / 127.0 * rng.uniform(0.5, 1.5, n))
+    elif t == Q5_K:
+        b[:, 0:2] = _f16_bytes(rng.uniform(5e-4, 2e-3, n))
+        b[:, 2:4] = _f16_bytes(rng.uniform(0.0, 1e-3, n))
+    elif t == Q3_K:
+        b[:, 108:110] = _f16_bytes(rng.uniform(1e-4, 4e-4, n))
+    return b
+
+
 def q8_0_blocks(rng: np.random.Generator, n: int, stamp_d: bool = False) -> np.ndarray:
     b = np.empty((n, 34), dtype=np.uint8)
     if stamp_d:
@@ -72,6 +95,8 @@ def matrix(rng: np.random.Generator, ggml_type: int, rows: int, cols: int, stamp
         blk = q6k_blocks(rng, nb, stamp_d)
     elif ggml_type == Q8_0:
         blk = q8_0_blocks(rng, nb, stamp_d)
+    elif ggml_type in (Q5_0, Q5_1, IQ4_NL, Q5_K, Q3_K):
+        blk = other_blocks(rng, ggml_type, nb)
     elif ggml_type == F32:
         blk = rng.normal(0.0, 0.02, size=(rows, cols)).astype(np.float32).view(np.uint8)
     elif ggml_type == F16:

@@ -187,6 +187,226 @@ void orc_dequant_q6_k(const uint8_t *data, float *out, size_t n) {
     }
 }
 
+/* dequant.zig:201-217: d * ((nibble | qh bit << 4) - 16); element j < 16 takes
+ * the low nibble of qs[j] and qh bit j, element j + 16 the high nibble and bit
+ * j + 16. */
+void orc_dequant_q5_0(const uint8_t *data, float *out, size_t n) {
+    for (size_t b = 0; b < n / 32; b++) {
+        const uint8_t *blk = data + b * 22;
+        const float d = f16_at(blk);
+        const uint32_t qh = (uint32_t)blk[2] | (uint32_t)blk[3] << 8 | (uint32_t)blk[4] << 16 | (uint32_t)blk[5] << 24;
+        const uint8_t *qs = blk + 6;
+        for (int j = 0; j < 16; j++) {
+            const int x0 = (int)((qs[j] & 0x0f) | (((qh >> j) & 1u) << 4)) - 16;
+            const int x1 = (int)((qs[j] >> 4) | (((qh >> (j + 16)) & 1u) << 4)) - 16;
+            out[b * 32 + j] = d * (float)x0;
+            out[b * 32 + j + 16] = d * (float)x1;
+        }
+    }
+}
+
+/* dequant.zig:92-133: per block 8 lanes x 4 groups of (q5 - 16) * v (mul then
+ * add), ordered lane reduction, times d, accumulated block by block. */
+float orc_dot_q5_0(const uint8_t *data, const float *vec, size_t n) {
+    float total = 0.0f;
+    for (size_t b = 0; b < n / 32; b++) {
+        const uint8_t *blk = data + b * 22;
+        const float d = f16_at(blk);
+        const uint32_t qh = (uint32_t)blk[2] | (uint32_t)blk[3] << 8 | (uint32_t)blk[4] << 16 | (uint32_t)blk[5] << 24;
+        const uint8_t *qs = blk + 6;
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int g = 0; g < 4; g++) {
+            const int qs_off = (g & 1) * 8, hi = g >= 2, qh_off = g < 2 ? g * 8 : (g - 2) * 8 + 16;
+            for (int l = 0; l < 8; l++) {
+                const uint8_t nib = hi ? (uint8_t)(qs[qs_off + l] >> 4) : (uint8_t)(qs[qs_off + l] & 0x0f);
+                const uint8_t hb = (uint8_t)((qh >> (qh_off + l)) & 1u);
+                const float q5 = (float)(nib | (hb << 4)) - 16.0f;
+                acc[l] += q5 * vec[b * 32 + g * 8 + l];
+            }
+        }
+        float r = -0.0f;
+        for (int l = 0; l < 8; l++) r += acc[l];
+        total += r * d;
+    }
+    return total;
+}
+
+/* dequant.zig:469-487: d * q + m (two roundings) */
+void orc_dequant_q5_1(const uint8_t *data, float *out, size_t n) {
+    for (size_t b = 0; b < n / 32; b++) {
+        const uint8_t *blk = data + b * 24;
+        const float d = f16_at(blk), m = f16_at(blk + 2);
+        const uint8_t *qh = blk + 4, *qs = blk + 8;
+        for (int j = 0; j < 16; j++) {
+            const uint8_t hi0 = (uint8_t)(((qh[j / 8] >> (j % 8)) & 1) << 4);
+            const uint8_t hi1 = (uint8_t)(((qh[(j + 16) / 8] >> ((j + 16) % 8)) & 1) << 4);
+            out[b * 32 + j] = d * (float)((qs[j] & 0x0f) | hi0) + m;
+            out[b * 32 + j + 16] = d * (float)((qs[j] >> 4) | hi1) + m;
+        }
+    }
+}
+
+/* dequant.zig:324-367: Q4_K's (d*sc) * q - dmin*mn with q = nibble + 16 * bit,
+ * the bit from qh[l] & (1 << 2c) (low nibbles) or (2 << 2c) (high nibbles). */
+void orc_dequant_q5_k(const uint8_t *data, float *out, size_t n) {
+    for (size_t b = 0; b < n / QK_K; b++) {
+        const uint8_t *blk = data + b * 176;
+        const float d = f16_at(blk), dmin = f16_at(blk + 2);
+        const uint8_t *scales = blk + 4, *qh = blk + 16, *ql = blk + 48;
+        uint8_t um1 = 1, um2 = 2;
+        for (int c = 0; c < 4; c++) {
+            uint8_t sc1, mn1, sc2, mn2;
+            scale_min(2 * c, scales, &sc1, &mn1);
+            scale_min(2 * c + 1, scales, &sc2, &mn2);
+            const float d1 = d * (float)sc1, m1 = dmin * (float)mn1;
+            const float d2 = d * (float)sc2, m2 = dmin * (float)mn2;
+            for (int l = 0; l < 32; l++) {
+                const float hi = (qh[l] & um1) ? 16.0f : 0.0f;
+                out[b * QK_K + 64 * c + l] = d1 * ((float)(ql[32 * c + l] & 0x0f) + hi) - m1;
+            }
+            for (int l = 0; l < 32; l++) {
+                const float hi = (qh[l] & um2) ? 16.0f : 0.0f;
+                out[b * QK_K + 64 * c + 32 + l] = d2 * ((float)(ql[32 * c + l] >> 4) + hi) - m2;
+            }
+            um1 = (uint8_t)(um1 * 4);
+            um2 = (uint8_t)(um2 * 4);
+        }
+    }
+}
+
+/* dequant.zig:388-464: sixteen 6-bit scales unpacked from 12 bytes with the
+ * kmask steps, dl = d * (sc - 32); value dl * ((qs >> shift & 3) - (hmask bit ? 0 : 4)). */
+void orc_dequant_q3_k(const uint8_t *data, float *out, size_t n) {
+    for (size_t b = 0; b < n / QK_K; b++) {
+        const uint8_t *blk = data + b * 110;
+        const uint8_t *hmask = blk, *qs = blk + 32;
+        const float d_all = f16_at(blk + 108);
+        uint32_t aux[4], tmp;
+        memcpy(&aux[0], blk + 96, 4);
+        memcpy(&aux[1], blk + 100, 4);
+        memcpy(&tmp, blk + 104, 4);
+        const uint32_t k1 = 0x03030303u, k2 = 0x0f0f0f0fu;
+        aux[2] = ((aux[0] >> 4) & k2) | (((tmp >> 4) & k1) << 4);
+        aux[3] = ((aux[1] >> 4) & k2) | (((tmp >> 6) & k1) << 4);
+        aux[0] = (aux[0] & k2) | (((tmp >> 0) & k1) << 4);
+        aux[1] = (aux[1] & k2) | (((tmp >> 2) & k1) << 4);
+        uint8_t sc[16];
+        memcpy(sc, aux, 16);
+        int is = 0;
+        uint8_t m = 1;
+        size_t o = b * QK_K;
+        for (int half = 0; half < 2; half++) {
+            const uint8_t *q = qs + 32 * half;
+            int shift = 0;
+            for (int j = 0; j < 4; j++) {
+                for (int g = 0; g < 2; g++) {
+                    const float dl = d_all * ((float)sc[is++] - 32.0f);
+                    for (int l = 0; l < 16; l++) {
+                        const int lo2 = (q[16 * g + l] >> shift) & 3;
+                        const int v = lo2 - ((hmask[16 * g + l] & m) ? 0 : 4);
+                        out[o++] = (float)v * dl;
+                    }
+                }
+                shift += 2;
+                m = (uint8_t)(m << 1);
+            }
+        }
+    }
+}
+
+static const float kIq4Table[16] = {-127.0f, -104.0f, -83.0f, -65.0f, -49.0f, -35.0f, -22.0f, -10.0f,
+                                    1.0f,    13.0f,   25.0f,  38.0f,  53.0f,  69.0f,  89.0f,  113.0f};
+
+/* dequant.zig:623-640 */
+void orc_dequant_iq4_nl(const uint8_t *data, float *out, size_t n) {
+    for (size_t b = 0; b < n / 32; b++) {
+        const uint8_t *blk = data + b * 18;
+        const float d = f16_at(blk);
+        for (int j = 0; j < 16; j++) {
+            out[b * 32 + j] = d * kIq4Table[blk[2 + j] & 0x0f];
+            out[b * 32 + j + 16] = d * kIq4Table[blk[2 + j] >> 4];
+        }
+    }
+}
+
+/* dequant.zig:642-660: one scalar accumulator per block (low nibble's term,
+ * then the high nibble's), d * acc added block by block. */
+float orc_dot_iq4_nl(const uint8_t *data, const float *vec, size_t n) {
+    float total = 0.0f;
+    for (size_t b = 0; b < n / 32; b++) {
+        const uint8_t *blk = data + b * 18;
+        const float d = f16_at(blk);
+        float acc = 0.0f;
+        for (int j = 0; j < 16; j++) {
+            const uint8_t q = blk[2 + j];
+            acc += kIq4Table[q & 0x0f] * vec[b * 32 + j];
+            acc += kIq4Table[q >> 4] * vec[b * 32 + j + 16];
+        }
+        total += d * acc;
+    }
+    return total;
+}
+
+/* dequant.zig:517-547: d = amax / 127, q = clamp(round(x / d)) with Zig's
+ * @round (halves away from zero), s = d * sum(q), both stored as f16. */
+void orc_quantize_q8_1(const float *in, uint8_t *out, size_t n) {
+    for (size_t b = 0; b < n / 32; b++) {
+        const float *src = in + b * 32;
+        uint8_t *blk = out + b * 36;
+        float amax = 0.0f;
+        for (int i = 0; i < 32; i++) {
+            const float a = fabsf(src[i]);
+            if (a > amax) amax = a;
+        }
+        const float d = amax / 127.0f;
+        const float inv_d = d != 0.0f ? 1.0f / d : 0.0f;
+        int32_t sum_qs = 0;
+        const uint16_t dh = orc_f32_to_f16(d);
+        blk[0] = (uint8_t)(dh & 0xff);
+        blk[1] = (uint8_t)(dh >> 8);
+        for (int i = 0; i < 32; i++) {
+            float q = roundf(src[i] * inv_d);
+            q = q < -127.0f ? -127.0f : (q > 127.0f ? 127.0f : q);
+            const int32_t qi = (int32_t)q;
+            sum_qs += qi;
+            blk[4 + i] = (uint8_t)(int8_t)qi;
+        }
+        const uint16_t sh = orc_f32_to_f16(d * (float)sum_qs);
+        blk[2] = (uint8_t)(sh & 0xff);
+        blk[3] = (uint8_t)(sh >> 8);
+    }
+}
+
+/* dequant.zig:549-558 */
+void orc_dequant_q8_1(const uint8_t *data, float *out, size_t n) {
+    for (size_t b = 0; b < n / 32; b++) {
+        const uint8_t *blk = data + b * 36;
+        const float d = f16_at(blk);
+        for (int i = 0; i < 32; i++) out[b * 32 + i] = d * (float)(int8_t)blk[4 + i];
+    }
+}
+
+/* dequant.zig:569-586: groups of four blocks as {ds[4], qs[4][32]}, the last
+ * group zero-padded. */
+void orc_pack_q8_1_x4(const uint8_t *basic, size_t n_blocks, uint8_t *x4) {
+    const size_t n_groups = (n_blocks + 3) / 4;
+    memset(x4, 0, n_groups * 144);
+    for (size_t bi = 0; bi < n_blocks; bi++) {
+        const size_t g = bi / 4, i = bi % 4;
+        memcpy(x4 + g * 144 + i * 4, basic + bi * 36, 4);
+        memcpy(x4 + g * 144 + 16 + i * 32, basic + bi * 36 + 4, 32);
+    }
+}
+
+/* dequant.zig:588-613 */
+void orc_unpack_q8_1_x4(const uint8_t *x4, size_t n_groups, uint8_t *basic) {
+    for (size_t g = 0; g < n_groups; g++)
+        for (int i = 0; i < 4; i++) {
+            memcpy(basic + (g * 4 + i) * 36, x4 + g * 144 + i * 4, 4);
+            memcpy(basic + (g * 4 + i) * 36 + 4, x4 + g * 144 + 16 + i * 32, 32);
+        }
+}
+
 /* math.zig:194-208 */
 size_t orc_row_bytes(uint32_t type, size_t cols) {
     switch (type) {
@@ -195,6 +415,11 @@ size_t orc_row_bytes(uint32_t type, size_t cols) {
     case ORC_Q8_0: return (cols / Q8_0_BLOCK_ELEMS) * Q8_0_BLOCK_BYTES;
     case ORC_Q4_K: return (cols / QK_K) * Q4_K_BLOCK_BYTES;
     case ORC_Q6_K: return (cols / QK_K) * Q6_K_BLOCK_BYTES;
+    case ORC_Q5_0: return (cols / 32) * 22;
+    case ORC_Q5_1: return (cols / 32) * 24;
+    case ORC_Q5_K: return (cols / QK_K) * 176;
+    case ORC_Q3_K: return (cols / QK_K) * 110;
+    case ORC_IQ4_NL: return (cols / 32) * 18;
     default: return 0;
     }
 }
@@ -207,6 +432,11 @@ int orc_dequant_row(const uint8_t *data, float *out, size_t n, uint32_t type) {
     case ORC_Q8_0: orc_dequant_q8_0(data, out, n); return 0;
     case ORC_Q4_K: orc_dequant_q4_k(data, out, n); return 0;
     case ORC_Q6_K: orc_dequant_q6_k(data, out, n); return 0;
+    case ORC_Q5_0: orc_dequant_q5_0(data, out, n); return 0;
+    case ORC_Q5_1: orc_dequant_q5_1(data, out, n); return 0;
+    case ORC_Q5_K: orc_dequant_q5_k(data, out, n); return 0;
+    case ORC_Q3_K: orc_dequant_q3_k(data, out, n); return 0;
+    case ORC_IQ4_NL: orc_dequant_iq4_nl(data, out, n); return 0;
     default: return -1;
     }
 }
@@ -252,6 +482,14 @@ static int quant_matvec_rows(float *out, const uint8_t *mat, uint32_t type, cons
         const uint8_t *row = mat + (row_start + i) * rb;
         if (type == ORC_Q8_0) {
             out[i] = orc_dot_q8_0(row, vec, cols);
+            continue;
+        }
+        if (type == ORC_Q5_0) {
+            out[i] = orc_dot_q5_0(row, vec, cols);
+            continue;
+        }
+        if (type == ORC_IQ4_NL) {
+            out[i] = orc_dot_iq4_nl(row, vec, cols);
             continue;
         }
         if (type == ORC_F32 && ((uintptr_t)row % 4) == 0) {

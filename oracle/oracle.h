@@ -30,7 +30,8 @@ extern "C" {
 
 /* GgmlType codes, src/gguf/types.zig:23-52 */
 enum {
-    ORC_F32 = 0, ORC_F16 = 1, ORC_Q8_0 = 8, ORC_Q4_K = 12, ORC_Q6_K = 14
+    ORC_F32 = 0, ORC_F16 = 1, ORC_Q5_0 = 6, ORC_Q5_1 = 7, ORC_Q8_0 = 8, ORC_Q3_K = 11, ORC_Q4_K = 12,
+    ORC_Q5_K = 13, ORC_Q6_K = 14, ORC_IQ4_NL = 20
 };
 
 /* f16 bits -> f32, exact (src/quant/dequant.zig:302-305) */
@@ -48,6 +49,19 @@ void orc_dequant_q8_0(const uint8_t *data, float *out, size_t n);  /* :42  */
 void orc_dequant_q4_k(const uint8_t *data, float *out, size_t n);  /* :157 */
 void orc_dequant_q6_k(const uint8_t *data, float *out, size_t n);  /* :237 */
 float orc_dot_q8_0(const uint8_t *data, const float *vec, size_t n); /* :59 */
+void orc_dequant_q5_0(const uint8_t *data, float *out, size_t n);   /* :201 */
+float orc_dot_q5_0(const uint8_t *data, const float *vec, size_t n); /* :92  */
+void orc_dequant_q5_1(const uint8_t *data, float *out, size_t n);   /* :469 */
+void orc_dequant_q5_k(const uint8_t *data, float *out, size_t n);   /* :324 */
+void orc_dequant_q3_k(const uint8_t *data, float *out, size_t n);   /* :388 */
+void orc_dequant_iq4_nl(const uint8_t *data, float *out, size_t n); /* :623 */
+float orc_dot_iq4_nl(const uint8_t *data, const float *vec, size_t n); /* :642 */
+/* Q8_1 activation blocks (36 B: f16 d, f16 s = d * sum q, 32 x i8) and the
+ * 4-block x4 layout, dequant.zig:508-613.  n is a multiple of 32. */
+void orc_quantize_q8_1(const float *in, uint8_t *out, size_t n);    /* :517 */
+void orc_dequant_q8_1(const uint8_t *data, float *out, size_t n);   /* :549 */
+void orc_pack_q8_1_x4(const uint8_t *basic, size_t n_blocks, uint8_t *x4);   /* :569 */
+void orc_unpack_q8_1_x4(const uint8_t *x4, size_t n_groups, uint8_t *basic); /* :588 */
 
 /* dequantRow, src/ops/math.zig:211-225.  Returns -1 for an unsupported type. */
 int orc_dequant_row(const uint8_t *data, float *out, size_t n, uint32_t type);

@@ -10,13 +10,19 @@ Two sources, both independent of oracle/oracle.c:
    non-zero Q4_K or any Q6_K known-answer test).  Each value is the f32 the
    reference's strict-float arithmetic produces: Q4_K's d1*q - m1 is one
    rounding of an exact quantity (d1*q and m1 are exact in f32), Q6_K's and
-   Q8_0's products are exact.
+   Q8_0's products are exact.  The same for Q5_0, Q5_1, Q5_K, Q3_K and IQ4_NL
+   (dequant.zig:196-217,307-506,615-640): Q5_1's d*q + m and Q5_K's d1*q - m1
+   are rounded once from the exact rational value; the other products are
+   exact.  Q8_1 activation blocks (dequant.zig:508-613) are quantised here with
+   numpy float32 arithmetic (IEEE-rounded division and products, halves
+   rounded away from zero as Zig's @round does, f16 by round-to-nearest-even).
 
 Run:  python tests/golden/gen_golden.py   (deterministic; rewrites golden.json)
 """
 from __future__ import annotations
 
 import json
+import math
 import struct
 from fractions import Fraction
 from pathlib import Path
@@ -82,6 +88,136 @@ def q4k_decode(blk: bytes) -> list[int]:
     return out
 
 
+def f32_round_exact(x: Fraction) -> int:
+    """Bit pattern of the f32 nearest to the rational x (ties to even)."""
+    if x == 0:
+        return 0x80000000 if x < 0 else 0
+    sign = 0x80000000 if x < 0 else 0
+    a = abs(x)
+    e = a.numerator.bit_length() - a.denominator.bit_length()
+    if Fraction(2) ** e > a:
+        e -= 1
+    e = max(e, -126)
+    m = a / Fraction(2) ** (e - 23)  # in [2^23, 2^24) for normals
+    q, r = divmod(m.numerator, m.denominator)
+    if 2 * r > m.denominator or (2 * r == m.denominator and q & 1):
+        q += 1
+    if q >= 1 << 24:
+        q >>= 1
+        e += 1
+    if q < 1 << 23:  # subnormal
+        return sign | q
+    return sign | ((e + 127) << 23) | (q - (1 << 23))
+
+
+def f32_of(exact: Fraction, approx: float) -> int:
+    """One rounding of an exact sum; an exact zero takes its sign from the
+    same sum in double, which follows IEEE's signed-zero rules."""
+    return f32_bits(approx) if exact == 0 else f32_round_exact(exact)
+
+
+def q5_bits(qh: int, qs: bytes) -> list[int]:
+    """The 32 five-bit values: element j < 16 = low nibble of qs[j] | bit j of
+    qh << 4, element j + 16 = high nibble | bit j + 16 << 4."""
+    return [((qs[e] & 15) if e < 16 else (qs[e - 16] >> 4)) | (((qh >> e) & 1) << 4) for e in range(32)]
+
+
+def q5_0_decode(blk: bytes) -> list[int]:
+    d = f16_value(blk[0] | blk[1] << 8)
+    qh = int.from_bytes(blk[2:6], "little")
+    return [f32_bits(float(d) * (v - 16)) for v in q5_bits(qh, blk[6:22])]  # exact products
+
+
+def q5_1_decode(blk: bytes) -> list[int]:
+    d, m = f16_value(blk[0] | blk[1] << 8), f16_value(blk[2] | blk[3] << 8)
+    qh = int.from_bytes(blk[4:8], "little")
+    # d * q is exact in f32 (11 x 5 bits); the sum rounds once
+    return [f32_of(d * v + m, float(d) * v + float(m)) for v in q5_bits(qh, blk[8:24])]
+
+
+IQ4_TABLE = [-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113]
+
+
+def iq4nl_decode(blk: bytes) -> list[int]:
+    d = f16_value(blk[0] | blk[1] << 8)
+    nib = [(blk[2 + e] & 15) if e < 16 else (blk[2 + e - 16] >> 4) for e in range(32)]
+    return [f32_bits(float(d) * IQ4_TABLE[n]) for n in nib]
+
+
+def q5k_decode(blk: bytes) -> list[int]:
+    d, dmin = f16_value(blk[0] | blk[1] << 8), f16_value(blk[2] | blk[3] << 8)
+    scales, qh, ql = blk[4:16], blk[16:48], blk[48:176]
+    out = [0] * 256
+    for e in range(256):
+        c, p = divmod(e, 64)
+        up = 1 if p >= 32 else 0
+        byte = ql[32 * c + (p & 31)]
+        q = (byte >> 4 if up else byte & 15) + 16 * ((qh[p & 31] >> (2 * c + up)) & 1)
+        sc, mn = k4_scale_min(2 * c + up, scales)
+        # d*sc, dmin*mn and d1*q are exact in f32; the difference rounds once
+        out[e] = f32_of(d * sc * q - dmin * mn, float(d) * sc * q - float(dmin) * mn)
+    return out
+
+
+def q3k_scales(s: bytes) -> list[int]:
+    """16 six-bit scales: low nibbles of bytes 0-7 then their high nibbles,
+    each with two high bits from byte 8 + k % 4 at bit 2 * (k // 4)."""
+    out = []
+    for k in range(16):
+        w, b = divmod(k, 4)
+        byte = s[4 * (w & 1) + b]
+        lo = byte >> 4 if w & 2 else byte & 15
+        out.append(lo | (((s[8 + b] >> (2 * w)) & 3) << 4))
+    return out
+
+
+def q3k_decode(blk: bytes) -> list[int]:
+    hmask, qs, sc = blk[0:32], blk[32:96], q3k_scales(blk[96:108])
+    d = f16_value(blk[108] | blk[109] << 8)
+    out = [0] * 256
+    for e in range(256):
+        h, r = divmod(e, 128)
+        j, r2 = divmod(r, 32)
+        g, l = divmod(r2, 16)
+        lo2 = (qs[32 * h + 16 * g + l] >> (2 * j)) & 3
+        hb = (hmask[16 * g + l] >> (4 * h + j)) & 1
+        out[e] = f32_bits(float(lo2 - (0 if hb else 4)) * (float(d) * (sc[8 * h + 2 * j + g] - 32)))
+    return out
+
+
+def pack_q3k_scales(sc: list[int]) -> bytes:
+    b = bytearray(12)
+    for k, v in enumerate(sc):
+        w, i = divmod(k, 4)
+        if w & 2:
+            b[4 * (w & 1) + i] |= (v & 15) << 4
+        else:
+            b[4 * (w & 1) + i] |= v & 15
+        b[8 + i] |= ((v >> 4) & 3) << (2 * w)
+    return bytes(b)
+
+
+def q8_1_quantize(x: np.ndarray) -> bytes:
+    """quantizeQ8_1 (dequant.zig:517-547) in numpy float32 arithmetic."""
+    out = bytearray()
+    for b in range(len(x) // 32):
+        src = np.asarray(x[32 * b:32 * b + 32], dtype=np.float32)
+        amax = np.float32(0)
+        for v in src:
+            if abs(v) > amax:
+                amax = np.float32(abs(v))
+        d = np.float32(amax / np.float32(127.0))
+        inv = np.float32(np.float32(1.0) / d) if d != 0 else np.float32(0)
+        qs = []
+        for v in src:
+            t = float(np.float32(v * inv))
+            q = math.floor(abs(t) + 0.5) * (1 if t >= 0 else -1)
+            qs.append(int(min(127, max(-127, q))))
+        s = np.float32(d * np.float32(sum(qs)))
+        out += np.float16(d).tobytes() + np.float16(s).tobytes() + bytes(q & 0xFF for q in qs)
+    return bytes(out)
+
+
 def q6k_decode(blk: bytes) -> list[int]:
     ql, qh, sc = blk[0:128], blk[128:192], blk[192:208]
     d = float(f16_value(blk[208] | blk[209] << 8))
@@ -145,6 +281,25 @@ def dequant_cases() -> list[dict]:
     cases.append({"name": "q6k_hand", "type": 14, "cols": 256, "hex": blk.hex(), "expect": q6k_decode(blk)})
     blk = bytes([0xFF] * 128) + bytes([0xFF] * 64) + bytes([0x80, 0x7F] * 8) + h16(-0.75)
     cases.append({"name": "q6k_extremes", "type": 14, "cols": 256, "hex": blk.hex(), "expect": q6k_decode(blk)})
+    # hand-built Q5_0 / Q5_1 / IQ4_NL blocks: every nibble and fifth-bit position
+    qs = bytes(((j * 11 + 7) & 0xFF) for j in range(16))
+    blk = h16(0.5) + (0xA5C3F00F).to_bytes(4, "little") + qs
+    cases.append({"name": "q5_0_hand", "type": 6, "cols": 32, "hex": blk.hex(), "expect": q5_0_decode(blk)})
+    blk = h16(-0.0625) + h16(3.0) + (0x5A3C0FF0).to_bytes(4, "little") + qs
+    cases.append({"name": "q5_1_hand", "type": 7, "cols": 32, "hex": blk.hex(), "expect": q5_1_decode(blk)})
+    blk = bytes([0x01, 0x00]) + h16(1e-7) + (0xFFFFFFFF).to_bytes(4, "little") + bytes([0xFF] * 16)
+    cases.append({"name": "q5_1_subnormal_d", "type": 7, "cols": 32, "hex": blk.hex(), "expect": q5_1_decode(blk)})
+    blk = h16(1.0) + bytes((i & 15) | ((15 - i) << 4) for i in range(16))
+    cases.append({"name": "iq4_nl_table", "type": 20, "cols": 32, "hex": blk.hex(), "expect": iq4nl_decode(blk)})
+    # hand-built Q5_K (Q4_K's scales, every qh bit plane) and Q3_K (all 16 scales incl. 0 and 63)
+    blk = h16(0.5) + h16(0.25) + pack_k4_scales(sc, mn) + bytes(((k * 37 + 1) & 0xFF) for k in range(32)) + \
+        bytes(((k * 7 + 3) & 0xFF) for k in range(128))
+    cases.append({"name": "q5k_hand", "type": 13, "cols": 256, "hex": blk.hex(), "expect": q5k_decode(blk)})
+    s3 = [0, 63, 32, 1, 31, 33, 17, 48, 5, 60, 40, 24, 12, 50, 2, 61]
+    blk = bytes(((k * 53 + 9) & 0xFF) for k in range(32)) + bytes(((k * 91 + 4) & 0xFF) for k in range(64)) + \
+        pack_q3k_scales(s3) + h16(0.01)
+    assert q3k_scales(pack_q3k_scales(s3)) == s3
+    cases.append({"name": "q3k_hand", "type": 11, "cols": 256, "hex": blk.hex(), "expect": q3k_decode(blk)})
     # seeded random superblocks, two per format, multi-block rows
     rng = np.random.Generator(np.random.PCG64(20261201))
     for t, nb, dec, nbytes, elems in ((12, 2, q4k_decode, 144, 256), (14, 2, q6k_decode, 210, 256),
@@ -163,6 +318,70 @@ def dequant_cases() -> list[dict]:
             expect += dec(bytes(raw[b * nbytes:(b + 1) * nbytes]))
         cases.append({"name": f"random_type{t}", "type": t, "cols": nb * elems, "hex": bytes(raw).hex(),
                       "expect": expect})
+    # the same for the further formats (a separate stream, so the cases above stay as they were)
+    rng = np.random.Generator(np.random.PCG64(20261202))
+    for t, nb, dec, nbytes, elems, scale_offs in ((6, 3, q5_0_decode, 22, 32, (0,)), (7, 3, q5_1_decode, 24, 32, (0, 2)),
+                                                  (20, 3, iq4nl_decode, 18, 32, (0,)),
+                                                  (13, 2, q5k_decode, 176, 256, (0, 2)),
+                                                  (11, 2, q3k_decode, 110, 256, (108,))):
+        raw = bytearray(rng.integers(0, 256, size=nb * nbytes, dtype=np.uint8).tobytes())
+        for b in range(nb):
+            for o in scale_offs:
+                raw[b * nbytes + o:b * nbytes + o + 2] = h16(float(rng.uniform(-4e-3, 4e-3)))
+        expect = []
+        for b in range(nb):
+            expect += dec(bytes(raw[b * nbytes:(b + 1) * nbytes]))
+        cases.append({"name": f"random_type{t}", "type": t, "cols": nb * elems, "hex": bytes(raw).hex(),
+                      "expect": expect})
+    return cases
+
+
+def dot_q5_0_case() -> dict:
+    # dequant.zig:716-735: block 0 d=0.5, qh=0xAAAAAAAA, qs[j] = j | (j+3)<<4;
+    # block 1 d=0.125, qh=0, qs all 0x55; vec[i] = i*0.1 - 3.0;
+    # dotQ5_0 == dequant + scalar dot within 1e-3
+    data = bytearray(44)
+    data[0], data[1] = 0x00, 0x38
+    data[2:6] = bytes([0xAA] * 4)
+    for j in range(16):
+        data[6 + j] = (j & 15) | (((j + 3) & 15) << 4)
+    data[22], data[23] = 0x00, 0x30
+    data[28:44] = bytes([0x55] * 16)
+    vec = [np.float32(np.float32(i) * np.float32(0.1)) - np.float32(3.0) for i in range(64)]
+    dec = [bits_to_f32(b) for b in q5_0_decode(bytes(data[:22])) + q5_0_decode(bytes(data[22:]))]
+    exp = np.float32(0)
+    for d, v in zip(dec, vec):
+        exp = np.float32(exp + np.float32(np.float32(d) * v))
+    return {"hex": data.hex(), "vec": [float(v) for v in vec], "expect": float(exp), "tol": 1e-3}
+
+
+def dot_iq4_nl_case() -> dict:
+    # dequant.zig:737-758: block 0 d=1, qs[i] = i | (15-i)<<4; block 1 d=2,
+    # qs[i] = (i+3)&15 | ((i+5)&15)<<4; vec[i] = ((i % 7) + 1) * 0.25
+    data = bytearray(36)
+    data[0], data[1] = 0x00, 0x3C
+    data[18], data[19] = 0x00, 0x40
+    for i in range(16):
+        data[2 + i] = (i & 15) | ((15 - i) << 4)
+        data[20 + i] = ((i + 3) & 15) | (((i + 5) & 15) << 4)
+    vec = [np.float32((i % 7) + 1) * np.float32(0.25) for i in range(64)]
+    dec = [bits_to_f32(b) for b in iq4nl_decode(bytes(data[:18])) + iq4nl_decode(bytes(data[18:]))]
+    exp = np.float32(0)
+    for d, v in zip(dec, vec):
+        exp = np.float32(exp + np.float32(np.float32(d) * v))
+    return {"hex": data.hex(), "vec": [float(v) for v in vec], "expect": float(exp), "tol": 1e-3}
+
+
+def q8_1_cases() -> list[dict]:
+    cases = []
+    # halves that round away from zero (d = 1 exactly: amax 127)
+    x = np.zeros(32, np.float32)
+    x[:8] = [127.0, 2.5, -3.5, 0.5, -0.5, 126.5, -126.5, 1.49]
+    cases.append({"name": "q8_1_halves", "x": [float(v) for v in x], "hex": q8_1_quantize(x).hex()})
+    cases.append({"name": "q8_1_zero_block", "x": [0.0] * 32, "hex": q8_1_quantize(np.zeros(32, np.float32)).hex()})
+    rng = np.random.Generator(np.random.PCG64(20261203))
+    x = rng.normal(0, 1.5, 96).astype(np.float32)
+    cases.append({"name": "q8_1_random", "x": [float(v) for v in x], "hex": q8_1_quantize(x).hex()})
     return cases
 
 
@@ -238,7 +457,8 @@ def misc_cases() -> dict:
 
 def main() -> None:
     g = {"comment": "generated by tests/golden/gen_golden.py; f32 values stored as bit patterns",
-         "dequant": dequant_cases(), "dot_q8_0": dot_q8_0_case(), "router": router_cases(),
+         "dequant": dequant_cases(), "dot_q8_0": dot_q8_0_case(), "dot_q5_0": dot_q5_0_case(),
+         "dot_iq4_nl": dot_iq4_nl_case(), "q8_1": q8_1_cases(), "router": router_cases(),
          "misc": misc_cases()}
     OUT.write_text(json.dumps(g, indent=1, default=float) + "\n")
     print(f"wrote {OUT} ({OUT.stat().st_size} bytes)")

@@ -15,6 +15,7 @@ REPO = Path(__file__).resolve().parent.parent
 LIB = REPO / "oracle" / "liboracle.so"
 
 F32, F16, Q8_0, Q4_K, Q6_K = 0, 1, 8, 12, 14
+Q5_0, Q5_1, Q3_K, Q5_K, IQ4_NL = 6, 7, 11, 13, 20
 
 
 class SoftmaxStats(ctypes.Structure):
@@ -38,6 +39,12 @@ def lib() -> ctypes.CDLL:
         "orc_row_bytes": (SZ, [U32, SZ]),
         "orc_dequant_row": (I, [P, P, SZ, U32]),
         "orc_dot_q8_0": (F, [P, P, SZ]),
+        "orc_dot_q5_0": (F, [P, P, SZ]),
+        "orc_dot_iq4_nl": (F, [P, P, SZ]),
+        "orc_quantize_q8_1": (None, [P, P, SZ]),
+        "orc_dequant_q8_1": (None, [P, P, SZ]),
+        "orc_pack_q8_1_x4": (None, [P, SZ, P]),
+        "orc_unpack_q8_1_x4": (None, [P, SZ, P]),
         "orc_dotf32": (F, [P, P, SZ]),
         "orc_matvec": (None, [P, P, P, SZ, SZ]),
         "orc_quant_matvec": (I, [P, P, U32, P, SZ, SZ, P]),
@@ -109,6 +116,20 @@ def dequant(data: np.ndarray, t: int, rows: int, cols: int) -> np.ndarray:
     for r in range(rows):
         rc = lib().orc_dequant_row(data[r * rb:].ctypes.data, out[r].ctypes.data, cols, t)
         assert rc == 0
+    return out
+
+
+def quantize_q8_1(x) -> bytes:
+    x = f32(x)
+    out = np.zeros(x.size // 32 * 36, np.uint8)
+    lib().orc_quantize_q8_1(_p(x), _p(out), x.size)
+    return out.tobytes()
+
+
+def dequant_q8_1(data: bytes, n: int) -> np.ndarray:
+    raw = np.frombuffer(data, np.uint8).copy()
+    out = np.empty(n, np.float32)
+    lib().orc_dequant_q8_1(_p(raw), _p(out), n)
     return out
 
 

@@ -64,12 +64,16 @@ def test_model_file_round_trip(tmp_path):
 
 def test_info_lists_undecodable_types(tmp_path):
     decoder, gguf, _ = _mods()
-    q3k = np.zeros(110 * 2, np.uint8)  # two Q3_K superblocks (256 x 2)
+    q40 = np.zeros(18 * 4, np.uint8)  # four Q4_0 blocks (64 x 2): no decoder here (nor in math.zig:194-225)
+    q3k = np.zeros(110 * 2, np.uint8)  # two Q3_K superblocks (256 x 2): decodable
     gguf.write_gguf(tmp_path / "x.gguf", {"general.architecture": "llama", "general.name": "x"},
-                    [("a.weight", 11, [256, 2], q3k), ("b.weight", 0, [4], np.zeros(4, np.float32))])
+                    [("a.weight", 2, [64, 2], q40), ("b.weight", 0, [4], np.zeros(4, np.float32)),
+                     ("c.weight", 11, [256, 2], q3k)])
     with decoder.GgufFile(tmp_path / "x.gguf") as g:
         info = g.info()
-        assert "[q3_k] a.weight  dims={ 256, 2 }" in info
+        unsupported = info.split("unsupported GPU quant tensors:")[1].split("first 16 tensors:")[0]
+        assert "[q4_0] a.weight  dims={ 64, 2 }" in unsupported
+        assert "c.weight" not in unsupported and "q3_k: 1" in info
         assert "name:      x" in info
 
 

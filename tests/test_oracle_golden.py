@@ -27,7 +27,14 @@ def test_row_bytes_matches_types_table(oracle):
     assert oracle.row_bytes(oracle.Q4_K, 2048) == 8 * 144
     assert oracle.row_bytes(oracle.Q6_K, 2816) == 11 * 210
     assert oracle.row_bytes(oracle.F32, 5) == 20
+    # src/gguf/types.zig:150-166 for the further formats
+    assert oracle.row_bytes(oracle.Q5_0, 64) == 2 * 22
+    assert oracle.row_bytes(oracle.Q5_1, 64) == 2 * 24
+    assert oracle.row_bytes(oracle.IQ4_NL, 64) == 2 * 18
+    assert oracle.row_bytes(oracle.Q5_K, 512) == 2 * 176
+    assert oracle.row_bytes(oracle.Q3_K, 512) == 2 * 110
     assert oracle.row_bytes(99, 256) == 0  # unsupported type
+    assert oracle.row_bytes(9, 256) == 0  # Q8_1 is an activation format, not a matrix type (math.zig:194-208)
 
 
 def test_dot_q8_0_matches_dequant_dot(oracle, golden):
@@ -36,6 +43,80 @@ def test_dot_q8_0_matches_dequant_dot(oracle, golden):
     vec = np.array(c["vec"], dtype=np.float32)
     got = oracle.lib().orc_dot_q8_0(raw.ctypes.data, vec.ctypes.data, 64)
     assert abs(got - c["expect"]) <= c["tol"]
+
+
+@pytest.mark.parametrize("key,fn", [("dot_q5_0", "orc_dot_q5_0"), ("dot_iq4_nl", "orc_dot_iq4_nl")])
+def test_fused_dots_match_dequant_dot(oracle, golden, key, fn):
+    """dequant.zig:716-758: dotQ5_0 / dotIQ4NL == dequant + scalar dot (1e-3)."""
+    c = golden[key]
+    raw = np.frombuffer(bytes.fromhex(c["hex"]), dtype=np.uint8)
+    vec = np.array(c["vec"], dtype=np.float32)
+    got = getattr(oracle.lib(), fn)(raw.ctypes.data, vec.ctypes.data, 64)
+    assert abs(got - c["expect"]) <= c["tol"]
+
+
+@pytest.mark.parametrize("t", [6, 20, 7, 13, 11])
+def test_quant_matvec_paths(oracle, t):
+    """quantMatvec (math.zig:133-171): Q5_0 and IQ4_NL rows go through their
+    fused dots, the others through dequantRow + dotf32."""
+    synth = pytest.importorskip("importlib").import_module("llmtoy-zig_b200.synth")
+    rng = np.random.default_rng(t)
+    cols = 512
+    mat = synth.matrix(rng, t, 5, cols)
+    vec = rng.normal(0, 1, cols).astype(np.float32)
+    got = oracle.quant_matvec(mat, t, vec, 5, cols)
+    rb = oracle.row_bytes(t, cols)
+    for r in range(5):
+        row = np.ascontiguousarray(mat.reshape(-1)[r * rb:(r + 1) * rb])
+        if t in (6, 20):
+            fn = oracle.lib().orc_dot_q5_0 if t == 6 else oracle.lib().orc_dot_iq4_nl
+            want = fn(row.ctypes.data, vec.ctypes.data, cols)
+        else:
+            deq = np.ascontiguousarray(oracle.dequant(row, t, 1, cols)[0])
+            want = oracle.lib().orc_dotf32(deq.ctypes.data, vec.ctypes.data, cols)
+        assert np.float32(got[r]) == np.float32(want)
+
+
+def test_q8_1_golden(oracle, golden):
+    """quantizeQ8_1 bit-exact against the fixture (halves away from zero, zero
+    blocks, random rows)."""
+    for c in golden["q8_1"]:
+        assert oracle.quantize_q8_1(c["x"]).hex() == c["hex"], c["name"]
+
+
+def test_q8_1_roundtrip_within_bound(oracle):
+    """dequant.zig:768-794: |dequant(quantize(x)) - x| <= amax/127 (+1e-5), the
+    inputs drawn from DefaultPrng(0xC0FFEE) as the reference's test does."""
+    r = oracle.Rng(0xC0FFEE)
+    x = np.array([(r.float() - 0.5) * 4.0 for _ in range(128)], np.float32)
+    dec = oracle.dequant_q8_1(oracle.quantize_q8_1(x), 128)
+    for b in range(4):
+        blk = x[32 * b:32 * b + 32]
+        assert np.all(np.abs(dec[32 * b:32 * b + 32] - blk) <= np.abs(blk).max() / 127.0 + 1e-5)
+
+
+def test_q8_1_sum_term(oracle):
+    """dequant.zig:796-815: the stored s equals d * sum(q) within 1e-2."""
+    r = oracle.Rng(7)
+    x = np.array([(r.float() - 0.5) * 3.0 for _ in range(32)], np.float32)
+    b = np.frombuffer(oracle.quantize_q8_1(x), np.uint8)
+    d, s = (float(np.frombuffer(b[i:i + 2].tobytes(), np.float16)[0]) for i in (0, 2))
+    assert abs(d * int(b[4:].view(np.int8).astype(np.int64).sum()) - s) <= 1e-2
+
+
+def test_q8_1_x4_roundtrip(oracle):
+    """dequant.zig:817-829: pack / unpack of one x4 group is byte-exact; a
+    partial last group is zero-padded."""
+    rng = np.random.default_rng(11)
+    basic = rng.integers(0, 256, 4 * 36, dtype=np.uint8)
+    x4 = np.zeros(144, np.uint8)
+    oracle.lib().orc_pack_q8_1_x4(basic.ctypes.data, 4, x4.ctypes.data)
+    back = np.zeros(144, np.uint8)
+    oracle.lib().orc_unpack_q8_1_x4(x4.ctypes.data, 1, back.ctypes.data)
+    assert back.tobytes() == basic.tobytes()
+    x4 = np.full(288, 7, np.uint8)
+    oracle.lib().orc_pack_q8_1_x4(basic.ctypes.data, 3, x4.ctypes.data)
+    assert x4[12:16].tolist() == [0] * 4 and x4[16 + 96:144].tolist() == [0] * 32 and x4[144:].tolist() == [7] * 144
 
 
 def test_quant_matvec_f32_equals_matvec(oracle, golden):
@@ -170,7 +251,7 @@ def test_greedy_lowest_index(oracle, golden):
     assert oracle.greedy(v) == a[1]["expect"]
 
 
-@pytest.mark.parametrize("t", [12, 14, 8])
+@pytest.mark.parametrize("t", [12, 14, 8, 6, 7, 11, 13, 20])
 def test_golden_regenerates_identically(t, golden):
     """The committed fixture equals what gen_golden.py derives (no drift)."""
     import importlib.util
