@@ -61,6 +61,21 @@ LT_DEVINL float f16_bits_to_f32(uint32_t h) {
     return __half2float(__ushort_as_half((unsigned short)(h & 0xffffu)));
 }
 
+// IEEE f32 -> f16 bits, round to nearest even (what Zig's @floatCast does),
+// in integer arithmetic: normals by mantissa rounding, subnormals as the
+// nearest integer multiple of 2^-24, overflow to infinity.
+LT_DEVINL uint32_t f32_to_f16_bits(float f) {
+    const uint32_t x = __float_as_uint(f);
+    const uint32_t sign = (x >> 16) & 0x8000u, ax = x & 0x7fffffffu;
+    if (ax >= 0x7f800000u) return sign | 0x7c00u | (ax > 0x7f800000u ? 0x200u : 0u);
+    if (ax >= 0x477ff000u) return sign | 0x7c00u;
+    if (ax < 0x38800000u) return sign | (uint32_t)__float2int_rn(__uint_as_float(ax) * 16777216.0f);
+    uint32_t r = (((ax >> 23) - 112u) << 10) | ((ax >> 13) & 0x3ffu);
+    const uint32_t rem = ax & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (r & 1u))) r++;
+    return sign | r;
+}
+
 // Read-only 128-bit global load (weights are never written while a kernel
 // runs), allocated in L1 only if it streams: weights are touched once.
 LT_DEVINL uint4 ldg_stream(const void *p) {

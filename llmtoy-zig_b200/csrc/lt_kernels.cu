@@ -294,12 +294,11 @@ __global__ void k_quantize_q8_1(const float *x, uint64_t nb, uint64_t nb_pad, in
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
         qs[lane] = (uint8_t)(int8_t)qi;
         if (lane == 0) {
-            const unsigned short dh = __half_as_ushort(__float2half_rn(d));
-            const unsigned short sh = __half_as_ushort(__float2half_rn(__fmul_rn(d, (float)sum)));
-            ds[0] = (uint8_t)(dh & 0xff);
-            ds[1] = (uint8_t)(dh >> 8);
-            ds[2] = (uint8_t)(sh & 0xff);
-            ds[3] = (uint8_t)(sh >> 8);
+            const uint32_t w = f32_to_f16_bits(d) | f32_to_f16_bits(__fmul_rn(d, (float)sum)) << 16;
+            ds[0] = (uint8_t)w;
+            ds[1] = (uint8_t)(w >> 8);
+            ds[2] = (uint8_t)(w >> 16);
+            ds[3] = (uint8_t)(w >> 24);
         }
     }
 }

@@ -24,7 +24,11 @@ def _torch():
 
 
 def dev(a: np.ndarray):
-    return _torch().from_numpy(np.ascontiguousarray(a)).cuda()
+    """A device copy, complete before returning: the context runs on its own
+    stream, which does not wait for the copy engine's work on torch's."""
+    t = _torch().from_numpy(np.ascontiguousarray(a)).cuda()
+    _torch().cuda.synchronize()
+    return t
 
 
 def empty(n, dtype="float32"):

@@ -86,7 +86,6 @@ def _run(ctx, pkg, oracle, n, temp, k, tp, seed, draws, scale=3.0, ties=False):
         if ties:
             lg = np.round(lg * 2) / 2
         lgd = dev(lg)
-        host(lgd[:1])  # the copy is complete before the context's stream reads it
         ctx.sample_step(lgd, n, params, st.rng, st.toks, st.state[0:1], st.state[1:2])
         before = ref.copy()
         want = oracle.sample(lg, temp, k, tp, ref)
