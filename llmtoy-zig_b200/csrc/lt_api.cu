@@ -46,6 +46,8 @@ struct lt_ctx {
     uint8_t *pinned = nullptr;       // pinned staging for the host-buffer entry points
     size_t pinned_bytes = 0;
     bool capturing = false;          // between lt_capture_begin and lt_capture_end
+    cudaStream_t cap_user = nullptr; // the caller's stream while a capture runs on `own`
+    cudaEvent_t cap_ev = nullptr;    // joins `own` to the caller's stream for such a capture
     lt::Profiler prof;
 };
 
@@ -329,6 +331,7 @@ void lt_free(lt_ctx *ctx) {
     if (ctx->ones) cudaFree(ctx->ones);
     if (ctx->zeros) cudaFree(ctx->zeros);
     if (ctx->pinned) cudaFreeHost(ctx->pinned);
+    if (ctx->cap_ev) cudaEventDestroy(ctx->cap_ev);
     if (ctx->own) cudaStreamDestroy(ctx->own);
     delete ctx;
 }
@@ -377,7 +380,22 @@ lt_status lt_capture_begin(lt_ctx *ctx) {
     if (st != LT_OK) return st;
     if (ctx->capturing) return fail(ctx, LT_EINVAL, "lt_capture_begin: already capturing");
     if (ctx->prof.on) return fail(ctx, LT_EINVAL, "lt_capture_begin: turn profiling off first");
-    LT_CUDA(ctx, cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+    ctx->cap_user = nullptr;
+    if (ctx->stream == cudaStreamLegacy || ctx->stream == cudaStreamPerThread) {
+        // the default streams cannot be captured: capture on the context's own
+        // stream, ordered after the caller's work; the graph launches on any stream
+        if (!ctx->cap_ev) LT_CUDA(ctx, cudaEventCreateWithFlags(&ctx->cap_ev, cudaEventDisableTiming), "cudaEventCreate");
+        LT_CUDA(ctx, cudaEventRecord(ctx->cap_ev, ctx->stream), "cudaEventRecord");
+        LT_CUDA(ctx, cudaStreamWaitEvent(ctx->own, ctx->cap_ev, 0), "cudaStreamWaitEvent");
+        ctx->cap_user = ctx->stream;
+        ctx->stream = ctx->own;
+    }
+    cudaError_t e = cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) {
+        if (ctx->cap_user) ctx->stream = ctx->cap_user;
+        ctx->cap_user = nullptr;
+        return cuda_fail(ctx, e, "cudaStreamBeginCapture");
+    }
     ctx->capturing = true;
     return LT_OK;
 }
@@ -388,7 +406,10 @@ lt_status lt_capture_end(lt_ctx *ctx, lt_graph **out) {
     if (!ctx->capturing) return fail(ctx, LT_EINVAL, "lt_capture_end: not capturing");
     ctx->capturing = false;
     cudaGraph_t g = nullptr;
-    LT_CUDA(ctx, cudaStreamEndCapture(ctx->stream, &g), "cudaStreamEndCapture");
+    const cudaError_t ce = cudaStreamEndCapture(ctx->stream, &g);
+    if (ctx->cap_user) ctx->stream = ctx->cap_user;
+    ctx->cap_user = nullptr;
+    LT_CUDA(ctx, ce, "cudaStreamEndCapture");
     if (!out) {
         cudaGraphDestroy(g);
         return fail(ctx, LT_EINVAL, "lt_capture_end: null output");

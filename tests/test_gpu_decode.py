@@ -179,7 +179,7 @@ def test_decode_stack_graph_replay(ctx, multi_ctx, config1_layer_decode):
                     results.append(bits(host(xg)))
                 graph.free()
             finally:
-                c.set_stream(torch.cuda.current_stream())
+                c.set_stream(None)  # back to the context's own stream (the session fixture's choice)
         for t_ in tensors:
             if t_ is not None:
                 t_.free()

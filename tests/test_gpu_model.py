@@ -313,3 +313,23 @@ def test_gemma_config3_shape_vs_oracle(ctx, oracle, pool):
     m = synth.GemmaModel(np.random.default_rng(42), n_layers=6, vocab=4096, sliding_window=8, norms_random=True,
                          lm_type=8)
     _compare_gemma(ctx, oracle, pool, m, [7, 70, 700, 4000, 1, 2, 3, 4, 5, 6], 6)
+
+
+def test_decoder_graph_on_default_stream(pkg, oracle, pool):
+    """A context on the legacy default stream (which CUDA cannot capture)
+    still replays generations as a graph: the capture runs on the context's
+    own stream, ordered after the caller's work, and launches on the caller's."""
+    import torch
+    synth, decoder = _mods()
+    m = synth.DecoderModel(np.random.default_rng(31), 2, 256, 4, 2, 64, 700, d_ffn=512, norms_random=True)
+    c = pkg.Context(0)
+    c.set_stream(torch.cuda.current_stream())
+    try:
+        spec = decoder.upload_decoder(c, m, kv_cap=64)
+        dec = decoder.Decoder(c, spec)
+        ref = oracle.OracleDecoder(m, 64, pool).generate([4, 2, 9], 6)[0]
+        assert dec.generate([4, 2, 9], 6) == ref
+        assert dec.generate([4, 2, 9], 6) == ref
+        dec.close()
+    finally:
+        c.close()
