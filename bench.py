@@ -562,13 +562,14 @@ MODEL_CFG = {
 def model_bytes_per_token(name: str, ctx_len: float) -> float:
     """Algorithmic HBM bytes of one decode step: every weight the token reads
     (attention projections, router + 8 experts or the dense FFN, norms, the
-    embedding row, lm_head) plus the KV cache read at the mean context."""
+    embedding row, lm_head) plus the KV cache read at the mean context
+    (f16 elements for config 2, whose cache the config specifies as f16)."""
     L, d, nh, nkv, hd, V, F, lm, _, _, moe = MODEL_CFG[name]
     q8 = lambda r, c: r * (c // 32) * 34  # noqa: E731
     attn = q8(nh * hd + 2 * nkv * hd, d) + q8(d, nh * hd)
     ffn = TOP_K * EXPERT_BYTES + ROUTER_BYTES if moe else 3 * q8(F, d)
     lm_bytes = V * (d // 256) * 210 if lm == "q6_k" else q8(V, d)
-    kv = 2 * ctx_len * nkv * hd * 4
+    kv = 2 * ctx_len * nkv * hd * (2 if name == "config2" else 4)
     return L * (attn + ffn + kv + 2 * d * 4) + lm_bytes + q8(1, d)
 
 
@@ -614,7 +615,8 @@ def measure_model_decode(args, pkg, ctx, torch, stream, moe_layers, rank, world,
         up(q8_0_bytes_device(torch, gen, V, d), pkg.Q8_0, V, d)
     spec = decoder.ModelSpec(d_model=d, n_heads=nh, n_kv_heads=nkv, head_dim=hd, vocab=V, token_emb=emb,
                              lm_head=lmh, out_norm=ones(d), layers=specs, n_used=TOP_K if moe else 0,
-                             norm_topk=moe, rope_neox=neox, eps=1e-6, rope_theta=1e6, kv_cap=cap)
+                             norm_topk=moe, rope_neox=neox, eps=1e-6, rope_theta=1e6, kv_cap=cap,
+                             kv_f16=name == "config2")
     torch.cuda.synchronize()
     prompt = np.random.Generator(np.random.PCG64(0x11A70000 + (2 if moe else 0))).integers(0, V, n_prompt).tolist()
     steps = n_prompt + n_gen - 1
@@ -669,6 +671,7 @@ def measure_model_decode(args, pkg, ctx, torch, stream, moe_layers, rank, world,
         "metric": f"greedy decode tok/s ({name}: {'Qwen3-30B-A3B' if moe else 'Qwen2-0.5B'} shape, {L} layers)",
         "value": world / (ms_step / 1e3), "unit": "tok/s", "ms_per_token": ms_step, "steps": steps,
         "prompt_tokens": n_prompt, "generated_tokens": n_gen, "scaling": "weak",
+        "kv_cache": {"dtype": "f16" if name == "config2" else "f32", "capacity": cap},
         "deterministic_stream": deterministic,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": kind, "algorithmic_bytes_per_token": bpt,

@@ -307,6 +307,8 @@ typedef struct lt_attn_cfg {
     uint32_t kv_cap;     /* positions per layer cache; slot = pos % kv_cap */
     uint32_t window;     /* 0: attend to every position; else the last `window` (sliding) */
     uint32_t v_norm;     /* 1: RMSNorm without weights on each V head (gemma4/forward.zig:269) */
+    uint32_t kv_f16;     /* 1: the caches hold IEEE f16 elements (stored rounded to nearest even, as the
+                            reference's GPU cache does); 0: f32 (its CPU KvCache) */
 } lt_attn_cfg;
 
 /* embedLookup (src/model/forward.zig:319-341): dev_out[cols] = dequantised
@@ -325,16 +327,16 @@ lt_status lt_qmatvec_add(lt_ctx *ctx, const lt_tensor *w, uint32_t expert, const
  * per-head RMSNorm of q and k when their weights (head_dim floats) are
  * given (gemma4/forward.zig:267-268), RoPE on q and k (rope.zig), q updated in
  * place; k and v written to the caches at slot *dev_pos % kv_cap.  Caches are
- * [kv_cap][n_kv*hd] f32. */
+ * [kv_cap][n_kv*hd] elements, f32 or f16 (cfg->kv_f16). */
 lt_status lt_attn_prep(lt_ctx *ctx, const lt_attn_cfg *cfg, float *dev_qkv, const float *dev_q_norm,
-                       const float *dev_k_norm, const uint32_t *dev_pos, float *dev_k_cache,
-                       float *dev_v_cache);
+                       const float *dev_k_norm, const uint32_t *dev_pos, void *dev_k_cache,
+                       void *dev_v_cache);
 
 /* sdpAttn (src/ops/attn.zig:13-42) of every query head over the cached
  * positions max(0, pos+1-window) .. pos (query head h reads KV head
  * h / (n_heads / n_kv_heads)); dev_out[n_heads*hd]. */
 lt_status lt_attn_decode(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_q,
-                         const float *dev_k_cache, const float *dev_v_cache,
+                         const void *dev_k_cache, const void *dev_v_cache,
                          const uint32_t *dev_pos, float *dev_out);
 
 /* The attention half of a decoder layer for one token (forward.zig:272-305
@@ -349,7 +351,7 @@ lt_status lt_attn_decode(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_q
 lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x, const float *dev_norm_w,
                         float eps, const lt_tensor *wqkv, const float *dev_qkv_bias,
                         const float *dev_q_norm, const float *dev_k_norm, const uint32_t *dev_pos,
-                        float *dev_k_cache, float *dev_v_cache, const lt_tensor *wo, float *dev_out);
+                        void *dev_k_cache, void *dev_v_cache, const lt_tensor *wo, float *dev_out);
 
 /* L2 prefetch hint: the next lt_attn_block, or single-token lt_moe_block /
  * lt_moe_forward, launched on this context starts by prefetching these

@@ -61,7 +61,7 @@ class AttnCfg(ctypes.Structure):
     _fields_ = [("n_heads", ctypes.c_uint32), ("n_kv_heads", ctypes.c_uint32), ("head_dim", ctypes.c_uint32),
                 ("rope_neox", ctypes.c_uint32), ("rope_theta", ctypes.c_float), ("eps", ctypes.c_float),
                 ("scale", ctypes.c_float), ("kv_cap", ctypes.c_uint32), ("window", ctypes.c_uint32),
-                ("v_norm", ctypes.c_uint32)]
+                ("v_norm", ctypes.c_uint32), ("kv_f16", ctypes.c_uint32)]
 
 
 class SampleParams(ctypes.Structure):

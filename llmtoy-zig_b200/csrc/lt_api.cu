@@ -738,11 +738,12 @@ static lt_status attn_geom(lt_ctx *ctx, const lt_attn_cfg *cfg, lt::AttnGeom &g,
     g.cap = cfg->kv_cap;
     g.window = cfg->window;
     g.v_norm = cfg->v_norm ? 1u : 0u;
+    g.kv_f16 = cfg->kv_f16 ? 1u : 0u;
     return LT_OK;
 }
 
 lt_status lt_attn_prep(lt_ctx *ctx, const lt_attn_cfg *cfg, float *dev_qkv, const float *dev_q_norm,
-                       const float *dev_k_norm, const uint32_t *dev_pos, float *dev_k_cache, float *dev_v_cache) {
+                       const float *dev_k_norm, const uint32_t *dev_pos, void *dev_k_cache, void *dev_v_cache) {
     lt_status st = enter(ctx);
     if (st != LT_OK) return st;
     lt::AttnGeom g;
@@ -753,8 +754,8 @@ lt_status lt_attn_prep(lt_ctx *ctx, const lt_attn_cfg *cfg, float *dev_qkv, cons
                     "attn prep");
 }
 
-lt_status lt_attn_decode(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_q, const float *dev_k_cache,
-                         const float *dev_v_cache, const uint32_t *dev_pos, float *dev_out) {
+lt_status lt_attn_decode(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_q, const void *dev_k_cache,
+                         const void *dev_v_cache, const uint32_t *dev_pos, float *dev_out) {
     lt_status st = enter(ctx);
     if (st != LT_OK) return st;
     lt::AttnGeom g;
@@ -781,7 +782,7 @@ lt_status lt_prefetch_next(lt_ctx *ctx, const lt_tensor *a, const lt_tensor *b) 
 
 lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x, const float *dev_norm_w, float eps,
                         const lt_tensor *wqkv, const float *dev_qkv_bias, const float *dev_q_norm,
-                        const float *dev_k_norm, const uint32_t *dev_pos, float *dev_k_cache, float *dev_v_cache,
+                        const float *dev_k_norm, const uint32_t *dev_pos, void *dev_k_cache, void *dev_v_cache,
                         const lt_tensor *wo, float *dev_out) {
     lt_status st = enter(ctx);
     if (st != LT_OK) return st;

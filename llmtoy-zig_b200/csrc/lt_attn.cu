@@ -10,8 +10,9 @@
 //                gemma4/forward.zig:315-319)
 //
 // The position comes from a device word, so one captured graph serves every
-// decode step; the KV cache is a ring of `cap` f32 positions per layer,
-// [cap][n_kv * head_dim] for K and for V (the reference's KvCache layout).
+// decode step; the KV cache is a ring of `cap` positions per layer,
+// [cap][n_kv * head_dim] for K and for V (the reference's KvCache layout), f32
+// or f16 elements (the reference's GPU cache keeps f16).
 #include "lt_launch.cuh"
 
 namespace lt {
@@ -42,8 +43,8 @@ LT_DEVINL float rope_freq(float theta, uint32_t i, uint32_t len) {
 // [n_heads, n_heads + n_kv) the key heads (which also append their value
 // head).  Thread i < hd/2 rotates pair i.
 __global__ void __launch_bounds__(kAttnThreads) k_attn_prep(AttnGeom g, float *qkv, const float *q_norm,
-                                                            const float *k_norm, const uint32_t *pos_p, float *kc,
-                                                            float *vc) {
+                                                            const float *k_norm, const uint32_t *pos_p, void *kc,
+                                                            void *vc) {
     __shared__ float v[kAttnMaxHd];
     __shared__ float red[kAttnWarps];
     pdl_launch_dependents();
@@ -65,7 +66,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_prep(AttnGeom g, float *q
         for (uint32_t i = threadIdx.x; i < hd; i += kAttnThreads) v[i] = __fmul_rn(__fmul_rn(v[i], rms_inv), nw[i]);
     }
     __syncthreads();
-    float *dst = is_q ? src : kc + (size_t)(pos % g.cap) * nkv + (size_t)kh * hd;
+    const size_t slot = (size_t)(pos % g.cap) * nkv + (size_t)kh * hd;  // K and V heads in the caches
     const float fpos = (float)pos;
     for (uint32_t i = threadIdx.x; i < half; i += kAttnThreads) {
         const float ang = __fmul_rn(fpos, rope_freq(g.theta, i, hd));
@@ -73,21 +74,27 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_prep(AttnGeom g, float *q
         sincosf(ang, &s, &c);
         const uint32_t i0 = g.rope_neox ? i : 2 * i, i1 = g.rope_neox ? i + half : 2 * i + 1;
         const float x0 = v[i0], x1 = v[i1];
-        dst[i0] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-        dst[i1] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+        const float r0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+        const float r1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+        if (is_q) {
+            src[i0] = r0;
+            src[i1] = r1;
+        } else {
+            kv_st(kc, slot + i0, r0, g.kv_f16);
+            kv_st(kc, slot + i1, r1, g.kv_f16);
+        }
     }
     if (!is_q) {
         const float *vs = qkv + nq + nkv + (size_t)kh * hd;
-        float *vd = vc + (size_t)(pos % g.cap) * nkv + (size_t)kh * hd;
         if (g.v_norm) {  // rmsnormRaw (math.zig:43-48) of the V head
             __syncthreads();
             float ss = 0.0f;
             for (uint32_t i = threadIdx.x; i < hd; i += kAttnThreads) ss = __fadd_rn(ss, __fmul_rn(vs[i], vs[i]));
             ss = block_sum128(ss, red);
             const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), g.eps)));
-            for (uint32_t i = threadIdx.x; i < hd; i += kAttnThreads) vd[i] = __fmul_rn(vs[i], r);
+            for (uint32_t i = threadIdx.x; i < hd; i += kAttnThreads) kv_st(vc, slot + i, __fmul_rn(vs[i], r), g.kv_f16);
         } else {
-            for (uint32_t i = threadIdx.x; i < hd; i += kAttnThreads) vd[i] = vs[i];
+            for (uint32_t i = threadIdx.x; i < hd; i += kAttnThreads) kv_st(vc, slot + i, vs[i], g.kv_f16);
         }
     }
 }
@@ -97,8 +104,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_prep(AttnGeom g, float *q
 // per CTA; the last CTA of a head merges the splits (partials in scratch,
 // one counter per head, reset by the merger).  Each lane holds hd/32 dims.
 template <int HD>
-__global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnGeom g, const float *q, const float *kc,
-                                                              const float *vc, const uint32_t *pos_p, float *out,
+__global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnGeom g, const float *q, const void *kc,
+                                                              const void *vc, const uint32_t *pos_p, float *out,
                                                               float *part, uint32_t *counters) {
     constexpr int PER = HD / 32;
     __shared__ float s_m[kAttnWarps], s_l[kAttnWarps];
@@ -123,13 +130,12 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnGeom g, const 
     const uint32_t stride = kAttnWarps * nsplit;
     for (uint32_t j = split * kAttnWarps + warp; j < win; j += stride) {
         const uint32_t slot = (first + j) % g.cap;
-        const float *kr = kc + (size_t)slot * nkv + (size_t)kh * HD;
-        const float *vr = vc + (size_t)slot * nkv + (size_t)kh * HD;
+        const size_t row = (size_t)slot * nkv + (size_t)kh * HD;
         float kv[PER], vv[PER];
 #pragma unroll
         for (int i = 0; i < PER; i++) {
-            kv[i] = kr[lane + 32 * i];
-            vv[i] = vr[lane + 32 * i];
+            kv[i] = kv_ld(kc, row + lane + 32 * i, g.kv_f16);
+            vv[i] = kv_ld(vc, row + lane + 32 * i, g.kv_f16);
         }
         float dot = 0.0f;
 #pragma unroll
@@ -204,13 +210,13 @@ size_t attn_scratch_floats(const AttnGeom &g, int num_sms) {
 }
 
 cudaError_t launch_attn_prep(const LaunchCfg &c, const AttnGeom &g, float *qkv, const float *q_norm,
-                             const float *k_norm, const uint32_t *pos, float *kc, float *vc) {
+                             const float *k_norm, const uint32_t *pos, void *kc, void *vc) {
     return launch_k(c, "attn_prep", k_attn_prep, dim3(g.n_heads + g.n_kv), dim3(kAttnThreads), 0, g, qkv, q_norm,
                     k_norm, pos, kc, vc);
 }
 
-cudaError_t launch_attn_decode(const LaunchCfg &c, const AttnGeom &g, const float *q, const float *kc,
-                               const float *vc, const uint32_t *pos, float *out, float *part, uint32_t *counters) {
+cudaError_t launch_attn_decode(const LaunchCfg &c, const AttnGeom &g, const float *q, const void *kc,
+                               const void *vc, const uint32_t *pos, float *out, float *part, uint32_t *counters) {
     const dim3 grid(g.n_heads, attn_splits(g, c.num_sms));
     switch (g.hd) {
     case 64: return launch_k(c, "attn_decode", k_attn_decode<64>, grid, dim3(kAttnThreads), 0, g, q, kc, vc, pos, out, part, counters);

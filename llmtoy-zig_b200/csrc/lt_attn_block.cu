@@ -43,7 +43,7 @@ struct AttnBlockArgs {
     const float *bias;    // nullable [qrows]
     const float *q_norm, *k_norm;
     const uint32_t *pos;
-    float *kc, *vc;
+    void *kc, *vc;  // f32 or f16 elements (g.kv_f16)
     const uint8_t *wo;
     uint64_t opitch;
     uint32_t onb;  // 32-blocks per wo row (nq / 32)
@@ -297,9 +297,17 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
         if (s == 0 && h % group == 0) {  // this position's K/V into the cache
             const size_t slot = (size_t)(pos % a.g.cap) * nkv + (size_t)kh * HD;
             for (uint32_t i = tid; i < HD; i += kAbThreads) {
-                a.kc[slot + i] = hk[i];
-                a.vc[slot + i] = hv[i];
+                kv_st(a.kc, slot + i, hk[i], a.g.kv_f16);
+                kv_st(a.vc, slot + i, hv[i], a.g.kv_f16);
             }
+        }
+        if (a.g.kv_f16) {  // attend to this position as the cache holds it
+            __syncthreads();
+            for (uint32_t i = tid; i < HD; i += kAbThreads) {
+                hk[i] = kv_round(hk[i], 1u);
+                hv[i] = kv_round(hv[i], 1u);
+            }
+            __syncthreads();
         }
         float qv[PER], o[PER];
 #pragma unroll
@@ -318,8 +326,8 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
                     const size_t slot = (size_t)((first + j) % a.g.cap) * nkv + (size_t)kh * HD;
 #pragma unroll
                     for (int i = 0; i < PER; i++) {
-                        kv[b][i] = a.kc[slot + lane + 32 * i];
-                        vv[b][i] = a.vc[slot + lane + 32 * i];
+                        kv[b][i] = kv_ld(a.kc, slot + lane + 32 * i, a.g.kv_f16);
+                        vv[b][i] = kv_ld(a.vc, slot + lane + 32 * i, a.g.kv_f16);
                     }
                 } else {  // the current position (or past the window: unused)
 #pragma unroll

@@ -76,6 +76,20 @@ LT_DEVINL uint32_t f32_to_f16_bits(float f) {
     return sign | r;
 }
 
+// KV-cache elements: f32, or IEEE f16 stored rounded to nearest even.
+LT_DEVINL float kv_ld(const void *base, size_t i, uint32_t f16) {
+    return f16 ? f16_bits_to_f32(reinterpret_cast<const unsigned short *>(base)[i])
+               : reinterpret_cast<const float *>(base)[i];
+}
+LT_DEVINL void kv_st(void *base, size_t i, float v, uint32_t f16) {
+    if (f16)
+        reinterpret_cast<unsigned short *>(base)[i] = (unsigned short)f32_to_f16_bits(v);
+    else
+        reinterpret_cast<float *>(base)[i] = v;
+}
+// The value a cache store then load returns.
+LT_DEVINL float kv_round(float v, uint32_t f16) { return f16 ? f16_bits_to_f32(f32_to_f16_bits(v)) : v; }
+
 // Read-only 128-bit global load (weights are never written while a kernel
 // runs), allocated in L1 only if it streams: weights are touched once.
 LT_DEVINL uint4 ldg_stream(const void *p) {

@@ -111,13 +111,14 @@ struct AttnGeom {
     uint32_t cap;
     uint32_t window;  // 0: every cached position; else the last `window`
     uint32_t v_norm;  // 1: RMSNorm without weights on each V head before caching (gemma4/forward.zig:269)
+    uint32_t kv_f16;  // 1: caches hold f16 elements, else f32
 };
 uint32_t attn_splits(const AttnGeom &g, int num_sms);
 size_t attn_scratch_floats(const AttnGeom &g, int num_sms);
 cudaError_t launch_attn_prep(const LaunchCfg &c, const AttnGeom &g, float *qkv, const float *q_norm,
-                             const float *k_norm, const uint32_t *pos, float *kc, float *vc);
-cudaError_t launch_attn_decode(const LaunchCfg &c, const AttnGeom &g, const float *q, const float *kc,
-                               const float *vc, const uint32_t *pos, float *out, float *part, uint32_t *counters);
+                             const float *k_norm, const uint32_t *pos, void *kc, void *vc);
+cudaError_t launch_attn_decode(const LaunchCfg &c, const AttnGeom &g, const float *q, const void *kc,
+                               const void *vc, const uint32_t *pos, float *out, float *part, uint32_t *counters);
 
 // The attention half of a decoder layer for one token in one persistent
 // kernel (lt_attn_block.cu): out = x + wo . attention(rope(norm(W_qkv .
@@ -130,7 +131,7 @@ struct AttnBlockParams {
     DevMat wqkv, wo;
     const float *bias, *q_norm, *k_norm;
     const uint32_t *pos;
-    float *kc, *vc;
+    void *kc, *vc;  // f32 or f16 elements (AttnGeom::kv_f16)
     float *out;            // may alias x
     float *scratch;        // attn_block_scratch_floats floats
     uint8_t *sync;         // kAttnSyncBytes zero-initialised, this kernel only

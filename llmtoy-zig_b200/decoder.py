@@ -35,7 +35,7 @@ class _Model(ctypes.Structure):
                 ("eps", ctypes.c_float), ("rope_theta", ctypes.c_float), ("kv_cap", U32),
                 ("token_emb", P), ("lm_head", P), ("out_norm", P), ("layers", ctypes.POINTER(_Layer)),
                 ("family", U32), ("rope_theta_swa", ctypes.c_float), ("logit_softcap", ctypes.c_float),
-                ("sliding_window", U32)]
+                ("sliding_window", U32), ("kv_f16", U32)]
 
 LLAMA, GEMMA4 = 0, 1
 
@@ -143,6 +143,7 @@ class ModelSpec:
     rope_theta_swa: float = 1e4
     logit_softcap: float = 0.0
     sliding_window: int = 0
+    kv_f16: bool = False  # f16 KV caches (the reference's GPU format) instead of f32
 
 
 class Decoder:
@@ -168,7 +169,7 @@ class Decoder:
         self._model = _Model(len(s.layers), s.d_model, s.n_heads, s.n_kv_heads, s.head_dim, s.vocab, s.n_used,
                              int(s.norm_topk), int(s.rope_neox), s.act, s.eps, s.rope_theta, s.kv_cap,
                              _h(s.token_emb), _h(s.lm_head), _ptr(s.out_norm), self._layers, s.family,
-                             s.rope_theta_swa, s.logit_softcap, s.sliding_window)
+                             s.rope_theta_swa, s.logit_softcap, s.sliding_window, int(s.kv_f16))
         h = P()
         self._check(self.lib.lth_decoder_create(ctx.ptr, ctypes.byref(self._model), ctypes.byref(h)))
         self.ptr = h.value
@@ -224,7 +225,7 @@ class Decoder:
         return list(out)
 
 
-def upload_decoder(ctx: Context, m, kv_cap: int = 4096, stacked_qkv: bool = True) -> ModelSpec:
+def upload_decoder(ctx: Context, m, kv_cap: int = 4096, stacked_qkv: bool = True, kv_f16: bool = False) -> ModelSpec:
     """Upload a synth.DecoderModel (host GGUF bytes) and return its ModelSpec.
     Norm weights and biases go to torch CUDA tensors, which the spec keeps
     alive; stacked_qkv uploads Q, K and V rows as one tensor (one matvec)."""
@@ -262,7 +263,7 @@ def upload_decoder(ctx: Context, m, kv_cap: int = 4096, stacked_qkv: bool = True
                      token_emb=ctx.upload(m.token_emb, m.emb_type, m.vocab, d),
                      lm_head=ctx.upload(m.lm_head, m.lm_type, m.vocab, d), out_norm=dev(m.out_norm),
                      layers=layers, n_used=m.k, norm_topk=m.norm_topk, rope_neox=m.rope_neox, eps=m.eps,
-                     rope_theta=m.rope_theta, kv_cap=kv_cap)
+                     rope_theta=m.rope_theta, kv_cap=kv_cap, kv_f16=kv_f16)
 
 
 class GgufFile:

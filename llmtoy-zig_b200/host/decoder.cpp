@@ -22,8 +22,9 @@ struct lth_decoder {
     lt_attn_cfg attn{};
     uint32_t nq = 0, nkv = 0;
     float *x = nullptr, *xb = nullptr, *qkv = nullptr, *att = nullptr, *logits = nullptr;
-    float *kcache = nullptr, *vcache = nullptr;
-    std::vector<size_t> kv_off;  // per layer: offset of its cache (floats)
+    uint8_t *kcache = nullptr, *vcache = nullptr;
+    size_t kv_esize = 4;         // bytes per cache element: 4 (f32) or 2 (f16)
+    std::vector<size_t> kv_off;  // per layer: offset of its cache (elements)
     // Gemma 4: attention output, dense FFN, MoE accumulator, expert and router inputs, routing
     float *ybuf = nullptr, *fbuf = nullptr, *mbuf = nullptr, *moe_in = nullptr, *router_in = nullptr;
     uint32_t *ids = nullptr;
@@ -53,14 +54,14 @@ lt_status alloc(lth_decoder *d, T **p, size_t count) {
         if (st_ != LT_OK) return st_;        \
     } while (0)
 
-lt_status attn_ops(lth_decoder *d, const lth_layer &L, float *kc, float *vc);
+lt_status attn_ops(lth_decoder *d, const lth_layer &L, void *kc, void *vc);
 
 lt_status layer_step(lth_decoder *d, uint32_t l) {
     const lth_model &m = d->m;
     const lth_layer &L = d->layers[l];
     lt_ctx *c = d->ctx;
     const uint32_t *pos = d->state;
-    float *kc = d->kcache + d->kv_off[l], *vc = d->vcache + d->kv_off[l];
+    void *kc = d->kcache + d->kv_off[l] * d->kv_esize, *vc = d->vcache + d->kv_off[l] * d->kv_esize;
     const lth_layer *next = l + 1 < m.n_layers ? &d->layers[l + 1] : nullptr;
     if (L.wqkv) {  // the whole attention half in one launch; warm this layer's router in L2 meanwhile
         LTH_TRY(lt_prefetch_next(c, L.router, nullptr));
@@ -78,7 +79,7 @@ lt_status layer_step(lth_decoder *d, uint32_t l) {
 }
 
 // The attention half as separate ops (separate Q/K/V tensors).
-lt_status attn_ops(lth_decoder *d, const lth_layer &L, float *kc, float *vc) {
+lt_status attn_ops(lth_decoder *d, const lth_layer &L, void *kc, void *vc) {
     const lth_model &m = d->m;
     lt_ctx *c = d->ctx;
     const uint32_t *pos = d->state;
@@ -122,7 +123,8 @@ lt_status gemma_layer(lth_decoder *d, uint32_t l) {
     a.kv_cap = L.is_swa ? m.sliding_window : m.kv_cap;
     a.window = L.is_swa ? m.sliding_window : 0;
     a.v_norm = 1;
-    float *kc = d->kcache + d->kv_off[l], *vc = d->vcache + d->kv_off[l];
+    a.kv_f16 = m.kv_f16 ? 1u : 0u;
+    void *kc = d->kcache + d->kv_off[l] * d->kv_esize, *vc = d->vcache + d->kv_off[l] * d->kv_esize;
     LTH_TRY(lt_rmsnorm(c, d->x, L.attn_norm, m.eps, m.d_model, 1, d->xb));
     LTH_TRY(lt_qmatvec(c, L.wq, 0, d->xb, d->qkv, 1));
     LTH_TRY(lt_qmatvec(c, L.wk, 0, d->xb, d->qkv + nq, 1));
@@ -201,6 +203,8 @@ lt_status lth_decoder_create(lt_ctx *ctx, const lth_model *m, lth_decoder **out)
     d->attn.scale = 1.0f / __builtin_sqrtf((float)m->head_dim);  // forward.zig:300
     d->attn.kv_cap = m->kv_cap;
     d->attn.window = 0;
+    d->attn.kv_f16 = m->kv_f16 ? 1u : 0u;
+    d->kv_esize = m->kv_f16 ? 2 : 4;
     // per-layer caches: the model's heads and kv_cap positions, or (Gemma 4)
     // this layer's heads and, for sliding-window layers, a ring of the window
     size_t cache = 0, max_q = d->nq, max_kv = d->nkv;
@@ -223,8 +227,8 @@ lt_status lth_decoder_create(lt_ctx *ctx, const lth_model *m, lth_decoder **out)
     lt_status st;
     if ((st = alloc(d, &d->x, dm)) != LT_OK || (st = alloc(d, &d->xb, dm)) != LT_OK ||
         (st = alloc(d, &d->qkv, max_q + 2 * max_kv)) != LT_OK || (st = alloc(d, &d->att, max_q)) != LT_OK ||
-        (st = alloc(d, &d->logits, m->vocab)) != LT_OK || (st = alloc(d, &d->kcache, cache)) != LT_OK ||
-        (st = alloc(d, &d->vcache, cache)) != LT_OK || (st = alloc(d, &d->tokens, (size_t)m->kv_cap + 1)) != LT_OK ||
+        (st = alloc(d, &d->logits, m->vocab)) != LT_OK || (st = alloc(d, &d->kcache, cache * d->kv_esize)) != LT_OK ||
+        (st = alloc(d, &d->vcache, cache * d->kv_esize)) != LT_OK || (st = alloc(d, &d->tokens, (size_t)m->kv_cap + 1)) != LT_OK ||
         (st = alloc(d, &d->state, 2)) != LT_OK || (st = alloc(d, &d->ids_zero, 4)) != LT_OK ||
         (st = alloc(d, &d->rng, 4)) != LT_OK ||
         (m->family == LTH_GEMMA4 &&

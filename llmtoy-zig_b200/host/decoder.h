@@ -62,6 +62,7 @@ typedef struct lth_model {
     uint32_t family;
     float rope_theta_swa, logit_softcap;
     uint32_t sliding_window;
+    uint32_t kv_f16;       /* 1: f16 KV caches (the reference's GPU cache format), 0: f32 */
 } lth_model;
 
 typedef struct lth_decoder lth_decoder;

@@ -1011,6 +1011,11 @@ int orc_model_step(const orc_model *m, float *k_cache, float *v_cache, size_t kv
         if (L->k_norm) for (size_t h = 0; h < m->n_kv_heads; h++) orc_rmsnorm(kn + h * hd, kn + h * hd, L->k_norm, hd, m->eps);
         for (size_t h = 0; h < m->n_heads; h++) orc_rope(q + h * hd, hd, pos, m->rope_theta, m->rope_neox);
         for (size_t h = 0; h < m->n_kv_heads; h++) orc_rope(kn + h * hd, hd, pos, m->rope_theta, m->rope_neox);
+        if (m->kv_f16)  /* an f16 cache returns the stored values rounded to nearest even */
+            for (size_t i = 0; i < nkv; i++) {
+                kn[i] = orc_f16_to_f32(orc_f32_to_f16(kn[i]));
+                vn[i] = orc_f16_to_f32(orc_f32_to_f16(vn[i]));
+            }
         memcpy(kc + pos * nkv, kn, nkv * 4);
         memcpy(vc + pos * nkv, vn, nkv * 4);
         for (size_t h = 0; h < m->n_heads; h++) {

@@ -179,6 +179,7 @@ typedef struct orc_model {
     const float *out_norm;
     const uint8_t *lm_head; uint32_t lm_type;
     const orc_layer *layers;
+    int kv_f16;  /* cache K and V rounded to f16 (the reference's GPU cache format) */
 } orc_model;
 
 int orc_model_step(const orc_model *m, float *k_cache, float *v_cache, size_t kv_cap, uint32_t token,

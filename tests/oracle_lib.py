@@ -212,13 +212,14 @@ class OrcModel(ctypes.Structure):
                 ("norm_topk", ctypes.c_int), ("rope_neox", ctypes.c_int), ("eps", ctypes.c_float),
                 ("rope_theta", ctypes.c_float), ("token_emb", ctypes.c_void_p), ("emb_type", ctypes.c_uint32),
                 ("out_norm", ctypes.c_void_p), ("lm_head", ctypes.c_void_p), ("lm_type", ctypes.c_uint32),
-                ("layers", ctypes.POINTER(OrcLayer))]
+                ("layers", ctypes.POINTER(OrcLayer)), ("kv_f16", ctypes.c_int)]
 
 
 class OracleDecoder:
-    """orc_model_step over a synth.DecoderModel, with its own f32 KV cache."""
+    """orc_model_step over a synth.DecoderModel, with its own KV cache (f32, or
+    f16-rounded values with kv_f16)."""
 
-    def __init__(self, m, kv_cap: int, pool: Pool | None = None):
+    def __init__(self, m, kv_cap: int, pool: Pool | None = None, kv_f16: bool = False):
         self.m, self.cap, self.pool = m, kv_cap, pool
         self._keep = []
 
@@ -250,7 +251,8 @@ class OracleDecoder:
             self._layers[i] = o
         self.model = OrcModel(m.n_layers, m.d_model, m.n_heads, m.n_kv_heads, m.head_dim, m.d_ffn, m.vocab,
                               m.n_experts, m.k, m.d_expert, int(m.norm_topk), int(m.rope_neox), m.eps, m.rope_theta,
-                              p(m.token_emb), m.emb_type, p(m.out_norm), p(m.lm_head), m.lm_type, self._layers)
+                              p(m.token_emb), m.emb_type, p(m.out_norm), p(m.lm_head), m.lm_type, self._layers,
+                              int(kv_f16))
         self.kc = np.zeros(m.n_layers * kv_cap * nkv, np.float32)
         self.vc = np.zeros_like(self.kc)
 

@@ -55,16 +55,18 @@ def test_embed_out_of_range_reports(ctx, pkg):
 
 @pytest.mark.parametrize("hd,nh,nkv,neox,qk_norm", [(64, 4, 2, False, False), (128, 32, 4, True, True),
                                                     (256, 8, 8, True, True)])
-def test_attention_step_vs_oracle(ctx, pkg, oracle, hd, nh, nkv, neox, qk_norm):
+@pytest.mark.parametrize("kv_f16", [False, True])
+def test_attention_step_vs_oracle(ctx, pkg, oracle, hd, nh, nkv, neox, qk_norm, kv_f16):
     """attn_prep + attn_decode over 1..40 positions against orc_rope +
-    orc_rmsnorm + orc_sdp_attn on the same q/k/v."""
+    orc_rmsnorm + orc_sdp_attn on the same q/k/v; with f16 caches the cached
+    K/V are the oracle's values rounded to f16, bit for bit."""
     rng = np.random.default_rng(hd + nh)
     cap = 64
     nq, nk = nh * hd, nkv * hd
-    cfg = pkg.AttnCfg(nh, nkv, hd, int(neox), 1e6, 1e-6, 1.0 / np.sqrt(hd), cap, 0)
+    cfg = pkg.AttnCfg(nh, nkv, hd, int(neox), 1e6, 1e-6, 1.0 / np.sqrt(hd), cap, 0, 0, int(kv_f16))
     qn = rng.uniform(0.5, 1.5, hd).astype(np.float32) if qk_norm else None
     kn = rng.uniform(0.5, 1.5, hd).astype(np.float32) if qk_norm else None
-    kc, vc = empty(cap * nk), empty(cap * nk)
+    kc, vc = (empty(cap * nk, "float16"), empty(cap * nk, "float16")) if kv_f16 else (empty(cap * nk), empty(cap * nk))
     rk, rv = np.zeros((cap, nk), np.float32), np.zeros((cap, nk), np.float32)
     lib = oracle.lib()
 
@@ -91,7 +93,11 @@ def test_attention_step_vs_oracle(ctx, pkg, oracle, hd, nh, nkv, neox, qk_norm):
                 k[h] = onorm(np.ascontiguousarray(k[h]), kn)
             lib.orc_rope(k[h].ctypes.data, hd, pos, 1e6, int(neox))
         rk[pos], rv[pos] = k.reshape(-1), qkv[nq + nk:]
-        np.testing.assert_allclose(host(kc).reshape(cap, nk)[pos], rk[pos], rtol=2e-5, atol=2e-5)
+        if kv_f16:
+            rk[pos] = rk[pos].astype(np.float16).astype(np.float32)
+            rv[pos] = rv[pos].astype(np.float16).astype(np.float32)
+            np.testing.assert_array_equal(host(vc).reshape(cap, nk)[pos].astype(np.float32), rv[pos])
+        np.testing.assert_allclose(host(kc).reshape(cap, nk)[pos].astype(np.float32), rk[pos], rtol=2e-5, atol=2e-5)
         np.testing.assert_allclose(host(dq)[:nq], q.reshape(-1), rtol=2e-5, atol=2e-5)
         ref = np.empty(nq, np.float32)
         for h in range(nh):
@@ -142,11 +148,11 @@ def test_greedy_step_stream(ctx, pkg):
     assert host(state).tolist() == [4, 3]
 
 
-def _compare_generation(ctx, oracle, pool, m, prompt, n_gen, stacked=True, graph_check=True):
+def _compare_generation(ctx, oracle, pool, m, prompt, n_gen, stacked=True, graph_check=True, kv_f16=False):
     _, decoder = _mods()
-    spec = decoder.upload_decoder(ctx, m, kv_cap=64, stacked_qkv=stacked)
+    spec = decoder.upload_decoder(ctx, m, kv_cap=64, stacked_qkv=stacked, kv_f16=kv_f16)
     dec = decoder.Decoder(ctx, spec)
-    ref_toks, ref_logits = oracle.OracleDecoder(m, 64, pool).generate(prompt, n_gen)
+    ref_toks, ref_logits = oracle.OracleDecoder(m, 64, pool, kv_f16=kv_f16).generate(prompt, n_gen)
     dec.start(prompt)
     worst = 0.0
     for i, rl in enumerate(ref_logits):
@@ -199,13 +205,25 @@ def test_decoder_config2_shape_vs_oracle(ctx, oracle, pool):
     _compare_generation(ctx, oracle, pool, m, [100, 2000, 30000, 151935], 6, graph_check=False)
 
 
-@pytest.mark.parametrize("name,d,nh,nkv,hd,wt,neox,qk,bias,window", [
-    ("config2", 2048, 32, 4, 128, 8, True, True, False, 0),
-    ("config0", 896, 14, 2, 64, 8, False, False, True, 0),
-    ("gemma-swa", 1024, 8, 4, 256, 12, True, True, False, 16),
-    ("q6k", 512, 4, 4, 128, 14, False, True, True, 0),
+@pytest.mark.parametrize("stacked", [True, False])
+def test_decoder_config2_f16_kv_vs_oracle(ctx, oracle, pool, stacked):
+    """Config 2 keeps an f16 KV cache: the attention-block kernel (stacked
+    Q/K/V) and the separate ops both against the oracle caching f16-rounded
+    K/V."""
+    synth, _ = _mods()
+    m = synth.config2_model(np.random.default_rng(25), n_layers=2)
+    _compare_generation(ctx, oracle, pool, m, [7, 151000, 42], 6, stacked=stacked, kv_f16=True)
+
+
+@pytest.mark.parametrize("name,d,nh,nkv,hd,wt,neox,qk,bias,window,f16", [
+    ("config2", 2048, 32, 4, 128, 8, True, True, False, 0, False),
+    ("config2-f16kv", 2048, 32, 4, 128, 8, True, True, False, 0, True),
+    ("config0", 896, 14, 2, 64, 8, False, False, True, 0, False),
+    ("gemma-swa", 1024, 8, 4, 256, 12, True, True, False, 16, False),
+    ("gemma-swa-f16kv", 1024, 8, 4, 256, 12, True, True, False, 16, True),
+    ("q6k", 512, 4, 4, 128, 14, False, True, True, 0, False),
 ])
-def test_attn_block_matches_separate_ops(pkg, oracle, name, d, nh, nkv, hd, wt, neox, qk, bias, window):
+def test_attn_block_matches_separate_ops(pkg, oracle, name, d, nh, nkv, hd, wt, neox, qk, bias, window, f16):
     """The persistent attention-block kernel against the same computation as
     separate ops (rmsnorm, Q/K/V matvec, prep, attention, wo + residual),
     step by step over 24 positions with shared caches."""
@@ -221,7 +239,7 @@ def test_attn_block_matches_separate_ops(pkg, oracle, name, d, nh, nkv, hd, wt, 
     kn = rng.uniform(0.5, 1.5, hd).astype(np.float32) if qk else None
     bs = rng.normal(0, 0.1, nq + 2 * nk).astype(np.float32) if bias else None
     cap = window if window else 64
-    cfg = pkg.AttnCfg(nh, nkv, hd, int(neox), 1e6, 1e-6, 1.0 / np.sqrt(hd), cap, window)
+    cfg = pkg.AttnCfg(nh, nkv, hd, int(neox), 1e6, 1e-6, 1.0 / np.sqrt(hd), cap, window, 0, int(f16))
     ctxs = []
     old = os.environ.get("LLMTOY_ATTN_BLOCK")
     for flag in ("1", "0"):
@@ -236,7 +254,7 @@ def test_attn_block_matches_separate_ops(pkg, oracle, name, d, nh, nkv, hd, wt, 
     res = []
     for c in ctxs:
         tq, to = c.upload(wqkv, wt, nq + 2 * nk, d), c.upload(wo, wt, d, nq)
-        kc, vc = empty(cap * nk), empty(cap * nk)
+        kc, vc = (empty(cap * nk, "float16"), empty(cap * nk, "float16")) if f16 else (empty(cap * nk), empty(cap * nk))
         xs = []
         rng2 = np.random.default_rng(77)
         for pos in range(24):
