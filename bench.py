@@ -287,7 +287,8 @@ def main() -> None:
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline work (rank 0, N=1)")
     ap.add_argument("--profile-steps", type=int, default=5)
     ap.add_argument("--no-graph", action="store_true")
-    ap.add_argument("--prefill-tokens", type=int, default=512, help="T of the prefill measurement (0: skip)")
+    ap.add_argument("--prefill-tokens", default="16,512",
+                    help="comma list of T for the multi-token MoE layer measurement (config 1's T=16 and 512; 0: skip)")
     ap.add_argument("--prefill-layers", type=int, default=8)
     ap.add_argument("--ep-tokens", type=int, default=8 * 2048,
                     help="config 4: prompt tokens over all ranks, experts sharded 128/N (0: skip)")
@@ -447,8 +448,10 @@ def main() -> None:
 
     # ---- prefill: T tokens through the MoE blocks (tensor-core expert GEMM) ----
     prefill = None
-    if args.prefill_tokens > 0:
-        prefill = measure_prefill(args, pkg, ctx, torch, stream, gen, layers, rank, world, dist)
+    t_list = [int(t) for t in str(args.prefill_tokens).split(",") if int(t) > 0]
+    if t_list:
+        prefill = {f"T={T}": measure_prefill(args, pkg, ctx, torch, stream, gen, layers, rank, world, dist, T)
+                   for T in t_list}
 
     model_decode = None
     if args.model_tokens > 0:
@@ -489,11 +492,11 @@ def main() -> None:
         dist.destroy_process_group()
 
 
-def measure_prefill(args, pkg, ctx, torch, stream, gen, layers, rank, world, dist) -> dict:
-    """T prompt tokens through `prefill_layers` MoE blocks in place (router,
-    dispatch, tensor-core gate/up and down GEMMs, combine, residual); value =
-    tokens per second through one MoE layer, all ranks (replicas)."""
-    T = args.prefill_tokens
+def measure_prefill(args, pkg, ctx, torch, stream, gen, layers, rank, world, dist, T: int) -> dict:
+    """T tokens through `prefill_layers` MoE blocks in place (router, dispatch,
+    gate/up and down -- the tensor-core GEMM from 64 tokens, the CUDA-core
+    grouped kernels below -- combine, residual); value = tokens per second
+    through one MoE layer, all ranks (replicas)."""
     nl = min(args.prefill_layers, len(layers))
     xp = torch.randn(T, D_MODEL, device="cuda", generator=gen)
     xp0 = xp.clone()
@@ -534,21 +537,37 @@ def measure_prefill(args, pkg, ctx, torch, stream, gen, layers, rank, world, dis
     k_us = {k: 1e3 * v["total_ms"] / v["count"] for k, v in prof.items()}
     gemm_us = k_us.get("moe_gemm_gate_up", 0.0) + k_us.get("moe_gemm_down", 0.0)
     flops = 2.0 * T * TOP_K * 3 * D_EXPERT * D_MODEL  # gate + up + down, algorithmic
-    peak, kind = measured_tflops()
+    if gemm_us:  # tensor-core path: bound by the tensor pipe
+        peak, kind = measured_tflops()
+        achieved = flops / (gemm_us * 1e-6) / 1e12
+        roofline = {"kernel": "moe_gemm_gate_up + moe_gemm_down", "bound": "tensor", "achieved": achieved,
+                    "peak": peak, "unit": "TFLOP/s", "peak_kind": kind, "frac": achieved / peak,
+                    "algorithmic_flops": flops, "traffic": None,
+                    "note": "f16 tcgen05 MMAs; the activation's lo plane doubles the issued MMA work"}
+    else:  # CUDA-core grouped kernels: bound by HBM (the distinct experts' bytes once each)
+        L0 = layers[0]
+        xn, ids, wts = torch.empty_like(xp0), torch.empty(T * TOP_K, dtype=torch.int32, device="cuda"), \
+            torch.empty(T * TOP_K, device="cuda")
+        ctx.rmsnorm(xp0, L0.norm, 1e-6, D_MODEL, T, xn)
+        ctx.moe_route(L0.router, xn, T, TOP_K, True, None, ids, wts)
+        ctx.sync()
+        U = int(torch.unique(ids).numel())
+        nbytes = U * EXPERT_BYTES + ROUTER_BYTES + 2 * T * D_MODEL * 4
+        peak, kind = measured_peaks()
+        achieved = nbytes / (ms_layer / 1e3) / 1e9
+        roofline = {"kernel": "whole MoE layer (router, moe_gate_up, moe_down)", "bound": "hbm",
+                    "achieved": achieved, "peak": peak, "unit": "GB/s", "peak_kind": kind, "frac": achieved / peak,
+                    "algorithmic_bytes_per_layer": nbytes, "experts_selected": U, "traffic": None,
+                    "note": "U distinct experts of the first layer's routing, each read once"}
     out = {
-        "metric": f"MoE layer prefill tok/s (config 1, T={T})", "value": world * T / (ms_layer / 1e3),
+        "metric": f"MoE layer tok/s (config 1, T={T})", "value": world * T / (ms_layer / 1e3),
         "unit": "tok/s", "ms_per_layer": ms_layer, "layers_timed": nl, "reps": reps,
         "stack_equivalent_tok_s": world * T / (ms_layer / 1e3) / args.layers,
         "kernels_us": {k: round(v, 1) for k, v in k_us.items()},
-        "roofline": {"kernel": "moe_gemm_gate_up + moe_gemm_down", "bound": "tensor",
-                     "achieved": flops / (gemm_us * 1e-6) / 1e12 if gemm_us else None, "peak": peak,
-                     "unit": "TFLOP/s", "peak_kind": kind,
-                     "frac": (flops / (gemm_us * 1e-6) / 1e12) / peak if gemm_us else None,
-                     "algorithmic_flops": flops, "traffic": None,
-                     "note": "f16 tcgen05 MMAs; the activation's lo plane doubles the issued MMA work"},
+        "roofline": roofline,
     }
     if rank == 0 and world == 1 and args.cpu_budget > 0:
-        out["cpu_baseline"] = cpu_prefill_rate(min(args.cpu_budget, 10.0))
+        out["cpu_baseline"] = cpu_prefill_rate(min(args.cpu_budget, 10.0), T)
     return out
 
 
@@ -1056,9 +1075,12 @@ def measure_ep_prefill(args, pkg, torch, stream, rank, world, local, dist) -> di
     return out
 
 
-def cpu_prefill_rate(budget_s: float) -> dict:
-    """The CPU restatement on a bounded sample of the same prefill: batches of
-    16 tokens through one MoE layer (router + experts), all host threads."""
+def cpu_prefill_rate(budget_s: float, T: int) -> dict:
+    """The CPU restatement on a bounded sample of the same workload: batches of
+    min(T, 16) tokens through one MoE layer (router + experts), all host
+    threads (the CPU path handles tokens one by one, so the rate does not
+    depend on the batch)."""
+    B = min(T, 16)
     sys.path.insert(0, str(REPO / "tests"))
     oracle = importlib.import_module("oracle_lib")
     synth = importlib.import_module("llmtoy-zig_b200.synth")
@@ -1066,7 +1088,7 @@ def cpu_prefill_rate(budget_s: float) -> dict:
     L = synth.MoeLayer(rng, D_MODEL, N_EXPERTS, D_EXPERT)
     threads = os.cpu_count() or 1
     pool = oracle.Pool(threads)
-    x = rng.normal(0, 1, size=(16, D_MODEL)).astype(np.float32)
+    x = rng.normal(0, 1, size=(B, D_MODEL)).astype(np.float32)
     oracle.moe_layer(L, x, TOP_K, True, 0, None, pool)
     t0 = time.perf_counter()
     n = 0
@@ -1075,8 +1097,8 @@ def cpu_prefill_rate(budget_s: float) -> dict:
         n += 1
     dt = time.perf_counter() - t0
     pool.close()
-    return {"value": 16 * n / dt, "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"{n} batches of 16 tokens through one config-1 MoE layer in {dt:.1f}s"}
+    return {"value": B * n / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{n} batches of {B} tokens through one config-1 MoE layer in {dt:.1f}s"}
 
 
 if __name__ == "__main__":
