@@ -11,11 +11,12 @@
 //            this position (by split 0 of the group's first head), and
 //            online-softmax attention over the split's positions; the
 //            current position's K/V come from registers, older ones from the
-//            cache; each split publishes (max, sum, weighted values).
+//            cache; each split publishes (max, sum, weighted values), and the
+//            last split of a head to finish (a per-head counter) merges the
+//            head's splits and quantises the head into the attention row.
 //                                                      -> grid barrier
-//   phase O  every CTA merges the splits of every head itself (no third
-//            hand-off), quantises the attention vector and computes its wo
-//            rows plus the residual: out = x + wo . att (forward.zig:304-305).
+//   phase O  every CTA copies the quantised attention row and computes its
+//            wo rows plus the residual: out = x + wo . att (forward.zig:304-305).
 //
 // The weights are static, so both tiles (this CTA's Q/K/V rows and wo rows)
 // stream in while the previous kernel finishes; an optional L2 prefetch
@@ -29,7 +30,7 @@ constexpr int kAbWarps = 16;
 constexpr int kAbThreads = kAbWarps * 32;
 
 // Layout of the context's attention sync block.
-constexpr size_t kAbEpoch = 0, kAbB1 = 8, kAbB2 = 16;
+constexpr size_t kAbEpoch = 0, kAbB1 = 8, kAbB2 = 16, kAbHeadCnt = 256;
 constexpr uint32_t kAbMaxSplits = 8;  // splits of a head's positions (one CTA each)
 
 struct AttnBlockArgs {
@@ -48,7 +49,8 @@ struct AttnBlockArgs {
     uint64_t opitch;
     uint32_t onb;  // 32-blocks per wo row (nq / 32)
     float *out;
-    float *qkv, *part, *att;  // global scratch
+    float *qkv, *part;  // global scratch
+    uint8_t *att;       // the attention vector as a quantised activation row (qact layout)
     uint8_t *sync;
     const uint8_t *pf[2];
     uint64_t pf_bytes[2];
@@ -122,6 +124,32 @@ LT_DEVINL void ab_load(float *dst, const float *src, uint32_t n) {
         }
     }
     for (uint32_t i = 4 * n4 + threadIdx.x; i < n; i += kAbThreads) dst[i] = __ldcg(src + i);
+}
+
+// A quantised activation row (lt_qact.cuh layout, written by other CTAs of
+// this launch) into the shared layout X, loads through L2.
+LT_DEVINL void ab_load_qact(const XS &X, const uint8_t *row, uint32_t cols) {
+    const uint32_t nhi = cols / 8, nlo = cols / 16, ng = cols / 16;
+    for (uint32_t i = threadIdx.x; i < nhi + nlo; i += kAbThreads) {
+        if (i < nhi) {
+            const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(row) + i);
+            const uint32_t e0 = 8 * i;
+            *reinterpret_cast<uint4 *>(X.xq + (e0 >> 8) * kXHiPitch + 2 * (e0 & 255)) = v;
+        } else {
+            const uint32_t c = i - nhi;
+            const uint4 v = __ldcg(reinterpret_cast<const uint4 *>(row + (size_t)cols * 2) + c);
+            const uint32_t e0 = 16 * c;
+            *reinterpret_cast<uint4 *>(X.xl + (e0 >> 8) * kXLoPitch + (e0 & 255)) = v;
+        }
+    }
+    const float *sc = reinterpret_cast<const float *>(row + (size_t)cols * 3);
+    for (uint32_t i = threadIdx.x; i < 2 * ng; i += kAbThreads) {
+        const float v = __ldcg(sc + i);
+        if (i < ng)
+            X.xs[i] = v;
+        else
+            X.xsum16[i - ng] = v;
+    }
 }
 
 // rows [0, nrows) of a shared tile (pitch) against X: y[r] per row.  Lanes
@@ -225,6 +253,8 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     unsigned long long *ctr_epoch = reinterpret_cast<unsigned long long *>(a.sync + kAbEpoch);
     unsigned long long *ctr1 = reinterpret_cast<unsigned long long *>(a.sync + kAbB1);
     unsigned long long *ctr2 = reinterpret_cast<unsigned long long *>(a.sync + kAbB2);
+    uint32_t *head_cnt = reinterpret_cast<uint32_t *>(a.sync + kAbHeadCnt);
+    int *s_last = reinterpret_cast<int *>(smem + L.misc + 128);
 
     const uint32_t q0 = (uint32_t)((uint64_t)c * a.qrows / G), q1 = (uint32_t)((uint64_t)(c + 1) * a.qrows / G);
     const uint32_t o0 = (uint32_t)((uint64_t)c * a.d / G), o1 = (uint32_t)((uint64_t)(c + 1) * a.d / G);
@@ -392,52 +422,42 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
             }
             *reinterpret_cast<float2 *>(pml) = make_float2(M, Lsum);
         }
+        // the last split of head h to get here merges the head's splits and
+        // quantises it (16-groups never straddle heads: HD % 32 == 0)
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) s_last[0] = atomicAdd(head_cnt + h, 1u) == S - 1;
+        __syncthreads();
+        if (s_last[0]) {
+            __threadfence();
+            const float *ho = a.part + (size_t)h * S * HD;
+            const float *hml = a.part + (size_t)a.g.n_heads * S * HD + 2 * (size_t)h * S;
+            for (uint32_t t = tid; t < HD; t += kAbThreads) {
+                float GM = -INFINITY;
+                for (uint32_t k = 0; k < S; k++) GM = fmaxf(GM, __ldcg(hml + 2 * k));
+                float GL = 0.0f, acc = 0.0f;
+                for (uint32_t k = 0; k < S; k++) {
+                    const float mk = __ldcg(hml + 2 * k);
+                    if (mk != -INFINITY) {
+                        const float f = expf(mk - GM);
+                        GL += __ldcg(hml + 2 * k + 1) * f;
+                        acc += __ldcg(ho + (size_t)k * HD + t) * f;
+                    }
+                }
+                hq[t] = acc / GL;  // this item's query head is no longer needed
+            }
+            __syncthreads();
+            for (uint32_t b = warp; b < (uint32_t)HD / 32; b += kAbWarps)
+                qact_store_block(a.att, (int)nq, (int)(h * HD / 32 + b), hq[32 * b + lane], lane);
+            if (tid == 0) head_cnt[h] = 0;
+        }
         __syncthreads();
     }
     grid_arrive(ctr2);
     grid_wait(ctr2, epoch, a.dev_err, kWaitLimitNs);
 
     // ── phase O ──────────────────────────────────────────────────────────────
-    // every CTA merges the heads' splits itself: 4 output values per thread
-    for (uint32_t g4 = tid; g4 < nq / 4; g4 += kAbThreads) {
-        const uint32_t h = 4 * g4 / HD, t = 4 * g4 - h * HD;
-        const float *ho = a.part + (size_t)h * S * HD + t;
-        const float *hml = a.part + (size_t)a.g.n_heads * S * HD + 2 * (size_t)h * S;
-        float ms[kAbMaxSplits], ls[kAbMaxSplits];
-        float4 os[kAbMaxSplits];
-#pragma unroll
-        for (int k = 0; k < (int)kAbMaxSplits; k++) {
-            if ((uint32_t)k < S) {
-                const float2 ml = __ldcg(reinterpret_cast<const float2 *>(hml) + k);
-                ms[k] = ml.x;
-                ls[k] = ml.y;
-                os[k] = __ldcg(reinterpret_cast<const float4 *>(ho + (size_t)k * HD));
-            }
-        }
-        float GM = -INFINITY;
-#pragma unroll
-        for (int k = 0; k < (int)kAbMaxSplits; k++)
-            if ((uint32_t)k < S) GM = fmaxf(GM, ms[k]);
-        float GL = 0.0f;
-        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-        for (int k = 0; k < (int)kAbMaxSplits; k++) {
-            if ((uint32_t)k < S && ms[k] != -INFINITY) {
-                const float f = expf(ms[k] - GM);
-                GL += ls[k] * f;
-                acc.x += os[k].x * f;
-                acc.y += os[k].y * f;
-                acc.z += os[k].z * f;
-                acc.w += os[k].w * f;
-            }
-        }
-        xf[4 * g4] = acc.x / GL;
-        xf[4 * g4 + 1] = acc.y / GL;
-        xf[4 * g4 + 2] = acc.z / GL;
-        xf[4 * g4 + 3] = acc.w / GL;
-    }
-    __syncthreads();
-    ab_quantise(Xa, xf, nq, warp, lane);
+    ab_load_qact(Xa, a.att, nq);
     __syncthreads();
     float *yo = xf;  // the attention vector is quantised already
     if (nor && tile_wait(&bars[1], a.dev_err)) ab_rows<OT>(wo, a.opitch, nor, nq, a.onb, Xa, warp, lane, yo);
@@ -476,7 +496,8 @@ size_t attn_block_smem(const AttnGeom &g, int num_sms, uint32_t d, const DevMat 
 
 size_t attn_block_scratch_floats(const AttnGeom &g, int num_sms, uint32_t d, const DevMat &wqkv, const DevMat &wo) {
     const AttnBlockArgs a = ab_args(g, num_sms, d, wqkv, wo);
-    return (size_t)a.qrows + (size_t)g.n_heads * a.splits * (g.hd + 2) + (size_t)g.n_heads * g.hd + 64;
+    return (size_t)a.qrows + 32 + (size_t)g.n_heads * a.splits * (g.hd + 2) + 32 +
+           qact_pitch((uint64_t)g.n_heads * g.hd) / 4 + 64;
 }
 
 template <uint32_t QT, uint32_t OT>
@@ -516,7 +537,7 @@ cudaError_t launch_attn_block(const LaunchCfg &c, const AttnBlockParams &p) {
     float *sc = p.scratch;
     a.qkv = sc;
     a.part = sc + ((a.qrows + 31) & ~31u);
-    a.att = a.part + (((size_t)p.g.n_heads * a.splits * (p.g.hd + 2) + 31) & ~(size_t)31);  // o then (max, sum)
+    a.att = reinterpret_cast<uint8_t *>(a.part + (((size_t)p.g.n_heads * a.splits * (p.g.hd + 2) + 31) & ~(size_t)31));
     a.sync = p.sync;
     for (int i = 0; i < 2; i++) {
         a.pf[i] = p.pf[i];

@@ -138,7 +138,7 @@ struct AttnBlockParams {
     const uint8_t *pf[2];  // optional L2 prefetch ranges (the next kernel's weights)
     uint64_t pf_bytes[2];
 };
-constexpr size_t kAttnSyncBytes = 256;
+constexpr size_t kAttnSyncBytes = 256 + 4 * 1024;  // counters, then one merge counter per head (<= 1024)
 bool attn_block_supported(const AttnGeom &g, const DevMat &wqkv, const DevMat &wo, uint32_t d);
 size_t attn_block_smem(const AttnGeom &g, int num_sms, uint32_t d, const DevMat &wqkv, const DevMat &wo);
 size_t attn_block_scratch_floats(const AttnGeom &g, int num_sms, uint32_t d, const DevMat &wqkv, const DevMat &wo);
