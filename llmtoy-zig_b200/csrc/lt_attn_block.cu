@@ -32,6 +32,7 @@ constexpr int kAbThreads = kAbWarps * 32;
 // Layout of the context's attention sync block.
 constexpr size_t kAbEpoch = 0, kAbB1 = 8, kAbB2 = 16, kAbHeadCnt = 256;
 constexpr uint32_t kAbMaxSplits = 8;  // splits of a head's positions (one CTA each)
+constexpr uint32_t kAbSplitPositions = 256;  // positions per split before another CTA joins
 
 struct AttnBlockArgs {
     AttnGeom g;
@@ -81,7 +82,7 @@ __host__ __device__ inline AbLayout ab_layout(const AttnBlockArgs &a) {
     L.nw = take((size_t)a.d * 4);
     L.xres = take((size_t)a.maxo * 4);
     // per-item head vectors q, k, v and the warps' softmax partials
-    L.head = take((size_t)(3 * a.g.hd + kAbWarps * (a.g.hd + 2)) * 4);
+    L.head = take((size_t)(3 * a.g.hd + kAbWarps * (a.g.hd + 2) + kAbWarps + 2) * 4);
     L.total = off;
     return L;
 }
@@ -230,6 +231,115 @@ LT_DEVINL void ab_norm_rope2(float *hq, const float *qn, float *hk, const float 
     __syncthreads();
 }
 
+// Online-softmax attention of one query head over the split's positions of
+// the window (src/ops/attn.zig:13-42): warp w takes positions s*16 + w,
+// + 16 S, ...; lane owns head dims [lane*PER, lane*PER + PER) and loads them
+// as one vector per position.  The next batch of NB positions is in flight
+// while the current one is scored; the current position (the last of the
+// window) comes from shared memory, older ones from the cache (f16 or f32).
+template <int HD, bool F16>
+LT_DEVINL void ab_attend(const AttnBlockArgs &a, uint32_t s, uint32_t S, uint32_t win, uint32_t first, size_t kvoff,
+                         uint32_t nkv, const float *hq, const float *hk, const float *hv, int warp, int lane,
+                         float &m, float &l, float (&o)[HD / 32]) {
+    constexpr int PER = HD / 32;
+    constexpr int W = F16 ? PER / 2 : PER;  // 32-bit words of a lane's slice of one vector
+    constexpr int NB = 8 / W > 0 ? 8 / W : 1;  // two batches of K and V words: 32 registers
+    const size_t esz = F16 ? 2 : 4;
+    const uint8_t *kc = static_cast<const uint8_t *>(a.kc), *vc = static_cast<const uint8_t *>(a.vc);
+    float qv[PER];
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        qv[i] = hq[lane * PER + i];
+        o[i] = 0.0f;
+    }
+    const uint32_t stride = S * kAbWarps, last = win - 1;  // position `last` is this step's
+    auto load = [&](uint32_t j0, uint32_t (&kr)[NB][W], uint32_t (&vr)[NB][W]) {
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            const uint32_t j = j0 + b * stride;
+            if (j < last) {
+                const size_t off = (((size_t)((first + j) % a.g.cap) * nkv + kvoff) + (size_t)lane * PER) * esz;
+#pragma unroll
+                for (int w4 = 0; w4 < W; w4 += 4) {
+                    if constexpr (W >= 4) {
+                        const uint4 kk = __ldg(reinterpret_cast<const uint4 *>(kc + off) + w4 / 4);
+                        const uint4 vv = __ldg(reinterpret_cast<const uint4 *>(vc + off) + w4 / 4);
+                        kr[b][w4] = kk.x; kr[b][w4 + 1] = kk.y; kr[b][w4 + 2] = kk.z; kr[b][w4 + 3] = kk.w;
+                        vr[b][w4] = vv.x; vr[b][w4 + 1] = vv.y; vr[b][w4 + 2] = vv.z; vr[b][w4 + 3] = vv.w;
+                    } else if constexpr (W == 2) {
+                        const uint2 kk = __ldg(reinterpret_cast<const uint2 *>(kc + off));
+                        const uint2 vv = __ldg(reinterpret_cast<const uint2 *>(vc + off));
+                        kr[b][0] = kk.x; kr[b][1] = kk.y;
+                        vr[b][0] = vv.x; vr[b][1] = vv.y;
+                    } else {
+                        kr[b][0] = __ldg(reinterpret_cast<const uint32_t *>(kc + off));
+                        vr[b][0] = __ldg(reinterpret_cast<const uint32_t *>(vc + off));
+                    }
+                }
+            }
+        }
+    };
+    auto val = [&](const uint32_t (&r)[W], int i) -> float {
+        if constexpr (F16)
+            return f16_bits_to_f32((r[i >> 1] >> (16 * (i & 1))) & 0xffffu);
+        else
+            return __uint_as_float(r[i]);
+    };
+    auto update = [&](float sc, const float *vals) {
+        const float mn = fmaxf(m, sc);
+        const float al = expf(m - mn), p = expf(sc - mn);
+        l = l * al + p;
+#pragma unroll
+        for (int i = 0; i < PER; i++) o[i] = fmaf(p, vals[i], o[i] * al);
+        m = mn;
+    };
+    uint32_t ka[NB][W], va[NB][W], kb[NB][W], vb[NB][W];
+    uint32_t j0 = s * kAbWarps + warp;
+    if (j0 < last) load(j0, ka, va);
+    for (; j0 < last; j0 += NB * stride) {
+        const uint32_t jn = j0 + NB * stride;
+        if (jn < last) load(jn, kb, vb);
+        float dot[NB];
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            dot[b] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < PER; i++) dot[b] = fmaf(qv[i], val(ka[b], i), dot[b]);
+        }
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1)
+#pragma unroll
+            for (int b = 0; b < NB; b++) dot[b] += __shfl_xor_sync(0xffffffffu, dot[b], o2);
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            if (j0 + b * stride < last) {
+                float vals[PER];
+#pragma unroll
+                for (int i = 0; i < PER; i++) vals[i] = val(va[b], i);
+                update(dot[b] * a.g.scale, vals);
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < NB; b++)
+#pragma unroll
+            for (int w = 0; w < W; w++) {
+                ka[b][w] = kb[b][w];
+                va[b][w] = vb[b][w];
+            }
+    }
+    // this step's position: the warp whose sequence it ends
+    if (last % stride == s * kAbWarps + (uint32_t)warp) {
+        float dot = 0.0f, vals[PER];
+#pragma unroll
+        for (int i = 0; i < PER; i++) {
+            dot = fmaf(qv[i], hk[lane * PER + i], dot);
+            vals[i] = hv[lane * PER + i];
+        }
+        dot = warp_sum(dot);
+        update(dot * a.g.scale, vals);
+    }
+}
+
 template <uint32_t QT, uint32_t OT, int HD>
 __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -305,8 +415,11 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     grid_wait(ctr1, epoch, a.dev_err, kWaitLimitNs);
 
     // ── phase A ──────────────────────────────────────────────────────────────
-    const uint32_t S = a.splits, group = a.g.n_heads / a.g.n_kv;
+    const uint32_t group = a.g.n_heads / a.g.n_kv;
     const uint32_t seq = pos + 1, win = a.g.window ? min(seq, a.g.window) : seq, first = seq - win;
+    // splits of a head's window: one per kAbSplitPositions positions (a short
+    // window is one CTA's, with no merge across CTAs), at most a.splits
+    const uint32_t S = min(a.splits, max(1u, (win + kAbSplitPositions - 1) / kAbSplitPositions));
     for (uint32_t item = c; item < a.g.n_heads * S; item += G) {
         const uint32_t h = item / S, s = item - h * S, kh = h / group;
         if (tid < 3 * HD / 4) {  // q, k, v heads: one float4 each
@@ -339,94 +452,67 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
             }
             __syncthreads();
         }
-        float qv[PER], o[PER];
-#pragma unroll
-        for (int i = 0; i < PER; i++) {
-            qv[i] = hq[lane + 32 * i];
-            o[i] = 0.0f;
-        }
-        float m = -INFINITY, l = 0.0f;
-        const uint32_t stride = S * kAbWarps;
-        for (uint32_t j0 = s * kAbWarps + warp; j0 < win; j0 += NB * stride) {
-            float kv[NB][PER], vv[NB][PER];
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-                const uint32_t j = j0 + b * stride;
-                if (j + 1 < win) {
-                    const size_t slot = (size_t)((first + j) % a.g.cap) * nkv + (size_t)kh * HD;
-#pragma unroll
-                    for (int i = 0; i < PER; i++) {
-                        kv[b][i] = kv_ld(a.kc, slot + lane + 32 * i, a.g.kv_f16);
-                        vv[b][i] = kv_ld(a.vc, slot + lane + 32 * i, a.g.kv_f16);
-                    }
-                } else {  // the current position (or past the window: unused)
-#pragma unroll
-                    for (int i = 0; i < PER; i++) {
-                        kv[b][i] = hk[lane + 32 * i];
-                        vv[b][i] = hv[lane + 32 * i];
-                    }
-                }
-            }
-            float dot[NB];
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-                dot[b] = 0.0f;
-#pragma unroll
-                for (int i = 0; i < PER; i++) dot[b] = fmaf(qv[i], kv[b][i], dot[b]);
-            }
-#pragma unroll
-            for (int o2 = 16; o2 > 0; o2 >>= 1)
-#pragma unroll
-                for (int b = 0; b < NB; b++) dot[b] += __shfl_xor_sync(0xffffffffu, dot[b], o2);
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-                if (j0 + b * stride < win) {
-                    const float sc = dot[b] * a.g.scale;
-                    const float mn = fmaxf(m, sc);
-                    const float al = expf(m - mn), p = expf(sc - mn);
-                    l = l * al + p;
-#pragma unroll
-                    for (int i = 0; i < PER; i++) o[i] = fmaf(p, vv[b][i], o[i] * al);
-                    m = mn;
-                }
-            }
-        }
+        float o[PER], m = -INFINITY, l = 0.0f;
+        if (a.g.kv_f16)
+            ab_attend<HD, true>(a, s, S, win, first, (size_t)kh * HD, nkv, hq, hk, hv, warp, lane, m, l, o);
+        else
+            ab_attend<HD, false>(a, s, S, win, first, (size_t)kh * HD, nkv, hq, hk, hv, warp, lane, m, l, o);
         float *wp = wpart + warp * (HD + 2);
         if (lane == 0) {
             wp[0] = m;
             wp[1] = l;
         }
 #pragma unroll
-        for (int i = 0; i < PER; i++) wp[2 + lane + 32 * i] = o[i];
+        for (int i = 0; i < PER; i++) wp[2 + lane * PER + i] = o[i];  // lane owns dims [lane*PER, +PER)
         __syncthreads();
-        float M = -INFINITY;
+        // the warps' partials: warp 0 finds the maximum and each warp's scale once
+        float *sf = wpart + kAbWarps * (HD + 2);  // [kAbWarps] scales, then the sum
+        if (warp == 0) {
+            const float mw = lane < kAbWarps ? wpart[lane * (HD + 2)] : -INFINITY;
+            float M = mw;
 #pragma unroll
-        for (int w = 0; w < kAbWarps; w++) M = fmaxf(M, wpart[w * (HD + 2)]);
+            for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
+            if (lane < kAbWarps) sf[lane] = mw != -INFINITY ? expf(mw - M) : 0.0f;
+            __syncwarp();
+            if (lane == 0) {
+                float Lsum = 0.0f;
+                for (int w = 0; w < kAbWarps; w++) Lsum += wpart[w * (HD + 2) + 1] * sf[w];
+                sf[kAbWarps] = Lsum;
+                sf[kAbWarps + 1] = M;
+            }
+        }
+        __syncthreads();
+        if (S == 1) {  // the whole window: normalise, quantise into the attention row
+            const float Lsum = sf[kAbWarps];
+            for (uint32_t t = tid; t < HD; t += kAbThreads) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int w = 0; w < kAbWarps; w++) acc += wpart[w * (HD + 2) + 2 + t] * sf[w];
+                hq[t] = acc / Lsum;  // this item's query head is no longer needed
+            }
+            __syncthreads();
+            for (uint32_t b = warp; b < (uint32_t)HD / 32; b += kAbWarps)
+                qact_store_block(a.att, (int)nq, (int)(h * HD / 32 + b), hq[32 * b + lane], lane);
+            __syncthreads();
+            continue;
+        }
         // split partials: o [h][s][HD] (16-byte aligned rows), (max, sum) [h][s]
         float *po = a.part + ((size_t)h * S + s) * HD;
         float *pml = a.part + (size_t)a.g.n_heads * S * HD + 2 * ((size_t)h * S + s);
         for (uint32_t t = tid; t < HD; t += kAbThreads) {
             float acc = 0.0f;
 #pragma unroll
-            for (int w = 0; w < kAbWarps; w++) {
-                const float mw = wpart[w * (HD + 2)];
-                if (mw != -INFINITY) acc += wpart[w * (HD + 2) + 2 + t] * expf(mw - M);
-            }
+            for (int w = 0; w < kAbWarps; w++) acc += wpart[w * (HD + 2) + 2 + t] * sf[w];
             po[t] = acc;
         }
-        if (tid == 0) {
-            float Lsum = 0.0f;
-            for (int w = 0; w < kAbWarps; w++) {
-                const float mw = wpart[w * (HD + 2)];
-                if (mw != -INFINITY) Lsum += wpart[w * (HD + 2) + 1] * expf(mw - M);
-            }
-            *reinterpret_cast<float2 *>(pml) = make_float2(M, Lsum);
-        }
+        if (tid == 0) *reinterpret_cast<float2 *>(pml) = make_float2(sf[kAbWarps + 1], sf[kAbWarps]);
         // the last split of head h to get here merges the head's splits and
         // quantises it (16-groups never straddle heads: HD % 32 == 0)
-        __threadfence();
         __syncthreads();
-        if (tid == 0) s_last[0] = atomicAdd(head_cnt + h, 1u) == S - 1;
+        if (tid == 0) {
+            __threadfence();
+            s_last[0] = atomicAdd(head_cnt + h, 1u) == S - 1;
+        }
         __syncthreads();
         if (s_last[0]) {
             __threadfence();
@@ -444,7 +530,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
                         acc += __ldcg(ho + (size_t)k * HD + t) * f;
                     }
                 }
-                hq[t] = acc / GL;  // this item's query head is no longer needed
+                hq[t] = acc / GL;
             }
             __syncthreads();
             for (uint32_t b = warp; b < (uint32_t)HD / 32; b += kAbWarps)
