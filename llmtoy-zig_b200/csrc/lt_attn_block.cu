@@ -154,7 +154,7 @@ LT_DEVINL void ab_load_qact(const XS &X, const uint8_t *row, uint32_t cols) {
 }
 
 // rows [0, nrows) of a shared tile (pitch) against X: y[r] per row.  Lanes
-// own 64-column chunks (cb = lane, lane + 32, ...), loaded once per chunk;
+// own 64-column chunks (spread_chunk within each group of 32), loaded once per chunk;
 // warp w takes rows w, w+16, ... (up to 4 at a time).
 template <uint32_t T>
 LT_DEVINL void ab_rows(const uint8_t *tile, uint64_t pitch, uint32_t nrows, uint32_t cols, uint32_t nb, const XS &X,
@@ -165,13 +165,17 @@ LT_DEVINL void ab_rows(const uint8_t *tile, uint64_t pitch, uint32_t nrows, uint
         float acc[R];
 #pragma unroll
         for (int i = 0; i < R; i++) acc[i] = 0.0f;
-        for (uint32_t cb = lane; cb < nch; cb += 32) {
-            XChunk xc;
-            xchunk_load(X, 0, (int)cb, xc);
+        for (uint32_t g = 0; g < nch; g += 32) {
+            const uint32_t n = min(32u, nch - g);
+            if ((uint32_t)lane < n) {
+                const uint32_t cb = g + spread_chunk((uint32_t)lane, n);
+                XChunk xc;
+                xchunk_load(X, 0, (int)cb, xc);
 #pragma unroll
-            for (int i = 0; i < R; i++) {
-                const uint32_t r = r0 + i * kAbWarps;
-                if (r < nrows) acc[i] += dot64<T>(tile + (size_t)r * pitch, (int)cb, (int)nb, xc);
+                for (int i = 0; i < R; i++) {
+                    const uint32_t r = r0 + i * kAbWarps;
+                    if (r < nrows) acc[i] += dot64<T>(tile + (size_t)r * pitch, (int)cb, (int)nb, xc);
+                }
             }
         }
 #pragma unroll

@@ -288,9 +288,12 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     const uint32_t gstride = 2 * a.maxpairs + 1;  // partials [chunk][tile row], odd stride: no bank conflicts
     {
         const uint32_t lpr = min(cpr_g, 32u), rps = 32 / lpr;  // lanes per row, rows per step
-        const uint32_t sub = lane / lpr, cb0 = lane % lpr, nrows = 2 * np;
+        const uint32_t sub = lane / lpr, nrows = 2 * np;
         if (sub < rps) {
-            for (uint32_t cb = cb0; cb < cpr_g; cb += lpr) {
+            for (uint32_t cg = 0; cg < cpr_g; cg += lpr) {
+                const uint32_t n = min(lpr, cpr_g - cg);
+                if (lane % lpr >= n) continue;
+                const uint32_t cb = cg + spread_chunk(lane % lpr, n);
                 XChunk xc;
                 xchunk_load(Xx, 0, (int)cb, xc);
                 // two rows per iteration (independent chains for the scheduler);
@@ -353,13 +356,16 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     const uint32_t dstride = a.k * a.maxrows + 1;  // partials [chunk][slot row]
     {
         const uint32_t lpr = min(cpr_d, 32u), rps = 32 / lpr;
-        const uint32_t sub = lane / lpr, cb0 = lane % lpr;
+        const uint32_t sub = lane / lpr;
         const uint32_t wps = max(1u, (uint32_t)kDecWarps / a.k);
         const uint32_t s = warp / wps, ws = warp % wps;
         if (s < a.k && sub < rps && nr) {
             const bool ok = tile_wait(&bars[kDecMaxChunks + s], a.dev_err) && hok;
             const XS Xh = xs_carve(himg_s + (size_t)s * a.img, 1, (int)a.di);
-            for (uint32_t cb = cb0; cb < cpr_d; cb += lpr) {
+            for (uint32_t cg = 0; cg < cpr_d; cg += lpr) {
+                const uint32_t n = min(lpr, cpr_d - cg);
+                if (lane % lpr >= n) continue;
+                const uint32_t cb = cg + spread_chunk(lane % lpr, n);
                 XChunk xc;
                 xchunk_load(Xh, 0, (int)cb, xc);
                 const uint32_t step = wps * rps;

@@ -25,6 +25,17 @@ struct XChunk {
     float sum[4];
 };
 
+// The chunk taken by lane l of n lanes that cover n consecutive chunks.  The
+// four chunks of a 256-column item sit 128 bytes apart in X (the same banks),
+// items 528 bytes apart (different banks), so consecutive lanes take chunks
+// of different items: an 8-lane wavefront of 16-byte loads then falls in 8
+// bank groups instead of 2 (n % 4 == 0; otherwise lane l takes chunk l).
+LT_DEVINL uint32_t spread_chunk(uint32_t l, uint32_t n) {
+    if (n % 4 != 0) return l;
+    const uint32_t q = n / 4;
+    return (l % q) * 4 + l / q;
+}
+
 // Chunk cb (columns [64 cb, 64 cb + 64)) of row t of the padded layout X.
 LT_DEVINL void xchunk_load(const XS &X, int t, int cb, XChunk &x) {
     const int e0 = 64 * cb;
