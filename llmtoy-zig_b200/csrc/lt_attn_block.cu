@@ -155,13 +155,14 @@ LT_DEVINL void ab_load_qact(const XS &X, const uint8_t *row, uint32_t cols) {
 
 // rows [0, nrows) of a shared tile (pitch) against X: y[r] per row.  Lanes
 // own 64-column chunks (spread_chunk within each group of 32), loaded once per chunk;
-// warp w takes rows w, w+16, ... (up to 4 at a time).
+// warp w takes rows 4w .. 4w+3 (then 64 further): each activation chunk a
+// warp loads serves four rows, so few warps load it.
 template <uint32_t T>
 LT_DEVINL void ab_rows(const uint8_t *tile, uint64_t pitch, uint32_t nrows, uint32_t cols, uint32_t nb, const XS &X,
                        int warp, int lane, float *y) {
     constexpr int R = 4;
     const uint32_t nch = (cols + 63) / 64;
-    for (uint32_t r0 = warp; r0 < nrows; r0 += kAbWarps * R) {
+    for (uint32_t r0 = warp * R; r0 < nrows; r0 += kAbWarps * R) {
         float acc[R];
 #pragma unroll
         for (int i = 0; i < R; i++) acc[i] = 0.0f;
@@ -173,14 +174,14 @@ LT_DEVINL void ab_rows(const uint8_t *tile, uint64_t pitch, uint32_t nrows, uint
                 xchunk_load(X, 0, (int)cb, xc);
 #pragma unroll
                 for (int i = 0; i < R; i++) {
-                    const uint32_t r = r0 + i * kAbWarps;
+                    const uint32_t r = r0 + i;
                     if (r < nrows) acc[i] += dot64<T>(tile + (size_t)r * pitch, (int)cb, (int)nb, xc);
                 }
             }
         }
 #pragma unroll
         for (int i = 0; i < R; i++) {
-            const uint32_t r = r0 + i * kAbWarps;
+            const uint32_t r = r0 + i;
             const float v = warp_sum(acc[i]);
             if (lane == 0 && r < nrows) y[r] = v;
         }
