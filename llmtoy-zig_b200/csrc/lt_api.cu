@@ -1187,6 +1187,38 @@ lt_status lt_ffn_block(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, 
     const MoeScratch s = moe_layout(ctx->scratch, ntok, 1, 1, d, F, 0);
     float *xn = (float *)(ctx->scratch + probe.bytes);
     const lt::LaunchCfg c = cfg_of(ctx);
+    if (ntok == 1 && ctx->decode_kernel) {  // the single-token persistent kernel, dense mode
+        lt::DecodeParams p;
+        p.router = nullptr;
+        p.E = 1;
+        p.d = (uint32_t)d;
+        p.router_ld = 0;
+        p.x = dev_x;
+        p.norm_w = dev_norm_w;
+        p.eps = eps;
+        p.k = 1;
+        p.norm_topk = 0;
+        p.escale = nullptr;
+        p.ids = nullptr;
+        p.w = nullptr;
+        p.gate = gate->m;
+        p.up_data = up->m.data;
+        p.down = down->m;
+        p.F = (uint32_t)F;
+        p.act = act;
+        p.himg = s.himg;
+        p.residual = residual;
+        p.out = dev_out;
+        p.sync = ctx->dec_sync;
+        for (int i = 0; i < 2; i++) {
+            p.pf[i] = ctx->pf[i];
+            p.pf_bytes[i] = ctx->pf_bytes[i];
+        }
+        if (lt::moe_decode_fits(p, ctx->num_sms)) {
+            clear_prefetch(ctx);
+            return launched(ctx, lt::launch_moe_decode(c, p), "ffn decode");
+        }
+    }
     st = launched(ctx, lt::launch_rmsnorm(c, dev_x, dev_norm_w, eps, (uint32_t)d, ntok, xn), "rmsnorm");
     if (st != LT_OK) return st;
     st = launched(ctx, lt::launch_quantize(c, xn, (uint32_t)d, ntok, s.xq, s.xq_pitch), "quantize");

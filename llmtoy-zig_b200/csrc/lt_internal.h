@@ -188,7 +188,7 @@ cudaError_t launch_moe_down(const LaunchCfg &c, const DevMat &down, const uint8_
 // SM, grid barriers): RMSNorm (norm_w != nullptr), router, top-k, gate/up,
 // down, combine, residual (residual != 0: out = x + moe).  out may alias x.
 struct DecodeParams {
-    const float *router;  // F32 [E][router_ld]
+    const float *router;  // F32 [E][router_ld]; nullptr: a dense FFN (E = k = 1, weight 1)
     uint32_t E, d, router_ld;
     const float *x, *norm_w;
     float eps;

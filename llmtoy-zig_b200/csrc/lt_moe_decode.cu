@@ -26,6 +26,9 @@
 //            finishes its down rows for every slot, combines them in slot
 //            order and adds the residual kept from phase R.
 //
+// Dense mode (a dense FFN block, forward.zig:307-312): no router; one slot
+// holds "expert" 0 -- the 2-D gate/up/down tensors -- with weight 1.
+//
 // Per-item decoding, partial-sum orders and the combine are those of the
 // router / gate_up / down kernels, so both paths give the same bits.
 #include "lt_qact.cuh"
@@ -69,6 +72,7 @@ struct DecodeArgs {
     uint8_t *himg;  // [k][img] quantised h in the shared-memory layout (xs_bytes(1, di) per slot)
     uint32_t img;
     int residual;
+    int dense;   // no router: slot 0 = expert 0 with weight 1
     float *out;  // [d], may alias x
     uint8_t *sync;
     int *dev_err;
@@ -162,7 +166,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     // static inputs first: this CTA's router rows and the norm weights
     float w0[kRouterChunk];
     const uint32_t e_mine = c + (uint32_t)warp * G;
-    const bool has_e = e_mine < a.E;
+    const bool has_e = !a.dense && e_mine < a.E;
     router_prefetch(a.rw + (size_t)(has_e ? e_mine : 0) * a.rw_ld, a.d, lane, has_e, w0);
     if (a.norm_w)
         for (uint32_t i = tid; i < a.d; i += kDecThreads) nwsm[i] = __ldg(a.norm_w + i);
@@ -205,7 +209,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     const uint32_t tag = (uint32_t)epoch;
     // warps [0, nlw) compute this CTA's logits; the others quantise the
     // normalised x for this CTA's gate/up meanwhile
-    const uint32_t nlw = a.E > c ? (a.E - c + G - 1) / G : 0;
+    const uint32_t nlw = a.dense ? 0 : a.E > c ? (a.E - c + G - 1) / G : 0;
     if (has_e) {
         const float v = router_logit(a.rw + (size_t)e_mine * a.rw_ld, xsm, a.d, lane, w0);
         if (lane == 0) st_relaxed_u64(lslots + e_mine, ((uint64_t)tag << 32) | __float_as_uint(v));
@@ -213,7 +217,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
         for (uint32_t b = warp - nlw; b < a.d / 32; b += kDecWarps - nlw)
             qact_block_to_xs(Xx, 0, (int)b, xsm[32 * b + lane], lane);
     }
-    if (tid < a.E) {  // poll this expert's logit until it carries this launch's tag
+    if (!a.dense && tid < a.E) {  // poll this expert's logit until it carries this launch's tag
         uint64_t v = ld_relaxed_u64(lslots + tid);
         if ((uint32_t)(v >> 32) != tag) {
             const uint64_t t0 = globaltimer_ns();
@@ -232,15 +236,17 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     }
     if (tid == 0) s_key[a.E] = 0;
     __syncthreads();
-    if (warp == kDecWarps - 1) {  // softmax statistics while the other warps rank
-        float mx, es;
-        router_softmax_stats(s_lg, a.E, lane, mx, es);
-        if (lane == 0) {
-            s_stat[1] = mx;
-            s_stat[2] = es;
+    if (!a.dense) {
+        if (warp == kDecWarps - 1) {  // softmax statistics while the other warps rank
+            float mx, es;
+            router_softmax_stats(s_lg, a.E, lane, mx, es);
+            if (lane == 0) {
+                s_stat[1] = mx;
+                s_stat[2] = es;
+            }
         }
+        router_rank_keys_split(s_key, a.E, a.k, s_sel, min(4u, (uint32_t)(kDecThreads - 32) / a.E), s_cnt, tid);
     }
-    router_rank_keys_split(s_key, a.E, a.k, s_sel, min(4u, (uint32_t)(kDecThreads - 32) / a.E), s_cnt, tid);
     __syncthreads();
 
     // ── phase G ──────────────────────────────────────────────────────────────
@@ -275,8 +281,11 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
                         &bars[kDecMaxChunks + lane]);
         }
     } else if (warp == 2 && lane == 0) {
-        router_weights(s_lg, s_sel, a.k, s_stat[1], s_stat[2], a.norm_topk, a.escale, s_w);
-        if (c == 0)
+        if (a.dense)
+            s_w[0] = 1.0f;
+        else
+            router_weights(s_lg, s_sel, a.k, s_stat[1], s_stat[2], a.norm_topk, a.escale, s_w);
+        if (c == 0 && !a.dense)
             for (uint32_t i = 0; i < a.k; i++) {
                 a.ids[i] = s_sel[i];
                 a.wout[i] = s_w[i];
@@ -408,6 +417,7 @@ struct DecodePlan {
 
 bool decode_plan(const DecodeParams &p, int num_sms, DecodePlan &out) {
     if (num_sms <= 0 || p.k == 0 || p.k > 16 || p.E == 0 || p.E > (uint32_t)kRouterMaxE) return false;
+    if (!p.router && (p.k != 1 || p.E != 1)) return false;  // dense mode: one slot, expert 0
     auto ok_type = [](uint32_t t) { return t == T_Q8_0 || t == T_Q4_K || t == T_Q6_K; };
     if (!ok_type(p.gate.type) || !ok_type(p.down.type)) return false;  // the grouped kernels take the rest
     const uint32_t G = (uint32_t)num_sms;
@@ -438,6 +448,7 @@ bool decode_plan(const DecodeParams &p, int num_sms, DecodePlan &out) {
     a.himg = p.himg;
     a.img = (uint32_t)moe_decode_img_bytes(p.F);
     a.residual = p.residual;
+    a.dense = p.router == nullptr;
     a.out = p.out;
     a.sync = p.sync;
     a.dev_err = nullptr;

@@ -63,15 +63,16 @@ lt_status layer_step(lth_decoder *d, uint32_t l) {
     const uint32_t *pos = d->state;
     void *kc = d->kcache + d->kv_off[l] * d->kv_esize, *vc = d->vcache + d->kv_off[l] * d->kv_esize;
     const lth_layer *next = l + 1 < m.n_layers ? &d->layers[l + 1] : nullptr;
-    if (L.wqkv) {  // the whole attention half in one launch; warm this layer's router in L2 meanwhile
-        LTH_TRY(lt_prefetch_next(c, L.router, nullptr));
+    if (L.wqkv) {  // the whole attention half in one launch; warm this layer's router (or FFN) in L2 meanwhile
+        LTH_TRY(lt_prefetch_next(c, L.router ? L.router : L.ffn_gate, L.router ? nullptr : L.ffn_up));
         LTH_TRY(lt_attn_block(c, &d->attn, d->x, L.attn_norm, m.eps, L.wqkv, L.qkv_bias, L.q_norm, L.k_norm, pos,
                               kc, vc, L.wo, d->x));
     } else {
         LTH_TRY(attn_ops(d, L, kc, vc));
     }
-    if (L.router) {  // the MoE block warms the next layer's attention weights in L2
-        if (next && next->wqkv) LTH_TRY(lt_prefetch_next(c, next->wqkv, next->wo));
+    // the FFN block warms the next layer's attention weights in L2
+    if (next && next->wqkv) LTH_TRY(lt_prefetch_next(c, next->wqkv, next->wo));
+    if (L.router) {
         return lt_moe_block(c, L.router, L.exp_gate, L.exp_up, L.exp_down, (int)m.act, (int)m.norm_topk, nullptr,
                             L.ffn_norm, m.eps, d->x, 1, m.n_used, d->x, nullptr, nullptr);
     }

@@ -495,3 +495,34 @@ def test_router_token_major_matches_expert_major(ctx, oracle, norm):
             rid, _ = oracle.router_topk_softmax(w, x[t], k)
             assert np.array_equal(outs[1][0][t].astype(np.uint32), rid)
     rt.free()
+
+
+@pytest.mark.parametrize("t,d,F,act", [(8, 896, 4864, 0), (12, 2048, 768, 0), (14, 2816, 2048, 1), (13, 1024, 512, 0)])
+@pytest.mark.parametrize("ntok,residual", [(1, True), (1, False), (5, True)])
+def test_ffn_block_vs_oracle(ctx, oracle, t, d, F, act, ntok, residual):
+    """lt_ffn_block (forward.zig:307-312): out = (x if residual) + down .
+    (act(gate . xn) * (up . xn)), xn = rmsnorm(x) * w -- one token through the
+    persistent decode kernel's dense mode (Q8_0/Q4_K/Q6_K), the grouped
+    kernels otherwise."""
+    import importlib
+    synth = importlib.import_module("llmtoy-zig_b200.synth")
+    rng = np.random.Generator(np.random.PCG64(d + F + t))
+    gate, up, down = synth.matrix(rng, t, F, d), synth.matrix(rng, t, F, d), synth.matrix(rng, t, d, F)
+    nw = rng.uniform(0.5, 1.5, d).astype(np.float32)
+    x = rng.normal(0, 1, (ntok, d)).astype(np.float32)
+    tg, tu, td = ctx.upload(gate, t, F, d), ctx.upload(up, t, F, d), ctx.upload(down, t, d, F)
+    out = empty(ntok * d)
+    ctx.ffn_block(tg, tu, td, act, dev(nw), 1e-6, dev(x), ntok, out, residual=residual)
+    got = host(out).reshape(ntok, d)
+    lib = oracle.lib()
+    for i in range(ntok):
+        xn = np.empty(d, np.float32)
+        lib.orc_rmsnorm(xn.ctypes.data, x[i].ctypes.data, nw.ctypes.data, d, 1e-6)
+        g = oracle.quant_matvec(gate, t, xn, F, d)
+        u = oracle.quant_matvec(up, t, xn, F, d)
+        f = lib.orc_gelu if act else lib.orc_silu
+        h = (np.array([f(float(v)) for v in g], np.float32) * u).astype(np.float32)
+        ref = oracle.quant_matvec(down, t, h, d, F) + (x[i] if residual else 0)
+        assert rel_l2(got[i], ref) < 1e-4, (i, rel_l2(got[i], ref))
+    for w in (tg, tu, td):
+        w.free()
