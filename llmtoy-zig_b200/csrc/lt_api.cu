@@ -982,9 +982,10 @@ static lt_status ffn_impl(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *u
     const bool direct = ntok == 1;
     lt::DevMat upm = up ? up->m : lt::DevMat{};
     if (!up) upm.data = nullptr;
+    const uint32_t E = gate->m.n_experts ? gate->m.n_experts : 1;  // a dense FFN is expert 0 of one
     lt_status st;
     if (!direct && s.gemm) {
-        st = launched(ctx, lt::launch_moe_plan(c, ids, ntok, k, gate->m.n_experts, s.plan), "moe plan");
+        st = launched(ctx, lt::launch_moe_plan(c, ids, ntok, k, E, s.plan), "moe plan");
         if (st != LT_OK) return st;
         return launched(ctx,
                         lt::launch_moe_gemm_ffn(c, gate->m, upm.data, down->m, act, xf, ntok, k, w, s.plan, resid,
@@ -996,7 +997,7 @@ static lt_status ffn_impl(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *u
     st = ensure_counters(ctx, lt::kMoeCounterBase + s.counters);
     if (st != LT_OK) return st;
     if (!direct) {
-        st = launched(ctx, lt::launch_moe_plan(c, ids, ntok, k, gate->m.n_experts, s.plan), "moe plan");
+        st = launched(ctx, lt::launch_moe_plan(c, ids, ntok, k, E, s.plan), "moe plan");
         if (st != LT_OK) return st;
     }
     st = launched(ctx,

@@ -34,7 +34,11 @@ cudaError_t launch_quantize(const LaunchCfg &c, const float *x, uint32_t cols, u
 
 // ── routing plan (dispatch bookkeeping for more than one token) ───────────────
 
-__global__ void k_moe_plan(const uint32_t *ids, uint32_t npairs, uint32_t E, MoePlan p) {
+// Pairs whose id is not below E (an invalid caller id) get no position: the
+// down kernel skips them and the context's error word records it.
+constexpr uint32_t kNoPos = 0xffffffffu;
+
+__global__ void k_moe_plan(const uint32_t *ids, uint32_t npairs, uint32_t E, MoePlan p, int *dev_err) {
     extern __shared__ uint32_t sm_plan[];
     uint32_t *cnt = sm_plan, *cur = sm_plan + E;
     pdl_launch_dependents();
@@ -67,13 +71,16 @@ __global__ void k_moe_plan(const uint32_t *ids, uint32_t npairs, uint32_t E, Moe
             const uint32_t pos = atomicAdd(&cur[e], 1u);
             p.pair_pos[i] = pos;
             p.pos_pair[pos] = i;
+        } else {
+            p.pair_pos[i] = kNoPos;
+            if (dev_err) atomicExch(dev_err, DEV_ERR_BAD_INDEX);
         }
     }
 }
 
 cudaError_t launch_moe_plan(const LaunchCfg &c, const uint32_t *ids, uint32_t ntok, uint32_t k, uint32_t E,
                             const MoePlan &p) {
-    return launch_k(c, "moe_plan", k_moe_plan, dim3(1), dim3(1024), (size_t)2 * E * 4, ids, ntok * k, E, p);
+    return launch_k(c, "moe_plan", k_moe_plan, dim3(1), dim3(1024), (size_t)2 * E * 4, ids, ntok * k, E, p, c.dev_err);
 }
 
 // ── grouped gate/up with the activation fused ────────────────────────────────
@@ -91,6 +98,7 @@ struct GateUpArgs {
     const uint8_t *gate, *up;  // up == nullptr: fused gate_up tensor
     uint64_t pitch;
     uint32_t F, d, nitems, nblocks;
+    uint32_t E;  // experts (1 for a dense FFN)
     int act;
     const uint8_t *xq;  // qact rows of the tokens
     uint64_t xq_pitch;
@@ -136,6 +144,10 @@ __global__ void __launch_bounds__(kGuWarps * 32) k_moe_gate_up(GateUpArgs a) {
     if (a.direct) {
         if (blockIdx.y >= a.k) return;
         e = a.ids[blockIdx.y];
+        if (e >= a.E) {  // an invalid caller id: expert 0's rows stand in, the error word says so
+            if (threadIdx.x == 0 && a.dev_err) atomicExch(a.dev_err, DEV_ERR_BAD_INDEX);
+            e = 0;
+        }
         off = blockIdx.y;
         cnt = 1;
     } else {
@@ -245,6 +257,7 @@ cudaError_t launch_moe_gate_up(const LaunchCfg &c, const DevMat &gate, const Dev
     a.pitch = gate.pitch;
     a.F = (uint32_t)(fused ? gate.rows / 2 : gate.rows);
     a.d = (uint32_t)gate.cols;
+    a.E = gate.n_experts ? gate.n_experts : 1;
     a.nitems = items_per_row(gate.type, gate.cols);
     a.nblocks = (uint32_t)(gate.cols / 32);
     a.act = act;
@@ -297,6 +310,7 @@ struct DownArgs {
     const uint8_t *down;
     uint64_t pitch;
     uint32_t D, F, nitems, nblocks;  // down: [E][D rows][F cols]
+    uint32_t E;
     const uint8_t *hq;
     uint64_t hq_pitch;
     uint32_t ntok, k;
@@ -342,7 +356,8 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_moe_down(DownArgs a) {
             mbar_init(&bars[s], 1);
             fence_barrier_init();
             const uint32_t bytes = (uint32_t)(nr * a.pitch);
-            const uint32_t e = __ldcg(a.ids + t * a.k + s);
+            uint32_t e = __ldcg(a.ids + t * a.k + s);
+            if (e >= a.E) e = 0;  // an invalid caller id (recorded by the plan or gate/up): weight ignored below
             mbar_arrive_expect_tx(&bars[s], bytes);
             tma_load_1d(tile + (size_t)s * a.rt * a.pitch, a.down + ((uint64_t)e * a.D + r0) * a.pitch, bytes,
                         &bars[s]);
@@ -350,7 +365,8 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_moe_down(DownArgs a) {
     }
     if (threadIdx.x < (unsigned)k) {
         const uint32_t pair = t * a.k + threadIdx.x;
-        const uint32_t pos = a.direct ? pair : __ldcg(a.p.pair_pos + pair);
+        uint32_t pos = a.direct ? pair : __ldcg(a.p.pair_pos + pair);
+        if (pos == kNoPos) pos = 0;  // skipped in the combine below
         src[threadIdx.x] = a.hq + (size_t)pos * a.hq_pitch;
     }
     pdl_wait();
@@ -371,6 +387,7 @@ __global__ void __launch_bounds__(kDnWarps * 32) k_moe_down(DownArgs a) {
     for (int r = threadIdx.x; r < (int)nr; r += blockDim.x) {
         float o = 0.0f;  // moe_buf is zeroed, then += scale * down, slot by slot
         for (int s = 0; s < k; s++) {
+            if (__ldcg(a.ids + t * a.k + s) >= a.E) continue;  // an invalid id contributes nothing
             const float *pp = part + (s * (int)a.rt + r) * ipr;
             float y = 0.0f;
             for (int i = 0; i < ipr; i++) y += pp[i];
@@ -389,6 +406,7 @@ cudaError_t launch_moe_down(const LaunchCfg &c, const DevMat &down, const uint8_
     a.pitch = down.pitch;
     a.D = (uint32_t)down.rows;
     a.F = (uint32_t)down.cols;
+    a.E = down.n_experts ? down.n_experts : 1;
     a.nitems = items_per_row(down.type, down.cols);
     a.nblocks = (uint32_t)(down.cols / 32);
     a.hq = hq;

@@ -577,8 +577,11 @@ __global__ void k_gemm_combine(const float *y, uint32_t D, const uint32_t *pair_
     const uint32_t t = blockIdx.x, c = blockIdx.y * blockDim.x + threadIdx.x;  // token rows in x: no 65535 cap
     if (c >= D) return;
     float o = 0.0f;  // moe_buf is zeroed, then += scale * down, slot by slot (no fused multiply-add)
-    for (uint32_t s = 0; s < k; s++)
-        o = __fadd_rn(o, __fmul_rn(w[(size_t)t * k + s], y[(size_t)pair_pos[(size_t)t * k + s] * D + c]));
+    for (uint32_t s = 0; s < k; s++) {
+        const uint32_t pp = pair_pos[(size_t)t * k + s];
+        if (pp == 0xffffffffu) continue;  // a pair whose id the dispatch plan rejected contributes nothing
+        o = __fadd_rn(o, __fmul_rn(w[(size_t)t * k + s], y[(size_t)pp * D + c]));
+    }
     const size_t oi = (size_t)t * D + c;
     out[oi] = resid ? resid[oi] + o : o;
 }

@@ -526,3 +526,35 @@ def test_ffn_block_vs_oracle(ctx, oracle, t, d, F, act, ntok, residual):
         assert rel_l2(got[i], ref) < 1e-4, (i, rel_l2(got[i], ref))
     for w in (tg, tu, td):
         w.free()
+
+
+@pytest.mark.parametrize("T", [1, 6])
+def test_moe_ffn_invalid_id_reported(ctx, pkg, oracle, pool, T):
+    """An expert id past the tensor is an error the context reports (LT_EINVAL
+    at the next sync), with no read outside the weights: the pair contributes
+    nothing and the other pairs are unaffected."""
+    import importlib
+    synth = importlib.import_module("llmtoy-zig_b200.synth")
+    rng = np.random.Generator(np.random.PCG64(91 + T))
+    L = synth.MoeLayer(rng, 512, 8, 256, 12, 12)
+    rt, g, u, dn = _upload_layer(ctx, L)
+    x = rng.normal(0, 1, (T, 512)).astype(np.float32)
+    ids = rng.integers(0, 8, (T, 2)).astype(np.int32)
+    ids[0, 1] = 99
+    w = np.full((T, 2), 0.5, np.float32)
+    out = empty(T * 512)
+    ctx.moe_ffn(g, u, dn, 0, dev(x), T, dev(ids), dev(w), 2, out)
+    with pytest.raises(pkg.LtError) as e:
+        ctx.sync()
+    assert e.value.status == 1
+    ctx.sync()  # the error word was cleared
+    got = host(out).reshape(T, 512)
+    assert np.all(np.isfinite(got))
+    if T > 1:  # tokens without the bad id match a clean run
+        ok = ids.copy()
+        ok[0, 1] = 0
+        out2 = empty(T * 512)
+        ctx.moe_ffn(g, u, dn, 0, dev(x), T, dev(ok), dev(w), 2, out2)
+        np.testing.assert_array_equal(host(out2).reshape(T, 512)[1:], got[1:])
+    for t_ in (rt, g, u, dn):
+        t_.free()
