@@ -4,7 +4,9 @@
 // Each warp owns `rw` consecutive weight rows (rw * items_per_row <= 32, one
 // item per lane) and streams them into its shared-memory slice with one TMA
 // bulk copy issued before the kernel waits on its producer (the weights are
-// static).  Activations come pre-quantised (lt_qact.cuh).
+// static).  Activations come pre-quantised (lt_qact.cuh), or for a single
+// token as f32, which every CTA quantises into shared memory itself (one
+// launch and one global round trip fewer than a separate quantiser).
 #include "lt_qact.cuh"
 
 namespace lt {
@@ -15,8 +17,9 @@ struct QmvArgs {
     const uint8_t *rows;  // first row of the (expert) matrix
     uint64_t pitch;
     uint32_t nrows, cols, nitems, nblocks;
-    const uint8_t *xq;
+    const uint8_t *xq;  // nullptr: quantise xf (one token) in the CTA
     uint64_t xq_pitch;
+    const float *xf;
     float *y;
     const float *add;  // nullptr or y's shape: y = W . x + add
     uint32_t ntok;
@@ -59,9 +62,14 @@ __global__ void __launch_bounds__(kQmvWarps * 32) k_qmv(QmvArgs a) {
     float *wpart = part + (size_t)warp * NT * a.rw * ipr;
     for (uint32_t c0 = 0; c0 < a.ntok; c0 += NT) {
         const int nt = (int)min((uint32_t)NT, a.ntok - c0);
-        if (threadIdx.x < (unsigned)nt) src[threadIdx.x] = a.xq + (size_t)(c0 + threadIdx.x) * a.xq_pitch;
-        __syncthreads();
-        qact_to_smem(X, src, nt, (int)a.cols);
+        if (a.xq) {
+            if (threadIdx.x < (unsigned)nt) src[threadIdx.x] = a.xq + (size_t)(c0 + threadIdx.x) * a.xq_pitch;
+            __syncthreads();
+            qact_to_smem(X, src, nt, (int)a.cols);
+        } else {  // one token: the same 16-group quantisation as k_quantize, here
+            for (uint32_t b = warp; b < a.cols / 32; b += kQmvWarps)
+                qact_block_to_xs(X, 0, (int)b, __ldcg(a.xf + 32 * b + lane), lane);
+        }
         __syncthreads();
         if (c0 == 0 && nr > 0) ok = tile_wait(&bars[warp], a.dev_err);
         if (ok && nr > 0) {
@@ -138,6 +146,8 @@ cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert,
     a.nblocks = (uint32_t)(m.cols / 32);
     a.xq = xq;
     a.xq_pitch = xq_pitch;
+    a.xf = x;
+    if (!xq && ntok != 1) return cudaErrorInvalidValue;
     a.y = y;
     a.add = add;
     a.ntok = ntok;
