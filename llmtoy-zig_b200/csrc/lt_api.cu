@@ -609,7 +609,9 @@ static lt_status qmatvec_impl(lt_ctx *ctx, const lt_tensor *w, uint32_t expert, 
     if ((st = check_kernel_shape(ctx, w->m, "lt_qmatvec")) != LT_OK) return st;
     if (w->m.rows > 0xffffffffull) return fail(ctx, LT_EINVAL, "lt_qmatvec: too many rows");
     const lt::LaunchCfg c = cfg_of(ctx);
-    if (!quantized(w->m.type) || ntok == 1)  // f32/f16 rows, or one token quantised inside the matvec
+    // f32/f16 rows; or one token over few enough CTAs that each quantising it
+    // costs less than a separate quantiser launch (not the lm_head's thousands)
+    if (!quantized(w->m.type) || (ntok == 1 && lt::qmv_ctas(w->m) <= 2u * (uint32_t)ctx->num_sms))
         return launched(ctx, lt::launch_qmatvec(c, w->m, expert, nullptr, 0, dev_x, dev_y, ntok, dev_add), "qmatvec");
     const uint64_t qp = lt::qact_row_pitch(w->m.cols);
     if ((st = ensure_scratch(ctx, al256((size_t)ntok * qp))) != LT_OK) return st;
@@ -843,8 +845,7 @@ lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x,
     const lt::LaunchCfg c = cfg_of(ctx);
     if ((st = launched(ctx, lt::launch_rmsnorm(c, dev_x, dev_norm_w, eps, (uint32_t)d, 1, xb), "rmsnorm")) != LT_OK)
         return st;
-    if ((st = launched(ctx, lt::launch_qmatvec(c, wqkv->m, 0, nullptr, 0, xb, qkv, 1, dev_qkv_bias), "qmatvec")) != LT_OK)
-        return st;
+    if ((st = qmatvec_impl(ctx, wqkv, 0, xb, qkv, 1, dev_qkv_bias)) != LT_OK) return st;
     if ((st = ensure_counters(ctx, g.n_heads)) != LT_OK) return st;
     if ((st = launched(ctx, lt::launch_attn_prep(c, g, qkv, dev_q_norm, dev_k_norm, dev_pos, dev_k_cache, dev_v_cache),
                        "attn prep")) != LT_OK)
@@ -853,7 +854,7 @@ lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x,
                                                    (float *)ctx->scratch, ctx->counters),
                        "attn decode")) != LT_OK)
         return st;
-    return launched(ctx, lt::launch_qmatvec(c, wo->m, 0, nullptr, 0, att, dev_out, 1, dev_x), "qmatvec");
+    return qmatvec_impl(ctx, wo, 0, att, dev_out, 1, dev_x);
 }
 
 void lt_rng_seed(uint64_t seed, uint64_t state_out[4]) {

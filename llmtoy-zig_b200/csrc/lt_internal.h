@@ -153,6 +153,9 @@ cudaError_t launch_quantize(const LaunchCfg &c, const float *x, uint32_t cols, u
 // y[tok][rows] = W[expert] . x[tok].  Quantised types read the activations
 // from xq (quantised rows); f32/f16 matrices read x directly.
 // add != nullptr: y = W . x + add (same shape as y; may alias y).
+// CTAs of a quantised matvec over m's rows (each quantises a one-token input
+// itself when launch_qmatvec gets no pre-quantised rows).
+uint32_t qmv_ctas(const DevMat &m);
 cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert, const uint8_t *xq,
                            uint64_t xq_pitch, const float *x, float *y, uint32_t ntok,
                            const float *add = nullptr);

@@ -120,6 +120,11 @@ __global__ void k_mv_float(const uint8_t *rows, uint64_t pitch, uint32_t type, u
     }
 }
 
+uint32_t qmv_ctas(const DevMat &m) {
+    const uint32_t rw = max(1u, 32u / items_per_row(m.type, m.cols));
+    return (uint32_t)((m.rows + kQmvWarps * rw - 1) / (kQmvWarps * rw));
+}
+
 template <uint32_t TYPE, int NT>
 static cudaError_t launch_qmv_t(const LaunchCfg &c, const QmvArgs &a) {
     const size_t smem = qmv_smem_bytes(a.pitch, a.rw, NT, (int)a.nitems);
