@@ -185,13 +185,27 @@ lt_status lt_moe_forward(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *
  * i.e. the pre-FFN rmsnorm (src/ops/math.zig:20-26, src/model/forward.zig:304),
  * the router and experts of lt_moe_forward on the normalised vector, and the
  * residual add (src/model/forward.zig:309).  The norm and the residual are
- * fused into the router and down kernels (three launches per layer at one
+ * fused into the router and down kernels (one persistent launch at one
  * token).  dev_out may alias dev_x. */
 lt_status lt_moe_block(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *gate,
                        const lt_tensor *up, const lt_tensor *down, int act, int norm_topk,
                        const float *dev_expert_scale, const float *dev_norm_w, float eps,
                        const float *dev_x, uint32_t ntok, uint32_t k, float *dev_out,
                        uint32_t *dev_ids, float *dev_w);
+
+/* Gemma 4's MoE half (src/model/gemma4/forward.zig:401-494): the experts take
+ * rmsnorm(dev_x) * dev_norm_w, the router dev_x * rms_inv * router_gs *
+ * dev_router_scale (rmsnormWeightedAndRawScaled, src/ops/math.zig:51-82)
+ * with dev_expert_scale[e] on the selected weights;
+ *   dev_out = (residual ? dev_x : 0) + moe(...)
+ * One persistent launch at one token (lt_norm_pair + lt_moe_route +
+ * lt_moe_ffn otherwise, with the same results).  dev_out may alias dev_x. */
+lt_status lt_moe_block_scaled(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *gate,
+                              const lt_tensor *up, const lt_tensor *down, int act, int norm_topk,
+                              const float *dev_expert_scale, const float *dev_norm_w,
+                              const float *dev_router_scale, float router_gs, float eps,
+                              const float *dev_x, uint32_t ntok, uint32_t k, int residual,
+                              float *dev_out, uint32_t *dev_ids, float *dev_w);
 
 /* greedy (src/model/sample.zig:11-17): index of the first maximum of each of
  * ntok rows of length n (the argmax shader, src/gpu/shaders/argmax.glsl). */

@@ -40,7 +40,7 @@ EXPORTS = [
     "lt_device_alloc", "lt_device_free", "lt_copy_to_device", "lt_copy_to_host",
     "lt_embed", "lt_qmatvec_add", "lt_attn_prep", "lt_attn_decode", "lt_attn_block", "lt_prefetch_next",
     "lt_ffn_block", "lt_greedy_step", "lt_scale", "lt_add_rmsnorm", "lt_norm_pair", "lt_ffn_tail", "lt_softcap",
-    "lt_sample_step", "lt_rng_seed", "lt_quantize_q8_1", "lt_dequant_q8_1",
+    "lt_sample_step", "lt_rng_seed", "lt_quantize_q8_1", "lt_dequant_q8_1", "lt_moe_block_scaled",
 ]
 
 
@@ -113,6 +113,7 @@ def load_library() -> ctypes.CDLL:
         "lt_moe_ffn": (I, [P, P, P, P, I, P, U32, P, P, U32, P]),
         "lt_moe_forward": (I, [P, P, P, P, P, I, I, P, P, U32, U32, P, P, P]),
         "lt_moe_block": (I, [P, P, P, P, P, I, I, P, P, F, P, U32, U32, P, P, P]),
+        "lt_moe_block_scaled": (I, [P, P, P, P, P, I, I, P, P, P, F, F, P, U32, U32, I, P, P, P]),
         "lt_argmax": (I, [P, P, U32, U32, P]),
         "lt_profile_enable": (I, [P, I]),
         "lt_profile_read": (I, [P, U32, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(U64),
@@ -374,6 +375,16 @@ class Context:
     def attn_decode(self, cfg: AttnCfg, q, k_cache, v_cache, pos, out) -> None:
         self._check(self.lib.lt_attn_decode(self.ptr, ctypes.byref(cfg), _ptr(q), _ptr(k_cache), _ptr(v_cache),
                                             _ptr(pos), _ptr(out)))
+
+    def moe_block_scaled(self, router: Tensor, gate: Tensor, up: Tensor | None, down: Tensor, act: int,
+                         norm_topk: bool, expert_scale, norm_w, router_scale, router_gs: float, eps: float, x,
+                         ntok: int, k: int, out, residual: bool = False, ids=None, w=None) -> None:
+        """out = (x if residual) + moe(...): experts on rmsnorm(x) * norm_w, router on
+        x * rms_inv * router_gs * router_scale (Gemma 4's MoE half)."""
+        self._check(self.lib.lt_moe_block_scaled(self.ptr, router.handle, gate.handle, up.handle if up else None,
+                                                 down.handle, act, int(norm_topk), _ptr(expert_scale), _ptr(norm_w),
+                                                 _ptr(router_scale), router_gs, eps, _ptr(x), ntok, k,
+                                                 int(residual), _ptr(out), _ptr(ids), _ptr(w)))
 
     def attn_block(self, cfg: AttnCfg, x, norm_w, eps: float, wqkv: Tensor, qkv_bias, q_norm, k_norm, pos,
                    k_cache, v_cache, wo: Tensor, out) -> None:

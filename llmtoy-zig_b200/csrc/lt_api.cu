@@ -1032,7 +1032,8 @@ lt_status lt_moe_ffn(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, co
 static lt_status forward_impl(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *gate, const lt_tensor *up,
                               const lt_tensor *down, int act, int norm_topk, const float *dev_expert_scale,
                               const float *dev_norm_w, float eps, int residual, const float *dev_x, uint32_t ntok,
-                              uint32_t k, float *dev_out, uint32_t *dev_ids, float *dev_w) {
+                              uint32_t k, float *dev_out, uint32_t *dev_ids, float *dev_w,
+                              const float *dev_router_scale = nullptr, float router_gs = 1.0f) {
     struct Clear {
         lt_ctx *c;
         ~Clear() { clear_prefetch(c); }
@@ -1052,7 +1053,8 @@ static lt_status forward_impl(lt_ctx *ctx, const lt_tensor *router, const lt_ten
     const uint64_t d = gate->m.cols;
     const size_t gb = gemm_bytes_of(ctx, gate, down, ntok, k);
     const MoeScratch probe = moe_layout(nullptr, ntok, k, E, d, F, gb);
-    if ((st = ensure_scratch(ctx, probe.bytes)) != LT_OK) return st;
+    const size_t pair_b = dev_router_scale ? 2 * al256((size_t)ntok * d * 4) : 0;  // expert and router inputs
+    if ((st = ensure_scratch(ctx, probe.bytes + pair_b)) != LT_OK) return st;
     const MoeScratch s = moe_layout(ctx->scratch, ntok, k, E, d, F, gb);
     uint32_t *ids = dev_ids ? dev_ids : s.ids;
     float *w = dev_w ? dev_w : s.w;
@@ -1064,6 +1066,8 @@ static lt_status forward_impl(lt_ctx *ctx, const lt_tensor *router, const lt_ten
         p.router_ld = (uint32_t)(router->m.pitch / 4);
         p.x = dev_x;
         p.norm_w = dev_norm_w;
+        p.router_scale = dev_router_scale;
+        p.router_gs = router_gs;
         p.eps = eps;
         p.k = k;
         p.norm_topk = norm_topk;
@@ -1085,12 +1089,40 @@ static lt_status forward_impl(lt_ctx *ctx, const lt_tensor *router, const lt_ten
         }
         if (lt::moe_decode_fits(p, ctx->num_sms)) return launched(ctx, lt::launch_moe_decode(cfg_of(ctx), p), "moe decode");
     }
+    if (dev_router_scale) {  // separate inputs: norm_pair, then route and experts on them
+        const lt::LaunchCfg c = cfg_of(ctx);
+        float *xe = (float *)(ctx->scratch + probe.bytes), *xr = xe + pair_b / 8;
+        st = launched(ctx, lt::launch_norm_pair(c, dev_x, dev_norm_w, dev_router_scale, router_gs, eps, (uint32_t)d,
+                                                ntok, xe, xr),
+                      "norm pair");
+        if (st != LT_OK) return st;
+        st = route_impl(ctx, router, xr, nullptr, 0.0f, ntok, k, norm_topk, dev_expert_scale, ids, w, s.logits,
+                        nullptr, 0, nullptr);
+        if (st != LT_OK) return st;
+        if (!s.gemm) {
+            st = launched(ctx, lt::launch_quantize(c, xe, (uint32_t)d, ntok, s.xq, s.xq_pitch), "quantize");
+            if (st != LT_OK) return st;
+        }
+        return ffn_impl(ctx, gate, up, down, act, ntok, ids, w, k, residual ? dev_x : nullptr, dev_out, xe, s);
+    }
     float *xn = s.gemm && dev_norm_w ? s.xn : nullptr;  // the tensor-core path reads f32 rows
     st = route_impl(ctx, router, dev_x, dev_norm_w, eps, ntok, k, norm_topk, dev_expert_scale, ids, w, s.logits,
                     s.gemm ? nullptr : s.xq, s.xq_pitch, xn);
     if (st != LT_OK) return st;
     return ffn_impl(ctx, gate, up, down, act, ntok, ids, w, k, residual ? dev_x : nullptr, dev_out, xn ? xn : dev_x,
                     s);
+}
+
+lt_status lt_moe_block_scaled(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *gate, const lt_tensor *up,
+                              const lt_tensor *down, int act, int norm_topk, const float *dev_expert_scale,
+                              const float *dev_norm_w, const float *dev_router_scale, float router_gs, float eps,
+                              const float *dev_x, uint32_t ntok, uint32_t k, int residual, float *dev_out,
+                              uint32_t *dev_ids, float *dev_w) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!dev_norm_w || !dev_router_scale) return fail(ctx, LT_EINVAL, "lt_moe_block_scaled: null norm weights");
+    return forward_impl(ctx, router, gate, up, down, act, norm_topk, dev_expert_scale, dev_norm_w, eps, residual ? 1 : 0,
+                        dev_x, ntok, k, dev_out, dev_ids, dev_w, dev_router_scale, router_gs);
 }
 
 lt_status lt_moe_forward(lt_ctx *ctx, const lt_tensor *router, const lt_tensor *gate, const lt_tensor *up,

@@ -194,6 +194,10 @@ struct DecodeParams {
     const float *router;  // F32 [E][router_ld]; nullptr: a dense FFN (E = k = 1, weight 1)
     uint32_t E, d, router_ld;
     const float *x, *norm_w;
+    // nullable: the router takes x * rms_inv * router_gs * router_scale, the
+    // experts rmsnorm(x) * norm_w (Gemma 4's rmsnormWeightedAndRawScaled)
+    const float *router_scale = nullptr;
+    float router_gs = 1.0f;
     float eps;
     uint32_t k;
     int norm_topk;

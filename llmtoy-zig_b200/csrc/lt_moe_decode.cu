@@ -28,6 +28,10 @@
 //
 // Dense mode (a dense FFN block, forward.zig:307-312): no router; one slot
 // holds "expert" 0 -- the 2-D gate/up/down tensors -- with weight 1.
+// Scaled-router mode (Gemma 4, gemma4/forward.zig:401-413): the experts take
+// rmsnorm(x) * norm_w and the router x * rms_inv * router_gs * router_scale
+// (rmsnormWeightedAndRawScaled, math.zig:51-82), both from one rms_inv with
+// the norm_pair glue kernel's arithmetic.
 //
 // Per-item decoding, partial-sum orders and the combine are those of the
 // router / gate_up / down kernels, so both paths give the same bits.
@@ -55,6 +59,8 @@ struct DecodeArgs {
     uint32_t E, d, rw_ld;
     const float *x;       // [d]
     const float *norm_w;  // nullable
+    const float *router_scale;  // nullable: the router input is x * rms_inv * router_gs * router_scale
+    float router_gs;
     float eps;
     uint32_t k;
     int norm_topk;
@@ -187,7 +193,26 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     }
     __syncthreads();
     for (uint32_t r = tid; r < nr; r += kDecThreads) s_xres[r] = xsm[r0 + r];
-    if (a.norm_w) {  // rmsnorm(out, x, w, eps) with the router kernel's reduction order
+    const float *xrouter = xsm;  // the router's input
+    if (a.norm_w && a.router_scale) {  // norm_pair: one rms_inv, per-thread sums over 512 strided values
+        float ss = 0.0f;
+        for (uint32_t i = tid; i < a.d; i += kDecThreads) ss = __fadd_rn(ss, __fmul_rn(xsm[i], xsm[i]));
+        ss = warp_sum(ss);
+        if (lane == 0) part[warp] = ss;
+        __syncthreads();
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kDecWarps; w++) s += part[w];
+        const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)a.d), a.eps)));
+        const float rb = __fmul_rn(r, a.router_gs);
+        for (uint32_t i = tid; i < a.d; i += kDecThreads) {  // each thread its own elements: no hazard
+            const float xi = xsm[i];
+            const float e = __fmul_rn(__fmul_rn(xi, r), nwsm[i]);
+            nwsm[i] = __fmul_rn(__fmul_rn(xi, rb), __ldg(a.router_scale + i));
+            xsm[i] = e;
+        }
+        xrouter = nwsm;
+    } else if (a.norm_w) {  // rmsnorm(out, x, w, eps) with the router kernel's reduction order
         float ss = 0.0f;
         if (tid < kDecNormThreads)
             for (uint32_t i = tid; i < a.d; i += kDecNormThreads) ss += xsm[i] * xsm[i];
@@ -211,7 +236,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     // normalised x for this CTA's gate/up meanwhile
     const uint32_t nlw = a.dense ? 0 : a.E > c ? (a.E - c + G - 1) / G : 0;
     if (has_e) {
-        const float v = router_logit(a.rw + (size_t)e_mine * a.rw_ld, xsm, a.d, lane, w0);
+        const float v = router_logit(a.rw + (size_t)e_mine * a.rw_ld, xrouter, a.d, lane, w0);
         if (lane == 0) st_relaxed_u64(lslots + e_mine, ((uint64_t)tag << 32) | __float_as_uint(v));
     } else {
         for (uint32_t b = warp - nlw; b < a.d / 32; b += kDecWarps - nlw)
@@ -428,6 +453,8 @@ bool decode_plan(const DecodeParams &p, int num_sms, DecodePlan &out) {
     a.rw_ld = p.router_ld;
     a.x = p.x;
     a.norm_w = p.norm_w;
+    a.router_scale = p.router_scale;
+    a.router_gs = p.router_gs;
     a.eps = p.eps;
     a.k = p.k;
     a.norm_topk = p.norm_topk;

@@ -142,12 +142,10 @@ lt_status gemma_layer(lth_decoder *d, uint32_t l) {
     LTH_TRY(lt_ffn_block(c, L.ffn_gate, L.ffn_up, L.ffn_down, LT_ACT_GELU_TANH, L.ffn_norm, m.eps, d->x, 1, 0,
                          d->fbuf));
     LTH_TRY(lt_rmsnorm(c, d->fbuf, L.post_ffw_norm_1, m.eps, m.d_model, 1, d->fbuf));
-    // MoE: weighted and raw-scaled norms of x, router, experts (:401-494)
-    LTH_TRY(lt_norm_pair(c, d->x, L.pre_ffw_norm_2, L.router_scale, 1.0f / __builtin_sqrtf((float)m.d_model), m.eps,
-                         m.d_model, 1, d->moe_in, d->router_in));
-    LTH_TRY(lt_moe_route(c, L.router, d->router_in, 1, m.n_used, 0, L.down_exps_scale, d->ids, d->wts));
-    LTH_TRY(lt_moe_ffn(c, L.exp_gate, L.exp_up, L.exp_down, LT_ACT_GELU_TANH, d->moe_in, 1, d->ids, d->wts, m.n_used,
-                       d->mbuf));
+    // MoE: weighted and raw-scaled norms of x, router, experts (:401-494) in one launch
+    LTH_TRY(lt_moe_block_scaled(c, L.router, L.exp_gate, L.exp_up, L.exp_down, LT_ACT_GELU_TANH, 0, L.down_exps_scale,
+                                L.pre_ffw_norm_2, L.router_scale, 1.0f / __builtin_sqrtf((float)m.d_model), m.eps,
+                                d->x, 1, m.n_used, 0, d->mbuf, d->ids, d->wts));
     return lt_ffn_tail(c, d->fbuf, d->mbuf, L.post_ffw_norm_2, L.post_ffw_norm, L.layer_output_scale, m.eps,
                        m.d_model, 1, d->x);
 }

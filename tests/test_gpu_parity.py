@@ -558,3 +558,40 @@ def test_moe_ffn_invalid_id_reported(ctx, pkg, oracle, pool, T):
         np.testing.assert_array_equal(host(out2).reshape(T, 512)[1:], got[1:])
     for t_ in (rt, g, u, dn):
         t_.free()
+
+
+@pytest.mark.parametrize("T", [1, 3])
+def test_moe_block_scaled_matches_ops(ctx, pkg, T):
+    """lt_moe_block_scaled (Gemma 4's MoE half) against the separate ops it
+    replaces -- lt_norm_pair, lt_moe_route on the raw-scaled input, lt_moe_ffn on
+    the weighted one: the same ids and weights bit for bit (the router input is
+    norm_pair's arithmetic), outputs within f32 rounding of the expert kernels'
+    different partial-sum grouping (one persistent launch at T = 1; at T = 3
+    the ops themselves, bit for bit)."""
+    import importlib
+    synth = importlib.import_module("llmtoy-zig_b200.synth")
+    rng = np.random.Generator(np.random.PCG64(2816 + T))
+    d, E, F, k = 2816, 32, 704, 8
+    L = synth.MoeLayer(rng, d, E, F, 12, 8, fused=True)
+    rt, g, u, dn = _upload_layer(ctx, L)
+    x = rng.normal(0, 2, (T, d)).astype(np.float32)
+    nw = dev(rng.uniform(0.5, 1.5, d).astype(np.float32))
+    rs = dev(rng.uniform(0.5, 1.5, d).astype(np.float32))
+    es = dev(rng.uniform(0.5, 2.0, E).astype(np.float32))
+    gs = float(np.float32(1.0 / np.sqrt(d)))
+    out, ids, w = empty(T * d), empty(T * k, "int32"), empty(T * k)
+    ctx.moe_block_scaled(rt, g, None, dn, 1, False, es, nw, rs, gs, 1e-6, dev(x), T, k, out, False, ids, w)
+    a, b = empty(T * d), empty(T * d)
+    ctx.norm_pair(dev(x), nw, rs, gs, 1e-6, d, T, a, b)
+    ids2, w2, out2 = empty(T * k, "int32"), empty(T * k), empty(T * d)
+    ctx.moe_route(rt, b, T, k, False, es, ids2, w2)
+    ctx.moe_ffn(g, None, dn, 1, a, T, ids2, w2, k, out2)
+    np.testing.assert_array_equal(host(ids), host(ids2))
+    np.testing.assert_array_equal(bits(host(w)), bits(host(w2)))
+    if T == 1:
+        assert rel_l2(host(out), host(out2)) < 1e-5
+    else:
+        np.testing.assert_array_equal(bits(host(out)), bits(host(out2)))
+    for t_ in (rt, g, u, dn):
+        if t_ is not None:
+            t_.free()
