@@ -79,6 +79,7 @@ struct DecodeArgs {
     uint32_t img;
     int residual;
     int dense;   // no router: slot 0 = expert 0 with weight 1
+    int late_down;  // down tiles copied after the h barrier into the gate/up tiles' space
     float *out;  // [d], may alias x
     uint8_t *sync;
     int *dev_err;
@@ -93,9 +94,11 @@ struct DecodeLayout {
 
 __host__ __device__ inline uint32_t chunks64(uint32_t cols) { return (cols + 63) / 64; }
 
+// late_down: the down tiles share the gate/up tiles' space and are copied
+// after the h barrier (when both do not fit at once).
 __host__ __device__ inline DecodeLayout decode_layout(uint32_t E, uint32_t d, uint32_t F, uint32_t k, uint64_t gpitch,
                                                       uint32_t gi, uint64_t dpitch, uint32_t di, uint32_t img,
-                                                      uint32_t maxpairs, uint32_t maxrows) {
+                                                      uint32_t maxpairs, uint32_t maxrows, int late_down) {
     DecodeLayout L;
     size_t off = 0;
     auto take = [&](size_t b) {
@@ -116,8 +119,14 @@ __host__ __device__ inline DecodeLayout decode_layout(uint32_t E, uint32_t d, ui
     L.xsx = take(xs_bytes(1, gi));
     const size_t rr0 = (size_t)2 * d * 4, rr1 = (size_t)k * img;
     L.rr = take(rr0 > rr1 ? rr0 : rr1);
-    L.gt = take((size_t)maxpairs * 2 * gpitch);
-    L.dt = take((size_t)k * maxrows * dpitch);
+    const size_t gtb = (size_t)maxpairs * 2 * gpitch, dtb = (size_t)k * maxrows * dpitch;
+    if (late_down) {
+        L.gt = take(gtb > dtb ? gtb : dtb);
+        L.dt = L.gt;
+    } else {
+        L.gt = take(gtb);
+        L.dt = take(dtb);
+    }
     take(128);  // the last Q8_0 chunk of a row reads up to 34 bytes past it
     L.total = off;
     return L;
@@ -129,7 +138,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t G = gridDim.x, c = blockIdx.x;
     const DecodeLayout L =
-        decode_layout(a.E, a.d, a.F, a.k, a.gpitch, a.gi, a.dpitch, a.di, a.img, a.maxpairs, a.maxrows);
+        decode_layout(a.E, a.d, a.F, a.k, a.gpitch, a.gi, a.dpitch, a.di, a.img, a.maxpairs, a.maxrows, a.late_down);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
     uint64_t *hbar = bars + kDecMaxChunks + 16;
     uint32_t *s_sel = reinterpret_cast<uint32_t *>(smem + L.misc);    // [16]
@@ -298,7 +307,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
             tma_load_1d(dst + bytes, ub + urow * a.gpitch, bytes, &bars[j]);
         }
     } else if (warp == 1) {  // down rows [r0, r1) of each slot's expert
-        if ((uint32_t)lane < a.k && nr) {
+        if (!a.late_down && (uint32_t)lane < a.k && nr) {
             const uint32_t e = min(s_sel[lane], a.E - 1);
             const uint32_t bytes = (uint32_t)(nr * a.dpitch);
             mbar_arrive_expect_tx(&bars[kDecMaxChunks + lane], bytes);
@@ -382,6 +391,14 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
         mbar_arrive_expect_tx(hbar, a.k * a.img);
         for (uint32_t s = 0; s < a.k; s++)
             tma_load_1d(himg_s + (size_t)s * a.img, a.himg + (size_t)s * a.img, a.img, hbar);
+        if (a.late_down && nr)  // the gate/up tiles are consumed: the down rows take their place
+            for (uint32_t s = 0; s < a.k; s++) {
+                const uint32_t e = min(s_sel[s], a.E - 1);
+                const uint32_t bytes = (uint32_t)(nr * a.dpitch);
+                mbar_arrive_expect_tx(&bars[kDecMaxChunks + s], bytes);
+                tma_load_1d(dt + (size_t)s * a.maxrows * a.dpitch, a.down + ((uint64_t)e * a.d + r0) * a.dpitch, bytes,
+                            &bars[kDecMaxChunks + s]);
+            }
     }
     const bool hok = tile_wait(hbar, a.dev_err);
     // down: warps [s*wps, (s+1)*wps) take slot s; a lane owns one 64-column
@@ -488,8 +505,12 @@ bool decode_plan(const DecodeParams &p, int num_sms, DecodePlan &out) {
     a.maxpairs = (uint32_t)(kDecUnit * ((nunits + G - 1) / G));
     a.maxrows = (p.d + G - 1) / G;
     if (a.maxpairs / kDecChunk > (uint32_t)kDecMaxChunks) return false;
-    const DecodeLayout L =
-        decode_layout(a.E, a.d, a.F, a.k, a.gpitch, a.gi, a.dpitch, a.di, a.img, a.maxpairs, a.maxrows);
+    a.late_down = 0;
+    DecodeLayout L = decode_layout(a.E, a.d, a.F, a.k, a.gpitch, a.gi, a.dpitch, a.di, a.img, a.maxpairs, a.maxrows, 0);
+    if (L.total > kDecodeSmemLimit) {
+        a.late_down = 1;
+        L = decode_layout(a.E, a.d, a.F, a.k, a.gpitch, a.gi, a.dpitch, a.di, a.img, a.maxpairs, a.maxrows, 1);
+    }
     out.smem = L.total;
     return L.total <= kDecodeSmemLimit;
 }
