@@ -331,6 +331,14 @@ typedef struct lt_attn_cfg {
 lt_status lt_embed(lt_ctx *ctx, const lt_tensor *emb, const uint32_t *dev_tokens,
                    const uint32_t *dev_pos, float *dev_out);
 
+/* Up to four one-token quantMatvec calls on the same input vector in one
+ * launch, e.g. a layer's separate Q, K and V projections (forward.zig:278-281):
+ * dev_y[i] = w[i] . xn with xn = dev_x, or rmsnorm(dev_x) * dev_norm_w when
+ * dev_norm_w is given (the pre-attention norm folded in, math.zig:20-26).
+ * The tensors share cols and may differ in type. */
+lt_status lt_qmatvec_multi(lt_ctx *ctx, uint32_t n, const lt_tensor *const *w, const float *dev_x,
+                           const float *dev_norm_w, float eps, float *const *dev_y);
+
 /* quantMatvec plus an addend of y's shape: y = W . x + add -- the residual
  * `x += wo . attn` (forward.zig:304-305) or the Q/K/V biases (:285-287).
  * dev_add may alias dev_y. */

@@ -41,6 +41,7 @@ EXPORTS = [
     "lt_embed", "lt_qmatvec_add", "lt_attn_prep", "lt_attn_decode", "lt_attn_block", "lt_prefetch_next",
     "lt_ffn_block", "lt_greedy_step", "lt_scale", "lt_add_rmsnorm", "lt_norm_pair", "lt_ffn_tail", "lt_softcap",
     "lt_sample_step", "lt_rng_seed", "lt_quantize_q8_1", "lt_dequant_q8_1", "lt_moe_block_scaled",
+    "lt_qmatvec_multi",
 ]
 
 
@@ -114,6 +115,7 @@ def load_library() -> ctypes.CDLL:
         "lt_moe_forward": (I, [P, P, P, P, P, I, I, P, P, U32, U32, P, P, P]),
         "lt_moe_block": (I, [P, P, P, P, P, I, I, P, P, F, P, U32, U32, P, P, P]),
         "lt_moe_block_scaled": (I, [P, P, P, P, P, I, I, P, P, P, F, F, P, U32, U32, I, P, P, P]),
+        "lt_qmatvec_multi": (I, [P, U32, P, P, P, F, P]),
         "lt_argmax": (I, [P, P, U32, U32, P]),
         "lt_profile_enable": (I, [P, I]),
         "lt_profile_read": (I, [P, U32, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(U64),
@@ -364,6 +366,13 @@ class Context:
     # -- decode-step ops ---------------------------------------------------
     def embed(self, emb: Tensor, tokens, pos, out) -> None:
         self._check(self.lib.lt_embed(self.ptr, emb.handle, _ptr(tokens), _ptr(pos), _ptr(out)))
+
+    def qmatvec_multi(self, ws: list, x, ys: list, norm_w=None, eps: float = 1e-6) -> None:
+        """ys[i] = ws[i] . xn for one token, xn = x or rmsnorm(x) * norm_w, in one launch."""
+        n = len(ws)
+        hw = (ctypes.c_void_p * n)(*[w.handle for w in ws])
+        hy = (ctypes.c_void_p * n)(*[_ptr(y) for y in ys])
+        self._check(self.lib.lt_qmatvec_multi(self.ptr, n, hw, _ptr(x), _ptr(norm_w), eps, hy))
 
     def qmatvec_add(self, w: Tensor, x, add, y, ntok: int = 1, expert: int = 0) -> None:
         self._check(self.lib.lt_qmatvec_add(self.ptr, w.handle, expert, _ptr(x), _ptr(add), _ptr(y), ntok))

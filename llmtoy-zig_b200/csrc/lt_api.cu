@@ -621,6 +621,23 @@ static lt_status qmatvec_impl(lt_ctx *ctx, const lt_tensor *w, uint32_t expert, 
     return launched(ctx, lt::launch_qmatvec(c, w->m, expert, xq, qp, dev_x, dev_y, ntok, dev_add), "qmatvec");
 }
 
+lt_status lt_qmatvec_multi(lt_ctx *ctx, uint32_t n, const lt_tensor *const *w, const float *dev_x,
+                           const float *dev_norm_w, float eps, float *const *dev_y) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (n == 0 || n > 4 || !w || !dev_x || !dev_y) return fail(ctx, LT_EINVAL, "lt_qmatvec_multi: bad argument");
+    const lt::DevMat *m[4];
+    for (uint32_t i = 0; i < n; i++) {
+        if (!w[i] || !dev_y[i]) return fail(ctx, LT_EINVAL, "lt_qmatvec_multi: null tensor or output %u", i);
+        if (!quantized(w[i]->m.type)) return fail(ctx, LT_EUNSUPPORTED_TYPE, "lt_qmatvec_multi: tensor %u not block-quantised", i);
+        if (w[i]->m.n_experts) return fail(ctx, LT_EINVAL, "lt_qmatvec_multi: tensor %u is an expert tensor", i);
+        if (w[i]->m.cols != w[0]->m.cols) return fail(ctx, LT_EINVAL, "lt_qmatvec_multi: column counts differ");
+        if ((st = check_kernel_shape(ctx, w[i]->m, "lt_qmatvec_multi")) != LT_OK) return st;
+        m[i] = &w[i]->m;
+    }
+    return launched(ctx, lt::launch_qmatvec_multi(cfg_of(ctx), n, m, dev_x, dev_norm_w, eps, dev_y), "qmatvec multi");
+}
+
 lt_status lt_qmatvec(lt_ctx *ctx, const lt_tensor *w, uint32_t expert, const float *dev_x, float *dev_y,
                      uint32_t ntok) {
     return qmatvec_impl(ctx, w, expert, dev_x, dev_y, ntok, nullptr);

@@ -136,6 +136,39 @@ LT_DEVINL float warp_sum(float v) {
     return v;
 }
 
+// Sum of one value per thread over the block (warp sums, then the warps in order).
+LT_DEVINL float block_sum(float v, float *red) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float s = 0.0f;
+    for (int i = 0; i < nw; i++) s += red[i];
+    return s;
+}
+
+// 1 / sqrt(sum(x^2) / n + eps) over the block (math.zig:20-26): per-thread sums
+// over 16-element strided batches, then block_sum.  One order for every kernel
+// that normalises a row this way, so they agree bit for bit.
+LT_DEVINL float rms_inv_block(const float *x, uint32_t n, float eps, float *red) {
+    constexpr int kBatch = 16;
+    float ss = 0.0f;
+    for (uint32_t base = threadIdx.x; base < n; base += kBatch * blockDim.x) {
+        float v[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; j++) {
+            const uint32_t i = base + j * blockDim.x;
+            v[j] = i < n ? x[i] : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; j++) ss += v[j] * v[j];
+    }
+    ss = block_sum(ss, red);
+    return 1.0f / sqrtf(ss / (float)n + eps);
+}
+
+
 // Programmatic dependent launch.  Data written by the previous kernel on the
 // stream may only be read after pdl_wait(); kernels that are not launched
 // with the PDL attribute see these as no-ops.

@@ -156,6 +156,10 @@ cudaError_t launch_quantize(const LaunchCfg &c, const float *x, uint32_t cols, u
 // CTAs of a quantised matvec over m's rows (each quantises a one-token input
 // itself when launch_qmatvec gets no pre-quantised rows).
 uint32_t qmv_ctas(const DevMat &m);
+// n <= 4 one-token matvecs y[s] = m[s] . x (x normalised by norm_w first when
+// given) in one launch; the matrices share cols and may differ in type.
+cudaError_t launch_qmatvec_multi(const LaunchCfg &c, uint32_t n, const DevMat *const *m, const float *x,
+                                 const float *norm_w, float eps, float *const *y);
 cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert, const uint8_t *xq,
                            uint64_t xq_pitch, const float *x, float *y, uint32_t ntok,
                            const float *add = nullptr);

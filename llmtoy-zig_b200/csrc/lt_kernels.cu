@@ -331,17 +331,6 @@ cudaError_t launch_dequant_q8_1(const LaunchCfg &c, const uint8_t *q, uint64_t n
 
 // ── rmsnorm / softmax / argmax ─────────────────────────────────────────────
 
-LT_DEVINL float block_sum(float v, float *red) {
-    v = warp_sum(v);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float s = 0.0f;
-    for (int i = 0; i < nw; i++) s += red[i];
-    return s;
-}
-
 LT_DEVINL float block_max(float v, float *red) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -356,25 +345,12 @@ LT_DEVINL float block_max(float v, float *red) {
 
 // src/ops/math.zig:20-26
 __global__ void k_rmsnorm(const float *x, const float *w, float eps, uint32_t n, float *y) {
-    constexpr int kBatch = 16;
     __shared__ float red[32];
     pdl_launch_dependents();
     pdl_wait();
     const float *xt = x + (size_t)blockIdx.x * n;
     float *yt = y + (size_t)blockIdx.x * n;
-    float ss = 0.0f;
-    for (uint32_t base = threadIdx.x; base < n; base += kBatch * blockDim.x) {
-        float v[kBatch];
-#pragma unroll
-        for (int j = 0; j < kBatch; j++) {
-            const uint32_t i = base + j * blockDim.x;
-            v[j] = i < n ? xt[i] : 0.0f;
-        }
-#pragma unroll
-        for (int j = 0; j < kBatch; j++) ss += v[j] * v[j];
-    }
-    ss = block_sum(ss, red);
-    const float rms_inv = 1.0f / sqrtf(ss / (float)n + eps);
+    const float rms_inv = rms_inv_block(xt, n, eps, red);
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) yt[i] = xt[i] * rms_inv * w[i];
 }
 

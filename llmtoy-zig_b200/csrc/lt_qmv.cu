@@ -20,6 +20,8 @@ struct QmvArgs {
     const uint8_t *xq;  // nullptr: quantise xf (one token) in the CTA
     uint64_t xq_pitch;
     const float *xf;
+    const float *norm_w;  // with xq == nullptr: quantise rmsnorm(xf) * norm_w instead
+    float eps;
     float *y;
     const float *add;  // nullptr or y's shape: y = W . x + add
     uint32_t ntok;
@@ -32,9 +34,9 @@ __host__ __device__ inline size_t qmv_smem_bytes(uint64_t pitch, uint32_t rw, in
            (size_t)kQmvWarps * nt * rw * ipr * 4;
 }
 
+// One CTA's rows (CTA index cta of the matrix's grid).
 template <uint32_t TYPE, int NT>
-__global__ void __launch_bounds__(kQmvWarps * 32) k_qmv(QmvArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
+LT_DEVINL void qmv_cta(const QmvArgs &a, uint32_t cta, uint8_t *smem) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ipr = (int)a.nitems;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
@@ -45,7 +47,7 @@ __global__ void __launch_bounds__(kQmvWarps * 32) k_qmv(QmvArgs a) {
     p += align16(xs_bytes(NT, ipr));
     float *part = reinterpret_cast<float *>(p);
 
-    const uint32_t wr0 = (blockIdx.x * kQmvWarps + warp) * a.rw;
+    const uint32_t wr0 = (cta * kQmvWarps + warp) * a.rw;
     const int nr = wr0 < a.nrows ? (int)min(a.rw, a.nrows - wr0) : 0;
     uint8_t *wt = tile + (size_t)warp * a.rw * a.pitch;
     if (lane == 0 && nr > 0) {  // weights are static: fetch before waiting on the producer
@@ -66,6 +68,13 @@ __global__ void __launch_bounds__(kQmvWarps * 32) k_qmv(QmvArgs a) {
             if (threadIdx.x < (unsigned)nt) src[threadIdx.x] = a.xq + (size_t)(c0 + threadIdx.x) * a.xq_pitch;
             __syncthreads();
             qact_to_smem(X, src, nt, (int)a.cols);
+        } else if (a.norm_w) {  // one token, normalised as k_rmsnorm does, quantised as k_quantize does
+            float *red = reinterpret_cast<float *>(smem + 64);  // the row-pointer slots, unused here
+            const float r = rms_inv_block(a.xf, a.cols, a.eps, red);
+            for (uint32_t b = warp; b < a.cols / 32; b += kQmvWarps) {
+                const uint32_t i = 32 * b + lane;
+                qact_block_to_xs(X, 0, (int)b, __ldcg(a.xf + i) * r * __ldg(a.norm_w + i), lane);
+            }
         } else {  // one token: the same 16-group quantisation as k_quantize, here
             for (uint32_t b = warp; b < a.cols / 32; b += kQmvWarps)
                 qact_block_to_xs(X, 0, (int)b, __ldcg(a.xf + 32 * b + lane), lane);
@@ -94,6 +103,40 @@ __global__ void __launch_bounds__(kQmvWarps * 32) k_qmv(QmvArgs a) {
             }
         }
         __syncthreads();
+    }
+}
+
+template <uint32_t TYPE, int NT>
+__global__ void __launch_bounds__(kQmvWarps * 32) k_qmv(QmvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    qmv_cta<TYPE, NT>(a, blockIdx.x, smem);
+}
+
+// Up to four one-token matvecs on the same input in one launch: CTAs
+// [begin[s], begin[s+1]) run matrix s, whatever its type.
+constexpr int kQmvMaxSeg = 4;
+struct QmvMulti {
+    QmvArgs seg[kQmvMaxSeg];
+    uint32_t type[kQmvMaxSeg];
+    uint32_t begin[kQmvMaxSeg + 1];
+    uint32_t n;
+};
+
+__global__ void __launch_bounds__(kQmvWarps * 32) k_qmv_multi(QmvMulti m) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint32_t s = 0;
+    while (s + 1 < m.n && blockIdx.x >= m.begin[s + 1]) s++;
+    const uint32_t cta = blockIdx.x - m.begin[s];
+    switch (m.type[s]) {
+    case T_Q4_K: qmv_cta<T_Q4_K, 1>(m.seg[s], cta, smem); break;
+    case T_Q6_K: qmv_cta<T_Q6_K, 1>(m.seg[s], cta, smem); break;
+    case T_Q8_0: qmv_cta<T_Q8_0, 1>(m.seg[s], cta, smem); break;
+    case T_Q5_K: qmv_cta<T_Q5_K, 1>(m.seg[s], cta, smem); break;
+    case T_Q3_K: qmv_cta<T_Q3_K, 1>(m.seg[s], cta, smem); break;
+    case T_Q5_0: qmv_cta<T_Q5_0, 1>(m.seg[s], cta, smem); break;
+    case T_Q5_1: qmv_cta<T_Q5_1, 1>(m.seg[s], cta, smem); break;
+    case T_IQ4_NL: qmv_cta<T_IQ4_NL, 1>(m.seg[s], cta, smem); break;
+    default: break;
     }
 }
 
@@ -152,6 +195,8 @@ cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert,
     a.xq = xq;
     a.xq_pitch = xq_pitch;
     a.xf = x;
+    a.norm_w = nullptr;
+    a.eps = 0.0f;
     if (!xq && ntok != 1) return cudaErrorInvalidValue;
     a.y = y;
     a.add = add;
@@ -170,6 +215,48 @@ cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert,
     case T_Q3_K: return one ? launch_qmv_t<T_Q3_K, 1>(c, a) : launch_qmv_t<T_Q3_K, 2>(c, a);
     default: return cudaErrorInvalidValue;
     }
+}
+
+static QmvArgs qmv_args_one(const LaunchCfg &c, const DevMat &m, const float *x, float *y, const float *norm_w,
+                            float eps) {
+    QmvArgs a{};
+    a.rows = m.data;
+    a.pitch = m.pitch;
+    a.nrows = (uint32_t)m.rows;
+    a.cols = (uint32_t)m.cols;
+    a.nitems = items_per_row(m.type, m.cols);
+    a.nblocks = (uint32_t)(m.cols / 32);
+    a.xq = nullptr;
+    a.xq_pitch = 0;
+    a.xf = x;
+    a.norm_w = norm_w;
+    a.eps = eps;
+    a.y = y;
+    a.add = nullptr;
+    a.ntok = 1;
+    a.rw = max(1u, 32u / a.nitems);
+    a.dev_err = c.dev_err;
+    return a;
+}
+
+cudaError_t launch_qmatvec_multi(const LaunchCfg &c, uint32_t n, const DevMat *const *m, const float *x,
+                                 const float *norm_w, float eps, float *const *y) {
+    if (n == 0 || n > (uint32_t)kQmvMaxSeg) return cudaErrorInvalidValue;
+    QmvMulti q{};
+    q.n = n;
+    size_t smem = 0;
+    uint32_t ctas = 0;
+    for (uint32_t s = 0; s < n; s++) {
+        if (!is_quant_type(m[s]->type)) return cudaErrorInvalidValue;
+        q.seg[s] = qmv_args_one(c, *m[s], x, y[s], norm_w, eps);
+        q.type[s] = m[s]->type;
+        q.begin[s] = ctas;
+        ctas += qmv_ctas(*m[s]);
+        const size_t b = qmv_smem_bytes(q.seg[s].pitch, q.seg[s].rw, 1, (int)q.seg[s].nitems);
+        smem = b > smem ? b : smem;
+    }
+    q.begin[n] = ctas;
+    return launch_k(c, "qmv_multi", k_qmv_multi, dim3(ctas), dim3(kQmvWarps * 32), smem, q);
 }
 
 }  // namespace lt

@@ -84,13 +84,19 @@ lt_status attn_ops(lth_decoder *d, const lth_layer &L, void *kc, void *vc) {
     const lth_model &m = d->m;
     lt_ctx *c = d->ctx;
     const uint32_t *pos = d->state;
-    LTH_TRY(lt_rmsnorm(c, d->x, L.attn_norm, m.eps, m.d_model, 1, d->xb));
+    if (!L.wqkv && !L.qkv_bias) {  // the norm and the three projections in one launch
+        const lt_tensor *w[3] = {L.wq, L.wk, L.wv};
+        float *y[3] = {d->qkv, d->qkv + d->nq, d->qkv + d->nq + d->nkv};
+        LTH_TRY(lt_qmatvec_multi(c, 3, w, d->x, L.attn_norm, m.eps, y));
+    } else {
+        LTH_TRY(lt_rmsnorm(c, d->x, L.attn_norm, m.eps, m.d_model, 1, d->xb));
+    }
     if (L.wqkv) {
         if (L.qkv_bias)
             LTH_TRY(lt_qmatvec_add(c, L.wqkv, 0, d->xb, L.qkv_bias, d->qkv, 1));
         else
             LTH_TRY(lt_qmatvec(c, L.wqkv, 0, d->xb, d->qkv, 1));
-    } else {
+    } else if (L.qkv_bias) {
         const lt_tensor *w[3] = {L.wq, L.wk, L.wv};
         const uint32_t off[3] = {0, d->nq, d->nq + d->nkv};
         for (int i = 0; i < 3; i++) {
@@ -126,13 +132,10 @@ lt_status gemma_layer(lth_decoder *d, uint32_t l) {
     a.v_norm = 1;
     a.kv_f16 = m.kv_f16 ? 1u : 0u;
     void *kc = d->kcache + d->kv_off[l] * d->kv_esize, *vc = d->vcache + d->kv_off[l] * d->kv_esize;
-    LTH_TRY(lt_rmsnorm(c, d->x, L.attn_norm, m.eps, m.d_model, 1, d->xb));
-    LTH_TRY(lt_qmatvec(c, L.wq, 0, d->xb, d->qkv, 1));
-    LTH_TRY(lt_qmatvec(c, L.wk, 0, d->xb, d->qkv + nq, 1));
-    if (L.wv) {
-        LTH_TRY(lt_qmatvec(c, L.wv, 0, d->xb, d->qkv + nq + nkv, 1));
-    } else {  // V = K before the norms (forward.zig:250)
-        LTH_TRY(lt_gather_rows(c, d->qkv + nq, nkv, d->ids_zero, 1, d->qkv + nq + nkv));
+    {  // the attention norm and Q, K, V in one launch; without wv, V = K before the norms (forward.zig:250)
+        const lt_tensor *w[3] = {L.wq, L.wk, L.wv ? L.wv : L.wk};
+        float *y[3] = {d->qkv, d->qkv + nq, d->qkv + nq + nkv};
+        LTH_TRY(lt_qmatvec_multi(c, 3, w, d->x, L.attn_norm, m.eps, y));
     }
     LTH_TRY(lt_attn_prep(c, &a, d->qkv, L.q_norm, L.k_norm, pos, kc, vc));
     LTH_TRY(lt_attn_decode(c, &a, d->qkv, kc, vc, pos, d->att));

@@ -595,3 +595,32 @@ def test_moe_block_scaled_matches_ops(ctx, pkg, T):
     for t_ in (rt, g, u, dn):
         if t_ is not None:
             t_.free()
+
+
+@pytest.mark.parametrize("norm", [False, True])
+def test_qmatvec_multi_matches_separate(ctx, pkg, norm):
+    """lt_qmatvec_multi: three matrices of different types on one input in one
+    launch, optionally normalising it first, bit for bit as lt_rmsnorm followed
+    by three lt_qmatvec calls."""
+    import importlib
+    synth = importlib.import_module("llmtoy-zig_b200.synth")
+    rng = np.random.Generator(np.random.PCG64(77 + int(norm)))
+    d = 2816
+    shapes = [(12, 4096), (14, 2048), (8, 2048)]
+    mats = [synth.matrix(rng, t, r, d) for t, r in shapes]
+    ts = [ctx.upload(m, t, r, d) for m, (t, r) in zip(mats, shapes)]
+    x = dev(rng.normal(0, 1, d).astype(np.float32))
+    nw = dev(rng.uniform(0.5, 1.5, d).astype(np.float32))
+    ys = [empty(r) for _, r in shapes]
+    ctx.qmatvec_multi(ts, x, ys, nw if norm else None, 1e-6)
+    xn = empty(d)
+    if norm:
+        ctx.rmsnorm(x, nw, 1e-6, d, 1, xn)
+    else:
+        xn.copy_(x)
+    for t, y in zip(ts, ys):
+        ref = empty(t.rows if hasattr(t, "rows") else y.numel())
+        ctx.qmatvec(t, xn, ref, 1)
+        np.testing.assert_array_equal(bits(host(y)), bits(host(ref)))
+    for t in ts:
+        t.free()
