@@ -375,6 +375,17 @@ lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x,
                         const float *dev_q_norm, const float *dev_k_norm, const uint32_t *dev_pos,
                         void *dev_k_cache, void *dev_v_cache, const lt_tensor *wo, float *dev_out);
 
+/* lt_attn_block over separate Q, K and V tensors ([nq][d], [nkv][d], [nkv][d];
+ * the types may differ).  wv NULL: V is the K projection before the norms
+ * (gemma4/forward.zig:250), and dev_qkv_bias (nullable) then holds nq + nkv
+ * entries.  dev_post_norm non-NULL: out = x + rmsnorm(wo . att) * post_norm
+ * (gemma4/forward.zig:329-333) instead of x + wo . att. */
+lt_status lt_attn_block_split(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x, const float *dev_norm_w,
+                              float eps, const lt_tensor *wq, const lt_tensor *wk, const lt_tensor *wv,
+                              const float *dev_qkv_bias, const float *dev_q_norm, const float *dev_k_norm,
+                              const uint32_t *dev_pos, void *dev_k_cache, void *dev_v_cache,
+                              const lt_tensor *wo, const float *dev_post_norm, float *dev_out);
+
 /* L2 prefetch hint: the next lt_attn_block, or single-token lt_moe_block /
  * lt_moe_forward, launched on this context starts by prefetching these
  * tensors into L2 (a later op's weights, fetched while this one waits on its

@@ -38,7 +38,7 @@ EXPORTS = [
     "lt_graph_launch", "lt_graph_free", "lt_moe_ffn_noalloc", "lt_quant_matvec_host", "lt_moe_forward_host",
     "lt_ep_dispatch", "lt_gather_rows", "lt_moe_combine",
     "lt_device_alloc", "lt_device_free", "lt_copy_to_device", "lt_copy_to_host",
-    "lt_embed", "lt_qmatvec_add", "lt_attn_prep", "lt_attn_decode", "lt_attn_block", "lt_prefetch_next",
+    "lt_embed", "lt_qmatvec_add", "lt_attn_prep", "lt_attn_decode", "lt_attn_block", "lt_attn_block_split", "lt_prefetch_next",
     "lt_ffn_block", "lt_greedy_step", "lt_scale", "lt_add_rmsnorm", "lt_norm_pair", "lt_ffn_tail", "lt_softcap",
     "lt_sample_step", "lt_rng_seed", "lt_quantize_q8_1", "lt_dequant_q8_1", "lt_moe_block_scaled",
     "lt_qmatvec_multi",
@@ -148,6 +148,7 @@ def load_library() -> ctypes.CDLL:
         "lt_sample_step": (I, [P, P, U32, ctypes.POINTER(SampleParams), P, P, P, P]),
         "lt_rng_seed": (None, [U64, ctypes.POINTER(U64)]),
         "lt_attn_block": (I, [P, ctypes.POINTER(AttnCfg), P, P, F, P, P, P, P, P, P, P, P, P]),
+        "lt_attn_block_split": (I, [P, ctypes.POINTER(AttnCfg), P, P, F, P, P, P, P, P, P, P, P, P, P, P, P]),
         "lt_prefetch_next": (I, [P, P, P]),
         "lt_quant_matvec_host": (I, [P, P, P, U32, P, U64, U64]),
         "lt_moe_forward_host": (I, [P, P, P, P, P, I, I, P, P, U32, U32, P, P, P]),
@@ -401,6 +402,14 @@ class Context:
         self._check(self.lib.lt_attn_block(self.ptr, ctypes.byref(cfg), _ptr(x), _ptr(norm_w), eps, wqkv.handle,
                                            _ptr(qkv_bias), _ptr(q_norm), _ptr(k_norm), _ptr(pos), _ptr(k_cache),
                                            _ptr(v_cache), wo.handle, _ptr(out)))
+
+    def attn_block_split(self, cfg: AttnCfg, x, norm_w, eps: float, wq: Tensor, wk: Tensor, wv: Tensor | None,
+                         qkv_bias, q_norm, k_norm, pos, k_cache, v_cache, wo: Tensor, post_norm, out) -> None:
+        """attn_block over separate Q/K/V tensors; wv None: V = K; post_norm: out = x + rmsnorm(wo . att) * post_norm."""
+        self._check(self.lib.lt_attn_block_split(self.ptr, ctypes.byref(cfg), _ptr(x), _ptr(norm_w), eps, wq.handle,
+                                                 wk.handle, wv.handle if wv else None, _ptr(qkv_bias), _ptr(q_norm),
+                                                 _ptr(k_norm), _ptr(pos), _ptr(k_cache), _ptr(v_cache), wo.handle,
+                                                 _ptr(post_norm), _ptr(out)))
 
     def prefetch_next(self, a: Tensor | None, b: Tensor | None = None) -> None:
         self._check(self.lib.lt_prefetch_next(self.ptr, a.handle if a else None, b.handle if b else None))

@@ -799,10 +799,14 @@ lt_status lt_prefetch_next(lt_ctx *ctx, const lt_tensor *a, const lt_tensor *b) 
     return LT_OK;
 }
 
-lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x, const float *dev_norm_w, float eps,
-                        const lt_tensor *wqkv, const float *dev_qkv_bias, const float *dev_q_norm,
-                        const float *dev_k_norm, const uint32_t *dev_pos, void *dev_k_cache, void *dev_v_cache,
-                        const lt_tensor *wo, float *dev_out) {
+// The attention half of a layer: the persistent kernel when it takes the
+// shape, else the same computation as separate kernels.  seg: the stacked
+// Q/K/V tensor (nseg 1), or wq, wk and wv (3), or wq and wk with V = K (2).
+static lt_status attn_block_impl(lt_ctx *ctx, const char *who, const lt_attn_cfg *cfg, const float *dev_x,
+                                 const float *dev_norm_w, float eps, const lt_tensor *const *seg, uint32_t nseg,
+                                 const float *dev_qkv_bias, const float *dev_q_norm, const float *dev_k_norm,
+                                 const uint32_t *dev_pos, void *dev_k_cache, void *dev_v_cache, const lt_tensor *wo,
+                                 const float *dev_post_norm, float *dev_out) {
     lt_status st = enter(ctx);
     if (st != LT_OK) return st;
     struct Clear {
@@ -810,38 +814,48 @@ lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x,
         ~Clear() { clear_prefetch(c); }
     } clear{ctx};
     lt::AttnGeom g;
-    if ((st = attn_geom(ctx, cfg, g, "lt_attn_block")) != LT_OK) return st;
-    if (!dev_x || !dev_norm_w || !wqkv || !wo || !dev_pos || !dev_k_cache || !dev_v_cache || !dev_out)
-        return fail(ctx, LT_EINVAL, "lt_attn_block: null argument");
+    if ((st = attn_geom(ctx, cfg, g, who)) != LT_OK) return st;
+    if (!dev_x || !dev_norm_w || !wo || !dev_pos || !dev_k_cache || !dev_v_cache || !dev_out)
+        return fail(ctx, LT_EINVAL, "%s: null argument", who);
+    for (uint32_t s = 0; s < nseg; s++)
+        if (!seg[s]) return fail(ctx, LT_EINVAL, "%s: null Q/K/V tensor", who);
     const uint32_t nq = g.n_heads * g.hd, nkv = g.n_kv * g.hd;
+    const bool v_is_k = nseg == 2;
     const uint64_t d = wo->m.rows;
-    if (wqkv->m.n_experts || wo->m.n_experts || wqkv->m.rows != (uint64_t)nq + 2 * nkv || wqkv->m.cols != d ||
-        wo->m.cols != nq)
-        return fail(ctx, LT_EINVAL, "lt_attn_block: wqkv %llux%llu / wo %llux%llu do not fit the heads",
-                    (unsigned long long)wqkv->m.rows, (unsigned long long)wqkv->m.cols,
-                    (unsigned long long)wo->m.rows, (unsigned long long)wo->m.cols);
-    if ((st = check_kernel_shape(ctx, wqkv->m, "lt_attn_block wqkv")) != LT_OK) return st;
-    if ((st = check_kernel_shape(ctx, wo->m, "lt_attn_block wo")) != LT_OK) return st;
-    const bool fused = ctx->attn_block && lt::attn_block_supported(g, wqkv->m, wo->m, (uint32_t)d) &&
-                       lt::attn_block_smem(g, ctx->num_sms, (uint32_t)d, wqkv->m, wo->m) <= lt::kDecodeSmemLimit;
-    if (fused) {
-        const size_t sf = lt::attn_block_scratch_floats(g, ctx->num_sms, (uint32_t)d, wqkv->m, wo->m);
+    const uint64_t want[3] = {nseg == 1 ? (uint64_t)nq + 2 * nkv : nq, nkv, nkv};
+    for (uint32_t s = 0; s < nseg; s++) {
+        const lt::DevMat &m = seg[s]->m;
+        if (m.n_experts || m.rows != want[s] || m.cols != d)
+            return fail(ctx, LT_EINVAL, "%s: Q/K/V tensor %u is %llux%llu, the heads want %llux%llu", who, s,
+                        (unsigned long long)m.rows, (unsigned long long)m.cols, (unsigned long long)want[s],
+                        (unsigned long long)d);
+        if ((st = check_kernel_shape(ctx, m, who)) != LT_OK) return st;
+    }
+    if (wo->m.n_experts || wo->m.cols != nq)
+        return fail(ctx, LT_EINVAL, "%s: wo %llux%llu does not fit the heads", who, (unsigned long long)wo->m.rows,
+                    (unsigned long long)wo->m.cols);
+    if ((st = check_kernel_shape(ctx, wo->m, who)) != LT_OK) return st;
+    lt::AttnBlockParams p;
+    p.g = g;
+    p.d = (uint32_t)d;
+    p.x = dev_x;
+    p.norm_w = dev_norm_w;
+    p.eps = eps;
+    for (uint32_t s = 0; s < nseg; s++) p.seg[s] = seg[s]->m;
+    p.nseg = nseg;
+    p.v_is_k = v_is_k ? 1 : 0;
+    p.wo = wo->m;
+    p.bias = dev_qkv_bias;
+    p.q_norm = dev_q_norm;
+    p.k_norm = dev_k_norm;
+    p.post_norm = dev_post_norm;
+    p.pos = dev_pos;
+    p.kc = dev_k_cache;
+    p.vc = dev_v_cache;
+    p.out = dev_out;
+    size_t sf = 0;
+    if (ctx->attn_block && lt::attn_block_plan(p, ctx->num_sms, &sf)) {
         if ((st = ensure_scratch(ctx, sf * 4 + 1024)) != LT_OK) return st;
-        lt::AttnBlockParams p;
-        p.g = g;
-        p.d = (uint32_t)d;
-        p.x = dev_x;
-        p.norm_w = dev_norm_w;
-        p.eps = eps;
-        p.wqkv = wqkv->m;
-        p.wo = wo->m;
-        p.bias = dev_qkv_bias;
-        p.q_norm = dev_q_norm;
-        p.k_norm = dev_k_norm;
-        p.pos = dev_pos;
-        p.kc = dev_k_cache;
-        p.vc = dev_v_cache;
-        p.out = dev_out;
         p.scratch = (float *)ctx->scratch;
         p.sync = ctx->attn_sync;
         for (int i = 0; i < 2; i++) {
@@ -850,19 +864,39 @@ lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x,
         }
         return launched(ctx, lt::launch_attn_block(cfg_of(ctx), p), "attn block");
     }
-    // the same computation as separate kernels: norm, Q/K/V, prep, attention, wo + residual
+    // the same computation as separate kernels: norm, Q/K/V, prep, attention, wo + residual (or + normed wo)
     const size_t xb_b = al256((size_t)d * 4), qkv_b = al256(((size_t)nq + 2 * nkv) * 4), att_b = al256((size_t)nq * 4);
     // [0, base): the quantised activation row of each matvec, then the attention partials
     const size_t attn_sc = lt::attn_scratch_floats(g, ctx->num_sms) * 4;
     const size_t qrow = lt::qact_row_pitch(d > nq ? d : nq);
     const size_t base = al256(attn_sc > qrow ? attn_sc : qrow);
-    if ((st = ensure_scratch(ctx, base + xb_b + qkv_b + att_b)) != LT_OK) return st;
+    if ((st = ensure_scratch(ctx, base + 2 * xb_b + qkv_b + att_b)) != LT_OK) return st;
     float *xb = (float *)(ctx->scratch + base), *qkv = (float *)(ctx->scratch + base + xb_b);
     float *att = (float *)(ctx->scratch + base + xb_b + qkv_b);
+    float *yb = (float *)(ctx->scratch + base + xb_b + qkv_b + att_b);
     const lt::LaunchCfg c = cfg_of(ctx);
-    if ((st = launched(ctx, lt::launch_rmsnorm(c, dev_x, dev_norm_w, eps, (uint32_t)d, 1, xb), "rmsnorm")) != LT_OK)
-        return st;
-    if ((st = qmatvec_impl(ctx, wqkv, 0, xb, qkv, 1, dev_qkv_bias)) != LT_OK) return st;
+    if (nseg > 1 && !dev_qkv_bias) {  // the norm and the projections in one launch (V = K: K once more)
+        const lt::DevMat *m[3] = {&seg[0]->m, &seg[1]->m, v_is_k ? &seg[1]->m : &seg[2]->m};
+        float *y[3] = {qkv, qkv + nq, qkv + nq + nkv};
+        if ((st = launched(ctx, lt::launch_qmatvec_multi(c, 3, m, dev_x, dev_norm_w, eps, y), "qmatvec multi")) !=
+            LT_OK)
+            return st;
+    } else {
+        if ((st = launched(ctx, lt::launch_rmsnorm(c, dev_x, dev_norm_w, eps, (uint32_t)d, 1, xb), "rmsnorm")) != LT_OK)
+            return st;
+        if (nseg == 1) {
+            if ((st = qmatvec_impl(ctx, seg[0], 0, xb, qkv, 1, dev_qkv_bias)) != LT_OK) return st;
+        } else {
+            const uint32_t off[3] = {0, nq, nq + nkv};
+            for (uint32_t s = 0; s < 3; s++) {  // bias rows follow the rows present: V = K takes K's
+                const lt_tensor *w = s == 2 && v_is_k ? seg[1] : seg[s];
+                const uint32_t boff = s == 2 && v_is_k ? nq : off[s];
+                if ((st = qmatvec_impl(ctx, w, 0, xb, qkv + off[s], 1, dev_qkv_bias ? dev_qkv_bias + boff : nullptr)) !=
+                    LT_OK)
+                    return st;
+            }
+        }
+    }
     if ((st = ensure_counters(ctx, g.n_heads)) != LT_OK) return st;
     if ((st = launched(ctx, lt::launch_attn_prep(c, g, qkv, dev_q_norm, dev_k_norm, dev_pos, dev_k_cache, dev_v_cache),
                        "attn prep")) != LT_OK)
@@ -871,7 +905,32 @@ lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x,
                                                    (float *)ctx->scratch, ctx->counters),
                        "attn decode")) != LT_OK)
         return st;
-    return qmatvec_impl(ctx, wo, 0, att, dev_out, 1, dev_x);
+    if (!dev_post_norm) return qmatvec_impl(ctx, wo, 0, att, dev_out, 1, dev_x);
+    if ((st = qmatvec_impl(ctx, wo, 0, att, yb, 1, nullptr)) != LT_OK) return st;
+    if (dev_out != dev_x &&
+        (st = launched(ctx, cudaMemcpyAsync(dev_out, dev_x, d * 4, cudaMemcpyDeviceToDevice, ctx->stream), "copy")) !=
+            LT_OK)
+        return st;
+    return launched(ctx, lt::launch_add_rmsnorm(c, yb, dev_post_norm, eps, (uint32_t)d, 1, dev_out), "add_rmsnorm");
+}
+
+lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x, const float *dev_norm_w, float eps,
+                        const lt_tensor *wqkv, const float *dev_qkv_bias, const float *dev_q_norm,
+                        const float *dev_k_norm, const uint32_t *dev_pos, void *dev_k_cache, void *dev_v_cache,
+                        const lt_tensor *wo, float *dev_out) {
+    const lt_tensor *seg[1] = {wqkv};
+    return attn_block_impl(ctx, "lt_attn_block", cfg, dev_x, dev_norm_w, eps, seg, 1, dev_qkv_bias, dev_q_norm,
+                           dev_k_norm, dev_pos, dev_k_cache, dev_v_cache, wo, nullptr, dev_out);
+}
+
+lt_status lt_attn_block_split(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x, const float *dev_norm_w,
+                              float eps, const lt_tensor *wq, const lt_tensor *wk, const lt_tensor *wv,
+                              const float *dev_qkv_bias, const float *dev_q_norm, const float *dev_k_norm,
+                              const uint32_t *dev_pos, void *dev_k_cache, void *dev_v_cache, const lt_tensor *wo,
+                              const float *dev_post_norm, float *dev_out) {
+    const lt_tensor *seg[3] = {wq, wk, wv};
+    return attn_block_impl(ctx, "lt_attn_block_split", cfg, dev_x, dev_norm_w, eps, seg, wv ? 3 : 2, dev_qkv_bias,
+                           dev_q_norm, dev_k_norm, dev_pos, dev_k_cache, dev_v_cache, wo, dev_post_norm, dev_out);
 }
 
 void lt_rng_seed(uint64_t seed, uint64_t state_out[4]) {

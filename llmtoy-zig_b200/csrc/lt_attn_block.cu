@@ -30,7 +30,7 @@ constexpr int kAbWarps = 16;
 constexpr int kAbThreads = kAbWarps * 32;
 
 // Layout of the context's attention sync block.
-constexpr size_t kAbEpoch = 0, kAbB1 = 8, kAbB2 = 16, kAbHeadCnt = 256;
+constexpr size_t kAbEpoch = 0, kAbB1 = 8, kAbB2 = 16, kAbB3 = 24, kAbHeadCnt = 256;
 constexpr uint32_t kAbMaxSplits = 8;  // splits of a head's positions (one CTA each)
 constexpr uint32_t kAbSplitPositions = 256;  // positions per split before another CTA joins
 
@@ -39,16 +39,24 @@ struct AttnBlockArgs {
     uint32_t d;
     const float *x, *norm_w;
     float eps;
-    const uint8_t *wqkv;
-    uint64_t qpitch;
-    uint32_t qrows, qnb;  // rows (nq + 2 nkv), 32-blocks per row (d / 32)
+    // the Q/K/V rows: qrows = nq + nkv (+ nkv) rows in segments, rows
+    // [seg_end[s-1], seg_end[s]) from seg_w[s] (one segment for a stacked tensor)
+    const uint8_t *seg_w[3];
+    uint64_t seg_pitch[3];
+    uint32_t seg_type[3], seg_end[3], nseg;
+    uint64_t qpitch;      // the largest segment pitch
+    uint32_t qrows, qnb;  // rows, 32-blocks per row (d / 32)
+    uint32_t v_is_k;      // no V rows: V is the raw K head (gemma4/forward.zig:250)
     const float *bias;    // nullable [qrows]
     const float *q_norm, *k_norm;
     const uint32_t *pos;
     void *kc, *vc;  // f32 or f16 elements (g.kv_f16)
     const uint8_t *wo;
     uint64_t opitch;
-    uint32_t onb;  // 32-blocks per wo row (nq / 32)
+    uint32_t onb, otype;  // 32-blocks per wo row (nq / 32), type
+    const float *post_norm;  // nullable: out = x + rmsnorm(wo . att) * post_norm (gemma4/forward.zig:329-333)
+    float *ss_part;          // [grid] partial sums of squares for post_norm
+    uint32_t late_wo;        // the wo tile lands in the Q/K/V tile's space once phase Q is done
     float *out;
     float *qkv, *part;  // global scratch
     uint8_t *att;       // the attention vector as a quantised activation row (qact layout)
@@ -74,8 +82,15 @@ __host__ __device__ inline AbLayout ab_layout(const AttnBlockArgs &a) {
     const uint32_t nq = a.g.n_heads * a.g.hd;
     L.bars = take(64);
     L.misc = take(256);
-    L.wq = take((size_t)a.maxq * a.qpitch + 128);  // + slack: a Q8_0 chunk reads up to 34 bytes past a row
-    L.wo = take((size_t)a.maxo * a.opitch + 128);
+    // + slack: a Q8_0 chunk reads up to 34 bytes past a row
+    const size_t qb = (size_t)a.maxq * a.qpitch + 128, ob = (size_t)a.maxo * a.opitch + 128;
+    if (a.late_wo) {
+        L.wq = take(qb > ob ? qb : ob);
+        L.wo = L.wq;
+    } else {
+        L.wq = take(qb);
+        L.wo = take(ob);
+    }
     L.xs = take(xs_bytes(1, (int)((a.d + 255) / 256)));
     L.as = take(xs_bytes(1, (int)((nq + 255) / 256)));
     L.xf = take((size_t)(a.d > nq ? a.d : nq) * 4);
@@ -184,6 +199,22 @@ LT_DEVINL void ab_rows(const uint8_t *tile, uint64_t pitch, uint32_t nrows, uint
             const uint32_t r = r0 + i;
             const float v = warp_sum(acc[i]);
             if (lane == 0 && r < nrows) y[r] = v;
+        }
+    }
+}
+
+// ab_rows for a tile of type T, or (T == 0) of the run-time type `type`.
+template <uint32_t T>
+LT_DEVINL void ab_rows_any(uint32_t type, const uint8_t *tile, uint64_t pitch, uint32_t nrows, uint32_t cols,
+                           uint32_t nb, const XS &X, int warp, int lane, float *y) {
+    if constexpr (T != 0) {
+        ab_rows<T>(tile, pitch, nrows, cols, nb, X, warp, lane, y);
+    } else {
+        switch (type) {
+        case T_Q8_0: ab_rows<T_Q8_0>(tile, pitch, nrows, cols, nb, X, warp, lane, y); break;
+        case T_Q4_K: ab_rows<T_Q4_K>(tile, pitch, nrows, cols, nb, X, warp, lane, y); break;
+        case T_Q6_K: ab_rows<T_Q6_K>(tile, pitch, nrows, cols, nb, X, warp, lane, y); break;
+        default: break;
         }
     }
 }
@@ -368,6 +399,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     unsigned long long *ctr_epoch = reinterpret_cast<unsigned long long *>(a.sync + kAbEpoch);
     unsigned long long *ctr1 = reinterpret_cast<unsigned long long *>(a.sync + kAbB1);
     unsigned long long *ctr2 = reinterpret_cast<unsigned long long *>(a.sync + kAbB2);
+    unsigned long long *ctr3 = reinterpret_cast<unsigned long long *>(a.sync + kAbB3);
     uint32_t *head_cnt = reinterpret_cast<uint32_t *>(a.sync + kAbHeadCnt);
     int *s_last = reinterpret_cast<int *>(smem + L.misc + 128);
 
@@ -380,11 +412,24 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
         fence_barrier_init();
-        if (nqr) {
-            mbar_arrive_expect_tx(&bars[0], (uint32_t)(nqr * a.qpitch));
-            tma_load_1d(wq, a.wqkv + (uint64_t)q0 * a.qpitch, (uint32_t)(nqr * a.qpitch), &bars[0]);
+        if (nqr) {  // this CTA's rows of each segment, one after another
+            uint32_t total = 0;
+            for (uint32_t sg = 0; sg < a.nseg; sg++) {
+                const uint32_t sb = sg ? a.seg_end[sg - 1] : 0, lo = max(q0, sb), hi = min(q1, a.seg_end[sg]);
+                if (lo < hi) total += (uint32_t)((hi - lo) * a.seg_pitch[sg]);
+            }
+            mbar_arrive_expect_tx(&bars[0], total);
+            uint32_t off = 0;
+            for (uint32_t sg = 0; sg < a.nseg; sg++) {
+                const uint32_t sb = sg ? a.seg_end[sg - 1] : 0, lo = max(q0, sb), hi = min(q1, a.seg_end[sg]);
+                if (lo < hi) {
+                    const uint32_t bytes = (uint32_t)((hi - lo) * a.seg_pitch[sg]);
+                    tma_load_1d(wq + off, a.seg_w[sg] + (uint64_t)(lo - sb) * a.seg_pitch[sg], bytes, &bars[0]);
+                    off += bytes;
+                }
+            }
         }
-        if (nor) {
+        if (nor && !a.late_wo) {
             mbar_arrive_expect_tx(&bars[1], (uint32_t)(nor * a.opitch));
             tma_load_1d(wo, a.wo + (uint64_t)o0 * a.opitch, (uint32_t)(nor * a.opitch), &bars[1]);
         }
@@ -412,7 +457,17 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     __syncthreads();
     const uint64_t epoch = *s_epoch;
     float *yq = xf;  // the normalised x is quantised already
-    if (nqr && tile_wait(&bars[0], a.dev_err)) ab_rows<QT>(wq, a.qpitch, nqr, a.d, a.qnb, Xx, warp, lane, yq);
+    if (nqr && tile_wait(&bars[0], a.dev_err)) {
+        uint32_t off = 0;
+        for (uint32_t sg = 0; sg < a.nseg; sg++) {
+            const uint32_t sb = sg ? a.seg_end[sg - 1] : 0, lo = max(q0, sb), hi = min(q1, a.seg_end[sg]);
+            if (lo < hi) {
+                ab_rows_any<QT>(a.seg_type[sg], wq + off, a.seg_pitch[sg], hi - lo, a.d, a.qnb, Xx, warp, lane,
+                                yq + (lo - q0));
+                off += (uint32_t)((hi - lo) * a.seg_pitch[sg]);
+            }
+        }
+    }
     __syncthreads();
     for (uint32_t r = tid; r < nqr; r += kAbThreads)
         a.qkv[q0 + r] = a.bias ? __fadd_rn(yq[r], a.bias[q0 + r]) : yq[r];
@@ -420,6 +475,14 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     grid_wait(ctr1, epoch, a.dev_err, kWaitLimitNs);
 
     // ── phase A ──────────────────────────────────────────────────────────────
+    if (a.late_wo) {  // the Q/K/V rows are consumed: the wo rows take their place
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+        if (tid == 0 && nor) {
+            mbar_arrive_expect_tx(&bars[1], (uint32_t)(nor * a.opitch));
+            tma_load_1d(wo, a.wo + (uint64_t)o0 * a.opitch, (uint32_t)(nor * a.opitch), &bars[1]);
+        }
+    }
     const uint32_t group = a.g.n_heads / a.g.n_kv;
     const uint32_t seq = pos + 1, win = a.g.window ? min(seq, a.g.window) : seq, first = seq - win;
     // splits of a head's window: one per kAbSplitPositions positions (a short
@@ -429,7 +492,9 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
         const uint32_t h = item / S, s = item - h * S, kh = h / group;
         if (tid < 3 * HD / 4) {  // q, k, v heads: one float4 each
             const uint32_t part = tid / (HD / 4), i = tid % (HD / 4);
-            const size_t off = part == 0 ? (size_t)h * HD : part == 1 ? nq + (size_t)kh * HD : nq + nkv + (size_t)kh * HD;
+            const size_t off = part == 0   ? (size_t)h * HD
+                               : part == 1 ? nq + (size_t)kh * HD
+                                           : (a.v_is_k ? nq : nq + nkv) + (size_t)kh * HD;
             reinterpret_cast<float4 *>(hq + part * HD)[i] = __ldcg(reinterpret_cast<const float4 *>(a.qkv + off) + i);
         }
         __syncthreads();
@@ -551,44 +616,82 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     ab_load_qact(Xa, a.att, nq);
     __syncthreads();
     float *yo = xf;  // the attention vector is quantised already
-    if (nor && tile_wait(&bars[1], a.dev_err)) ab_rows<OT>(wo, a.opitch, nor, nq, a.onb, Xa, warp, lane, yo);
+    if (nor && tile_wait(&bars[1], a.dev_err)) ab_rows_any<OT>(a.otype, wo, a.opitch, nor, nq, a.onb, Xa, warp, lane, yo);
     __syncthreads();
-    for (uint32_t r = tid; r < nor; r += kAbThreads) a.out[o0 + r] = __fadd_rn(xres[r], yo[r]);
+    if (a.post_norm) {  // x + rmsnorm(y) * w over all d outputs: partial sums, a third hand-off
+        float ss = 0.0f;
+        for (uint32_t r = tid; r < nor; r += kAbThreads) ss = __fadd_rn(ss, __fmul_rn(yo[r], yo[r]));
+        ss = ab_block_sum(ss, red);
+        if (tid == 0) a.ss_part[c] = ss;
+        grid_arrive(ctr3);
+        grid_wait(ctr3, epoch, a.dev_err, kWaitLimitNs);
+        float t = 0.0f;
+        for (uint32_t i = tid; i < G; i += kAbThreads) t = __fadd_rn(t, __ldcg(a.ss_part + i));
+        t = ab_block_sum(t, red);
+        const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)a.d), a.eps)));
+        for (uint32_t i = tid; i < nor; i += kAbThreads)
+            a.out[o0 + i] = __fadd_rn(xres[i], __fmul_rn(__fmul_rn(yo[i], r), __ldg(a.post_norm + o0 + i)));
+    } else {
+        grid_arrive(ctr3);  // every launch counts on every counter: the epochs stay aligned
+        for (uint32_t r = tid; r < nor; r += kAbThreads) a.out[o0 + r] = __fadd_rn(xres[r], yo[r]);
+    }
 }
 
-bool attn_block_supported(const AttnGeom &g, const DevMat &wqkv, const DevMat &wo, uint32_t d) {
-    auto ok_type = [](uint32_t t) { return t == T_Q8_0 || t == T_Q4_K || t == T_Q6_K; };
-    if (!ok_type(wqkv.type) || !ok_type(wo.type)) return false;
+static bool ab_type_ok(uint32_t t) { return t == T_Q8_0 || t == T_Q4_K || t == T_Q6_K; }
+
+// Arguments without the pointers that vary per call; false if the shape is outside the kernel.
+static bool ab_args(const AttnBlockParams &p, int num_sms, AttnBlockArgs &a) {
+    const AttnGeom &g = p.g;
+    a = AttnBlockArgs{};
     if (g.hd != 64 && g.hd != 128 && g.hd != 256) return false;
-    if (wqkv.cols != d || wqkv.rows != (uint64_t)(g.n_heads + 2 * g.n_kv) * g.hd) return false;
-    if (wo.rows != d || wo.cols != (uint64_t)g.n_heads * g.hd) return false;
-    return d % 32 == 0 && d <= 8192 && wo.cols <= 16384;
-}
-
-static AttnBlockArgs ab_args(const AttnGeom &g, int num_sms, uint32_t d, const DevMat &wqkv, const DevMat &wo) {
-    AttnBlockArgs a{};
+    if (p.nseg < 1 || p.nseg > 3 || p.d % 32 != 0 || p.d > 8192) return false;
+    const uint32_t nq = g.n_heads * g.hd, nkv = g.n_kv * g.hd;
+    const uint32_t want = nq + nkv + (p.v_is_k ? 0u : nkv);
+    uint32_t rows = 0;
+    a.qpitch = 0;
+    for (uint32_t s = 0; s < p.nseg; s++) {
+        const DevMat &m = p.seg[s];
+        if (!ab_type_ok(m.type) || m.cols != p.d || m.n_experts) return false;
+        rows += (uint32_t)m.rows;
+        a.seg_w[s] = m.data;
+        a.seg_pitch[s] = m.pitch;
+        a.seg_type[s] = m.type;
+        a.seg_end[s] = rows;
+        a.qpitch = m.pitch > a.qpitch ? m.pitch : a.qpitch;
+    }
+    if (rows != want) return false;
+    if (!ab_type_ok(p.wo.type) || p.wo.rows != p.d || p.wo.cols != nq || nq > 16384) return false;
     a.g = g;
-    a.d = d;
-    a.qpitch = wqkv.pitch;
-    a.qrows = (uint32_t)wqkv.rows;
-    a.qnb = (uint32_t)(wqkv.cols / 32);
-    a.opitch = wo.pitch;
-    a.onb = (uint32_t)(wo.cols / 32);
+    a.d = p.d;
+    a.nseg = p.nseg;
+    a.v_is_k = p.v_is_k ? 1u : 0u;
+    a.qrows = rows;
+    a.qnb = p.d / 32;
+    a.opitch = p.wo.pitch;
+    a.onb = (uint32_t)(p.wo.cols / 32);
+    a.otype = p.wo.type;
     const uint32_t G = (uint32_t)num_sms;
     a.splits = max(1u, min(kAbMaxSplits, G / g.n_heads));
     a.maxq = (a.qrows + G - 1) / G;
-    a.maxo = (d + G - 1) / G;
-    return a;
+    a.maxo = (p.d + G - 1) / G;
+    a.late_wo = 0;
+    if (ab_layout(a).total > kDecodeSmemLimit) {  // the wo rows wait for the Q/K/V rows' space
+        a.late_wo = 1;
+        if (ab_layout(a).total > kDecodeSmemLimit) return false;
+    }
+    return true;
 }
 
-size_t attn_block_smem(const AttnGeom &g, int num_sms, uint32_t d, const DevMat &wqkv, const DevMat &wo) {
-    return ab_layout(ab_args(g, num_sms, d, wqkv, wo)).total;
+static size_t ab_scratch_floats(const AttnBlockArgs &a, int num_sms) {
+    return (size_t)((a.qrows + 31) & ~31u) + (((size_t)a.g.n_heads * a.splits * (a.g.hd + 2) + 31) & ~(size_t)31) +
+           ((qact_pitch((uint64_t)a.g.n_heads * a.g.hd) / 4 + 31) & ~(size_t)31) + (size_t)num_sms + 64;
 }
 
-size_t attn_block_scratch_floats(const AttnGeom &g, int num_sms, uint32_t d, const DevMat &wqkv, const DevMat &wo) {
-    const AttnBlockArgs a = ab_args(g, num_sms, d, wqkv, wo);
-    return (size_t)a.qrows + 32 + (size_t)g.n_heads * a.splits * (g.hd + 2) + 32 +
-           qact_pitch((uint64_t)g.n_heads * g.hd) / 4 + 64;
+bool attn_block_plan(const AttnBlockParams &p, int num_sms, size_t *scratch_floats) {
+    AttnBlockArgs a;
+    if (!ab_args(p, num_sms, a)) return false;
+    if (scratch_floats) *scratch_floats = ab_scratch_floats(a, num_sms);
+    return true;
 }
 
 template <uint32_t QT, uint32_t OT>
@@ -612,14 +715,15 @@ static cudaError_t launch_ab_q(const LaunchCfg &c, const AttnBlockArgs &a, size_
 }
 
 cudaError_t launch_attn_block(const LaunchCfg &c, const AttnBlockParams &p) {
-    AttnBlockArgs a = ab_args(p.g, c.num_sms, p.d, p.wqkv, p.wo);
+    AttnBlockArgs a;
+    if (!ab_args(p, c.num_sms, a)) return cudaErrorInvalidValue;
     a.x = p.x;
     a.norm_w = p.norm_w;
     a.eps = p.eps;
-    a.wqkv = p.wqkv.data;
     a.bias = p.bias;
     a.q_norm = p.q_norm;
     a.k_norm = p.k_norm;
+    a.post_norm = p.post_norm;
     a.pos = p.pos;
     a.kc = p.kc;
     a.vc = p.vc;
@@ -628,7 +732,9 @@ cudaError_t launch_attn_block(const LaunchCfg &c, const AttnBlockParams &p) {
     float *sc = p.scratch;
     a.qkv = sc;
     a.part = sc + ((a.qrows + 31) & ~31u);
-    a.att = reinterpret_cast<uint8_t *>(a.part + (((size_t)p.g.n_heads * a.splits * (p.g.hd + 2) + 31) & ~(size_t)31));
+    float *att = a.part + (((size_t)p.g.n_heads * a.splits * (p.g.hd + 2) + 31) & ~(size_t)31);
+    a.att = reinterpret_cast<uint8_t *>(att);
+    a.ss_part = att + ((qact_pitch((uint64_t)p.g.n_heads * p.g.hd) / 4 + 31) & ~(size_t)31);
     a.sync = p.sync;
     for (int i = 0; i < 2; i++) {
         a.pf[i] = p.pf[i];
@@ -636,11 +742,13 @@ cudaError_t launch_attn_block(const LaunchCfg &c, const AttnBlockParams &p) {
     }
     a.dev_err = c.dev_err;
     const size_t smem = ab_layout(a).total;
-    if (smem > kDecodeSmemLimit) return cudaErrorInvalidValue;
-    switch (p.wqkv.type) {
-    case T_Q8_0: return launch_ab_q<T_Q8_0>(c, a, smem, p.wo.type);
-    case T_Q4_K: return launch_ab_q<T_Q4_K>(c, a, smem, p.wo.type);
-    case T_Q6_K: return launch_ab_q<T_Q6_K>(c, a, smem, p.wo.type);
+    bool uniform = true;  // one Q/K/V type: the instantiation for it; otherwise run-time types
+    for (uint32_t s = 1; s < a.nseg; s++) uniform = uniform && a.seg_type[s] == a.seg_type[0];
+    if (!uniform) return launch_ab_t<0, 0>(c, a, smem);
+    switch (a.seg_type[0]) {
+    case T_Q8_0: return launch_ab_q<T_Q8_0>(c, a, smem, a.otype);
+    case T_Q4_K: return launch_ab_q<T_Q4_K>(c, a, smem, a.otype);
+    case T_Q6_K: return launch_ab_q<T_Q6_K>(c, a, smem, a.otype);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -128,20 +128,26 @@ struct AttnBlockParams {
     uint32_t d;
     const float *x, *norm_w;
     float eps;
-    DevMat wqkv, wo;
+    // Q/K/V rows: one stacked tensor [nq + 2 nkv][d] (nseg 1), or wq, wk and wv
+    // (nseg 3), or wq and wk with V = the raw K head (nseg 2, v_is_k)
+    DevMat seg[3];
+    uint32_t nseg = 1;
+    int v_is_k = 0;
+    DevMat wo;
     const float *bias, *q_norm, *k_norm;
+    const float *post_norm = nullptr;  // out = x + rmsnorm(wo . att) * post_norm instead of x + wo . att
     const uint32_t *pos;
     void *kc, *vc;  // f32 or f16 elements (AttnGeom::kv_f16)
     float *out;            // may alias x
-    float *scratch;        // attn_block_scratch_floats floats
+    float *scratch;        // the floats attn_block_plan gives
     uint8_t *sync;         // kAttnSyncBytes zero-initialised, this kernel only
     const uint8_t *pf[2];  // optional L2 prefetch ranges (the next kernel's weights)
     uint64_t pf_bytes[2];
 };
 constexpr size_t kAttnSyncBytes = 256 + 4 * 1024;  // counters, then one merge counter per head (<= 1024)
-bool attn_block_supported(const AttnGeom &g, const DevMat &wqkv, const DevMat &wo, uint32_t d);
-size_t attn_block_smem(const AttnGeom &g, int num_sms, uint32_t d, const DevMat &wqkv, const DevMat &wo);
-size_t attn_block_scratch_floats(const AttnGeom &g, int num_sms, uint32_t d, const DevMat &wqkv, const DevMat &wo);
+// Whether the persistent kernel takes this shape (and fits in shared memory);
+// its global scratch in floats.
+bool attn_block_plan(const AttnBlockParams &p, int num_sms, size_t *scratch_floats);
 cudaError_t launch_attn_block(const LaunchCfg &c, const AttnBlockParams &p);
 
 // Bytes of one quantised activation row (lt_qact.cuh) of `cols` values.

@@ -20,13 +20,12 @@ struct lth_decoder {
     lth_model m{};
     std::vector<lth_layer> layers;
     lt_attn_cfg attn{};
-    uint32_t nq = 0, nkv = 0;
-    float *x = nullptr, *xb = nullptr, *qkv = nullptr, *att = nullptr, *logits = nullptr;
+    float *x = nullptr, *xb = nullptr, *logits = nullptr;
     uint8_t *kcache = nullptr, *vcache = nullptr;
     size_t kv_esize = 4;         // bytes per cache element: 4 (f32) or 2 (f16)
     std::vector<size_t> kv_off;  // per layer: offset of its cache (elements)
-    // Gemma 4: attention output, dense FFN, MoE accumulator, expert and router inputs, routing
-    float *ybuf = nullptr, *fbuf = nullptr, *mbuf = nullptr, *moe_in = nullptr, *router_in = nullptr;
+    // Gemma 4: dense FFN, MoE accumulator, expert and router inputs, routing
+    float *fbuf = nullptr, *mbuf = nullptr, *moe_in = nullptr, *router_in = nullptr;
     uint32_t *ids = nullptr;
     float *wts = nullptr;
     uint32_t *ids_zero = nullptr;  // {0}: row index of a one-row gather
@@ -54,8 +53,6 @@ lt_status alloc(lth_decoder *d, T **p, size_t count) {
         if (st_ != LT_OK) return st_;        \
     } while (0)
 
-lt_status attn_ops(lth_decoder *d, const lth_layer &L, void *kc, void *vc);
-
 lt_status layer_step(lth_decoder *d, uint32_t l) {
     const lth_model &m = d->m;
     const lth_layer &L = d->layers[l];
@@ -63,52 +60,21 @@ lt_status layer_step(lth_decoder *d, uint32_t l) {
     const uint32_t *pos = d->state;
     void *kc = d->kcache + d->kv_off[l] * d->kv_esize, *vc = d->vcache + d->kv_off[l] * d->kv_esize;
     const lth_layer *next = l + 1 < m.n_layers ? &d->layers[l + 1] : nullptr;
-    if (L.wqkv) {  // the whole attention half in one launch; warm this layer's router (or FFN) in L2 meanwhile
-        LTH_TRY(lt_prefetch_next(c, L.router ? L.router : L.ffn_gate, L.router ? nullptr : L.ffn_up));
+    // the whole attention half in one launch; warm this layer's router (or FFN) in L2 meanwhile
+    LTH_TRY(lt_prefetch_next(c, L.router ? L.router : L.ffn_gate, L.router ? nullptr : L.ffn_up));
+    if (L.wqkv)
         LTH_TRY(lt_attn_block(c, &d->attn, d->x, L.attn_norm, m.eps, L.wqkv, L.qkv_bias, L.q_norm, L.k_norm, pos,
                               kc, vc, L.wo, d->x));
-    } else {
-        LTH_TRY(attn_ops(d, L, kc, vc));
-    }
+    else
+        LTH_TRY(lt_attn_block_split(c, &d->attn, d->x, L.attn_norm, m.eps, L.wq, L.wk, L.wv, L.qkv_bias, L.q_norm,
+                                    L.k_norm, pos, kc, vc, L.wo, nullptr, d->x));
     // the FFN block warms the next layer's attention weights in L2
-    if (next && next->wqkv) LTH_TRY(lt_prefetch_next(c, next->wqkv, next->wo));
+    if (next) LTH_TRY(lt_prefetch_next(c, next->wqkv ? next->wqkv : next->wq, next->wo));
     if (L.router) {
         return lt_moe_block(c, L.router, L.exp_gate, L.exp_up, L.exp_down, (int)m.act, (int)m.norm_topk, nullptr,
                             L.ffn_norm, m.eps, d->x, 1, m.n_used, d->x, nullptr, nullptr);
     }
     return lt_ffn_block(c, L.ffn_gate, L.ffn_up, L.ffn_down, (int)m.act, L.ffn_norm, m.eps, d->x, 1, 1, d->x);
-}
-
-// The attention half as separate ops (separate Q/K/V tensors).
-lt_status attn_ops(lth_decoder *d, const lth_layer &L, void *kc, void *vc) {
-    const lth_model &m = d->m;
-    lt_ctx *c = d->ctx;
-    const uint32_t *pos = d->state;
-    if (!L.wqkv && !L.qkv_bias) {  // the norm and the three projections in one launch
-        const lt_tensor *w[3] = {L.wq, L.wk, L.wv};
-        float *y[3] = {d->qkv, d->qkv + d->nq, d->qkv + d->nq + d->nkv};
-        LTH_TRY(lt_qmatvec_multi(c, 3, w, d->x, L.attn_norm, m.eps, y));
-    } else {
-        LTH_TRY(lt_rmsnorm(c, d->x, L.attn_norm, m.eps, m.d_model, 1, d->xb));
-    }
-    if (L.wqkv) {
-        if (L.qkv_bias)
-            LTH_TRY(lt_qmatvec_add(c, L.wqkv, 0, d->xb, L.qkv_bias, d->qkv, 1));
-        else
-            LTH_TRY(lt_qmatvec(c, L.wqkv, 0, d->xb, d->qkv, 1));
-    } else if (L.qkv_bias) {
-        const lt_tensor *w[3] = {L.wq, L.wk, L.wv};
-        const uint32_t off[3] = {0, d->nq, d->nq + d->nkv};
-        for (int i = 0; i < 3; i++) {
-            if (L.qkv_bias)
-                LTH_TRY(lt_qmatvec_add(c, w[i], 0, d->xb, L.qkv_bias + off[i], d->qkv + off[i], 1));
-            else
-                LTH_TRY(lt_qmatvec(c, w[i], 0, d->xb, d->qkv + off[i], 1));
-        }
-    }
-    LTH_TRY(lt_attn_prep(c, &d->attn, d->qkv, L.q_norm, L.k_norm, pos, kc, vc));
-    LTH_TRY(lt_attn_decode(c, &d->attn, d->qkv, kc, vc, pos, d->att));
-    return lt_qmatvec_add(c, L.wo, 0, d->att, d->x, d->x, 1);
 }
 
 // One Gemma 4 layer (gemma4/forward.zig:195-533, the CPU branches).
@@ -118,7 +84,6 @@ lt_status gemma_layer(lth_decoder *d, uint32_t l) {
     lt_ctx *c = d->ctx;
     const uint32_t *pos = d->state;
     const uint32_t hd = L.head_dim ? L.head_dim : m.head_dim, nkvh = L.n_kv_heads ? L.n_kv_heads : m.n_kv_heads;
-    const uint32_t nq = m.n_heads * hd, nkv = nkvh * hd;
     lt_attn_cfg a{};
     a.n_heads = m.n_heads;
     a.n_kv_heads = nkvh;
@@ -132,15 +97,10 @@ lt_status gemma_layer(lth_decoder *d, uint32_t l) {
     a.v_norm = 1;
     a.kv_f16 = m.kv_f16 ? 1u : 0u;
     void *kc = d->kcache + d->kv_off[l] * d->kv_esize, *vc = d->vcache + d->kv_off[l] * d->kv_esize;
-    {  // the attention norm and Q, K, V in one launch; without wv, V = K before the norms (forward.zig:250)
-        const lt_tensor *w[3] = {L.wq, L.wk, L.wv ? L.wv : L.wk};
-        float *y[3] = {d->qkv, d->qkv + nq, d->qkv + nq + nkv};
-        LTH_TRY(lt_qmatvec_multi(c, 3, w, d->x, L.attn_norm, m.eps, y));
-    }
-    LTH_TRY(lt_attn_prep(c, &a, d->qkv, L.q_norm, L.k_norm, pos, kc, vc));
-    LTH_TRY(lt_attn_decode(c, &a, d->qkv, kc, vc, pos, d->att));
-    LTH_TRY(lt_qmatvec(c, L.wo, 0, d->att, d->ybuf, 1));
-    LTH_TRY(lt_add_rmsnorm(c, d->ybuf, L.post_attention_norm, m.eps, m.d_model, 1, d->x));
+    // norm, Q/K/V (without wv, V = K before the norms: forward.zig:250), Q/K/V norms, RoPE, attention,
+    // wo and the post-attention norm into the residual (:329-333) in one launch
+    LTH_TRY(lt_attn_block_split(c, &a, d->x, L.attn_norm, m.eps, L.wq, L.wk, L.wv, nullptr, L.q_norm, L.k_norm, pos,
+                                kc, vc, L.wo, L.post_attention_norm, d->x));
     // dense GeGLU FFN, post_ffw_norm_1 (:390-396)
     LTH_TRY(lt_ffn_block(c, L.ffn_gate, L.ffn_up, L.ffn_down, LT_ACT_GELU_TANH, L.ffn_norm, m.eps, d->x, 1, 0,
                          d->fbuf));
@@ -173,8 +133,8 @@ lt_status step(lth_decoder *d) {
 
 void release(lth_decoder *d) {
     if (d->graph) lt_graph_free(d->ctx, d->graph);
-    void *bufs[] = {d->x,    d->xb,     d->qkv,       d->att,       d->logits,    d->kcache, d->vcache,
-                    d->ybuf, d->fbuf,   d->mbuf,      d->moe_in,    d->router_in, d->ids,    d->wts,
+    void *bufs[] = {d->x,    d->xb,     d->logits,    d->kcache, d->vcache,
+                    d->fbuf,   d->mbuf,      d->moe_in,    d->router_in, d->ids,    d->wts,
                     d->ids_zero, d->tokens, d->state, d->rng};
     for (void *b : bufs)
         if (b) lt_device_free(d->ctx, b);
@@ -194,8 +154,6 @@ lt_status lth_decoder_create(lt_ctx *ctx, const lth_model *m, lth_decoder **out)
     d->m = *m;
     d->layers.assign(m->layers, m->layers + m->n_layers);
     d->m.layers = nullptr;
-    d->nq = m->n_heads * m->head_dim;
-    d->nkv = m->n_kv_heads * m->head_dim;
     d->attn.n_heads = m->n_heads;
     d->attn.n_kv_heads = m->n_kv_heads;
     d->attn.head_dim = m->head_dim;
@@ -209,7 +167,7 @@ lt_status lth_decoder_create(lt_ctx *ctx, const lth_model *m, lth_decoder **out)
     d->kv_esize = m->kv_f16 ? 2 : 4;
     // per-layer caches: the model's heads and kv_cap positions, or (Gemma 4)
     // this layer's heads and, for sliding-window layers, a ring of the window
-    size_t cache = 0, max_q = d->nq, max_kv = d->nkv;
+    size_t cache = 0;
     for (uint32_t l = 0; l < m->n_layers; l++) {
         const lth_layer &L = m->layers[l];
         const bool g4 = m->family == LTH_GEMMA4;
@@ -222,19 +180,16 @@ lt_status lth_decoder_create(lt_ctx *ctx, const lth_model *m, lth_decoder **out)
         }
         d->kv_off.push_back(cache);
         cache += cap * nkv;
-        if (m->n_heads * hd > max_q) max_q = m->n_heads * hd;
-        if (nkv > max_kv) max_kv = nkv;
     }
     const size_t dm = m->d_model;
     lt_status st;
     if ((st = alloc(d, &d->x, dm)) != LT_OK || (st = alloc(d, &d->xb, dm)) != LT_OK ||
-        (st = alloc(d, &d->qkv, max_q + 2 * max_kv)) != LT_OK || (st = alloc(d, &d->att, max_q)) != LT_OK ||
         (st = alloc(d, &d->logits, m->vocab)) != LT_OK || (st = alloc(d, &d->kcache, cache * d->kv_esize)) != LT_OK ||
         (st = alloc(d, &d->vcache, cache * d->kv_esize)) != LT_OK || (st = alloc(d, &d->tokens, (size_t)m->kv_cap + 1)) != LT_OK ||
         (st = alloc(d, &d->state, 2)) != LT_OK || (st = alloc(d, &d->ids_zero, 4)) != LT_OK ||
         (st = alloc(d, &d->rng, 4)) != LT_OK ||
         (m->family == LTH_GEMMA4 &&
-         ((st = alloc(d, &d->ybuf, dm)) != LT_OK || (st = alloc(d, &d->fbuf, dm)) != LT_OK ||
+         ((st = alloc(d, &d->fbuf, dm)) != LT_OK ||
           (st = alloc(d, &d->mbuf, dm)) != LT_OK || (st = alloc(d, &d->moe_in, dm)) != LT_OK ||
           (st = alloc(d, &d->router_in, dm)) != LT_OK || (st = alloc(d, &d->ids, 16)) != LT_OK ||
           (st = alloc(d, &d->wts, 16)) != LT_OK))) {

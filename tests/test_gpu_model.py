@@ -277,6 +277,80 @@ def test_attn_block_matches_separate_ops(pkg, oracle, name, d, nh, nkv, hd, wt, 
     assert rel_l2(res[0], res[1]) < 2e-5, rel_l2(res[0], res[1])
 
 
+@pytest.mark.parametrize("name,d,nh,nkv,hd,types,vk,neox,qk,vnorm,bias,post,window,f16", [
+    # Q4_K_M-style: Q/K Q4_K, V Q6_K (so no stacked tensor), f16 KV
+    ("qwen3-mixed", 2048, 32, 4, 128, (12, 12, 14, 12), False, True, True, False, False, False, 0, True),
+    # Gemma 4 sliding layer: V normed, post-attention norm into the residual
+    ("gemma-swa", 1024, 8, 4, 256, (8, 8, 8, 8), False, True, True, True, False, True, 16, False),
+    # Gemma 4 full-attention layer without wv: V is the raw K projection
+    ("gemma-v=k", 1024, 8, 2, 256, (8, 14, None, 12), True, True, True, True, False, True, 0, True),
+    ("bias-v=k", 512, 4, 2, 128, (14, 8, None, 8), True, False, False, False, True, False, 0, False),
+    ("bias-split", 896, 14, 2, 64, (8, 8, 8, 8), False, False, False, False, True, False, 0, False),
+])
+def test_attn_block_split_matches_separate_ops(pkg, oracle, name, d, nh, nkv, hd, types, vk, neox, qk, vnorm, bias,
+                                                post, window, f16):
+    """lt_attn_block_split (separate Q/K/V tensors of mixed types, V = K,
+    post-attention norm) as the persistent kernel against the same computation
+    as separate ops, step by step over 24 positions."""
+    import os
+    synth, _ = _mods()
+    rng = np.random.default_rng(d + nh + 7)
+    nq, nk = nh * hd, nkv * hd
+    tq_, tk_, tv_, to_ = types
+    wq = synth.matrix(rng, tq_, nq, d)
+    wk = synth.matrix(rng, tk_, nk, d)
+    wv = None if vk else synth.matrix(rng, tv_, nk, d)
+    wo = synth.matrix(rng, to_, d, nq)
+    nw = rng.uniform(0.5, 1.5, d).astype(np.float32)
+    pn = rng.uniform(0.5, 1.5, d).astype(np.float32) if post else None
+    qn = rng.uniform(0.5, 1.5, hd).astype(np.float32) if qk else None
+    kn = rng.uniform(0.5, 1.5, hd).astype(np.float32) if qk else None
+    bs = rng.normal(0, 0.1, nq + (1 if vk else 2) * nk).astype(np.float32) if bias else None
+    cap = window if window else 64
+    cfg = pkg.AttnCfg(nh, nkv, hd, int(neox), 1e6, 1e-6, 1.0 if qk else 1.0 / np.sqrt(hd), cap, window, int(vnorm),
+                      int(f16))
+    ctxs = []
+    old = os.environ.get("LLMTOY_ATTN_BLOCK")
+    for flag in ("1", "0"):
+        os.environ["LLMTOY_ATTN_BLOCK"] = flag
+        c = pkg.Context(0)
+        c.set_stream(None)
+        ctxs.append(c)
+    if old is None:
+        del os.environ["LLMTOY_ATTN_BLOCK"]
+    else:
+        os.environ["LLMTOY_ATTN_BLOCK"] = old
+    res = []
+    for fused, c in zip((True, False), ctxs):
+        tq, tk = c.upload(wq, tq_, nq, d), c.upload(wk, tk_, nk, d)
+        tv = None if vk else c.upload(wv, tv_, nk, d)
+        to = c.upload(wo, to_, d, nq)
+        kc, vc = (empty(cap * nk, "float16"), empty(cap * nk, "float16")) if f16 else (empty(cap * nk), empty(cap * nk))
+        xs = []
+        rng2 = np.random.default_rng(78)
+        c.profile(True)
+        for pos in range(24):
+            x = dev(rng2.normal(0, 1, d).astype(np.float32))
+            out = x if pos % 2 else empty(d)  # in place and out of place
+            x0 = host(x)
+            c.attn_block_split(cfg, x, dev(nw), 1e-6, tq, tk, tv, None if bs is None else dev(bs),
+                               None if qn is None else dev(qn), None if kn is None else dev(kn),
+                               dev(np.array([pos], np.int32)), kc, vc, to, None if pn is None else dev(pn), out)
+            c.sync()
+            xs.append(host(out) - x0)
+        labels = c.profile_read()
+        c.profile(False)
+        assert any(k.startswith("attn_block") for k in labels) == fused, labels
+        res.append(np.stack(xs))
+        for t in (tq, tk, tv, to):
+            if t is not None:
+                t.free()
+        c.close()
+    # f16 caches: the two paths' K/V may round to neighbouring halves (f32 sums in another order)
+    tol = 1e-4 if f16 else 2e-5
+    assert rel_l2(res[0], res[1]) < tol, rel_l2(res[0], res[1])
+
+
 @pytest.mark.parametrize("moe", [True, False])
 def test_gguf_loaded_model_matches_oracle(ctx, oracle, pool, tmp_path, moe):
     """A synthetic model written as a GGUF file, loaded by the C++ loader
