@@ -44,7 +44,6 @@ struct AttnBlockArgs {
     const uint8_t *seg_w[3];
     uint64_t seg_pitch[3];
     uint32_t seg_type[3], seg_end[3], nseg;
-    uint64_t qpitch;      // the largest segment pitch
     uint32_t qrows, qnb;  // rows, 32-blocks per row (d / 32)
     uint32_t v_is_k;      // no V rows: V is the raw K head (gemma4/forward.zig:250)
     const float *bias;    // nullable [qrows]
@@ -64,7 +63,7 @@ struct AttnBlockArgs {
     const uint8_t *pf[2];
     uint64_t pf_bytes[2];
     int *dev_err;
-    uint32_t splits, maxq, maxo;
+    uint32_t splits, qtile, maxo;  // qtile: bytes of the largest CTA's Q/K/V rows
 };
 
 struct AbLayout {
@@ -83,13 +82,20 @@ __host__ __device__ inline AbLayout ab_layout(const AttnBlockArgs &a) {
     L.bars = take(64);
     L.misc = take(256);
     // + slack: a Q8_0 chunk reads up to 34 bytes past a row
-    const size_t qb = (size_t)a.maxq * a.qpitch + 128, ob = (size_t)a.maxo * a.opitch + 128;
+    const size_t qb = (size_t)a.qtile + 128, ob = (size_t)a.maxo * a.opitch + 128;
+    // the head vectors live only in phase A, when the Q/K/V rows are consumed:
+    // they take the Q/K/V tile's space (after the wo rows, when those follow there)
+    const size_t hb = (size_t)(3 * a.g.hd + kAbWarps * (a.g.hd + 2) + kAbWarps + 2) * 4;
+    const size_t ob128 = (ob + 127) & ~(size_t)127;
+    size_t head_in = SIZE_MAX;
     if (a.late_wo) {
         L.wq = take(qb > ob ? qb : ob);
         L.wo = L.wq;
+        if (qb >= ob128 + hb) head_in = L.wq + ob128;
     } else {
         L.wq = take(qb);
         L.wo = take(ob);
+        if (qb >= hb) head_in = L.wq;
     }
     L.xs = take(xs_bytes(1, (int)((a.d + 255) / 256)));
     L.as = take(xs_bytes(1, (int)((nq + 255) / 256)));
@@ -97,7 +103,7 @@ __host__ __device__ inline AbLayout ab_layout(const AttnBlockArgs &a) {
     L.nw = take((size_t)a.d * 4);
     L.xres = take((size_t)a.maxo * 4);
     // per-item head vectors q, k, v and the warps' softmax partials
-    L.head = take((size_t)(3 * a.g.hd + kAbWarps * (a.g.hd + 2) + kAbWarps + 2) * 4);
+    L.head = head_in != SIZE_MAX ? head_in : take(hb);
     L.total = off;
     return L;
 }
@@ -648,7 +654,6 @@ static bool ab_args(const AttnBlockParams &p, int num_sms, AttnBlockArgs &a) {
     const uint32_t nq = g.n_heads * g.hd, nkv = g.n_kv * g.hd;
     const uint32_t want = nq + nkv + (p.v_is_k ? 0u : nkv);
     uint32_t rows = 0;
-    a.qpitch = 0;
     for (uint32_t s = 0; s < p.nseg; s++) {
         const DevMat &m = p.seg[s];
         if (!ab_type_ok(m.type) || m.cols != p.d || m.n_experts) return false;
@@ -657,7 +662,6 @@ static bool ab_args(const AttnBlockParams &p, int num_sms, AttnBlockArgs &a) {
         a.seg_pitch[s] = m.pitch;
         a.seg_type[s] = m.type;
         a.seg_end[s] = rows;
-        a.qpitch = m.pitch > a.qpitch ? m.pitch : a.qpitch;
     }
     if (rows != want) return false;
     if (!ab_type_ok(p.wo.type) || p.wo.rows != p.d || p.wo.cols != nq || nq > 16384) return false;
@@ -672,7 +676,16 @@ static bool ab_args(const AttnBlockParams &p, int num_sms, AttnBlockArgs &a) {
     a.otype = p.wo.type;
     const uint32_t G = (uint32_t)num_sms;
     a.splits = max(1u, min(kAbMaxSplits, G / g.n_heads));
-    a.maxq = (a.qrows + G - 1) / G;
+    a.qtile = 0;
+    for (uint32_t c = 0; c < G; c++) {  // the kernel's split of the rows over the CTAs
+        const uint32_t q0 = (uint32_t)((uint64_t)c * a.qrows / G), q1 = (uint32_t)((uint64_t)(c + 1) * a.qrows / G);
+        uint64_t bytes = 0;
+        for (uint32_t sg = 0; sg < a.nseg; sg++) {
+            const uint32_t sb = sg ? a.seg_end[sg - 1] : 0, lo = max(q0, sb), hi = min(q1, a.seg_end[sg]);
+            if (lo < hi) bytes += (uint64_t)(hi - lo) * a.seg_pitch[sg];
+        }
+        if (bytes > a.qtile) a.qtile = (uint32_t)bytes;
+    }
     a.maxo = (p.d + G - 1) / G;
     a.late_wo = 0;
     if (ab_layout(a).total > kDecodeSmemLimit) {  // the wo rows wait for the Q/K/V rows' space

@@ -285,6 +285,10 @@ def test_attn_block_matches_separate_ops(pkg, oracle, name, d, nh, nkv, hd, wt, 
     # Gemma 4 full-attention layer without wv: V is the raw K projection
     ("gemma-v=k", 1024, 8, 2, 256, (8, 14, None, 12), True, True, True, True, False, True, 0, True),
     ("bias-v=k", 512, 4, 2, 128, (14, 8, None, 8), True, False, False, False, True, False, 0, False),
+    # Gemma-4-26B-A4B attention shape: the Q8_0 tile leaves no room for the wo rows until phase Q ends
+    ("gemma26b-q8", 2816, 16, 8, 256, (8, 8, 8, 8), False, True, True, True, False, True, 1024, True),
+    # the same shape whose tiles fit together with the head vectors in the consumed Q/K/V space
+    ("gemma26b-mixed", 2816, 16, 8, 256, (14, 12, 12, 12), False, True, True, True, False, True, 1024, False),
     ("bias-split", 896, 14, 2, 64, (8, 8, 8, 8), False, False, False, False, True, False, 0, False),
 ])
 def test_attn_block_split_matches_separate_ops(pkg, oracle, name, d, nh, nkv, hd, types, vk, neox, qk, vnorm, bias,
