@@ -84,6 +84,7 @@ struct DecodeArgs {
     uint8_t *sync;
     int *dev_err;
     uint32_t maxpairs, maxrows;  // per-CTA maxima the layout is sized for
+    uint32_t gchunks;            // gate/up chunks the tile space holds: more are copied in rounds
     const uint8_t *pf[2];        // optional L2 prefetch ranges (the next kernel's weights)
     uint64_t pf_bytes[2];
 };
@@ -98,7 +99,8 @@ __host__ __device__ inline uint32_t chunks64(uint32_t cols) { return (cols + 63)
 // after the h barrier (when both do not fit at once).
 __host__ __device__ inline DecodeLayout decode_layout(uint32_t E, uint32_t d, uint32_t F, uint32_t k, uint64_t gpitch,
                                                       uint32_t gi, uint64_t dpitch, uint32_t di, uint32_t img,
-                                                      uint32_t maxpairs, uint32_t maxrows, int late_down) {
+                                                      uint32_t maxpairs, uint32_t maxrows, int late_down,
+                                                      uint32_t gchunks) {
     DecodeLayout L;
     size_t off = 0;
     auto take = [&](size_t b) {
@@ -119,7 +121,7 @@ __host__ __device__ inline DecodeLayout decode_layout(uint32_t E, uint32_t d, ui
     L.xsx = take(xs_bytes(1, gi));
     const size_t rr0 = (size_t)2 * d * 4, rr1 = (size_t)k * img;
     L.rr = take(rr0 > rr1 ? rr0 : rr1);
-    const size_t gtb = (size_t)maxpairs * 2 * gpitch, dtb = (size_t)k * maxrows * dpitch;
+    const size_t gtb = (size_t)gchunks * 2 * kDecChunk * gpitch, dtb = (size_t)k * maxrows * dpitch;
     if (late_down) {
         L.gt = take(gtb > dtb ? gtb : dtb);
         L.dt = L.gt;
@@ -138,7 +140,8 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t G = gridDim.x, c = blockIdx.x;
     const DecodeLayout L =
-        decode_layout(a.E, a.d, a.F, a.k, a.gpitch, a.gi, a.dpitch, a.di, a.img, a.maxpairs, a.maxrows, a.late_down);
+        decode_layout(a.E, a.d, a.F, a.k, a.gpitch, a.gi, a.dpitch, a.di, a.img, a.maxpairs, a.maxrows, a.late_down,
+                      a.gchunks);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
     uint64_t *hbar = bars + kDecMaxChunks + 16;
     uint32_t *s_sel = reinterpret_cast<uint32_t *>(smem + L.misc);    // [16]
@@ -284,28 +287,30 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     __syncthreads();
 
     // ── phase G ──────────────────────────────────────────────────────────────
-    if (warp == 0) {  // one TMA chunk per lane: [n gate rows][n up rows]
-        for (uint32_t j = lane; j < nchunks; j += 32) {
-            const uint32_t q0 = p0 + j * kDecChunk;
-            const uint32_t s = q0 / a.F, f0 = q0 - s * a.F;
-            const uint32_t e = min(s_sel[s], a.E - 1);
-            const uint32_t bytes = (uint32_t)(kDecChunk * a.gpitch);
-            uint64_t grow, urow;
-            const uint8_t *ub;
-            if (a.up) {
-                grow = (uint64_t)e * a.F + f0;
-                urow = grow;
-                ub = a.up;
-            } else {  // fused: gate rows [0,F), up rows [F,2F) (gemma4/forward.zig:469-471)
-                grow = (uint64_t)e * 2 * a.F + f0;
-                urow = grow + a.F;
-                ub = a.gate;
-            }
-            uint8_t *dst = gt + (size_t)2 * j * kDecChunk * a.gpitch;
-            mbar_arrive_expect_tx(&bars[j], 2 * bytes);
-            tma_load_1d(dst, a.gate + grow * a.gpitch, bytes, &bars[j]);
-            tma_load_1d(dst + bytes, ub + urow * a.gpitch, bytes, &bars[j]);
+    // chunk j: [8 gate rows][8 up rows] of pairs p0 + 8j.., into tile slot j % gchunks
+    auto issue_chunk = [&](uint32_t j) {
+        const uint32_t q0 = p0 + j * kDecChunk;
+        const uint32_t s = q0 / a.F, f0 = q0 - s * a.F;
+        const uint32_t e = min(s_sel[s], a.E - 1);
+        const uint32_t bytes = (uint32_t)(kDecChunk * a.gpitch);
+        uint64_t grow, urow;
+        const uint8_t *ub;
+        if (a.up) {
+            grow = (uint64_t)e * a.F + f0;
+            urow = grow;
+            ub = a.up;
+        } else {  // fused: gate rows [0,F), up rows [F,2F) (gemma4/forward.zig:469-471)
+            grow = (uint64_t)e * 2 * a.F + f0;
+            urow = grow + a.F;
+            ub = a.gate;
         }
+        uint8_t *dst = gt + (size_t)2 * (j % a.gchunks) * kDecChunk * a.gpitch;
+        mbar_arrive_expect_tx(&bars[j], 2 * bytes);
+        tma_load_1d(dst, a.gate + grow * a.gpitch, bytes, &bars[j]);
+        tma_load_1d(dst + bytes, ub + urow * a.gpitch, bytes, &bars[j]);
+    };
+    if (warp == 0) {  // one TMA chunk per lane: the first round's
+        for (uint32_t j = lane; j < min(nchunks, a.gchunks); j += 32) issue_chunk(j);
     } else if (warp == 1) {  // down rows [r0, r1) of each slot's expert
         if (!a.late_down && (uint32_t)lane < a.k && nr) {
             const uint32_t e = min(s_sel[lane], a.E - 1);
@@ -326,12 +331,22 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
             }
     }
     // gate/up: warp w takes tile rows w*rps.., one TMA chunk (16 tile rows)
-    // after another; a lane owns one 64-column chunk of x in registers
+    // after another; a lane owns one 64-column chunk of x in registers.  When
+    // the tile space holds fewer chunks than this CTA's share, the share goes
+    // in rounds of gchunks chunks, each copied over the previous round's.
     const uint32_t cpr_g = chunks64(a.d);
     const uint32_t gstride = 2 * a.maxpairs + 1;  // partials [chunk][tile row], odd stride: no bank conflicts
-    {
+    const uint32_t rows_round = 2 * kDecChunk * a.gchunks;
+    for (uint32_t rbase = 0; rbase < 2 * np; rbase += rows_round) {
+        if (rbase) {  // the previous round's rows are consumed
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncthreads();
+            if (tid == 0)
+                for (uint32_t j = rbase / (2 * kDecChunk); j < min(nchunks, (rbase + rows_round) / (2 * kDecChunk)); j++)
+                    issue_chunk(j);
+        }
         const uint32_t lpr = min(cpr_g, 32u), rps = 32 / lpr;  // lanes per row, rows per step
-        const uint32_t sub = lane / lpr, nrows = 2 * np;
+        const uint32_t sub = lane / lpr, nrows = min(2 * np, rbase + rows_round);
         if (sub < rps) {
             for (uint32_t cg = 0; cg < cpr_g; cg += lpr) {
                 const uint32_t n = min(lpr, cpr_g - cg);
@@ -342,14 +357,14 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
                 // two rows per iteration (independent chains for the scheduler);
                 // an odd last row is computed twice and stored once
                 const uint32_t step = kDecWarps * rps;
-                for (uint32_t r = warp * rps + sub; r < nrows; r += 2 * step) {
+                for (uint32_t r = rbase + warp * rps + sub; r < nrows; r += 2 * step) {
                     const uint32_t rb = r + step < nrows ? r + step : r;
                     const bool ok = tile_wait(&bars[r / (2 * kDecChunk)], a.dev_err) &
                                     tile_wait(&bars[rb / (2 * kDecChunk)], a.dev_err);
                     float ya = 0.0f, yb = 0.0f;
                     if (ok) {
-                        ya = dot64<GT>(gt + (size_t)r * a.gpitch, (int)cb, (int)a.gnb, xc);
-                        yb = dot64<GT>(gt + (size_t)rb * a.gpitch, (int)cb, (int)a.gnb, xc);
+                        ya = dot64<GT>(gt + (size_t)(r - rbase) * a.gpitch, (int)cb, (int)a.gnb, xc);
+                        yb = dot64<GT>(gt + (size_t)(rb - rbase) * a.gpitch, (int)cb, (int)a.gnb, xc);
                     }
                     part[cb * gstride + r] = ya;
                     part[cb * gstride + rb] = yb;
@@ -505,14 +520,21 @@ bool decode_plan(const DecodeParams &p, int num_sms, DecodePlan &out) {
     a.maxpairs = (uint32_t)(kDecUnit * ((nunits + G - 1) / G));
     a.maxrows = (p.d + G - 1) / G;
     if (a.maxpairs / kDecChunk > (uint32_t)kDecMaxChunks) return false;
-    a.late_down = 0;
-    DecodeLayout L = decode_layout(a.E, a.d, a.F, a.k, a.gpitch, a.gi, a.dpitch, a.di, a.img, a.maxpairs, a.maxrows, 0);
-    if (L.total > kDecodeSmemLimit) {
-        a.late_down = 1;
-        L = decode_layout(a.E, a.d, a.F, a.k, a.gpitch, a.gi, a.dpitch, a.di, a.img, a.maxpairs, a.maxrows, 1);
+    // the whole share at once with the down rows beside it; else the down rows
+    // after the h barrier in the gate/up space; else the gate/up share in rounds
+    for (uint32_t gc = a.maxpairs / kDecChunk; gc >= 1; gc--) {
+        for (int late = 0; late < 2; late++) {
+            const DecodeLayout L = decode_layout(a.E, a.d, a.F, a.k, a.gpitch, a.gi, a.dpitch, a.di, a.img,
+                                                 a.maxpairs, a.maxrows, late, gc);
+            if (L.total <= kDecodeSmemLimit) {
+                a.late_down = late;
+                a.gchunks = gc;
+                out.smem = L.total;
+                return true;
+            }
+        }
     }
-    out.smem = L.total;
-    return L.total <= kDecodeSmemLimit;
+    return false;
 }
 
 template <uint32_t GT, uint32_t DT>

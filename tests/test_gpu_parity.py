@@ -560,19 +560,20 @@ def test_moe_ffn_invalid_id_reported(ctx, pkg, oracle, pool, T):
         t_.free()
 
 
-@pytest.mark.parametrize("T", [1, 3])
-def test_moe_block_scaled_matches_ops(ctx, pkg, T):
+@pytest.mark.parametrize("T,gt", [(1, 12), (1, 14), (1, 8), (3, 12)])
+def test_moe_block_scaled_matches_ops(ctx, pkg, T, gt):
     """lt_moe_block_scaled (Gemma 4's MoE half) against the separate ops it
     replaces -- lt_norm_pair, lt_moe_route on the raw-scaled input, lt_moe_ffn on
     the weighted one: the same ids and weights bit for bit (the router input is
     norm_pair's arithmetic), outputs within f32 rounding of the expert kernels'
     different partial-sum grouping (one persistent launch at T = 1; at T = 3
-    the ops themselves, bit for bit)."""
+    the ops themselves, bit for bit).  Q6_K and Q8_0 gate/up tiles of this
+    shape exceed shared memory: the persistent kernel takes them in rounds."""
     import importlib
     synth = importlib.import_module("llmtoy-zig_b200.synth")
-    rng = np.random.Generator(np.random.PCG64(2816 + T))
+    rng = np.random.Generator(np.random.PCG64(2816 + T + gt))
     d, E, F, k = 2816, 32, 704, 8
-    L = synth.MoeLayer(rng, d, E, F, 12, 8, fused=True)
+    L = synth.MoeLayer(rng, d, E, F, gt, 8, fused=True)
     rt, g, u, dn = _upload_layer(ctx, L)
     x = rng.normal(0, 2, (T, d)).astype(np.float32)
     nw = dev(rng.uniform(0.5, 1.5, d).astype(np.float32))
@@ -580,7 +581,13 @@ def test_moe_block_scaled_matches_ops(ctx, pkg, T):
     es = dev(rng.uniform(0.5, 2.0, E).astype(np.float32))
     gs = float(np.float32(1.0 / np.sqrt(d)))
     out, ids, w = empty(T * d), empty(T * k, "int32"), empty(T * k)
+    ctx.profile(True)
     ctx.moe_block_scaled(rt, g, None, dn, 1, False, es, nw, rs, gs, 1e-6, dev(x), T, k, out, False, ids, w)
+    ctx.sync()
+    labels = ctx.profile_read()
+    ctx.profile_reset()
+    ctx.profile(False)
+    assert ("moe_decode" in labels) == (T == 1), labels
     a, b = empty(T * d), empty(T * d)
     ctx.norm_pair(dev(x), nw, rs, gs, 1e-6, d, T, a, b)
     ids2, w2, out2 = empty(T * k, "int32"), empty(T * k), empty(T * d)
