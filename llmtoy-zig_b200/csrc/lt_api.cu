@@ -610,8 +610,11 @@ static lt_status qmatvec_impl(lt_ctx *ctx, const lt_tensor *w, uint32_t expert, 
     if (w->m.rows > 0xffffffffull) return fail(ctx, LT_EINVAL, "lt_qmatvec: too many rows");
     const lt::LaunchCfg c = cfg_of(ctx);
     // f32/f16 rows; or one token over few enough CTAs that each quantising it
-    // costs less than a separate quantiser launch (not the lm_head's thousands)
-    if (!quantized(w->m.type) || (ntok == 1 && lt::qmv_ctas(w->m) <= 2u * (uint32_t)ctx->num_sms))
+    // costs less than a separate quantiser launch; or the persistent streaming
+    // kernel (one CTA per SM) for a large matrix such as an lm_head
+    if (!quantized(w->m.type) ||
+        (ntok == 1 && (lt::qmv_ctas(w->m) <= 2u * (uint32_t)ctx->num_sms ||
+                       lt::qmv_streams(w->m, 1, ctx->num_sms))))
         return launched(ctx, lt::launch_qmatvec(c, w->m, expert, nullptr, 0, dev_x, dev_y, ntok, dev_add), "qmatvec");
     const uint64_t qp = lt::qact_row_pitch(w->m.cols);
     if ((st = ensure_scratch(ctx, al256((size_t)ntok * qp))) != LT_OK) return st;

@@ -162,6 +162,9 @@ cudaError_t launch_quantize(const LaunchCfg &c, const float *x, uint32_t cols, u
 // CTAs of a quantised matvec over m's rows (each quantises a one-token input
 // itself when launch_qmatvec gets no pre-quantised rows).
 uint32_t qmv_ctas(const DevMat &m);
+// Whether launch_qmatvec runs this matvec as the persistent streaming kernel
+// (one token over a large matrix; it quantises the f32 row itself).
+bool qmv_streams(const DevMat &m, uint32_t ntok, int num_sms);
 // n <= 4 one-token matvecs y[s] = m[s] . x (x normalised by norm_w first when
 // given) in one launch; the matrices share cols and may differ in type.
 cudaError_t launch_qmatvec_multi(const LaunchCfg &c, uint32_t n, const DevMat *const *m, const float *x,

@@ -38,15 +38,17 @@ inline cudaError_t launch_k(const LaunchCfg &c, const char *label, Kern kern, di
 // Static per-type profiler labels for "qmv", "moe_gate_up" and "moe_down".
 template <uint32_t TYPE>
 inline const char *type_label(const char *kind) {
-    static const char *const names[3][8] = {
+    static const char *const names[4][8] = {
         {"qmv_q4k", "qmv_q6k", "qmv_q8_0", "qmv_q5_0", "qmv_q5_1", "qmv_q3k", "qmv_q5k", "qmv_iq4nl"},
         {"moe_gate_up_q4k", "moe_gate_up_q6k", "moe_gate_up_q8_0", "moe_gate_up_q5_0", "moe_gate_up_q5_1",
          "moe_gate_up_q3k", "moe_gate_up_q5k", "moe_gate_up_iq4nl"},
         {"moe_down_q4k", "moe_down_q6k", "moe_down_q8_0", "moe_down_q5_0", "moe_down_q5_1", "moe_down_q3k",
-         "moe_down_q5k", "moe_down_iq4nl"}};
+         "moe_down_q5k", "moe_down_iq4nl"},
+        {"qmv_stream_q4k", "qmv_stream_q6k", "qmv_stream_q8_0", "qmv_stream_q5_0", "qmv_stream_q5_1",
+         "qmv_stream_q3k", "qmv_stream_q5k", "qmv_stream_iq4nl"}};
     const int t = TYPE == T_Q4_K ? 0 : TYPE == T_Q6_K ? 1 : TYPE == T_Q8_0 ? 2 : TYPE == T_Q5_0 ? 3
                 : TYPE == T_Q5_1 ? 4 : TYPE == T_Q3_K ? 5 : TYPE == T_Q5_K ? 6 : 7;
-    const int k = kind[0] == 'q' ? 0 : kind[4] == 'g' ? 1 : 2;
+    const int k = kind[0] == 'q' ? (kind[3] == '_' ? 3 : 0) : kind[4] == 'g' ? 1 : 2;
     return names[k][t];
 }
 

@@ -163,6 +163,149 @@ __global__ void k_mv_float(const uint8_t *rows, uint64_t pitch, uint32_t type, u
     }
 }
 
+// Large one-token matvecs (an lm_head of hundreds of MB): a persistent kernel,
+// one CTA per SM with 16 warps, 8 to 16 of which stream rows (as many as
+// have two stages' room).  Each streaming warp takes groups of rw rows (group
+// g goes to streaming warp g % (CTAs * warps)) through its own ring of shared-memory
+// stages, one TMA bulk copy per group, so the next groups' copies are in
+// flight while it computes the current one.  Per-item partials and the
+// per-row order of their sum are k_qmv's: the same bits.
+constexpr int kQsWarps = 16;
+constexpr uint32_t kQsMaxStages = 8;
+constexpr size_t kQsBars = 0, kQsSrc = 1024, kQsPart = 1152, kQsX = 3200;  // + X, then the rings
+
+struct QsArgs {
+    QmvArgs a;
+    uint32_t stages;  // ring depth per warp
+    uint32_t stage;   // bytes per stage (a multiple of 128)
+    uint32_t warps;   // warps that stream rows (the rest help stage the activations)
+};
+
+__host__ __device__ inline size_t qs_ring_offset(int ipr) { return kQsX + ((xs_bytes(1, ipr) + 127) & ~(size_t)127); }
+
+template <uint32_t TYPE>
+__global__ void __launch_bounds__(kQsWarps * 32, 1) k_qmv_stream(QsArgs q) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const QmvArgs &a = q.a;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ipr = (int)a.nitems;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kQsBars) + warp * kQsMaxStages;
+    float *wpart = reinterpret_cast<float *>(smem + kQsPart) + warp * 32;
+    const XS X = xs_carve(smem + kQsX, 1, ipr);
+    uint8_t *ring = smem + qs_ring_offset(ipr) + (size_t)warp * q.stages * q.stage;
+    const uint32_t W = gridDim.x * q.warps, gw = blockIdx.x * q.warps + warp;
+    const uint32_t ngroups = (a.nrows + a.rw - 1) / a.rw;
+    // groups gw, gw + W, ...
+    const uint32_t mine = (uint32_t)warp < q.warps && gw < ngroups ? (ngroups - gw + W - 1) / W : 0;
+    auto issue = [&](uint32_t i) {
+        const uint32_t r0 = (gw + i * W) * a.rw, nr = min(a.rw, a.nrows - r0), st = i % q.stages;
+        mbar_arrive_expect_tx(&bars[st], (uint32_t)(nr * a.pitch));
+        tma_load_1d(ring + (size_t)st * q.stage, a.rows + (uint64_t)r0 * a.pitch, (uint32_t)(nr * a.pitch), &bars[st]);
+    };
+    if (lane == 0) {  // weights are static: the first stages before waiting on the producer
+        for (uint32_t st = 0; st < q.stages; st++) mbar_init(&bars[st], 1);
+        fence_barrier_init();
+        for (uint32_t i = 0; i < min(mine, q.stages); i++) issue(i);
+    }
+    __syncwarp();
+    pdl_launch_dependents();
+    pdl_wait();
+    if (a.xq) {
+        const uint8_t **src = reinterpret_cast<const uint8_t **>(smem + kQsSrc);
+        if (threadIdx.x == 0) src[0] = a.xq;
+        __syncthreads();
+        qact_to_smem(X, src, 1, (int)a.cols);
+    } else {  // the same 16-group quantisation as k_quantize
+        for (uint32_t b = warp; b < a.cols / 32; b += kQsWarps)
+            qact_block_to_xs(X, 0, (int)b, __ldcg(a.xf + 32 * b + lane), lane);
+    }
+    __syncthreads();
+    uint32_t i = 0;
+    bool ok = true;
+    for (; i < mine; i++) {
+        const uint32_t st = i % q.stages;
+        if (!mbar_wait_bounded(&bars[st], (i / q.stages) & 1, kWaitLimitNs)) {
+            ok = false;
+            break;
+        }
+        const uint32_t r0 = (gw + i * W) * a.rw, nr = min(a.rw, a.nrows - r0);
+        const uint8_t *t = ring + (size_t)st * q.stage;
+        const int nitem = (int)nr * ipr;
+        for (int f = lane; f < nitem; f += 32) {
+            float res[1] = {0.0f};
+            dot_item<TYPE, 1>(t + (size_t)(f / ipr) * a.pitch, f % ipr, (int)a.nblocks, X, 0, 1, res);
+            wpart[f] = res[0];
+        }
+        __syncwarp();
+        if (lane == 0 && i + q.stages < mine) {  // the stage is read: the group after next takes it
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(i + q.stages);
+        }
+        if ((uint32_t)lane < nr) {
+            const float *pp = wpart + lane * ipr;
+            float sum = 0.0f;
+            for (int k = 0; k < ipr; k++) sum += pp[k];
+            const size_t yi = r0 + lane;
+            a.y[yi] = a.add ? __fadd_rn(a.add[yi], sum) : sum;
+        }
+        __syncwarp();
+    }
+    if (!ok && lane == 0) {  // report, then let the copies in flight land before the CTA exits
+        if (a.dev_err) atomicExch(a.dev_err, DEV_ERR_TMA_TIMEOUT);
+        for (uint32_t j = i; j < min(mine, i + q.stages); j++)
+            mbar_wait_bounded(&bars[j % q.stages], (j / q.stages) & 1, kWaitLimitNs);
+    }
+}
+
+// The ring layout for a one-token matvec over m, or false when the persistent
+// kernel does not pay (few rows) or two stages per warp do not fit.
+static bool qs_plan(const DevMat &m, uint32_t rw, uint32_t ipr, int num_sms, uint32_t &stages, uint32_t &stage,
+                    uint32_t &warps, size_t &smem) {
+    if (!is_quant_type(m.type) || num_sms <= 0 || ipr > 32) return false;  // a group's items: one per lane
+    if (m.rows * m.pitch < ((uint64_t)32 << 20) || qmv_ctas(m) <= 4u * (uint32_t)num_sms) return false;
+    stage = (uint32_t)((rw * m.pitch + 127) & ~(uint64_t)127);
+    const size_t fixed = qs_ring_offset((int)ipr) + 256;  // + slack: a Q8_0 chunk reads past its row
+    for (warps = kQsWarps; warps >= 8; warps -= 4) {  // at least two stages per warp
+        if (fixed + (size_t)2 * warps * stage > kDecodeSmemLimit) continue;
+        stages = (uint32_t)min((size_t)kQsMaxStages, (kDecodeSmemLimit - fixed) / ((size_t)warps * stage));
+        smem = fixed + (size_t)stages * warps * stage;
+        return true;
+    }
+    return false;
+}
+
+bool qmv_streams(const DevMat &m, uint32_t ntok, int num_sms) {
+    if (ntok != 1 || !is_quant_type(m.type)) return false;
+    const uint32_t ipr = items_per_row(m.type, m.cols), rw = max(1u, 32u / ipr);
+    uint32_t stages, stage, warps;
+    size_t smem;
+    return qs_plan(m, rw, ipr, num_sms, stages, stage, warps, smem);
+}
+
+template <uint32_t TYPE>
+static cudaError_t launch_qs_t(const LaunchCfg &c, const QsArgs &q, size_t smem) {
+    return launch_k(c, type_label<TYPE>("qmv_stream"), k_qmv_stream<TYPE>, dim3((unsigned)c.num_sms),
+                    dim3(kQsWarps * 32), smem, q);
+}
+
+static cudaError_t launch_qmv_stream(const LaunchCfg &c, const DevMat &m, const QmvArgs &a) {
+    QsArgs q;
+    q.a = a;
+    size_t smem;
+    if (!qs_plan(m, a.rw, a.nitems, c.num_sms, q.stages, q.stage, q.warps, smem)) return cudaErrorInvalidValue;
+    switch (m.type) {
+    case T_Q4_K: return launch_qs_t<T_Q4_K>(c, q, smem);
+    case T_Q6_K: return launch_qs_t<T_Q6_K>(c, q, smem);
+    case T_Q8_0: return launch_qs_t<T_Q8_0>(c, q, smem);
+    case T_Q5_0: return launch_qs_t<T_Q5_0>(c, q, smem);
+    case T_Q5_1: return launch_qs_t<T_Q5_1>(c, q, smem);
+    case T_IQ4_NL: return launch_qs_t<T_IQ4_NL>(c, q, smem);
+    case T_Q5_K: return launch_qs_t<T_Q5_K>(c, q, smem);
+    case T_Q3_K: return launch_qs_t<T_Q3_K>(c, q, smem);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
 uint32_t qmv_ctas(const DevMat &m) {
     const uint32_t rw = max(1u, 32u / items_per_row(m.type, m.cols));
     return (uint32_t)((m.rows + kQmvWarps * rw - 1) / (kQmvWarps * rw));
@@ -203,6 +346,7 @@ cudaError_t launch_qmatvec(const LaunchCfg &c, const DevMat &m, uint32_t expert,
     a.ntok = ntok;
     a.rw = max(1u, 32u / a.nitems);
     a.dev_err = c.dev_err;
+    if (qmv_streams(m, ntok, c.num_sms)) return launch_qmv_stream(c, m, a);
     const bool one = ntok == 1;
     switch (m.type) {
     case T_Q4_K: return one ? launch_qmv_t<T_Q4_K, 1>(c, a) : launch_qmv_t<T_Q4_K, 4>(c, a);

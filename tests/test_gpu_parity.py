@@ -140,6 +140,34 @@ def test_qmatvec_reference_fuzz(ctx, oracle, ggml_type, rows, cols):
     t.free()
 
 
+@pytest.mark.parametrize("ggml_type,rows,cols", [(14, 40000, 2816), (12, 60000, 2048), (8, 50001, 896),
+                                                 (13, 40000, 2048)])
+def test_qmatvec_streaming_lm_head(ctx, oracle, ggml_type, rows, cols):
+    """One token over an lm_head-sized matrix runs as the persistent streaming
+    kernel (per-warp TMA rings): against the oracle, and against the
+    multi-token kernel on the same row."""
+    import importlib
+    synth = importlib.import_module("llmtoy-zig_b200.synth")
+    rng = np.random.Generator(np.random.PCG64(rows + cols + ggml_type))
+    mat = synth.matrix(rng, ggml_type, rows, cols)
+    x = rng.normal(0, 1, size=(3, cols)).astype(np.float32)
+    t = ctx.upload(mat, ggml_type, rows, cols)
+    y1, y3 = empty(rows), empty(3 * rows)
+    ctx.profile(True)
+    ctx.qmatvec(t, dev(x[0]), y1, 1)
+    ctx.sync()
+    labels = ctx.profile_read()
+    ctx.profile_reset()
+    ctx.profile(False)
+    assert any(k.startswith("qmv_stream") for k in labels), labels
+    ctx.qmatvec(t, dev(x), y3, 3)
+    got = host(y1)
+    ref = oracle.quant_matvec(mat, ggml_type, x[0], rows, cols)
+    assert max_rel(got, ref) < MATVEC_TOL
+    assert rel_l2(got, host(y3)[:rows]) < 1e-6
+    t.free()
+
+
 def test_qmatvec_expert_slice(ctx, oracle):
     import importlib
     synth = importlib.import_module("llmtoy-zig_b200.synth")
