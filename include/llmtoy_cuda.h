@@ -404,15 +404,16 @@ lt_status lt_ffn_block(lt_ctx *ctx, const lt_tensor *gate, const lt_tensor *up, 
  *   lt_scale        x *= s                                   (:117-120 embedding, :531 layer_output_scale)
  *   lt_add_rmsnorm  x += rmsnorm(y) * w                      (:329-333 post_attention_norm)
  *   lt_norm_pair    a = rmsnorm(x) * w, b = x * rms_inv * gs * g   (:401-410, math.zig:51-82)
- *   lt_ffn_tail     m = rmsnorm(m) * w2; x = (x + rmsnorm(f + m) * w) * los   (:520-532)
+ *   lt_ffn_tail     m = rmsnorm(m) * w2; x = (x + rmsnorm(f' + m) * w) * los   (:520-532),
+ *                   f' = rmsnorm(f) * w1 (post_ffw_norm_1, :396), or f when w1 is NULL
  *   lt_softcap      x = tanh(x / cap) * cap over n values   (:560-564) */
 lt_status lt_scale(lt_ctx *ctx, float *dev_x, uint32_t n, uint32_t ntok, float s);
 lt_status lt_add_rmsnorm(lt_ctx *ctx, const float *dev_y, const float *dev_w, float eps, uint32_t n,
                          uint32_t ntok, float *dev_x);
 lt_status lt_norm_pair(lt_ctx *ctx, const float *dev_x, const float *dev_w, const float *dev_g, float gs,
                        float eps, uint32_t n, uint32_t ntok, float *dev_a, float *dev_b);
-lt_status lt_ffn_tail(lt_ctx *ctx, const float *dev_f, float *dev_m, const float *dev_w2, const float *dev_w,
-                      float los, float eps, uint32_t n, uint32_t ntok, float *dev_x);
+lt_status lt_ffn_tail(lt_ctx *ctx, const float *dev_f, const float *dev_w1, float *dev_m, const float *dev_w2,
+                      const float *dev_w, float los, float eps, uint32_t n, uint32_t ntok, float *dev_x);
 lt_status lt_softcap(lt_ctx *ctx, float *dev_x, uint64_t n, float cap);
 
 /* greedy (sample.zig:11-17) as the last op of a decode step: with

@@ -143,7 +143,7 @@ def load_library() -> ctypes.CDLL:
         "lt_scale": (I, [P, P, U32, U32, F]),
         "lt_add_rmsnorm": (I, [P, P, P, F, U32, U32, P]),
         "lt_norm_pair": (I, [P, P, P, P, F, F, U32, U32, P, P]),
-        "lt_ffn_tail": (I, [P, P, P, P, P, F, F, U32, U32, P]),
+        "lt_ffn_tail": (I, [P, P, P, P, P, P, F, F, U32, U32, P]),
         "lt_softcap": (I, [P, P, U64, F]),
         "lt_sample_step": (I, [P, P, U32, ctypes.POINTER(SampleParams), P, P, P, P]),
         "lt_rng_seed": (None, [U64, ctypes.POINTER(U64)]),
@@ -430,8 +430,10 @@ class Context:
     def norm_pair(self, x, w, g, gs: float, eps: float, n: int, ntok: int, a, b) -> None:
         self._check(self.lib.lt_norm_pair(self.ptr, _ptr(x), _ptr(w), _ptr(g), gs, eps, n, ntok, _ptr(a), _ptr(b)))
 
-    def ffn_tail(self, f, m, w2, w, los: float, eps: float, n: int, ntok: int, x) -> None:
-        self._check(self.lib.lt_ffn_tail(self.ptr, _ptr(f), _ptr(m), _ptr(w2), _ptr(w), los, eps, n, ntok, _ptr(x)))
+    def ffn_tail(self, f, m, w2, w, los: float, eps: float, n: int, ntok: int, x, w1=None) -> None:
+        """m = rmsnorm(m) * w2; x = (x + rmsnorm(f' + m) * w) * los, f' = rmsnorm(f) * w1 when w1 is given."""
+        self._check(self.lib.lt_ffn_tail(self.ptr, _ptr(f), _ptr(w1), _ptr(m), _ptr(w2), _ptr(w), los, eps, n, ntok,
+                                         _ptr(x)))
 
     def softcap(self, x, n: int, cap: float) -> None:
         self._check(self.lib.lt_softcap(self.ptr, _ptr(x), n, cap))

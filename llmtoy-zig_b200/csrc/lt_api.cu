@@ -1252,13 +1252,13 @@ lt_status lt_norm_pair(lt_ctx *ctx, const float *dev_x, const float *dev_w, cons
                     "norm_pair");
 }
 
-lt_status lt_ffn_tail(lt_ctx *ctx, const float *dev_f, float *dev_m, const float *dev_w2, const float *dev_w, float los,
-                      float eps, uint32_t n, uint32_t ntok, float *dev_x) {
+lt_status lt_ffn_tail(lt_ctx *ctx, const float *dev_f, const float *dev_w1, float *dev_m, const float *dev_w2,
+                      const float *dev_w, float los, float eps, uint32_t n, uint32_t ntok, float *dev_x) {
     lt_status st = enter(ctx);
     if (st != LT_OK) return st;
     if (!dev_f || !dev_m || !dev_w2 || !dev_w || !dev_x || n == 0) return fail(ctx, LT_EINVAL, "lt_ffn_tail: bad argument");
     if (ntok == 0) return LT_OK;
-    return launched(ctx, lt::launch_ffn_tail(cfg_of(ctx), dev_f, dev_m, dev_w2, dev_w, los, eps, n, ntok, dev_x),
+    return launched(ctx, lt::launch_ffn_tail(cfg_of(ctx), dev_f, dev_w1, dev_m, dev_w2, dev_w, los, eps, n, ntok, dev_x),
                     "ffn_tail");
 }
 

@@ -441,6 +441,9 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
         }
     }
     if (tid < 2 && a.pf[tid]) prefetch_l2_share(a.pf[tid], a.pf_bytes[tid], c, G);
+    // the third hand-off (post-norm only) counts every launch: without it, CTA 0
+    // adds the whole grid's arrivals at once, off the critical path
+    if (!a.post_norm && c == 0 && tid == 0) atomicAdd(ctr3, (unsigned long long)G);
     for (uint32_t i = tid; i < a.d; i += kAbThreads) nw[i] = __ldg(a.norm_w + i);
     pdl_launch_dependents();
     pdl_wait();
@@ -638,7 +641,6 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
         for (uint32_t i = tid; i < nor; i += kAbThreads)
             a.out[o0 + i] = __fadd_rn(xres[i], __fmul_rn(__fmul_rn(yo[i], r), __ldg(a.post_norm + o0 + i)));
     } else {
-        grid_arrive(ctr3);  // every launch counts on every counter: the epochs stay aligned
         for (uint32_t r = tid; r < nor; r += kAbThreads) a.out[o0 + r] = __fadd_rn(xres[r], yo[r]);
     }
 }

@@ -5,7 +5,7 @@
 //   scale       x *= s                          (embedding scale, layer_output_scale)
 //   add_rmsnorm x += rmsnorm(y) * w             (post_attention_norm + residual)
 //   norm_pair   a = rmsnorm(x) * w, b = x * rms_inv * g * s   (rmsnormWeightedAndRawScaled)
-//   ffn_tail    x = (x + rmsnorm(f + rmsnorm(m) * w2) * w) * los
+//   ffn_tail    x = (x + rmsnorm(f' + rmsnorm(m) * w2) * w) * los, f' = rmsnorm(f) * w1 or f
 //   softcap     x = tanh(x / cap) * cap
 //
 // The norms follow math.zig:20-26 (rms_inv = 1 / sqrt(sum(x^2) / n + eps)),
@@ -68,15 +68,18 @@ __global__ void __launch_bounds__(kGlueThreads) k_norm_pair(const float *x, cons
     }
 }
 
-__global__ void __launch_bounds__(kGlueThreads) k_ffn_tail(const float *f, float *m, const float *w2, const float *w,
-                                                           float los, float eps, uint32_t n, float *x) {
+__global__ void __launch_bounds__(kGlueThreads) k_ffn_tail(const float *f, const float *w1, float *m, const float *w2,
+                                                           const float *w, float los, float eps, uint32_t n, float *x) {
     __shared__ float red[kGlueThreads / 32];
     pdl_launch_dependents();
     pdl_wait();
     const size_t o = (size_t)blockIdx.x * n;
+    const float rf1 = w1 ? glue_rms_inv(f + o, n, eps, red) : 1.0f;
     const float rm = glue_rms_inv(m + o, n, eps, red);
-    for (uint32_t i = threadIdx.x; i < n; i += kGlueThreads)
-        m[o + i] = __fadd_rn(f[o + i], __fmul_rn(__fmul_rn(m[o + i], rm), w2[i]));
+    for (uint32_t i = threadIdx.x; i < n; i += kGlueThreads) {
+        const float fi = w1 ? __fmul_rn(__fmul_rn(f[o + i], rf1), w1[i]) : f[o + i];
+        m[o + i] = __fadd_rn(fi, __fmul_rn(__fmul_rn(m[o + i], rm), w2[i]));
+    }
     __syncthreads();
     const float rf = glue_rms_inv(m + o, n, eps, red);
     for (uint32_t i = threadIdx.x; i < n; i += kGlueThreads) {
@@ -104,9 +107,9 @@ cudaError_t launch_norm_pair(const LaunchCfg &c, const float *x, const float *w,
                              uint32_t n, uint32_t ntok, float *a, float *b) {
     return launch_k(c, "norm_pair", k_norm_pair, dim3(ntok), dim3(kGlueThreads), 0, x, w, g, gs, eps, n, a, b);
 }
-cudaError_t launch_ffn_tail(const LaunchCfg &c, const float *f, float *m, const float *w2, const float *w, float los,
-                            float eps, uint32_t n, uint32_t ntok, float *x) {
-    return launch_k(c, "ffn_tail", k_ffn_tail, dim3(ntok), dim3(kGlueThreads), 0, f, m, w2, w, los, eps, n, x);
+cudaError_t launch_ffn_tail(const LaunchCfg &c, const float *f, const float *w1, float *m, const float *w2,
+                            const float *w, float los, float eps, uint32_t n, uint32_t ntok, float *x) {
+    return launch_k(c, "ffn_tail", k_ffn_tail, dim3(ntok), dim3(kGlueThreads), 0, f, w1, m, w2, w, los, eps, n, x);
 }
 cudaError_t launch_softcap(const LaunchCfg &c, float *x, size_t n, float cap) {
     const size_t want = (n + 255) / 256;

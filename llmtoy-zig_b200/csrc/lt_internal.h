@@ -94,8 +94,8 @@ cudaError_t launch_add_rmsnorm(const LaunchCfg &c, const float *y, const float *
                                uint32_t ntok, float *x);
 cudaError_t launch_norm_pair(const LaunchCfg &c, const float *x, const float *w, const float *g, float gs, float eps,
                              uint32_t n, uint32_t ntok, float *a, float *b);
-cudaError_t launch_ffn_tail(const LaunchCfg &c, const float *f, float *m, const float *w2, const float *w, float los,
-                            float eps, uint32_t n, uint32_t ntok, float *x);
+cudaError_t launch_ffn_tail(const LaunchCfg &c, const float *f, const float *w1, float *m, const float *w2,
+                            const float *w, float los, float eps, uint32_t n, uint32_t ntok, float *x);
 cudaError_t launch_softcap(const LaunchCfg &c, float *x, size_t n, float cap);
 // out = dequantised row tokens[*pos] of m (embedLookup); rows >= m.rows set
 // DEV_ERR_BAD_INDEX and read row 0.

@@ -134,7 +134,9 @@ __host__ __device__ inline DecodeLayout decode_layout(uint32_t E, uint32_t d, ui
     return L;
 }
 
-template <uint32_t GT, uint32_t DT>
+// ROUNDS: the gate/up share is taken in rounds of a.gchunks chunks (only
+// instantiated for launches whose share exceeds the tile space).
+template <uint32_t GT, uint32_t DT, bool ROUNDS>
 __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -304,13 +306,13 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
             urow = grow + a.F;
             ub = a.gate;
         }
-        uint8_t *dst = gt + (size_t)2 * (j % a.gchunks) * kDecChunk * a.gpitch;
+        uint8_t *dst = gt + (size_t)2 * (ROUNDS ? j % a.gchunks : j) * kDecChunk * a.gpitch;
         mbar_arrive_expect_tx(&bars[j], 2 * bytes);
         tma_load_1d(dst, a.gate + grow * a.gpitch, bytes, &bars[j]);
         tma_load_1d(dst + bytes, ub + urow * a.gpitch, bytes, &bars[j]);
     };
     if (warp == 0) {  // one TMA chunk per lane: the first round's
-        for (uint32_t j = lane; j < min(nchunks, a.gchunks); j += 32) issue_chunk(j);
+        for (uint32_t j = lane; j < (ROUNDS ? min(nchunks, a.gchunks) : nchunks); j += 32) issue_chunk(j);
     } else if (warp == 1) {  // down rows [r0, r1) of each slot's expert
         if (!a.late_down && (uint32_t)lane < a.k && nr) {
             const uint32_t e = min(s_sel[lane], a.E - 1);
@@ -336,17 +338,10 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     // in rounds of gchunks chunks, each copied over the previous round's.
     const uint32_t cpr_g = chunks64(a.d);
     const uint32_t gstride = 2 * a.maxpairs + 1;  // partials [chunk][tile row], odd stride: no bank conflicts
-    const uint32_t rows_round = 2 * kDecChunk * a.gchunks;
-    for (uint32_t rbase = 0; rbase < 2 * np; rbase += rows_round) {
-        if (rbase) {  // the previous round's rows are consumed
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncthreads();
-            if (tid == 0)
-                for (uint32_t j = rbase / (2 * kDecChunk); j < min(nchunks, (rbase + rows_round) / (2 * kDecChunk)); j++)
-                    issue_chunk(j);
-        }
+    // tile rows [rbase, nrows) of the share, held from tile row 0
+    auto gate_up_rows = [&](uint32_t rbase, uint32_t nrows) {
         const uint32_t lpr = min(cpr_g, 32u), rps = 32 / lpr;  // lanes per row, rows per step
-        const uint32_t sub = lane / lpr, nrows = min(2 * np, rbase + rows_round);
+        const uint32_t sub = lane / lpr;
         if (sub < rps) {
             for (uint32_t cg = 0; cg < cpr_g; cg += lpr) {
                 const uint32_t n = min(lpr, cpr_g - cg);
@@ -371,6 +366,22 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
                 }
             }
         }
+    };
+    if constexpr (ROUNDS) {
+        const uint32_t rows_round = 2 * kDecChunk * a.gchunks;
+        for (uint32_t rbase = 0; rbase < 2 * np; rbase += rows_round) {
+            if (rbase) {  // the previous round's rows are consumed
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncthreads();
+                if (tid == 0)
+                    for (uint32_t j = rbase / (2 * kDecChunk); j < min(nchunks, (rbase + rows_round) / (2 * kDecChunk));
+                         j++)
+                        issue_chunk(j);
+            }
+            gate_up_rows(rbase, min(2 * np, rbase + rows_round));
+        }
+    } else {
+        gate_up_rows(0, 2 * np);
     }
     __syncthreads();
     for (uint32_t lp = tid; lp < np; lp += kDecThreads) {  // chunk partials summed in column order
@@ -539,7 +550,11 @@ bool decode_plan(const DecodeParams &p, int num_sms, DecodePlan &out) {
 
 template <uint32_t GT, uint32_t DT>
 cudaError_t launch_decode_t(const LaunchCfg &c, const DecodePlan &pl) {
-    return launch_k(c, "moe_decode", k_moe_decode<GT, DT>, dim3((unsigned)c.num_sms), dim3(kDecThreads), pl.smem, pl.a);
+    if (pl.a.gchunks * kDecChunk < pl.a.maxpairs)
+        return launch_k(c, "moe_decode", k_moe_decode<GT, DT, true>, dim3((unsigned)c.num_sms), dim3(kDecThreads),
+                        pl.smem, pl.a);
+    return launch_k(c, "moe_decode", k_moe_decode<GT, DT, false>, dim3((unsigned)c.num_sms), dim3(kDecThreads),
+                    pl.smem, pl.a);
 }
 
 template <uint32_t GT>

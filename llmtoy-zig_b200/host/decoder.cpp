@@ -101,16 +101,15 @@ lt_status gemma_layer(lth_decoder *d, uint32_t l) {
     // wo and the post-attention norm into the residual (:329-333) in one launch
     LTH_TRY(lt_attn_block_split(c, &a, d->x, L.attn_norm, m.eps, L.wq, L.wk, L.wv, nullptr, L.q_norm, L.k_norm, pos,
                                 kc, vc, L.wo, L.post_attention_norm, d->x));
-    // dense GeGLU FFN, post_ffw_norm_1 (:390-396)
+    // dense GeGLU FFN (:390-396; its post_ffw_norm_1 is applied in the tail)
     LTH_TRY(lt_ffn_block(c, L.ffn_gate, L.ffn_up, L.ffn_down, LT_ACT_GELU_TANH, L.ffn_norm, m.eps, d->x, 1, 0,
                          d->fbuf));
-    LTH_TRY(lt_rmsnorm(c, d->fbuf, L.post_ffw_norm_1, m.eps, m.d_model, 1, d->fbuf));
     // MoE: weighted and raw-scaled norms of x, router, experts (:401-494) in one launch
     LTH_TRY(lt_moe_block_scaled(c, L.router, L.exp_gate, L.exp_up, L.exp_down, LT_ACT_GELU_TANH, 0, L.down_exps_scale,
                                 L.pre_ffw_norm_2, L.router_scale, 1.0f / __builtin_sqrtf((float)m.d_model), m.eps,
                                 d->x, 1, m.n_used, 0, d->mbuf, d->ids, d->wts));
-    return lt_ffn_tail(c, d->fbuf, d->mbuf, L.post_ffw_norm_2, L.post_ffw_norm, L.layer_output_scale, m.eps,
-                       m.d_model, 1, d->x);
+    return lt_ffn_tail(c, d->fbuf, L.post_ffw_norm_1, d->mbuf, L.post_ffw_norm_2, L.post_ffw_norm,
+                       L.layer_output_scale, m.eps, m.d_model, 1, d->x);
 }
 
 lt_status step(lth_decoder *d) {
