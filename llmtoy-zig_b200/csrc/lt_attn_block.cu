@@ -382,7 +382,9 @@ LT_DEVINL void ab_attend(const AttnBlockArgs &a, uint32_t s, uint32_t S, uint32_
     }
 }
 
-template <uint32_t QT, uint32_t OT, int HD>
+// GEN: segments, V = K, the post-attention norm or the late wo tile may occur
+// (otherwise: one stacked Q/K/V tensor, plain residual, both tiles at once).
+template <uint32_t QT, uint32_t OT, int HD, bool GEN>
 __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int PER = HD / 32;
@@ -418,7 +420,10 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
         fence_barrier_init();
-        if (nqr) {  // this CTA's rows of each segment, one after another
+        if (nqr && !GEN) {
+            mbar_arrive_expect_tx(&bars[0], (uint32_t)(nqr * a.seg_pitch[0]));
+            tma_load_1d(wq, a.seg_w[0] + (uint64_t)q0 * a.seg_pitch[0], (uint32_t)(nqr * a.seg_pitch[0]), &bars[0]);
+        } else if (nqr) {  // this CTA's rows of each segment, one after another
             uint32_t total = 0;
             for (uint32_t sg = 0; sg < a.nseg; sg++) {
                 const uint32_t sb = sg ? a.seg_end[sg - 1] : 0, lo = max(q0, sb), hi = min(q1, a.seg_end[sg]);
@@ -435,7 +440,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
                 }
             }
         }
-        if (nor && !a.late_wo) {
+        if (nor && (!GEN || !a.late_wo)) {
             mbar_arrive_expect_tx(&bars[1], (uint32_t)(nor * a.opitch));
             tma_load_1d(wo, a.wo + (uint64_t)o0 * a.opitch, (uint32_t)(nor * a.opitch), &bars[1]);
         }
@@ -466,7 +471,9 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     __syncthreads();
     const uint64_t epoch = *s_epoch;
     float *yq = xf;  // the normalised x is quantised already
-    if (nqr && tile_wait(&bars[0], a.dev_err)) {
+    if constexpr (!GEN) {
+        if (nqr && tile_wait(&bars[0], a.dev_err)) ab_rows<QT>(wq, a.seg_pitch[0], nqr, a.d, a.qnb, Xx, warp, lane, yq);
+    } else if (nqr && tile_wait(&bars[0], a.dev_err)) {
         uint32_t off = 0;
         for (uint32_t sg = 0; sg < a.nseg; sg++) {
             const uint32_t sb = sg ? a.seg_end[sg - 1] : 0, lo = max(q0, sb), hi = min(q1, a.seg_end[sg]);
@@ -484,7 +491,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     grid_wait(ctr1, epoch, a.dev_err, kWaitLimitNs);
 
     // ── phase A ──────────────────────────────────────────────────────────────
-    if (a.late_wo) {  // the Q/K/V rows are consumed: the wo rows take their place
+    if (GEN && a.late_wo) {  // the Q/K/V rows are consumed: the wo rows take their place
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();
         if (tid == 0 && nor) {
@@ -503,7 +510,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
             const uint32_t part = tid / (HD / 4), i = tid % (HD / 4);
             const size_t off = part == 0   ? (size_t)h * HD
                                : part == 1 ? nq + (size_t)kh * HD
-                                           : (a.v_is_k ? nq : nq + nkv) + (size_t)kh * HD;
+                                           : (GEN && a.v_is_k ? nq : nq + nkv) + (size_t)kh * HD;
             reinterpret_cast<float4 *>(hq + part * HD)[i] = __ldcg(reinterpret_cast<const float4 *>(a.qkv + off) + i);
         }
         __syncthreads();
@@ -627,7 +634,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     float *yo = xf;  // the attention vector is quantised already
     if (nor && tile_wait(&bars[1], a.dev_err)) ab_rows_any<OT>(a.otype, wo, a.opitch, nor, nq, a.onb, Xa, warp, lane, yo);
     __syncthreads();
-    if (a.post_norm) {  // x + rmsnorm(y) * w over all d outputs: partial sums, a third hand-off
+    if (GEN && a.post_norm) {  // x + rmsnorm(y) * w over all d outputs: partial sums, a third hand-off
         float ss = 0.0f;
         for (uint32_t r = tid; r < nor; r += kAbThreads) ss = __fadd_rn(ss, __fmul_rn(yo[r], yo[r]));
         ss = ab_block_sum(ss, red);
@@ -709,13 +716,26 @@ bool attn_block_plan(const AttnBlockParams &p, int num_sms, size_t *scratch_floa
     return true;
 }
 
+template <uint32_t QT, uint32_t OT, bool GEN>
+static cudaError_t launch_ab_g(const LaunchCfg &c, const AttnBlockArgs &a, size_t smem) {
+    switch (a.g.hd) {
+    case 64:
+        return launch_k(c, "attn_block", k_attn_block<QT, OT, 64, GEN>, dim3(c.num_sms), dim3(kAbThreads), smem, a);
+    case 128:
+        return launch_k(c, "attn_block", k_attn_block<QT, OT, 128, GEN>, dim3(c.num_sms), dim3(kAbThreads), smem, a);
+    case 256:
+        return launch_k(c, "attn_block", k_attn_block<QT, OT, 256, GEN>, dim3(c.num_sms), dim3(kAbThreads), smem, a);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
 template <uint32_t QT, uint32_t OT>
 static cudaError_t launch_ab_t(const LaunchCfg &c, const AttnBlockArgs &a, size_t smem) {
-    switch (a.g.hd) {
-    case 64: return launch_k(c, "attn_block", k_attn_block<QT, OT, 64>, dim3(c.num_sms), dim3(kAbThreads), smem, a);
-    case 128: return launch_k(c, "attn_block", k_attn_block<QT, OT, 128>, dim3(c.num_sms), dim3(kAbThreads), smem, a);
-    case 256: return launch_k(c, "attn_block", k_attn_block<QT, OT, 256>, dim3(c.num_sms), dim3(kAbThreads), smem, a);
-    default: return cudaErrorInvalidValue;
+    if constexpr (QT == 0) {
+        return launch_ab_g<QT, OT, true>(c, a, smem);
+    } else {
+        if (a.nseg > 1 || a.v_is_k || a.post_norm || a.late_wo) return launch_ab_g<QT, OT, true>(c, a, smem);
+        return launch_ab_g<QT, OT, false>(c, a, smem);
     }
 }
 
