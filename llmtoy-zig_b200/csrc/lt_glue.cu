@@ -68,8 +68,78 @@ __global__ void __launch_bounds__(kGlueThreads) k_norm_pair(const float *x, cons
     }
 }
 
+LT_DEVINL float glue_rinv(float ss, uint32_t n, float eps) {
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+}
+
+// Rows of up to kGlueThreads * kTailPer values: each thread keeps its values
+// (i = tid + k * kGlueThreads) in registers, so the three norms take two block
+// reductions and no global round trip; sums in glue_rms_inv's order.
+constexpr int kTailPer = 16;
+
 __global__ void __launch_bounds__(kGlueThreads) k_ffn_tail(const float *f, const float *w1, float *m, const float *w2,
                                                            const float *w, float los, float eps, uint32_t n, float *x) {
+    __shared__ float red[kGlueThreads / 32], red2[kGlueThreads / 32];
+    pdl_launch_dependents();
+    pdl_wait();
+    const size_t o = (size_t)blockIdx.x * n;
+    float fv[kTailPer], mv[kTailPer];
+    float sf = 0.0f, sm = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kTailPer; k++) {
+        const uint32_t i = threadIdx.x + k * kGlueThreads;
+        fv[k] = i < n ? f[o + i] : 0.0f;
+        mv[k] = i < n ? m[o + i] : 0.0f;
+        if (i < n) {
+            sf = __fadd_rn(sf, __fmul_rn(fv[k], fv[k]));
+            sm = __fadd_rn(sm, __fmul_rn(mv[k], mv[k]));
+        }
+    }
+    {  // both sums in one reduction (glue_sum's order for each)
+        sf = warp_sum(sf);
+        sm = warp_sum(sm);
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        if (lane == 0) {
+            red[warp] = sf;
+            red2[warp] = sm;
+        }
+        __syncthreads();
+        sf = 0.0f;
+        sm = 0.0f;
+#pragma unroll
+        for (int q = 0; q < kGlueThreads / 32; q++) {
+            sf += red[q];
+            sm += red2[q];
+        }
+    }
+    const float rf1 = w1 ? glue_rinv(sf, n, eps) : 1.0f, rm = glue_rinv(sm, n, eps);
+    float sh = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kTailPer; k++) {
+        const uint32_t i = threadIdx.x + k * kGlueThreads;
+        if (i < n) {
+            const float fi = w1 ? __fmul_rn(__fmul_rn(fv[k], rf1), w1[i]) : fv[k];
+            mv[k] = __fadd_rn(fi, __fmul_rn(__fmul_rn(mv[k], rm), w2[i]));
+            m[o + i] = mv[k];
+            sh = __fadd_rn(sh, __fmul_rn(mv[k], mv[k]));
+        }
+    }
+    const float rf = glue_rinv(glue_sum(sh, red), n, eps);
+#pragma unroll
+    for (int k = 0; k < kTailPer; k++) {
+        const uint32_t i = threadIdx.x + k * kGlueThreads;
+        if (i < n) {
+            float v = __fadd_rn(x[o + i], __fmul_rn(__fmul_rn(mv[k], rf), w[i]));
+            if (los != 1.0f) v = __fmul_rn(v, los);
+            x[o + i] = v;
+        }
+    }
+}
+
+// Longer rows: the same arithmetic through global memory.
+__global__ void __launch_bounds__(kGlueThreads) k_ffn_tail_long(const float *f, const float *w1, float *m,
+                                                                const float *w2, const float *w, float los, float eps,
+                                                                uint32_t n, float *x) {
     __shared__ float red[kGlueThreads / 32];
     pdl_launch_dependents();
     pdl_wait();
@@ -109,6 +179,9 @@ cudaError_t launch_norm_pair(const LaunchCfg &c, const float *x, const float *w,
 }
 cudaError_t launch_ffn_tail(const LaunchCfg &c, const float *f, const float *w1, float *m, const float *w2,
                             const float *w, float los, float eps, uint32_t n, uint32_t ntok, float *x) {
+    if (n > (uint32_t)(kGlueThreads * kTailPer))
+        return launch_k(c, "ffn_tail", k_ffn_tail_long, dim3(ntok), dim3(kGlueThreads), 0, f, w1, m, w2, w, los, eps, n,
+                        x);
     return launch_k(c, "ffn_tail", k_ffn_tail, dim3(ntok), dim3(kGlueThreads), 0, f, w1, m, w2, w, los, eps, n, x);
 }
 cudaError_t launch_softcap(const LaunchCfg &c, float *x, size_t n, float cap) {
