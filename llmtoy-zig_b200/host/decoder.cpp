@@ -31,7 +31,10 @@ struct lth_decoder {
     uint32_t *ids_zero = nullptr;  // {0}: row index of a one-row gather
     uint32_t *tokens = nullptr;  // [kv_cap + 1]
     uint32_t *state = nullptr;   // {pos, n_prompt}
-    lt_graph *graph = nullptr;
+    lt_graph *graph = nullptr;   // the full step
+    lt_graph *pgraph = nullptr;  // a prompt step: no logits
+    float *one = nullptr;        // a one-element logits row for the prompt step's position advance
+    uint32_t host_pos = 0, n_prompt = 0;  // the host's copy of the position (steps enqueued)
     bool warmed = false;
     lt_sample_params sampling{0.0f, 0, 1.0f};  // temperature 0: greedy
     uint64_t *rng = nullptr;                   // xoshiro256++ state (device)
@@ -112,7 +115,7 @@ lt_status gemma_layer(lth_decoder *d, uint32_t l) {
                        L.layer_output_scale, m.eps, m.d_model, 1, d->x);
 }
 
-lt_status step(lth_decoder *d) {
+lt_status step(lth_decoder *d, bool logits) {
     const lth_model &m = d->m;
     LTH_TRY(lt_embed(d->ctx, m.token_emb, d->tokens, d->state, d->x));
     if (m.family == LTH_GEMMA4) {
@@ -121,6 +124,8 @@ lt_status step(lth_decoder *d) {
     } else {
         for (uint32_t l = 0; l < m.n_layers; l++) LTH_TRY(layer_step(d, l));
     }
+    // a prompt position before the last: no logits, the position advances (tokens[pos+1] is a prompt id)
+    if (!logits) return lt_greedy_step(d->ctx, d->one, 1, d->tokens, d->state, d->state + 1);
     LTH_TRY(lt_rmsnorm(d->ctx, d->x, m.out_norm, m.eps, m.d_model, 1, d->xb));
     LTH_TRY(lt_qmatvec(d->ctx, m.lm_head, 0, d->xb, d->logits, 1));
     if (m.family == LTH_GEMMA4 && m.logit_softcap != 0.0f)
@@ -132,9 +137,10 @@ lt_status step(lth_decoder *d) {
 
 void release(lth_decoder *d) {
     if (d->graph) lt_graph_free(d->ctx, d->graph);
+    if (d->pgraph) lt_graph_free(d->ctx, d->pgraph);
     void *bufs[] = {d->x,    d->xb,     d->logits,    d->kcache, d->vcache,
                     d->fbuf,   d->mbuf,      d->moe_in,    d->router_in, d->ids,    d->wts,
-                    d->ids_zero, d->tokens, d->state, d->rng};
+                    d->ids_zero, d->tokens, d->state, d->rng, d->one};
     for (void *b : bufs)
         if (b) lt_device_free(d->ctx, b);
 }
@@ -186,7 +192,7 @@ lt_status lth_decoder_create(lt_ctx *ctx, const lth_model *m, lth_decoder **out)
         (st = alloc(d, &d->logits, m->vocab)) != LT_OK || (st = alloc(d, &d->kcache, cache * d->kv_esize)) != LT_OK ||
         (st = alloc(d, &d->vcache, cache * d->kv_esize)) != LT_OK || (st = alloc(d, &d->tokens, (size_t)m->kv_cap + 1)) != LT_OK ||
         (st = alloc(d, &d->state, 2)) != LT_OK || (st = alloc(d, &d->ids_zero, 4)) != LT_OK ||
-        (st = alloc(d, &d->rng, 4)) != LT_OK ||
+        (st = alloc(d, &d->rng, 4)) != LT_OK || (st = alloc(d, &d->one, 1)) != LT_OK ||
         (m->family == LTH_GEMMA4 &&
          ((st = alloc(d, &d->fbuf, dm)) != LT_OK ||
           (st = alloc(d, &d->mbuf, dm)) != LT_OK || (st = alloc(d, &d->moe_in, dm)) != LT_OK ||
@@ -209,15 +215,20 @@ void lth_decoder_free(lth_decoder *d) {
 lt_status lth_decoder_start(lth_decoder *d, const uint32_t *prompt, uint32_t n_prompt) {
     if (!d || !prompt || n_prompt == 0 || n_prompt > d->m.kv_cap) return LT_EINVAL;
     const uint32_t state[2] = {0, n_prompt};
+    const float zero = 0.0f;
     LTH_TRY(lt_copy_to_device(d->ctx, d->tokens, prompt, (size_t)n_prompt * 4));
     LTH_TRY(lt_copy_to_device(d->ctx, d->state, state, sizeof state));
+    LTH_TRY(lt_copy_to_device(d->ctx, d->one, &zero, sizeof zero));
+    d->host_pos = 0;
+    d->n_prompt = n_prompt;
     return lt_sync(d->ctx);  // the host arrays may go away after this call
 }
 
 lt_status lth_decoder_step(lth_decoder *d) {
     if (!d) return LT_EINVAL;
-    LTH_TRY(step(d));
+    LTH_TRY(step(d, true));
     d->warmed = true;
+    d->host_pos++;
     return LT_OK;
 }
 
@@ -225,23 +236,28 @@ lt_status lth_decoder_capture(lth_decoder *d) {
     if (!d) return LT_EINVAL;
     if (d->graph) return LT_OK;
     if (!d->warmed) return LT_EINVAL;  // an eager step first sizes the scratch buffers
-    LTH_TRY(lt_capture_begin(d->ctx));
-    lt_status st = step(d);
-    lt_graph *g = nullptr;
-    lt_status st2 = lt_capture_end(d->ctx, &g);
-    if (st != LT_OK) {
-        if (g) lt_graph_free(d->ctx, g);
-        return st;
+    for (int full = 1; full >= 0; full--) {
+        LTH_TRY(lt_capture_begin(d->ctx));
+        lt_status st = step(d, full != 0);
+        lt_graph *g = nullptr;
+        lt_status st2 = lt_capture_end(d->ctx, &g);
+        if (st != LT_OK || st2 != LT_OK) {
+            if (g) lt_graph_free(d->ctx, g);
+            if (d->pgraph) lt_graph_free(d->ctx, d->pgraph);
+            if (d->graph) lt_graph_free(d->ctx, d->graph);
+            d->graph = d->pgraph = nullptr;
+            return st != LT_OK ? st : st2;
+        }
+        (full ? d->graph : d->pgraph) = g;
     }
-    if (st2 != LT_OK) return st2;
-    d->graph = g;
     return LT_OK;
 }
 
 lt_status lth_decoder_replay(lth_decoder *d, uint32_t n_steps) {
     if (!d) return LT_EINVAL;
-    if (!d->graph) return LT_EINVAL;
-    for (uint32_t i = 0; i < n_steps; i++) LTH_TRY(lt_graph_launch(d->ctx, d->graph));
+    if (!d->graph || !d->pgraph) return LT_EINVAL;
+    for (uint32_t i = 0; i < n_steps; i++, d->host_pos++)
+        LTH_TRY(lt_graph_launch(d->ctx, d->host_pos + 1 < d->n_prompt ? d->pgraph : d->graph));
     return LT_OK;
 }
 
@@ -259,6 +275,10 @@ lt_status lth_decoder_set_sampling(lth_decoder *d, float temperature, uint32_t t
     if (d->graph) {  // the step's last op changed
         lt_graph_free(d->ctx, d->graph);
         d->graph = nullptr;
+    }
+    if (d->pgraph) {
+        lt_graph_free(d->ctx, d->pgraph);
+        d->pgraph = nullptr;
     }
     return LT_OK;
 }

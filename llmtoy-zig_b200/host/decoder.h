@@ -74,11 +74,15 @@ void lth_decoder_free(lth_decoder *d);
 /* Start a sequence: prompt into the device token stream, position 0. */
 lt_status lth_decoder_start(lth_decoder *d, const uint32_t *prompt, uint32_t n_prompt);
 /* Enqueue one step with eager launches (the first call also sizes every
- * scratch buffer, so a capture afterwards allocates nothing). */
+ * scratch buffer, so a capture afterwards allocates nothing).  Every eager
+ * step computes the logits, prompt positions included. */
 lt_status lth_decoder_step(lth_decoder *d);
-/* Capture one step as a graph (done on first use by lth_decoder_replay). */
+/* Capture the step as graphs (done on first use by lth_generate): the full
+ * step, and the prompt step without the output norm, lm_head and sampling
+ * (main.zig:1916-1919 asks for logits only at the last prompt position). */
 lt_status lth_decoder_capture(lth_decoder *d);
-/* Replay the captured step n_steps times (asynchronous). */
+/* Replay n_steps steps (asynchronous): the prompt graph while the next
+ * position is still a prompt position, the full step after. */
 lt_status lth_decoder_replay(lth_decoder *d, uint32_t n_steps);
 /* Device address of the last step's logits [vocab]. */
 const float *lth_decoder_logits(const lth_decoder *d);
