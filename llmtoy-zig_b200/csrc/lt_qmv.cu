@@ -8,6 +8,7 @@
 // token as f32, which every CTA quantises into shared memory itself (one
 // launch and one global round trip fewer than a separate quantiser).
 #include "lt_qact.cuh"
+#include "lt_rowdot.cuh"
 
 namespace lt {
 
@@ -181,6 +182,8 @@ struct QsArgs {
     uint32_t warps;   // warps that stream rows (the rest help stage the activations)
 };
 
+__host__ __device__ inline uint32_t qs_chunks(uint64_t cols) { return (uint32_t)((cols + 63) / 64); }
+
 __host__ __device__ inline size_t qs_ring_offset(int ipr) { return kQsX + ((xs_bytes(1, ipr) + 127) & ~(size_t)127); }
 
 template <uint32_t TYPE>
@@ -257,6 +260,96 @@ __global__ void __launch_bounds__(kQsWarps * 32, 1) k_qmv_stream(QsArgs q) {
     }
 }
 
+// Q8_0: the same streaming with lanes on 64-column chunks of the
+// activation held in registers (lt_rowdot.cuh): a lane walks the group's rows
+// reading only its chunk's weight bytes, chunk partials are summed per row in
+// column order.  Groups of rw rows; part: [rw][cpr] floats per warp after X.
+template <uint32_t TYPE>
+__global__ void __launch_bounds__(kQsWarps * 32, 1) k_qmv_stream64(QsArgs q) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const QmvArgs &a = q.a;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t cpr = qs_chunks(a.cols);
+    const size_t part_w = ((size_t)a.rw * cpr * 4 + 127) & ~(size_t)127;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kQsBars) + warp * kQsMaxStages;
+    const XS X = xs_carve(smem + kQsX, 1, (int)a.nitems);
+    float *part = reinterpret_cast<float *>(smem + qs_ring_offset((int)a.nitems) + (size_t)warp * part_w);
+    uint8_t *ring = smem + qs_ring_offset((int)a.nitems) + kQsWarps * part_w + (size_t)warp * q.stages * q.stage;
+    const uint32_t W = gridDim.x * q.warps, gw = blockIdx.x * q.warps + warp;
+    const uint32_t ngroups = (a.nrows + a.rw - 1) / a.rw;
+    const uint32_t mine = (uint32_t)warp < q.warps && gw < ngroups ? (ngroups - gw + W - 1) / W : 0;
+    auto issue = [&](uint32_t i) {
+        const uint32_t r0 = (gw + i * W) * a.rw, nr = min(a.rw, a.nrows - r0), st = i % q.stages;
+        mbar_arrive_expect_tx(&bars[st], (uint32_t)(nr * a.pitch));
+        tma_load_1d(ring + (size_t)st * q.stage, a.rows + (uint64_t)r0 * a.pitch, (uint32_t)(nr * a.pitch), &bars[st]);
+    };
+    if (lane == 0) {
+        for (uint32_t st = 0; st < q.stages; st++) mbar_init(&bars[st], 1);
+        fence_barrier_init();
+        for (uint32_t i = 0; i < min(mine, q.stages); i++) issue(i);
+    }
+    __syncwarp();
+    pdl_launch_dependents();
+    pdl_wait();
+    if (a.xq) {
+        const uint8_t **src = reinterpret_cast<const uint8_t **>(smem + kQsSrc);
+        if (threadIdx.x == 0) src[0] = a.xq;
+        __syncthreads();
+        qact_to_smem(X, src, 1, (int)a.cols);
+    } else {
+        for (uint32_t b = warp; b < a.cols / 32; b += kQsWarps)
+            qact_block_to_xs(X, 0, (int)b, __ldcg(a.xf + 32 * b + lane), lane);
+    }
+    __syncthreads();
+    const bool one_pass = cpr <= 32;
+    XChunk xc;
+    if (one_pass && (uint32_t)lane < (32 / cpr) * cpr)
+        xchunk_load(X, 0, (int)spread_chunk(lane % cpr, cpr), xc);
+    uint32_t i = 0;
+    bool ok = true;
+    for (; i < mine; i++) {
+        const uint32_t st = i % q.stages;
+        if (!mbar_wait_bounded(&bars[st], (i / q.stages) & 1, kWaitLimitNs)) {
+            ok = false;
+            break;
+        }
+        const uint32_t r0 = (gw + i * W) * a.rw, nr = min(a.rw, a.nrows - r0);
+        const uint8_t *t = ring + (size_t)st * q.stage;
+        for (uint32_t cg = 0; cg < cpr; cg += 32) {  // lanes: n chunks of rps rows at a time
+            const uint32_t n = min(32u, cpr - cg), rps = 32 / n, sub = lane / n;
+            if (sub < rps) {
+                const uint32_t cb = cg + spread_chunk(lane % n, n);
+                if (!one_pass) xchunk_load(X, 0, (int)cb, xc);
+                for (uint32_t r = sub; r < nr; r += rps)
+                    part[r * cpr + cb] = dot64<TYPE>(t + (size_t)r * a.pitch, (int)cb, (int)a.nblocks, xc);
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && i + q.stages < mine) {  // the stage is read: the group after next takes it
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(i + q.stages);
+        }
+        if ((uint32_t)lane < nr) {
+            const float *pp = part + lane * cpr;
+            float sum = 0.0f;
+            for (uint32_t k = 0; k < cpr; k++) sum += pp[k];
+            const size_t yi = r0 + lane;
+            a.y[yi] = a.add ? __fadd_rn(a.add[yi], sum) : sum;
+        }
+        __syncwarp();
+    }
+    if (!ok && lane == 0) {
+        if (a.dev_err) atomicExch(a.dev_err, DEV_ERR_TMA_TIMEOUT);
+        for (uint32_t j = i; j < min(mine, i + q.stages); j++)
+            mbar_wait_bounded(&bars[j % q.stages], (j / q.stages) & 1, kWaitLimitNs);
+    }
+}
+
+// Measured on the lm_heads: Q8_0 rows (d 896) run faster with register-held
+// chunks (33 vs 37 us for 145 MB); Q6_K rows (d 2048, 2816) slower (86 vs 80,
+// 265 vs 222 us), so the K types keep one item per lane.
+static bool qs64_type(uint32_t t) { return t == T_Q8_0; }
+
 // The ring layout for a one-token matvec over m, or false when the persistent
 // kernel does not pay (few rows) or two stages per warp do not fit.
 static bool qs_plan(const DevMat &m, uint32_t rw, uint32_t ipr, int num_sms, uint32_t &stages, uint32_t &stage,
@@ -264,7 +357,8 @@ static bool qs_plan(const DevMat &m, uint32_t rw, uint32_t ipr, int num_sms, uin
     if (!is_quant_type(m.type) || num_sms <= 0 || ipr > 32) return false;  // a group's items: one per lane
     if (m.rows * m.pitch < ((uint64_t)32 << 20) || qmv_ctas(m) <= 4u * (uint32_t)num_sms) return false;
     stage = (uint32_t)((rw * m.pitch + 127) & ~(uint64_t)127);
-    const size_t fixed = qs_ring_offset((int)ipr) + 256;  // + slack: a Q8_0 chunk reads past its row
+    size_t fixed = qs_ring_offset((int)ipr) + 256;  // + slack: a Q8_0 chunk reads past its row
+    if (qs64_type(m.type)) fixed += kQsWarps * (((size_t)rw * qs_chunks((uint32_t)m.cols) * 4 + 127) & ~(size_t)127);
     for (warps = kQsWarps; warps >= 8; warps -= 4) {  // at least two stages per warp
         if (fixed + (size_t)2 * warps * stage > kDecodeSmemLimit) continue;
         stages = (uint32_t)min((size_t)kQsMaxStages, (kDecodeSmemLimit - fixed) / ((size_t)warps * stage));
@@ -274,9 +368,17 @@ static bool qs_plan(const DevMat &m, uint32_t rw, uint32_t ipr, int num_sms, uin
     return false;
 }
 
+// Rows per group: one item per lane (k_qmv_stream), or about 6 KB of rows
+// (k_qmv_stream64, at most 8).
+static uint32_t qs_rows(const DevMat &m, uint32_t ipr) {
+    if (!qs64_type(m.type)) return max(1u, 32u / ipr);
+    const uint64_t r = 6144 / m.pitch;
+    return r < 1 ? 1u : r > 8 ? 8u : (uint32_t)r;
+}
+
 bool qmv_streams(const DevMat &m, uint32_t ntok, int num_sms) {
     if (ntok != 1 || !is_quant_type(m.type)) return false;
-    const uint32_t ipr = items_per_row(m.type, m.cols), rw = max(1u, 32u / ipr);
+    const uint32_t ipr = items_per_row(m.type, m.cols), rw = qs_rows(m, ipr);
     uint32_t stages, stage, warps;
     size_t smem;
     return qs_plan(m, rw, ipr, num_sms, stages, stage, warps, smem);
@@ -284,12 +386,17 @@ bool qmv_streams(const DevMat &m, uint32_t ntok, int num_sms) {
 
 template <uint32_t TYPE>
 static cudaError_t launch_qs_t(const LaunchCfg &c, const QsArgs &q, size_t smem) {
-    return launch_k(c, type_label<TYPE>("qmv_stream"), k_qmv_stream<TYPE>, dim3((unsigned)c.num_sms),
-                    dim3(kQsWarps * 32), smem, q);
+    if constexpr (TYPE == T_Q8_0)
+        return launch_k(c, type_label<TYPE>("qmv_stream"), k_qmv_stream64<TYPE>, dim3((unsigned)c.num_sms),
+                        dim3(kQsWarps * 32), smem, q);
+    else
+        return launch_k(c, type_label<TYPE>("qmv_stream"), k_qmv_stream<TYPE>, dim3((unsigned)c.num_sms),
+                        dim3(kQsWarps * 32), smem, q);
 }
 
-static cudaError_t launch_qmv_stream(const LaunchCfg &c, const DevMat &m, const QmvArgs &a) {
+static cudaError_t launch_qmv_stream(const LaunchCfg &c, const DevMat &m, QmvArgs a) {
     QsArgs q;
+    a.rw = qs_rows(m, a.nitems);
     q.a = a;
     size_t smem;
     if (!qs_plan(m, a.rw, a.nitems, c.num_sms, q.stages, q.stage, q.warps, smem)) return cudaErrorInvalidValue;
