@@ -375,16 +375,28 @@ lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x,
                         const float *dev_q_norm, const float *dev_k_norm, const uint32_t *dev_pos,
                         void *dev_k_cache, void *dev_v_cache, const lt_tensor *wo, float *dev_out);
 
+/* The end of a Gemma 4 layer (lt_ffn_tail's inputs, gemma4/forward.zig:520-532):
+ * x' = (x + rmsnorm(f' + rmsnorm(m) * w2) * w) * los, f' = rmsnorm(f) * w1
+ * (w1 nullable: f' = f); rmsnorm with eps.  m is only read. */
+typedef struct lt_ffn_tail_in {
+    const float *dev_f, *dev_w1, *dev_m, *dev_w2, *dev_w;
+    float los, eps;
+} lt_ffn_tail_in;
+
 /* lt_attn_block over separate Q, K and V tensors ([nq][d], [nkv][d], [nkv][d];
  * the types may differ).  wv NULL: V is the K projection before the norms
  * (gemma4/forward.zig:250), and dev_qkv_bias (nullable) then holds nq + nkv
  * entries.  dev_post_norm non-NULL: out = x + rmsnorm(wo . att) * post_norm
- * (gemma4/forward.zig:329-333) instead of x + wo . att. */
+ * (gemma4/forward.zig:329-333) instead of x + wo . att.  tail non-NULL: the
+ * block's input is the previous layer's tail of dev_x (x' above) instead of
+ * dev_x itself, in the same launch; dev_x is not written (unless it is
+ * dev_out). */
 lt_status lt_attn_block_split(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x, const float *dev_norm_w,
                               float eps, const lt_tensor *wq, const lt_tensor *wk, const lt_tensor *wv,
                               const float *dev_qkv_bias, const float *dev_q_norm, const float *dev_k_norm,
                               const uint32_t *dev_pos, void *dev_k_cache, void *dev_v_cache,
-                              const lt_tensor *wo, const float *dev_post_norm, float *dev_out);
+                              const lt_tensor *wo, const float *dev_post_norm, const lt_ffn_tail_in *tail,
+                              float *dev_out);
 
 /* L2 prefetch hint: the next lt_attn_block, or single-token lt_moe_block /
  * lt_moe_forward, launched on this context starts by prefetching these

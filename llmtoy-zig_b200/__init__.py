@@ -65,6 +65,12 @@ class AttnCfg(ctypes.Structure):
                 ("v_norm", ctypes.c_uint32), ("kv_f16", ctypes.c_uint32)]
 
 
+class TailIn(ctypes.Structure):
+    """lt_ffn_tail_in: the previous Gemma 4 layer's FFN tail, fused into the next attention block."""
+    _fields_ = [("f", ctypes.c_void_p), ("w1", ctypes.c_void_p), ("m", ctypes.c_void_p), ("w2", ctypes.c_void_p),
+                ("w", ctypes.c_void_p), ("los", ctypes.c_float), ("eps", ctypes.c_float)]
+
+
 class SampleParams(ctypes.Structure):
     """lt_sample_params (src/model/sample.zig:4-8)."""
     _fields_ = [("temperature", ctypes.c_float), ("top_k", ctypes.c_uint32), ("top_p", ctypes.c_float)]
@@ -148,7 +154,8 @@ def load_library() -> ctypes.CDLL:
         "lt_sample_step": (I, [P, P, U32, ctypes.POINTER(SampleParams), P, P, P, P]),
         "lt_rng_seed": (None, [U64, ctypes.POINTER(U64)]),
         "lt_attn_block": (I, [P, ctypes.POINTER(AttnCfg), P, P, F, P, P, P, P, P, P, P, P, P]),
-        "lt_attn_block_split": (I, [P, ctypes.POINTER(AttnCfg), P, P, F, P, P, P, P, P, P, P, P, P, P, P, P]),
+        "lt_attn_block_split": (I, [P, ctypes.POINTER(AttnCfg), P, P, F, P, P, P, P, P, P, P, P, P, P, P,
+                                    ctypes.POINTER(TailIn), P]),
         "lt_prefetch_next": (I, [P, P, P]),
         "lt_quant_matvec_host": (I, [P, P, P, U32, P, U64, U64]),
         "lt_moe_forward_host": (I, [P, P, P, P, P, I, I, P, P, U32, U32, P, P, P]),
@@ -404,12 +411,18 @@ class Context:
                                            _ptr(v_cache), wo.handle, _ptr(out)))
 
     def attn_block_split(self, cfg: AttnCfg, x, norm_w, eps: float, wq: Tensor, wk: Tensor, wv: Tensor | None,
-                         qkv_bias, q_norm, k_norm, pos, k_cache, v_cache, wo: Tensor, post_norm, out) -> None:
-        """attn_block over separate Q/K/V tensors; wv None: V = K; post_norm: out = x + rmsnorm(wo . att) * post_norm."""
+                         qkv_bias, q_norm, k_norm, pos, k_cache, v_cache, wo: Tensor, post_norm, out,
+                         tail: tuple | None = None) -> None:
+        """attn_block over separate Q/K/V tensors; wv None: V = K; post_norm: out = x + rmsnorm(wo . att) *
+        post_norm; tail (f, w1, m, w2, w, los, eps): the block's input is that FFN tail of x."""
+        t = None
+        if tail is not None:
+            f, w1, m, w2, w, los, teps = tail
+            t = ctypes.byref(TailIn(_ptr(f), _ptr(w1), _ptr(m), _ptr(w2), _ptr(w), los, teps))
         self._check(self.lib.lt_attn_block_split(self.ptr, ctypes.byref(cfg), _ptr(x), _ptr(norm_w), eps, wq.handle,
                                                  wk.handle, wv.handle if wv else None, _ptr(qkv_bias), _ptr(q_norm),
                                                  _ptr(k_norm), _ptr(pos), _ptr(k_cache), _ptr(v_cache), wo.handle,
-                                                 _ptr(post_norm), _ptr(out)))
+                                                 _ptr(post_norm), t, _ptr(out)))
 
     def prefetch_next(self, a: Tensor | None, b: Tensor | None = None) -> None:
         self._check(self.lib.lt_prefetch_next(self.ptr, a.handle if a else None, b.handle if b else None))

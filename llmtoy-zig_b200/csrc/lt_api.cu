@@ -809,7 +809,7 @@ static lt_status attn_block_impl(lt_ctx *ctx, const char *who, const lt_attn_cfg
                                  const float *dev_norm_w, float eps, const lt_tensor *const *seg, uint32_t nseg,
                                  const float *dev_qkv_bias, const float *dev_q_norm, const float *dev_k_norm,
                                  const uint32_t *dev_pos, void *dev_k_cache, void *dev_v_cache, const lt_tensor *wo,
-                                 const float *dev_post_norm, float *dev_out) {
+                                 const float *dev_post_norm, const lt_ffn_tail_in *tail, float *dev_out) {
     lt_status st = enter(ctx);
     if (st != LT_OK) return st;
     struct Clear {
@@ -822,6 +822,8 @@ static lt_status attn_block_impl(lt_ctx *ctx, const char *who, const lt_attn_cfg
         return fail(ctx, LT_EINVAL, "%s: null argument", who);
     for (uint32_t s = 0; s < nseg; s++)
         if (!seg[s]) return fail(ctx, LT_EINVAL, "%s: null Q/K/V tensor", who);
+    if (tail && (!tail->dev_f || !tail->dev_m || !tail->dev_w2 || !tail->dev_w))
+        return fail(ctx, LT_EINVAL, "%s: null tail input", who);
     const uint32_t nq = g.n_heads * g.hd, nkv = g.n_kv * g.hd;
     const bool v_is_k = nseg == 2;
     const uint64_t d = wo->m.rows;
@@ -852,6 +854,15 @@ static lt_status attn_block_impl(lt_ctx *ctx, const char *who, const lt_attn_cfg
     p.q_norm = dev_q_norm;
     p.k_norm = dev_k_norm;
     p.post_norm = dev_post_norm;
+    if (tail) {
+        p.tail_f = tail->dev_f;
+        p.tail_w1 = tail->dev_w1;
+        p.tail_m = tail->dev_m;
+        p.tail_w2 = tail->dev_w2;
+        p.tail_w = tail->dev_w;
+        p.tail_los = tail->los;
+        p.tail_eps = tail->eps;
+    }
     p.pos = dev_pos;
     p.kc = dev_k_cache;
     p.vc = dev_v_cache;
@@ -873,11 +884,23 @@ static lt_status attn_block_impl(lt_ctx *ctx, const char *who, const lt_attn_cfg
     const size_t attn_sc = lt::attn_scratch_floats(g, ctx->num_sms) * 4;
     const size_t qrow = lt::qact_row_pitch(d > nq ? d : nq);
     const size_t base = al256(attn_sc > qrow ? attn_sc : qrow);
-    if ((st = ensure_scratch(ctx, base + 2 * xb_b + qkv_b + att_b)) != LT_OK) return st;
+    if ((st = ensure_scratch(ctx, base + 4 * xb_b + qkv_b + att_b)) != LT_OK) return st;
     float *xb = (float *)(ctx->scratch + base), *qkv = (float *)(ctx->scratch + base + xb_b);
     float *att = (float *)(ctx->scratch + base + xb_b + qkv_b);
     float *yb = (float *)(ctx->scratch + base + xb_b + qkv_b + att_b);
     const lt::LaunchCfg c = cfg_of(ctx);
+    if (tail) {  // the tail of copies of x and m (neither is written): the block's input
+        float *xt = (float *)(ctx->scratch + base + 2 * xb_b + qkv_b + att_b), *mt = xt + xb_b / 4;
+        if ((st = launched(ctx, cudaMemcpyAsync(xt, dev_x, d * 4, cudaMemcpyDeviceToDevice, ctx->stream), "copy")) !=
+                LT_OK ||
+            (st = launched(ctx, cudaMemcpyAsync(mt, tail->dev_m, d * 4, cudaMemcpyDeviceToDevice, ctx->stream),
+                           "copy")) != LT_OK ||
+            (st = launched(ctx, lt::launch_ffn_tail(c, tail->dev_f, tail->dev_w1, mt, tail->dev_w2, tail->dev_w,
+                                                    tail->los, tail->eps, (uint32_t)d, 1, xt),
+                           "ffn_tail")) != LT_OK)
+            return st;
+        dev_x = xt;
+    }
     if (nseg > 1 && !dev_qkv_bias) {  // the norm and the projections in one launch (V = K: K once more)
         const lt::DevMat *m[3] = {&seg[0]->m, &seg[1]->m, v_is_k ? &seg[1]->m : &seg[2]->m};
         float *y[3] = {qkv, qkv + nq, qkv + nq + nkv};
@@ -923,17 +946,18 @@ lt_status lt_attn_block(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x,
                         const lt_tensor *wo, float *dev_out) {
     const lt_tensor *seg[1] = {wqkv};
     return attn_block_impl(ctx, "lt_attn_block", cfg, dev_x, dev_norm_w, eps, seg, 1, dev_qkv_bias, dev_q_norm,
-                           dev_k_norm, dev_pos, dev_k_cache, dev_v_cache, wo, nullptr, dev_out);
+                           dev_k_norm, dev_pos, dev_k_cache, dev_v_cache, wo, nullptr, nullptr, dev_out);
 }
 
 lt_status lt_attn_block_split(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *dev_x, const float *dev_norm_w,
                               float eps, const lt_tensor *wq, const lt_tensor *wk, const lt_tensor *wv,
                               const float *dev_qkv_bias, const float *dev_q_norm, const float *dev_k_norm,
                               const uint32_t *dev_pos, void *dev_k_cache, void *dev_v_cache, const lt_tensor *wo,
-                              const float *dev_post_norm, float *dev_out) {
+                              const float *dev_post_norm, const lt_ffn_tail_in *tail, float *dev_out) {
     const lt_tensor *seg[3] = {wq, wk, wv};
     return attn_block_impl(ctx, "lt_attn_block_split", cfg, dev_x, dev_norm_w, eps, seg, wv ? 3 : 2, dev_qkv_bias,
-                           dev_q_norm, dev_k_norm, dev_pos, dev_k_cache, dev_v_cache, wo, dev_post_norm, dev_out);
+                           dev_q_norm, dev_k_norm, dev_pos, dev_k_cache, dev_v_cache, wo, dev_post_norm, tail,
+                           dev_out);
 }
 
 void lt_rng_seed(uint64_t seed, uint64_t state_out[4]) {

@@ -54,6 +54,9 @@ struct AttnBlockArgs {
     uint64_t opitch;
     uint32_t onb, otype;  // 32-blocks per wo row (nq / 32), type
     const float *post_norm;  // nullable: out = x + rmsnorm(wo . att) * post_norm (gemma4/forward.zig:329-333)
+    // nullable tail_f: the previous layer's FFN tail applied to x first (gemma4/forward.zig:520-532)
+    const float *tail_f, *tail_w1, *tail_m, *tail_w2, *tail_w;
+    float tail_los, tail_eps;
     float *ss_part;          // [grid] partial sums of squares for post_norm
     uint32_t late_wo;        // the wo tile lands in the Q/K/V tile's space once phase Q is done
     float *out;
@@ -223,6 +226,43 @@ LT_DEVINL void ab_rows_any(uint32_t type, const uint8_t *tile, uint64_t pitch, u
         default: break;
         }
     }
+}
+
+LT_DEVINL float ab_rinv(float ss, uint32_t n, float eps) {
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+}
+
+// xf = (xf + rmsnorm(f' + rmsnorm(m) * w2) * w) * los, f' = rmsnorm(f) * w1 or f:
+// k_ffn_tail's arithmetic and sum orders (512 threads, strided, then warps in
+// order), so the fused and separate paths give the same bits.
+LT_DEVINL void ab_tail(const AttnBlockArgs &a, float *xf, float *red) {
+    const uint32_t n = a.d, tid = threadIdx.x;
+    float sf = 0.0f, sm = 0.0f;
+    for (uint32_t i = tid; i < n; i += kAbThreads) {
+        const float f = __ldcg(a.tail_f + i), m = __ldcg(a.tail_m + i);
+        sf = __fadd_rn(sf, __fmul_rn(f, f));
+        sm = __fadd_rn(sm, __fmul_rn(m, m));
+    }
+    sf = ab_block_sum(sf, red);
+    sm = ab_block_sum(sm, red);
+    const float rf1 = a.tail_w1 ? ab_rinv(sf, n, a.tail_eps) : 1.0f, rm = ab_rinv(sm, n, a.tail_eps);
+    auto h_of = [&](uint32_t i) {
+        const float f = __ldcg(a.tail_f + i);
+        const float fi = a.tail_w1 ? __fmul_rn(__fmul_rn(f, rf1), __ldg(a.tail_w1 + i)) : f;
+        return __fadd_rn(fi, __fmul_rn(__fmul_rn(__ldcg(a.tail_m + i), rm), __ldg(a.tail_w2 + i)));
+    };
+    float sh = 0.0f;
+    for (uint32_t i = tid; i < n; i += kAbThreads) {
+        const float h = h_of(i);
+        sh = __fadd_rn(sh, __fmul_rn(h, h));
+    }
+    const float rf = ab_rinv(ab_block_sum(sh, red), n, a.tail_eps);
+    for (uint32_t i = tid; i < n; i += kAbThreads) {
+        float v = __fadd_rn(xf[i], __fmul_rn(__fmul_rn(h_of(i), rf), __ldg(a.tail_w + i)));
+        if (a.tail_los != 1.0f) v = __fmul_rn(v, a.tail_los);
+        xf[i] = v;
+    }
+    __syncthreads();
 }
 
 // Per-head RMSNorm (optional weights) and RoPE of the query head hq and the
@@ -458,6 +498,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     const uint32_t pos = *a.pos;
     ab_load(xf, a.x, a.d);
     __syncthreads();
+    if (GEN && a.tail_f) ab_tail(a, xf, red);  // the block's input is the previous layer's output
     for (uint32_t r = tid; r < nor; r += kAbThreads) xres[r] = xf[o0 + r];
     {
         float ss = 0.0f;
@@ -734,7 +775,8 @@ static cudaError_t launch_ab_t(const LaunchCfg &c, const AttnBlockArgs &a, size_
     if constexpr (QT == 0) {
         return launch_ab_g<QT, OT, true>(c, a, smem);
     } else {
-        if (a.nseg > 1 || a.v_is_k || a.post_norm || a.late_wo) return launch_ab_g<QT, OT, true>(c, a, smem);
+        if (a.nseg > 1 || a.v_is_k || a.post_norm || a.late_wo || a.tail_f)
+            return launch_ab_g<QT, OT, true>(c, a, smem);
         return launch_ab_g<QT, OT, false>(c, a, smem);
     }
 }
@@ -759,6 +801,13 @@ cudaError_t launch_attn_block(const LaunchCfg &c, const AttnBlockParams &p) {
     a.q_norm = p.q_norm;
     a.k_norm = p.k_norm;
     a.post_norm = p.post_norm;
+    a.tail_f = p.tail_f;
+    a.tail_w1 = p.tail_w1;
+    a.tail_m = p.tail_m;
+    a.tail_w2 = p.tail_w2;
+    a.tail_w = p.tail_w;
+    a.tail_los = p.tail_los;
+    a.tail_eps = p.tail_eps;
     a.pos = p.pos;
     a.kc = p.kc;
     a.vc = p.vc;

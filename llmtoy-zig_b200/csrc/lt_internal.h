@@ -136,6 +136,9 @@ struct AttnBlockParams {
     DevMat wo;
     const float *bias, *q_norm, *k_norm;
     const float *post_norm = nullptr;  // out = x + rmsnorm(wo . att) * post_norm instead of x + wo . att
+    // non-null tail_f: x is first replaced by the previous layer's FFN tail of it (launch_ffn_tail's arguments)
+    const float *tail_f = nullptr, *tail_w1 = nullptr, *tail_m = nullptr, *tail_w2 = nullptr, *tail_w = nullptr;
+    float tail_los = 1.0f, tail_eps = 0.0f;
     const uint32_t *pos;
     void *kc, *vc;  // f32 or f16 elements (AttnGeom::kv_f16)
     float *out;            // may alias x

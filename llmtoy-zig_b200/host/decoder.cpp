@@ -70,7 +70,7 @@ lt_status layer_step(lth_decoder *d, uint32_t l) {
                               kc, vc, L.wo, d->x));
     else
         LTH_TRY(lt_attn_block_split(c, &d->attn, d->x, L.attn_norm, m.eps, L.wq, L.wk, L.wv, L.qkv_bias, L.q_norm,
-                                    L.k_norm, pos, kc, vc, L.wo, nullptr, d->x));
+                                    L.k_norm, pos, kc, vc, L.wo, nullptr, nullptr, d->x));
     // the FFN block warms the next layer's attention weights in L2
     if (next) LTH_TRY(lt_prefetch_next(c, next->wqkv ? next->wqkv : next->wq, next->wo));
     if (L.router) {
@@ -81,6 +81,15 @@ lt_status layer_step(lth_decoder *d, uint32_t l) {
 }
 
 // One Gemma 4 layer (gemma4/forward.zig:195-533, the CPU branches).
+// The end of layer l (forward.zig:520-532): x = (x + rmsnorm(f' + m') * w) * los.
+lt_ffn_tail_in gemma_tail(const lth_decoder *d, uint32_t l) {
+    const lth_layer &L = d->layers[l];
+    return lt_ffn_tail_in{d->fbuf, L.post_ffw_norm_1, d->mbuf, L.post_ffw_norm_2, L.post_ffw_norm,
+                          L.layer_output_scale, d->m.eps};
+}
+
+// Layer l up to its FFN tail, which the next layer's attention block (or the
+// step, after the last layer) applies.
 lt_status gemma_layer(lth_decoder *d, uint32_t l) {
     const lth_model &m = d->m;
     const lth_layer &L = d->layers[l];
@@ -102,17 +111,17 @@ lt_status gemma_layer(lth_decoder *d, uint32_t l) {
     void *kc = d->kcache + d->kv_off[l] * d->kv_esize, *vc = d->vcache + d->kv_off[l] * d->kv_esize;
     // norm, Q/K/V (without wv, V = K before the norms: forward.zig:250), Q/K/V norms, RoPE, attention,
     // wo and the post-attention norm into the residual (:329-333) in one launch
+    // and first the previous layer's FFN tail
+    const lt_ffn_tail_in prev = l ? gemma_tail(d, l - 1) : lt_ffn_tail_in{};
     LTH_TRY(lt_attn_block_split(c, &a, d->x, L.attn_norm, m.eps, L.wq, L.wk, L.wv, nullptr, L.q_norm, L.k_norm, pos,
-                                kc, vc, L.wo, L.post_attention_norm, d->x));
+                                kc, vc, L.wo, L.post_attention_norm, l ? &prev : nullptr, d->x));
     // dense GeGLU FFN (:390-396; its post_ffw_norm_1 is applied in the tail)
     LTH_TRY(lt_ffn_block(c, L.ffn_gate, L.ffn_up, L.ffn_down, LT_ACT_GELU_TANH, L.ffn_norm, m.eps, d->x, 1, 0,
                          d->fbuf));
     // MoE: weighted and raw-scaled norms of x, router, experts (:401-494) in one launch
-    LTH_TRY(lt_moe_block_scaled(c, L.router, L.exp_gate, L.exp_up, L.exp_down, LT_ACT_GELU_TANH, 0, L.down_exps_scale,
-                                L.pre_ffw_norm_2, L.router_scale, 1.0f / __builtin_sqrtf((float)m.d_model), m.eps,
-                                d->x, 1, m.n_used, 0, d->mbuf, d->ids, d->wts));
-    return lt_ffn_tail(c, d->fbuf, L.post_ffw_norm_1, d->mbuf, L.post_ffw_norm_2, L.post_ffw_norm,
-                       L.layer_output_scale, m.eps, m.d_model, 1, d->x);
+    return lt_moe_block_scaled(c, L.router, L.exp_gate, L.exp_up, L.exp_down, LT_ACT_GELU_TANH, 0, L.down_exps_scale,
+                               L.pre_ffw_norm_2, L.router_scale, 1.0f / __builtin_sqrtf((float)m.d_model), m.eps,
+                               d->x, 1, m.n_used, 0, d->mbuf, d->ids, d->wts);
 }
 
 lt_status step(lth_decoder *d, bool logits) {
@@ -121,6 +130,8 @@ lt_status step(lth_decoder *d, bool logits) {
     if (m.family == LTH_GEMMA4) {
         LTH_TRY(lt_scale(d->ctx, d->x, m.d_model, 1, __builtin_sqrtf((float)m.d_model)));  // forward.zig:117-120
         for (uint32_t l = 0; l < m.n_layers; l++) LTH_TRY(gemma_layer(d, l));
+        const lt_ffn_tail_in t = gemma_tail(d, m.n_layers - 1);
+        LTH_TRY(lt_ffn_tail(d->ctx, t.dev_f, t.dev_w1, d->mbuf, t.dev_w2, t.dev_w, t.los, t.eps, m.d_model, 1, d->x));
     } else {
         for (uint32_t l = 0; l < m.n_layers; l++) LTH_TRY(layer_step(d, l));
     }

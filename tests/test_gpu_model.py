@@ -277,25 +277,26 @@ def test_attn_block_matches_separate_ops(pkg, oracle, name, d, nh, nkv, hd, wt, 
     assert rel_l2(res[0], res[1]) < 2e-5, rel_l2(res[0], res[1])
 
 
-@pytest.mark.parametrize("name,d,nh,nkv,hd,types,vk,neox,qk,vnorm,bias,post,window,f16", [
+@pytest.mark.parametrize("name,d,nh,nkv,hd,types,vk,neox,qk,vnorm,bias,post,window,f16,tail", [
     # Q4_K_M-style: Q/K Q4_K, V Q6_K (so no stacked tensor), f16 KV
-    ("qwen3-mixed", 2048, 32, 4, 128, (12, 12, 14, 12), False, True, True, False, False, False, 0, True),
-    # Gemma 4 sliding layer: V normed, post-attention norm into the residual
-    ("gemma-swa", 1024, 8, 4, 256, (8, 8, 8, 8), False, True, True, True, False, True, 16, False),
+    ("qwen3-mixed", 2048, 32, 4, 128, (12, 12, 14, 12), False, True, True, False, False, False, 0, True, False),
+    # Gemma 4 sliding layer: V normed, post-attention norm into the residual, the previous layer's tail first
+    ("gemma-swa", 1024, 8, 4, 256, (8, 8, 8, 8), False, True, True, True, False, True, 16, False, True),
     # Gemma 4 full-attention layer without wv: V is the raw K projection
-    ("gemma-v=k", 1024, 8, 2, 256, (8, 14, None, 12), True, True, True, True, False, True, 0, True),
-    ("bias-v=k", 512, 4, 2, 128, (14, 8, None, 8), True, False, False, False, True, False, 0, False),
+    ("gemma-v=k", 1024, 8, 2, 256, (8, 14, None, 12), True, True, True, True, False, True, 0, True, False),
+    ("bias-v=k", 512, 4, 2, 128, (14, 8, None, 8), True, False, False, False, True, False, 0, False, False),
     # Gemma-4-26B-A4B attention shape: the Q8_0 tile leaves no room for the wo rows until phase Q ends
-    ("gemma26b-q8", 2816, 16, 8, 256, (8, 8, 8, 8), False, True, True, True, False, True, 1024, True),
+    ("gemma26b-q8", 2816, 16, 8, 256, (8, 8, 8, 8), False, True, True, True, False, True, 1024, True, True),
     # the same shape whose tiles fit together with the head vectors in the consumed Q/K/V space
-    ("gemma26b-mixed", 2816, 16, 8, 256, (14, 12, 12, 12), False, True, True, True, False, True, 1024, False),
-    ("bias-split", 896, 14, 2, 64, (8, 8, 8, 8), False, False, False, False, True, False, 0, False),
+    ("gemma26b-mixed", 2816, 16, 8, 256, (14, 12, 12, 12), False, True, True, True, False, True, 1024, False, False),
+    ("bias-split", 896, 14, 2, 64, (8, 8, 8, 8), False, False, False, False, True, False, 0, False, False),
 ])
 def test_attn_block_split_matches_separate_ops(pkg, oracle, name, d, nh, nkv, hd, types, vk, neox, qk, vnorm, bias,
-                                                post, window, f16):
+                                                post, window, f16, tail):
     """lt_attn_block_split (separate Q/K/V tensors of mixed types, V = K,
-    post-attention norm) as the persistent kernel against the same computation
-    as separate ops, step by step over 24 positions."""
+    post-attention norm, the previous layer's FFN tail fused in) as the
+    persistent kernel against the same computation as separate ops, step by
+    step over 24 positions."""
     import os
     synth, _ = _mods()
     rng = np.random.default_rng(d + nh + 7)
@@ -313,6 +314,11 @@ def test_attn_block_split_matches_separate_ops(pkg, oracle, name, d, nh, nkv, hd
     cap = window if window else 64
     cfg = pkg.AttnCfg(nh, nkv, hd, int(neox), 1e6, 1e-6, 1.0 if qk else 1.0 / np.sqrt(hd), cap, window, int(vnorm),
                       int(f16))
+    tail_in = None
+    if tail:  # f, w1, m, w2, w as device vectors; m must come back unchanged
+        tvec = [rng.normal(0, 1, d).astype(np.float32) for _ in range(2)] + \
+            [rng.uniform(0.5, 1.5, d).astype(np.float32) for _ in range(3)]
+        tail_in = (dev(tvec[0]), dev(tvec[2]), dev(tvec[1]), dev(tvec[3]), dev(tvec[4]), 0.75, 1e-6)
     ctxs = []
     old = os.environ.get("LLMTOY_ATTN_BLOCK")
     for flag in ("1", "0"):
@@ -339,9 +345,12 @@ def test_attn_block_split_matches_separate_ops(pkg, oracle, name, d, nh, nkv, hd
             x0 = host(x)
             c.attn_block_split(cfg, x, dev(nw), 1e-6, tq, tk, tv, None if bs is None else dev(bs),
                                None if qn is None else dev(qn), None if kn is None else dev(kn),
-                               dev(np.array([pos], np.int32)), kc, vc, to, None if pn is None else dev(pn), out)
+                               dev(np.array([pos], np.int32)), kc, vc, to, None if pn is None else dev(pn), out,
+                               tail=tail_in)
             c.sync()
             xs.append(host(out) - x0)
+            if tail:
+                np.testing.assert_array_equal(host(tail_in[2]), tvec[1])
         labels = c.profile_read()
         c.profile(False)
         assert any(k.startswith("attn_block") for k in labels) == fused, labels
