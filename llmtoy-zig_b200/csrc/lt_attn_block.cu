@@ -232,35 +232,64 @@ LT_DEVINL float ab_rinv(float ss, uint32_t n, float eps) {
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
 }
 
+// The FFN tail's values per thread: elements i = tid + k * kAbThreads (d <= 8192).
+constexpr int kAbTailPer = 16;
+struct AbTailW {
+    float w1[kAbTailPer], w2[kAbTailPer], w[kAbTailPer];
+};
+
+// The tail's norm weights, into registers before the kernel waits on its producer (they are static).
+LT_DEVINL void ab_tail_weights(const AttnBlockArgs &a, AbTailW &t) {
+#pragma unroll
+    for (int k = 0; k < kAbTailPer; k++) {
+        const uint32_t i = threadIdx.x + k * kAbThreads;
+        const bool in = i < a.d;
+        t.w1[k] = in && a.tail_w1 ? __ldg(a.tail_w1 + i) : 0.0f;
+        t.w2[k] = in ? __ldg(a.tail_w2 + i) : 0.0f;
+        t.w[k] = in ? __ldg(a.tail_w + i) : 0.0f;
+    }
+}
+
 // xf = (xf + rmsnorm(f' + rmsnorm(m) * w2) * w) * los, f' = rmsnorm(f) * w1 or f:
 // k_ffn_tail's arithmetic and sum orders (512 threads, strided, then warps in
-// order), so the fused and separate paths give the same bits.
-LT_DEVINL void ab_tail(const AttnBlockArgs &a, float *xf, float *red) {
+// order), so the fused and separate paths give the same bits.  One global
+// round trip (f and m); the weights are already in registers.
+LT_DEVINL void ab_tail(const AttnBlockArgs &a, const AbTailW &t, float *xf, float *red) {
     const uint32_t n = a.d, tid = threadIdx.x;
+    float fv[kAbTailPer], hv[kAbTailPer];
     float sf = 0.0f, sm = 0.0f;
-    for (uint32_t i = tid; i < n; i += kAbThreads) {
-        const float f = __ldcg(a.tail_f + i), m = __ldcg(a.tail_m + i);
-        sf = __fadd_rn(sf, __fmul_rn(f, f));
-        sm = __fadd_rn(sm, __fmul_rn(m, m));
+#pragma unroll
+    for (int k = 0; k < kAbTailPer; k++) {
+        const uint32_t i = tid + k * kAbThreads;
+        fv[k] = i < n ? __ldcg(a.tail_f + i) : 0.0f;
+        hv[k] = i < n ? __ldcg(a.tail_m + i) : 0.0f;
+        if (i < n) {
+            sf = __fadd_rn(sf, __fmul_rn(fv[k], fv[k]));
+            sm = __fadd_rn(sm, __fmul_rn(hv[k], hv[k]));
+        }
     }
     sf = ab_block_sum(sf, red);
     sm = ab_block_sum(sm, red);
     const float rf1 = a.tail_w1 ? ab_rinv(sf, n, a.tail_eps) : 1.0f, rm = ab_rinv(sm, n, a.tail_eps);
-    auto h_of = [&](uint32_t i) {
-        const float f = __ldcg(a.tail_f + i);
-        const float fi = a.tail_w1 ? __fmul_rn(__fmul_rn(f, rf1), __ldg(a.tail_w1 + i)) : f;
-        return __fadd_rn(fi, __fmul_rn(__fmul_rn(__ldcg(a.tail_m + i), rm), __ldg(a.tail_w2 + i)));
-    };
     float sh = 0.0f;
-    for (uint32_t i = tid; i < n; i += kAbThreads) {
-        const float h = h_of(i);
-        sh = __fadd_rn(sh, __fmul_rn(h, h));
+#pragma unroll
+    for (int k = 0; k < kAbTailPer; k++) {
+        const uint32_t i = tid + k * kAbThreads;
+        if (i < n) {
+            const float fi = a.tail_w1 ? __fmul_rn(__fmul_rn(fv[k], rf1), t.w1[k]) : fv[k];
+            hv[k] = __fadd_rn(fi, __fmul_rn(__fmul_rn(hv[k], rm), t.w2[k]));
+            sh = __fadd_rn(sh, __fmul_rn(hv[k], hv[k]));
+        }
     }
     const float rf = ab_rinv(ab_block_sum(sh, red), n, a.tail_eps);
-    for (uint32_t i = tid; i < n; i += kAbThreads) {
-        float v = __fadd_rn(xf[i], __fmul_rn(__fmul_rn(h_of(i), rf), __ldg(a.tail_w + i)));
-        if (a.tail_los != 1.0f) v = __fmul_rn(v, a.tail_los);
-        xf[i] = v;
+#pragma unroll
+    for (int k = 0; k < kAbTailPer; k++) {
+        const uint32_t i = tid + k * kAbThreads;
+        if (i < n) {
+            float v = __fadd_rn(xf[i], __fmul_rn(__fmul_rn(hv[k], rf), t.w[k]));
+            if (a.tail_los != 1.0f) v = __fmul_rn(v, a.tail_los);
+            xf[i] = v;
+        }
     }
     __syncthreads();
 }
@@ -486,6 +515,8 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
         }
     }
     if (tid < 2 && a.pf[tid]) prefetch_l2_share(a.pf[tid], a.pf_bytes[tid], c, G);
+    AbTailW tw;
+    if (GEN && a.tail_f) ab_tail_weights(a, tw);
     // the third hand-off (post-norm only) counts every launch: without it, CTA 0
     // adds the whole grid's arrivals at once, off the critical path
     if (!a.post_norm && c == 0 && tid == 0) atomicAdd(ctr3, (unsigned long long)G);
@@ -498,7 +529,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     const uint32_t pos = *a.pos;
     ab_load(xf, a.x, a.d);
     __syncthreads();
-    if (GEN && a.tail_f) ab_tail(a, xf, red);  // the block's input is the previous layer's output
+    if (GEN && a.tail_f) ab_tail(a, tw, xf, red);  // the block's input is the previous layer's output
     for (uint32_t r = tid; r < nor; r += kAbThreads) xres[r] = xf[o0 + r];
     {
         float ss = 0.0f;
