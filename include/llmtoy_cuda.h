@@ -212,6 +212,19 @@ lt_status lt_moe_block_scaled(lt_ctx *ctx, const lt_tensor *router, const lt_ten
 lt_status lt_argmax(lt_ctx *ctx, const float *dev_x, uint32_t n, uint32_t ntok,
                     uint32_t *dev_idx);
 
+/* Self-test of the bounded device waits (no reference counterpart: the
+ * reference has no device-side timeouts; on a GPU error its forward loop falls
+ * back to the CPU, src/model/gemma4/forward.zig:456-480).  Launches two CTAs
+ * that run the library's own wait helpers with a limit of limit_us
+ * (1..2000000):
+ *   kind 0 -- a grid barrier every CTA reaches: lt_sync returns LT_OK;
+ *   kind 1 -- a grid barrier expecting one arrival more than the grid gives;
+ *   kind 2 -- an mbarrier expecting one arrival more than it gets.
+ * Kinds 1 and 2 give up after the limit, record the code in the device error
+ * word and return, so lt_sync returns LT_ETIMEOUT and the context stays
+ * usable.  The persistent kernels' waits use the same helpers with a 2 s limit. */
+lt_status lt_selftest_wait(lt_ctx *ctx, uint32_t kind, uint32_t limit_us);
+
 /* ── kernel timing ────────────────────────────────────────────────────────
  * GpuProfiler (src/gpu/context.zig:34-268, LLMTOY_GPU_PROFILE): when on,
  * every kernel launch is bracketed by CUDA events on its stream and its
@@ -258,13 +271,24 @@ lt_status lt_graph_free(lt_ctx *ctx, lt_graph *graph);
  *     call on each device looks up the array's device address; make that
  *     first call before any stream capture.
  *   - Calls share the array: calls that overlap on the GPU race.
+ *   - The array's address is kept per device for the life of the process:
+ *     after a cudaDeviceReset of a device it ran on, unload the library.
  * Returns LT_EINVAL / LT_EUNSUPPORTED_TYPE for bad arguments, LT_ECUDA if a
- * launch fails. */
+ * launch fails.  Faults the kernels detect on the device (an id >= n_experts,
+ * whose token's output is then unspecified; a copy that timed out) are not in
+ * this return value: lt_noalloc_status reports them. */
 lt_status lt_moe_ffn_noalloc(void *cuda_stream, const void *gate, const void *up,
                              const void *down, uint32_t gate_type, uint32_t down_type,
                              uint32_t n_experts, uint64_t d_model, uint64_t d_expert, int act,
                              const float *dev_x, uint32_t ntok, const uint32_t *dev_ids,
                              const float *dev_w, uint32_t k, float *dev_out);
+
+/* The device-detected fault of the lt_moe_ffn_noalloc calls issued on
+ * cuda_stream since the last call started (each call clears the word first):
+ * waits for the stream, then returns LT_OK, LT_EINVAL (an expert id past
+ * n_experts) or LT_ETIMEOUT (a device-side wait gave up), and clears it.
+ * Allocates nothing; not for use during stream capture. */
+lt_status lt_noalloc_status(void *cuda_stream);
 
 /* ── expert parallelism building blocks ──────────────────────────────────────
  * No counterpart in the reference, whose MoE runs on one device: these let a

@@ -676,6 +676,14 @@ lt_status lt_argmax(lt_ctx *ctx, const float *dev_x, uint32_t n, uint32_t ntok, 
     return launched(ctx, lt::launch_argmax(cfg_of(ctx), dev_x, n, ntok, dev_idx, pv, pi, ctx->counters), "argmax");
 }
 
+lt_status lt_selftest_wait(lt_ctx *ctx, uint32_t kind, uint32_t limit_us) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (kind > 2 || limit_us == 0 || limit_us > 2000000) return fail(ctx, LT_EINVAL, "lt_selftest_wait: bad argument");
+    return launched(ctx, lt::launch_selftest_wait(cfg_of(ctx), (int)kind, (uint64_t)limit_us * 1000ull),
+                    "selftest_wait");
+}
+
 // ── device buffers ─────────────────────────────────────────────────────────
 
 lt_status lt_device_alloc(lt_ctx *ctx, size_t bytes, void **dev_out) {

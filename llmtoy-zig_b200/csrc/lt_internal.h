@@ -97,6 +97,7 @@ cudaError_t launch_norm_pair(const LaunchCfg &c, const float *x, const float *w,
 cudaError_t launch_ffn_tail(const LaunchCfg &c, const float *f, const float *w1, float *m, const float *w2,
                             const float *w, float los, float eps, uint32_t n, uint32_t ntok, float *x);
 cudaError_t launch_softcap(const LaunchCfg &c, float *x, size_t n, float cap);
+cudaError_t launch_selftest_wait(const LaunchCfg &c, int kind, uint64_t limit_ns);
 // out = dequantised row tokens[*pos] of m (embedLookup); rows >= m.rows set
 // DEV_ERR_BAD_INDEX and read row 0.
 cudaError_t launch_embed(const LaunchCfg &c, const DevMat &m, const uint32_t *tokens, const uint32_t *pos,

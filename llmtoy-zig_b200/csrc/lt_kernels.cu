@@ -447,4 +447,37 @@ cudaError_t launch_argmax(const LaunchCfg &c, const float *x, uint32_t n, uint32
                     n_prompt);
 }
 
+// ── self-test of the bounded device waits ───────────────────────────────────
+// Grid-barrier counter of the self-test kernel: grows by gridDim.x (2) per
+// launch, like the persistent kernels' counters.
+__device__ unsigned long long g_selftest_ctr;
+
+// kind 0: a grid barrier every CTA reaches (completes); kind 1: the same
+// barrier expecting one arrival more than the grid gives; kind 2: an mbarrier
+// expecting one arrival more than it gets.  Kinds 1 and 2 give up after
+// limit_ns through the same wait helpers the persistent kernels use, record
+// the error code and return.
+__global__ void k_selftest_wait(int kind, uint64_t limit_ns, int *dev_err) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ uint64_t s_epoch;
+    if (kind == 2) {
+        if (threadIdx.x == 0) {
+            mbar_init(&bar, 2);
+            fence_barrier_init();
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&bar)) : "memory");
+            if (!mbar_wait_bounded(&bar, 0, limit_ns) && dev_err) atomicExch(dev_err, DEV_ERR_TMA_TIMEOUT);
+        }
+        return;
+    }
+    if (threadIdx.x == 0) s_epoch = grid_epoch(&g_selftest_ctr, gridDim.x);
+    __syncthreads();
+    grid_wait(&g_selftest_ctr, s_epoch + (kind == 1 ? 1 : 0), dev_err, limit_ns);
+}
+
+cudaError_t launch_selftest_wait(const LaunchCfg &c, int kind, uint64_t limit_ns) {
+    LaunchCfg plain = c;
+    plain.pdl = false;
+    return launch_k(plain, "selftest_wait", k_selftest_wait, dim3(2), dim3(32), 0, kind, limit_ns, c.dev_err);
+}
+
 }  // namespace lt

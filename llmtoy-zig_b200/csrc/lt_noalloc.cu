@@ -12,8 +12,13 @@
 // The array (kNoallocScratchBytes) is part of the module, so every GPU that
 // loads the library holds it until the process exits.  Every call shares it
 // and it keeps the previous call's contents: the dispatch plan and the
-// activations are fully rewritten each call, and the gate/up block counters,
-// which must start at zero, are cleared at the start of every call.  Calls
+// activations are fully rewritten each call, and the device error word and
+// the gate/up block counters, which must start at zero, are cleared at the
+// start of every call.  Kernels record a device-detected fault (an expert id
+// past n_experts, a TMA copy that never landed) in the error word instead of
+// faulting; lt_noalloc_status reads and clears it.  The array's device address
+// is looked up once per device and kept: the library does not survive a
+// cudaDeviceReset of a device it has already run on.  Calls
 // whose work overlaps on the GPU (different streams, or graphs replayed
 // concurrently) race on it; serialise them.
 #include <mutex>
@@ -125,8 +130,10 @@ extern "C" lt_status lt_moe_ffn_noalloc(void *cuda_stream, const void *gate, con
     DevMat dn{static_cast<const uint8_t *>(down), down_type, d_model, F, drb, drb, n_experts};
     const bool direct = ntok == 1;
 
-    // The gate/up block counters must start at zero: clear them (a memset, not an allocation).
-    cudaError_t e = cudaMemsetAsync(base + o_cnt, 0, n_cnt * 4, c.stream);
+    // The error word and the gate/up block counters must start at zero: clear
+    // them (memsets, not allocations).
+    cudaError_t e = cudaMemsetAsync(base, 0, 4, c.stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(base + o_cnt, 0, n_cnt * 4, c.stream);
     if (e == cudaSuccess) e = launch_quantize(c, dev_x, (uint32_t)d_model, ntok, base + o_xq, xq_pitch);
     if (e == cudaSuccess && !direct) e = launch_moe_plan(c, dev_ids, ntok, k, n_experts, plan);
     if (e == cudaSuccess)
@@ -141,4 +148,30 @@ extern "C" lt_status lt_moe_ffn_noalloc(void *cuda_stream, const void *gate, con
         return e == cudaErrorMemoryAllocation ? LT_ENOMEM : LT_ECUDA;
     }
     return LT_OK;
+}
+
+extern "C" lt_status lt_noalloc_status(void *cuda_stream) {
+    using namespace lt;
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) {
+        cudaGetLastError();
+        return LT_ECUDA;
+    }
+    uint8_t *base = nullptr;
+    lt_status st = scratch_address(device, &base);
+    if (st != LT_OK) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
+    int h = 0;
+    // Ordered after the caller's lt_moe_ffn_noalloc calls on the same stream;
+    // the copy to this pageable host word returns once it has landed.
+    cudaError_t e = cudaMemcpyAsync(&h, base, 4, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e == cudaSuccess && h != 0) e = cudaMemsetAsync(base, 0, 4, s);
+    if (e == cudaSuccess && h != 0) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return LT_ECUDA;
+    }
+    if (h == DEV_ERR_BAD_INDEX) return LT_EINVAL;
+    return h ? LT_ETIMEOUT : LT_OK;
 }

@@ -225,6 +225,21 @@ class Decoder:
         return list(out)
 
 
+class _Uploads:
+    """ctx.upload once per host array: layers that share weight arrays (a
+    model whose depth cycles a few distinct layer sets) share device tensors,
+    which are read-only."""
+
+    def __init__(self, ctx: Context):
+        self.ctx, self.done = ctx, {}
+
+    def __call__(self, a, t, rows, cols, n_experts=0):
+        key = (id(a), t, rows, cols, n_experts)
+        if key not in self.done:
+            self.done[key] = (a, self.ctx.upload(a, t, rows, cols, n_experts=n_experts))
+        return self.done[key][1]
+
+
 def upload_decoder(ctx: Context, m, kv_cap: int = 4096, stacked_qkv: bool = True, kv_f16: bool = False) -> ModelSpec:
     """Upload a synth.DecoderModel (host GGUF bytes) and return its ModelSpec.
     Norm weights and biases go to torch CUDA tensors, which the spec keeps
@@ -236,28 +251,29 @@ def upload_decoder(ctx: Context, m, kv_cap: int = 4096, stacked_qkv: bool = True
         return None if a is None else torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda()
 
     d = m.d_model
+    up = _Uploads(ctx)
     layers = []
     for L in m.layers:
         nq, nkv = m.n_heads * m.head_dim, m.n_kv_heads * m.head_dim
         ls = LayerSpec(attn_norm=dev(L.attn_norm), ffn_norm=dev(L.ffn_norm),
-                       wo=ctx.upload(L.wo, L.attn_type, d, nq), qkv_bias=dev(L.qkv_bias),
+                       wo=up(L.wo, L.attn_type, d, nq), qkv_bias=dev(L.qkv_bias),
                        q_norm=dev(L.q_norm), k_norm=dev(L.k_norm))
         if stacked_qkv:
             ls.wqkv = ctx.upload(L.wqkv, L.attn_type, nq + 2 * nkv, d)
         else:
-            ls.wq = ctx.upload(L.wq, L.attn_type, nq, d)
-            ls.wk = ctx.upload(L.wk, L.attn_type, nkv, d)
-            ls.wv = ctx.upload(L.wv, L.attn_type, nkv, d)
+            ls.wq = up(L.wq, L.attn_type, nq, d)
+            ls.wk = up(L.wk, L.attn_type, nkv, d)
+            ls.wv = up(L.wv, L.attn_type, nkv, d)
         if L.moe is None:
-            ls.ffn_gate = ctx.upload(L.ffn_gate, L.ffn_type, m.d_ffn, d)
-            ls.ffn_up = ctx.upload(L.ffn_up, L.ffn_type, m.d_ffn, d)
-            ls.ffn_down = ctx.upload(L.ffn_down, L.ffn_type, d, m.d_ffn)
+            ls.ffn_gate = up(L.ffn_gate, L.ffn_type, m.d_ffn, d)
+            ls.ffn_up = up(L.ffn_up, L.ffn_type, m.d_ffn, d)
+            ls.ffn_down = up(L.ffn_down, L.ffn_type, d, m.d_ffn)
         else:
             E, F = m.n_experts, m.d_expert
-            ls.router = ctx.upload(L.moe.router, 0, E, d)
-            ls.exp_gate = ctx.upload(L.moe.gate, L.moe.gate_type, F, d, n_experts=E)
-            ls.exp_up = ctx.upload(L.moe.up, L.moe.gate_type, F, d, n_experts=E)
-            ls.exp_down = ctx.upload(L.moe.down, L.moe.down_type, d, F, n_experts=E)
+            ls.router = up(L.moe.router, 0, E, d)
+            ls.exp_gate = up(L.moe.gate, L.moe.gate_type, F, d, n_experts=E)
+            ls.exp_up = up(L.moe.up, L.moe.gate_type, F, d, n_experts=E)
+            ls.exp_down = up(L.moe.down, L.moe.down_type, d, F, n_experts=E)
         layers.append(ls)
     return ModelSpec(d_model=d, n_heads=m.n_heads, n_kv_heads=m.n_kv_heads, head_dim=m.head_dim, vocab=m.vocab,
                      token_emb=ctx.upload(m.token_emb, m.emb_type, m.vocab, d),
@@ -346,20 +362,21 @@ def upload_gemma(ctx: Context, m, kv_cap: int = 4096) -> ModelSpec:
         return None if a is None else torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda()
 
     d, E, F = m.d_model, m.n_experts, m.d_expert
+    up = _Uploads(ctx)
     layers = []
     for L in m.layers:
         nq, nkv = m.n_heads * L.head_dim, L.n_kv_heads * L.head_dim
         t = L.types
-        ls = LayerSpec(attn_norm=dev(L.attn_norm), ffn_norm=dev(L.ffn_norm), wo=ctx.upload(L.wo, t["wo"], d, nq),
-                       wq=ctx.upload(L.wq, t["wq"], nq, d), wk=ctx.upload(L.wk, t["wk"], nkv, d),
-                       wv=None if L.wv is None else ctx.upload(L.wv, t["wv"], nkv, d),
+        ls = LayerSpec(attn_norm=dev(L.attn_norm), ffn_norm=dev(L.ffn_norm), wo=up(L.wo, t["wo"], d, nq),
+                       wq=up(L.wq, t["wq"], nq, d), wk=up(L.wk, t["wk"], nkv, d),
+                       wv=None if L.wv is None else up(L.wv, t["wv"], nkv, d),
                        q_norm=dev(L.q_norm), k_norm=dev(L.k_norm),
-                       ffn_gate=ctx.upload(L.w_gate, t["gate"], m.d_ffn, d),
-                       ffn_up=ctx.upload(L.w_up, t["up"], m.d_ffn, d),
-                       ffn_down=ctx.upload(L.w_down, t["down"], d, m.d_ffn),
-                       router=ctx.upload(L.router_w, 0, E, d),
-                       exp_gate=ctx.upload(L.gate_up_exps, t["gate_up_exps"], 2 * F, d, n_experts=E),
-                       exp_down=ctx.upload(L.down_exps, t["down_exps"], d, F, n_experts=E),
+                       ffn_gate=up(L.w_gate, t["gate"], m.d_ffn, d),
+                       ffn_up=up(L.w_up, t["up"], m.d_ffn, d),
+                       ffn_down=up(L.w_down, t["down"], d, m.d_ffn),
+                       router=up(L.router_w, 0, E, d),
+                       exp_gate=up(L.gate_up_exps, t["gate_up_exps"], 2 * F, d, n_experts=E),
+                       exp_down=up(L.down_exps, t["down_exps"], d, F, n_experts=E),
                        post_attention_norm=dev(L.post_attention_norm), pre_ffw_norm_2=dev(L.pre_ffw_norm_2),
                        post_ffw_norm_1=dev(L.post_ffw_norm_1), post_ffw_norm_2=dev(L.post_ffw_norm_2),
                        post_ffw_norm=dev(L.post_ffw_norm), router_scale=dev(L.router_scale),

@@ -31,6 +31,7 @@ ops object, so the host-side tests drive it over gloo with CPU ops.
 """
 from __future__ import annotations
 
+import time
 from dataclasses import dataclass
 
 
@@ -141,6 +142,70 @@ class DeviceOps:
         return out
 
 
+class PeerLost(RuntimeError):
+    """A rank did not reach the current step (it left, or is late beyond the
+    heartbeat's limit).  Raised on the host before any kernel or collective of
+    the step is issued, so nothing of the step is in flight."""
+
+    def __init__(self, rank: int, step: int, why: str):
+        super().__init__(f"rank {rank} did not reach step {step}: {why}")
+        self.rank, self.step, self.why = rank, step, why
+
+
+class Heartbeat:
+    """Host-side liveness of the ranks over a torch.distributed Store (the
+    TCPStore the process group was created with).
+
+    Before step n every rank posts n, then waits up to timeout_s for every
+    other rank to post n as well.  A rank that leaves posts a leave mark
+    (leave()), so the others stop at their next step at once; a rank that is
+    late beyond timeout_s, or died without a mark, is reported when the limit
+    runs out.  Either way PeerLost is raised before the step issues a kernel
+    or a collective, so the survivors never block inside NCCL on a rank that
+    is gone (NCCL collectives on a dead peer end only at the process group's
+    own timeout)."""
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 5.0, prefix: str = "lt_ep"):
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout_s, self.prefix = timeout_s, prefix
+
+    def _key(self, kind: str, r: int) -> str:
+        return f"{self.prefix}/{kind}/{r}"
+
+    def leave(self) -> None:
+        try:
+            self.store.set(self._key("left", self.rank), "1")
+        except RuntimeError:  # the store's host is gone already: nobody is left to tell
+            pass
+
+    def step(self, n: int) -> None:
+        """Post step n and wait for every other rank to reach it.  A store
+        that cannot be reached (its host process is gone) counts as a lost
+        peer too."""
+        try:
+            self._step(n)
+        except RuntimeError as e:
+            if isinstance(e, PeerLost):
+                raise
+            raise PeerLost(-1, n, f"store unreachable ({e})") from e
+
+    def _step(self, n: int) -> None:
+        self.store.set(self._key("step", self.rank), str(n))
+        deadline = time.monotonic() + self.timeout_s
+        for r in range(self.world):
+            if r == self.rank:
+                continue
+            while True:
+                if self.store.check([self._key("left", r)]):
+                    raise PeerLost(r, n, "it left")
+                k = self._key("step", r)
+                if self.store.check([k]) and int(self.store.get(k)) >= n:
+                    break
+                if time.monotonic() > deadline:
+                    raise PeerLost(r, n, f"no heartbeat within {self.timeout_s:.1f} s")
+                time.sleep(0.002)
+
+
 class ExpertParallelMoE:
     """Runs MoE layers expert-parallel over a process group.
 
@@ -150,10 +215,14 @@ class ExpertParallelMoE:
     world: a replacement for the all-to-all (called as exchange(out, inp,
     out_splits, in_splits) like all_to_all_single) with this caller's rank
     and the rank count.  Every rank must call forward() for the same layers
-    in the same order (each call issues four exchanges)."""
+    in the same order (each call issues four exchanges).  heartbeat: an
+    optional Heartbeat checked before each layer, so that a rank that left or
+    stalls is reported (PeerLost) before any exchange of that layer starts."""
 
-    def __init__(self, ops, k: int, group=None, exchange=None, rank: int | None = None, world: int | None = None):
-        self.ops, self.k, self.group = ops, k, group
+    def __init__(self, ops, k: int, group=None, exchange=None, rank: int | None = None, world: int | None = None,
+                 heartbeat: Heartbeat | None = None):
+        self.ops, self.k, self.group, self.heartbeat = ops, k, group, heartbeat
+        self.n_forward = 0
         if exchange is not None:
             self._a2a, self.rank, self.world = exchange, rank, world
         else:
@@ -174,6 +243,9 @@ class ExpertParallelMoE:
         x + moe(rmsnorm(x) * norm_w) when layer.norm_w is set, else moe(x)."""
         ops, k, world = self.ops, self.k, self.world
         T = x.shape[0]
+        if self.heartbeat is not None and world > 1:
+            self.heartbeat.step(self.n_forward)
+        self.n_forward += 1
         if world == 1:
             return ops.local_forward(layer, x, T, k)
         torch = ops.torch

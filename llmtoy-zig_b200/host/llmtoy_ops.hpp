@@ -17,8 +17,11 @@
 
 namespace llmtoy {
 
-// GgmlType, src/gguf/types.zig:23-52 (the subset the backend decodes).
-enum class GgmlType : uint32_t { f32 = 0, f16 = 1, q8_0 = 8, q4_k = 12, q6_k = 14 };
+// GgmlType, src/gguf/types.zig:23-52: the ten matrix types rowBytes /
+// dequantRow handle (src/ops/math.zig:194-225), all of which the backend decodes.
+enum class GgmlType : uint32_t {
+    f32 = 0, f16 = 1, q5_0 = 6, q5_1 = 7, q8_0 = 8, q3_k = 11, q4_k = 12, q5_k = 13, q6_k = 14, iq4_nl = 20
+};
 
 // GpuContext (src/gpu/context.zig) -> one CUDA context + stream per GPU.
 class Backend {

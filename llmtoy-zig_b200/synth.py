@@ -271,3 +271,26 @@ class GemmaModel:
         self.out_norm = (rng.uniform(0.5, 1.5, d_model) if norms_random else np.ones(d_model)).astype(np.float32)
         self.lm_type = lm_type
         self.lm_head = matrix(rng, lm_type, vocab, d_model)
+
+
+def cycle_layers(m, n_layers: int, swa_period: int | None = None):
+    """Deepen model m to n_layers by cycling its distinct layers (layer i
+    shares the weight arrays of layer i % len(m.layers)).  A full-depth model
+    then costs the host memory of a few layers while every layer still reads
+    its weights from memory far larger than any cache.  swa_period (Gemma 4):
+    layer i is sliding-window unless (i + 1) % swa_period == 0, the pattern of
+    the full-depth model, whatever the pattern of the layer it shares."""
+    base = list(m.layers)
+    out = []
+    for i in range(n_layers):
+        src = base[i % len(base)]
+        if swa_period is None:
+            out.append(src)
+            continue
+        lay = object.__new__(type(src))
+        lay.__dict__.update(src.__dict__)
+        lay.is_swa = (i + 1) % swa_period != 0
+        out.append(lay)
+    m.layers = out
+    m.n_layers = n_layers
+    return m

@@ -1,0 +1,153 @@
+"""Whole-model greedy decode against the CPU oracle on the benchmark configs'
+own workloads: full depth, full vocabulary, the configs' prompt and
+generation lengths and KV caches.
+
+- config 0: the dense Qwen2-0.5B shape, 24 distinct Q8_0 layers, a 5-token
+  prompt and 20 greedy tokens;
+- config 2: the Qwen3-30B-A3B shape, 48 layers, f16 KV cache of 4096
+  positions, a 32-token prompt and 128 greedy tokens;
+- config 3: the Gemma-4-26B-A4B-like shape, 30 layers (5 sliding-window layers
+  of 1024 positions : 1 global), the seeded Q4_K/Q6_K/Q8_0 mix, a 64-token
+  prompt and 80 greedy tokens;
+- the sliding-window ring past its wrap: config 3's layer shape with one
+  window-1024 layer and one global layer over 1040 prompt positions.
+
+The deep models cycle a few distinct layer weight sets through their depth
+(synth.cycle_layers) on both sides, so host memory and oracle time stay
+small while every layer still streams its weights from HBM.  The loops
+compared are the reference's generate loop (src/main.zig:1969-1995) over
+forwardOneModel (src/model/forward.zig:229-316) and Gemma 4's forwardOne
+(src/model/gemma4/forward.zig:37-567), restated in oracle/oracle.c.
+
+Bars (the north star's): every step's logits within relative L2 1e-3 of the
+oracle's and the greedy token stream identical.  A sampled step whose
+top-1/top-2 margin in the oracle's logits is not larger than the device's
+error on those two logits would be a near tie, where equality of the token
+means nothing; each such step fails with its own message instead of passing
+or failing silently.  Setting LLMTOY_PARITY_REPORT=<path> appends one JSON
+line per workload (worst rel-L2, smallest margin-to-error ratio).
+"""
+from __future__ import annotations
+
+import importlib
+import json
+import os
+
+import numpy as np
+import pytest
+
+from test_gpu_parity import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-3
+
+
+def _mods():
+    return (importlib.import_module("llmtoy-zig_b200.synth"), importlib.import_module("llmtoy-zig_b200.decoder"))
+
+
+@pytest.fixture(scope="module")
+def big_pool(oracle):
+    p = oracle.Pool(os.cpu_count() or 1)
+    yield p
+    p.close()
+
+
+def _report(name: str, stats: dict) -> None:
+    path = os.environ.get("LLMTOY_PARITY_REPORT")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps({"workload": name, **stats}) + "\n")
+
+
+def _check_stream(ctx, dec, prompt, ref_toks, ref_logits, vocab, name, check_every=1):
+    """Step the device decoder eagerly over prompt + generated positions,
+    comparing logits with the oracle's at every check_every-th step and at
+    every sampled step; then the token stream and a graph replay of it."""
+    n_prompt = len(prompt)
+    dec.start(prompt)
+    worst, min_ratio, compared = 0.0, np.inf, 0
+    for i, rl in enumerate(ref_logits):
+        dec.step()
+        sampled = i + 1 >= n_prompt
+        if not sampled and i % check_every:
+            continue
+        got = ctx.copy_to_host(dec.logits_ptr(), vocab * 4)
+        err = rel_l2(got, rl)
+        worst = max(worst, err)
+        compared += 1
+        assert err < LOGIT_TOL, (name, i, err)
+        if sampled:
+            i1, i2 = np.argsort(rl)[-1], np.argsort(rl)[-2]
+            margin = float(rl[i1] - rl[i2])
+            local = float(abs(got[i1] - rl[i1]) + abs(got[i2] - rl[i2]))
+            min_ratio = min(min_ratio, margin / max(local, 1e-30))
+            assert margin > local, f"{name}: near tie at step {i} (margin {margin:.3e} <= device error {local:.3e})"
+    toks = dec.tokens(n_prompt + len(ref_toks))
+    assert toks[:n_prompt] == list(prompt), name
+    assert toks[n_prompt:] == ref_toks, (name, toks[n_prompt:], ref_toks)
+    assert dec.generate(prompt, len(ref_toks)) == ref_toks, name  # the captured graph replays it
+    stats = {"worst_rel_l2": worst, "min_margin_over_error": min_ratio, "steps_compared": compared,
+             "tokens": len(ref_toks)}
+    _report(name, stats)
+    return stats
+
+
+def test_config0_full_workload(ctx, oracle, big_pool):
+    """24 distinct layers, vocabulary 151936, 5 + 20 tokens."""
+    synth, decoder = _mods()
+    rng = np.random.Generator(np.random.PCG64(synth.config_seed(0)))
+    m = synth.config0_model(rng)
+    prompt = np.random.Generator(np.random.PCG64(synth.config_seed(0) + 1)).integers(0, m.vocab, 5).tolist()
+    n_gen = 20
+    ref_toks, ref_logits = oracle.OracleDecoder(m, 4096, big_pool).generate(prompt, n_gen)
+    spec = decoder.upload_decoder(ctx, m, kv_cap=4096)
+    with decoder.Decoder(ctx, spec) as dec:
+        _check_stream(ctx, dec, prompt, ref_toks, ref_logits, m.vocab, "config0")
+
+
+def test_config2_full_workload(ctx, oracle, big_pool):
+    """48 layers (4 distinct sets cycled), vocabulary 151936, f16 KV of 4096
+    positions, 32 + 128 tokens."""
+    synth, decoder = _mods()
+    rng = np.random.Generator(np.random.PCG64(synth.config_seed(2)))
+    m = synth.cycle_layers(synth.config2_model(rng, n_layers=4), 48)
+    prompt = np.random.Generator(np.random.PCG64(synth.config_seed(2) + 1)).integers(0, m.vocab, 32).tolist()
+    n_gen = 128
+    ref_toks, ref_logits = oracle.OracleDecoder(m, 4096, big_pool, kv_f16=True).generate(prompt, n_gen)
+    spec = decoder.upload_decoder(ctx, m, kv_cap=4096, kv_f16=True)
+    with decoder.Decoder(ctx, spec) as dec:
+        _check_stream(ctx, dec, prompt, ref_toks, ref_logits, m.vocab, "config2")
+
+
+def test_config3_full_workload(ctx, oracle, big_pool):
+    """30 layers (3 distinct sets cycled, 5 SWA : 1 global by index), window
+    1024, vocabulary 262144, softcap 30, 64 + 80 tokens."""
+    synth, decoder = _mods()
+    rng = np.random.Generator(np.random.PCG64(synth.config_seed(3)))
+    m = synth.cycle_layers(synth.GemmaModel(rng, n_layers=3), 30, swa_period=6)
+    prompt = np.random.Generator(np.random.PCG64(synth.config_seed(3) + 1)).integers(0, m.vocab, 64).tolist()
+    n_gen = 80
+    ref_toks, ref_logits = oracle.OracleGemma(m, 4096, big_pool).generate(prompt, n_gen)
+    spec = decoder.upload_gemma(ctx, m, kv_cap=4096)
+    with decoder.Decoder(ctx, spec) as dec:
+        _check_stream(ctx, dec, prompt, ref_toks, ref_logits, m.vocab, "config3")
+
+
+def test_sliding_window_wraps(ctx, oracle, big_pool):
+    """Config 3's layer shape with one sliding-window layer (a ring of 1024
+    positions) and one global layer, over a 1040-token prompt and 8 greedy
+    tokens: positions 1024.. overwrite the ring's oldest slots, and every
+    step's logits (checked every 16th prompt step and at every sampled step)
+    must still match the oracle's."""
+    synth, decoder = _mods()
+    rng = np.random.Generator(np.random.PCG64(synth.config_seed(3) + 7))
+    m = synth.GemmaModel(rng, n_layers=2, vocab=4096, norms_random=True, lm_type=synth.Q8_0)
+    m.layers[0].is_swa, m.layers[1].is_swa = True, False
+    prompt = np.random.Generator(np.random.PCG64(synth.config_seed(3) + 8)).integers(0, m.vocab, 1040).tolist()
+    n_gen = 8
+    ref_toks, ref_logits = oracle.OracleGemma(m, 2048, big_pool).generate(prompt, n_gen)
+    spec = decoder.upload_gemma(ctx, m, kv_cap=2048)
+    with decoder.Decoder(ctx, spec) as dec:
+        _check_stream(ctx, dec, prompt, ref_toks, ref_logits, m.vocab, "config3-ring-wrap", check_every=16)
