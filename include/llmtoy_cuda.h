@@ -422,6 +422,43 @@ lt_status lt_attn_block_split(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *
                               const lt_tensor *wo, const float *dev_post_norm, const lt_ffn_tail_in *tail,
                               float *dev_out);
 
+/* ── whole-stack decode ─────────────────────────────────────────────────────
+ * Every decoder layer of one token in one launch: the per-layer loop of
+ * forwardOneModel (src/model/forward.zig:260-316) -- for each layer
+ * lt_attn_block (stacked Q/K/V) followed by lt_moe_block (router + Q4_K
+ * experts) or lt_ffn_block (dense SwiGLU) -- as one persistent kernel.  The
+ * layers hand over inside the kernel and the next layer's static weights are
+ * copied while the current one runs, so a batch-1 step pays no kernel
+ * boundary per half-layer.  Same results as the per-layer entry points up to
+ * f32 rounding (the attention's split merge order).
+ *
+ * Shapes the kernel takes (otherwise lt_stack_create returns
+ * LT_EUNSUPPORTED_TYPE and the caller keeps the per-layer calls): head_dim 64
+ * or 128, no sliding window and no V norm; Q8_0 wqkv and wo; a MoE FFN with an
+ * F32 router over at most num_SMs experts and Q4_K gate/up/down, or a dense
+ * FFN with Q8_0 gate/up/down; every layer the same kind, types and shapes. */
+typedef struct lt_stack lt_stack;
+typedef struct lt_stack_layer {
+    const lt_tensor *wqkv;                 /* [nq + 2 nkv][d] stacked Q, K, V rows */
+    const lt_tensor *wo;                   /* [d][nq] */
+    const float *attn_norm, *ffn_norm;     /* device [d] */
+    const float *q_norm, *k_norm;          /* device [head_dim] or NULL */
+    const float *qkv_bias;                 /* device [nq + 2 nkv] or NULL */
+    void *k_cache, *v_cache;               /* this layer's caches, [kv_cap][nkv] (cfg->kv_f16: f16) */
+    const lt_tensor *router;               /* F32 [E][d]; NULL: a dense FFN */
+    const lt_tensor *gate, *up, *down;     /* [E][F][d], [E][F][d], [E][d][F] (2-D when dense) */
+} lt_stack_layer;
+
+/* Checks the layers, copies their descriptors to the device and allocates the
+ * stack's scratch (not while capturing).  k: experts per token (MoE);
+ * norm_topk: renormalise the selected weights; eps: the layer RMSNorms'. */
+lt_status lt_stack_create(lt_ctx *ctx, const lt_attn_cfg *cfg, uint32_t d_model, const lt_stack_layer *layers,
+                          uint32_t n_layers, uint32_t k, int act, int norm_topk, float eps, lt_stack **out);
+/* dev_x[d] <- the stack applied to dev_x at position *dev_pos (asynchronous on
+ * the context's stream; capturable).  One stack's launches must not overlap. */
+lt_status lt_stack_run(lt_ctx *ctx, const lt_stack *stack, float *dev_x, const uint32_t *dev_pos);
+lt_status lt_stack_free(lt_ctx *ctx, lt_stack *stack);
+
 /* L2 prefetch hint: the next lt_attn_block, or single-token lt_moe_block /
  * lt_moe_forward, launched on this context starts by prefetching these
  * tensors into L2 (a later op's weights, fetched while this one waits on its

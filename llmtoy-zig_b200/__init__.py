@@ -42,6 +42,7 @@ EXPORTS = [
     "lt_ffn_block", "lt_greedy_step", "lt_scale", "lt_add_rmsnorm", "lt_norm_pair", "lt_ffn_tail", "lt_softcap",
     "lt_sample_step", "lt_rng_seed", "lt_quantize_q8_1", "lt_dequant_q8_1", "lt_moe_block_scaled",
     "lt_qmatvec_multi", "lt_noalloc_status", "lt_selftest_wait",
+    "lt_stack_create", "lt_stack_run", "lt_stack_free",
 ]
 
 
@@ -135,6 +136,9 @@ def load_library() -> ctypes.CDLL:
         "lt_moe_ffn_noalloc": (I, [P, P, P, P, U32, U32, U32, U64, U64, I, P, U32, P, P, U32, P]),
         "lt_noalloc_status": (I, [P]),
         "lt_selftest_wait": (I, [P, U32, U32]),
+        "lt_stack_create": (I, [P, P, U32, P, U32, U32, I, I, F, ctypes.POINTER(P)]),
+        "lt_stack_run": (I, [P, P, P, P]),
+        "lt_stack_free": (I, [P, P]),
         "lt_ep_dispatch": (I, [P, P, U32, U32, U32, U32, P, P, P, P]),
         "lt_gather_rows": (I, [P, P, U64, P, U32, P]),
         "lt_moe_combine": (I, [P, P, U64, P, P, U32, U32, P, P]),

@@ -56,6 +56,13 @@ struct lt_graph {
     cudaGraphExec_t exec;
 };
 
+struct lt_stack {
+    lt::StackParams p;
+    void *dev_layers = nullptr;  // lt::StackLayerDev[n_layers]
+    uint8_t *scratch = nullptr;  // activations between phases, then the zeroed sync block
+    size_t scratch_bytes = 0;
+};
+
 namespace {
 
 lt_status fail(lt_ctx *ctx, lt_status st, const char *fmt, ...) {
@@ -966,6 +973,113 @@ lt_status lt_attn_block_split(lt_ctx *ctx, const lt_attn_cfg *cfg, const float *
     return attn_block_impl(ctx, "lt_attn_block_split", cfg, dev_x, dev_norm_w, eps, seg, wv ? 3 : 2, dev_qkv_bias,
                            dev_q_norm, dev_k_norm, dev_pos, dev_k_cache, dev_v_cache, wo, dev_post_norm, tail,
                            dev_out);
+}
+
+// ── whole-stack decode ──────────────────────────────────────────────────────
+
+lt_status lt_stack_create(lt_ctx *ctx, const lt_attn_cfg *cfg, uint32_t d_model, const lt_stack_layer *layers,
+                          uint32_t n_layers, uint32_t k, int act, int norm_topk, float eps, lt_stack **out) {
+    lt_status st = enter_uncaptured(ctx, "lt_stack_create");
+    if (st != LT_OK) return st;
+    if (!out || !layers || n_layers == 0) return fail(ctx, LT_EINVAL, "lt_stack_create: bad argument");
+    *out = nullptr;
+    lt::AttnGeom g;
+    if ((st = attn_geom(ctx, cfg, g, "lt_stack_create")) != LT_OK) return st;
+    if (act != LT_ACT_SILU && act != LT_ACT_GELU_TANH) return fail(ctx, LT_EINVAL, "lt_stack_create: act %d", act);
+    const uint32_t nq = g.n_heads * g.hd, nkv = g.n_kv * g.hd;
+    const lt_stack_layer &f = layers[0];
+    const bool dense = f.router == nullptr;
+    if (!f.wqkv || !f.wo || !f.gate || !f.up || !f.down)
+        return fail(ctx, LT_EINVAL, "lt_stack_create: layer 0 lacks a tensor");
+    lt::StackParams p{};
+    p.g = g;
+    p.d = d_model;
+    p.dense = dense ? 1 : 0;
+    p.E = dense ? 1 : (uint32_t)f.gate->m.n_experts;
+    p.k = dense ? 1 : k;
+    p.F = (uint32_t)f.gate->m.rows;
+    p.norm_topk = norm_topk ? 1 : 0;
+    p.act = act;
+    p.eps = eps;
+    p.n_layers = n_layers;
+    p.qtype = f.wqkv->m.type;
+    p.otype = f.wo->m.type;
+    p.gtype = f.gate->m.type;
+    p.dtype = f.down->m.type;
+    p.qpitch = f.wqkv->m.pitch;
+    p.opitch = f.wo->m.pitch;
+    p.gpitch = f.gate->m.pitch;
+    p.dpitch = f.down->m.pitch;
+    std::vector<lt::StackLayerDev> dl(n_layers);
+    for (uint32_t l = 0; l < n_layers; l++) {
+        const lt_stack_layer &L = layers[l];
+        auto same = [](const lt_tensor *t, uint32_t type, uint64_t rows, uint64_t cols, uint32_t E, uint64_t pitch) {
+            return t && t->m.type == type && t->m.rows == rows && t->m.cols == cols && t->m.n_experts == E &&
+                   t->m.pitch == pitch;
+        };
+        bool ok = same(L.wqkv, p.qtype, nq + 2 * nkv, d_model, 0, p.qpitch) &&
+                  same(L.wo, p.otype, d_model, nq, 0, p.opitch) && L.attn_norm && L.ffn_norm && L.k_cache && L.v_cache &&
+                  (L.router == nullptr) == dense &&
+                  same(L.gate, p.gtype, p.F, d_model, dense ? 0 : p.E, p.gpitch) &&
+                  same(L.up, p.gtype, p.F, d_model, dense ? 0 : p.E, p.gpitch) &&
+                  same(L.down, p.dtype, d_model, p.F, dense ? 0 : p.E, p.dpitch);
+        if (ok && !dense) ok = L.router->m.type == LT_TYPE_F32 && L.router->m.rows == p.E &&
+                               L.router->m.cols == d_model && L.router->m.pitch == (uint64_t)d_model * 4;
+        if (!ok) return fail(ctx, LT_EINVAL, "lt_stack_create: layer %u differs from layer 0 or lacks a tensor", l);
+        lt::StackLayerDev &o = dl[l];
+        o.wqkv = L.wqkv->m.data;
+        o.wo = L.wo->m.data;
+        o.attn_norm = L.attn_norm;
+        o.ffn_norm = L.ffn_norm;
+        o.q_norm = L.q_norm;
+        o.k_norm = L.k_norm;
+        o.bias = L.qkv_bias;
+        o.kc = L.k_cache;
+        o.vc = L.v_cache;
+        o.router = dense ? nullptr : reinterpret_cast<const float *>(L.router->m.data);
+        o.gate = L.gate->m.data;
+        o.up = L.up->m.data;
+        o.down = L.down->m.data;
+    }
+    size_t smem = 0, scratch = 0, sync_off = 0;
+    if (!lt::stack_plan(p, ctx->num_sms, &smem, &scratch, &sync_off))
+        return fail(ctx, LT_EUNSUPPORTED_TYPE, "lt_stack_create: shape or types outside the stack kernel");
+    lt_stack *s = new (std::nothrow) lt_stack;
+    if (!s) return fail(ctx, LT_ENOMEM, "lt_stack_create: host allocation");
+    s->p = p;
+    s->scratch_bytes = scratch;
+    cudaError_t e = cudaMalloc(&s->dev_layers, sizeof(lt::StackLayerDev) * n_layers);
+    if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void **>(&s->scratch), scratch);
+    if (e == cudaSuccess) e = cudaMemsetAsync(s->scratch, 0, scratch, ctx->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(s->dev_layers, dl.data(), sizeof(lt::StackLayerDev) * n_layers, cudaMemcpyHostToDevice,
+                            ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) {
+        if (s->dev_layers) cudaFree(s->dev_layers);
+        if (s->scratch) cudaFree(s->scratch);
+        delete s;
+        return cuda_fail(ctx, e, "lt_stack_create");
+    }
+    *out = s;
+    return LT_OK;
+}
+
+lt_status lt_stack_run(lt_ctx *ctx, const lt_stack *s, float *dev_x, const uint32_t *dev_pos) {
+    lt_status st = enter(ctx);
+    if (st != LT_OK) return st;
+    if (!s || !dev_x || !dev_pos) return fail(ctx, LT_EINVAL, "lt_stack_run: bad argument");
+    return launched(ctx, lt::launch_stack(cfg_of(ctx), s->p, s->dev_layers, dev_x, dev_pos, s->scratch), "stack");
+}
+
+lt_status lt_stack_free(lt_ctx *ctx, lt_stack *s) {
+    if (!s) return LT_OK;
+    if (ctx) cudaSetDevice(ctx->device);
+    if (ctx) cudaStreamSynchronize(ctx->stream);
+    cudaFree(s->dev_layers);
+    cudaFree(s->scratch);
+    delete s;
+    return LT_OK;
 }
 
 void lt_rng_seed(uint64_t seed, uint64_t state_out[4]) {

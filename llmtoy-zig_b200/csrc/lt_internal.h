@@ -253,6 +253,34 @@ constexpr size_t kDecodeSmemLimit = 227 * 1024;
 bool moe_decode_fits(const DecodeParams &p, int num_sms);
 cudaError_t launch_moe_decode(const LaunchCfg &c, const DecodeParams &p);
 
+// Every decoder layer of one token in one persistent kernel (lt_stack.cu):
+// attention (stacked Q8_0 Q/K/V rows, optional bias and Q/K norms, RoPE,
+// f32/f16 KV, Q8_0 wo) and a Q4_K MoE or Q8_0 dense SwiGLU FFN per layer,
+// x updated in place.  One descriptor per layer, in device memory.
+struct StackLayerDev {
+    const uint8_t *wqkv, *wo;
+    const float *attn_norm, *ffn_norm, *q_norm, *k_norm, *bias;
+    void *kc, *vc;
+    const float *router;              // nullptr: a dense FFN (gate/up/down are 2-D)
+    const uint8_t *gate, *up, *down;  // up == nullptr: fused gate_up
+};
+struct StackParams {
+    AttnGeom g;
+    uint32_t d, E, k, F;
+    int norm_topk, act, dense;
+    float eps;
+    uint32_t n_layers;
+    uint32_t qtype, otype, gtype, dtype;
+    uint64_t qpitch, opitch, gpitch, dpitch;
+};
+constexpr size_t kStackSyncBytes = 8192;
+// Whether the stack kernel takes this shape: its shared memory and global
+// scratch bytes (the sync block at sync_offset must be zeroed once, before
+// the first launch, and used by no other kernel).
+bool stack_plan(const StackParams &p, int num_sms, size_t *smem, size_t *scratch_bytes, size_t *sync_offset);
+cudaError_t launch_stack(const LaunchCfg &c, const StackParams &p, const void *dev_layers, float *x,
+                         const uint32_t *pos, uint8_t *scratch);
+
 // out[t] = (resid ? resid[t] : 0) + sum_s w[t][s] * y[pair_pos[t*k + s]]  (slot order), D columns.
 cudaError_t launch_combine(const LaunchCfg &c, const float *y, uint64_t D, const uint32_t *pair_pos, const float *w,
                            uint32_t ntok, uint32_t k, const float *resid, float *out);

@@ -11,6 +11,7 @@
 //   logits = lm_head rmsnorm(x); tokens[pos+1] = greedy; pos++ (:314-316)
 #include "decoder.h"
 
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <vector>
@@ -38,6 +39,7 @@ struct lth_decoder {
     bool warmed = false;
     lt_sample_params sampling{0.0f, 0, 1.0f};  // temperature 0: greedy
     uint64_t *rng = nullptr;                   // xoshiro256++ state (device)
+    lt_stack *stack = nullptr;                 // all layers in one launch, when the kernel takes the shape
 };
 
 namespace {
@@ -132,6 +134,8 @@ lt_status step(lth_decoder *d, bool logits) {
         for (uint32_t l = 0; l < m.n_layers; l++) LTH_TRY(gemma_layer(d, l));
         const lt_ffn_tail_in t = gemma_tail(d, m.n_layers - 1);
         LTH_TRY(lt_ffn_tail(d->ctx, t.dev_f, t.dev_w1, d->mbuf, t.dev_w2, t.dev_w, t.los, t.eps, m.d_model, 1, d->x));
+    } else if (d->stack) {
+        LTH_TRY(lt_stack_run(d->ctx, d->stack, d->x, d->state));
     } else {
         for (uint32_t l = 0; l < m.n_layers; l++) LTH_TRY(layer_step(d, l));
     }
@@ -146,7 +150,40 @@ lt_status step(lth_decoder *d, bool logits) {
     return lt_greedy_step(d->ctx, d->logits, m.vocab, d->tokens, d->state, d->state + 1);
 }
 
+// The whole-stack kernel for a LTH_LLAMA model whose layers it takes (stacked
+// Q/K/V, same FFN kind and types everywhere); LLMTOY_STACK=0 keeps the
+// per-layer kernels.  Any refusal leaves d->stack null: the per-layer path runs.
+void try_stack(lth_decoder *d) {
+    const lth_model &m = d->m;
+    const char *env = getenv("LLMTOY_STACK");
+    if (m.family != LTH_LLAMA || (env && env[0] == '0')) return;
+    std::vector<lt_stack_layer> sl(m.n_layers);
+    for (uint32_t l = 0; l < m.n_layers; l++) {
+        const lth_layer &L = d->layers[l];
+        if (!L.wqkv) return;
+        lt_stack_layer &o = sl[l];
+        o.wqkv = L.wqkv;
+        o.wo = L.wo;
+        o.attn_norm = L.attn_norm;
+        o.ffn_norm = L.ffn_norm;
+        o.q_norm = L.q_norm;
+        o.k_norm = L.k_norm;
+        o.qkv_bias = L.qkv_bias;
+        o.k_cache = d->kcache + d->kv_off[l] * d->kv_esize;
+        o.v_cache = d->vcache + d->kv_off[l] * d->kv_esize;
+        o.router = L.router;
+        o.gate = L.router ? L.exp_gate : L.ffn_gate;
+        o.up = L.router ? L.exp_up : L.ffn_up;
+        o.down = L.router ? L.exp_down : L.ffn_down;
+    }
+    lt_stack *s = nullptr;
+    if (lt_stack_create(d->ctx, &d->attn, m.d_model, sl.data(), m.n_layers, m.n_used, (int)m.act, (int)m.norm_topk,
+                        m.eps, &s) == LT_OK)
+        d->stack = s;
+}
+
 void release(lth_decoder *d) {
+    if (d->stack) lt_stack_free(d->ctx, d->stack);
     if (d->graph) lt_graph_free(d->ctx, d->graph);
     if (d->pgraph) lt_graph_free(d->ctx, d->pgraph);
     void *bufs[] = {d->x,    d->xb,     d->logits,    d->kcache, d->vcache,
@@ -213,6 +250,7 @@ lt_status lth_decoder_create(lt_ctx *ctx, const lth_model *m, lth_decoder **out)
         delete d;
         return st;
     }
+    try_stack(d);
     *out = d;
     return LT_OK;
 }
