@@ -59,6 +59,8 @@ def load_host_library() -> ctypes.CDLL:
         "lth_decoder_step": (I, [P]),
         "lth_decoder_capture": (I, [P]),
         "lth_decoder_replay": (I, [P, U32]),
+        "lth_decoder_run_layers": (I, [P]),
+        "lth_decoder_uses_stack": (I, [P]),
         "lth_decoder_logits": (P, [P]),
         "lth_decoder_tokens": (I, [P, P, U32]),
         "lth_generate": (I, [P, P, U32, U32, P]),
@@ -204,6 +206,14 @@ class Decoder:
 
     def replay(self, n_steps: int) -> None:
         self._check(self.lib.lth_decoder_replay(self.ptr, n_steps))
+
+    def run_layers(self) -> None:
+        """The decoder layers alone at the current position (no embedding, logits or advance)."""
+        self._check(self.lib.lth_decoder_run_layers(self.ptr))
+
+    @property
+    def uses_stack(self) -> bool:
+        return bool(self.lib.lth_decoder_uses_stack(self.ptr))
 
     def logits_ptr(self) -> int:
         return self.lib.lth_decoder_logits(self.ptr)

@@ -281,6 +281,16 @@ lt_status lth_decoder_step(lth_decoder *d) {
     return LT_OK;
 }
 
+lt_status lth_decoder_run_layers(lth_decoder *d) {
+    if (!d) return LT_EINVAL;
+    if (d->m.family != LTH_LLAMA) return LT_EINVAL;
+    if (d->stack) return lt_stack_run(d->ctx, d->stack, d->x, d->state);
+    for (uint32_t l = 0; l < d->m.n_layers; l++) LTH_TRY(layer_step(d, l));
+    return LT_OK;
+}
+
+int lth_decoder_uses_stack(const lth_decoder *d) { return d && d->stack ? 1 : 0; }
+
 lt_status lth_decoder_capture(lth_decoder *d) {
     if (!d) return LT_EINVAL;
     if (d->graph) return LT_OK;

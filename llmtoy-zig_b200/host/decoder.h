@@ -81,6 +81,12 @@ lt_status lth_decoder_step(lth_decoder *d);
  * step, and the prompt step without the output norm, lm_head and sampling
  * (main.zig:1916-1919 asks for logits only at the last prompt position). */
 lt_status lth_decoder_capture(lth_decoder *d);
+/* LTH_LLAMA only: the decoder layers alone at the current position (no
+ * embedding, logits or position advance) -- x is updated in place and the
+ * layer caches' slot at the position rewritten.  For timing the layer stack. */
+lt_status lth_decoder_run_layers(lth_decoder *d);
+/* 1 when the steps run every layer in one launch (lt_stack_run), else 0. */
+int lth_decoder_uses_stack(const lth_decoder *d);
 /* Replay n_steps steps (asynchronous): the prompt graph while the next
  * position is still a prompt position, the full step after. */
 lt_status lth_decoder_replay(lth_decoder *d, uint32_t n_steps);
