@@ -1,24 +1,29 @@
-"""Benchmark: batch-1 MoE decode through a stack of config-1 MoE layers.
+"""Benchmark: batch-1 greedy decode of the Qwen3-30B-A3B-shaped MoE model (config 2).
 
-Workload (T=1): one token through L=48 chained MoE
-FFN layers of the Qwen3-30B-A3B shape -- d_model 2048, 128 experts, top-8 with
-renormalised softmax, SwiGLU expert width 768, Q4_K experts, f32 router --
-each layer the pre-norm residual MoE block x <- x + moe(rmsnorm(x))
-(src/model/forward.zig:304-309 with the FFN replaced by the MoE; one
-lt_moe_block call per layer, which at one token is a single persistent kernel:
-norm, router, top-k, gate/up, down, combine and residual).
-48 distinct weight sets (16.3 GB) make every
-step read ~1.07 GB of weights, far more than the 126 MB L2, so no flush is
-needed.  Weights are seeded synthetic bytes with the config's distributions,
-generated on the device.
+Headline workload (the north star's target): 48
+layers, d_model 2048, 32 query / 4 KV heads of 128, QK-RMSNorm, NeoX RoPE,
+128 Q4_K experts top-8 renormalised (SwiGLU 768), Q8_0 attention, Q6_K
+lm_head over 151936 tokens, an f16 KV cache of 4096 positions; a 32-token
+seeded prompt, then 128 greedy tokens.  Weights are seeded synthetic bytes
+with the config's distributions, generated on the device (48 distinct layers,
+2.3 GB read per token, far beyond the 126 MB L2: no flush needed).
+
+One bench step = one generation of that workload: 159 decode steps (the 32
+prompt tokens and 127 sampled ones, each one token through the model, as the
+reference's generate loop runs them), replayed as one captured CUDA graph per
+token through the C++ host loop (llmtoy-zig_b200/host/decoder.cpp), whose
+layers run as one persistent kernel per token (lt_stack_run).  value = decode
+steps per second of device time; e2e = the same through lth_generate with the
+prompt ids copied in and the token ids copied out every generation.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-One JSON line on rank 0.  `value` is device time of CUDA-graph replays (one
-graph per token, captured through the C ABI); `e2e` adds the per-token
-host->device copy of the input and device->host read of the output through
-the same API.  `--impl reference` times the CPU restatement of the reference
-path (oracle/, C, all host threads) on the same workload.
+N > 1: N independent replicas (batch-1 decode does not shard; weak scaling),
+and the expert-parallel prefill line (config 4) shards its experts over the N
+ranks.  `--impl reference` times the CPU restatement of the reference path
+(oracle/, C, all host threads, built for the host CPU) on the same config-2
+workload.  Extra keys: the config-1 MoE layer stack (T=1, 16 and 512), the
+config-0 and config-3 decodes, and config 4.
 """
 from __future__ import annotations
 
@@ -43,7 +48,7 @@ D_MODEL, N_EXPERTS, TOP_K, D_EXPERT = 2048, 128, 8, 768
 Q4K_ROW = lambda cols: (cols // 256) * 144  # noqa: E731
 EXPERT_BYTES = 2 * D_EXPERT * Q4K_ROW(D_MODEL) + D_MODEL * Q4K_ROW(D_EXPERT)  # 2,654,208
 ROUTER_BYTES = N_EXPERTS * D_MODEL * 4
-METRIC = "MoE decode tok/s (config-1 MoE layer, T=1, 48-layer stack)"
+METRIC = "MoE decode tok/s (config 2: Qwen3-30B-A3B-shaped MoE, batch-1 greedy decode)"
 
 
 def env_rank():
@@ -192,87 +197,101 @@ class DeviceLayer:
         self.norm = torch.ones(D_MODEL, device="cuda")
 
 
-# ── CPU restatement (oracle) on the same workload ────────────────────────────
 
-class CpuStack:
-    """The reference CPU path (C restatement in oracle/, all host threads)
-    through n_layers MoE layers, cycling `distinct` host weight sets (each
-    340 MB, far beyond the CPU caches)."""
+# ── CPU restatement (oracle) on the same workloads ───────────────────────────
 
-    def __init__(self, n_layers: int, distinct: int = 4, seed: int = 0):
-        sys.path.insert(0, str(REPO / "tests"))
-        self.oracle = importlib.import_module("oracle_lib")
+NATIVE_FLAGS = "gcc -O3 -march=native -ffp-contract=off -fno-fast-math"
+
+
+def oracle_module():
+    """The CPU oracle's binding, built for this host's CPU (-march=native,
+    as `zig build -Doptimize=ReleaseFast` targets the native CPU) when that
+    build succeeds here, else the portable build; returns (module, flags).
+    Both builds give the same bits: -ffp-contract=off and no fast-math keep
+    every rounding of the restated Zig code."""
+    sys.path.insert(0, str(REPO / "tests"))
+    oracle = importlib.import_module("oracle_lib")
+    flags = "gcc -O3 -march=x86-64-v2 -ffp-contract=off -fno-fast-math (portable build)"
+    if oracle._lib is None:
+        r = subprocess.run(["make", "-s", "-C", str(REPO / "oracle"), "native"], capture_output=True, text=True)
+        native = REPO / "oracle" / "liboracle_native.so"
+        if r.returncode == 0 and native.exists():
+            oracle.use_library(native)
+            flags = NATIVE_FLAGS
+    elif str(oracle.LIB).endswith("liboracle_native.so"):
+        flags = NATIVE_FLAGS
+    oracle.lib()
+    return oracle, flags
+
+
+class CpuModel:
+    """The reference CPU path (C restatement in oracle/, all host threads) on
+    the config-2 model: forwardOneModel per token, 4 distinct host layer
+    weight sets cycled through the 48 layers (each ~360 MB, far beyond the CPU
+    caches), full vocabulary, f16-rounded KV values (the config's cache)."""
+
+    def __init__(self, name: str = "config2"):
+        self.oracle, self.flags = oracle_module()
         synth = importlib.import_module("llmtoy-zig_b200.synth")
-        rng = np.random.Generator(np.random.PCG64(synth.config_seed(1) + seed))
-        self.layers = [synth.MoeLayer(rng, D_MODEL, N_EXPERTS, D_EXPERT) for _ in range(distinct)]
-        self.norm = np.ones(D_MODEL, np.float32)
-        self.n_layers, self.distinct = n_layers, distinct
+        rng = np.random.Generator(np.random.PCG64(synth.config_seed(2 if name == "config2" else 0)))
+        L = MODEL_CFG[name][0]
+        m = synth.config2_model(rng, n_layers=4) if name == "config2" else synth.config0_model(rng, n_layers=4)
+        self.m = synth.cycle_layers(m, L)
         self.threads = os.cpu_count() or 1
         self.pool = self.oracle.Pool(self.threads)
-        self.x = rng.normal(0, 1, size=(1, D_MODEL)).astype(np.float32)
+        self.dec = self.oracle.OracleDecoder(self.m, 4096, self.pool, kv_f16=name == "config2")
+        self.prompt = np.random.Generator(np.random.PCG64(0x11A70000 + (2 if name == "config2" else 0))) \
+            .integers(0, self.m.vocab, 32).tolist()
+        self.pos = 0
 
-    def token(self) -> None:
-        L = self.oracle.lib()
-        xx = self.x
-        for li in range(self.n_layers):
-            xn = np.empty_like(xx)
-            L.orc_rmsnorm(xn.ctypes.data, xx.ctypes.data, self.norm.ctypes.data, D_MODEL, 1e-6)
-            y, _, _ = self.oracle.moe_layer(self.layers[li % self.distinct], xn, TOP_K, True, 0, None, self.pool)
-            xx = (xx + y).astype(np.float32)
-        self.x = xx
-
-    def rate(self, budget_s: float, min_tokens: int = 1):
-        t0 = time.perf_counter()
-        n = 0
-        while n < min_tokens or time.perf_counter() - t0 < budget_s:
-            self.token()
-            n += 1
-        dt = time.perf_counter() - t0
-        return n / dt, n, dt
+    def tokens(self, n: int) -> None:
+        """n decode steps of the workload, positions cycling over its 159."""
+        for _ in range(n):
+            tok = self.prompt[self.pos] if self.pos < len(self.prompt) else (7 * self.pos) % self.m.vocab
+            self.dec.step(tok, self.pos)
+            self.pos = (self.pos + 1) % 159
 
     def close(self) -> None:
         self.pool.close()
 
 
-def cpu_decode_rate(n_layers: int, budget_s: float):
-    s = CpuStack(n_layers)
-    s.token()  # warm
-    rate, n, dt = s.rate(budget_s)
-    s.close()
-    return rate, n, dt, s.threads, s.distinct
+REF_TOKENS_PER_STEP = 8
 
 
 def run_reference(args) -> None:
     rank, world, _ = env_rank()
     if rank != 0:
         return
-    # per step: one token through the L-layer stack on the CPU restatement
-    s = CpuStack(args.layers)
-    s.rate(0.0, min_tokens=args.warmup)
-    rate, n, dt = s.rate(0.0, min_tokens=args.steps)
-    threads, distinct = s.threads, s.distinct
+    # per step: a bounded sample of the config-2 workload, 8 decode steps
+    s = CpuModel()
+    s.tokens(REF_TOKENS_PER_STEP * args.warmup)
+    t0 = time.perf_counter()
+    s.tokens(REF_TOKENS_PER_STEP * args.steps)
+    dt = time.perf_counter() - t0
     s.close()
+    n = REF_TOKENS_PER_STEP * args.steps
+    rate = n / dt
     line = {
-        "metric": METRIC, "value": rate, "unit": "tok/s", "n_gpus": args.gpus, "steps": n, "warmup": args.warmup,
-        "ms_per_step": 1e3 * dt / n, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic (seeded, config-1 distributions)", "impl": "reference",
-        "config": config_block(args, world),
-        "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": f"{n} tokens x {args.layers} layers, {distinct} distinct host weight sets "
-                                   f"cycled (C restatement of the Zig CPU path; zig absent)"},
+        "metric": METRIC, "value": rate, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (Q8_0/Q4_K/Q6_K weights dequantised per row)",
+        "data": "synthetic (seeded, config-2 distributions)", "impl": "reference", "config": config_block(args, world),
+        "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": s.threads, "kind": "port", "build": s.flags,
+                         "sample": f"{n} decode steps of the 48-layer config-2 model (positions cycling over the "
+                                   f"workload's 159, {REF_TOKENS_PER_STEP} per step), 4 distinct layer weight sets "
+                                   f"cycled; C restatement of forwardOneModel (zig absent)"},
         "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 def config_block(args, world: int) -> dict:
-    return {"workload": f"config-1 MoE layer (d_model {D_MODEL}, {N_EXPERTS} experts, top-{TOP_K} renormalised, "
-                        f"SwiGLU {D_EXPERT}, Q4_K experts, f32 router), T=1 decode, {args.layers} chained layers "
-                        f"x <- x + moe(rmsnorm(x))",
-            "model": "qwen3-30b-a3b MoE stack (synthetic)", "global_batch": world, "seq_len": 1,
-            "layers": args.layers, "parallelism": f"replicas x{world}" if world > 1 else "single",
-            "l2": f"inputs larger than L2: {args.layers} distinct layers, "
-                  f"{args.layers * (TOP_K * EXPERT_BYTES + ROUTER_BYTES) / 1e9:.2f} GB read per step"}
+    return {"workload": "config 2: Qwen3-30B-A3B-shaped MoE model, batch-1 greedy decode -- 48 layers, d_model 2048, "
+                        "32/4 heads of 128, QK-RMSNorm, NeoX RoPE, 128 Q4_K experts top-8 renormalised (SwiGLU 768), "
+                        "Q8_0 attention, Q6_K lm_head (vocab 151936), f16 KV of 4096 positions; 32-token prompt + "
+                        "128 greedy tokens = 159 decode steps per bench step",
+            "global_batch": world, "seq_len": 160, "parallelism": f"replicas x{world}" if world > 1 else "single",
+            "l2": "inputs larger than L2: 48 distinct layers, ~2.3 GB of weights read per decode step"}
 
 
 # ── our path ─────────────────────────────────────────────────────────────────
@@ -280,22 +299,20 @@ def config_block(args, world: int) -> dict:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=5, help="generations of the config-2 workload (159 decode steps each)")
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline work (rank 0, N=1)")
-    ap.add_argument("--profile-steps", type=int, default=5)
-    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline work per line (rank 0, N=1)")
     ap.add_argument("--prefill-tokens", default="16,512",
                     help="comma list of T for the multi-token MoE layer measurement (config 1's T=16 and 512; 0: skip)")
     ap.add_argument("--prefill-layers", type=int, default=8)
     ap.add_argument("--ep-tokens", type=int, default=8 * 2048,
                     help="config 4: prompt tokens over all ranks, experts sharded 128/N (0: skip)")
     ap.add_argument("--ep-layers", type=int, default=2)
-    ap.add_argument("--model-tokens", type=int, default=128,
-                    help="configs 2 and 0: greedy tokens after a 32-token prompt (0: skip)")
-    ap.add_argument("--models", default="config2,config0,config3", help="whole-model decode lines to run")
+    ap.add_argument("--model-tokens", type=int, default=128, help="greedy tokens after the prompt (configs 2 and 0)")
+    ap.add_argument("--models", default="config0,config3", help="extra whole-model decode lines")
+    ap.add_argument("--moe-stack", type=int, default=1, help="the config-1 MoE layer stack line (0: skip)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -323,145 +340,24 @@ def main() -> None:
     layers = [DeviceLayer(pkg, ctx, torch, gen) for _ in range(args.layers)]
     torch.cuda.synchronize()
 
-    x0 = torch.randn(1, D_MODEL, device="cuda", generator=gen)
-    xa = torch.empty(1, D_MODEL, device="cuda")
+    # ---- headline: config-2 whole-model greedy decode ----
+    head = measure_model_decode(args, pkg, ctx, torch, stream, layers, rank, world, dist, "config2",
+                                runs=args.steps, warm=args.warmup, headline=True)
 
-    def step():
-        for L in layers:  # in place: xa <- xa + moe(rmsnorm(xa))
-            ctx.moe_block(L.router, L.gate, L.up, L.down, pkg.ACT_SILU, True, None, L.norm, 1e-6, xa, 1, TOP_K, xa)
-        return xa
+    moe_stack = measure_moe_stack(args, pkg, ctx, torch, stream, layers, rank, world, dist) if args.moe_stack else None
 
-    with torch.cuda.stream(stream):
-        xa.copy_(x0)
-    out_buf = step()  # eager warm-up (and the buffer that holds each step's result)
-    ctx.sync()
-    graph = None
-    if not args.no_graph:
-        ctx.capture_begin()
-        step()
-        graph = ctx.capture_end()
-
-    def run_step():
-        if graph is not None:
-            graph.launch()
-        else:
-            step()
-
-    def barrier():
-        if dist is not None:
-            t = torch.zeros(1, device="cuda")
-            dist.all_reduce(t)
-        torch.cuda.synchronize()
-
-    def max_over_ranks(v: float) -> float:
-        if dist is None:
-            return v
-        t = torch.tensor([v], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    # ---- device-timed throughput (value) ----
-    for _ in range(args.warmup):
-        run_step()
-    barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            run_step()
-        ev1.record(stream)
-        stream.synchronize()
-    barrier()
-    ms = max_over_ranks(ev0.elapsed_time(ev1))
-    clocks = clk.summary()
-    ms_step = ms / args.steps
-    value = world * args.steps / (ms / 1e3)
-
-    # ---- end to end: host input -> device -> host result, every step ----
-    x_host = torch.randn(1, D_MODEL, generator=torch.Generator().manual_seed(7)).pin_memory()
-    y_host = torch.empty(1, D_MODEL).pin_memory()
-    for _ in range(args.warmup):
-        with torch.cuda.stream(stream):
-            xa.copy_(x_host, non_blocking=True)
-        run_step()
-        with torch.cuda.stream(stream):
-            y_host.copy_(out_buf, non_blocking=True)
-        stream.synchronize()
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        with torch.cuda.stream(stream):
-            xa.copy_(x_host, non_blocking=True)
-        run_step()
-        with torch.cuda.stream(stream):
-            y_host.copy_(out_buf, non_blocking=True)
-        stream.synchronize()
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
-    barrier()
-    e2e = {"value": world * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": D_MODEL * 4,
-           "d2h_bytes_per_step": D_MODEL * 4, "ms_per_step": 1e3 * e2e_s / args.steps,
-           "path": "C ABI graph replay (lt_graph_launch) with pinned host input/output copies"}
-
-    # ---- per-kernel timing (profiler on, eager launches) ----
-    ctx.profile(True)
-    ctx.profile_reset()
-    for _ in range(args.profile_steps):
-        step()
-    ctx.sync()
-    prof = ctx.profile_read()
-    ctx.profile(False)
-
-    peak, peak_kind = measured_peaks()
-    roofline = None
-    tr = ncu_traffic()
-    if prof.get("moe_decode", {}).get("count"):
-        # one launch = the whole block: router rows, 8 experts' gate/up/down
-        # rows, norm weights, x in and out
-        kname = "moe_decode"
-        kbytes = TOP_K * EXPERT_BYTES + ROUTER_BYTES + 3 * D_MODEL * 4
-    else:
-        kname = "moe_gate_up_q4k"
-        kbytes = TOP_K * 2 * D_EXPERT * Q4K_ROW(D_MODEL) + D_MODEL * 4 + TOP_K * D_EXPERT * 4
-    kp = prof.get(kname)
-    if kp and kp["count"]:
-        k_ms = kp["total_ms"] / kp["count"]
-        achieved = kbytes / (k_ms / 1e3) / 1e9
-        traffic = tr.get(kname, {}).get("dram_bytes_per_launch") if tr else None
-        roofline = {"kernel": kname, "bound": "hbm", "achieved": achieved, "peak": peak,
-                    "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
-                    "algorithmic_bytes_per_launch": kbytes, "avg_launch_ms": k_ms, "traffic": traffic}
-    launches_per_step = sum(v["count"] for v in prof.values()) / max(1, args.profile_steps)
-    step_bytes = args.layers * (TOP_K * EXPERT_BYTES + ROUTER_BYTES)
-    kernels = {k: {"count": v["count"], "avg_us": 1e3 * v["total_ms"] / max(1, v["count"])} for k, v in prof.items()}
-    layer_bytes = TOP_K * EXPERT_BYTES + ROUTER_BYTES
-
-    cpu = None
-    if rank == 0 and world == 1 and args.cpu_budget > 0:
-        rate, n, dt, threads, distinct = cpu_decode_rate(args.layers, args.cpu_budget)
-        cpu = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
-               "sample": f"{n} tokens x {args.layers} layers in {dt:.1f}s, {distinct} distinct host weight sets "
-                         f"cycled (C restatement of the Zig CPU path; zig absent)"}
-
-    if graph is not None:
-        graph.free()
-        graph = None
-
-    # ---- prefill: T tokens through the MoE blocks (tensor-core expert GEMM) ----
     prefill = None
     t_list = [int(t) for t in str(args.prefill_tokens).split(",") if int(t) > 0]
     if t_list:
         prefill = {f"T={T}": measure_prefill(args, pkg, ctx, torch, stream, gen, layers, rank, world, dist, T)
                    for T in t_list}
 
-    model_decode = None
-    if args.model_tokens > 0:
-        model_decode = {}
-        for name in [m for m in args.models.split(",") if m]:
-            if name == "config3":
-                model_decode[name] = measure_gemma_decode(args, pkg, ctx, torch, stream, rank, world, dist)
-            else:
-                model_decode[name] = measure_model_decode(args, pkg, ctx, torch, stream, layers, rank, world, dist,
-                                                          name)
+    model_decode = {}
+    for name in [m for m in args.models.split(",") if m]:
+        if name == "config3":
+            model_decode[name] = measure_gemma_decode(args, pkg, ctx, torch, stream, rank, world, dist)
+        else:
+            model_decode[name] = measure_model_decode(args, pkg, ctx, torch, stream, layers, rank, world, dist, name)
 
     ep_prefill = None
     if args.ep_tokens > 0:
@@ -469,17 +365,18 @@ def main() -> None:
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "q4_k weights x int16 activations (dp2a), f32 accumulate",
-            "data": "synthetic (seeded, config-1 distributions, generated on device)",
+            "metric": METRIC, "value": head["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q4_k/q8_0/q6_k weights x int16+int8 activations (dp2a/dp4a), f32 accumulate",
+            "data": "synthetic (seeded, config-2 distributions, generated on device)",
             "config": config_block(args, world),
-            "expert_hbm_gbs": step_bytes / (ms_step / 1e3) / 1e9,
-            "hbm_frac_of_step": (step_bytes / (ms_step / 1e3) / 1e9) / peak,
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": int(round(args.steps * launches_per_step)), "clocks": clocks,
-            "kernels_profiled": kernels, "layer_bytes": layer_bytes,
-            "graph": not args.no_graph, "prefill": prefill, "model_decode": model_decode,
+            "ms_per_token": head["ms_per_token"], "decode_steps_per_step": head["steps_per_run"],
+            "roofline": head["roofline"], "step_roofline": head["step_roofline"],
+            "cpu_baseline": head.get("cpu_baseline"), "e2e": head["e2e"],
+            "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
+            "stack_kernel": head["uses_stack"], "deterministic_stream": head["deterministic_stream"],
+            "kernels_per_token": head["kernels_per_token"],
+            "moe_layer_stack": moe_stack, "prefill": prefill, "model_decode": model_decode,
             "ep_prefill": ep_prefill,
         }
         print(json.dumps(line), flush=True)
@@ -490,6 +387,102 @@ def main() -> None:
     ctx.close()
     if dist is not None:
         dist.destroy_process_group()
+
+
+def _barrier(torch, dist):
+    if dist is not None:
+        t = torch.zeros(1, device="cuda")
+        dist.all_reduce(t)
+    torch.cuda.synchronize()
+
+
+def _max_over_ranks(torch, dist, v: float) -> float:
+    if dist is None:
+        return v
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def measure_moe_stack(args, pkg, ctx, torch, stream, layers, rank, world, dist) -> dict:
+    """Config 1 at T=1: one token through the 48 chained MoE layers
+    x <- x + moe(rmsnorm(x)) (one lt_moe_block per layer, a single persistent
+    kernel each), replayed as one CUDA graph; 20 timed replays after the
+    warm-up.  value = tokens per second through the 48-layer stack."""
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(0x11A70101 + 1000 * rank)
+    x0 = torch.randn(1, D_MODEL, device="cuda", generator=gen)
+    xa = torch.empty(1, D_MODEL, device="cuda")
+
+    def step():
+        for L in layers:  # in place: xa <- xa + moe(rmsnorm(xa))
+            ctx.moe_block(L.router, L.gate, L.up, L.down, pkg.ACT_SILU, True, None, L.norm, 1e-6, xa, 1, TOP_K, xa)
+
+    with torch.cuda.stream(stream):
+        xa.copy_(x0)
+    step()
+    ctx.sync()
+    ctx.capture_begin()
+    step()
+    graph = ctx.capture_end()
+    reps = 20
+    for _ in range(args.warmup):
+        graph.launch()
+    _barrier(torch, dist)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(reps):
+        graph.launch()
+    ev1.record(stream)
+    stream.synchronize()
+    ms = _max_over_ranks(torch, dist, ev0.elapsed_time(ev1)) / reps
+    graph.free()
+    n = len(layers)
+    kbytes = TOP_K * EXPERT_BYTES + ROUTER_BYTES + 3 * D_MODEL * 4
+    peak, kind = measured_peaks()
+    achieved = kbytes / (ms / n / 1e3) / 1e9
+    out = {"metric": f"MoE decode tok/s (config-1 MoE layer, T=1, {n}-layer stack)", "value": world / (ms / 1e3),
+           "unit": "tok/s", "ms_per_token": ms, "layers": n,
+           "roofline": {"kernel": "moe_decode", "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                        "frac": achieved / peak, "peak_kind": kind, "algorithmic_bytes_per_launch": kbytes,
+                        "us_per_launch": 1e3 * ms / n,
+                        "note": "us_per_launch = graph replay time / launches (in-step, PDL hand-overs included)"}}
+    if rank == 0 and world == 1 and args.cpu_budget > 0:
+        out["cpu_baseline"] = cpu_stack_rate(n, min(args.cpu_budget, 10.0))
+    return out
+
+
+def cpu_stack_rate(n_layers: int, budget_s: float) -> dict:
+    """The CPU restatement through n_layers config-1 MoE layers, 4 distinct
+    host weight sets cycled, all host threads."""
+    oracle, flags = oracle_module()
+    synth = importlib.import_module("llmtoy-zig_b200.synth")
+    rng = np.random.Generator(np.random.PCG64(synth.config_seed(1)))
+    sets = [synth.MoeLayer(rng, D_MODEL, N_EXPERTS, D_EXPERT) for _ in range(4)]
+    norm = np.ones(D_MODEL, np.float32)
+    threads = os.cpu_count() or 1
+    pool = oracle.Pool(threads)
+    x = rng.normal(0, 1, size=(1, D_MODEL)).astype(np.float32)
+    L = oracle.lib()
+
+    def token(xx):
+        for li in range(n_layers):
+            xn = np.empty_like(xx)
+            L.orc_rmsnorm(xn.ctypes.data, xx.ctypes.data, norm.ctypes.data, D_MODEL, 1e-6)
+            y, _, _ = oracle.moe_layer(sets[li % 4], xn, TOP_K, True, 0, None, pool)
+            xx = (xx + y).astype(np.float32)
+        return xx
+
+    x = token(x)
+    t0 = time.perf_counter()
+    n = 0
+    while n < 1 or time.perf_counter() - t0 < budget_s:
+        x = token(x)
+        n += 1
+    dt = time.perf_counter() - t0
+    pool.close()
+    return {"value": n / dt, "unit": "tok/s", "cores": threads, "kind": "port", "build": flags,
+            "sample": f"{n} tokens x {n_layers} layers in {dt:.1f}s, 4 distinct host weight sets cycled"}
 
 
 def measure_prefill(args, pkg, ctx, torch, stream, gen, layers, rank, world, dist, T: int) -> dict:
@@ -578,31 +571,42 @@ MODEL_CFG = {
 }
 
 
-def model_bytes_per_token(name: str, ctx_len: float) -> float:
-    """Algorithmic HBM bytes of one decode step: every weight the token reads
-    (attention projections, router + 8 experts or the dense FFN, norms, the
-    embedding row, lm_head) plus the KV cache read at the mean context
-    (f16 elements for config 2, whose cache the config specifies as f16)."""
+def model_layer_bytes(name: str, ctx_len: float) -> float:
+    """Algorithmic HBM bytes of the decoder layers for one token: attention
+    projections, router + 8 experts (or the dense FFN), the two norms and
+    the KV cache read at ctx_len positions (f16 elements for config 2, whose
+    cache the config specifies as f16)."""
     L, d, nh, nkv, hd, V, F, lm, _, _, moe = MODEL_CFG[name]
     q8 = lambda r, c: r * (c // 32) * 34  # noqa: E731
     attn = q8(nh * hd + 2 * nkv * hd, d) + q8(d, nh * hd)
     ffn = TOP_K * EXPERT_BYTES + ROUTER_BYTES if moe else 3 * q8(F, d)
-    lm_bytes = V * (d // 256) * 210 if lm == "q6_k" else q8(V, d)
     kv = 2 * ctx_len * nkv * hd * (2 if name == "config2" else 4)
-    return L * (attn + ffn + kv + 2 * d * 4) + lm_bytes + q8(1, d)
+    return L * (attn + ffn + kv + 2 * d * 4)
 
 
-def measure_model_decode(args, pkg, ctx, torch, stream, moe_layers, rank, world, dist, name: str) -> dict:
+def model_bytes_per_token(name: str, ctx_len: float) -> float:
+    """Algorithmic HBM bytes of one decode step: the layers, the lm_head and
+    the embedding row."""
+    L, d, nh, nkv, hd, V, F, lm, _, _, moe = MODEL_CFG[name]
+    q8 = lambda r, c: r * (c // 32) * 34  # noqa: E731
+    lm_bytes = V * (d // 256) * 210 if lm == "q6_k" else q8(V, d)
+    return model_layer_bytes(name, ctx_len) + lm_bytes + q8(1, d) + d * 4
+
+
+def measure_model_decode(args, pkg, ctx, torch, stream, moe_layers, rank, world, dist, name: str, runs: int = 1,
+                         warm: int = 1, headline: bool = False) -> dict:
     """Greedy decode of a whole model through the C++ host loop
-    (llmtoy-zig_b200/host/decoder.cpp): a 32-token prompt, then
-    args.model_tokens tokens, one captured graph per token.  config2 reuses
-    the stack's 48 MoE layers (router + experts) and adds Q8_0 attention with
-    QK norm, NeoX RoPE, a Q8_0 embedding and the Q6_K lm_head; config0 is the
-    dense Q8_0 Qwen2-0.5B shape.  Device time of all steps (prompt and
-    generated tokens are the same one-token step), replicas on N > 1."""
+    (llmtoy-zig_b200/host/decoder.cpp): a 32-token prompt (config 0: 5
+    tokens, its workload), then args.model_tokens tokens, one captured graph
+    per token.  config2 reuses the stack's 48 MoE layers (router + experts)
+    and adds Q8_0 attention with QK norm, NeoX RoPE, a Q8_0 embedding and the
+    Q6_K lm_head; config0 is the dense Q8_0 Qwen2-0.5B shape.  `runs`
+    generations are timed, each bracketed by a barrier and CUDA events on the
+    context stream (the position reset between them is a host copy outside
+    the timing); replicas on N > 1."""
     decoder = importlib.import_module("llmtoy-zig_b200.decoder")
     L, d, nh, nkv, hd, V, F, lm, qk, neox, moe = MODEL_CFG[name]
-    n_prompt, n_gen = 32, args.model_tokens
+    n_prompt, n_gen = (32, args.model_tokens) if moe else (5, min(20, args.model_tokens))
     cap = 4096
     gen = torch.Generator(device="cuda")
     gen.manual_seed(0x11A70002 + 1000 * rank if moe else 0x11A70000 + 1000 * rank)
@@ -641,36 +645,57 @@ def measure_model_decode(args, pkg, ctx, torch, stream, moe_layers, rank, world,
     steps = n_prompt + n_gen - 1
     dec = decoder.Decoder(ctx, spec)
     first = dec.generate(prompt, n_gen)  # warm-up: eager step, capture, replays
-    for _ in range(max(0, args.warmup - 1)):
+    for _ in range(max(0, warm - 1)):
         dec.generate(prompt, n_gen)
-    # device time of the whole generation (graph replays on the context stream)
-    dec.start(prompt)
-    if dist is not None:
-        dist.barrier()
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    # device time of `runs` whole generations (graph replays on the context stream)
+    total_ms, deterministic = 0.0, True
     with ClockSampler(torch.cuda.current_device()) as clk:
-        ev0.record(stream)
-        dec.replay(steps)
-        ev1.record(stream)
-        stream.synchronize()
-    ms = ev0.elapsed_time(ev1)
-    toks = dec.tokens(n_prompt + n_gen)[n_prompt:]
-    deterministic = toks == first
-    if dist is not None:
-        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    ms_step = ms / steps
-    # end to end through the public entry point: host prompt in, host tokens out
+        for _ in range(runs):
+            dec.start(prompt)
+            _barrier(torch, dist)
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record(stream)
+            dec.replay(steps)
+            ev1.record(stream)
+            stream.synchronize()
+            total_ms += _max_over_ranks(torch, dist, ev0.elapsed_time(ev1))
+            deterministic = deterministic and dec.tokens(n_prompt + n_gen)[n_prompt:] == first
+    clocks = clk.summary()
+    ms_step = total_ms / (runs * steps)
+
+    # end to end through the public entry point: host prompt in, host tokens out, every generation
+    e2e_runs = max(1, runs if headline else 1)
+    _barrier(torch, dist)
     t0 = time.perf_counter()
-    dec.generate(prompt, n_gen)
-    e2e_s = time.perf_counter() - t0
-    if dist is not None:
-        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    # per-kernel times of one eager step
+    for _ in range(e2e_runs):
+        dec.generate(prompt, n_gen)
+    e2e_s = _max_over_ranks(torch, dist, time.perf_counter() - t0)
+
+    # the dominant kernel alone: the layer stack at the workload's mean context,
+    # replayed as a graph (the position and caches stay put)
+    mean_ctx = n_prompt + (n_gen - 1) / 2.0
+    dec.start(prompt)
+    dec.replay(int(mean_ctx))
+    ctx.sync()
+    ctx.capture_begin()
+    dec.run_layers()
+    lg = ctx.capture_end()
+    for _ in range(3):
+        lg.launch()
+    _barrier(torch, dist)
+    reps = 20
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(reps):
+        lg.launch()
+    ev1.record(stream)
+    stream.synchronize()
+    layers_ms = _max_over_ranks(torch, dist, ev0.elapsed_time(ev1)) / reps
+    lg.free()
+    uses_stack = dec.uses_stack
+
+    # per-kernel times and launches of one eager prompt step and one full step
     dec.start(prompt)
     ctx.profile(True)
     ctx.profile_reset()
@@ -679,28 +704,43 @@ def measure_model_decode(args, pkg, ctx, torch, stream, moe_layers, rank, world,
     prof = ctx.profile_read()
     ctx.profile(False)
     ctx.profile_reset()
+    launches_full = int(sum(v["count"] for v in prof.values()))
+    # a prompt step skips the final norm, the lm_head matvec and the soft-cap
+    launches_prompt = launches_full - int(sum(v["count"] for k, v in prof.items()
+                                              if k.startswith(("rmsnorm", "qmv", "quantize", "softcap"))))
     dec.close()
     for tt in tensors:
         tt.free()
     peak, kind = measured_peaks()
-    mean_ctx = n_prompt + (n_gen - 1) / 2.0
     bpt = model_bytes_per_token(name, mean_ctx)
     achieved = bpt / (ms_step / 1e3) / 1e9
+    lbytes = model_layer_bytes(name, mean_ctx)
+    k_achieved = lbytes / (layers_ms / 1e3) / 1e9
+    kname = "stack" if uses_stack else f"{L} x (attn_block + moe_decode)"
+    step_roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                 "peak_kind": kind, "algorithmic_bytes_per_token": bpt, "ms_per_token": ms_step,
+                 "note": "whole decode step (every kernel of one token, lm_head included) in graph replays; "
+                         "weights + KV at the mean context"}
+    roof = {"kernel": kname, "bound": "hbm", "achieved": k_achieved, "peak": peak, "unit": "GB/s",
+            "frac": k_achieved / peak, "peak_kind": kind, "algorithmic_bytes_per_launch": lbytes,
+            "avg_launch_ms": layers_ms, "traffic": (ncu_traffic() or {}).get(name, {}).get("dram_bytes_per_launch"),
+            "note": f"the {L} decoder layers of one token at position {int(mean_ctx)} (the workload's mean "
+                    f"context) as one graph replayed {reps} times, CUDA events on the launching stream"}
+    n_runs_launches = runs * ((n_prompt - 1) * launches_prompt + n_gen * launches_full)
     out = {
         "metric": f"greedy decode tok/s ({name}: {'Qwen3-30B-A3B' if moe else 'Qwen2-0.5B'} shape, {L} layers)",
-        "value": world / (ms_step / 1e3), "unit": "tok/s", "ms_per_token": ms_step, "steps": steps,
+        "value": world / (ms_step / 1e3), "unit": "tok/s", "ms_per_token": ms_step, "ms_per_step": total_ms / runs,
+        "steps_per_run": steps, "runs": runs,
         "prompt_tokens": n_prompt, "generated_tokens": n_gen, "scaling": "weak",
         "kv_cache": {"dtype": "f16" if name == "config2" else "f32", "capacity": cap},
-        "deterministic_stream": deterministic,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": kind, "algorithmic_bytes_per_token": bpt,
-                     "note": "whole decode step (all kernels of one token); weights + KV at the mean context"},
-        "e2e": {"value": world * n_gen / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * n_prompt / n_gen,
-                "d2h_bytes_per_step": 4.0 * (n_prompt + n_gen) / n_gen,
-                "path": "lth_generate: host prompt ids in, host token ids out (prompt steps included)"},
+        "deterministic_stream": deterministic, "uses_stack": uses_stack,
+        "roofline": roof, "step_roofline": step_roof,
+        "e2e": {"value": world * e2e_runs * steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * n_prompt,
+                "d2h_bytes_per_step": 4 * (n_prompt + n_gen), "runs": e2e_runs,
+                "path": "lth_generate: host prompt ids in, host token ids out; decode steps per second"},
         "kernels_per_token": {k: {"count": v["count"], "us": round(1e3 * v["total_ms"], 1)} for k, v in prof.items()},
-        "gpu_launches_per_token": int(sum(v["count"] for v in prof.values())),
-        "clocks": clk.summary(),
+        "gpu_launches_per_token": launches_full, "gpu_launches": n_runs_launches,
+        "clocks": clocks,
     }
     if rank == 0 and world == 1 and args.cpu_budget > 0:
         out["cpu_baseline"] = cpu_model_rate(name, min(args.cpu_budget, 10.0))
@@ -859,21 +899,10 @@ def measure_gemma_decode(args, pkg, ctx, torch, stream, rank, world, dist) -> di
 def cpu_gemma_rate(budget_s: float) -> dict:
     """orc_gemma_step (all host threads) on the config-3 shape: 3 distinct host
     layer weight sets cycled through the 30 layers, full vocabulary."""
-    sys.path.insert(0, str(REPO / "tests"))
-    oracle = importlib.import_module("oracle_lib")
+    oracle, flags = oracle_module()
     synth = importlib.import_module("llmtoy-zig_b200.synth")
     rng = np.random.Generator(np.random.PCG64(synth.config_seed(3)))
-    m = synth.GemmaModel(rng, n_layers=3)
-    L = GEMMA["n_layers"]
-    base = m.layers
-    m.layers = []
-    for i in range(L):  # per-index sliding-window pattern over the cycled weights
-        src = base[i % 3]
-        lay = object.__new__(type(src))
-        lay.__dict__.update(src.__dict__)
-        lay.is_swa = (i + 1) % GEMMA["period"] != 0
-        m.layers.append(lay)
-    m.n_layers = L
+    m = synth.cycle_layers(synth.GemmaModel(rng, n_layers=3), GEMMA["n_layers"], swa_period=GEMMA["period"])
     threads = os.cpu_count() or 1
     pool = oracle.Pool(threads)
     dec = oracle.OracleGemma(m, 64, pool)
@@ -885,36 +914,26 @@ def cpu_gemma_rate(budget_s: float) -> dict:
         n += 1
     dt = time.perf_counter() - t0
     pool.close()
-    return {"value": n / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+    return {"value": n / dt, "unit": "tok/s", "cores": threads, "kind": "port", "build": flags,
             "sample": f"{n} decode steps of the 30-layer model in {dt:.1f}s (3 distinct layer weight sets cycled; "
                       f"C restatement of gemma4 forwardOne, zig absent)"}
 
 
 def cpu_model_rate(name: str, budget_s: float) -> dict:
     """The CPU restatement (orc_model_step, all host threads) on the same
-    model shape: 4 distinct host layer sets cycled through all layers (each
-    ~360 MB for config2, far beyond the CPU caches), full vocabulary."""
-    sys.path.insert(0, str(REPO / "tests"))
-    oracle = importlib.import_module("oracle_lib")
-    synth = importlib.import_module("llmtoy-zig_b200.synth")
-    rng = np.random.Generator(np.random.PCG64(synth.config_seed(2 if name == "config2" else 0)))
-    L = MODEL_CFG[name][0]
-    m = synth.config2_model(rng, n_layers=4) if name == "config2" else synth.config0_model(rng, n_layers=4)
-    m.layers = [m.layers[i % 4] for i in range(L)]
-    m.n_layers = L
-    threads = os.cpu_count() or 1
-    pool = oracle.Pool(threads)
-    dec = oracle.OracleDecoder(m, 64, pool)
-    dec.step(1, 0)
+    model shape: 4 distinct host layer sets cycled through all layers, full
+    vocabulary (CpuModel)."""
+    s = CpuModel(name)
+    s.tokens(1)
     t0 = time.perf_counter()
     n = 0
     while n < 2 or time.perf_counter() - t0 < budget_s:
-        dec.step(1 + n, (n + 1) % 64)
+        s.tokens(1)
         n += 1
     dt = time.perf_counter() - t0
-    pool.close()
-    return {"value": n / dt, "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"{n} decode steps of the {L}-layer model in {dt:.1f}s (4 distinct layer weight sets "
+    s.close()
+    return {"value": n / dt, "unit": "tok/s", "cores": s.threads, "kind": "port", "build": s.flags,
+            "sample": f"{n} decode steps of the {s.m.n_layers}-layer model in {dt:.1f}s (4 distinct layer weight sets "
                       f"cycled; C restatement of forwardOneModel, zig absent)"}
 
 
@@ -936,6 +955,54 @@ def zipf_router(torch, n_experts: int, d: int, s: float, mu: float, seed: int):
     b = b - b.mean()
     rms = (1.0 + mu * mu / d) ** 0.5
     return (base + (b * rms / mu)[:, None] * u[None, :]).contiguous(), u
+
+
+def ep_expert_bytes(torch, layer: int, e: int):
+    """Expert e of EP layer `layer`: gate, up and down GGUF bytes from a seed of
+    their own, so every rank can rebuild any expert (the parity check needs the
+    whole layer on each rank's host)."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0x11A74100 + 1000 * layer + e)
+    return (q4k_bytes_device(torch, g, D_EXPERT, D_MODEL), q4k_bytes_device(torch, g, D_EXPERT, D_MODEL),
+            q4k_bytes_device(torch, g, D_MODEL, D_EXPERT))
+
+
+def ep_parity(torch, dist, moe, layer, x, mu: float, world: int, n_sample: int = 8) -> dict:
+    """A seeded sample of this rank's tokens through the expert-parallel layer
+    against orc_moe_layer on the whole layer (rebuilt on the host from the
+    per-expert seeds): worst relative L2 of the MoE part over the sample, max
+    over ranks."""
+    import types
+    oracle, _ = oracle_module()
+    T = x.shape[0]
+    rank = dist.get_rank() if dist is not None else 0
+    idx = np.random.Generator(np.random.PCG64(0x11A7E000 + rank)).choice(T, size=min(n_sample, T), replace=False)
+    out = moe.forward(layer, x)
+    torch.cuda.synchronize()
+    got = out[torch.from_numpy(idx).cuda()].cpu().numpy()
+    xs = x[torch.from_numpy(idx).cuda()].cpu().numpy()
+    gs, us, ds = [], [], []
+    for e in range(N_EXPERTS):
+        g, u, dn = ep_expert_bytes(torch, 0, e)
+        gs.append(g.cpu().numpy())
+        us.append(u.cpu().numpy())
+        ds.append(dn.cpu().numpy())
+    rw, _ = zipf_router(torch, N_EXPERTS, D_MODEL, 1.1, mu, 0x11A74000)
+    full = types.SimpleNamespace(router=rw.cpu().numpy(), gate=np.concatenate(gs), up=np.concatenate(us),
+                                 down=np.concatenate(ds), gate_type=12, down_type=12, d_model=D_MODEL,
+                                 n_experts=N_EXPERTS, d_expert=D_EXPERT)
+    norm = np.ones(D_MODEL, np.float32)
+    xn = np.empty_like(xs)
+    for t in range(xs.shape[0]):
+        oracle.lib().orc_rmsnorm(xn[t].ctypes.data, xs[t].ctypes.data, norm.ctypes.data, D_MODEL, 1e-6)
+    pool = oracle.Pool(max(1, (os.cpu_count() or 1) // world))
+    ref, _, _ = oracle.moe_layer(full, xn, TOP_K, True, pool=pool)
+    pool.close()
+    worst = max(float(np.linalg.norm((got[t] - xs[t]) - ref[t]) / np.linalg.norm(ref[t])) for t in range(xs.shape[0]))
+    worst = float(_max_over_ranks(torch, dist, worst))
+    return {"worst_rel_l2": worst, "tokens_per_rank": int(len(idx)), "bar": 1e-4, "ok": worst < 1e-4,
+            "against": "orc_moe_layer (router + 8 experts + renormalised combine) on the whole layer, the MoE part "
+                       "of out = x + moe(rmsnorm(x))"}
 
 
 def measure_ep_prefill(args, pkg, torch, stream, rank, world, local, dist) -> dict:
@@ -967,13 +1034,11 @@ def measure_ep_prefill(args, pkg, torch, stream, rank, world, local, dist) -> di
             rw, u = zipf_router(torch, N_EXPERTS, D_MODEL, 1.1, mu, 0x11A74000 + li)
             router = ctx.upload_device(rw.view(torch.uint8).view(-1), pkg.F32, N_EXPERTS, D_MODEL)
             del rw
-            g = q4k_bytes_device(torch, gen, ne * D_EXPERT, D_MODEL)
-            gate = ctx.upload_device(g, pkg.Q4_K, D_EXPERT, D_MODEL, ne)
-            g = q4k_bytes_device(torch, gen, ne * D_EXPERT, D_MODEL)
-            up = ctx.upload_device(g, pkg.Q4_K, D_EXPERT, D_MODEL, ne)
-            g = q4k_bytes_device(torch, gen, ne * D_MODEL, D_EXPERT)
-            down = ctx.upload_device(g, pkg.Q4_K, D_MODEL, D_EXPERT, ne)
-            del g
+            parts = [ep_expert_bytes(torch, li, e) for e in range(lo, hi)]
+            gate = ctx.upload_device(torch.cat([q[0] for q in parts]), pkg.Q4_K, D_EXPERT, D_MODEL, ne)
+            up = ctx.upload_device(torch.cat([q[1] for q in parts]), pkg.Q4_K, D_EXPERT, D_MODEL, ne)
+            down = ctx.upload_device(torch.cat([q[2] for q in parts]), pkg.Q4_K, D_MODEL, D_EXPERT, ne)
+            del parts
             layers.append((ep.EPLayer(router=router, gate=gate, up=up, down=down, n_experts=N_EXPERTS,
                                       d_model=D_MODEL, norm_w=torch.ones(D_MODEL, device="cuda")), u))
         x = torch.randn(T, D_MODEL, device="cuda", generator=gen) + mu * layers[0][1][None, :]
@@ -1033,6 +1098,7 @@ def measure_ep_prefill(args, pkg, torch, stream, rank, world, local, dist) -> di
             loads = [float(t.item()) for t in allr]
         else:
             a2a_us, a2a_bytes, loads = 0.0, 0, [float(recv.item())]
+        parity = ep_parity(torch, dist, moe, layers[0][0], x, mu, world)
         # expert popularity of the biased router over this rank's tokens
         xn = torch.empty_like(x)
         ctx.rmsnorm(x, layers[0][0].norm_w, 1e-6, D_MODEL, T, xn)
@@ -1057,6 +1123,7 @@ def measure_ep_prefill(args, pkg, torch, stream, rank, world, local, dist) -> di
         "load_pairs_per_rank": loads, "load_imbalance_max_over_mean": max(loads) / mean_load,
         "expert_popularity_max_over_mean": float(cnt.max() / cnt.mean()),
         "expert_popularity_top8_share": float(cnt.sort(descending=True).values[:8].sum() / cnt.sum()),
+        "parity": parity,
         "roofline": {"kernel": "moe_gemm_gate_up + moe_gemm_down (busiest rank)", "bound": "tensor",
                      "achieved": flops_rank / (gemm_us * 1e-6) / 1e12 if gemm_us else None, "peak": peak,
                      "unit": "TFLOP/s", "peak_kind": kind,
@@ -1081,8 +1148,7 @@ def cpu_prefill_rate(budget_s: float, T: int) -> dict:
     threads (the CPU path handles tokens one by one, so the rate does not
     depend on the batch)."""
     B = min(T, 16)
-    sys.path.insert(0, str(REPO / "tests"))
-    oracle = importlib.import_module("oracle_lib")
+    oracle, flags = oracle_module()
     synth = importlib.import_module("llmtoy-zig_b200.synth")
     rng = np.random.Generator(np.random.PCG64(synth.config_seed(1) + 77))
     L = synth.MoeLayer(rng, D_MODEL, N_EXPERTS, D_EXPERT)
@@ -1097,7 +1163,7 @@ def cpu_prefill_rate(budget_s: float, T: int) -> dict:
         n += 1
     dt = time.perf_counter() - t0
     pool.close()
-    return {"value": B * n / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+    return {"value": B * n / dt, "unit": "tok/s", "cores": threads, "kind": "port", "build": flags,
             "sample": f"{n} batches of {B} tokens through one config-1 MoE layer in {dt:.1f}s"}
 
 

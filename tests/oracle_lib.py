@@ -25,6 +25,15 @@ class SoftmaxStats(ctypes.Structure):
 _lib = None
 
 
+def use_library(path) -> None:
+    """Load the oracle from another build of oracle.c (the timed CPU baseline's
+    -march=native build); only before the first lib() call."""
+    global LIB
+    if _lib is not None:
+        raise RuntimeError("the oracle library is loaded already")
+    LIB = Path(path)
+
+
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is not None:

@@ -173,12 +173,14 @@ def test_ep_threads_vs_oracle(pkg, oracle, pool, world, Ts, block):
         assert rel_l2(got, ref) < MOE_L2_TOL, (rank, rel_l2(got, ref))
 
 
-def test_ep_nccl_two_gpus():
+def test_ep_nccl_all_gpus():
+    """The NCCL expert-parallel layer over every visible GPU (2, 4 or 8 ranks)."""
     import torch
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs two GPUs")
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+    n = max(w for w in (2, 4, 8) if w <= n)
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
            "--master-addr=127.0.0.1", "--master-port=29531", str(REPO / "tests" / "ep_nccl_worker.py")]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(["timeout", "-k", "30", "600"] + cmd, env=env, capture_output=True, text=True)
