@@ -135,6 +135,23 @@ LT_DEVINL void st_prefetch_rows(const uint8_t *base, uint64_t pitch, uint32_t r0
     for (uint64_t b = 0; b < bytes; b += 65536) prefetch_l2(p + b, (uint32_t)(bytes - b < 65536 ? bytes - b : 65536));
 }
 
+// Phase timestamps for tuning builds (-DLT_STACK_TRACE): thread 0 of each CTA
+// records globaltimer at the phase boundaries of every layer.  Off in the
+// library the package builds.
+#ifdef LT_STACK_TRACE
+constexpr int kTraceCtas = 160, kTraceLayers = 64, kTraceMarks = 16;
+__device__ unsigned long long g_stack_trace[kTraceCtas * kTraceLayers * kTraceMarks];
+#define ST_MARK(m)                                                                              \
+    do {                                                                                       \
+        if (tid == 0 && c < kTraceCtas && l < kTraceLayers)                                    \
+            g_stack_trace[((size_t)c * kTraceLayers + l) * kTraceMarks + (m)] = globaltimer_ns(); \
+    } while (0)
+#else
+#define ST_MARK(m) \
+    do {           \
+    } while (0)
+#endif
+
 // One expert logit in dotf32 order (router_logit's), the weight row in shared memory.
 LT_DEVINL float st_router_logit(const float *wsm, const float *xs, uint32_t cols, int lane) {
     const uint32_t n32 = cols & ~31u;
@@ -241,6 +258,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
         const bool more = l + 1 < a.n_layers;
 
         // ── Q ────────────────────────────────────────────────────────────────
+        ST_MARK(0);
         ab_load(XF, a.x, d);
         __syncthreads();
         for (uint32_t r = tid; r < nor; r += kStThreads) xres[r] = XF[o0 + r];
@@ -259,7 +277,9 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
         for (uint32_t r = tid; r < nqr; r += kStThreads)
             a.qkv[q0 + r] = Ly.bias ? __fadd_rn(XF[r], __ldg(Ly.bias + q0 + r)) : XF[r];
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // W is copied over next
+        ST_MARK(1);
         gsync();
+        ST_MARK(2);
 
         // ── A ────────────────────────────────────────────────────────────────
         if (tid == 0) {
@@ -386,7 +406,9 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
                 __syncthreads();
             }
         }
+        ST_MARK(3);
         gsync();
+        ST_MARK(4);
 
         // ── O ────────────────────────────────────────────────────────────────
         ab_load_qact(Xa, a.att, nq);
@@ -399,7 +421,9 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
             xres[r] = v;  // x' rows: the FFN block's residual
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // W takes the expert rows next
+        ST_MARK(5);
         gsync();
+        ST_MARK(6);
 
         // ── R ────────────────────────────────────────────────────────────────
         ab_load(XF, a.x, d);
@@ -466,6 +490,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
         }
         __syncthreads();
 
+        ST_MARK(7);
         // ── G ────────────────────────────────────────────────────────────────
         if (warp == 0) {  // one TMA chunk per lane: [8 gate rows][8 up rows] of pairs p0 + 8j..
             for (uint32_t j = lane; j < nchunks; j += 32) {
@@ -553,7 +578,9 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
         }
         fence_proxy_async_global();  // the images are read by TMA after the barrier
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // W, RT and XS are copied over next
+        ST_MARK(8);
         gsync();
+        ST_MARK(9);
 
         // ── D ────────────────────────────────────────────────────────────────
         if (tid == 0) {
@@ -619,7 +646,9 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // DN and XS are copied over next
         if (!more) pdl_launch_dependents();
+        ST_MARK(10);
         gsync();
+        ST_MARK(11);
     }
 }
 
@@ -705,6 +734,13 @@ static cudaError_t launch_stack_t(const LaunchCfg &c, const StackArgs &a, size_t
     return launch_k(c, "stack", k_stack<T_Q8_0, T_Q8_0, HD, GT, DT>, dim3((unsigned)c.num_sms), dim3(kStThreads),
                     smem, a);
 }
+
+#ifdef LT_STACK_TRACE
+// Tuning builds only (not declared in the public header): copy the trace out.
+extern "C" int lt_stack_trace_copy(void *dst, size_t bytes) {
+    return (int)cudaMemcpyFromSymbol(dst, g_stack_trace, bytes);
+}
+#endif
 
 cudaError_t launch_stack(const LaunchCfg &c, const StackParams &p, const void *dev_layers, float *x,
                          const uint32_t *pos, uint8_t *scratch) {
