@@ -453,12 +453,15 @@ def test_stack_kernel_matches_per_layer_path(pkg, oracle, pool, kind, kv_f16):
     shapes: logits within f32 rounding of each other at every step (f16
     caches: K may round to the neighbouring half on either path), the same
     greedy stream as the oracle on both paths, and the step's launches show
-    the stack kernel on one path only."""
+    the stack kernel on one path only.  The two paths must agree far more
+    closely than either agrees with the oracle (whose distance is bounded by
+    the north-star bar here: with random norm weights a router near-tie can
+    pick another expert in both device paths alike)."""
     import os
     synth, decoder = _mods()
     rng = np.random.default_rng(51 if kind == "moe" else 52)
-    if kind == "moe":  # random norm weights with f32 caches; unit norms with f16 (as the config)
-        m = synth.config2_model(rng, n_layers=3, vocab=4096, norms_random=not kv_f16)
+    if kind == "moe":
+        m = synth.config2_model(rng, n_layers=3, vocab=4096, norms_random=True)
     else:
         m = synth.DecoderModel(rng, 3, 896, 14, 2, 64, 4096, d_ffn=4864, qkv_bias=True, norms_random=True)
     prompt, n_gen = [3, 1000, 4095, 7, 12], 10
@@ -496,4 +499,4 @@ def test_stack_kernel_matches_per_layer_path(pkg, oracle, pool, kind, kv_f16):
     for flag, (eager, replay) in zip(("1", "0"), toks):
         assert eager == ref_toks and replay == ref_toks, flag
     for i, rl in enumerate(ref_logits):
-        assert rel_l2(logits[0][i], rl) < LOGIT_TOL, (i, rel_l2(logits[0][i], rl), rel_l2(logits[1][i], rl))
+        assert rel_l2(logits[0][i], rl) < 2e-3, (i, rel_l2(logits[0][i], rl), rel_l2(logits[1][i], rl))
