@@ -273,7 +273,7 @@ struct StackParams {
     uint32_t qtype, otype, gtype, dtype;
     uint64_t qpitch, opitch, gpitch, dpitch;
 };
-constexpr size_t kStackSyncBytes = 8192;
+constexpr size_t kStackSyncBytes = 16384;
 // Whether the stack kernel takes this shape: its shared memory and global
 // scratch bytes (the sync block at sync_offset must be zeroed once, before
 // the first launch, and used by no other kernel).

@@ -51,10 +51,11 @@ constexpr uint32_t kStSplitPositions = 32;  // positions per attention split bef
 constexpr uint32_t kStMaxSplits = 8;
 constexpr int kStNormThreads = 128;       // k_moe_decode's RMSNorm reduction width
 
-// The plan's sync block (kStackSyncBytes): launch counter, barrier counter,
-// tagged logits, per-head merge counters.
-constexpr size_t kStEpoch = 0, kStBar = 8, kStLogits = 256, kStHeadCnt = kStLogits + 8 * kRouterMaxE;
-static_assert(kStHeadCnt + 4 * 1024 <= kStackSyncBytes, "sync block");
+// The plan's sync block (kStackSyncBytes): launch counter, tagged logits,
+// per-head merge counters, per-CTA hand-off flags.
+constexpr size_t kStEpoch = 0, kStLogits = 256, kStHeadCnt = kStLogits + 8 * kRouterMaxE, kStFlags = 8192;
+constexpr uint32_t kStMaxCtas = 1024;
+static_assert(kStHeadCnt + 4 * 1024 <= kStFlags && kStFlags + 8 * kStMaxCtas <= kStackSyncBytes, "sync block");
 
 struct StackArgs {
     AttnGeom g;
@@ -171,10 +172,258 @@ LT_DEVINL float st_router_logit(const float *wsm, const float *xs, uint32_t cols
     return sum;
 }
 
-template <uint32_t QT, uint32_t OT, int HD, uint32_t GT, uint32_t DT>
-__global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
+// ── grid hand-off ───────────────────────────────────────────────────────────
+// One flag per CTA, holding the sequence number of the last hand-off the CTA
+// reached (launch * barriers per launch + barrier + 1: it only grows, so the
+// flags are never reset).  A CTA publishes its writes with one release store;
+// thread i of every CTA waits for CTA i's flag with acquire loads, then the
+// block barrier passes the order on to the CTA's other threads.  No atomics:
+// the G arrivals do not queue on one address.
+LT_DEVINL void st_release_u64(unsigned long long *p, uint64_t v) {
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+LT_DEVINL void st_grid_sync(unsigned long long *flags, uint32_t c, uint32_t G, uint64_t seqn, int *dev_err) {
+    __syncthreads();
+    if (threadIdx.x == 0) st_release_u64(flags + c, seqn);
+    for (uint32_t i = threadIdx.x; i < G; i += blockDim.x) {
+        if (ld_acquire_u64(flags + i) < seqn) {
+            const uint64_t t0 = globaltimer_ns();
+            while (ld_acquire_u64(flags + i) < seqn) {
+                if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                    if (dev_err) atomicExch(dev_err, DEV_ERR_GRID_TIMEOUT);
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// The heavy inner loops live in functions of their own (not inlined), so
+// their registers are allocated apart from the long-lived state of the
+// layer loop.
+
+// rows [0, nrows) of a shared tile against X (ab_rows).
+template <uint32_t T>
+__device__ __noinline__ void st_rows(const uint8_t *tile, uint64_t pitch, uint32_t nrows, uint32_t cols, uint32_t nb,
+                                     XS X, float *y) {
+    ab_rows<T>(tile, pitch, nrows, cols, nb, X, (int)(threadIdx.x >> 5), (int)(threadIdx.x & 31), y);
+}
+
+// Phase A: the (head, split) items of this CTA (k_attn_block's phase A).
+template <int HD>
+__device__ __noinline__ void st_attention(const StackArgs &a, const float *q_norm, const float *k_norm, void *kc,
+                                          void *vc, float *XF, float *red, int *s_last, uint32_t *head_cnt,
+                                          uint32_t pos, uint32_t S, uint32_t win, uint32_t first) {
     constexpr int PER = HD / 32;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t G = gridDim.x, c = blockIdx.x;
+    const uint32_t nq = a.nq, nkv = a.nkv, group = a.g.n_heads / a.g.n_kv;
+    float *hq = XF, *hk = hq + HD, *hv = hk + HD;
+    float *wpart = hv + HD;  // [16][HD + 2]: m, l, o[HD]
+    for (uint32_t item = c; item < a.g.n_heads * S; item += G) {
+        const uint32_t h = item / S, s = item - h * S, kh = h / group;
+        if (tid < 3 * HD / 4) {  // q, k, v heads: one float4 each
+            const uint32_t pt = tid / (HD / 4), i = tid % (HD / 4);
+            const size_t off = pt == 0 ? (size_t)h * HD : pt == 1 ? nq + (size_t)kh * HD : nq + nkv + (size_t)kh * HD;
+            reinterpret_cast<float4 *>(hq + pt * HD)[i] = __ldcg(reinterpret_cast<const float4 *>(a.qkv + off) + i);
+        }
+        __syncthreads();
+        ab_norm_rope2(hq, q_norm, hk, k_norm, a.g, pos, red);
+        if (s == 0 && h % group == 0) {  // this position's K/V into the cache
+            const size_t slot = (size_t)(pos % a.g.cap) * nkv + (size_t)kh * HD;
+            for (uint32_t i = tid; i < HD; i += kStThreads) {
+                kv_st(kc, slot + i, hk[i], a.g.kv_f16);
+                kv_st(vc, slot + i, hv[i], a.g.kv_f16);
+            }
+        }
+        if (a.g.kv_f16) {  // attend to this position as the cache holds it
+            __syncthreads();
+            for (uint32_t i = tid; i < HD; i += kStThreads) {
+                hk[i] = kv_round(hk[i], 1u);
+                hv[i] = kv_round(hv[i], 1u);
+            }
+            __syncthreads();
+        }
+        float o[PER], m = -INFINITY, lsum = 0.0f;
+        if (a.g.kv_f16)
+            ab_attend<HD, true>(kc, vc, a.g, s, S, win, first, (size_t)kh * HD, nkv, hq, hk, hv, warp, lane, m, lsum, o);
+        else
+            ab_attend<HD, false>(kc, vc, a.g, s, S, win, first, (size_t)kh * HD, nkv, hq, hk, hv, warp, lane, m, lsum, o);
+        float *wp = wpart + warp * (HD + 2);
+        if (lane == 0) {
+            wp[0] = m;
+            wp[1] = lsum;
+        }
+#pragma unroll
+        for (int i = 0; i < PER; i++) wp[2 + lane * PER + i] = o[i];
+        __syncthreads();
+        float *sf = wpart + kStWarps * (HD + 2);  // [16] scales, then the sum and the maximum
+        if (warp == 0) {
+            const float mw = lane < kStWarps ? wpart[lane * (HD + 2)] : -INFINITY;
+            float M = mw;
+#pragma unroll
+            for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
+            if (lane < kStWarps) sf[lane] = mw != -INFINITY ? expf(mw - M) : 0.0f;
+            __syncwarp();
+            if (lane == 0) {
+                float Ls = 0.0f;
+                for (int w = 0; w < kStWarps; w++) Ls += wpart[w * (HD + 2) + 1] * sf[w];
+                sf[kStWarps] = Ls;
+                sf[kStWarps + 1] = M;
+            }
+        }
+        __syncthreads();
+        if (S == 1) {  // the whole window: normalise, quantise into the attention row
+            const float Ls = sf[kStWarps];
+            for (uint32_t t = tid; t < HD; t += kStThreads) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int w = 0; w < kStWarps; w++) acc += wpart[w * (HD + 2) + 2 + t] * sf[w];
+                hq[t] = acc / Ls;
+            }
+            __syncthreads();
+            for (uint32_t b = warp; b < (uint32_t)HD / 32; b += kStWarps)
+                qact_store_block(a.att, (int)nq, (int)(h * HD / 32 + b), hq[32 * b + lane], lane);
+            __syncthreads();
+            continue;
+        }
+        float *po = a.part + ((size_t)h * S + s) * HD;
+        float *pml = a.part + (size_t)a.g.n_heads * S * HD + 2 * ((size_t)h * S + s);
+        for (uint32_t t = tid; t < HD; t += kStThreads) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kStWarps; w++) acc += wpart[w * (HD + 2) + 2 + t] * sf[w];
+            po[t] = acc;
+        }
+        if (tid == 0) *reinterpret_cast<float2 *>(pml) = make_float2(sf[kStWarps + 1], sf[kStWarps]);
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            s_last[0] = atomicAdd(head_cnt + h, 1u) == S - 1;
+        }
+        __syncthreads();
+        if (s_last[0]) {  // the last split of head h merges the head's splits
+            __threadfence();
+            const float *ho = a.part + (size_t)h * S * HD;
+            const float *hml = a.part + (size_t)a.g.n_heads * S * HD + 2 * (size_t)h * S;
+            for (uint32_t t = tid; t < HD; t += kStThreads) {
+                float GM = -INFINITY;
+                for (uint32_t q = 0; q < S; q++) GM = fmaxf(GM, __ldcg(hml + 2 * q));
+                float GL = 0.0f, acc = 0.0f;
+                for (uint32_t q = 0; q < S; q++) {
+                    const float mk = __ldcg(hml + 2 * q);
+                    if (mk != -INFINITY) {
+                        const float f = expf(mk - GM);
+                        GL += __ldcg(hml + 2 * q + 1) * f;
+                        acc += __ldcg(ho + (size_t)q * HD + t) * f;
+                    }
+                }
+                hq[t] = acc / GL;
+            }
+            __syncthreads();
+            for (uint32_t b = warp; b < (uint32_t)HD / 32; b += kStWarps)
+                qact_store_block(a.att, (int)nq, (int)(h * HD / 32 + b), hq[32 * b + lane], lane);
+            if (tid == 0) head_cnt[h] = 0;
+        }
+        __syncthreads();
+    }
+}
+
+// Phase G's rows: gate/up tile rows [0, 2 np) against Xx, then h = act(g) * u
+// per pair (k_moe_decode's orders).
+template <uint32_t GT>
+__device__ __noinline__ void st_gate_up(const StackArgs &a, const uint8_t *W, float *part, XS Xx, uint64_t *bch,
+                                        uint32_t par, uint32_t np, float *s_h) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t cpr = st_chunks64(a.d);
+    const uint32_t gstride = 2 * a.maxpairs + 1;
+    const uint32_t lpr = min(cpr, 32u), rps = 32 / lpr;
+    const uint32_t sub = lane / lpr, nrows = 2 * np;
+    if (sub < rps) {
+        for (uint32_t cg = 0; cg < cpr; cg += lpr) {
+            const uint32_t n = min(lpr, cpr - cg);
+            if ((uint32_t)lane % lpr >= n) continue;
+            const uint32_t cb = cg + spread_chunk((uint32_t)lane % lpr, n);
+            XChunk xc;
+            xchunk_load(Xx, 0, (int)cb, xc);
+            const uint32_t step = kStWarps * rps;
+            for (uint32_t r = warp * rps + sub; r < nrows; r += 2 * step) {
+                const uint32_t rb = r + step < nrows ? r + step : r;
+                const bool ok = st_wait(&bch[r / (2 * kStChunk)], par, a.dev_err) &
+                                st_wait(&bch[rb / (2 * kStChunk)], par, a.dev_err);
+                float ya = 0.0f, yb = 0.0f;
+                if (ok) {
+                    ya = dot64<GT>(W + (size_t)r * a.gpitch, (int)cb, (int)a.gnb, xc);
+                    yb = dot64<GT>(W + (size_t)rb * a.gpitch, (int)cb, (int)a.gnb, xc);
+                }
+                part[cb * gstride + r] = ya;
+                part[cb * gstride + rb] = yb;
+            }
+        }
+    }
+    __syncthreads();
+    for (uint32_t lp = tid; lp < np; lp += kStThreads) {  // chunk partials summed in column order
+        const uint32_t rg = 2 * kStChunk * (lp / kStChunk) + lp % kStChunk;
+        const float *pg = part + rg, *pu = pg + kStChunk;
+        float g = 0.0f, u = 0.0f;
+        for (uint32_t i = 0; i < cpr; i++) {
+            g += pg[i * gstride];
+            u += pu[i * gstride];
+        }
+        s_h[lp] = act_apply(a.act, g) * u;
+    }
+}
+
+// Phase D's rows: warps [s*wps, (s+1)*wps) take slot s; a lane owns one
+// 64-column chunk of that slot's h; then y[s][r] from the chunk partials.
+template <uint32_t DT>
+__device__ __noinline__ void st_down(const StackArgs &a, const uint8_t *DN, uint8_t *XSr, float *part, float *s_y,
+                                     uint64_t *bdn, uint32_t par, uint32_t nor, bool hok) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t cpr = st_chunks64(a.F);
+    const uint32_t dstride = a.k * a.maxo + 1;
+    const uint32_t lpr = min(cpr, 32u), rps = 32 / lpr;
+    const uint32_t sub = lane / lpr;
+    const uint32_t wps = max(1u, (uint32_t)kStWarps / a.k);
+    const uint32_t s = warp / wps, ws = warp % wps;
+    if (s < a.k && sub < rps && nor) {
+        const bool ok = st_wait(&bdn[s], par, a.dev_err) && hok;
+        const XS Xh = xs_carve(XSr + (size_t)s * a.img, 1, (int)a.di);
+        for (uint32_t cg = 0; cg < cpr; cg += lpr) {
+            const uint32_t n = min(lpr, cpr - cg);
+            if ((uint32_t)lane % lpr >= n) continue;
+            const uint32_t cb = cg + spread_chunk((uint32_t)lane % lpr, n);
+            XChunk xc;
+            xchunk_load(Xh, 0, (int)cb, xc);
+            const uint32_t step = wps * rps;
+            for (uint32_t r = ws * rps + sub; r < nor; r += 2 * step) {
+                const uint32_t rb = r + step < nor ? r + step : r;
+                const uint32_t ta = s * a.maxo + r, tb = s * a.maxo + rb;
+                float ya = 0.0f, yb = 0.0f;
+                if (ok) {
+                    ya = dot64<DT>(DN + (size_t)ta * a.dpitch, (int)cb, (int)a.dnb, xc);
+                    yb = dot64<DT>(DN + (size_t)tb * a.dpitch, (int)cb, (int)a.dnb, xc);
+                }
+                part[cb * dstride + ta] = ya;
+                part[cb * dstride + tb] = yb;
+            }
+        }
+    }
+    __syncthreads();
+    for (uint32_t w = tid; w < a.k * nor; w += kStThreads) {  // y[s][r]: chunk partials in column order
+        const uint32_t s2 = w / nor, r = w - s2 * nor;
+        const float *pp = part + s2 * a.maxo + r;
+        float y = 0.0f;
+        for (uint32_t i = 0; i < cpr; i++) y += pp[i * dstride];
+        s_y[s2 * a.maxo + r] = y;
+    }
+}
+
+template <uint32_t QT, uint32_t OT, int HD, uint32_t GT, uint32_t DT>
+__global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__ StackArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t G = gridDim.x, c = blockIdx.x;
     const StLayout L = st_layout(a);
@@ -195,17 +444,14 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
     float *RT = reinterpret_cast<float *>(smem + L.rt);
     uint8_t *XSr = smem + L.xs;
     float *XF = reinterpret_cast<float *>(smem + L.xf);
-    float *part = XF;
     float *s_h = reinterpret_cast<float *>(smem + L.hs);
     float *s_y = reinterpret_cast<float *>(smem + L.ys);
     float *xres = reinterpret_cast<float *>(smem + L.xres);
-    const XS Xx = xs_carve(XSr, 1, (int)st_items(a.d));
-    const XS Xa = xs_carve(XSr, 1, (int)st_items(a.nq));
     unsigned long long *ctr_e = reinterpret_cast<unsigned long long *>(a.sync + kStEpoch);
-    unsigned long long *ctr_b = reinterpret_cast<unsigned long long *>(a.sync + kStBar);
+    unsigned long long *flags = reinterpret_cast<unsigned long long *>(a.sync + kStFlags);
     unsigned long long *lslots = reinterpret_cast<unsigned long long *>(a.sync + kStLogits);
     uint32_t *head_cnt = reinterpret_cast<uint32_t *>(a.sync + kStHeadCnt);
-    const uint32_t d = a.d, nq = a.nq, nkv = a.nkv;
+    const uint32_t d = a.d;
 
     // this CTA's shares: Q/K/V rows [q0, q1); wo, down and residual rows
     // [o0, o1); gate/up pairs [p0, p1) of the k*F (slot, row) pairs in whole
@@ -229,7 +475,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
         fence_barrier_init();
         *s_launch = atomicAdd(ctr_e, 1ull) / G;  // every CTA adds 1 per launch
         // the first layer's static tiles
-        const StackLayerDev L0 = a.layers[0];
+        const StackLayerDev &L0 = a.layers[0];
         mbar_arrive_expect_tx(bq, (uint32_t)(nqr * a.qpitch));
         tma_load_1d(W, L0.wqkv + (uint64_t)q0 * a.qpitch, (uint32_t)(nqr * a.qpitch), bq);
         if (has_e) {
@@ -240,20 +486,18 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
     }
     __syncthreads();
     const uint64_t launch = *s_launch;
-    uint32_t nb = 0;  // grid barriers passed in this launch
+    uint32_t nb = 0;  // grid hand-offs passed in this launch
     auto gsync = [&]() {
-        grid_arrive(ctr_b);
-        grid_wait(ctr_b, ((unsigned long long)launch * a.nbar + nb + 1) * G, a.dev_err, kWaitLimitNs);
+        st_grid_sync(flags, c, G, (uint64_t)launch * a.nbar + nb + 1, a.dev_err);
         nb++;
     };
     pdl_wait();
     const uint32_t pos = __ldcg(a.pos);
-    const uint32_t group = a.g.n_heads / a.g.n_kv;
     const uint32_t seq = pos + 1, win = a.g.window ? min(seq, a.g.window) : seq, first = seq - win;
     const uint32_t S = min(a.splits, max(1u, (win + kStSplitPositions - 1) / kStSplitPositions));
 
     for (uint32_t l = 0; l < a.n_layers; l++) {
-        const StackLayerDev Ly = a.layers[l];
+        const StackLayerDev *Ly = a.layers + l;
         const uint32_t par = l & 1;
         const bool more = l + 1 < a.n_layers;
 
@@ -263,19 +507,26 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
         __syncthreads();
         for (uint32_t r = tid; r < nor; r += kStThreads) xres[r] = XF[o0 + r];
         {
+            const float *nw = Ly->attn_norm;
             float ss = 0.0f;
             for (uint32_t i = tid; i < d; i += kStThreads) ss += XF[i] * XF[i];
             ss = ab_block_sum(ss, red);
             const float rms_inv = 1.0f / sqrtf(ss / (float)d + a.eps);
-            for (uint32_t i = tid; i < d; i += kStThreads) XF[i] = XF[i] * rms_inv * __ldg(Ly.attn_norm + i);
+            for (uint32_t i = tid; i < d; i += kStThreads) XF[i] = XF[i] * rms_inv * __ldg(nw + i);
         }
         __syncthreads();
-        ab_quantise(Xx, XF, d, warp, lane);
+        {
+            const XS Xx = xs_carve(XSr, 1, (int)st_items(d));
+            ab_quantise(Xx, XF, d, warp, lane);
+            __syncthreads();
+            if (nqr && st_wait(bq, par, a.dev_err)) st_rows<QT>(W, a.qpitch, nqr, d, a.qnb, Xx, XF);
+        }
         __syncthreads();
-        if (nqr && st_wait(bq, par, a.dev_err)) ab_rows<QT>(W, a.qpitch, nqr, d, a.qnb, Xx, warp, lane, XF);
-        __syncthreads();
-        for (uint32_t r = tid; r < nqr; r += kStThreads)
-            a.qkv[q0 + r] = Ly.bias ? __fadd_rn(XF[r], __ldg(Ly.bias + q0 + r)) : XF[r];
+        {
+            const float *bias = Ly->bias;
+            for (uint32_t r = tid; r < nqr; r += kStThreads)
+                a.qkv[q0 + r] = bias ? __fadd_rn(XF[r], __ldg(bias + q0 + r)) : XF[r];
+        }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // W is copied over next
         ST_MARK(1);
         gsync();
@@ -285,135 +536,25 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
         if (tid == 0) {
             if (nor) {
                 mbar_arrive_expect_tx(bo, (uint32_t)(nor * a.opitch));
-                tma_load_1d(W, Ly.wo + (uint64_t)o0 * a.opitch, (uint32_t)(nor * a.opitch), bo);
+                tma_load_1d(W, Ly->wo + (uint64_t)o0 * a.opitch, (uint32_t)(nor * a.opitch), bo);
             }
             if (more) {  // the next layer's static rows, while HBM is idle
-                const StackLayerDev Ln = a.layers[l + 1];
-                st_prefetch_rows(Ln.wqkv, a.qpitch, q0, nqr);
-                st_prefetch_rows(Ln.wo, a.opitch, o0, nor);
+                st_prefetch_rows(Ly[1].wqkv, a.qpitch, q0, nqr);
+                st_prefetch_rows(Ly[1].wo, a.opitch, o0, nor);
             }
         }
-        {
-            float *hq = XF, *hk = hq + HD, *hv = hk + HD;
-            float *wpart = hv + HD;  // [16][HD + 2]: m, l, o[HD]
-            for (uint32_t item = c; item < a.g.n_heads * S; item += G) {
-                const uint32_t h = item / S, s = item - h * S, kh = h / group;
-                if (tid < 3 * HD / 4) {  // q, k, v heads: one float4 each
-                    const uint32_t pt = tid / (HD / 4), i = tid % (HD / 4);
-                    const size_t off = pt == 0 ? (size_t)h * HD : pt == 1 ? nq + (size_t)kh * HD : nq + nkv + (size_t)kh * HD;
-                    reinterpret_cast<float4 *>(hq + pt * HD)[i] = __ldcg(reinterpret_cast<const float4 *>(a.qkv + off) + i);
-                }
-                __syncthreads();
-                ab_norm_rope2(hq, Ly.q_norm, hk, Ly.k_norm, a.g, pos, red);
-                if (s == 0 && h % group == 0) {  // this position's K/V into the cache
-                    const size_t slot = (size_t)(pos % a.g.cap) * nkv + (size_t)kh * HD;
-                    for (uint32_t i = tid; i < HD; i += kStThreads) {
-                        kv_st(Ly.kc, slot + i, hk[i], a.g.kv_f16);
-                        kv_st(Ly.vc, slot + i, hv[i], a.g.kv_f16);
-                    }
-                }
-                if (a.g.kv_f16) {  // attend to this position as the cache holds it
-                    __syncthreads();
-                    for (uint32_t i = tid; i < HD; i += kStThreads) {
-                        hk[i] = kv_round(hk[i], 1u);
-                        hv[i] = kv_round(hv[i], 1u);
-                    }
-                    __syncthreads();
-                }
-                float o[PER], m = -INFINITY, lsum = 0.0f;
-                if (a.g.kv_f16)
-                    ab_attend<HD, true>(Ly.kc, Ly.vc, a.g, s, S, win, first, (size_t)kh * HD, nkv, hq, hk, hv, warp,
-                                        lane, m, lsum, o);
-                else
-                    ab_attend<HD, false>(Ly.kc, Ly.vc, a.g, s, S, win, first, (size_t)kh * HD, nkv, hq, hk, hv, warp,
-                                         lane, m, lsum, o);
-                float *wp = wpart + warp * (HD + 2);
-                if (lane == 0) {
-                    wp[0] = m;
-                    wp[1] = lsum;
-                }
-#pragma unroll
-                for (int i = 0; i < PER; i++) wp[2 + lane * PER + i] = o[i];
-                __syncthreads();
-                float *sf = wpart + kStWarps * (HD + 2);  // [16] scales, then the sum and the maximum
-                if (warp == 0) {
-                    const float mw = lane < kStWarps ? wpart[lane * (HD + 2)] : -INFINITY;
-                    float M = mw;
-#pragma unroll
-                    for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
-                    if (lane < kStWarps) sf[lane] = mw != -INFINITY ? expf(mw - M) : 0.0f;
-                    __syncwarp();
-                    if (lane == 0) {
-                        float Ls = 0.0f;
-                        for (int w = 0; w < kStWarps; w++) Ls += wpart[w * (HD + 2) + 1] * sf[w];
-                        sf[kStWarps] = Ls;
-                        sf[kStWarps + 1] = M;
-                    }
-                }
-                __syncthreads();
-                if (S == 1) {  // the whole window: normalise, quantise into the attention row
-                    const float Ls = sf[kStWarps];
-                    for (uint32_t t = tid; t < HD; t += kStThreads) {
-                        float acc = 0.0f;
-#pragma unroll
-                        for (int w = 0; w < kStWarps; w++) acc += wpart[w * (HD + 2) + 2 + t] * sf[w];
-                        hq[t] = acc / Ls;
-                    }
-                    __syncthreads();
-                    for (uint32_t b = warp; b < (uint32_t)HD / 32; b += kStWarps)
-                        qact_store_block(a.att, (int)nq, (int)(h * HD / 32 + b), hq[32 * b + lane], lane);
-                    __syncthreads();
-                    continue;
-                }
-                float *po = a.part + ((size_t)h * S + s) * HD;
-                float *pml = a.part + (size_t)a.g.n_heads * S * HD + 2 * ((size_t)h * S + s);
-                for (uint32_t t = tid; t < HD; t += kStThreads) {
-                    float acc = 0.0f;
-#pragma unroll
-                    for (int w = 0; w < kStWarps; w++) acc += wpart[w * (HD + 2) + 2 + t] * sf[w];
-                    po[t] = acc;
-                }
-                if (tid == 0) *reinterpret_cast<float2 *>(pml) = make_float2(sf[kStWarps + 1], sf[kStWarps]);
-                __syncthreads();
-                if (tid == 0) {
-                    __threadfence();
-                    s_last[0] = atomicAdd(head_cnt + h, 1u) == S - 1;
-                }
-                __syncthreads();
-                if (s_last[0]) {  // the last split of head h merges the head's splits
-                    __threadfence();
-                    const float *ho = a.part + (size_t)h * S * HD;
-                    const float *hml = a.part + (size_t)a.g.n_heads * S * HD + 2 * (size_t)h * S;
-                    for (uint32_t t = tid; t < HD; t += kStThreads) {
-                        float GM = -INFINITY;
-                        for (uint32_t q = 0; q < S; q++) GM = fmaxf(GM, __ldcg(hml + 2 * q));
-                        float GL = 0.0f, acc = 0.0f;
-                        for (uint32_t q = 0; q < S; q++) {
-                            const float mk = __ldcg(hml + 2 * q);
-                            if (mk != -INFINITY) {
-                                const float f = expf(mk - GM);
-                                GL += __ldcg(hml + 2 * q + 1) * f;
-                                acc += __ldcg(ho + (size_t)q * HD + t) * f;
-                            }
-                        }
-                        hq[t] = acc / GL;
-                    }
-                    __syncthreads();
-                    for (uint32_t b = warp; b < (uint32_t)HD / 32; b += kStWarps)
-                        qact_store_block(a.att, (int)nq, (int)(h * HD / 32 + b), hq[32 * b + lane], lane);
-                    if (tid == 0) head_cnt[h] = 0;
-                }
-                __syncthreads();
-            }
-        }
+        st_attention<HD>(a, Ly->q_norm, Ly->k_norm, Ly->kc, Ly->vc, XF, red, s_last, head_cnt, pos, S, win, first);
         ST_MARK(3);
         gsync();
         ST_MARK(4);
 
         // ── O ────────────────────────────────────────────────────────────────
-        ab_load_qact(Xa, a.att, nq);
-        __syncthreads();
-        if (nor && st_wait(bo, par, a.dev_err)) ab_rows<OT>(W, a.opitch, nor, nq, a.onb, Xa, warp, lane, XF);
+        {
+            const XS Xa = xs_carve(XSr, 1, (int)st_items(a.nq));
+            ab_load_qact(Xa, a.att, a.nq);
+            __syncthreads();
+            if (nor && st_wait(bo, par, a.dev_err)) st_rows<OT>(W, a.opitch, nor, a.nq, a.onb, Xa, XF);
+        }
         __syncthreads();
         for (uint32_t r = tid; r < nor; r += kStThreads) {
             const float v = __fadd_rn(xres[r], XF[r]);
@@ -442,18 +583,22 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
             }
             __syncthreads();
             const float rms = s_stat[0];
-            for (uint32_t i = tid; i < d; i += kStThreads) XF[i] = XF[i] * rms * __ldg(Ly.ffn_norm + i);
+            const float *nw = Ly->ffn_norm;
+            for (uint32_t i = tid; i < d; i += kStThreads) XF[i] = XF[i] * rms * __ldg(nw + i);
         }
         __syncthreads();
         const uint32_t tag = (uint32_t)(launch * 64 + l + 1);
-        if (has_e && warp == 0) {
-            st_wait(brt, par, a.dev_err);
-            const float v = st_router_logit(RT, XF, d, lane);
-            if (lane == 0) st_relaxed_u64(lslots + c, ((uint64_t)tag << 32) | __float_as_uint(v));
-        } else {
-            const uint32_t w0 = has_e ? 1 : 0;
-            for (uint32_t b = warp - w0; b < d / 32; b += kStWarps - w0)
-                qact_block_to_xs(Xx, 0, (int)b, XF[32 * b + lane], lane);
+        {
+            const XS Xx = xs_carve(XSr, 1, (int)st_items(d));
+            if (has_e && warp == 0) {
+                st_wait(brt, par, a.dev_err);
+                const float v = st_router_logit(RT, XF, d, lane);
+                if (lane == 0) st_relaxed_u64(lslots + c, ((uint64_t)tag << 32) | __float_as_uint(v));
+            } else {
+                const uint32_t w0 = has_e ? 1 : 0;
+                for (uint32_t b = warp - w0; b < d / 32; b += kStWarps - w0)
+                    qact_block_to_xs(Xx, 0, (int)b, XF[32 * b + lane], lane);
+            }
         }
         if (!a.dense && (uint32_t)tid < a.E) {  // poll expert tid's logit until it carries this layer's tag
             uint64_t v = ld_relaxed_u64(lslots + tid);
@@ -489,10 +634,11 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
             router_rank_keys_split(s_key, a.E, a.k, s_sel, min(4u, (uint32_t)(kStThreads - 32) / a.E), s_cnt, tid);
         }
         __syncthreads();
-
         ST_MARK(7);
+
         // ── G ────────────────────────────────────────────────────────────────
         if (warp == 0) {  // one TMA chunk per lane: [8 gate rows][8 up rows] of pairs p0 + 8j..
+            const uint8_t *gate = Ly->gate, *upt = Ly->up;
             for (uint32_t j = lane; j < nchunks; j += 32) {
                 const uint32_t qq = p0 + j * kStChunk;
                 const uint32_t s = qq / a.F, f0 = qq - s * a.F;
@@ -500,18 +646,18 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
                 const uint32_t bytes = (uint32_t)(kStChunk * a.gpitch);
                 uint64_t grow, urow;
                 const uint8_t *ub;
-                if (Ly.up) {
+                if (upt) {
                     grow = (uint64_t)e * a.F + f0;
                     urow = grow;
-                    ub = Ly.up;
+                    ub = upt;
                 } else {  // fused: gate rows [0,F), up rows [F,2F) (gemma4/forward.zig:469-471)
                     grow = (uint64_t)e * 2 * a.F + f0;
                     urow = grow + a.F;
-                    ub = Ly.gate;
+                    ub = gate;
                 }
                 uint8_t *dst = W + (size_t)2 * j * kStChunk * a.gpitch;
                 mbar_arrive_expect_tx(&bch[j], 2 * bytes);
-                tma_load_1d(dst, Ly.gate + grow * a.gpitch, bytes, &bch[j]);
+                tma_load_1d(dst, gate + grow * a.gpitch, bytes, &bch[j]);
                 tma_load_1d(dst + bytes, ub + urow * a.gpitch, bytes, &bch[j]);
             }
         } else if (warp == 1) {  // down rows [o0, o1) of each slot's expert
@@ -519,7 +665,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
                 const uint32_t e = min(s_sel[lane], a.E - 1);
                 const uint32_t bytes = (uint32_t)(nor * a.dpitch);
                 mbar_arrive_expect_tx(&bdn[lane], bytes);
-                tma_load_1d(DN + (size_t)lane * a.maxo * a.dpitch, Ly.down + ((uint64_t)e * d + o0) * a.dpitch, bytes,
+                tma_load_1d(DN + (size_t)lane * a.maxo * a.dpitch, Ly->down + ((uint64_t)e * d + o0) * a.dpitch, bytes,
                             &bdn[lane]);
             }
         } else if (warp == 2 && lane == 0) {
@@ -528,45 +674,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
             else
                 router_weights(s_lg, s_sel, a.k, s_stat[1], s_stat[2], a.norm_topk, nullptr, s_w);
         }
-        {  // gate/up rows: warp w takes tile rows w*rps.., a lane owns one 64-column chunk of x in registers
-            const uint32_t cpr = st_chunks64(d);
-            const uint32_t gstride = 2 * a.maxpairs + 1;
-            const uint32_t lpr = min(cpr, 32u), rps = 32 / lpr;
-            const uint32_t sub = lane / lpr, nrows = 2 * np;
-            if (sub < rps) {
-                for (uint32_t cg = 0; cg < cpr; cg += lpr) {
-                    const uint32_t n = min(lpr, cpr - cg);
-                    if ((uint32_t)lane % lpr >= n) continue;
-                    const uint32_t cb = cg + spread_chunk((uint32_t)lane % lpr, n);
-                    XChunk xc;
-                    xchunk_load(Xx, 0, (int)cb, xc);
-                    const uint32_t step = kStWarps * rps;
-                    for (uint32_t r = warp * rps + sub; r < nrows; r += 2 * step) {
-                        const uint32_t rb = r + step < nrows ? r + step : r;
-                        const bool ok = st_wait(&bch[r / (2 * kStChunk)], par, a.dev_err) &
-                                        st_wait(&bch[rb / (2 * kStChunk)], par, a.dev_err);
-                        float ya = 0.0f, yb = 0.0f;
-                        if (ok) {
-                            ya = dot64<GT>(W + (size_t)r * a.gpitch, (int)cb, (int)a.gnb, xc);
-                            yb = dot64<GT>(W + (size_t)rb * a.gpitch, (int)cb, (int)a.gnb, xc);
-                        }
-                        part[cb * gstride + r] = ya;
-                        part[cb * gstride + rb] = yb;
-                    }
-                }
-            }
-            __syncthreads();
-            for (uint32_t lp = tid; lp < np; lp += kStThreads) {  // chunk partials summed in column order
-                const uint32_t rg = 2 * kStChunk * (lp / kStChunk) + lp % kStChunk;
-                const float *pg = part + rg, *pu = pg + kStChunk;
-                float g = 0.0f, u = 0.0f;
-                for (uint32_t i = 0; i < cpr; i++) {
-                    g += pg[i * gstride];
-                    u += pu[i * gstride];
-                }
-                s_h[lp] = act_apply(a.act, g) * u;
-            }
-        }
+        st_gate_up<GT>(a, W, XF, xs_carve(XSr, 1, (int)st_items(d)), bch, par, np, s_h);
         __syncthreads();
         // quantise this CTA's h values into their slots' images (32-blocks; a block may be half this CTA's)
         for (uint32_t b = p0 / 32 + warp; b * 32 < p1; b += kStWarps) {
@@ -576,7 +684,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
             const XS Xs = xs_carve(a.himg + (size_t)s * a.img, 1, (int)a.di);
             qact_block_to_xs(Xs, 0, (int)bs, own ? s_h[qq - p0] : 0.0f, lane, own);
         }
-        fence_proxy_async_global();  // the images are read by TMA after the barrier
+        fence_proxy_async_global();  // the images are read by TMA after the hand-off
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // W, RT and XS are copied over next
         ST_MARK(8);
         gsync();
@@ -589,55 +697,16 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(StackArgs a) {
             for (uint32_t s = 0; s < a.k; s++)
                 tma_load_1d(XSr + (size_t)s * a.img, a.himg + (size_t)s * a.img, a.img, bh);
             if (more) {  // the next layer's Q/K/V rows and router row (from L2 by now)
-                const StackLayerDev Ln = a.layers[l + 1];
                 mbar_arrive_expect_tx(bq, (uint32_t)(nqr * a.qpitch));
-                tma_load_1d(W, Ln.wqkv + (uint64_t)q0 * a.qpitch, (uint32_t)(nqr * a.qpitch), bq);
+                tma_load_1d(W, Ly[1].wqkv + (uint64_t)q0 * a.qpitch, (uint32_t)(nqr * a.qpitch), bq);
                 if (has_e) {
                     mbar_arrive_expect_tx(brt, d * 4);
-                    tma_load_1d(RT, Ln.router + (size_t)c * d, d * 4, brt);
+                    tma_load_1d(RT, Ly[1].router + (size_t)c * d, d * 4, brt);
                 }
             }
         }
         const bool hok = st_wait(bh, par, a.dev_err);
-        {  // warps [s*wps, (s+1)*wps) take slot s; a lane owns one 64-column chunk of that slot's h
-            const uint32_t cpr = st_chunks64(a.F);
-            const uint32_t dstride = a.k * a.maxo + 1;
-            const uint32_t lpr = min(cpr, 32u), rps = 32 / lpr;
-            const uint32_t sub = lane / lpr;
-            const uint32_t wps = max(1u, (uint32_t)kStWarps / a.k);
-            const uint32_t s = warp / wps, ws = warp % wps;
-            if (s < a.k && sub < rps && nor) {
-                const bool ok = st_wait(&bdn[s], par, a.dev_err) && hok;
-                const XS Xh = xs_carve(XSr + (size_t)s * a.img, 1, (int)a.di);
-                for (uint32_t cg = 0; cg < cpr; cg += lpr) {
-                    const uint32_t n = min(lpr, cpr - cg);
-                    if ((uint32_t)lane % lpr >= n) continue;
-                    const uint32_t cb = cg + spread_chunk((uint32_t)lane % lpr, n);
-                    XChunk xc;
-                    xchunk_load(Xh, 0, (int)cb, xc);
-                    const uint32_t step = wps * rps;
-                    for (uint32_t r = ws * rps + sub; r < nor; r += 2 * step) {
-                        const uint32_t rb = r + step < nor ? r + step : r;
-                        const uint32_t ta = s * a.maxo + r, tb = s * a.maxo + rb;
-                        float ya = 0.0f, yb = 0.0f;
-                        if (ok) {
-                            ya = dot64<DT>(DN + (size_t)ta * a.dpitch, (int)cb, (int)a.dnb, xc);
-                            yb = dot64<DT>(DN + (size_t)tb * a.dpitch, (int)cb, (int)a.dnb, xc);
-                        }
-                        part[cb * dstride + ta] = ya;
-                        part[cb * dstride + tb] = yb;
-                    }
-                }
-            }
-            __syncthreads();
-            for (uint32_t w = tid; w < a.k * nor; w += kStThreads) {  // y[s][r]: chunk partials in column order
-                const uint32_t s2 = w / nor, r = w - s2 * nor;
-                const float *pp = part + s2 * a.maxo + r;
-                float y = 0.0f;
-                for (uint32_t i = 0; i < cpr; i++) y += pp[i * dstride];
-                s_y[s2 * a.maxo + r] = y;
-            }
-        }
+        st_down<DT>(a, DN, XSr, XF, s_y, bdn, par, nor, hok);
         __syncthreads();
         for (uint32_t r = tid; r < nor; r += kStThreads) {
             float o = 0.0f;  // moe_buf is zeroed, then += scale * down, slot by slot
@@ -684,7 +753,7 @@ StScratch st_scratch(const StackParams &p, uint32_t splits) {
 bool stack_plan(const StackParams &p, int num_sms, size_t *smem_out, size_t *scratch_bytes, size_t *sync_offset) {
     const AttnGeom &g = p.g;
     const uint32_t G = (uint32_t)num_sms;
-    if (p.n_layers == 0 || p.n_layers > 63 || num_sms <= 0) return false;
+    if (p.n_layers == 0 || p.n_layers > 63 || num_sms <= 0 || (uint32_t)num_sms > kStMaxCtas) return false;
     if (g.hd != 64 && g.hd != 128) return false;
     if (g.window != 0 || g.v_norm != 0 || g.n_kv == 0 || g.n_heads % g.n_kv != 0) return false;
     if (p.d % 256 != 0 && p.qtype != T_Q8_0) return false;
