@@ -20,8 +20,9 @@
 //      the previous layer's D phase)                          -> barrier
 //   A  (head, split) items: Q/K norm, RoPE, K/V append, online-softmax
 //      attention over the split's positions; the last split of a head merges
-//      it into the quantised attention row.  The wo rows are copied meanwhile,
-//      and the next layer's Q/K/V and wo rows prefetched into L2 -> barrier
+//      it into the quantised attention row.  The wo rows are copied meanwhile
+//      (an L2 prefetch of the next layer's rows here measured ~1.5 us slower
+//      per layer: it competes with the attention's loads)       -> barrier
 //   O  wo rows, residual: x' (kept in shared memory for the MoE residual)
 //                                                             -> barrier
 //   R  x' -> RMSNorm; CTA e computes the logit of expert e (router row copied
@@ -51,11 +52,11 @@ constexpr uint32_t kStSplitPositions = 32;  // positions per attention split bef
 constexpr uint32_t kStMaxSplits = 8;
 constexpr int kStNormThreads = 128;       // k_moe_decode's RMSNorm reduction width
 
-// The plan's sync block (kStackSyncBytes): launch counter, tagged logits,
-// per-head merge counters, per-CTA hand-off flags.
-constexpr size_t kStEpoch = 0, kStLogits = 256, kStHeadCnt = kStLogits + 8 * kRouterMaxE, kStFlags = 8192;
+// The plan's sync block (kStackSyncBytes): launch counter, hand-off counter,
+// tagged logits, per-head merge counters.
+constexpr size_t kStEpoch = 0, kStBar = 128, kStLogits = 256, kStHeadCnt = kStLogits + 8 * kRouterMaxE;
 constexpr uint32_t kStMaxCtas = 1024;
-static_assert(kStHeadCnt + 4 * 1024 <= kStFlags && kStFlags + 8 * kStMaxCtas <= kStackSyncBytes, "sync block");
+static_assert(kStHeadCnt + 4 * 1024 <= kStackSyncBytes, "sync block");
 
 struct StackArgs {
     AttnGeom g;
@@ -140,7 +141,7 @@ LT_DEVINL void st_prefetch_rows(const uint8_t *base, uint64_t pitch, uint32_t r0
 // records globaltimer at the phase boundaries of every layer.  Off in the
 // library the package builds.
 #ifdef LT_STACK_TRACE
-constexpr int kTraceCtas = 160, kTraceLayers = 64, kTraceMarks = 16;
+constexpr int kTraceCtas = 160, kTraceLayers = 64, kTraceMarks = 32;
 __device__ unsigned long long g_stack_trace[kTraceCtas * kTraceLayers * kTraceMarks];
 #define ST_MARK(m)                                                                              \
     do {                                                                                       \
@@ -173,23 +174,22 @@ LT_DEVINL float st_router_logit(const float *wsm, const float *xs, uint32_t cols
 }
 
 // ── grid hand-off ───────────────────────────────────────────────────────────
-// One flag per CTA, holding the sequence number of the last hand-off the CTA
-// reached (launch * barriers per launch + barrier + 1: it only grows, so the
-// flags are never reset).  A CTA publishes its writes with one release store;
-// thread i of every CTA waits for CTA i's flag with acquire loads, then the
-// block barrier passes the order on to the CTA's other threads.  No atomics:
-// the G arrivals do not queue on one address.
-LT_DEVINL void st_release_u64(unsigned long long *p, uint64_t v) {
-    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-LT_DEVINL void st_grid_sync(unsigned long long *flags, uint32_t c, uint32_t G, uint64_t seqn, int *dev_err) {
+// One counter that only grows: every CTA adds 1 per hand-off, so hand-off n
+// (counted over all launches of the plan, from 1) completes at n * G.  The
+// arrival is one release add by thread 0 after the block barrier (the
+// release covers the CTA's writes ordered before it by that barrier), the
+// wait one acquire poll by thread 0 before the next block barrier.  Measured
+// on B200: ~1 us from the last arrival to the first departure, against ~3.5
+// us for per-CTA flags polled by every CTA (G x G acquire loads at once) and
+// ~2 us with a full fence before the add.
+LT_DEVINL void st_grid_sync(unsigned long long *ctr, uint32_t G, uint64_t seqn, int *dev_err) {
     __syncthreads();
-    if (threadIdx.x == 0) st_release_u64(flags + c, seqn);
-    for (uint32_t i = threadIdx.x; i < G; i += blockDim.x) {
-        if (ld_acquire_u64(flags + i) < seqn) {
+    if (threadIdx.x == 0) {
+        red_release_add_u64(ctr, 1ull);
+        const uint64_t target = seqn * G;
+        if (ld_acquire_u64(ctr) < target) {
             const uint64_t t0 = globaltimer_ns();
-            while (ld_acquire_u64(flags + i) < seqn) {
+            while (ld_acquire_u64(ctr) < target) {
                 if (globaltimer_ns() - t0 > kWaitLimitNs) {
                     if (dev_err) atomicExch(dev_err, DEV_ERR_GRID_TIMEOUT);
                     break;
@@ -448,7 +448,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
     float *s_y = reinterpret_cast<float *>(smem + L.ys);
     float *xres = reinterpret_cast<float *>(smem + L.xres);
     unsigned long long *ctr_e = reinterpret_cast<unsigned long long *>(a.sync + kStEpoch);
-    unsigned long long *flags = reinterpret_cast<unsigned long long *>(a.sync + kStFlags);
+    unsigned long long *ctr_b = reinterpret_cast<unsigned long long *>(a.sync + kStBar);
     unsigned long long *lslots = reinterpret_cast<unsigned long long *>(a.sync + kStLogits);
     uint32_t *head_cnt = reinterpret_cast<uint32_t *>(a.sync + kStHeadCnt);
     const uint32_t d = a.d;
@@ -488,7 +488,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
     const uint64_t launch = *s_launch;
     uint32_t nb = 0;  // grid hand-offs passed in this launch
     auto gsync = [&]() {
-        st_grid_sync(flags, c, G, (uint64_t)launch * a.nbar + nb + 1, a.dev_err);
+        st_grid_sync(ctr_b, G, (uint64_t)launch * a.nbar + nb + 1, a.dev_err);
         nb++;
     };
     pdl_wait();
@@ -505,6 +505,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
         ST_MARK(0);
         ab_load(XF, a.x, d);
         __syncthreads();
+        ST_MARK(12);
         for (uint32_t r = tid; r < nor; r += kStThreads) xres[r] = XF[o0 + r];
         {
             const float *nw = Ly->attn_norm;
@@ -515,13 +516,18 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
             for (uint32_t i = tid; i < d; i += kStThreads) XF[i] = XF[i] * rms_inv * __ldg(nw + i);
         }
         __syncthreads();
+        ST_MARK(13);
         {
             const XS Xx = xs_carve(XSr, 1, (int)st_items(d));
             ab_quantise(Xx, XF, d, warp, lane);
             __syncthreads();
-            if (nqr && st_wait(bq, par, a.dev_err)) st_rows<QT>(W, a.qpitch, nqr, d, a.qnb, Xx, XF);
+            ST_MARK(14);
+            const bool ok = nqr && st_wait(bq, par, a.dev_err);
+            ST_MARK(15);
+            if (ok) st_rows<QT>(W, a.qpitch, nqr, d, a.qnb, Xx, XF);
         }
         __syncthreads();
+        ST_MARK(16);
         {
             const float *bias = Ly->bias;
             for (uint32_t r = tid; r < nqr; r += kStThreads)
@@ -538,10 +544,6 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
                 mbar_arrive_expect_tx(bo, (uint32_t)(nor * a.opitch));
                 tma_load_1d(W, Ly->wo + (uint64_t)o0 * a.opitch, (uint32_t)(nor * a.opitch), bo);
             }
-            if (more) {  // the next layer's static rows, while HBM is idle
-                st_prefetch_rows(Ly[1].wqkv, a.qpitch, q0, nqr);
-                st_prefetch_rows(Ly[1].wo, a.opitch, o0, nor);
-            }
         }
         st_attention<HD>(a, Ly->q_norm, Ly->k_norm, Ly->kc, Ly->vc, XF, red, s_last, head_cnt, pos, S, win, first);
         ST_MARK(3);
@@ -553,7 +555,10 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
             const XS Xa = xs_carve(XSr, 1, (int)st_items(a.nq));
             ab_load_qact(Xa, a.att, a.nq);
             __syncthreads();
-            if (nor && st_wait(bo, par, a.dev_err)) st_rows<OT>(W, a.opitch, nor, a.nq, a.onb, Xa, XF);
+            ST_MARK(28);
+            const bool ok = nor && st_wait(bo, par, a.dev_err);
+            ST_MARK(29);
+            if (ok) st_rows<OT>(W, a.opitch, nor, a.nq, a.onb, Xa, XF);
         }
         __syncthreads();
         for (uint32_t r = tid; r < nor; r += kStThreads) {
@@ -569,6 +574,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
         // ── R ────────────────────────────────────────────────────────────────
         ab_load(XF, a.x, d);
         __syncthreads();
+        ST_MARK(17);
         {  // rmsnorm(out, x, w, eps) with k_moe_decode's reduction order
             float ss = 0.0f;
             if (tid < kStNormThreads)
@@ -587,6 +593,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
             for (uint32_t i = tid; i < d; i += kStThreads) XF[i] = XF[i] * rms * __ldg(nw + i);
         }
         __syncthreads();
+        ST_MARK(18);
         const uint32_t tag = (uint32_t)(launch * 64 + l + 1);
         {
             const XS Xx = xs_carve(XSr, 1, (int)st_items(d));
@@ -600,6 +607,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
                     qact_block_to_xs(Xx, 0, (int)b, XF[32 * b + lane], lane);
             }
         }
+        ST_MARK(19);
         if (!a.dense && (uint32_t)tid < a.E) {  // poll expert tid's logit until it carries this layer's tag
             uint64_t v = ld_relaxed_u64(lslots + tid);
             if ((uint32_t)(v >> 32) != tag) {
@@ -622,6 +630,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
             if (a.dense) s_sel[0] = 0;
         }
         __syncthreads();
+        ST_MARK(20);
         if (!a.dense) {
             if (warp == kStWarps - 1) {
                 float mxv, es;
@@ -674,8 +683,10 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
             else
                 router_weights(s_lg, s_sel, a.k, s_stat[1], s_stat[2], a.norm_topk, nullptr, s_w);
         }
+        ST_MARK(22);
         st_gate_up<GT>(a, W, XF, xs_carve(XSr, 1, (int)st_items(d)), bch, par, np, s_h);
         __syncthreads();
+        ST_MARK(23);
         // quantise this CTA's h values into their slots' images (32-blocks; a block may be half this CTA's)
         for (uint32_t b = p0 / 32 + warp; b * 32 < p1; b += kStWarps) {
             const uint32_t qq = 32 * b + lane;
@@ -684,6 +695,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
             const XS Xs = xs_carve(a.himg + (size_t)s * a.img, 1, (int)a.di);
             qact_block_to_xs(Xs, 0, (int)bs, own ? s_h[qq - p0] : 0.0f, lane, own);
         }
+        ST_MARK(24);
         fence_proxy_async_global();  // the images are read by TMA after the hand-off
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // W, RT and XS are copied over next
         ST_MARK(8);
@@ -706,8 +718,10 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
             }
         }
         const bool hok = st_wait(bh, par, a.dev_err);
+        ST_MARK(25);
         st_down<DT>(a, DN, XSr, XF, s_y, bdn, par, nor, hok);
         __syncthreads();
+        ST_MARK(26);
         for (uint32_t r = tid; r < nor; r += kStThreads) {
             float o = 0.0f;  // moe_buf is zeroed, then += scale * down, slot by slot
             for (uint32_t s = 0; s < a.k; s++) o += s_w[s] * s_y[s * a.maxo + r];
