@@ -1026,6 +1026,10 @@ lt_status lt_stack_create(lt_ctx *ctx, const lt_attn_cfg *cfg, uint32_t d_model,
         if (ok && !dense) ok = L.router->m.type == LT_TYPE_F32 && L.router->m.rows == p.E &&
                                L.router->m.cols == d_model && L.router->m.pitch == (uint64_t)d_model * 4;
         if (!ok) return fail(ctx, LT_EINVAL, "lt_stack_create: layer %u differs from layer 0 or lacks a tensor", l);
+        // the norm weights are copied into shared memory by TMA: 16-byte aligned
+        auto a16 = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+        if (!a16(L.attn_norm) || !a16(L.ffn_norm) || !a16(L.q_norm) || !a16(L.k_norm))
+            return fail(ctx, LT_EUNSUPPORTED_TYPE, "lt_stack_create: layer %u norm weights not 16-byte aligned", l);
         lt::StackLayerDev &o = dl[l];
         o.wqkv = L.wqkv->m.data;
         o.wo = L.wo->m.data;
@@ -1040,6 +1044,7 @@ lt_status lt_stack_create(lt_ctx *ctx, const lt_attn_cfg *cfg, uint32_t d_model,
         o.gate = L.gate->m.data;
         o.up = L.up->m.data;
         o.down = L.down->m.data;
+        o.reserved = 0;
     }
     size_t smem = 0, scratch = 0, sync_off = 0;
     if (!lt::stack_plan(p, ctx->num_sms, &smem, &scratch, &sync_off))

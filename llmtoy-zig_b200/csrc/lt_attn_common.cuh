@@ -27,6 +27,7 @@ LT_DEVINL float ab_block_sum(float v, float *red) {
 
 // x[0, n) (f32, shared) -> quantised rows of X (16 warps, 32-blocks).
 LT_DEVINL void ab_quantise(const XS &X, const float *xf, uint32_t n, int warp, int lane) {
+#pragma unroll 4
     for (uint32_t b = warp; b < (n + 31) / 32; b += kAbWarps) {
         const uint32_t e = 32 * b + lane;
         qact_block_to_xs(X, 0, (int)b, e < n ? xf[e] : 0.0f, lane);
@@ -83,10 +84,9 @@ LT_DEVINL void ab_load_qact(const XS &X, const uint8_t *row, uint32_t cols) {
 // own 64-column chunks (spread_chunk within each group of 32), loaded once per chunk;
 // warp w takes rows 4w .. 4w+3 (then 64 further): each activation chunk a
 // warp loads serves four rows, so few warps load it.
-template <uint32_t T>
+template <uint32_t T, int R = 4>
 LT_DEVINL void ab_rows(const uint8_t *tile, uint64_t pitch, uint32_t nrows, uint32_t cols, uint32_t nb, const XS &X,
                        int warp, int lane, float *y) {
-    constexpr int R = 4;
     const uint32_t nch = (cols + 63) / 64;
     for (uint32_t r0 = warp * R; r0 < nrows; r0 += kAbWarps * R) {
         float acc[R];

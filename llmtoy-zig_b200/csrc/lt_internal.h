@@ -263,7 +263,9 @@ struct StackLayerDev {
     void *kc, *vc;
     const float *router;              // nullptr: a dense FFN (gate/up/down are 2-D)
     const uint8_t *gate, *up, *down;  // up == nullptr: fused gate_up
+    uint64_t reserved;                // 112 bytes: the table is copied to shared memory by TMA
 };
+static_assert(sizeof(StackLayerDev) % 16 == 0, "layer descriptor size");
 struct StackParams {
     AttnGeom g;
     uint32_t d, E, k, F;

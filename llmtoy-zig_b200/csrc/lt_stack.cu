@@ -79,7 +79,8 @@ struct StackArgs {
 };
 
 struct StLayout {
-    size_t bars, misc, lg, keys, cnt, w, dn, rt, xs, xf, hs, ys, xres, total;
+    size_t bars, misc, lg, keys, cnt, w, dn, rt, xs, xf, hs, ys, xres, lay, bias, total;
+    size_t an, fn, qn, kn;  // norm weights inside W, after the Q/K/V or wo tile
 };
 
 __host__ __device__ inline uint32_t st_chunks64(uint32_t cols) { return (cols + 63) / 64; }
@@ -102,7 +103,18 @@ __host__ __device__ inline StLayout st_layout(const StackArgs &a) {
     // + slack: the last Q8_0 chunk of a row reads up to 34 bytes past it
     const size_t qt = (size_t)a.maxq * a.qpitch, ot = (size_t)a.maxo * a.opitch;
     const size_t gt = (size_t)2 * a.maxpairs * a.gpitch;
-    L.w = take(mx(mx(qt, ot), gt) + 128);
+    // the layer's norm weights ride with its static tiles: attn_norm and the
+    // Q/K norms with the Q/K/V rows, ffn_norm with the wo rows
+    const size_t t0 = (mx(qt, ot) + 128 + 127) & ~(size_t)127;
+    L.an = t0;
+    L.fn = L.an + (size_t)a.d * 4;
+    L.qn = L.fn + (size_t)a.d * 4;
+    L.kn = L.qn + (size_t)a.g.hd * 4;
+    L.w = take(mx(L.kn + (size_t)a.g.hd * 4, gt + 128));
+    L.an += L.w;
+    L.fn += L.w;
+    L.qn += L.w;
+    L.kn += L.w;
     L.dn = take((size_t)a.k * a.maxo * a.dpitch + 128);
     L.rt = take(a.dense ? 0 : (size_t)a.d * 4);
     L.xs = take(mx(mx(xs_bytes(1, (int)st_items(a.d)), xs_bytes(1, (int)st_items(a.nq))), (size_t)a.k * a.img));
@@ -115,6 +127,8 @@ __host__ __device__ inline StLayout st_layout(const StackArgs &a) {
     L.hs = take((size_t)a.maxpairs * 4);
     L.ys = take((size_t)a.k * a.maxo * 4);
     L.xres = take((size_t)a.maxo * 4);
+    L.lay = take((size_t)a.n_layers * sizeof(StackLayerDev));
+    L.bias = take((size_t)a.maxq * 4);
     L.total = off;
     return L;
 }
@@ -158,7 +172,8 @@ __device__ unsigned long long g_stack_trace[kTraceCtas * kTraceLayers * kTraceMa
 LT_DEVINL float st_router_logit(const float *wsm, const float *xs, uint32_t cols, int lane) {
     const uint32_t n32 = cols & ~31u;
     float acc = 0.0f;
-    for (uint32_t j = 0; 32u * j < n32; j++) acc = __fadd_rn(acc, __fmul_rn(wsm[32 * j + lane], xs[32 * j + lane]));
+#pragma unroll 16
+    for (uint32_t j = 0; j < n32 / 32; j++) acc = __fadd_rn(acc, __fmul_rn(wsm[32 * j + lane], xs[32 * j + lane]));
     uint32_t i = n32;
     const float a1 = __shfl_sync(0xffffffffu, acc, (lane + 8) & 31);
     const float a2 = __shfl_sync(0xffffffffu, acc, (lane + 16) & 31);
@@ -205,10 +220,20 @@ LT_DEVINL void st_grid_sync(unsigned long long *ctr, uint32_t G, uint64_t seqn, 
 // layer loop.
 
 // rows [0, nrows) of a shared tile against X (ab_rows).
+// Rows per warp: as few as fill the 16 warps (a warp's rows run one after
+// another; the chunk each lane takes, so every row's sum order, is the same).
 template <uint32_t T>
 __device__ __noinline__ void st_rows(const uint8_t *tile, uint64_t pitch, uint32_t nrows, uint32_t cols, uint32_t nb,
                                      XS X, float *y) {
-    ab_rows<T>(tile, pitch, nrows, cols, nb, X, (int)(threadIdx.x >> 5), (int)(threadIdx.x & 31), y);
+    const int warp = (int)(threadIdx.x >> 5), lane = (int)(threadIdx.x & 31);
+    if (nrows <= (uint32_t)kStWarps)
+        ab_rows<T, 1>(tile, pitch, nrows, cols, nb, X, warp, lane, y);
+    else if (nrows <= 2u * kStWarps)
+        ab_rows<T, 2>(tile, pitch, nrows, cols, nb, X, warp, lane, y);
+    else if (nrows <= 3u * kStWarps)
+        ab_rows<T, 3>(tile, pitch, nrows, cols, nb, X, warp, lane, y);
+    else
+        ab_rows<T, 4>(tile, pitch, nrows, cols, nb, X, warp, lane, y);
 }
 
 // Phase A: the (head, split) items of this CTA (k_attn_block's phase A).
@@ -421,6 +446,19 @@ __device__ __noinline__ void st_down(const StackArgs &a, const uint8_t *DN, uint
     }
 }
 
+// Thread 0: copy a layer's Q/K/V rows [q0, q0 + nqr), attn_norm and the Q/K
+// norms into shared memory, all on barrier bq.
+LT_DEVINL void st_issue_q(const StackArgs &a, const StLayout &L, uint8_t *smem, const StackLayerDev &Ly, uint32_t q0,
+                          uint32_t nqr, uint64_t *bq) {
+    const uint32_t hb = a.g.hd * 4;
+    const uint32_t bytes = (uint32_t)(nqr * a.qpitch) + a.d * 4 + (Ly.q_norm ? hb : 0) + (Ly.k_norm ? hb : 0);
+    mbar_arrive_expect_tx(bq, bytes);
+    tma_load_1d(smem + L.w, Ly.wqkv + (uint64_t)q0 * a.qpitch, (uint32_t)(nqr * a.qpitch), bq);
+    tma_load_1d(smem + L.an, Ly.attn_norm, a.d * 4, bq);
+    if (Ly.q_norm) tma_load_1d(smem + L.qn, Ly.q_norm, hb, bq);
+    if (Ly.k_norm) tma_load_1d(smem + L.kn, Ly.k_norm, hb, bq);
+}
+
 template <uint32_t QT, uint32_t OT, int HD, uint32_t GT, uint32_t DT>
 __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__ StackArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -447,6 +485,11 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
     float *s_h = reinterpret_cast<float *>(smem + L.hs);
     float *s_y = reinterpret_cast<float *>(smem + L.ys);
     float *xres = reinterpret_cast<float *>(smem + L.xres);
+    const StackLayerDev *s_lay = reinterpret_cast<const StackLayerDev *>(smem + L.lay);
+    float *s_bias = reinterpret_cast<float *>(smem + L.bias);
+    float *s_an = reinterpret_cast<float *>(smem + L.an), *s_fn = reinterpret_cast<float *>(smem + L.fn);
+    float *s_qn = reinterpret_cast<float *>(smem + L.qn), *s_kn = reinterpret_cast<float *>(smem + L.kn);
+    uint64_t *blay = bars + 4;
     unsigned long long *ctr_e = reinterpret_cast<unsigned long long *>(a.sync + kStEpoch);
     unsigned long long *ctr_b = reinterpret_cast<unsigned long long *>(a.sync + kStBar);
     unsigned long long *lslots = reinterpret_cast<unsigned long long *>(a.sync + kStLogits);
@@ -470,20 +513,25 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
         mbar_init(bo, 1);
         mbar_init(brt, 1);
         mbar_init(bh, 1);
+        mbar_init(blay, 1);
         for (uint32_t s = 0; s < a.k; s++) mbar_init(&bdn[s], 1);
         for (uint32_t j = 0; j < nchunks; j++) mbar_init(&bch[j], 1);
         fence_barrier_init();
         *s_launch = atomicAdd(ctr_e, 1ull) / G;  // every CTA adds 1 per launch
-        // the first layer's static tiles
+        // the layer table, then the first layer's static tiles
+        const uint32_t lay_bytes = a.n_layers * (uint32_t)sizeof(StackLayerDev);
+        mbar_arrive_expect_tx(blay, lay_bytes);
+        tma_load_1d(smem + L.lay, a.layers, lay_bytes, blay);
         const StackLayerDev &L0 = a.layers[0];
-        mbar_arrive_expect_tx(bq, (uint32_t)(nqr * a.qpitch));
-        tma_load_1d(W, L0.wqkv + (uint64_t)q0 * a.qpitch, (uint32_t)(nqr * a.qpitch), bq);
+        st_issue_q(a, L, smem, L0, q0, nqr, bq);
         if (has_e) {
             mbar_arrive_expect_tx(brt, d * 4);
             tma_load_1d(RT, L0.router + (size_t)c * d, d * 4, brt);
         }
         st_prefetch_rows(L0.wo, a.opitch, o0, nor);
     }
+    if (tid < nqr) s_bias[tid] = a.layers[0].bias ? __ldg(a.layers[0].bias + q0 + tid) : 0.0f;
+    if (tid == 0) st_wait(blay, 0, a.dev_err);
     __syncthreads();
     const uint64_t launch = *s_launch;
     uint32_t nb = 0;  // grid hand-offs passed in this launch
@@ -497,7 +545,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
     const uint32_t S = min(a.splits, max(1u, (win + kStSplitPositions - 1) / kStSplitPositions));
 
     for (uint32_t l = 0; l < a.n_layers; l++) {
-        const StackLayerDev *Ly = a.layers + l;
+        const StackLayerDev *Ly = s_lay + l;
         const uint32_t par = l & 1;
         const bool more = l + 1 < a.n_layers;
 
@@ -507,13 +555,13 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
         __syncthreads();
         ST_MARK(12);
         for (uint32_t r = tid; r < nor; r += kStThreads) xres[r] = XF[o0 + r];
+        const bool qok = nqr && st_wait(bq, par, a.dev_err);  // the Q/K/V rows and the layer's norm weights
         {
-            const float *nw = Ly->attn_norm;
             float ss = 0.0f;
             for (uint32_t i = tid; i < d; i += kStThreads) ss += XF[i] * XF[i];
             ss = ab_block_sum(ss, red);
             const float rms_inv = 1.0f / sqrtf(ss / (float)d + a.eps);
-            for (uint32_t i = tid; i < d; i += kStThreads) XF[i] = XF[i] * rms_inv * __ldg(nw + i);
+            for (uint32_t i = tid; i < d; i += kStThreads) XF[i] = XF[i] * rms_inv * s_an[i];
         }
         __syncthreads();
         ST_MARK(13);
@@ -522,16 +570,14 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
             ab_quantise(Xx, XF, d, warp, lane);
             __syncthreads();
             ST_MARK(14);
-            const bool ok = nqr && st_wait(bq, par, a.dev_err);
             ST_MARK(15);
-            if (ok) st_rows<QT>(W, a.qpitch, nqr, d, a.qnb, Xx, XF);
+            if (qok) st_rows<QT>(W, a.qpitch, nqr, d, a.qnb, Xx, XF);
         }
         __syncthreads();
         ST_MARK(16);
         {
-            const float *bias = Ly->bias;
-            for (uint32_t r = tid; r < nqr; r += kStThreads)
-                a.qkv[q0 + r] = bias ? __fadd_rn(XF[r], __ldg(bias + q0 + r)) : XF[r];
+            const bool bias = Ly->bias != nullptr;
+            for (uint32_t r = tid; r < nqr; r += kStThreads) a.qkv[q0 + r] = bias ? __fadd_rn(XF[r], s_bias[r]) : XF[r];
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // W is copied over next
         ST_MARK(1);
@@ -540,12 +586,12 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
 
         // ── A ────────────────────────────────────────────────────────────────
         if (tid == 0) {
-            if (nor) {
-                mbar_arrive_expect_tx(bo, (uint32_t)(nor * a.opitch));
-                tma_load_1d(W, Ly->wo + (uint64_t)o0 * a.opitch, (uint32_t)(nor * a.opitch), bo);
-            }
+            mbar_arrive_expect_tx(bo, (uint32_t)(nor * a.opitch) + d * 4);
+            tma_load_1d(W, Ly->wo + (uint64_t)o0 * a.opitch, (uint32_t)(nor * a.opitch), bo);
+            tma_load_1d(s_fn, Ly->ffn_norm, d * 4, bo);
         }
-        st_attention<HD>(a, Ly->q_norm, Ly->k_norm, Ly->kc, Ly->vc, XF, red, s_last, head_cnt, pos, S, win, first);
+        st_attention<HD>(a, Ly->q_norm ? s_qn : nullptr, Ly->k_norm ? s_kn : nullptr, Ly->kc, Ly->vc, XF, red, s_last,
+                         head_cnt, pos, S, win, first);
         ST_MARK(3);
         gsync();
         ST_MARK(4);
@@ -556,7 +602,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
             ab_load_qact(Xa, a.att, a.nq);
             __syncthreads();
             ST_MARK(28);
-            const bool ok = nor && st_wait(bo, par, a.dev_err);
+            const bool ok = st_wait(bo, par, a.dev_err);  // the wo rows and ffn_norm
             ST_MARK(29);
             if (ok) st_rows<OT>(W, a.opitch, nor, a.nq, a.onb, Xa, XF);
         }
@@ -589,8 +635,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
             }
             __syncthreads();
             const float rms = s_stat[0];
-            const float *nw = Ly->ffn_norm;
-            for (uint32_t i = tid; i < d; i += kStThreads) XF[i] = XF[i] * rms * __ldg(nw + i);
+            for (uint32_t i = tid; i < d; i += kStThreads) XF[i] = XF[i] * rms * s_fn[i];
         }
         __syncthreads();
         ST_MARK(18);
@@ -708,15 +753,15 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
             mbar_arrive_expect_tx(bh, a.k * a.img);
             for (uint32_t s = 0; s < a.k; s++)
                 tma_load_1d(XSr + (size_t)s * a.img, a.himg + (size_t)s * a.img, a.img, bh);
-            if (more) {  // the next layer's Q/K/V rows and router row (from L2 by now)
-                mbar_arrive_expect_tx(bq, (uint32_t)(nqr * a.qpitch));
-                tma_load_1d(W, Ly[1].wqkv + (uint64_t)q0 * a.qpitch, (uint32_t)(nqr * a.qpitch), bq);
+            if (more) {  // the next layer's Q/K/V rows, norm weights and router row
+                st_issue_q(a, L, smem, Ly[1], q0, nqr, bq);
                 if (has_e) {
                     mbar_arrive_expect_tx(brt, d * 4);
                     tma_load_1d(RT, Ly[1].router + (size_t)c * d, d * 4, brt);
                 }
             }
         }
+        if (more && tid < nqr) s_bias[tid] = Ly[1].bias ? __ldg(Ly[1].bias + q0 + tid) : 0.0f;
         const bool hok = st_wait(bh, par, a.dev_err);
         ST_MARK(25);
         st_down<DT>(a, DN, XSr, XF, s_y, bdn, par, nor, hok);
