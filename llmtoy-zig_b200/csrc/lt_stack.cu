@@ -809,7 +809,10 @@ StScratch st_scratch(const StackParams &p, uint32_t splits) {
 
 }  // namespace
 
-bool stack_plan(const StackParams &p, int num_sms, size_t *smem_out, size_t *scratch_bytes, size_t *sync_offset) {
+// The kernel's arguments without the per-call pointers: the one place both the
+// plan (shared-memory size) and the launch take them from.  false: a shape the
+// kernel does not take.
+static bool st_args(const StackParams &p, int num_sms, StackArgs &a) {
     const AttnGeom &g = p.g;
     const uint32_t G = (uint32_t)num_sms;
     if (p.n_layers == 0 || p.n_layers > 63 || num_sms <= 0 || (uint32_t)num_sms > kStMaxCtas) return false;
@@ -828,7 +831,7 @@ bool stack_plan(const StackParams &p, int num_sms, size_t *smem_out, size_t *scr
     }
     const uint32_t nunits = p.k * p.F / kStUnit;
     if (nunits < G || (p.k * p.F) % kStUnit) return false;
-    StackArgs a{};
+    a = StackArgs{};
     a.g = g;
     a.d = p.d;
     a.nq = nq;
@@ -836,24 +839,37 @@ bool stack_plan(const StackParams &p, int num_sms, size_t *smem_out, size_t *scr
     a.qrows = qrows;
     a.qpitch = p.qpitch;
     a.opitch = p.opitch;
+    a.qnb = p.d / 32;
+    a.onb = nq / 32;
     a.E = p.E;
     a.k = p.k;
     a.F = p.F;
+    a.norm_topk = p.norm_topk;
+    a.act = p.act;
     a.dense = p.dense;
     a.gpitch = p.gpitch;
     a.dpitch = p.dpitch;
+    a.gnb = p.d / 32;
+    a.dnb = p.F / 32;
     a.di = st_items(p.F);
     a.img = (uint32_t)xs_bytes(1, (int)a.di);
+    a.eps = p.eps;
+    a.n_layers = p.n_layers;
+    a.nbar = 5 * p.n_layers;
+    a.splits = max(1u, min(kStMaxSplits, G / g.n_heads));
     a.maxq = (qrows + G - 1) / G;
     a.maxo = (p.d + G - 1) / G;
     a.maxpairs = kStUnit * ((nunits + G - 1) / G);
     if (a.maxpairs / kStChunk > kStMaxChunks) return false;
-    const StLayout L = st_layout(a);
-    if (L.total > kDecodeSmemLimit) return false;
-    const uint32_t splits = max(1u, min(kStMaxSplits, G / g.n_heads));
-    if (smem_out) *smem_out = L.total;
-    if (scratch_bytes) *scratch_bytes = st_scratch(p, splits).total;
-    if (sync_offset) *sync_offset = st_scratch(p, splits).sync;
+    return st_layout(a).total <= kDecodeSmemLimit;
+}
+
+bool stack_plan(const StackParams &p, int num_sms, size_t *smem_out, size_t *scratch_bytes, size_t *sync_offset) {
+    StackArgs a;
+    if (!st_args(p, num_sms, a)) return false;
+    if (smem_out) *smem_out = st_layout(a).total;
+    if (scratch_bytes) *scratch_bytes = st_scratch(p, a.splits).total;
+    if (sync_offset) *sync_offset = st_scratch(p, a.splits).sync;
     return true;
 }
 
@@ -872,42 +888,12 @@ extern "C" int lt_stack_trace_copy(void *dst, size_t bytes) {
 
 cudaError_t launch_stack(const LaunchCfg &c, const StackParams &p, const void *dev_layers, float *x,
                          const uint32_t *pos, uint8_t *scratch) {
-    size_t smem = 0;
-    if (!stack_plan(p, c.num_sms, &smem, nullptr, nullptr)) return cudaErrorInvalidValue;
-    const uint32_t G = (uint32_t)c.num_sms;
-    const AttnGeom &g = p.g;
-    StackArgs a{};
-    a.g = g;
-    a.d = p.d;
-    a.nq = g.n_heads * g.hd;
-    a.nkv = g.n_kv * g.hd;
-    a.qrows = a.nq + 2 * a.nkv;
-    a.qpitch = p.qpitch;
-    a.opitch = p.opitch;
-    a.qnb = p.d / 32;
-    a.onb = a.nq / 32;
-    a.E = p.E;
-    a.k = p.k;
-    a.F = p.F;
-    a.norm_topk = p.norm_topk;
-    a.act = p.act;
-    a.dense = p.dense;
-    a.gpitch = p.gpitch;
-    a.dpitch = p.dpitch;
-    a.gnb = p.d / 32;
-    a.dnb = p.F / 32;
-    a.di = st_items(p.F);
-    a.img = (uint32_t)xs_bytes(1, (int)a.di);
-    a.eps = p.eps;
-    a.n_layers = p.n_layers;
-    a.nbar = 5 * p.n_layers;
+    StackArgs a;
+    if (!st_args(p, c.num_sms, a)) return cudaErrorInvalidValue;
+    const size_t smem = st_layout(a).total;  // the kernel carves exactly this layout from these arguments
     a.layers = static_cast<const StackLayerDev *>(dev_layers);
     a.x = x;
     a.pos = pos;
-    a.splits = max(1u, min(kStMaxSplits, G / g.n_heads));
-    a.maxq = (a.qrows + G - 1) / G;
-    a.maxo = (p.d + G - 1) / G;
-    a.maxpairs = kStUnit * ((p.k * p.F / kStUnit + G - 1) / G);
     const StScratch sc = st_scratch(p, a.splits);
     a.qkv = reinterpret_cast<float *>(scratch + sc.qkv);
     a.part = reinterpret_cast<float *>(scratch + sc.part);
@@ -916,10 +902,10 @@ cudaError_t launch_stack(const LaunchCfg &c, const StackParams &p, const void *d
     a.sync = scratch + sc.sync;
     a.dev_err = c.dev_err;
     if (p.dense) {
-        if (g.hd == 64) return launch_stack_t<64, T_Q8_0, T_Q8_0>(c, a, smem);
+        if (p.g.hd == 64) return launch_stack_t<64, T_Q8_0, T_Q8_0>(c, a, smem);
         return launch_stack_t<128, T_Q8_0, T_Q8_0>(c, a, smem);
     }
-    if (g.hd == 64) return launch_stack_t<64, T_Q4_K, T_Q4_K>(c, a, smem);
+    if (p.g.hd == 64) return launch_stack_t<64, T_Q4_K, T_Q4_K>(c, a, smem);
     return launch_stack_t<128, T_Q4_K, T_Q4_K>(c, a, smem);
 }
 
