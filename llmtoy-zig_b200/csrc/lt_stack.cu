@@ -48,7 +48,9 @@ constexpr uint32_t kStChunk = 8;          // gate/up pairs per TMA chunk
 constexpr uint32_t kStUnit = 16;          // pairs per work unit (one quantisation group)
 constexpr uint32_t kStMaxChunks = 32;     // gate/up chunk mbarriers per CTA
 constexpr uint32_t kStMaxSlots = 16;      // top-k slots
-constexpr uint32_t kStSplitPositions = 32;  // positions per attention split before another CTA joins
+constexpr uint32_t kStSplitPositions = 256;  // positions per attention split before another CTA joins
+                                              // (a merge across CTAs costs two L2 round trips: measured
+                                              // slower than one CTA per head up to a few hundred positions)
 constexpr uint32_t kStMaxSplits = 8;
 constexpr int kStNormThreads = 128;       // k_moe_decode's RMSNorm reduction width
 
@@ -753,16 +755,18 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
             mbar_arrive_expect_tx(bh, a.k * a.img);
             for (uint32_t s = 0; s < a.k; s++)
                 tma_load_1d(XSr + (size_t)s * a.img, a.himg + (size_t)s * a.img, a.img, bh);
-            if (more) {  // the next layer's Q/K/V rows, norm weights and router row
-                st_issue_q(a, L, smem, Ly[1], q0, nqr, bq);
-                if (has_e) {
-                    mbar_arrive_expect_tx(brt, d * 4);
-                    tma_load_1d(RT, Ly[1].router + (size_t)c * d, d * 4, brt);
-                }
-            }
         }
         if (more && tid < nqr) s_bias[tid] = Ly[1].bias ? __ldg(Ly[1].bias + q0 + tid) : 0.0f;
         const bool hok = st_wait(bh, par, a.dev_err);
+        // the next layer's Q/K/V rows, norm weights and router row, once the
+        // slot images are in (queued behind them they would delay the images)
+        if (tid == 0 && more) {
+            st_issue_q(a, L, smem, Ly[1], q0, nqr, bq);
+            if (has_e) {
+                mbar_arrive_expect_tx(brt, d * 4);
+                tma_load_1d(RT, Ly[1].router + (size_t)c * d, d * 4, brt);
+            }
+        }
         ST_MARK(25);
         st_down<DT>(a, DN, XSr, XF, s_y, bdn, par, nor, hok);
         __syncthreads();
