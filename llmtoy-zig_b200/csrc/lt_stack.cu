@@ -553,6 +553,13 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
 
         // ── Q ────────────────────────────────────────────────────────────────
         ST_MARK(0);
+        if (tid == 0 && c < 2 && win > 1) {  // this layer's cached K (CTA 0) / V (CTA 1) rows into L2 for phase A
+            const size_t row = (size_t)a.nkv * (a.g.kv_f16 ? 2 : 4);
+            const uint8_t *base = static_cast<const uint8_t *>(c == 0 ? Ly->kc : Ly->vc);
+            const uint32_t s0 = first % a.g.cap, n = win - 1, n0 = min(n, a.g.cap - s0);
+            st_prefetch_rows(base, row, s0, n0);
+            if (n > n0) st_prefetch_rows(base, row, 0, n - n0);
+        }
         ab_load(XF, a.x, d);
         __syncthreads();
         ST_MARK(12);
