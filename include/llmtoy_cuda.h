@@ -290,6 +290,38 @@ lt_status lt_moe_ffn_noalloc(void *cuda_stream, const void *gate, const void *up
  * Allocates nothing; not for use during stream capture. */
 lt_status lt_noalloc_status(void *cuda_stream);
 
+/* ── expert-parallel MoE layer ───────────────────────────────────────────────
+ * No counterpart in the reference, whose MoE runs on one device (the seam it
+ * plugs into is GpuWeights.runExpertBatch, src/model/gemma4/gpu_weights.zig:
+ * 2748).  Rank r of nranks holds experts [r*E/nranks, (r+1)*E/nranks) of each
+ * layer; the exchange runs over NCCL, which is loaded at run time
+ * (libnccl.so.2; LT_ENODEV when absent).
+ *
+ * lt_ep_unique_id: on one rank, the 128-byte id the host hands to every rank
+ * (its own channel: a store, MPI, a file).  lt_ep_init: every rank, one ep per
+ * context; the context's stream at this point is the ep's stream for life.
+ * timeout_ms bounds every host-side wait of a call: when it runs out the
+ * communicator is aborted (its kernels return) and the call returns
+ * LT_ETIMEOUT, as does every later call on that ep; an error NCCL reports
+ * aborts it too (LT_ECUDA). */
+typedef struct lt_ep lt_ep;
+lt_status lt_ep_unique_id(uint8_t id_out[128]);
+lt_status lt_ep_init(lt_ctx *ctx, uint32_t nranks, uint32_t rank, const uint8_t id[128], uint32_t timeout_ms,
+                     lt_ep **out);
+lt_status lt_ep_free(lt_ep *ep);
+
+/* One MoE layer over this rank's ntok tokens, expert-parallel (every rank
+ * calls it for the same layer, in the same order): router [E][d] replicated;
+ * gate/up/down this rank's E/nranks experts (up NULL: fused gate_up);
+ * dev_out[ntok][d] = dev_x + moe(rmsnorm(dev_x) * dev_norm_w) when dev_norm_w
+ * is given, else moe(dev_x) -- the same result as lt_moe_block / lt_moe_forward
+ * over all E experts on one device.  Synchronises with the stream twice (the
+ * split sizes, then the end of the exchanges): not capturable. */
+lt_status lt_moe_ffn_ep(lt_ctx *ctx, lt_ep *ep, const lt_tensor *router, const lt_tensor *gate,
+                        const lt_tensor *up, const lt_tensor *down, int act, int norm_topk,
+                        const float *dev_expert_scale, const float *dev_norm_w, float eps,
+                        const float *dev_x, uint32_t ntok, uint32_t k, float *dev_out);
+
 /* ── expert parallelism building blocks ──────────────────────────────────────
  * No counterpart in the reference, whose MoE runs on one device: these let a
  * host shard the experts across ranks (experts [r*E/n, (r+1)*E/n) on rank r)

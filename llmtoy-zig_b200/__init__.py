@@ -42,7 +42,8 @@ EXPORTS = [
     "lt_ffn_block", "lt_greedy_step", "lt_scale", "lt_add_rmsnorm", "lt_norm_pair", "lt_ffn_tail", "lt_softcap",
     "lt_sample_step", "lt_rng_seed", "lt_quantize_q8_1", "lt_dequant_q8_1", "lt_moe_block_scaled",
     "lt_qmatvec_multi", "lt_noalloc_status", "lt_selftest_wait",
-    "lt_stack_create", "lt_stack_run", "lt_stack_free",
+    "lt_stack_create", "lt_stack_run", "lt_stack_free", "lt_ep_unique_id", "lt_ep_init", "lt_ep_free",
+    "lt_moe_ffn_ep",
 ]
 
 
@@ -139,6 +140,10 @@ def load_library() -> ctypes.CDLL:
         "lt_stack_create": (I, [P, P, U32, P, U32, U32, I, I, F, ctypes.POINTER(P)]),
         "lt_stack_run": (I, [P, P, P, P]),
         "lt_stack_free": (I, [P, P]),
+        "lt_ep_unique_id": (I, [P]),
+        "lt_ep_init": (I, [P, U32, U32, P, U32, ctypes.POINTER(P)]),
+        "lt_ep_free": (I, [P]),
+        "lt_moe_ffn_ep": (I, [P, P, P, P, P, P, I, I, P, P, F, P, U32, U32, P]),
         "lt_ep_dispatch": (I, [P, P, U32, U32, U32, U32, P, P, P, P]),
         "lt_gather_rows": (I, [P, P, U64, P, U32, P]),
         "lt_moe_combine": (I, [P, P, U64, P, P, U32, U32, P, P]),

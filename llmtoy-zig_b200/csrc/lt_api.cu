@@ -56,6 +56,9 @@ struct lt_graph {
     cudaGraphExec_t exec;
 };
 
+int lt::ctx_device(const lt_ctx *ctx) { return ctx->device; }
+cudaStream_t lt::ctx_stream(const lt_ctx *ctx) { return ctx->stream; }
+
 struct lt_stack {
     lt::StackParams p;
     void *dev_layers = nullptr;  // lt::StackLayerDev[n_layers]

@@ -5,7 +5,14 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+struct lt_ctx;
+
 namespace lt {
+
+// The context's device and its current stream (lt_api.cu), for entry points
+// implemented in other files.
+int ctx_device(const lt_ctx *ctx);
+cudaStream_t ctx_stream(const lt_ctx *ctx);
 
 // A weight matrix as the kernels see it: GGUF rows at a 16-byte pitch.
 struct DevMat {

@@ -10,6 +10,7 @@ checked against the CPU oracle over the same tokens.
 """
 from __future__ import annotations
 
+import ctypes
 import importlib
 import os
 import subprocess
@@ -186,3 +187,63 @@ def test_ep_nccl_all_gpus():
     r = subprocess.run(["timeout", "-k", "30", "600"] + cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "EP_OK" in r.stdout
+
+
+def test_ep_capi_single_rank(ctx, pkg, oracle, pool):
+    """lt_ep_init / lt_moe_ffn_ep with one rank (NCCL to itself) on the config-1
+    shape: the same result as the single-device block and the oracle, on the
+    grouped CUDA-core path (5 tokens) and the tensor-core path (80 tokens)."""
+    import torch
+    synth = importlib.import_module("llmtoy-zig_b200.synth")
+    lib = pkg.load_library()
+    rng = np.random.default_rng(4444)
+    E, d, F, k = 128, 2048, 768, 8
+    L = synth.MoeLayer(rng, d_model=d, n_experts=E, d_expert=F)
+    nw = rng.uniform(0.5, 1.5, d).astype(np.float32)
+    router, gate = ctx.upload(L.router, 0, E, d), ctx.upload(L.gate, L.gate_type, F, d, n_experts=E)
+    up, down = ctx.upload(L.up, L.gate_type, F, d, n_experts=E), ctx.upload(L.down, L.down_type, d, F, n_experts=E)
+    uid = (ctypes.c_uint8 * 128)()
+    assert lib.lt_ep_unique_id(uid) == 0
+    h = ctypes.c_void_p()
+    st = lib.lt_ep_init(ctx.ptr, 1, 0, uid, 20000, ctypes.byref(h))
+    assert st == 0, pkg.STATUS.get(st, st)
+    nwd = torch.from_numpy(nw).cuda()
+    try:
+        for T in (5, 80):
+            x = synth.hidden(rng, T, d)
+            xd = torch.from_numpy(x).cuda()
+            out = torch.empty_like(xd)
+            st = lib.lt_moe_ffn_ep(ctx.ptr, h, router.ptr, gate.ptr, up.ptr, down.ptr, pkg.ACT_SILU, 1, None,
+                                   nwd.data_ptr(), ctypes.c_float(1e-6), xd.data_ptr(), T, k, out.data_ptr())
+            assert st == 0, pkg.STATUS.get(st, st)
+            single = torch.empty_like(xd)
+            ctx.moe_block(router, gate, up, down, pkg.ACT_SILU, True, None, nwd, 1e-6, xd, T, k, single)
+            ctx.sync()
+            got, one = out.cpu().numpy() - x, single.cpu().numpy() - x
+            xn = np.empty_like(x)
+            for t in range(T):
+                oracle.lib().orc_rmsnorm(xn[t].ctypes.data, x[t].ctypes.data, nw.ctypes.data, d, 1e-6)
+            ref, _, _ = oracle.moe_layer(L, xn, k, True, pool=pool)
+            assert rel_l2(got, ref) < MOE_L2_TOL, (T, rel_l2(got, ref))
+            assert rel_l2(got, one) < MOE_L2_TOL, (T, rel_l2(got, one))
+    finally:
+        lib.lt_ep_free(h)
+        for t in (router, gate, up, down):
+            t.free()
+
+
+def test_ep_capi_all_gpus():
+    """lt_moe_ffn_ep over every visible GPU (2, 4 or 8 ranks) against the oracle;
+    then one rank leaves between steps and the other's next call returns an
+    error within the ep's timeout, its context still usable (NVLS off)."""
+    import torch
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs two GPUs")
+    n = max(w for w in (2, 4, 8) if w <= n)
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
+           "--master-addr=127.0.0.1", "--master-port=29533", str(REPO / "tests" / "ep_capi_worker.py"), "--leave"]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(["timeout", "-k", "30", "600"] + cmd, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "EP_CAPI_OK" in r.stdout
