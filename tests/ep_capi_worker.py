@@ -62,7 +62,7 @@ def main() -> int:
         x = torch.from_numpy(xs[rank]).cuda()
         nwd = torch.from_numpy(nw).cuda()
         out = torch.empty_like(x)
-        st = lib.lt_moe_ffn_ep(c.ptr, h, router.ptr, gate.ptr, up.ptr, down.ptr, pkg.ACT_SILU, 1, None,
+        st = lib.lt_moe_ffn_ep(c.ptr, h, router.handle, gate.handle, up.handle, down.handle, pkg.ACT_SILU, 1, None,
                                nwd.data_ptr(), ctypes.c_float(1e-6), x.data_ptr(), x.shape[0], k, out.data_ptr())
         assert st == 0, pkg.STATUS.get(st, st)
         got = out.cpu().numpy() - xs[rank]
@@ -81,13 +81,13 @@ def main() -> int:
             dist.barrier()  # every rank is between steps: nothing is in flight
             if rank == 0:  # the next step: rank 1 never joins it
                 t0 = time.monotonic()
-                st = lib.lt_moe_ffn_ep(c.ptr, h, router.ptr, gate.ptr, up.ptr, down.ptr, pkg.ACT_SILU, 1, None,
+                st = lib.lt_moe_ffn_ep(c.ptr, h, router.handle, gate.handle, up.handle, down.handle, pkg.ACT_SILU, 1, None,
                                        nwd.data_ptr(), ctypes.c_float(1e-6), x.data_ptr(), x.shape[0], k,
                                        out.data_ptr())
                 dt = time.monotonic() - t0
                 print(f"rank 0: step without rank 1 -> {pkg.STATUS.get(st, st)} after {dt:.1f} s", flush=True)
                 ok = int(st in (4, 5) and dt < 30.0)  # LT_ECUDA (NCCL saw the peer go) or LT_ETIMEOUT
-                st2 = lib.lt_moe_ffn_ep(c.ptr, h, router.ptr, gate.ptr, up.ptr, down.ptr, pkg.ACT_SILU, 1, None,
+                st2 = lib.lt_moe_ffn_ep(c.ptr, h, router.handle, gate.handle, up.handle, down.handle, pkg.ACT_SILU, 1, None,
                                         nwd.data_ptr(), ctypes.c_float(1e-6), x.data_ptr(), x.shape[0], k,
                                         out.data_ptr())
                 ok = ok and st2 == 5  # the aborted ep refuses further calls

@@ -213,7 +213,7 @@ def test_ep_capi_single_rank(ctx, pkg, oracle, pool):
             x = synth.hidden(rng, T, d)
             xd = torch.from_numpy(x).cuda()
             out = torch.empty_like(xd)
-            st = lib.lt_moe_ffn_ep(ctx.ptr, h, router.ptr, gate.ptr, up.ptr, down.ptr, pkg.ACT_SILU, 1, None,
+            st = lib.lt_moe_ffn_ep(ctx.ptr, h, router.handle, gate.handle, up.handle, down.handle, pkg.ACT_SILU, 1, None,
                                    nwd.data_ptr(), ctypes.c_float(1e-6), xd.data_ptr(), T, k, out.data_ptr())
             assert st == 0, pkg.STATUS.get(st, st)
             single = torch.empty_like(xd)
