@@ -499,30 +499,26 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
 
 // ── activation prep: f32 rows -> f16 hi/lo planes (K permuted in groups of 4
 // as the dequantised weights are), sub-block sums, 2^e per row ─────────────
-__global__ void __launch_bounds__(256) k_gemm_prep(const float *src, uint32_t K, __half *xh, __half *xl, float *xsum,
-                                                   float *xinv) {
-    __shared__ float s_red[8];
+// One warp per row (eight rows per block): no block barriers, and every
+// warp's loads in flight at once.  K % 256 == 0.
+__global__ void __launch_bounds__(256) k_gemm_prep(const float *src, uint32_t K, uint32_t rows, __half *xh,
+                                                   __half *xl, float *xsum, float *xinv) {
     pdl_wait();
-    const uint32_t row = blockIdx.x;
+    const uint32_t lane = threadIdx.x & 31, row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (row >= rows) return;
     const float *s = src + (size_t)row * K;
     float amax = 0.0f;
-#pragma unroll 8
-    for (uint32_t i = threadIdx.x; i < K; i += blockDim.x) amax = fmaxf(amax, fabsf(s[i]));
+#pragma unroll 4
+    for (uint32_t i = 4 * lane; i < K; i += 128) {
+        const float4 v = *reinterpret_cast<const float4 *>(s + i);
+        amax = fmaxf(fmaxf(amax, fabsf(v.x)), fmaxf(fabsf(v.y), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = amax;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float m = threadIdx.x < blockDim.x / 32 ? s_red[threadIdx.x] : 0.0f;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (threadIdx.x == 0) s_red[0] = m;
-    }
-    __syncthreads();
     int ex = 0;
-    frexpf(s_red[0], &ex);  // max|x| * 2^-ex in [0.5, 1)
+    frexpf(amax, &ex);  // max|x| * 2^-ex in [0.5, 1)
     const float scale = ldexpf(1.0f, -ex);
-    for (uint32_t m = threadIdx.x; m < K / 8; m += blockDim.x) {
+    for (uint32_t m = lane; m < K / 8; m += 32) {
         const float4 p = *reinterpret_cast<const float4 *>(s + 8 * m);
         const float4 q = *reinterpret_cast<const float4 *>(s + 8 * m + 4);
         const float v[8] = {p.x, p.z, p.y, p.w, q.x, q.z, q.y, q.w};  // positions <- elements (0,2,1,3,...)
@@ -532,16 +528,22 @@ __global__ void __launch_bounds__(256) k_gemm_prep(const float *src, uint32_t K,
         *reinterpret_cast<uint4 *>(xh + (size_t)row * K + 8 * m) = *reinterpret_cast<uint4 *>(h);
         *reinterpret_cast<uint4 *>(xl + (size_t)row * K + 8 * m) = *reinterpret_cast<uint4 *>(l);
     }
-    for (uint32_t j = threadIdx.x; j < K / 32; j += blockDim.x) {
+    for (uint32_t j = lane; j < K / 32; j += 32) {  // each 32-column sum in column order
         float v[32];
 #pragma unroll
-        for (int i = 0; i < 32; i++) v[i] = s[32 * j + i];
+        for (int i = 0; i < 32; i += 4) {
+            const float4 q = *reinterpret_cast<const float4 *>(s + 32 * j + i);
+            v[i] = q.x;
+            v[i + 1] = q.y;
+            v[i + 2] = q.z;
+            v[i + 3] = q.w;
+        }
         float t = 0.0f;
 #pragma unroll
         for (int i = 0; i < 32; i++) t += v[i] * scale;
         xsum[(size_t)row * (K / 32) + j] = t;
     }
-    if (threadIdx.x == 0) xinv[row] = ldexpf(1.0f, ex);
+    if (lane == 0) xinv[row] = ldexpf(1.0f, ex);
 }
 
 // ── tile list: (active expert slot, first position) per NP positions ───────
@@ -571,10 +573,37 @@ __global__ void __launch_bounds__(kRouterMaxE) k_gemm_tiles(MoePlan p, uint2 *ti
 }
 
 // ── weighted combine in slot order (+ residual) ─────────────────────────────
+// One token row per blockIdx.x; with vec, four consecutive columns per thread
+// (16-byte loads and stores; D % 4 == 0 and every pointer 16-byte aligned),
+// else one.  Each element is the same sum in slot order either way.
 __global__ void k_gemm_combine(const float *y, uint32_t D, const uint32_t *pair_pos, const float *w, uint32_t k,
-                               const float *resid, float *out) {
+                               const float *resid, float *out, int vec) {
     pdl_wait();
     const uint32_t t = blockIdx.x, c = blockIdx.y * blockDim.x + threadIdx.x;  // token rows in x: no 65535 cap
+    if (vec) {
+        if (4 * c >= D) return;
+        float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // moe_buf is zeroed, then += scale * down, slot by slot
+        for (uint32_t s = 0; s < k; s++) {
+            const uint32_t pp = __ldg(pair_pos + (size_t)t * k + s);
+            if (pp == 0xffffffffu) continue;  // a pair whose id the dispatch plan rejected contributes nothing
+            const float ws = __ldg(w + (size_t)t * k + s);
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(y + (size_t)pp * D) + c);
+            o.x = __fadd_rn(o.x, __fmul_rn(ws, v.x));
+            o.y = __fadd_rn(o.y, __fmul_rn(ws, v.y));
+            o.z = __fadd_rn(o.z, __fmul_rn(ws, v.z));
+            o.w = __fadd_rn(o.w, __fmul_rn(ws, v.w));
+        }
+        const size_t oi = (size_t)t * D / 4 + c;
+        if (resid) {
+            const float4 r = reinterpret_cast<const float4 *>(resid)[oi];
+            o.x = r.x + o.x;
+            o.y = r.y + o.y;
+            o.z = r.z + o.z;
+            o.w = r.w + o.w;
+        }
+        reinterpret_cast<float4 *>(out)[oi] = o;
+        return;
+    }
     if (c >= D) return;
     float o = 0.0f;  // moe_buf is zeroed, then += scale * down, slot by slot (no fused multiply-add)
     for (uint32_t s = 0; s < k; s++) {
@@ -584,6 +613,17 @@ __global__ void k_gemm_combine(const float *y, uint32_t D, const uint32_t *pair_
     }
     const size_t oi = (size_t)t * D + c;
     out[oi] = resid ? resid[oi] + o : o;
+}
+
+// The combine's launch: the vector form when the shape and pointers allow it.
+static cudaError_t launch_combine_k(const LaunchCfg &c, const char *label, const float *y, uint64_t D,
+                                    const uint32_t *pair_pos, const float *w, uint32_t ntok, uint32_t k,
+                                    const float *resid, float *out) {
+    auto a16 = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    const int vec = D % 4 == 0 && a16(y) && a16(out) && (!resid || a16(resid));
+    const uint64_t per = vec ? D / 4 : D;
+    return launch_k(c, label, k_gemm_combine, dim3(ntok, (uint32_t)((per + 255) / 256)), dim3(256), 0, y, (uint32_t)D,
+                    pair_pos, w, k, resid, out, vec);
 }
 
 namespace {
@@ -624,8 +664,7 @@ bool encode_rows(CUtensorMap *map, const void *base, uint64_t pitch, uint64_t to
 
 cudaError_t launch_combine(const LaunchCfg &c, const float *y, uint64_t D, const uint32_t *pair_pos, const float *w,
                            uint32_t ntok, uint32_t k, const float *resid, float *out) {
-    return launch_k(c, "moe_combine", k_gemm_combine, dim3(ntok, (uint32_t)((D + 255) / 256)), dim3(256), 0, y,
-                    (uint32_t)D, pair_pos, w, k, resid, out);
+    return launch_combine_k(c, "moe_combine", y, D, pair_pos, w, ntok, k, resid, out);
 }
 
 bool moe_gemm_supported(const DevMat &gate, const DevMat &down, uint64_t F) {
@@ -675,7 +714,8 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
                          : launch_k(c, "moe_gemm_tiles", k_gemm_tiles<32>, dim3(1), dim3(kRouterMaxE), 0, p, tiles,
                                     n_tiles);
     if (e == cudaSuccess)
-        e = launch_k(c, "moe_gemm_prep", k_gemm_prep, dim3(T), dim3(256), 0, x, (uint32_t)d, xh, xl, xsum, xinv);
+        e = launch_k(c, "moe_gemm_prep", k_gemm_prep, dim3((T + 7) / 8), dim3(256), 0, x, (uint32_t)d, (uint32_t)T, xh,
+                     xl, xsum, xinv);
     GemmArgs g;
     const uint32_t E1 = E ? E : 1;
     if (!encode_rows(&g.map_w, gate.data, gate.pitch, (uint64_t)gate.rows * E1) ||
@@ -707,8 +747,8 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
                  : launch_k(c, "moe_gemm_gate_up", k_moe_gemm<0, 32>, dim3((uint32_t)c.num_sms), dim3(kGThreadsV2),
                             (size_t)GemmGeo<32>::kSmem, g);
     if (e == cudaSuccess)
-        e = launch_k(c, "moe_gemm_prep", k_gemm_prep, dim3((uint32_t)P), dim3(256), 0, (const float *)hbuf,
-                     (uint32_t)F, hh, hl, hsum, hinv);
+        e = launch_k(c, "moe_gemm_prep", k_gemm_prep, dim3((uint32_t)((P + 7) / 8)), dim3(256), 0, (const float *)hbuf,
+                     (uint32_t)F, (uint32_t)P, hh, hl, hsum, hinv);
     GemmArgs gd = g;
     if (!encode_rows(&gd.map_w, down.data, down.pitch, (uint64_t)down.rows * E1)) return cudaErrorInvalidValue;
     gd.map_up = gd.map_w;
@@ -730,8 +770,8 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
                  : launch_k(c, "moe_gemm_down", k_moe_gemm<1, 32>, dim3((uint32_t)c.num_sms), dim3(kGThreadsV2),
                             (size_t)GemmGeo<32>::kSmem, gd);
     if (e == cudaSuccess)
-        e = launch_k(c, "moe_gemm_combine", k_gemm_combine, dim3(T, (uint32_t)((d + 255) / 256)), dim3(256), 0,
-                     (const float *)ybuf, (uint32_t)d, (const uint32_t *)p.pair_pos, w, k, resid, out);
+        e = launch_combine_k(c, "moe_gemm_combine", (const float *)ybuf, d, (const uint32_t *)p.pair_pos, w, T, k,
+                             resid, out);
     return e;
 }
 
