@@ -265,16 +265,7 @@ __global__ void __launch_bounds__(kRtWarps * 32, 2) k_router_tok(RouterArgs a) {
         if (e < E) {
             float w0[kRouterChunk];
             router_prefetch(a.W + (size_t)e * a.w_ld, cols, lane, true, w0);
-            uint32_t tt = 0;
-            if (cols <= 32u * kRouterChunk)  // four tokens' chains at once, each in its own order
-                for (; tt + 4 <= nt; tt += 4) {
-                    float v[4];
-                    router_logit_n<4>(a.W + (size_t)e * a.w_ld, xs + tt * cols, cols, cols, lane, w0, v);
-                    if (lane == 0)
-#pragma unroll
-                        for (int q = 0; q < 4; q++) lg[(tt + q) * E + e] = v[q];
-                }
-            for (; tt < nt; tt++) {
+            for (uint32_t tt = 0; tt < nt; tt++) {
                 const float v = router_logit(a.W + (size_t)e * a.w_ld, xs + tt * cols, cols, lane, w0);
                 if (lane == 0) lg[tt * E + e] = v;
             }

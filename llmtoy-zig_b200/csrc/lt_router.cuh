@@ -56,37 +56,6 @@ LT_DEVINL float router_logit(const float *wrow, const float *xs, uint32_t cols, 
     return sum;
 }
 
-// router_logit for NT tokens at once (rows xs + t * ld), cols <= 2048: the
-// same per-token order, NT independent chains per lane for the scheduler.
-template <int NT>
-LT_DEVINL void router_logit_n(const float *wrow, const float *xs, uint32_t ld, uint32_t cols, int lane,
-                              const float (&w0)[kRouterChunk], float (&out)[NT]) {
-    const uint32_t n32 = cols & ~31u;
-    float acc[NT];
-#pragma unroll
-    for (int t = 0; t < NT; t++) acc[t] = 0.0f;
-#pragma unroll
-    for (int j = 0; j < kRouterChunk; j++)
-        if (32u * j < n32)
-#pragma unroll
-            for (int t = 0; t < NT; t++) acc[t] = __fadd_rn(acc[t], __fmul_rn(w0[j], xs[t * ld + 32 * j + lane]));
-#pragma unroll
-    for (int t = 0; t < NT; t++) {
-        const float a1 = __shfl_sync(0xffffffffu, acc[t], (lane + 8) & 31);
-        const float a2 = __shfl_sync(0xffffffffu, acc[t], (lane + 16) & 31);
-        const float a3 = __shfl_sync(0xffffffffu, acc[t], (lane + 24) & 31);
-        float v = __fadd_rn(__fadd_rn(acc[t], a1), __fadd_rn(a2, a3));
-        uint32_t i = n32;
-        for (; i + 8 <= cols; i += 8)
-            if (lane < 8) v = __fadd_rn(v, __fmul_rn(__ldg(wrow + i + lane), xs[t * ld + i + lane]));
-        float sum = -0.0f;
-#pragma unroll
-        for (int l = 0; l < 8; l++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, v, l));
-        for (; i < cols; i++) sum = __fadd_rn(sum, __fmul_rn(__ldg(wrow + i), xs[t * ld + i]));
-        out[t] = sum;
-    }
-}
-
 // Load this lane's first-chunk router weights for expert row wrow.
 LT_DEVINL void router_prefetch(const float *wrow, uint32_t cols, int lane, bool valid, float (&w0)[kRouterChunk]) {
     const uint32_t n32 = cols & ~31u;
