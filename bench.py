@@ -311,7 +311,7 @@ def main() -> None:
                     help="config 4: prompt tokens over all ranks, experts sharded 128/N (0: skip)")
     ap.add_argument("--ep-layers", type=int, default=2)
     ap.add_argument("--model-tokens", type=int, default=128, help="greedy tokens after the prompt (configs 2 and 0)")
-    ap.add_argument("--models", default="config0,config3", help="extra whole-model decode lines")
+    ap.add_argument("--models", default="config0,config3", help="extra whole-model decode lines ('none': skip)")
     ap.add_argument("--moe-stack", type=int, default=1, help="the config-1 MoE layer stack line (0: skip)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -353,7 +353,7 @@ def main() -> None:
                    for T in t_list}
 
     model_decode = {}
-    for name in [m for m in args.models.split(",") if m]:
+    for name in [m for m in args.models.split(",") if m and m != "none"]:
         if name == "config3":
             model_decode[name] = measure_gemma_decode(args, pkg, ctx, torch, stream, rank, world, dist)
         else:
