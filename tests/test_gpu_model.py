@@ -500,3 +500,47 @@ def test_stack_kernel_matches_per_layer_path(pkg, oracle, pool, kind, kv_f16):
         assert eager == ref_toks and replay == ref_toks, flag
     for i, rl in enumerate(ref_logits):
         assert rel_l2(logits[0][i], rl) < 2e-3, (i, rel_l2(logits[0][i], rl), rel_l2(logits[1][i], rl))
+
+
+@pytest.mark.parametrize("with_w1", [True, False])
+def test_fused_tail_equals_explicit_tail(pkg, with_w1):
+    """A Gemma 4 attention block with the previous layer's FFN tail fused in
+    gives the same bits as lt_ffn_tail followed by the block without a tail
+    (the fused tail follows k_ffn_tail's sum orders); with and without the
+    first post-FFN norm weight (w1 None: f enters the sum as it is)."""
+    import torch
+    synth, _ = _mods()
+    rng = np.random.default_rng(61 + int(with_w1))
+    d, nh, nkv, hd, window = 1024, 8, 4, 256, 16
+    nq, nk = nh * hd, nkv * hd
+    wq, wk, wv, wo = (synth.matrix(rng, 8, nq, d), synth.matrix(rng, 8, nk, d), synth.matrix(rng, 8, nk, d),
+                      synth.matrix(rng, 8, d, nq))
+    vec = lambda n, lo=0.5, hi=1.5: dev(rng.uniform(lo, hi, n).astype(np.float32))  # noqa: E731
+    nw, pn, qn, kn = vec(d), vec(d), vec(hd), vec(hd)
+    w1, w2, w = (vec(d) if with_w1 else None), vec(d), vec(d)
+    cfg = pkg.AttnCfg(nh, nkv, hd, 1, 1e4, 1e-6, 1.0, window, window, 1, 0)
+    c = pkg.Context(0)
+    c.set_stream(None)
+    try:
+        tq, tk, tv, to = c.upload(wq, 8, nq, d), c.upload(wk, 8, nk, d), c.upload(wv, 8, nk, d), c.upload(wo, 8, d, nq)
+        caches = [(empty(window * nk), empty(window * nk)) for _ in range(2)]
+        for pos in range(20):  # past the window's wrap
+            x = rng.normal(0, 1, d).astype(np.float32)
+            f = dev(rng.normal(0, 1, d).astype(np.float32))
+            m = rng.normal(0, 1, d).astype(np.float32)
+            p = dev(np.array([pos], np.int32))
+            # fused
+            x1, m1, out1 = dev(x), dev(m), empty(d)
+            c.attn_block_split(cfg, x1, nw, 1e-6, tq, tk, tv, None, qn, kn, p, caches[0][0], caches[0][1], to, pn,
+                               out1, tail=(f, w1, m1, w2, w, 0.75, 1e-6))
+            # explicit
+            x2, m2, out2 = dev(x), dev(m), empty(d)
+            c.ffn_tail(f, m2, w2, w, 0.75, 1e-6, d, 1, x2, w1=w1)
+            c.attn_block_split(cfg, x2, nw, 1e-6, tq, tk, tv, None, qn, kn, p, caches[1][0], caches[1][1], to, pn,
+                               out2)
+            c.sync()
+            np.testing.assert_array_equal(bits(host(out1)), bits(host(out2)))
+        for t in (tq, tk, tv, to):
+            t.free()
+    finally:
+        c.close()
