@@ -1,7 +1,9 @@
 // lt_moe_gemm.cu — grouped expert GEMM on the 5th-generation tensor cores
-// (tcgen05) for multi-token MoE batches with Q4_K experts (prefill; the
-// reference's expert loop src/model/gemma4/forward.zig:463-479 and
-// src/ops/moe.zig:61-76 run over many tokens).
+// (tcgen05) for multi-token MoE batches with Q4_K, Q6_K or Q8_0 experts
+// (prefill; the reference's expert loop src/model/gemma4/forward.zig:463-479
+// and src/ops/moe.zig:61-76 run over many tokens).  Q4_K up to 2048 columns
+// takes the single-plane scheme described next; Q6_K, Q8_0 and wider Q4_K
+// take the stacked-plane scheme (see StkFmt below).
 //
 // Pipeline: dispatch plan (lt_moe.cu) -> tile list -> activation prep (f32
 // rows -> f16 hi/lo planes) -> gate/up GEMM with SwiGLU/GeGLU epilogue ->
@@ -30,6 +32,7 @@
 #include <cuda.h>  // CUtensorMap (encoded through the runtime's driver entry point)
 #include <cuda_fp16.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "lt_launch.cuh"
@@ -43,7 +46,8 @@ constexpr int kGMaxSb = 8;  // superblocks per row (K <= 2048)
 
 // Roles (warps): 0-7 dequantise weight rows into the A stages and run the
 // epilogue (two threads per tile row: one per 64-column pair of the stage;
-// row = TMEM lane); 8 streams raw Q4_K superblocks (tiled TMA); 9 gathers
+// row = TMEM lane); 8 streams raw Q4_K superblocks (tiled TMA; stacked
+// planes: every lane copies row windows by cp.async); 9 gathers
 // the activation stages (cp.async, one position per lane) and the min-term
 // operand; 10 issues the MMAs (one lane).  The CTA is persistent: it walks the
 // (tile, 128-row block) work items of the launch with stride gridDim.x, and
@@ -91,11 +95,12 @@ struct GemmArgs {
     alignas(64) CUtensorMap map_up;
     const uint8_t *w;     // gate (mode 0) or down (mode 1) weights
     const uint8_t *w_up;  // mode 0: up weights; nullptr when w holds [gate; up] per expert
+    const uint8_t *w_end, *up_end;  // one past the last byte of w / w_up
     uint64_t pitch;
-    uint32_t K;       // columns (multiple of 256, <= 2048)
+    uint32_t K;       // columns (Q4_K single plane: multiple of 256, <= 2048; stacked planes: <= 4096)
     uint32_t rows_e;  // rows per expert in w
     uint32_t F;       // mode 0: expert width
-    uint32_t mt;      // 128-row blocks per tile
+    uint32_t mt;      // row blocks per tile (128 rows; 64 with stacked planes)
     int act;
     MoePlan p;
     const uint2 *tiles;  // (active expert slot, first position within it)
@@ -179,9 +184,205 @@ LT_DEVINL GemmItem gemm_item(const GemmArgs &a, uint32_t w) {
     return it;
 }
 
-template <int MODE, int NP>
+// ── stacked-plane weights (Q6_K, Q8_0, and Q4_K wider than 2048 columns) ──
+// The scheme above needs sc*q to be a small integer and one scale per
+// superblock; Q6_K's sc*(q-32) reaches 4096 (not exact in f16) and Q8_0 has
+// a scale per 32 columns.  For these an item covers 64 weight rows and the
+// tile's 128 MMA rows hold each of them twice: rows 0-63 the high f16 plane
+// of the row's values, rows 64-127 the low plane.  A value is the
+// reference's own f32 dequantisation (dequantRow: the same products and
+// roundings), times 2^-E for a power of two chosen per row and superblock
+// from the block header (|v| 2^-E < 2^15), split hi = f16(v'), lo =
+// f16(v' - hi) (22 significant bits; the scaling keeps both normal).  Each
+// superblock still accumulates in its own TMEM buffer and the fold applies
+// 2^E; the two planes' lanes add up in the epilogue.  No minimum term.
+//
+// Raw rows need not be 16-byte aligned (a Q6_K superblock is 210 bytes, a
+// Q8_0 row 34 bytes per 32 columns), so the producer warp copies each row's
+// superblock window with 16-byte cp.async from the aligned address below it
+// into a slot of kSlot bytes, and the dequantising threads read from the
+// window's offset inside the slot.
+template <int WS>
+struct StkFmt;
+template <>
+struct StkFmt<T_Q4_K> {
+    static constexpr uint32_t kSbBytes = 144, kSlot = 160;
+};
+template <>
+struct StkFmt<T_Q6_K> {
+    static constexpr uint32_t kSbBytes = 210, kSlot = 224;
+};
+template <>
+struct StkFmt<T_Q8_0> {
+    static constexpr uint32_t kSbBytes = 272, kSlot = 288;  // eight 34-byte blocks
+};
+constexpr int kStkRows = 64;
+constexpr int kStkMaxSb = 16;  // K <= 4096
+
+// Bytes of superblock sb of a row (a Q8_0 row may end inside its last 256 columns).
+template <int WS>
+LT_DEVINL uint32_t stk_len(uint32_t K, uint32_t sb) {
+    if constexpr (WS == T_Q8_0) return 34u * min(8u, K / 32 - 8 * sb);
+    return StkFmt<WS>::kSbBytes;
+}
+
+// First byte of weight row wr (0-63) of an item, and the end of its tensor.
+template <int MODE>
+LT_DEVINL const uint8_t *stk_row(const GemmArgs &a, const GemmItem &it, uint32_t wr, const uint8_t *&end) {
+    if (MODE == 1) {
+        end = a.w_end;
+        return a.w + (size_t)(it.e * a.rows_e + kStkRows * it.m0 + wr) * a.pitch;
+    }
+    if (wr < 32) {  // gate rows, then the same 32 up rows
+        end = a.w_end;
+        return a.w + (size_t)(it.e * a.rows_e + 32 * it.m0 + wr) * a.pitch;
+    }
+    const uint32_t u = 32 * it.m0 + wr - 32;
+    if (a.w_up) {
+        end = a.up_end;
+        return a.w_up + (size_t)(it.e * a.F + u) * a.pitch;
+    }
+    end = a.w_end;
+    return a.w + (size_t)(it.e * a.rows_e + a.F + u) * a.pitch;
+}
+
+LT_DEVINL uint32_t lds16(const uint8_t *p) { return *reinterpret_cast<const unsigned short *>(p); }
+
+// N little-endian words from a 2-byte aligned shared address (aligned loads,
+// one PRMT each).
+template <int N>
+LT_DEVINL void lds_words_a2(const uint8_t *p, uint32_t (&w)[N]) {
+    const uint32_t mis = smem_u32(p) & 3u;  // 0 or 2
+    const uint8_t *pa = p - mis;
+    const uint32_t sel = mis ? 0x5432u : 0x3210u;
+    uint32_t prev = lds32(pa);
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+        const uint32_t nx = lds32(pa + 4 * (i + 1));
+        w[i] = __byte_perm(prev, nx, sel);
+        prev = nx;
+    }
+}
+
+// 2^E for superblock sb of a row: |every value| * 2^-E < 2^15.
+template <int WS>
+LT_DEVINL float stk_exp2(const uint8_t *sbp, uint32_t K, uint32_t sb) {
+    float bound;
+    if constexpr (WS == T_Q4_K) {
+        const uint32_t h = lds16(sbp) | (lds16(sbp + 2) << 16);
+        bound = fabsf(f16_bits_to_f32(h & 0xffffu)) * 945.0f + fabsf(f16_bits_to_f32(h >> 16)) * 63.0f;
+    } else if constexpr (WS == T_Q6_K) {
+        bound = fabsf(f16_bits_to_f32(lds16(sbp + 208))) * 4096.0f;
+    } else {
+        const uint32_t nb = min(8u, K / 32 - 8 * sb);
+        float m = 0.0f;
+        for (uint32_t b = 0; b < nb; b++) m = fmaxf(m, fabsf(f16_bits_to_f32(lds16(sbp + 34 * b))));
+        bound = m * 128.0f;
+    }
+    if (!(bound > 0.0f)) return 1.0f;
+    const int e = (int)((__float_as_uint(bound) >> 23) & 0xffu) - 127 - 14;  // bound < 2^(e + 15)
+    return __uint_as_float((uint32_t)(127 + e) << 23);
+}
+
+// Element order inside each 8-column chunk of an A row, (0,2,1,3,4,6,5,7):
+// the activation rows are permuted the same way by k_gemm_prep.
+constexpr int chunk_perm(int i) { return (i & 4) | ((i & 1) << 1) | ((i >> 1) & 1); }
+
+// One plane (pl: 0 hi, 1 lo) of 64 columns (64-column chunk c of superblock
+// sbp, 2-byte aligned in shared memory) scaled by sv = 2^-E, written as eight
+// 16-byte 128B-swizzled chunks of the A row at arow.
+template <int WS>
+LT_DEVINL void stk_dequant(const uint8_t *sbp, uint32_t c, float sv, uint32_t pl, uint8_t *arow, uint32_t swz) {
+    float v[64];
+    if constexpr (WS == T_Q4_K) {
+        // dequant.zig:157-187: d1 * q - m1 with d1 = d*sc, m1 = dmin*m (sub-blocks 2c, 2c+1)
+        const uint32_t h = lds16(sbp) | (lds16(sbp + 2) << 16);
+        const float d = f16_bits_to_f32(h & 0xffffu), dmin = f16_bits_to_f32(h >> 16);
+        uint32_t s[3], q[8];
+        lds_words_a2<3>(sbp + 4, s);
+        lds_words_a2<8>(sbp + 16 + 32 * c, q);
+        float d1[2], m1[2];
+#pragma unroll
+        for (int t = 0; t < 2; t++) {
+            const uint32_t j = 2 * c + t;  // get_scale_min_k4 (dequant.zig:291-300)
+            uint32_t sc, mn;
+            if (j < 4) {
+                sc = (s[0] >> (8 * j)) & 63u;
+                mn = (s[1] >> (8 * j)) & 63u;
+            } else {
+                const uint32_t b = 8 * (j - 4);
+                sc = ((s[2] >> b) & 15u) | (((s[0] >> b) >> 6 & 3u) << 4);
+                mn = ((s[2] >> b) >> 4 & 15u) | (((s[1] >> b) >> 6 & 3u) << 4);
+            }
+            d1[t] = __fmul_rn(__fmul_rn(d, (float)sc), sv);
+            m1[t] = __fmul_rn(__fmul_rn(dmin, (float)mn), sv);
+        }
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            const uint32_t byte = (q[i >> 2] >> (8 * (i & 3))) & 0xffu;
+            v[i] = __fsub_rn(__fmul_rn(d1[0], (float)(byte & 15u)), m1[0]);
+            v[32 + i] = __fsub_rn(__fmul_rn(d1[1], (float)(byte >> 4)), m1[1]);
+        }
+    } else if constexpr (WS == T_Q6_K) {
+        // dequant.zig:237-287: (d*sc) * (q - 32); this thread's columns are
+        // half n = c >> 1 of the superblock, kinds 2(c&1) and 2(c&1)+1
+        const uint32_t n = c >> 1, hk = c & 1;
+        const float d = f16_bits_to_f32(lds16(sbp + 208));
+        uint32_t ql[16], qh[8], scw[1];
+        lds_words_a2<16>(sbp + 64 * n, ql);
+        lds_words_a2<8>(sbp + 128 + 32 * n, qh);
+        lds_words_a2<1>(sbp + 192 + 8 * n + 4 * hk, scw);
+#pragma unroll
+        for (int kk = 0; kk < 2; kk++) {  // kind 2hk + kk
+#pragma unroll
+            for (int l = 0; l < 32; l++) {
+                const uint32_t qlb = (ql[8 * kk + (l >> 2)] >> (8 * (l & 3))) & 0xffu;
+                const uint32_t qhb = (qh[l >> 2] >> (8 * (l & 3))) & 0xffu;
+                const uint32_t lo4 = hk ? qlb >> 4 : qlb & 15u;
+                const uint32_t hi2 = (qhb >> (4 * hk + 2 * kk)) & 3u;
+                const int sc = (int)(int8_t)((scw[0] >> (8 * (2 * kk + (l >> 4)))) & 0xffu);
+                const float s = __fmul_rn(__fmul_rn(d, (float)sc), sv);
+                v[32 * kk + l] = __fmul_rn(s, (float)((int)(lo4 | (hi2 << 4)) - 32));
+            }
+        }
+    } else {
+        // dequant.zig:42-52: d * q, blocks 2c and 2c+1 of the superblock
+#pragma unroll
+        for (int bb = 0; bb < 2; bb++) {
+            const uint8_t *blk = sbp + 34 * (2 * c + bb);
+            const float ds = __fmul_rn(f16_bits_to_f32(lds16(blk)), sv);
+            uint32_t q[8];
+            lds_words_a2<8>(blk + 2, q);
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+                v[32 * bb + i] = __fmul_rn(ds, (float)(int)(int8_t)((q[i >> 2] >> (8 * (i & 3))) & 0xffu));
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < 8; m++) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+            float p2[2];
+#pragma unroll
+            for (int t = 0; t < 2; t++) {
+                const float x = v[8 * m + chunk_perm(i + t)];
+                const float hi = __half2float(__float2half_rn(x));
+                p2[t] = pl ? x - hi : x;
+            }
+            const __half2 h2 = __floats2half2_rn(p2[0], p2[1]);
+            pk[i >> 1] = *reinterpret_cast<const uint32_t *>(&h2);
+        }
+        *reinterpret_cast<uint4 *>(arow + ((m ^ swz) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+}
+
+// WS: 0 for Q4_K in one exact plane with the minimum term; T_Q4_K, T_Q6_K or
+// T_Q8_0 for stacked planes.
+template <int MODE, int NP, int WS>
 __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_constant__ GemmArgs a) {
     using Geo = GemmGeo<NP>;
+    constexpr bool kStk = WS != 0;
     constexpr int NNP = Geo::NNP, kGBStages = Geo::kBStages, kGRawSlots = Geo::kRawSlots;
     constexpr uint32_t kOffA = Geo::kOffA, kOffB = Geo::kOffB, kOffAm = Geo::kOffAm, kOffBm = Geo::kOffBm;
     constexpr uint32_t kOffRaw = Geo::kOffRaw, kOffHdr = Geo::kOffHdr, kOffMisc = Geo::kOffMisc;
@@ -199,10 +400,10 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
     float *s_inv = reinterpret_cast<float *>(s_taddr + 4);  // [2][NP] by item parity
     float *hdr_d = reinterpret_cast<float *>(sm + kOffHdr);
 
-    const uint32_t nsb = a.K / 256;
+    const uint32_t nsb = (a.K + 255) / 256;  // stacked Q8_0: the last superblock may be partial
     if (tid == 0) {
         for (int i = 0; i < 3; i++) {
-            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_full[i], kStk ? 32 : 1);  // stacked: one cp.async arrival per producer lane
             mbar_init(&raw_empty[i], kGMath);
             mbar_init(&b_full[i], 32);
             mbar_init(&b_empty[i], 1);
@@ -232,7 +433,34 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
     const uint32_t taddr = *s_taddr;
     const uint32_t n_work = *a.n_tiles * a.mt;
 
-    if (warp == kGWarpRaw) {
+    if (warp == kGWarpRaw && kStk) {
+        // ── stacked planes: each row's superblock window by 16-byte cp.async,
+        //    from the aligned address below it (clamped to the tensor's end) ──
+        if constexpr (kStk) {
+            constexpr uint32_t kSlot = StkFmt<WS>::kSlot, kCh = kSlot / 16;
+            uint32_t gsb = 0;
+            for (uint32_t w = blockIdx.x; w < n_work; w += gridDim.x) {
+                const GemmItem it = gemm_item<NP>(a, w);
+                for (uint32_t sb = 0; sb < nsb; sb++, gsb++) {
+                    const uint32_t slot = gsb % kGRawSlots;
+                    if (gsb >= (uint32_t)kGRawSlots) gemm_wait(&raw_empty[slot], gsb / kGRawSlots - 1, a.dev_err);
+                    uint8_t *dst = sm + kOffRaw + slot * kRawStage;
+                    const uint32_t len = stk_len<WS>(a.K, sb);
+                    for (uint32_t idx = lane; idx < kStkRows * kCh; idx += 32) {
+                        const uint32_t row = idx / kCh, ch = idx % kCh;
+                        const uint8_t *end;
+                        const uint8_t *src = stk_row<MODE>(a, it, row, end) + (size_t)StkFmt<WS>::kSbBytes * sb;
+                        const uint32_t off = (uint32_t)(reinterpret_cast<uintptr_t>(src) & 15u);
+                        if (16 * ch >= off + len) continue;
+                        const uint8_t *cp = src - off + 16 * ch;
+                        const uint32_t nb = (uint32_t)min((uintptr_t)16, (uintptr_t)(end - cp));
+                        cp_async16(dst + row * kSlot + 16 * ch, cp, nb);
+                    }
+                    cp_async_arrive(&raw_full[slot]);
+                }
+            }
+        }
+    } else if (warp == kGWarpRaw) {
         // ── raw Q4_K superblocks: two 64-row x 144-byte tiled loads ──
         if (lane == 0) {
             uint32_t gsb = 0;
@@ -289,12 +517,14 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
 #pragma unroll
                     for (uint32_t cc = 0; cc < 16; cc++) {
                         const uint32_t o = (cc >> 3) * Geo::kBAtom + (((cc & 7) ^ (n & 7)) << 4);
-                        cp_async16(bs + o, srch + ks * 128 + cc * 8, valid[pp] ? 16u : 0u);
-                        cp_async16(bs + NP * 128 + o, srcl + ks * 128 + cc * 8, valid[pp] ? 16u : 0u);
+                        const uint32_t col = ks * 128 + cc * 8;  // zeros past K (stacked Q8_0 rows)
+                        const bool in = valid[pp] && col < a.K;
+                        cp_async16(bs + o, srch + (in ? col : 0), in ? 16u : 0u);
+                        cp_async16(bs + NP * 128 + o, srcl + (in ? col : 0), in ? 16u : 0u);
                     }
                 }
                 cp_async_arrive(&b_full[s]);
-                if (ks == ks_bm) {
+                if (!kStk && ks == ks_bm) {
                     // the previous item's min term has consumed the old B rows
                     if (gi >= 1) gemm_wait(min_full, gi - 1, a.dev_err);
 #pragma unroll
@@ -349,6 +579,7 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
                     }
                     umma_commit(&acc_full[ab]);
                 }
+                if constexpr (kStk) continue;
                 // min term: A planes (hi, lo) x B rows (hi plane | lo plane) over K = 8*nsb
                 gemm_wait(bm_full, gi, a.dev_err);
                 if (gi >= 1) gemm_wait(min_empty, gi - 1, a.dev_err);
@@ -381,18 +612,100 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
             }
             tmem_wait_ld();
         };
-        auto fold = [&](uint32_t n, uint32_t sb) {  // superblock accumulator n (global count) of superblock sb
+        // superblock accumulator n (global count) of superblock sb; stacked
+        // planes pass their own factor fs = 2^E
+        auto fold = [&](uint32_t n, uint32_t sb, float fs) {
             gemm_wait(&acc_full[n & 1], n / 2, a.dev_err);
             tc_fence_after();
             uint32_t vh[PH], vl[PH];
             tload((n & 1) * NNP + PH * hh, vh, vl);
             tc_fence_before();
             mbar_arrive(&acc_empty[n & 1]);
-            const float dsb = hdr_d[sb * kGM + r];
+            const float dsb = kStk ? fs : hdr_d[sb * kGM + r];
 #pragma unroll
             for (int q = 0; q < PH; q++)
                 y[q] = fmaf(dsb, __uint_as_float(vh[q]) + __uint_as_float(vl[q]), y[q]);
         };
+        if constexpr (kStk) {
+            // A row r = plane r >> 6 of weight row r & 63 (TMEM lane r)
+            constexpr uint32_t kSlot = StkFmt<WS>::kSlot;
+            const uint32_t wr = r & 63, pl = r >> 6;
+            for (uint32_t w = blockIdx.x; w < n_work; w += gridDim.x) {
+                const GemmItem it = gemm_item<NP>(a, w);
+                const uint8_t *end;
+                const uint8_t *srow = stk_row<MODE>(a, it, wr, end);
+#pragma unroll
+                for (int q = 0; q < PH; q++) y[q] = 0.0f;
+                float fs_prev = 1.0f;
+                for (uint32_t sb = 0; sb < nsb; sb++, gsb++) {
+                    const uint32_t slot = gsb % kGRawSlots;
+                    gemm_wait(&raw_full[slot], gsb / kGRawSlots, a.dev_err);
+                    const uint32_t off =
+                        (uint32_t)((reinterpret_cast<uintptr_t>(srow) + (size_t)StkFmt<WS>::kSbBytes * sb) & 15u);
+                    const uint8_t *sbp = sm + kOffRaw + slot * kRawStage + wr * kSlot + off;
+                    const float fs = stk_exp2<WS>(sbp, a.K, sb);
+                    const float sv = 1.0f / fs;  // a power of two: exact
+                    for (uint32_t hf = 0; hf < 2; hf++, gs++) {
+                        const uint32_t sa = gs % kGAStages;
+                        if (gs >= (uint32_t)kGAStages) gemm_wait(&a_empty[sa], gs / kGAStages - 1, a.dev_err);
+                        uint8_t *arow = sm + kOffA + sa * 32768 + hh * 16384 + r * 128;
+                        if (256 * sb + 128 * hf + 64 * hh < a.K) {
+                            stk_dequant<WS>(sbp, 2 * hf + hh, sv, pl, arow, r & 7);
+                        } else {
+#pragma unroll
+                            for (int m = 0; m < 8; m++) *reinterpret_cast<uint4 *>(arow + 16 * m) = make_uint4(0, 0, 0, 0);
+                        }
+                        fence_async_smem();
+                        mbar_arrive(&a_full[sa]);
+                    }
+                    mbar_arrive(&raw_empty[slot]);
+                    if (sb >= 1) fold(gsb - 1, sb - 1, fs_prev);
+                    fs_prev = fs;
+                }
+                fold(gsb - 1, nsb - 1, fs_prev);
+                // activation scale 2^e of each position, then the two planes' lanes add up
+                const uint32_t q0 = PH * hh;
+#pragma unroll
+                for (uint32_t q = 0; q < (uint32_t)PH; q++) {
+                    const uint32_t n = q0 + q;
+                    const uint32_t row = MODE == 0 ? a.p.pos_pair[it.pos0 + min(n, it.nvalid - 1)] / a.k
+                                                   : it.pos0 + min(n, it.nvalid - 1);
+                    y[q] = n < it.nvalid ? y[q] * a.xinv[row] : 0.0f;
+                }
+                constexpr int UX = NP + 1;  // odd stride: no bank conflicts
+                float *uex = reinterpret_cast<float *>(sm + kOffA);  // [64][UX]; the A stages are idle here
+                if (pl == 1)
+#pragma unroll
+                    for (int q = 0; q < PH; q++) uex[wr * UX + q0 + q] = y[q];
+                math_sync();
+                if (pl == 0)
+#pragma unroll
+                    for (int q = 0; q < PH; q++) y[q] += uex[wr * UX + q0 + q];
+                if (MODE == 1) {
+                    if (pl == 0) {
+                        const uint32_t orow = kStkRows * it.m0 + wr;
+#pragma unroll
+                        for (uint32_t q = 0; q < (uint32_t)PH; q++)
+                            if (q0 + q < it.nvalid) a.out[(size_t)(it.pos0 + q0 + q) * a.out_ld + orow] = y[q];
+                    }
+                } else {
+                    math_sync();
+                    if (pl == 0 && wr >= 32)
+#pragma unroll
+                        for (int q = 0; q < PH; q++) uex[(wr - 32) * UX + q0 + q] = y[q];
+                    math_sync();
+                    if (pl == 0 && wr < 32) {
+                        const uint32_t f = 32 * it.m0 + wr;
+#pragma unroll
+                        for (uint32_t q = 0; q < (uint32_t)PH; q++)
+                            if (q0 + q < it.nvalid)
+                                a.out[(size_t)(it.pos0 + q0 + q) * a.F + f] =
+                                    act_apply(a.act, y[q]) * uex[wr * UX + q0 + q];
+                    }
+                }
+                math_sync();  // uex read before the next item's A writes
+            }
+        } else
         for (uint32_t w = blockIdx.x; w < n_work; w += gridDim.x, gi++) {
             const GemmItem it = gemm_item<NP>(a, w);
 #pragma unroll
@@ -452,9 +765,9 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
                     mbar_arrive(&a_full[sa]);
                 }
                 mbar_arrive(&raw_empty[slot]);
-                if (sb >= 1) fold(gsb - 1, sb - 1);
+                if (sb >= 1) fold(gsb - 1, sb - 1, 0.0f);
             }
-            fold(gsb - 1, nsb - 1);
+            fold(gsb - 1, nsb - 1, 0.0f);
             gemm_wait(min_full, gi, a.dev_err);
             tc_fence_after();
             {
@@ -667,10 +980,21 @@ cudaError_t launch_combine(const LaunchCfg &c, const float *y, uint64_t D, const
     return launch_combine_k(c, "moe_combine", y, D, pair_pos, w, ntok, k, resid, out);
 }
 
+// The GEMM scheme of one weight tensor with K columns whose items take
+// `rows` consecutive rows (gate/up: the expert width, in gate/up pairs;
+// down: d_model): 0 for Q4_K in one exact plane, the type for stacked planes,
+// -1 when neither takes it.
+static int gemm_scheme(const DevMat &m, uint64_t K, uint64_t rows, bool gate_up) {
+    if (m.type == T_Q4_K && K % 256 == 0 && K <= 256u * kGMaxSb && rows % (gate_up ? 64 : kGM) == 0) return 0;
+    const bool rows_ok = rows % (gate_up ? 32 : kStkRows) == 0 && K <= 256u * kStkMaxSb;
+    if ((m.type == T_Q4_K || m.type == T_Q6_K) && K % 256 == 0 && rows_ok) return (int)m.type;
+    if (m.type == T_Q8_0 && K % 64 == 0 && rows_ok) return (int)m.type;
+    return -1;
+}
+
 bool moe_gemm_supported(const DevMat &gate, const DevMat &down, uint64_t F) {
-    return gate.type == T_Q4_K && down.type == T_Q4_K && gate.n_experts <= (uint32_t)kRouterMaxE &&
-           gate.cols % 256 == 0 && F % 256 == 0 &&
-           gate.cols <= 256u * kGMaxSb && F <= 256u * kGMaxSb && down.rows % kGM == 0;
+    return gate.n_experts <= (uint32_t)kRouterMaxE && gemm_scheme(gate, gate.cols, F, true) >= 0 &&
+           gemm_scheme(down, F, down.rows, false) >= 0;
 }
 
 size_t moe_gemm_scratch(uint32_t T, uint32_t k, uint32_t E, uint64_t d, uint64_t F) {
@@ -681,11 +1005,31 @@ size_t moe_gemm_scratch(uint32_t T, uint32_t k, uint32_t E, uint64_t d, uint64_t
            al(P * F * 4) + 2 * al(P * F * 2) + al(P * F / 8) + al(P * 4) + al(P * d * 4);
 }
 
+// One GEMM launch of a mode with the instantiation for its weight scheme and
+// tile width.
+template <int MODE>
+static cudaError_t launch_gemm(const LaunchCfg &c, const char *label, bool wide, int ws, const GemmArgs &g) {
+    const dim3 grid((uint32_t)c.num_sms), block(kGThreadsV2);
+#define LT_GEMM_CASE(WS_)                                                                                   \
+    return wide ? launch_k(c, label, k_moe_gemm<MODE, 64, WS_>, grid, block, (size_t)GemmGeo<64>::kSmem, g) \
+                : launch_k(c, label, k_moe_gemm<MODE, 32, WS_>, grid, block, (size_t)GemmGeo<32>::kSmem, g)
+    switch (ws) {
+        case 0: LT_GEMM_CASE(0);
+        case T_Q4_K: LT_GEMM_CASE(T_Q4_K);
+        case T_Q6_K: LT_GEMM_CASE(T_Q6_K);
+        case T_Q8_0: LT_GEMM_CASE(T_Q8_0);
+        default: return cudaErrorInvalidValue;
+    }
+#undef LT_GEMM_CASE
+}
+
 cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const uint8_t *up, const DevMat &down, int act,
                                 const float *x, uint32_t T, uint32_t k, const float *w, const MoePlan &p,
                                 const float *resid, float *out, uint8_t *scratch) {
     const uint32_t E = gate.n_experts;
     const uint64_t d = gate.cols, F = down.cols;
+    const int ws_gu = gemm_scheme(gate, d, F, true), ws_dn = gemm_scheme(down, F, d, false);
+    if (ws_gu < 0 || ws_dn < 0) return cudaErrorInvalidValue;
     const size_t P = (size_t)T * k;
     const size_t max_tiles = (E < P ? E : P) + P / kGN + 1;
     size_t off = 0;
@@ -718,17 +1062,21 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
                      xl, xsum, xinv);
     GemmArgs g;
     const uint32_t E1 = E ? E : 1;
-    if (!encode_rows(&g.map_w, gate.data, gate.pitch, (uint64_t)gate.rows * E1) ||
-        (up && !encode_rows(&g.map_up, up, gate.pitch, (uint64_t)F * E1)))
+    // tensor maps only for the single-plane Q4_K scheme (its rows are 16-byte multiples)
+    if (ws_gu == 0 && (!encode_rows(&g.map_w, gate.data, gate.pitch, (uint64_t)gate.rows * E1) ||
+                       (up && !encode_rows(&g.map_up, up, gate.pitch, (uint64_t)F * E1))))
         return cudaErrorInvalidValue;
-    if (!up) g.map_up = g.map_w;
+    if (ws_gu != 0) memset(&g.map_w, 0, sizeof(g.map_w));
+    if (!up || ws_gu != 0) g.map_up = g.map_w;
     g.w = gate.data;
     g.w_up = up;
+    g.w_end = gate.data + (size_t)gate.rows * E1 * gate.pitch;
+    g.up_end = up ? up + (size_t)F * E1 * gate.pitch : nullptr;
     g.pitch = gate.pitch;
     g.K = (uint32_t)d;
     g.rows_e = (uint32_t)gate.rows;
     g.F = (uint32_t)F;
-    g.mt = (uint32_t)(F / 64);
+    g.mt = (uint32_t)(ws_gu == 0 ? F / 64 : F / 32);
     g.act = act;
     g.p = p;
     g.tiles = tiles;
@@ -741,34 +1089,32 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
     g.out = hbuf;
     g.out_ld = (uint32_t)F;
     g.dev_err = c.dev_err;
-    if (e == cudaSuccess)
-        e = wide ? launch_k(c, "moe_gemm_gate_up", k_moe_gemm<0, 64>, dim3((uint32_t)c.num_sms), dim3(kGThreadsV2),
-                            (size_t)GemmGeo<64>::kSmem, g)
-                 : launch_k(c, "moe_gemm_gate_up", k_moe_gemm<0, 32>, dim3((uint32_t)c.num_sms), dim3(kGThreadsV2),
-                            (size_t)GemmGeo<32>::kSmem, g);
+    if (e == cudaSuccess) e = launch_gemm<0>(c, "moe_gemm_gate_up", wide, ws_gu, g);
     if (e == cudaSuccess)
         e = launch_k(c, "moe_gemm_prep", k_gemm_prep, dim3((uint32_t)((P + 7) / 8)), dim3(256), 0, (const float *)hbuf,
                      (uint32_t)F, (uint32_t)P, hh, hl, hsum, hinv);
     GemmArgs gd = g;
-    if (!encode_rows(&gd.map_w, down.data, down.pitch, (uint64_t)down.rows * E1)) return cudaErrorInvalidValue;
+    if (ws_dn == 0) {
+        if (!encode_rows(&gd.map_w, down.data, down.pitch, (uint64_t)down.rows * E1)) return cudaErrorInvalidValue;
+    } else {
+        memset(&gd.map_w, 0, sizeof(gd.map_w));
+    }
     gd.map_up = gd.map_w;
     gd.w = down.data;
     gd.w_up = nullptr;
+    gd.w_end = down.data + (size_t)down.rows * E1 * down.pitch;
+    gd.up_end = nullptr;
     gd.pitch = down.pitch;
     gd.K = (uint32_t)F;
     gd.rows_e = (uint32_t)down.rows;
-    gd.mt = (uint32_t)(d / kGM);
+    gd.mt = (uint32_t)(ws_dn == 0 ? d / kGM : d / kStkRows);
     gd.xh = hh;
     gd.xl = hl;
     gd.xsum = hsum;
     gd.xinv = hinv;
     gd.out = ybuf;
     gd.out_ld = (uint32_t)d;
-    if (e == cudaSuccess)
-        e = wide ? launch_k(c, "moe_gemm_down", k_moe_gemm<1, 64>, dim3((uint32_t)c.num_sms), dim3(kGThreadsV2),
-                            (size_t)GemmGeo<64>::kSmem, gd)
-                 : launch_k(c, "moe_gemm_down", k_moe_gemm<1, 32>, dim3((uint32_t)c.num_sms), dim3(kGThreadsV2),
-                            (size_t)GemmGeo<32>::kSmem, gd);
+    if (e == cudaSuccess) e = launch_gemm<1>(c, "moe_gemm_down", wide, ws_dn, gd);
     if (e == cudaSuccess)
         e = launch_combine_k(c, "moe_gemm_combine", (const float *)ybuf, d, (const uint32_t *)p.pair_pos, w, T, k,
                              resid, out);

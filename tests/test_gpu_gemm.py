@@ -151,3 +151,46 @@ def test_gemm_skewed_routing(tc, oracle, T):
     tc.sync()
     for t_ in (rt, g, u, dn):
         t_.free()
+
+
+# Stacked-plane schemes: Q6_K and Q8_0 experts, and Q4_K wider than 2048
+# columns (config 3's d_model 2816), each against the oracle.
+# d, F, E, k, gate/up type, down type, fused gate_up, act, T
+Q4, Q6, Q8 = 12, 14, 8
+TYPE_CASES = [
+    (2048, 768, 32, 8, Q6, Q6, False, 0, 70),
+    (2048, 768, 32, 8, Q8, Q8, False, 0, 70),
+    (2048, 768, 16, 8, Q4, Q6, False, 0, 100),    # single-plane Q4_K gate/up, stacked Q6_K down
+    (2048, 768, 8, 8, Q6, Q8, True, 1, 300),      # fused gate_up, GELU, 64-position tiles
+    (2816, 704, 16, 8, Q4, Q8, False, 1, 80),     # config-3 shape: Q4_K over 11 superblocks, Q8_0 down K = 704
+    (2816, 704, 16, 8, Q6, Q8, False, 1, 200),
+    (1024, 512, 8, 2, Q8, Q6, False, 0, 130),
+]
+
+
+def _type_id(c):
+    n = {Q4: "q4k", Q6: "q6k", Q8: "q8_0"}
+    return f"d{c[0]}F{c[1]}E{c[2]}T{c[8]}_{n[c[4]]}_{n[c[5]]}{'_fused' if c[6] else ''}"
+
+
+@pytest.mark.parametrize("case", TYPE_CASES, ids=_type_id)
+def test_gemm_stacked_types_vs_oracle(tc, oracle, pool, case):
+    d, F, E, k, gt, dt, fused, act, T = case
+    rng = np.random.Generator(np.random.PCG64(9100 + d + F + E + T + gt + 3 * dt))
+    L = _synth().MoeLayer(rng, d, E, F, gt, dt, fused)
+    x = rng.normal(0, 1, size=(T, d)).astype(np.float32)
+    rt, g, u, dn = _upload_layer(tc, L)
+    out, ids, ww = empty(T * d), empty(T * k, "int32"), empty(T * k)
+    xd = dev(x)
+    lab = _labels(tc, lambda: tc.moe_forward(rt, g, u, dn, act, True, None, xd, T, k, out, ids, ww))
+    assert "moe_gemm_gate_up" in lab and "moe_gemm_down" in lab, lab
+    got = host(out).reshape(T, d)
+    ref, rids, _ = oracle.moe_layer(L, x, k, True, act, None, pool)
+    assert np.array_equal(host(ids).view(np.uint32).reshape(T, k), rids)
+    assert np.all(np.isfinite(got))
+    assert rel_l2(got, ref) < MOE_L2_TOL
+    assert max_rel(got, ref) < 1e-3
+    tc.sync()
+    for t_ in (rt, g, u, dn):
+        if t_ is not None:
+            t_.free()

@@ -117,8 +117,8 @@ def test_host_library_exports():
     if not lib.exists():
         subprocess.run(["python", str(REPO / "llmtoy-zig_b200" / "build.py")], check=True)
     names = [ln.split("(")[0].split()[-1].lstrip("*") for ln in (REPO / "llmtoy-zig_b200" / "host" / "decoder.h")
-             .read_text().splitlines() if ln.startswith(("lt_status lth_", "void lth_", "const float *lth_"))]
-    assert len(names) == 10
+             .read_text().splitlines() if ln.startswith(("lt_status lth_", "void lth_", "const float *lth_", "int lth_"))]
+    assert len(names) == 12
     L = ctypes.CDLL(str(lib))
     for n in names:
         assert hasattr(L, n), n
