@@ -93,6 +93,11 @@ struct GemmArgs {
     // moves a 64-row x 144-byte box (one Q4_K superblock column)
     alignas(64) CUtensorMap map_w;
     alignas(64) CUtensorMap map_up;
+    // the activation planes [P][K] (f16, 128B swizzle, box 64 x NP), rows in
+    // dispatch-position order: an item's positions are consecutive rows, so
+    // the B warp loads each stage with four tiled TMA copies
+    alignas(64) CUtensorMap map_bh;
+    alignas(64) CUtensorMap map_bl;
     const uint8_t *w;     // gate (mode 0) or down (mode 1) weights
     const uint8_t *w_up;  // mode 0: up weights; nullptr when w holds [gate; up] per expert
     const uint8_t *w_end, *up_end;  // one past the last byte of w / w_up
@@ -106,9 +111,9 @@ struct GemmArgs {
     const uint2 *tiles;  // (active expert slot, first position within it)
     const uint32_t *n_tiles;
     uint32_t k;  // slots per token
-    const __half *xh, *xl;  // activation rows [R][K], K permuted in groups of 4
-    const float *xsum;      // [R][K/32] sub-block sums of the scaled rows
-    const float *xinv;      // [R] 2^e
+    const __half *xh, *xl;  // activation planes [P][K] by position, K permuted in groups of 4 (read through the maps)
+    const float *xsum;      // [P][K/32] sub-block sums of the scaled rows
+    const float *xinv;      // [P] 2^e
     float *out;             // mode 0: h [P][F]; mode 1: y [P][out_ld]
     uint32_t out_ld;
     int *dev_err;
@@ -405,7 +410,7 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
         for (int i = 0; i < 3; i++) {
             mbar_init(&raw_full[i], kStk ? 32 : 1);  // stacked: one cp.async arrival per producer lane
             mbar_init(&raw_empty[i], kGMath);
-            mbar_init(&b_full[i], 32);
+            mbar_init(&b_full[i], 1);
             mbar_init(&b_empty[i], 1);
         }
         for (int i = 0; i < 2; i++) {
@@ -503,27 +508,26 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
             for (int pp = 0; pp < PPL; pp++) {
                 const uint32_t n = lane + 32 * pp;
                 valid[pp] = n < it.nvalid;
-                row[pp] = !valid[pp] ? 0 : MODE == 0 ? a.p.pos_pair[it.pos0 + n] / a.k : it.pos0 + n;
+                row[pp] = valid[pp] ? it.pos0 + n : 0;  // the planes are in dispatch-position order
             }
             const uint32_t nks = 2 * nsb, ks_bm = nks > 2 ? 2 : nks - 1;
             for (uint32_t ks = 0; ks < nks; ks++, gs++) {
                 const uint32_t s = gs % kGBStages;
                 if (gs >= (uint32_t)kGBStages) gemm_wait(&b_empty[s], gs / kGBStages - 1, a.dev_err);
+                {
+                    // rows past the last position read as zeros, columns past K too;
+                    // rows of other experts' positions are never stored
+                    if (lane == 0) {
+                        uint8_t *bs = sm + kOffB + s * Geo::kBStage;
+                        mbar_arrive_expect_tx(&b_full[s], Geo::kBStage);
 #pragma unroll
-                for (int pp = 0; pp < PPL; pp++) {
-                    const uint32_t n = lane + 32 * pp;
-                    const __half *srch = a.xh + (size_t)row[pp] * a.K, *srcl = a.xl + (size_t)row[pp] * a.K;
-                    uint8_t *bs = sm + kOffB + s * Geo::kBStage + n * 128;
-#pragma unroll
-                    for (uint32_t cc = 0; cc < 16; cc++) {
-                        const uint32_t o = (cc >> 3) * Geo::kBAtom + (((cc & 7) ^ (n & 7)) << 4);
-                        const uint32_t col = ks * 128 + cc * 8;  // zeros past K (stacked Q8_0 rows)
-                        const bool in = valid[pp] && col < a.K;
-                        cp_async16(bs + o, srch + (in ? col : 0), in ? 16u : 0u);
-                        cp_async16(bs + NP * 128 + o, srcl + (in ? col : 0), in ? 16u : 0u);
+                        for (uint32_t at = 0; at < 2; at++) {
+                            tma_load_2d(bs + at * Geo::kBAtom, &a.map_bh, ks * 128 + at * 64, it.pos0, &b_full[s]);
+                            tma_load_2d(bs + at * Geo::kBAtom + NP * 128, &a.map_bl, ks * 128 + at * 64, it.pos0,
+                                        &b_full[s]);
+                        }
                     }
                 }
-                cp_async_arrive(&b_full[s]);
                 if (!kStk && ks == ks_bm) {
                     // the previous item's min term has consumed the old B rows
                     if (gi >= 1) gemm_wait(min_full, gi - 1, a.dev_err);
@@ -668,8 +672,7 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
 #pragma unroll
                 for (uint32_t q = 0; q < (uint32_t)PH; q++) {
                     const uint32_t n = q0 + q;
-                    const uint32_t row = MODE == 0 ? a.p.pos_pair[it.pos0 + min(n, it.nvalid - 1)] / a.k
-                                                   : it.pos0 + min(n, it.nvalid - 1);
+                    const uint32_t row = it.pos0 + min(n, it.nvalid - 1);
                     y[q] = n < it.nvalid ? y[q] * a.xinv[row] : 0.0f;
                 }
                 constexpr int UX = NP + 1;  // odd stride: no bank conflicts
@@ -814,12 +817,17 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
 // as the dequantised weights are), sub-block sums, 2^e per row ─────────────
 // One warp per row (eight rows per block): no block barriers, and every
 // warp's loads in flight at once.  K % 256 == 0.
+// With rowmap, output row r (a dispatch position) takes source row
+// rowmap[r] / kdiv (its token); positions past the plan's last one hold stale
+// map entries and are clamped to a valid row (no tile reads their results).
 __global__ void __launch_bounds__(256) k_gemm_prep(const float *src, uint32_t K, uint32_t rows, __half *xh,
-                                                   __half *xl, float *xsum, float *xinv) {
+                                                   __half *xl, float *xsum, float *xinv, const uint32_t *rowmap,
+                                                   uint32_t kdiv, uint32_t nsrc) {
     pdl_wait();
     const uint32_t lane = threadIdx.x & 31, row = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (row >= rows) return;
-    const float *s = src + (size_t)row * K;
+    const uint32_t srow = rowmap ? min(__ldg(rowmap + row) / kdiv, nsrc - 1) : row;
+    const float *s = src + (size_t)srow * K;
     float amax = 0.0f;
 #pragma unroll 4
     for (uint32_t i = 4 * lane; i < K; i += 128) {
@@ -973,6 +981,20 @@ bool encode_rows(CUtensorMap *map, const void *base, uint64_t pitch, uint64_t to
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// [rows][K] f16 activation plane as a tiled map: box 64 columns (128 bytes,
+// 128B swizzle, the UMMA K-major atom) x np rows; out-of-range reads as zero.
+bool encode_act(CUtensorMap *map, const void *base, uint64_t K, uint64_t rows, uint32_t np) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || (K * 2) % 16) return false;
+    const cuuint64_t dims[2] = {K, rows};
+    const cuuint64_t strides[1] = {K * 2};
+    const cuuint32_t box[2] = {64, np};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 cudaError_t launch_combine(const LaunchCfg &c, const float *y, uint64_t D, const uint32_t *pair_pos, const float *w,
@@ -1001,8 +1023,8 @@ size_t moe_gemm_scratch(uint32_t T, uint32_t k, uint32_t E, uint64_t d, uint64_t
     const size_t P = (size_t)T * k;
     auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
     const size_t max_tiles = (E < P ? E : P) + P / kGN + 1;
-    return al(max_tiles * 8) + al(4) + 2 * al((size_t)T * d * 2) + al((size_t)T * d / 8) + al((size_t)T * 4) +
-           al(P * F * 4) + 2 * al(P * F * 2) + al(P * F / 8) + al(P * 4) + al(P * d * 4);
+    return al(max_tiles * 8) + al(4) + 2 * al(P * d * 2) + al(P * d / 8) + al(P * 4) + al(P * F * 4) +
+           2 * al(P * F * 2) + al(P * F / 8) + al(P * 4) + al(P * d * 4);
 }
 
 // One GEMM launch of a mode with the instantiation for its weight scheme and
@@ -1040,10 +1062,12 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
     };
     uint2 *tiles = reinterpret_cast<uint2 *>(take(max_tiles * 8));
     uint32_t *n_tiles = reinterpret_cast<uint32_t *>(take(4));
-    __half *xh = reinterpret_cast<__half *>(take((size_t)T * d * 2));
-    __half *xl = reinterpret_cast<__half *>(take((size_t)T * d * 2));
-    float *xsum = reinterpret_cast<float *>(take((size_t)T * d / 8));
-    float *xinv = reinterpret_cast<float *>(take((size_t)T * 4));
+    // the expert input's planes in dispatch-position order (P rows: each
+    // token once per selected expert), so every tile's rows are consecutive
+    __half *xh = reinterpret_cast<__half *>(take(P * d * 2));
+    __half *xl = reinterpret_cast<__half *>(take(P * d * 2));
+    float *xsum = reinterpret_cast<float *>(take(P * d / 8));
+    float *xinv = reinterpret_cast<float *>(take(P * 4));
     float *hbuf = reinterpret_cast<float *>(take(P * F * 4));
     __half *hh = reinterpret_cast<__half *>(take(P * F * 2));
     __half *hl = reinterpret_cast<__half *>(take(P * F * 2));
@@ -1058,9 +1082,10 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
                          : launch_k(c, "moe_gemm_tiles", k_gemm_tiles<32>, dim3(1), dim3(kRouterMaxE), 0, p, tiles,
                                     n_tiles);
     if (e == cudaSuccess)
-        e = launch_k(c, "moe_gemm_prep", k_gemm_prep, dim3((T + 7) / 8), dim3(256), 0, x, (uint32_t)d, (uint32_t)T, xh,
-                     xl, xsum, xinv);
+        e = launch_k(c, "moe_gemm_prep", k_gemm_prep, dim3((uint32_t)((P + 7) / 8)), dim3(256), 0, x, (uint32_t)d,
+                     (uint32_t)P, xh, xl, xsum, xinv, (const uint32_t *)p.pos_pair, k, T);
     GemmArgs g;
+    memset(&g, 0, sizeof(g));  // the tensor maps a launch does not use stay zero
     const uint32_t E1 = E ? E : 1;
     // tensor maps only for the single-plane Q4_K scheme (its rows are 16-byte multiples)
     if (ws_gu == 0 && (!encode_rows(&g.map_w, gate.data, gate.pitch, (uint64_t)gate.rows * E1) ||
@@ -1084,6 +1109,8 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
     g.k = k;
     g.xh = xh;
     g.xl = xl;
+    if (!encode_act(&g.map_bh, xh, d, P, wide ? 64 : 32) || !encode_act(&g.map_bl, xl, d, P, wide ? 64 : 32))
+        return cudaErrorInvalidValue;
     g.xsum = xsum;
     g.xinv = xinv;
     g.out = hbuf;
@@ -1092,7 +1119,7 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
     if (e == cudaSuccess) e = launch_gemm<0>(c, "moe_gemm_gate_up", wide, ws_gu, g);
     if (e == cudaSuccess)
         e = launch_k(c, "moe_gemm_prep", k_gemm_prep, dim3((uint32_t)((P + 7) / 8)), dim3(256), 0, (const float *)hbuf,
-                     (uint32_t)F, (uint32_t)P, hh, hl, hsum, hinv);
+                     (uint32_t)F, (uint32_t)P, hh, hl, hsum, hinv, (const uint32_t *)nullptr, 1u, (uint32_t)P);
     GemmArgs gd = g;
     if (ws_dn == 0) {
         if (!encode_rows(&gd.map_w, down.data, down.pitch, (uint64_t)down.rows * E1)) return cudaErrorInvalidValue;
@@ -1110,6 +1137,8 @@ cudaError_t launch_moe_gemm_ffn(const LaunchCfg &c, const DevMat &gate, const ui
     gd.mt = (uint32_t)(ws_dn == 0 ? d / kGM : d / kStkRows);
     gd.xh = hh;
     gd.xl = hl;
+    if (!encode_act(&gd.map_bh, hh, F, P, wide ? 64 : 32) || !encode_act(&gd.map_bl, hl, F, P, wide ? 64 : 32))
+        return cudaErrorInvalidValue;
     gd.xsum = hsum;
     gd.xinv = hinv;
     gd.out = ybuf;
