@@ -534,18 +534,23 @@ __global__ void __launch_bounds__(kGThreadsV2, 1) k_moe_gemm(const __grid_consta
 #pragma unroll
                     for (int pp = 0; pp < PPL; pp++) {
                         const uint32_t n = lane + 32 * pp;
-                        const float inv = valid[pp] ? a.xinv[row[pp]] : 0.0f;
-                        const float *xs = a.xsum + (size_t)row[pp] * (a.K / 32);
-                        for (uint32_t j = 0; j < 8 * nsb; j += 4) {
-                            float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                            if (valid[pp]) v4 = *reinterpret_cast<const float4 *>(xs + j);
-                            const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+                        const float inv = valid[pp] ? __ldg(a.xinv + row[pp]) : 0.0f;
+                        // every sub-block sum of the row in flight at once (K <= 2048: 16 float4)
+                        const float4 *xs4 = reinterpret_cast<const float4 *>(a.xsum + (size_t)row[pp] * (a.K / 32));
+                        float4 v4[2 * kGMaxSb];
+#pragma unroll
+                        for (int u = 0; u < 2 * kGMaxSb; u++)
+                            v4[u] = valid[pp] && (uint32_t)u < 2 * nsb ? __ldg(xs4 + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                        for (int u = 0; u < 2 * kGMaxSb; u++) {
+                            if ((uint32_t)u >= 2 * nsb) break;
+                            const float v[4] = {v4[u].x, v4[u].y, v4[u].z, v4[u].w};
 #pragma unroll
                             for (int q = 0; q < 4; q++) {
                                 __half h, l;
                                 split_f16(v[q], h, l);
-                                *reinterpret_cast<__half *>(sm + kOffBm + sw128_offset(n, j + q)) = h;
-                                *reinterpret_cast<__half *>(sm + kOffBm + sw128_offset(NP + n, j + q)) = l;
+                                *reinterpret_cast<__half *>(sm + kOffBm + sw128_offset(n, 4 * u + q)) = h;
+                                *reinterpret_cast<__half *>(sm + kOffBm + sw128_offset(NP + n, 4 * u + q)) = l;
                             }
                         }
                         s_inv[(gi & 1) * NP + n] = inv;
