@@ -170,6 +170,23 @@ LT_DEVINL void ab_tail(const AttnBlockArgs &a, const AbTailW &t, float *xf, floa
     __syncthreads();
 }
 
+// Phase timestamps for tuning builds (-DLT_DECODE_TRACE): thread 0 of each
+// CTA records globaltimer at the phase boundaries of the latest launch.  Off
+// in the library the package builds.
+#ifdef LT_DECODE_TRACE
+constexpr int kAtCtas = 160, kAtMarks = 24;
+__device__ unsigned long long g_ab_trace[kAtCtas * kAtMarks];
+#define AT_MARK(m)                                                                     \
+    do {                                                                               \
+        if (tid == 0 && c < kAtCtas) g_ab_trace[c * kAtMarks + (m)] = globaltimer_ns(); \
+    } while (0)
+extern "C" int lt_ab_trace_copy(void *dst, size_t bytes) { return (int)cudaMemcpyFromSymbol(dst, g_ab_trace, bytes); }
+#else
+#define AT_MARK(m) \
+    do {           \
+    } while (0)
+#endif
+
 // GEN: segments, V = K, the post-attention norm or the late wo tile may occur
 // (otherwise: one stacked Q/K/V tensor, plain residual, both tiles at once).
 template <uint32_t QT, uint32_t OT, int HD, bool GEN>
@@ -202,6 +219,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     const uint32_t q0 = (uint32_t)((uint64_t)c * a.qrows / G), q1 = (uint32_t)((uint64_t)(c + 1) * a.qrows / G);
     const uint32_t o0 = (uint32_t)((uint64_t)c * a.d / G), o1 = (uint32_t)((uint64_t)(c + 1) * a.d / G);
     const uint32_t nqr = q1 - q0, nor = o1 - o0;
+    AT_MARK(0);
 
     // static inputs first: both weight tiles, the norm weights, the L2 prefetch
     if (tid == 0) {
@@ -242,12 +260,14 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     for (uint32_t i = tid; i < a.d; i += kAbThreads) nw[i] = __ldg(a.norm_w + i);
     pdl_launch_dependents();
     pdl_wait();
+    AT_MARK(1);
 
     // ── phase Q ──────────────────────────────────────────────────────────────
     if (tid == 0) *s_epoch = grid_epoch(ctr_epoch, G);
     const uint32_t pos = *a.pos;
     ab_load(xf, a.x, a.d);
     __syncthreads();
+    AT_MARK(2);
     if (GEN && a.tail_f) ab_tail(a, tw, xf, red);  // the block's input is the previous layer's output
     for (uint32_t r = tid; r < nor; r += kAbThreads) xres[r] = xf[o0 + r];
     {
@@ -260,6 +280,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     __syncthreads();
     ab_quantise(Xx, xf, a.d, warp, lane);
     __syncthreads();
+    AT_MARK(3);
     const uint64_t epoch = *s_epoch;
     float *yq = xf;  // the normalised x is quantised already
     if constexpr (!GEN) {
@@ -276,10 +297,12 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
         }
     }
     __syncthreads();
+    AT_MARK(4);
     for (uint32_t r = tid; r < nqr; r += kAbThreads)
         a.qkv[q0 + r] = a.bias ? __fadd_rn(yq[r], a.bias[q0 + r]) : yq[r];
     grid_arrive(ctr1);
     grid_wait(ctr1, epoch, a.dev_err, kWaitLimitNs);
+    AT_MARK(5);
 
     // ── phase A ──────────────────────────────────────────────────────────────
     if (GEN && a.late_wo) {  // the Q/K/V rows are consumed: the wo rows take their place
@@ -305,6 +328,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
             reinterpret_cast<float4 *>(hq + part * HD)[i] = __ldcg(reinterpret_cast<const float4 *>(a.qkv + off) + i);
         }
         __syncthreads();
+        AT_MARK(6);
         if (a.g.v_norm) {  // rmsnormRaw (math.zig:43-48) of the V head
             const float vv = tid < HD ? hv[tid] : 0.0f;
             const float ss = ab_block_sum(tid < HD ? __fmul_rn(vv, vv) : 0.0f, red);
@@ -314,6 +338,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
             __syncthreads();
         }
         ab_norm_rope2(hq, a.q_norm, hk, a.k_norm, a.g, pos, red);
+        AT_MARK(7);
         if (s == 0 && h % group == 0) {  // this position's K/V into the cache
             const size_t slot = (size_t)(pos % a.g.cap) * nkv + (size_t)kh * HD;
             for (uint32_t i = tid; i < HD; i += kAbThreads) {
@@ -334,6 +359,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
             ab_attend<HD, true>(a.kc, a.vc, a.g, s, S, win, first, (size_t)kh * HD, nkv, hq, hk, hv, warp, lane, m, l, o);
         else
             ab_attend<HD, false>(a.kc, a.vc, a.g, s, S, win, first, (size_t)kh * HD, nkv, hq, hk, hv, warp, lane, m, l, o);
+        AT_MARK(8);
         float *wp = wpart + warp * (HD + 2);
         if (lane == 0) {
             wp[0] = m;
@@ -371,6 +397,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
             for (uint32_t b = warp; b < (uint32_t)HD / 32; b += kAbWarps)
                 qact_store_block(a.att, (int)nq, (int)(h * HD / 32 + b), hq[32 * b + lane], lane);
             __syncthreads();
+            AT_MARK(9);
             continue;
         }
         // split partials: o [h][s][HD] (16-byte aligned rows), (max, sum) [h][s]
@@ -416,15 +443,19 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
         }
         __syncthreads();
     }
+    AT_MARK(10);
     grid_arrive(ctr2);
     grid_wait(ctr2, epoch, a.dev_err, kWaitLimitNs);
+    AT_MARK(11);
 
     // ── phase O ──────────────────────────────────────────────────────────────
     ab_load_qact(Xa, a.att, nq);
     __syncthreads();
+    AT_MARK(12);
     float *yo = xf;  // the attention vector is quantised already
     if (nor && tile_wait(&bars[1], a.dev_err)) ab_rows_any<OT>(a.otype, wo, a.opitch, nor, nq, a.onb, Xa, warp, lane, yo);
     __syncthreads();
+    AT_MARK(13);
     if (GEN && a.post_norm) {  // x + rmsnorm(y) * w over all d outputs: partial sums, a third hand-off
         float ss = 0.0f;
         for (uint32_t r = tid; r < nor; r += kAbThreads) ss = __fadd_rn(ss, __fmul_rn(yo[r], yo[r]));
@@ -441,6 +472,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     } else {
         for (uint32_t r = tid; r < nor; r += kAbThreads) a.out[o0 + r] = __fadd_rn(xres[r], yo[r]);
     }
+    AT_MARK(14);
 }
 
 static bool ab_type_ok(uint32_t t) { return t == T_Q8_0 || t == T_Q4_K || t == T_Q6_K; }

@@ -17,11 +17,11 @@
 //            separate barrier) and ranks them itself: identical inputs and
 //            code, so identical ids everywhere.
 //   phase G  each CTA issues one TMA bulk copy per 8 gate/up pairs of its
-//            share (whole 16-pair units of the k*F (slot, row) pairs) and one
-//            per slot for its share of the down rows, all at once, computes
-//            its h values as the copies land, quantises them (16-groups) and
-//            writes them into the shared-memory image of their slot in global
-//            memory.                                      -> grid barrier
+//            share (whole 16-pair units of the k*F (slot, row) pairs), all at
+//            once, computes its h values as the copies land, requests its
+//            share of the down rows (one copy per slot), quantises h
+//            (16-groups) and writes it into the shared-memory image of its
+//            slot in global memory.                       -> grid barrier
 //   phase D  each CTA copies the k slot images with one TMA copy each and
 //            finishes its down rows for every slot, combines them in slot
 //            order and adds the residual kept from phase R.
@@ -134,6 +134,25 @@ __host__ __device__ inline DecodeLayout decode_layout(uint32_t E, uint32_t d, ui
     return L;
 }
 
+// Phase timestamps for tuning builds (-DLT_DECODE_TRACE): thread 0 of each
+// CTA records globaltimer at the phase boundaries of the latest launch.  Off
+// in the library the package builds.
+#ifdef LT_DECODE_TRACE
+constexpr int kDtCtas = 160, kDtMarks = 24;
+__device__ unsigned long long g_moe_trace[kDtCtas * kDtMarks];
+#define DT_MARK(m)                                                                      \
+    do {                                                                                \
+        if (tid == 0 && c < kDtCtas) g_moe_trace[c * kDtMarks + (m)] = globaltimer_ns(); \
+    } while (0)
+extern "C" int lt_moe_trace_copy(void *dst, size_t bytes) {
+    return (int)cudaMemcpyFromSymbol(dst, g_moe_trace, bytes);
+}
+#else
+#define DT_MARK(m) \
+    do {           \
+    } while (0)
+#endif
+
 // ROUNDS: the gate/up share is taken in rounds of a.gchunks chunks (only
 // instantiated for launches whose share exceeds the tile space).
 template <uint32_t GT, uint32_t DT, bool ROUNDS>
@@ -176,6 +195,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     const uint32_t ch0 = p0 / kDecChunk;
     const uint32_t nchunks = np / kDecChunk;  // p0, p1 are multiples of 16
 
+    DT_MARK(0);
     if (tid < 16) s_sel[tid] = 0;  // ranks form a permutation; this only keeps ids in range regardless
     if (tid == 0) {
         for (uint32_t i = 0; i < nchunks; i++) mbar_init(&bars[i], 1);
@@ -193,6 +213,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     if (tid < 2 && a.pf[tid]) prefetch_l2_share(a.pf[tid], a.pf_bytes[tid], c, G);
     pdl_launch_dependents();
     pdl_wait();
+    DT_MARK(1);
 
     // ── phase R ──────────────────────────────────────────────────────────────
     uint64_t epoch = 0;
@@ -206,6 +227,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
         for (uint32_t i = tid; i < a.d; i += kDecThreads) xsm[i] = __ldcg(a.x + i);
     }
     __syncthreads();
+    DT_MARK(2);
     for (uint32_t r = tid; r < nr; r += kDecThreads) s_xres[r] = xsm[r0 + r];
     const float *xrouter = xsm;  // the router's input
     if (a.norm_w && a.router_scale) {  // norm_pair: one rms_inv, per-thread sums over 512 strided values
@@ -245,6 +267,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     if (tid == 0) *s_epoch = epoch;  // the atomic has long returned by now
     __syncthreads();
     epoch = *s_epoch;
+    DT_MARK(3);
     const uint32_t tag = (uint32_t)epoch;
     // warps [0, nlw) compute this CTA's logits; the others quantise the
     // normalised x for this CTA's gate/up meanwhile
@@ -252,6 +275,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     if (has_e) {
         const float v = router_logit(a.rw + (size_t)e_mine * a.rw_ld, xrouter, a.d, lane, w0);
         if (lane == 0) st_relaxed_u64(lslots + e_mine, ((uint64_t)tag << 32) | __float_as_uint(v));
+        DT_MARK(4);
     } else {
         for (uint32_t b = warp - nlw; b < a.d / 32; b += kDecWarps - nlw)
             qact_block_to_xs(Xx, 0, (int)b, xsm[32 * b + lane], lane);
@@ -275,6 +299,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     }
     if (tid == 0) s_key[a.E] = 0;
     __syncthreads();
+    DT_MARK(5);
     if (!a.dense) {
         if (warp == kDecWarps - 1) {  // softmax statistics while the other warps rank
             float mx, es;
@@ -287,6 +312,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
         router_rank_keys_split(s_key, a.E, a.k, s_sel, min(4u, (uint32_t)(kDecThreads - 32) / a.E), s_cnt, tid);
     }
     __syncthreads();
+    DT_MARK(6);
 
     // ── phase G ──────────────────────────────────────────────────────────────
     // chunk j: [8 gate rows][8 up rows] of pairs p0 + 8j.., into tile slot j % gchunks
@@ -313,14 +339,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     };
     if (warp == 0) {  // one TMA chunk per lane: the first round's
         for (uint32_t j = lane; j < (ROUNDS ? min(nchunks, a.gchunks) : nchunks); j += 32) issue_chunk(j);
-    } else if (warp == 1) {  // down rows [r0, r1) of each slot's expert
-        if (!a.late_down && (uint32_t)lane < a.k && nr) {
-            const uint32_t e = min(s_sel[lane], a.E - 1);
-            const uint32_t bytes = (uint32_t)(nr * a.dpitch);
-            mbar_arrive_expect_tx(&bars[kDecMaxChunks + lane], bytes);
-            tma_load_1d(dt + (size_t)lane * a.maxrows * a.dpitch, a.down + ((uint64_t)e * a.d + r0) * a.dpitch, bytes,
-                        &bars[kDecMaxChunks + lane]);
-        }
+        DT_MARK(7);
     } else if (warp == 2 && lane == 0) {
         if (a.dense)
             s_w[0] = 1.0f;
@@ -383,7 +402,19 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     } else {
         gate_up_rows(0, 2 * np);
     }
+    DT_MARK(8);
     __syncthreads();
+    DT_MARK(9);
+    // down rows [r0, r1) of each slot's expert, requested once this CTA's
+    // gate/up rows are consumed: until then every CTA's HBM requests are the
+    // gate/up rows, which the grid's slowest CTA (and so the h barrier) waits for
+    if (warp == 1 && !a.late_down && (uint32_t)lane < a.k && nr) {
+        const uint32_t e = min(s_sel[lane], a.E - 1);
+        const uint32_t bytes = (uint32_t)(nr * a.dpitch);
+        mbar_arrive_expect_tx(&bars[kDecMaxChunks + lane], bytes);
+        tma_load_1d(dt + (size_t)lane * a.maxrows * a.dpitch, a.down + ((uint64_t)e * a.d + r0) * a.dpitch, bytes,
+                    &bars[kDecMaxChunks + lane]);
+    }
     for (uint32_t lp = tid; lp < np; lp += kDecThreads) {  // chunk partials summed in column order
         const uint32_t rg = 2 * kDecChunk * (lp / kDecChunk) + lp % kDecChunk;
         const float *pg = part + rg, *pu = pg + kDecChunk;
@@ -395,6 +426,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
         s_h[lp] = act_apply(a.act, g) * u;
     }
     __syncthreads();
+    DT_MARK(10);
     // quantise this CTA's h values into their slots' images (32-blocks; a
     // block may be half this CTA's)
     for (uint32_t b = p0 / 32 + warp; b * 32 < p1; b += kDecWarps) {
@@ -407,8 +439,10 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     fence_proxy_async_global();  // the images are read by TMA after the barrier
     // the slot images land (by TMA) where x and the norm weights were
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    DT_MARK(11);
     grid_arrive(ctr_b);
     grid_wait(ctr_b, epoch, a.dev_err, kWaitLimitNs);
+    DT_MARK(12);
 
     // ── phase D ──────────────────────────────────────────────────────────────
     uint8_t *himg_s = smem + L.rr;  // k slot images, a.img bytes each
@@ -427,6 +461,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
             }
     }
     const bool hok = tile_wait(hbar, a.dev_err);
+    DT_MARK(13);
     // down: warps [s*wps, (s+1)*wps) take slot s; a lane owns one 64-column
     // chunk of that slot's h in registers
     const uint32_t cpr_d = chunks64(a.F);
@@ -461,6 +496,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
         }
     }
     __syncthreads();
+    DT_MARK(14);
     for (uint32_t w = tid; w < a.k * nr; w += kDecThreads) {  // y[s][r]: chunk partials in column order
         const uint32_t s = w / nr, r = w - s * nr;
         const float *pp = part + s * a.maxrows + r;
@@ -469,11 +505,13 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
         s_y[s * a.maxrows + r] = y;
     }
     __syncthreads();
+    DT_MARK(15);
     for (uint32_t r = tid; r < nr; r += kDecThreads) {
         float o = 0.0f;  // moe_buf is zeroed, then += scale * down, slot by slot
         for (uint32_t s = 0; s < a.k; s++) o += s_w[s] * s_y[s * a.maxrows + r];
         a.out[r0 + r] = a.residual ? s_xres[r] + o : o;
     }
+    DT_MARK(16);
 }
 
 namespace {

@@ -306,12 +306,281 @@ __global__ void __launch_bounds__(kRtWarps * 32, 2) k_router_tok(RouterArgs a) {
     }
 }
 
+// Register-tiled token-major router for large batches.  dotf32's order makes
+// each logit 32 independent chains (lane l sums w[l + 32j] * x[l + 32j] over
+// j in order), combined in a fixed order at the end; every chain is an
+// ordinary sequential accumulation, so a CTA can compute the logits of a
+// tile of TC tokens x EC experts like a GEMM with K split into 32 residue
+// classes: thread (warp, lane l) holds the chains of residue l for 8 tokens
+// x 8 experts in registers, and each 32-column step costs 16 shared-memory
+// loads for 64 multiply-adds (k_router_tok: one load per multiply-add, one
+// chain per warp).  x and the router rows stream through two stages of
+// 256 columns by cp.async; the chains are combined through shared memory in
+// router_logit's order; the last of a token tile's expert-group CTAs ranks
+// the tile's tokens with the shared ranking and weight code.  The norm, the
+// quantised / f32 rows and every result equal k_router_tok's bit for bit.
+constexpr int kRmTT = 8, kRmEE = 8;  // tokens x experts per thread
+constexpr uint32_t kRmKC = 256;      // columns per stage (8 steps of 32)
+constexpr int kRmNorm = 128;         // threads per token of the norm reduction (kRouterNormThreads)
+
+template <int WT, int WE>
+struct RmGeo {
+    static constexpr int NT = WT * WE * 32;
+    static constexpr int TC = WT * kRmTT, EC = WE * kRmEE;
+    static constexpr size_t kStage = (size_t)(TC + EC + 1) * kRmKC;  // floats per stage: x, router rows, norm weights
+    static constexpr size_t kSmem = 2 * kStage * 4;
+};
+
+namespace {
+LT_DEVINL void rm_cp16(float *dst_smem, const float *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst_smem)), "l"(src),
+                 "r"(src_bytes)
+                 : "memory");
+}
+LT_DEVINL void rm_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+LT_DEVINL void rm_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+}  // namespace
+
+template <int WT, int WE>
+__global__ void __launch_bounds__(WT *WE * 32, WT *WE <= 8 ? 2 : 1) k_router_mm(RouterArgs a) {
+    using Gm = RmGeo<WT, WE>;
+    constexpr int NT = Gm::NT, TC = Gm::TC, EC = Gm::EC;
+    constexpr int NG = NT / kRmNorm;  // tokens normalised at once
+    extern __shared__ __align__(16) float msm[];
+    __shared__ float s_part[TC][kRmNorm / 32];
+    __shared__ float s_rms[TC];
+    __shared__ uint32_t s_sel[TC][16];
+    __shared__ float s_mx[TC], s_es[TC];
+    __shared__ int s_last;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t cols = a.cols, E = a.E;
+    const uint32_t e0 = blockIdx.x * EC, t0 = blockIdx.y * TC;
+    const uint32_t nt = min((uint32_t)TC, a.ntok - t0);
+    const uint32_t wt = (uint32_t)warp / WE, we = (uint32_t)warp % WE;
+    const uint32_t nchunks = (cols + kRmKC - 1) / kRmKC;
+    auto sx = [&](uint32_t st) { return msm + st * Gm::kStage; };
+    auto sw = [&](uint32_t st) { return msm + st * Gm::kStage + (size_t)TC * kRmKC; };
+    auto sn = [&](uint32_t st) { return msm + st * Gm::kStage + (size_t)(TC + EC) * kRmKC; };
+    // chunk ch into stage ch & 1: x rows past the batch and router rows past E read as zeros
+    auto issue = [&](uint32_t ch) {
+        constexpr uint32_t Q = kRmKC / 4;  // 16-byte pieces of a full chunk row
+        const uint32_t c0 = ch * kRmKC, q = min(kRmKC, cols - c0) / 4;
+        float *xs = sx(ch & 1), *ws = sw(ch & 1);
+#pragma unroll
+        for (uint32_t i = tid; i < TC * Q; i += NT) {
+            const uint32_t r = i / Q, p = i % Q;
+            const bool ok = r < nt;
+            if (p < q)
+                rm_cp16(xs + r * kRmKC + 4 * p, a.x + (size_t)(t0 + (ok ? r : 0)) * cols + c0 + 4 * p, ok ? 16u : 0u);
+        }
+#pragma unroll
+        for (uint32_t i = tid; i < EC * Q; i += NT) {
+            const uint32_t r = i / Q, p = i % Q;
+            const bool ok = e0 + r < E;
+            if (p < q)
+                rm_cp16(ws + r * kRmKC + 4 * p, a.W + (size_t)(ok ? e0 + r : 0) * a.w_ld + c0 + 4 * p, ok ? 16u : 0u);
+        }
+        if (a.norm_w && (uint32_t)tid < q) rm_cp16(sn(ch & 1) + 4 * tid, a.norm_w + c0 + 4 * tid, 16u);
+        rm_commit();
+    };
+    pdl_launch_dependents();
+    pdl_wait();
+    issue(0);
+    if (nchunks > 1) issue(1);
+    if (a.norm_w) {
+        // k_router_tok's reduction: per token, 128 threads stride the columns,
+        // then their 4 warp sums in order (here every token of the tile at once)
+        const uint32_t g = (uint32_t)tid / kRmNorm, ti = (uint32_t)tid % kRmNorm;
+        constexpr int TPG = TC / NG;  // tokens per thread
+        const float *xb = a.x + (size_t)t0 * cols;
+        float ss[TPG];
+#pragma unroll
+        for (int k = 0; k < TPG; k++) ss[k] = 0.0f;
+        for (uint32_t i0 = ti; i0 < cols; i0 += 4 * kRmNorm) {  // four strides' loads in flight, then the sums in order
+            float v[4][TPG];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+#pragma unroll
+                for (int k = 0; k < TPG; k++) {
+                    const uint32_t tt = g + (uint32_t)k * NG, i = i0 + (uint32_t)u * kRmNorm;
+                    v[u][k] = tt < nt && i < cols ? __ldg(xb + (size_t)tt * cols + i) : 0.0f;
+                }
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+#pragma unroll
+                for (int k = 0; k < TPG; k++)
+                    if (i0 + (uint32_t)u * kRmNorm < cols) ss[k] += v[u][k] * v[u][k];
+        }
+#pragma unroll
+        for (int k = 0; k < TC / NG; k++) {
+            const float s = warp_sum(ss[k]);
+            if (lane == 0) s_part[g + k * NG][ti / 32] = s;
+        }
+        __syncthreads();
+        if ((uint32_t)tid < nt) {
+            float sum = 0.0f;
+            for (int w = 0; w < kRmNorm / 32; w++) sum += s_part[tid][w];
+            s_rms[tid] = 1.0f / sqrtf(sum / (float)cols + a.eps);
+        }
+    }
+    float acc[kRmTT][kRmEE];
+#pragma unroll
+    for (int i = 0; i < kRmTT; i++)
+#pragma unroll
+        for (int j = 0; j < kRmEE; j++) acc[i][j] = 0.0f;
+    for (uint32_t ch = 0; ch < nchunks; ch++) {
+        if (ch + 1 < nchunks)
+            rm_wait<1>();
+        else
+            rm_wait<0>();
+        __syncthreads();
+        float *xs = sx(ch & 1);
+        const float *ws = sw(ch & 1);
+        const uint32_t c0 = ch * kRmKC, cw = min(kRmKC, cols - c0);
+        if (a.norm_w || (blockIdx.x == 0 && (a.xn || a.xq))) {
+            constexpr uint32_t Q = kRmKC / 4;
+            if (a.norm_w) {  // x * rms * w per element, four at a time
+                const float4 *nws = reinterpret_cast<const float4 *>(sn(ch & 1));
+#pragma unroll
+                for (uint32_t i = tid; i < TC * Q; i += NT) {
+                    const uint32_t tt = i / Q, p = i % Q;
+                    if (tt < nt && 4 * p < cw) {
+                        float4 *px = reinterpret_cast<float4 *>(xs + tt * kRmKC) + p;
+                        float4 v = *px;
+                        const float4 w4 = nws[p];
+                        const float rs = s_rms[tt];
+                        v.x = v.x * rs * w4.x;
+                        v.y = v.y * rs * w4.y;
+                        v.z = v.z * rs * w4.z;
+                        v.w = v.w * rs * w4.w;
+                        *px = v;
+                    }
+                }
+                __syncthreads();
+            }
+            if (blockIdx.x == 0 && a.xn)
+#pragma unroll
+                for (uint32_t i = tid; i < TC * kRmKC; i += NT) {
+                    const uint32_t tt = i / kRmKC, cc = i % kRmKC;
+                    if (tt < nt && cc < cw) a.xn[(size_t)(t0 + tt) * cols + c0 + cc] = xs[tt * kRmKC + cc];
+                }
+            if (blockIdx.x == 0 && a.xq)
+                for (uint32_t task = (uint32_t)warp; task < TC * (kRmKC / 32); task += NT / 32) {
+                    const uint32_t tt = task / (kRmKC / 32), b = task % (kRmKC / 32);
+                    if (tt < nt && 32 * b < cw)
+                        qact_store_block(a.xq + (size_t)(t0 + tt) * a.xq_pitch, (int)cols, (int)(c0 / 32 + b),
+                                         xs[tt * kRmKC + 32 * b + lane], lane);
+                }
+        }
+        const float *xw = xs + (size_t)wt * kRmTT * kRmKC + lane;
+        const float *ww = ws + (size_t)we * kRmEE * kRmKC + lane;
+        auto step = [&](uint32_t j) {
+            float xv[kRmTT], wv[kRmEE];
+#pragma unroll
+            for (int i = 0; i < kRmTT; i++) xv[i] = xw[i * kRmKC + 32 * j];
+#pragma unroll
+            for (int e = 0; e < kRmEE; e++) wv[e] = ww[e * kRmKC + 32 * j];
+#pragma unroll
+            for (int i = 0; i < kRmTT; i++)
+#pragma unroll
+                for (int e = 0; e < kRmEE; e++) acc[i][e] = __fadd_rn(acc[i][e], __fmul_rn(wv[e], xv[i]));
+        };
+        if (cw == kRmKC) {
+#pragma unroll
+            for (uint32_t j = 0; j < kRmKC / 32; j++) step(j);
+        } else {
+            for (uint32_t j = 0; j < cw / 32; j++) step(j);
+        }
+        __syncthreads();
+        if (ch + 2 < nchunks) issue(ch + 2);
+    }
+    // combine each (token, expert)'s 32 chains in router_logit's order: lane l
+    // of the 8-vector takes (c_l + c_{l+8}) + (c_{l+16} + c_{l+24}), then
+    // ((-0 + v0) + v1) + ... + v7; the chains pass through shared memory
+    {
+        float *red = msm + (size_t)warp * 32 * 33;
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+#pragma unroll
+            for (int p = 0; p < 32; p++) red[p * 33 + lane] = acc[(32 * half + p) / kRmEE][(32 * half + p) % kRmEE];
+            __syncwarp();
+            const float *rr = red + lane * 33;
+            float sum = -0.0f;
+#pragma unroll
+            for (int l = 0; l < 8; l++) sum = __fadd_rn(sum, __fadd_rn(__fadd_rn(rr[l], rr[l + 8]), __fadd_rn(rr[l + 16], rr[l + 24])));
+            const uint32_t pp = 32u * half + lane, tt = wt * kRmTT + pp / kRmEE, e = e0 + we * kRmEE + pp % kRmEE;
+            if (tt < nt && e < E) a.logits[(size_t)(t0 + tt) * E + e] = sum;
+            __syncwarp();
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&a.counters[blockIdx.y], 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // the tile's tokens: logits and sort keys (even row stride, 16-byte aligned rows), ranks, weights
+    const uint32_t E2 = (E + 3) & ~1u;
+    float *lg = msm;                                                              // [TC][E]
+    uint64_t *keys = reinterpret_cast<uint64_t *>(msm + (((size_t)TC * E + 3) & ~(size_t)3));  // [TC][E2]
+    for (uint32_t i = tid; i < nt * E; i += NT) {
+        const uint32_t tt = i / E, ee = i - tt * E;
+        const float v = __ldcg(a.logits + (size_t)t0 * E + i);
+        lg[i] = v;
+        keys[tt * E2 + ee] = router_key(v, ee);
+    }
+    if ((uint32_t)tid < nt) keys[tid * E2 + E] = 0;
+    __syncthreads();
+    {
+        const uint32_t g = (uint32_t)tid / kRmNorm, ti = (uint32_t)tid % kRmNorm;
+        for (uint32_t base = 0; base < nt; base += NG)
+            if (base + g < nt) router_rank_keys(keys + (base + g) * E2, E, a.k, s_sel[base + g], (int)ti, kRmNorm);
+    }
+    for (uint32_t tt = (uint32_t)warp; tt < nt; tt += NT / 32) {
+        float mx, es;
+        router_softmax_stats(lg + tt * E, E, lane, mx, es);
+        if (lane == 0) {
+            s_mx[tt] = mx;
+            s_es[tt] = es;
+        }
+    }
+    __syncthreads();
+    if ((uint32_t)tid < nt) {
+        const uint32_t tt = tid;
+        float w[16];
+        router_weights(lg + tt * E, s_sel[tt], a.k, s_mx[tt], s_es[tt], a.norm_topk, a.escale, w);
+        for (uint32_t i = 0; i < a.k; i++) {
+            a.ids[(size_t)(t0 + tt) * a.k + i] = s_sel[tt][i];
+            a.wout[(size_t)(t0 + tt) * a.k + i] = w[i];
+        }
+    }
+    if (tid == 0) a.counters[blockIdx.y] = 0;
+}
+
+template <int WT, int WE>
+static cudaError_t launch_router_mm(const LaunchCfg &c, const RouterArgs &a) {
+    using Gm = RmGeo<WT, WE>;
+    const dim3 grid((a.E + Gm::EC - 1) / Gm::EC, (a.ntok + Gm::TC - 1) / Gm::TC);
+    return launch_k(c, "router_topk", k_router_mm<WT, WE>, grid, dim3(Gm::NT), Gm::kSmem, a);
+}
+
+// The register-tiled kernel needs whole 32-column steps and 16-byte aligned rows (cp.async).
+static bool router_mm_ok(const RouterArgs &a) {
+    return a.ntok >= kRtMinTokens && a.cols % 32 == 0 && a.w_ld % 4 == 0 &&
+           (reinterpret_cast<uintptr_t>(a.W) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
+           (!a.norm_w || (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0);
+}
+
 cudaError_t launch_router(const LaunchCfg &c, const float *w, uint32_t E, uint32_t cols, uint32_t w_ld,
                           const float *x, const float *norm_w, float eps, uint32_t ntok, uint32_t k, int norm_topk,
                           const float *escale, uint32_t *ids, float *wout, float *logits, uint32_t *counters,
                           uint8_t *xq, uint64_t xq_pitch, float *xn) {
     RouterArgs a{w,      E,   cols,      w_ld,   x,    norm_w, eps,      ntok, k,
                  norm_topk, escale, ids, wout, logits, counters, xq, xq_pitch, xn};
+    if (router_mm_ok(a)) return ntok >= 2048 ? launch_router_mm<2, 4>(c, a) : launch_router_mm<1, 4>(c, a);
     if (ntok >= kRtMinTokens && cols <= kRtMaxCols) {
         const size_t smem = rt_layout(cols, E).total;
         return launch_k(c, "router_topk", k_router_tok, dim3((ntok + kRtTok - 1) / kRtTok), dim3(kRtWarps * 32), smem,
