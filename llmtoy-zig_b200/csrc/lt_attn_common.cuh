@@ -27,7 +27,7 @@ LT_DEVINL float ab_block_sum(float v, float *red) {
 
 // x[0, n) (f32, shared) -> quantised rows of X (16 warps, 32-blocks).
 LT_DEVINL void ab_quantise(const XS &X, const float *xf, uint32_t n, int warp, int lane) {
-#pragma unroll 4
+#pragma unroll 1
     for (uint32_t b = warp; b < (n + 31) / 32; b += kAbWarps) {
         const uint32_t e = 32 * b + lane;
         qact_block_to_xs(X, 0, (int)b, e < n ? xf[e] : 0.0f, lane);

@@ -108,7 +108,7 @@ __host__ __device__ inline DecodeLayout decode_layout(uint32_t E, uint32_t d, ui
         off += (b + 127) & ~(size_t)127;
         return o;
     };
-    L.bars = take((size_t)(kDecMaxChunks + 17) * 8);
+    L.bars = take((size_t)(kDecMaxChunks + 18) * 8);
     L.misc = take(256);
     L.lg = take((size_t)E * 4);
     L.keys = take((size_t)(E + 2) * 8);
@@ -165,6 +165,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
                       a.gchunks);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
     uint64_t *hbar = bars + kDecMaxChunks + 16;
+    uint64_t *rbar = bars + kDecMaxChunks + 17;  // this CTA's router rows
     uint32_t *s_sel = reinterpret_cast<uint32_t *>(smem + L.misc);    // [16]
     float *s_w = reinterpret_cast<float *>(smem + L.misc + 64);       // [16]
     float *s_ss = reinterpret_cast<float *>(smem + L.misc + 128);     // [4]
@@ -197,20 +198,26 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
 
     DT_MARK(0);
     if (tid < 16) s_sel[tid] = 0;  // ranks form a permutation; this only keeps ids in range regardless
+    // static inputs first: this CTA's router rows (expert c + w*G for warp w,
+    // into the gate/up tile space, free until phase G) and the norm weights
+    const uint32_t e_mine = c + (uint32_t)warp * G;
+    const bool has_e = !a.dense && e_mine < a.E;
+    const uint32_t nlw = a.dense ? 0 : a.E > c ? (a.E - c + G - 1) / G : 0;  // warps with a logit
+    const float *wrow = reinterpret_cast<const float *>(gt) + (size_t)warp * a.d;
     if (tid == 0) {
         for (uint32_t i = 0; i < nchunks; i++) mbar_init(&bars[i], 1);
         for (uint32_t i = 0; i < a.k; i++) mbar_init(&bars[kDecMaxChunks + i], 1);
         mbar_init(hbar, 1);
+        mbar_init(rbar, 1);
         fence_barrier_init();
+        if (nlw) {
+            mbar_arrive_expect_tx(rbar, nlw * a.d * 4);
+            for (uint32_t w = 0; w < nlw; w++)
+                tma_load_1d(gt + (size_t)w * a.d * 4, a.rw + (size_t)(c + w * G) * a.rw_ld, a.d * 4, rbar);
+        }
     }
-    // static inputs first: this CTA's router rows and the norm weights
-    float w0[kRouterChunk];
-    const uint32_t e_mine = c + (uint32_t)warp * G;
-    const bool has_e = !a.dense && e_mine < a.E;
-    router_prefetch(a.rw + (size_t)(has_e ? e_mine : 0) * a.rw_ld, a.d, lane, has_e, w0);
     if (a.norm_w)
         for (uint32_t i = tid; i < a.d; i += kDecThreads) nwsm[i] = __ldg(a.norm_w + i);
-    if (tid < 2 && a.pf[tid]) prefetch_l2_share(a.pf[tid], a.pf_bytes[tid], c, G);
     pdl_launch_dependents();
     pdl_wait();
     DT_MARK(1);
@@ -271,9 +278,10 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     const uint32_t tag = (uint32_t)epoch;
     // warps [0, nlw) compute this CTA's logits; the others quantise the
     // normalised x for this CTA's gate/up meanwhile
-    const uint32_t nlw = a.dense ? 0 : a.E > c ? (a.E - c + G - 1) / G : 0;
     if (has_e) {
-        const float v = router_logit(a.rw + (size_t)e_mine * a.rw_ld, xrouter, a.d, lane, w0);
+        const float v = tile_wait(rbar, a.dev_err) ? router_logit_sm(wrow, xrouter, a.d, lane) : 0.0f;
+        // the row's space takes the gate/up tiles (async proxy) after this read
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         if (lane == 0) st_relaxed_u64(lslots + e_mine, ((uint64_t)tag << 32) | __float_as_uint(v));
         DT_MARK(4);
     } else {
@@ -405,9 +413,11 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     DT_MARK(8);
     __syncthreads();
     DT_MARK(9);
-    // down rows [r0, r1) of each slot's expert, requested once this CTA's
-    // gate/up rows are consumed: until then every CTA's HBM requests are the
-    // gate/up rows, which the grid's slowest CTA (and so the h barrier) waits for
+    // down rows [r0, r1) of each slot's expert and the L2 prefetch of the next
+    // kernel's weights, requested once this CTA's gate/up rows are consumed:
+    // until then every CTA's HBM requests are the gate/up rows, which the
+    // grid's slowest CTA (and so the h barrier) waits for
+    if (tid >= 64 && tid < 66 && a.pf[tid - 64]) prefetch_l2_share(a.pf[tid - 64], a.pf_bytes[tid - 64], c, G);
     if (warp == 1 && !a.late_down && (uint32_t)lane < a.k && nr) {
         const uint32_t e = min(s_sel[lane], a.E - 1);
         const uint32_t bytes = (uint32_t)(nr * a.dpitch);
@@ -565,6 +575,7 @@ bool decode_plan(const DecodeParams &p, int num_sms, DecodePlan &out) {
         a.pf_bytes[i] = p.pf_bytes[i];
     }
     if (p.d % 32 != 0 || p.F % 32 != 0) return false;
+    if (a.rw && ((p.router_ld % 4) != 0 || (reinterpret_cast<uintptr_t>(a.rw) & 15) != 0 || p.E > 2 * G)) return false;
     const uint64_t nunits = (uint64_t)p.k * p.F / kDecUnit;
     a.maxpairs = (uint32_t)(kDecUnit * ((nunits + G - 1) / G));
     a.maxrows = (p.d + G - 1) / G;

@@ -56,6 +56,28 @@ LT_DEVINL float router_logit(const float *wrow, const float *xs, uint32_t cols, 
     return sum;
 }
 
+// The same logit with the router row in shared memory (staged by TMA): a
+// rolled loop, so the code stays small (the persistent kernels run it once
+// per launch, from a cold instruction cache).
+LT_DEVINL float router_logit_sm(const float *wsm, const float *xs, uint32_t cols, int lane) {
+    const uint32_t n32 = cols & ~31u;
+    float acc = 0.0f;
+#pragma unroll 8
+    for (uint32_t j = 0; j < n32 / 32; j++) acc = __fadd_rn(acc, __fmul_rn(wsm[32 * j + lane], xs[32 * j + lane]));
+    uint32_t i = n32;
+    const float a1 = __shfl_sync(0xffffffffu, acc, (lane + 8) & 31);
+    const float a2 = __shfl_sync(0xffffffffu, acc, (lane + 16) & 31);
+    const float a3 = __shfl_sync(0xffffffffu, acc, (lane + 24) & 31);
+    float v = __fadd_rn(__fadd_rn(acc, a1), __fadd_rn(a2, a3));
+    for (; i + 8 <= cols; i += 8)
+        if (lane < 8) v = __fadd_rn(v, __fmul_rn(wsm[i + lane], xs[i + lane]));
+    float sum = -0.0f;
+#pragma unroll
+    for (int l = 0; l < 8; l++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, v, l));
+    for (; i < cols; i++) sum = __fadd_rn(sum, __fmul_rn(wsm[i], xs[i]));
+    return sum;
+}
+
 // Load this lane's first-chunk router weights for expert row wrow.
 LT_DEVINL void router_prefetch(const float *wrow, uint32_t cols, int lane, bool valid, float (&w0)[kRouterChunk]) {
     const uint32_t n32 = cols & ~31u;

@@ -170,26 +170,6 @@ __device__ unsigned long long g_stack_trace[kTraceCtas * kTraceLayers * kTraceMa
     } while (0)
 #endif
 
-// One expert logit in dotf32 order (router_logit's), the weight row in shared memory.
-LT_DEVINL float st_router_logit(const float *wsm, const float *xs, uint32_t cols, int lane) {
-    const uint32_t n32 = cols & ~31u;
-    float acc = 0.0f;
-#pragma unroll 16
-    for (uint32_t j = 0; j < n32 / 32; j++) acc = __fadd_rn(acc, __fmul_rn(wsm[32 * j + lane], xs[32 * j + lane]));
-    uint32_t i = n32;
-    const float a1 = __shfl_sync(0xffffffffu, acc, (lane + 8) & 31);
-    const float a2 = __shfl_sync(0xffffffffu, acc, (lane + 16) & 31);
-    const float a3 = __shfl_sync(0xffffffffu, acc, (lane + 24) & 31);
-    float v = __fadd_rn(__fadd_rn(acc, a1), __fadd_rn(a2, a3));
-    for (; i + 8 <= cols; i += 8)
-        if (lane < 8) v = __fadd_rn(v, __fmul_rn(wsm[i + lane], xs[i + lane]));
-    float sum = -0.0f;
-#pragma unroll
-    for (int l = 0; l < 8; l++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, v, l));
-    for (; i < cols; i++) sum = __fadd_rn(sum, __fmul_rn(wsm[i], xs[i]));
-    return sum;
-}
-
 // ── grid hand-off ───────────────────────────────────────────────────────────
 // One counter that only grows: every CTA adds 1 per hand-off, so hand-off n
 // (counted over all launches of the plan, from 1) completes at n * G.  The
@@ -653,7 +633,7 @@ __global__ void __launch_bounds__(kStThreads, 1) k_stack(const __grid_constant__
             const XS Xx = xs_carve(XSr, 1, (int)st_items(d));
             if (has_e && warp == 0) {
                 st_wait(brt, par, a.dev_err);
-                const float v = st_router_logit(RT, XF, d, lane);
+                const float v = router_logit_sm(RT, XF, d, lane);
                 if (lane == 0) st_relaxed_u64(lslots + c, ((uint64_t)tag << 32) | __float_as_uint(v));
             } else {
                 const uint32_t w0 = has_e ? 1 : 0;
