@@ -345,10 +345,124 @@ __global__ void __launch_bounds__(kQsWarps * 32, 1) k_qmv_stream64(QsArgs q) {
     }
 }
 
+// Wide rows (64-column chunks >= 32, e.g. a 2048-column lm_head; Q8_0):
+// lane l owns chunks l, l + 32, ... with the activation chunk in registers
+// (loaded once when the row is exactly 32 chunks), so only weight bytes are
+// read from shared memory per row; a group's <= 8 row partials are summed
+// across the warp by a transpose reduction (three halving exchanges, then two
+// butterfly steps: lane l ends with row ((l>>4)&1)*4 + ((l>>3)&1)*2 + ((l>>2)&1)).
+constexpr uint32_t kQsWideRows = 8;
+
+LT_DEVINL float qs_transpose_sum(float (&v)[kQsWideRows], int lane) {
+    const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const float send = b4 ? v[j] : v[j + 4], keep = b4 ? v[j + 4] : v[j];
+        v[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const float send = b3 ? v[j] : v[j + 2], keep = b3 ? v[j + 2] : v[j];
+        v[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    {
+        const float send = b2 ? v[0] : v[1], keep = b2 ? v[1] : v[0];
+        v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
+    v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+    return v[0];
+}
+
+template <uint32_t TYPE>
+__global__ void __launch_bounds__(kQsWarps * 32, 1) k_qmv_stream_w(QsArgs q) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const QmvArgs &a = q.a;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t cpr = qs_chunks(a.cols), npass = (cpr + 31) / 32;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kQsBars) + warp * kQsMaxStages;
+    const XS X = xs_carve(smem + kQsX, 1, (int)a.nitems);
+    uint8_t *ring = smem + qs_ring_offset((int)a.nitems) + (size_t)warp * q.stages * q.stage;
+    const uint32_t W = gridDim.x * q.warps, gw = blockIdx.x * q.warps + warp;
+    const uint32_t ngroups = (a.nrows + a.rw - 1) / a.rw;
+    const uint32_t mine = (uint32_t)warp < q.warps && gw < ngroups ? (ngroups - gw + W - 1) / W : 0;
+    auto issue = [&](uint32_t i) {
+        const uint32_t r0 = (gw + i * W) * a.rw, nr = min(a.rw, a.nrows - r0), st = i % q.stages;
+        mbar_arrive_expect_tx(&bars[st], (uint32_t)(nr * a.pitch));
+        tma_load_1d(ring + (size_t)st * q.stage, a.rows + (uint64_t)r0 * a.pitch, (uint32_t)(nr * a.pitch), &bars[st]);
+    };
+    if (lane == 0) {  // weights are static: the first stages before waiting on the producer
+        for (uint32_t st = 0; st < q.stages; st++) mbar_init(&bars[st], 1);
+        fence_barrier_init();
+        for (uint32_t i = 0; i < min(mine, q.stages); i++) issue(i);
+    }
+    __syncwarp();
+    pdl_launch_dependents();
+    pdl_wait();
+    if (a.xq) {
+        const uint8_t **src = reinterpret_cast<const uint8_t **>(smem + kQsSrc);
+        if (threadIdx.x == 0) src[0] = a.xq;
+        __syncthreads();
+        qact_to_smem(X, src, 1, (int)a.cols);
+    } else {
+        for (uint32_t b = warp; b < a.cols / 32; b += kQsWarps)
+            qact_block_to_xs(X, 0, (int)b, __ldcg(a.xf + 32 * b + lane), lane);
+    }
+    __syncthreads();
+    XChunk xc;
+    if (npass == 1) xchunk_load(X, 0, (int)spread_chunk((uint32_t)lane, 32), xc);
+    const int row_l = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+    uint32_t i = 0;
+    bool ok = true;
+    for (; i < mine; i++) {
+        const uint32_t st = i % q.stages;
+        if (!mbar_wait_bounded(&bars[st], (i / q.stages) & 1, kWaitLimitNs)) {
+            ok = false;
+            break;
+        }
+        const uint32_t r0 = (gw + i * W) * a.rw, nr = min(a.rw, a.nrows - r0);
+        const uint8_t *t = ring + (size_t)st * q.stage;
+        float v[kQsWideRows];
+#pragma unroll
+        for (int r = 0; r < (int)kQsWideRows; r++) v[r] = 0.0f;
+        for (uint32_t p = 0; p < npass; p++) {
+            const uint32_t n = min(32u, cpr - 32 * p);
+            if ((uint32_t)lane < n) {
+                const uint32_t cb = 32 * p + spread_chunk((uint32_t)lane, n);
+                if (npass > 1) xchunk_load(X, 0, (int)cb, xc);
+#pragma unroll
+                for (int r = 0; r < (int)kQsWideRows; r++)
+                    if ((uint32_t)r < nr) v[r] += dot64<TYPE>(t + (size_t)r * a.pitch, (int)cb, (int)a.nblocks, xc);
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && i + q.stages < mine) {  // the stage is read: the group after next takes it
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(i + q.stages);
+        }
+        const float sum = qs_transpose_sum(v, lane);
+        if ((lane & 3) == 0 && (uint32_t)row_l < nr) {
+            const size_t yi = r0 + row_l;
+            a.y[yi] = a.add ? __fadd_rn(a.add[yi], sum) : sum;
+        }
+    }
+    if (!ok && lane == 0) {
+        if (a.dev_err) atomicExch(a.dev_err, DEV_ERR_TMA_TIMEOUT);
+        for (uint32_t j = i; j < min(mine, i + q.stages); j++)
+            mbar_wait_bounded(&bars[j % q.stages], (j / q.stages) & 1, kWaitLimitNs);
+    }
+}
+
 // Measured on the lm_heads: Q8_0 rows (d 896) run faster with register-held
 // chunks (33 vs 37 us for 145 MB); Q6_K rows (d 2048, 2816) slower (86 vs 80,
 // 265 vs 222 us), so the K types keep one item per lane.
 static bool qs64_type(uint32_t t) { return t == T_Q8_0; }
+// Q8_0 rows of 32+ chunks: the wide-row kernel (measured on a 151936 x 2048
+// matrix: 54 us against 60 for k_qmv_stream64).  For Q6_K it measured no
+// faster at 2048 columns (70 vs 72 us) and slower at 2816 (242 vs 212 us: the
+// second pass over 12 of 44 chunks idles 20 lanes), so the K types keep one
+// superblock per lane.
+static bool qsw_type(const DevMat &m) { return m.type == T_Q8_0 && qs_chunks(m.cols) >= 32; }
 
 // The ring layout for a one-token matvec over m, or false when the persistent
 // kernel does not pay (few rows) or two stages per warp do not fit.
@@ -358,7 +472,8 @@ static bool qs_plan(const DevMat &m, uint32_t rw, uint32_t ipr, int num_sms, uin
     if (m.rows * m.pitch < ((uint64_t)32 << 20) || qmv_ctas(m) <= 4u * (uint32_t)num_sms) return false;
     stage = (uint32_t)((rw * m.pitch + 127) & ~(uint64_t)127);
     size_t fixed = qs_ring_offset((int)ipr) + 256;  // + slack: a Q8_0 chunk reads past its row
-    if (qs64_type(m.type)) fixed += kQsWarps * (((size_t)rw * qs_chunks((uint32_t)m.cols) * 4 + 127) & ~(size_t)127);
+    if (qs64_type(m.type) && !qsw_type(m))
+        fixed += kQsWarps * (((size_t)rw * qs_chunks((uint32_t)m.cols) * 4 + 127) & ~(size_t)127);
     for (warps = kQsWarps; warps >= 8; warps -= 4) {  // at least two stages per warp
         if (fixed + (size_t)2 * warps * stage > kDecodeSmemLimit) continue;
         stages = (uint32_t)min((size_t)kQsMaxStages, (kDecodeSmemLimit - fixed) / ((size_t)warps * stage));
@@ -371,6 +486,10 @@ static bool qs_plan(const DevMat &m, uint32_t rw, uint32_t ipr, int num_sms, uin
 // Rows per group: one item per lane (k_qmv_stream), or about 6 KB of rows
 // (k_qmv_stream64, at most 8).
 static uint32_t qs_rows(const DevMat &m, uint32_t ipr) {
+    if (qsw_type(m)) {  // about 7 KB of rows per group, at most kQsWideRows
+        const uint64_t r = 7168 / m.pitch;
+        return r < 1 ? 1u : r > kQsWideRows ? kQsWideRows : (uint32_t)r;
+    }
     if (!qs64_type(m.type)) return max(1u, 32u / ipr);
     const uint64_t r = 6144 / m.pitch;
     return r < 1 ? 1u : r > 8 ? 8u : (uint32_t)r;
@@ -385,7 +504,11 @@ bool qmv_streams(const DevMat &m, uint32_t ntok, int num_sms) {
 }
 
 template <uint32_t TYPE>
-static cudaError_t launch_qs_t(const LaunchCfg &c, const QsArgs &q, size_t smem) {
+static cudaError_t launch_qs_t(const LaunchCfg &c, const QsArgs &q, size_t smem, bool wide) {
+    if constexpr (TYPE == T_Q8_0)
+        if (wide)
+            return launch_k(c, type_label<TYPE>("qmv_stream"), k_qmv_stream_w<TYPE>, dim3((unsigned)c.num_sms),
+                            dim3(kQsWarps * 32), smem, q);
     if constexpr (TYPE == T_Q8_0)
         return launch_k(c, type_label<TYPE>("qmv_stream"), k_qmv_stream64<TYPE>, dim3((unsigned)c.num_sms),
                         dim3(kQsWarps * 32), smem, q);
@@ -396,19 +519,20 @@ static cudaError_t launch_qs_t(const LaunchCfg &c, const QsArgs &q, size_t smem)
 
 static cudaError_t launch_qmv_stream(const LaunchCfg &c, const DevMat &m, QmvArgs a) {
     QsArgs q;
+    const bool wide = qsw_type(m);
     a.rw = qs_rows(m, a.nitems);
     q.a = a;
     size_t smem;
     if (!qs_plan(m, a.rw, a.nitems, c.num_sms, q.stages, q.stage, q.warps, smem)) return cudaErrorInvalidValue;
     switch (m.type) {
-    case T_Q4_K: return launch_qs_t<T_Q4_K>(c, q, smem);
-    case T_Q6_K: return launch_qs_t<T_Q6_K>(c, q, smem);
-    case T_Q8_0: return launch_qs_t<T_Q8_0>(c, q, smem);
-    case T_Q5_0: return launch_qs_t<T_Q5_0>(c, q, smem);
-    case T_Q5_1: return launch_qs_t<T_Q5_1>(c, q, smem);
-    case T_IQ4_NL: return launch_qs_t<T_IQ4_NL>(c, q, smem);
-    case T_Q5_K: return launch_qs_t<T_Q5_K>(c, q, smem);
-    case T_Q3_K: return launch_qs_t<T_Q3_K>(c, q, smem);
+    case T_Q4_K: return launch_qs_t<T_Q4_K>(c, q, smem, wide);
+    case T_Q6_K: return launch_qs_t<T_Q6_K>(c, q, smem, wide);
+    case T_Q8_0: return launch_qs_t<T_Q8_0>(c, q, smem, wide);
+    case T_Q5_0: return launch_qs_t<T_Q5_0>(c, q, smem, wide);
+    case T_Q5_1: return launch_qs_t<T_Q5_1>(c, q, smem, wide);
+    case T_IQ4_NL: return launch_qs_t<T_IQ4_NL>(c, q, smem, wide);
+    case T_Q5_K: return launch_qs_t<T_Q5_K>(c, q, smem, wide);
+    case T_Q3_K: return launch_qs_t<T_Q3_K>(c, q, smem, wide);
     default: return cudaErrorInvalidValue;
     }
 }
