@@ -141,11 +141,12 @@ def test_qmatvec_reference_fuzz(ctx, oracle, ggml_type, rows, cols):
 
 
 @pytest.mark.parametrize("ggml_type,rows,cols", [(14, 40000, 2816), (12, 60000, 2048), (8, 50001, 896),
-                                                 (13, 40000, 2048)])
+                                                 (13, 40000, 2048), (8, 40001, 2048), (8, 20000, 4096)])
 def test_qmatvec_streaming_lm_head(ctx, oracle, ggml_type, rows, cols):
     """One token over an lm_head-sized matrix runs as the persistent streaming
-    kernel (per-warp TMA rings): against the oracle, and against the
-    multi-token kernel on the same row."""
+    kernel (per-warp TMA rings; Q8_0 rows of 2048+ columns through the
+    wide-row variant with a transpose reduction): against the oracle, and
+    against the multi-token kernel on the same row."""
     import importlib
     synth = importlib.import_module("llmtoy-zig_b200.synth")
     rng = np.random.Generator(np.random.PCG64(rows + cols + ggml_type))
