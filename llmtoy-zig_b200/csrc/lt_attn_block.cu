@@ -275,10 +275,8 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
         for (uint32_t i = tid; i < a.d; i += kAbThreads) ss += xf[i] * xf[i];
         ss = ab_block_sum(ss, red);
         const float rms_inv = 1.0f / sqrtf(ss / (float)a.d + a.eps);
-        for (uint32_t i = tid; i < a.d; i += kAbThreads) xf[i] = xf[i] * rms_inv * nw[i];
+        ab_quantise_norm(Xx, xf, a.d, rms_inv, nw, warp, lane);  // the rows need only the quantised x
     }
-    __syncthreads();
-    ab_quantise(Xx, xf, a.d, warp, lane);
     __syncthreads();
     AT_MARK(3);
     const uint64_t epoch = *s_epoch;

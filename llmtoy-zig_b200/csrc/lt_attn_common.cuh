@@ -34,6 +34,17 @@ LT_DEVINL void ab_quantise(const XS &X, const float *xf, uint32_t n, int warp, i
     }
 }
 
+// The same from x before the RMSNorm: quantises x[e] * rms_inv * w[e] (the
+// normalised value the norm loop would have stored, with the same rounding).
+LT_DEVINL void ab_quantise_norm(const XS &X, const float *xf, uint32_t n, float rms_inv, const float *w, int warp,
+                                int lane) {
+#pragma unroll 1
+    for (uint32_t b = warp; b < (n + 31) / 32; b += kAbWarps) {
+        const uint32_t e = 32 * b + lane;
+        qact_block_to_xs(X, 0, (int)b, e < n ? xf[e] * rms_inv * w[e] : 0.0f, lane);
+    }
+}
+
 // n f32 values from global (written by other CTAs of this launch) into
 // shared memory, float4 at a time with every load issued before any store.
 LT_DEVINL void ab_load(float *dst, const float *src, uint32_t n) {

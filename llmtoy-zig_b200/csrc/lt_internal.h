@@ -243,7 +243,7 @@ struct DecodeParams {
     const uint8_t *pf[2] = {nullptr, nullptr};
     uint64_t pf_bytes[2] = {0, 0};
 };
-constexpr size_t kDecodeSyncBytes = 4096;
+constexpr size_t kDecodeSyncBytes = 36864;
 
 // Grouped expert GEMM on the tensor cores (lt_moe_gemm.cu) for multi-token
 // batches with Q4_K gate/up/down (K <= 2048).  x: [T][d] expert input (already

@@ -51,7 +51,12 @@ constexpr int kDecNormThreads = 128;  // RMSNorm reduction width of the router k
 // Layout of the context's sync block (DecodeParams::sync).
 constexpr size_t kSyncEpoch = 0;   // u64 counter: epoch arrivals
 constexpr size_t kSyncB = 8;       // u64 counter: barrier after h
-constexpr size_t kSyncLogits = 256;  // u64 [kRouterMaxE]: tagged logits
+constexpr size_t kSyncLogits = 256;  // tagged logits, one 128-byte line each (u64 [kRouterMaxE][16])
+// Every CTA polls every logit: with the words packed into a few lines, the
+// 148 x E polls queue at a few L2 slices (measured: the exchange ended up to
+// 3 us after the last logit was stored); one line per logit spreads them.
+constexpr size_t kSyncLogitStride = 16;
+static_assert(kSyncLogits + 8 * kSyncLogitStride * kRouterMaxE <= kDecodeSyncBytes, "decode sync block");
 
 struct DecodeArgs {
     // router
@@ -282,18 +287,18 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
         const float v = tile_wait(rbar, a.dev_err) ? router_logit_sm(wrow, xrouter, a.d, lane) : 0.0f;
         // the row's space takes the gate/up tiles (async proxy) after this read
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        if (lane == 0) st_relaxed_u64(lslots + e_mine, ((uint64_t)tag << 32) | __float_as_uint(v));
+        if (lane == 0) st_relaxed_u64(lslots + kSyncLogitStride * e_mine, ((uint64_t)tag << 32) | __float_as_uint(v));
         DT_MARK(4);
     } else {
         for (uint32_t b = warp - nlw; b < a.d / 32; b += kDecWarps - nlw)
             qact_block_to_xs(Xx, 0, (int)b, xsm[32 * b + lane], lane);
     }
     if (!a.dense && tid < a.E) {  // poll this expert's logit until it carries this launch's tag
-        uint64_t v = ld_relaxed_u64(lslots + tid);
+        uint64_t v = ld_relaxed_u64(lslots + kSyncLogitStride * tid);
         if ((uint32_t)(v >> 32) != tag) {
             const uint64_t t0 = globaltimer_ns();
             for (;;) {
-                v = ld_relaxed_u64(lslots + tid);
+                v = ld_relaxed_u64(lslots + kSyncLogitStride * tid);
                 if ((uint32_t)(v >> 32) == tag) break;
                 if (globaltimer_ns() - t0 > kWaitLimitNs) {
                     if (a.dev_err) atomicExch(a.dev_err, DEV_ERR_GRID_TIMEOUT);
