@@ -26,7 +26,10 @@
 namespace lt {
 
 // Layout of the context's attention sync block.
-constexpr size_t kAbEpoch = 0, kAbB1 = 8, kAbB2 = 16, kAbB3 = 24, kAbHeadCnt = 256;
+constexpr size_t kAbEpoch = 0, kAbHeadCnt = 256;
+// the three hand-offs' split counters (kGridSplitBytes each) after the head counters
+constexpr size_t kAbB1 = 256 + 4 * 1024, kAbB2 = kAbB1 + kGridSplitBytes, kAbB3 = kAbB2 + kGridSplitBytes;
+static_assert(kAbB3 + kGridSplitBytes <= kAttnSyncBytes, "attention sync block");
 constexpr uint32_t kAbMaxSplits = 8;  // splits of a head's positions (one CTA each)
 constexpr uint32_t kAbSplitPositions = 256;  // positions per split before another CTA joins
 
@@ -256,7 +259,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     if (GEN && a.tail_f) ab_tail_weights(a, tw);
     // the third hand-off (post-norm only) counts every launch: without it, CTA 0
     // adds the whole grid's arrivals at once, off the critical path
-    if (!a.post_norm && c == 0 && tid == 0) atomicAdd(ctr3, (unsigned long long)G);
+    if (!a.post_norm && c == 0 && tid == 0) grid_arrive_split_all(ctr3, G);
     for (uint32_t i = tid; i < a.d; i += kAbThreads) nw[i] = __ldg(a.norm_w + i);
     pdl_launch_dependents();
     pdl_wait();
@@ -298,8 +301,8 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     AT_MARK(4);
     for (uint32_t r = tid; r < nqr; r += kAbThreads)
         a.qkv[q0 + r] = a.bias ? __fadd_rn(yq[r], a.bias[q0 + r]) : yq[r];
-    grid_arrive(ctr1);
-    grid_wait(ctr1, epoch, a.dev_err, kWaitLimitNs);
+    grid_arrive_split(ctr1);
+    grid_wait_split(ctr1, epoch, a.dev_err, kWaitLimitNs);
     AT_MARK(5);
 
     // ── phase A ──────────────────────────────────────────────────────────────
@@ -442,8 +445,8 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
         __syncthreads();
     }
     AT_MARK(10);
-    grid_arrive(ctr2);
-    grid_wait(ctr2, epoch, a.dev_err, kWaitLimitNs);
+    grid_arrive_split(ctr2);
+    grid_wait_split(ctr2, epoch, a.dev_err, kWaitLimitNs);
     AT_MARK(11);
 
     // ── phase O ──────────────────────────────────────────────────────────────
@@ -459,8 +462,8 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
         for (uint32_t r = tid; r < nor; r += kAbThreads) ss = __fadd_rn(ss, __fmul_rn(yo[r], yo[r]));
         ss = ab_block_sum(ss, red);
         if (tid == 0) a.ss_part[c] = ss;
-        grid_arrive(ctr3);
-        grid_wait(ctr3, epoch, a.dev_err, kWaitLimitNs);
+        grid_arrive_split(ctr3);
+        grid_wait_split(ctr3, epoch, a.dev_err, kWaitLimitNs);
         float t = 0.0f;
         for (uint32_t i = tid; i < G; i += kAbThreads) t = __fadd_rn(t, __ldcg(a.ss_part + i));
         t = ab_block_sum(t, red);

@@ -297,6 +297,53 @@ LT_DEVINL void grid_wait(const unsigned long long *ctr, uint64_t target, int *de
     __syncthreads();  // passes thread 0's acquire on to the block
 }
 
+// The same hand-off over kGridSplit counters, one 128-byte line each: CTA c
+// arrives on counter c % kGridSplit (fewer atomics queued at one L2 slice),
+// lanes 0..kGridSplit-1 of warp 0 poll one counter each and the hand-off
+// completes when their sum reaches the target.  Every counter only grows and
+// receives the same arrivals each launch, so a sum at the target means every
+// counter is at its own.
+constexpr uint32_t kGridSplit = 8;
+constexpr size_t kGridSplitStride = 16;  // u64 units
+constexpr size_t kGridSplitBytes = 8 * kGridSplitStride * kGridSplit;
+
+LT_DEVINL void grid_arrive_split(unsigned long long *ctr) {
+    __syncthreads();
+    if (threadIdx.x == 0) red_release_add_u64(ctr + kGridSplitStride * (blockIdx.x % kGridSplit), 1ull);
+}
+
+// Arrivals of every CTA of a G-CTA grid at once (by one thread), so that a
+// hand-off this launch skips keeps its counters in step.
+LT_DEVINL void grid_arrive_split_all(unsigned long long *ctr, uint32_t G) {
+    for (uint32_t j = 0; j < kGridSplit; j++)
+        atomicAdd(ctr + kGridSplitStride * j, (unsigned long long)((G + kGridSplit - 1 - j) / kGridSplit));
+}
+
+LT_DEVINL void grid_wait_split(const unsigned long long *ctr, uint64_t target, int *dev_err, uint64_t limit_ns) {
+    if (threadIdx.x < 32) {
+        const uint32_t lane = threadIdx.x;
+        const unsigned long long *p = ctr + kGridSplitStride * (lane % kGridSplit);
+        auto total = [&]() {
+            uint64_t v = lane < kGridSplit ? ld_acquire_u64(p) : 0ull;
+#pragma unroll
+            for (int o = kGridSplit / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            return __shfl_sync(0xffffffffu, v, 0);
+        };
+        if (total() < target) {
+            const uint64_t t0 = __shfl_sync(0xffffffffu, globaltimer_ns(), 0);
+            for (;;) {
+                if (total() >= target) break;
+                // lane 0's clock decides, so the warp leaves the loop together
+                if (__shfl_sync(0xffffffffu, globaltimer_ns() - t0 > limit_ns ? 1 : 0, 0)) {
+                    if (lane == 0 && dev_err) atomicExch(dev_err, DEV_ERR_GRID_TIMEOUT);
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();  // passes the pollers' acquire on to the block
+}
+
 // Fire-and-forget prefetch of [p, p + bytes) into L2 (16-byte aligned, bytes a multiple of 16).
 LT_DEVINL void prefetch_l2(const void *p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");

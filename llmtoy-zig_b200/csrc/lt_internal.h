@@ -155,7 +155,7 @@ struct AttnBlockParams {
     const uint8_t *pf[2];  // optional L2 prefetch ranges (the next kernel's weights)
     uint64_t pf_bytes[2];
 };
-constexpr size_t kAttnSyncBytes = 256 + 4 * 1024;  // counters, then one merge counter per head (<= 1024)
+constexpr size_t kAttnSyncBytes = 8192;  // counters, one merge counter per head (<= 1024), hand-off counters
 // Whether the persistent kernel takes this shape (and fits in shared memory);
 // its global scratch in floats.
 bool attn_block_plan(const AttnBlockParams &p, int num_sms, size_t *scratch_floats);

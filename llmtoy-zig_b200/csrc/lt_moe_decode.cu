@@ -50,13 +50,14 @@ constexpr int kDecNormThreads = 128;  // RMSNorm reduction width of the router k
 
 // Layout of the context's sync block (DecodeParams::sync).
 constexpr size_t kSyncEpoch = 0;   // u64 counter: epoch arrivals
-constexpr size_t kSyncB = 8;       // u64 counter: barrier after h
+constexpr size_t kSyncB = 33024;   // split counters (kGridSplitBytes): the hand-off after h, after the logits
 constexpr size_t kSyncLogits = 256;  // tagged logits, one 128-byte line each (u64 [kRouterMaxE][16])
 // Every CTA polls every logit: with the words packed into a few lines, the
 // 148 x E polls queue at a few L2 slices (measured: the exchange ended up to
 // 3 us after the last logit was stored); one line per logit spreads them.
 constexpr size_t kSyncLogitStride = 16;
-static_assert(kSyncLogits + 8 * kSyncLogitStride * kRouterMaxE <= kDecodeSyncBytes, "decode sync block");
+static_assert(kSyncLogits + 8 * kSyncLogitStride * kRouterMaxE <= kSyncB && kSyncB + kGridSplitBytes <= kDecodeSyncBytes,
+              "decode sync block");
 
 struct DecodeArgs {
     // router
@@ -455,8 +456,8 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     // the slot images land (by TMA) where x and the norm weights were
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     DT_MARK(11);
-    grid_arrive(ctr_b);
-    grid_wait(ctr_b, epoch, a.dev_err, kWaitLimitNs);
+    grid_arrive_split(ctr_b);
+    grid_wait_split(ctr_b, epoch, a.dev_err, kWaitLimitNs);
     DT_MARK(12);
 
     // ── phase D ──────────────────────────────────────────────────────────────
