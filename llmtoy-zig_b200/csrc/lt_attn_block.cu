@@ -228,6 +228,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     if (tid == 0) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
+        mbar_init(&bars[2], 1);  // the norm weights
         fence_barrier_init();
         if (nqr && !GEN) {
             mbar_arrive_expect_tx(&bars[0], (uint32_t)(nqr * a.seg_pitch[0]));
@@ -260,7 +261,15 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     // the third hand-off (post-norm only) counts every launch: without it, CTA 0
     // adds the whole grid's arrivals at once, off the critical path
     if (!a.post_norm && c == 0 && tid == 0) grid_arrive_split_all(ctr3, G);
-    for (uint32_t i = tid; i < a.d; i += kAbThreads) nw[i] = __ldg(a.norm_w + i);
+    // the norm weights by TMA as well: a load loop here would hold every thread
+    // until its loads return before it reaches the wait for the producer
+    const bool nw_tma = (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0;
+    if (nw_tma && tid == 0) {
+        mbar_arrive_expect_tx(&bars[2], a.d * 4);
+        tma_load_1d(nw, a.norm_w, a.d * 4, &bars[2]);
+    } else if (!nw_tma) {
+        for (uint32_t i = tid; i < a.d; i += kAbThreads) nw[i] = __ldg(a.norm_w + i);
+    }
     pdl_launch_dependents();
     pdl_wait();
     AT_MARK(1);
@@ -278,6 +287,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
         for (uint32_t i = tid; i < a.d; i += kAbThreads) ss += xf[i] * xf[i];
         ss = ab_block_sum(ss, red);
         const float rms_inv = 1.0f / sqrtf(ss / (float)a.d + a.eps);
+        if (nw_tma) tile_wait(&bars[2], a.dev_err);
         ab_quantise_norm(Xx, xf, a.d, rms_inv, nw, warp, lane);  // the rows need only the quantised x
     }
     __syncthreads();

@@ -114,7 +114,7 @@ __host__ __device__ inline DecodeLayout decode_layout(uint32_t E, uint32_t d, ui
         off += (b + 127) & ~(size_t)127;
         return o;
     };
-    L.bars = take((size_t)(kDecMaxChunks + 18) * 8);
+    L.bars = take((size_t)(kDecMaxChunks + 19) * 8);
     L.misc = take(256);
     L.lg = take((size_t)E * 4);
     L.keys = take((size_t)(E + 2) * 8);
@@ -172,6 +172,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);
     uint64_t *hbar = bars + kDecMaxChunks + 16;
     uint64_t *rbar = bars + kDecMaxChunks + 17;  // this CTA's router rows
+    uint64_t *nbar = bars + kDecMaxChunks + 18;  // the norm weights
     uint32_t *s_sel = reinterpret_cast<uint32_t *>(smem + L.misc);    // [16]
     float *s_w = reinterpret_cast<float *>(smem + L.misc + 64);       // [16]
     float *s_ss = reinterpret_cast<float *>(smem + L.misc + 128);     // [4]
@@ -215,6 +216,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
         for (uint32_t i = 0; i < a.k; i++) mbar_init(&bars[kDecMaxChunks + i], 1);
         mbar_init(hbar, 1);
         mbar_init(rbar, 1);
+        mbar_init(nbar, 1);
         fence_barrier_init();
         if (nlw) {
             mbar_arrive_expect_tx(rbar, nlw * a.d * 4);
@@ -222,8 +224,15 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
                 tma_load_1d(gt + (size_t)w * a.d * 4, a.rw + (size_t)(c + w * G) * a.rw_ld, a.d * 4, rbar);
         }
     }
-    if (a.norm_w)
+    // the norm weights by TMA as well: a load loop here would hold every thread
+    // until its loads return before it reaches the wait for the producer
+    const bool nw_tma = a.norm_w && (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0;
+    if (nw_tma && tid == 0) {
+        mbar_arrive_expect_tx(nbar, a.d * 4);
+        tma_load_1d(nwsm, a.norm_w, a.d * 4, nbar);
+    } else if (a.norm_w && !nw_tma) {
         for (uint32_t i = tid; i < a.d; i += kDecThreads) nwsm[i] = __ldg(a.norm_w + i);
+    }
     pdl_launch_dependents();
     pdl_wait();
     DT_MARK(1);
@@ -241,6 +250,7 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     }
     __syncthreads();
     DT_MARK(2);
+    if (nw_tma) tile_wait(nbar, a.dev_err);
     for (uint32_t r = tid; r < nr; r += kDecThreads) s_xres[r] = xsm[r0 + r];
     const float *xrouter = xsm;  // the router's input
     if (a.norm_w && a.router_scale) {  // norm_pair: one rms_inv, per-thread sums over 512 strided values
