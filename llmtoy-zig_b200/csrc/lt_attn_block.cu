@@ -20,7 +20,7 @@
 //
 // The weights are static, so both tiles (this CTA's Q/K/V rows and wo rows)
 // stream in while the previous kernel finishes; an optional L2 prefetch
-// range (the next kernel's weights) is issued at the same time.
+// range (the next kernel's weights) is issued once the Q/K/V rows are done.
 #include "lt_attn_common.cuh"
 
 namespace lt {
@@ -255,7 +255,6 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
             tma_load_1d(wo, a.wo + (uint64_t)o0 * a.opitch, (uint32_t)(nor * a.opitch), &bars[1]);
         }
     }
-    if (tid < 2 && a.pf[tid]) prefetch_l2_share(a.pf[tid], a.pf_bytes[tid], c, G);
     AbTailW tw;
     if (GEN && a.tail_f) ab_tail_weights(a, tw);
     // the third hand-off (post-norm only) counts every launch: without it, CTA 0
@@ -309,6 +308,10 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     }
     __syncthreads();
     AT_MARK(4);
+    // the L2 prefetch of the next kernel's weights, once this CTA's weight
+    // tiles have landed (issued at the start, it queued behind them in the
+    // copy engine and held threads 0 and 1 back from the wait for the producer)
+    if (tid < 2 && a.pf[tid]) prefetch_l2_share(a.pf[tid], a.pf_bytes[tid], c, G);
     for (uint32_t r = tid; r < nqr; r += kAbThreads)
         a.qkv[q0 + r] = a.bias ? __fadd_rn(yq[r], a.bias[q0 + r]) : yq[r];
     grid_arrive_split(ctr1);
