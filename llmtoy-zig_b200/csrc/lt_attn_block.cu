@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(kAbThreads, 1) k_attn_block(AttnBlockArgs a) {
     const uint64_t epoch = *s_epoch;
     float *yq = xf;  // the normalised x is quantised already
     if constexpr (!GEN) {
-        if (nqr && tile_wait(&bars[0], a.dev_err)) ab_rows<QT>(wq, a.seg_pitch[0], nqr, a.d, a.qnb, Xx, warp, lane, yq);
+        if (nqr && tile_wait(&bars[0], a.dev_err)) ab_rows_fit<QT>(wq, a.seg_pitch[0], nqr, a.d, a.qnb, Xx, warp, lane, yq);
     } else if (nqr && tile_wait(&bars[0], a.dev_err)) {
         uint32_t off = 0;
         for (uint32_t sg = 0; sg < a.nseg; sg++) {

@@ -125,17 +125,33 @@ LT_DEVINL void ab_rows(const uint8_t *tile, uint64_t pitch, uint32_t nrows, uint
     }
 }
 
-// ab_rows for a tile of type T, or (T == 0) of the run-time type `type`.
+// ab_rows with as few rows per warp as fill the 16 warps (a warp's rows share
+// its activation chunk loads but run on one warp; every row's sum order is the
+// same for any split).
+template <uint32_t T>
+LT_DEVINL void ab_rows_fit(const uint8_t *tile, uint64_t pitch, uint32_t nrows, uint32_t cols, uint32_t nb,
+                           const XS &X, int warp, int lane, float *y) {
+    if (nrows <= (uint32_t)kAbWarps)
+        ab_rows<T, 1>(tile, pitch, nrows, cols, nb, X, warp, lane, y);
+    else if (nrows <= 2u * kAbWarps)
+        ab_rows<T, 2>(tile, pitch, nrows, cols, nb, X, warp, lane, y);
+    else if (nrows <= 3u * kAbWarps)
+        ab_rows<T, 3>(tile, pitch, nrows, cols, nb, X, warp, lane, y);
+    else
+        ab_rows<T, 4>(tile, pitch, nrows, cols, nb, X, warp, lane, y);
+}
+
+// ab_rows_fit for a tile of type T, or (T == 0) of the run-time type `type`.
 template <uint32_t T>
 LT_DEVINL void ab_rows_any(uint32_t type, const uint8_t *tile, uint64_t pitch, uint32_t nrows, uint32_t cols,
                            uint32_t nb, const XS &X, int warp, int lane, float *y) {
     if constexpr (T != 0) {
-        ab_rows<T>(tile, pitch, nrows, cols, nb, X, warp, lane, y);
+        ab_rows_fit<T>(tile, pitch, nrows, cols, nb, X, warp, lane, y);
     } else {
         switch (type) {
-        case T_Q8_0: ab_rows<T_Q8_0>(tile, pitch, nrows, cols, nb, X, warp, lane, y); break;
-        case T_Q4_K: ab_rows<T_Q4_K>(tile, pitch, nrows, cols, nb, X, warp, lane, y); break;
-        case T_Q6_K: ab_rows<T_Q6_K>(tile, pitch, nrows, cols, nb, X, warp, lane, y); break;
+        case T_Q8_0: ab_rows_fit<T_Q8_0>(tile, pitch, nrows, cols, nb, X, warp, lane, y); break;
+        case T_Q4_K: ab_rows_fit<T_Q4_K>(tile, pitch, nrows, cols, nb, X, warp, lane, y); break;
+        case T_Q6_K: ab_rows_fit<T_Q6_K>(tile, pitch, nrows, cols, nb, X, warp, lane, y); break;
         default: break;
         }
     }
