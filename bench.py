@@ -684,14 +684,17 @@ def measure_model_decode(args, pkg, ctx, torch, stream, moe_layers, rank, world,
     for _ in range(3):
         lg.launch()
     _barrier(torch, dist)
-    reps = 20
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for _ in range(reps):
-        lg.launch()
-    ev1.record(stream)
-    stream.synchronize()
-    layers_ms = _max_over_ranks(torch, dist, ev0.elapsed_time(ev1)) / reps
+    reps, batches = 10, 5  # the median of five batches of ten replays (single batches varied by a few percent)
+    batch_ms = []
+    for _ in range(batches):
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(reps):
+            lg.launch()
+        ev1.record(stream)
+        stream.synchronize()
+        batch_ms.append(ev0.elapsed_time(ev1) / reps)
+    layers_ms = _max_over_ranks(torch, dist, float(np.median(batch_ms)))
     lg.free()
     uses_stack = dec.uses_stack
 
@@ -725,7 +728,8 @@ def measure_model_decode(args, pkg, ctx, torch, stream, moe_layers, rank, world,
             "frac": k_achieved / peak, "peak_kind": kind, "algorithmic_bytes_per_launch": lbytes,
             "avg_launch_ms": layers_ms, "traffic": (ncu_traffic() or {}).get(name, {}).get("dram_bytes_per_launch"),
             "note": f"the {L} decoder layers of one token at position {int(mean_ctx)} (the workload's mean "
-                    f"context) as one graph replayed {reps} times, CUDA events on the launching stream"}
+                    f"context) as one graph: the median of {batches} batches of {reps} replays, CUDA events on the "
+                    f"launching stream"}
     n_runs_launches = runs * ((n_prompt - 1) * launches_prompt + n_gen * launches_full)
     out = {
         "metric": f"greedy decode tok/s ({name}: {'Qwen3-30B-A3B' if moe else 'Qwen2-0.5B'} shape, {L} layers)",
