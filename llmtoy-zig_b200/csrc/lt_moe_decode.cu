@@ -429,11 +429,9 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     DT_MARK(8);
     __syncthreads();
     DT_MARK(9);
-    // down rows [r0, r1) of each slot's expert and the L2 prefetch of the next
-    // kernel's weights, requested once this CTA's gate/up rows are consumed:
-    // until then every CTA's HBM requests are the gate/up rows, which the
-    // grid's slowest CTA (and so the h barrier) waits for
-    if (tid >= 64 && tid < 66 && a.pf[tid - 64]) prefetch_l2_share(a.pf[tid - 64], a.pf_bytes[tid - 64], c, G);
+    // down rows [r0, r1) of each slot's expert, requested once this CTA's
+    // gate/up rows are consumed: until then every CTA's HBM requests are the
+    // gate/up rows, which the grid's slowest CTA (and so the h barrier) waits for
     if (warp == 1 && !a.late_down && (uint32_t)lane < a.k && nr) {
         const uint32_t e = min(s_sel[lane], a.E - 1);
         const uint32_t bytes = (uint32_t)(nr * a.dpitch);
@@ -469,6 +467,9 @@ __global__ void __launch_bounds__(kDecThreads) k_moe_decode(DecodeArgs a) {
     grid_arrive_split(ctr_b);
     grid_wait_split(ctr_b, epoch, a.dev_err, kWaitLimitNs);
     DT_MARK(12);
+    // the L2 prefetch of the next kernel's weights: after the h hand-off, so
+    // that it does not compete with this launch's down rows for DRAM
+    if (tid >= 64 && tid < 66 && a.pf[tid - 64]) prefetch_l2_share(a.pf[tid - 64], a.pf_bytes[tid - 64], c, G);
 
     // ── phase D ──────────────────────────────────────────────────────────────
     uint8_t *himg_s = smem + L.rr;  // k slot images, a.img bytes each
